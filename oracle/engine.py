@@ -1,0 +1,601 @@
+"""CPU restatement of the reference CDB engine in its synchronous mode.
+
+TEST INFRASTRUCTURE ONLY: the checker for the CUDA engine's schedules, block tables and
+logits. Nothing in the product imports this module.
+
+It restates ``ContinuousDepthBatchingEngine`` with ``use_async_batching=False`` (every
+stage synchronous, the mode the reference's CPU tests and replay parity use):
+
+* refill loop ``continuous_depth_batching/continuous_api.py:503-606`` with
+  ``CDBScheduler.schedule_next`` ``scheduler.py:101-140`` (coda >= min -> prefill if admitted
+  -> recurrent FIFO -> coda flush);
+* prefill admission/packing ``scheduler_base.py:129-201,466-515`` and ``scheduler.py:211-320``;
+* recurrent routing ``continuous_api.py:1090-1203`` (survivors return to the queue head in
+  order, ``scheduler.py:164-180``), exits to the coda queue;
+* coda + re-entry ``continuous_api.py:1378-1448`` (sampled token -> next decode item at the
+  head of the queue);
+* no-refill lockstep waves ``continuous_api.py:608-944`` (``refill=False``);
+* FIFO block ids ``continuous_batching/cache_manager.py:33-91`` with exact-ceil allocation
+  ``scheduler_base.py:416-433`` / ``continuous_api.py:1654-1669``;
+* exit policies ``exit_policy.py:150-169`` (cumulative hazard) and replay
+  ``continuous_api.py:1671-1697``; ``last_exited`` copy-on-exit ``:1205-1245``.
+
+Every launch is appended to ``launches`` in the golden-fixture format:
+``{"kind": "prefill", "items": [[req, past, q_len, has_new], ...], "blocks": [...]}``,
+``{"kind": "recurrent", "items": [[req, pos, step], ...], "blocks": [[block ids], ...]}``,
+``{"kind": "coda", "items": [[req, pos, step], ...]}``.
+
+``forced_tokens`` (teacher forcing) makes the engine continue every request with the given
+tokens instead of its own argmax, so a second engine's per-position predictions can be
+compared against these without autoregressive divergence.
+"""
+
+from __future__ import annotations
+
+from collections import Counter, OrderedDict, deque
+from dataclasses import dataclass, field
+
+import torch
+
+from continuous_depth_batching_b200.ouro import OuroShape
+
+from .ouro_math import OracleKVCache, OuroOracle, OuroWeights
+
+PENDING, PREFILLING, DECODING, FINISHED = 0, 1, 2, 3
+KV_POLICIES = ("depth_indexed", "last_exited", "single", "first_then_shared")
+
+
+def slots_per_layer(policy: str, steps: int, requested: int | None = None) -> int:
+    """``resolve_kv_slots_per_layer`` (``kv_cache_policy.py:52-79``)."""
+
+    fixed = {"depth_indexed": steps, "last_exited": steps, "single": 1}
+    if policy in fixed:
+        return fixed[policy]
+    return 2 if requested is None else requested
+
+
+def slot_for_step(policy: str, step: int, slots: int) -> int:
+    """``kv_slot_for_step`` (``kv_cache_policy.py:82-103``)."""
+
+    if policy in ("depth_indexed", "last_exited"):
+        return step
+    if policy == "single":
+        return 0
+    return min(step, slots - 1)
+
+
+@dataclass
+class OracleConfig:
+    block_size: int = 16
+    num_blocks: int = 4096
+    max_num_batched_tokens: int = 8192
+    safety_margin: float = 0.2
+    max_model_len: int = 16384
+    max_recurrent_steps: int = 4
+    exit_threshold: float | None = None
+    synthetic_exit_replay: bool = False
+    min_recurrent_steps: int = 1
+    min_coda_batch_size: int = 1
+    max_num_seqs: int = 256
+    min_free_slots: int | None = None
+    refill: bool = True
+    kv_policy: str = "single"
+    kv_slots_per_layer: int | None = None
+    kv_pressure_mode: str = "recompute"
+
+
+@dataclass
+class Req:
+    idx: int
+    prompt: list[int]
+    max_new: int
+    depths: list[int]
+    status: int = PENDING
+    remaining: list[int] = field(default_factory=list)
+    to_process: list[int] = field(default_factory=list)
+    generated: list[int] = field(default_factory=list)
+    position: int = 0
+    allocated: int = 0
+    in_flight_tokens: int = 0
+    cursor: int = 0
+    exit_depths: list[int] = field(default_factory=list)
+
+    def next_depth(self) -> int | None:
+        if not self.depths:
+            return None
+        d = self.depths[self.cursor]
+        self.cursor += 1
+        return d
+
+
+@dataclass
+class Item:
+    req: Req
+    token: int
+    position: int
+    step: int
+    depth: int | None
+    hidden: torch.Tensor | None = None
+    cdf: float = 0.0
+    survival: float = 1.0
+
+
+class OracleEngine:
+    """Synchronous-mode CDB engine on CPU over :class:`OuroOracle` math."""
+
+    def __init__(self, shape: OuroShape, state_dict: dict, cfg: OracleConfig, dtype: torch.dtype = torch.float32):
+        if cfg.kv_policy not in KV_POLICIES:
+            raise ValueError(f"unknown kv_policy {cfg.kv_policy!r}")
+        self.shape = shape
+        self.cfg = cfg
+        self.dtype = dtype
+        self.slots = slots_per_layer(cfg.kv_policy, cfg.max_recurrent_steps, cfg.kv_slots_per_layer)
+        self.num_cache_layers = self.slots * shape.num_hidden_layers
+        self.weights = OuroWeights.from_state_dict(shape, state_dict, dtype)
+        self.max_num_seqs = min(cfg.max_num_seqs, cfg.max_num_batched_tokens)
+        self.min_free = (
+            max(1, self.max_num_seqs // 8) if cfg.min_free_slots is None else min(cfg.min_free_slots, self.max_num_seqs)
+        )
+        self.safety = 0.0 if cfg.kv_pressure_mode == "reserve" else cfg.safety_margin
+        self.width = -(-cfg.max_model_len // cfg.block_size)
+
+    # ------------------------------------------------------------------ block pool
+    def _alloc(self, r: Req, n: int) -> bool:
+        if n > len(self.free):
+            return False
+        got = [self.free.popleft() for _ in range(n)]
+        self.tables.setdefault(r.idx, []).extend(got)
+        r.allocated += n
+        return True
+
+    def _free(self, r: Req) -> None:
+        self.free.extend(self.tables.pop(r.idx, []))
+
+    def _alloc_if_needed(self, r: Req, n_next: int) -> bool:
+        bs = self.cfg.block_size
+        if r.allocated * bs - r.position < n_next:
+            need = -(-(r.position + n_next) // bs) - r.allocated
+            return self._alloc(r, need)
+        return True
+
+    def _alloc_one_decode(self, r: Req) -> bool:
+        bs = self.cfg.block_size
+        if r.allocated * bs - r.position >= 1 and r.allocated > 0:
+            return True
+        need = -(-(r.position + 1) // bs) - r.allocated
+        return self._alloc(r, need)
+
+    # ------------------------------------------------------------------ request bookkeeping
+    def _update(self, r: Req, token: int) -> bool:
+        """``RequestState.update_and_check_completion`` (``continuous_batching/requests.py:185-218``), eos=None."""
+
+        r.in_flight_tokens = max(0, r.in_flight_tokens - 1)
+        if len(r.generated) < r.max_new:
+            r.generated.append(token)
+            r.to_process = [token]
+        if len(r.generated) >= r.max_new:
+            r.status = FINISHED
+            return True
+        return False
+
+    def _retire(self, r: Req) -> None:
+        self._free(r)
+        self.active.pop(r.idx, None)
+        self.in_flight.discard(r.idx)
+        self.finished[r.idx] = list(r.generated)
+
+    def _stage_decode(self, r: Req) -> Item:
+        if not self._alloc_one_decode(r):
+            raise RuntimeError("oracle: KV cache full (size num_blocks to fit the workload)")
+        return Item(req=r, token=r.to_process[0], position=r.position, step=0, depth=r.next_depth())
+
+    def _next_token(self, r: Req, computed: int) -> int:
+        if self.forced is not None:
+            return self.forced[r.idx][len(r.generated)]
+        return computed
+
+    # ------------------------------------------------------------------ queues
+    def _enqueue(self, item: Item, front: bool = False) -> None:
+        self.in_flight.add(item.req.idx)
+        if item.step == 0 and self.ready:
+            self.refills += 1
+        if front:
+            self.ready.appendleft(item)
+        else:
+            self.ready.append(item)
+
+    def _enqueue_front(self, items: list[Item]) -> None:
+        for item in reversed(items):
+            self._enqueue(item, front=True)
+
+    def _has_pending(self) -> bool:
+        return bool(self.coda_q or self.ready or self.active or self.waiting)
+
+    def _has_decode_work(self) -> bool:
+        return any(r.status == DECODING for r in self.active.values())
+
+    def _admit_prefill(self) -> bool:
+        return not self._has_decode_work() or len(self.free) > self.safety * self.cfg.num_blocks
+
+    def _reserved_peak(self, r: Req) -> int:
+        total = min(len(r.prompt) + r.max_new, self.cfg.max_model_len)
+        return -(-total // self.cfg.block_size)
+
+    def _prefill_candidates(self) -> list[Req]:
+        prefilling = [r for r in self.active.values() if r.status == PREFILLING and r.idx not in self.in_flight]
+        free_slots = max(0, self.max_num_seqs - len(self.active))
+        admissible = [self.waiting[i] for i in list(self.waiting)[:free_slots]]
+        if self.cfg.kv_pressure_mode == "reserve":
+            committed = sum(self._reserved_peak(r) for r in self.active.values())
+            kept = []
+            for r in admissible:
+                need = self._reserved_peak(r)
+                if committed + need > self.cfg.num_blocks:
+                    break
+                committed += need
+                kept.append(r)
+            admissible = kept
+        cands = prefilling + admissible
+        if not cands:
+            return []
+        if any(r.status == PREFILLING for r in cands):
+            return cands
+        return cands if free_slots >= self.min_free else []
+
+    def _schedule_prefill(self) -> list[tuple[Req, int, int, bool]] | None:
+        cands = self._prefill_candidates()
+        if not cands:
+            return None
+        bs = self.cfg.block_size
+        token_budget = self.cfg.max_num_batched_tokens
+        cache_budget = self.cfg.num_blocks * bs
+        margin = self.safety * self.cfg.num_blocks
+        fast = True
+        out = []
+        for r in cands:
+            n_free = len(self.free)
+            if n_free < margin and out:
+                break
+            toks = r.remaining
+            qlen = min(len(toks), token_budget)
+            if qlen == 0:
+                continue
+            eligible = qlen == 1 and r.position < self.width * bs
+            read_needed = r.position
+            if not (fast and eligible) and cache_budget < read_needed:
+                continue
+            if not self._alloc_if_needed(r, qlen):
+                if n_free == 0 and r.idx in self.waiting:
+                    break
+                continue
+            past = r.position
+            if len(toks) <= qlen:
+                if r.status == PENDING:
+                    self.active[r.idx] = r
+                if r.status <= PREFILLING:
+                    r.to_process = toks
+                    r.remaining = []
+                    r.status = DECODING
+            else:
+                if r.status == PENDING:
+                    self.active[r.idx] = r
+                    r.status = PREFILLING
+                r.remaining = toks[qlen:]
+                r.to_process = toks[:qlen]
+            self.in_flight.add(r.idx)
+            qlen = len(r.to_process)
+            fast = fast and qlen == 1 and r.position < self.width * bs
+            token_budget -= qlen
+            cache_budget -= read_needed
+            has_new = not r.remaining
+            out.append((r, past, qlen, has_new))
+            self.waiting.pop(r.idx, None)
+            if token_budget == 0 or (cache_budget <= 0 and not fast):
+                break
+        return out or None
+
+    # ------------------------------------------------------------------ launches
+    def _run_prefill(self, batch: list[tuple[Req, int, int, bool]]) -> list[tuple[Req, int]]:
+        """Full-depth prefill; returns ``(req, sampled token)`` for prompts that finished."""
+
+        chunks = []
+        for r, past, qlen, _has in batch:
+            chunks.append((list(r.to_process), past, self.tables[r.idx]))
+        steps = [slot_for_step(self.cfg.kv_policy, s, self.slots) for s in range(self.cfg.max_recurrent_steps)]
+        hidden = self.model.prefill(chunks, steps)
+        rows, offset = [], 0
+        for r, past, qlen, has in batch:
+            r.position = past + qlen
+            offset += qlen
+            if has:
+                rows.append(offset - 1)
+                r.to_process = [-1]
+                r.in_flight_tokens += 1
+        self.launches.append(
+            {
+                "kind": "prefill",
+                "items": [[r.idx, past, qlen, int(has)] for r, past, qlen, has in batch],
+                "blocks": [list(self.tables[r.idx][: -(-r.position // self.cfg.block_size)]) for r, *_ in batch],
+            }
+        )
+        if not rows:
+            return []
+        logits = self.model.lm_head(hidden[torch.tensor(rows)])
+        self.logits.append(("prefill", logits))
+        toks = torch.argmax(logits, dim=-1).tolist()
+        sampled = [r for r, _p, _q, has in batch if has]
+        return list(zip(sampled, toks, strict=True))
+
+    def _run_recurrent(self, items: list[Item]) -> torch.Tensor | None:
+        bs = self.cfg.block_size
+        slot = slot_for_step(self.cfg.kv_policy, items[0].step, self.slots)
+        blocks = [self.tables[it.req.idx][: -(-(it.position + 1) // bs)] for it in items]
+        self.launches.append(
+            {
+                "kind": "recurrent",
+                "items": [[it.req.idx, it.position, it.step] for it in items],
+                "blocks": [list(b) for b in blocks],
+            }
+        )
+        hidden = torch.stack([it.hidden for it in items])
+        out, gate = self.model.recurrent_step(
+            hidden, [it.position for it in items], blocks, slot * self.shape.num_hidden_layers
+        )
+        for i, it in enumerate(items):
+            it.hidden = out[i]
+        self.stats["recurrent_batches"] += 1
+        self.stats["recurrent_steps"] += len(items)
+        return gate
+
+    def _should_exit(self, item: Item, step: int, gate: torch.Tensor | None, i: int) -> bool:
+        if step == self.cfg.max_recurrent_steps - 1:
+            return True
+        if item.depth is not None:
+            return step >= item.depth
+        if self.cfg.exit_threshold is None:
+            return False
+        hazard = float(torch.sigmoid(gate[i]).float().item())
+        item.cdf += hazard * item.survival
+        item.survival *= 1.0 - hazard
+        return step + 1 >= self.cfg.min_recurrent_steps and item.cdf >= self.cfg.exit_threshold
+
+    def _record_exit(self, item: Item, step: int) -> None:
+        item.req.exit_depths.append(step)
+        self.hist[step] += 1
+        if self.cfg.kv_policy == "last_exited" and step < self.cfg.max_recurrent_steps - 1:
+            self.backlog.append((item, step))
+
+    def _flush_exit_copies(self) -> None:
+        """``_flush_exit_kv_copies`` + ``LoopedKvLayout.exit_copy_layer_groups`` (``kv_cache_policy.py:235-258``)."""
+
+        if not self.backlog:
+            return
+        backlog, self.backlog = self.backlog, []
+        by_step: dict[int, list[Item]] = {}
+        for item, step in backlog:
+            by_step.setdefault(step, []).append(item)
+        bs, layers = self.cfg.block_size, self.shape.num_hidden_layers
+        for step, items in sorted(by_step.items()):
+            rows = torch.tensor(
+                [self.tables[it.req.idx][it.position // bs] * bs + it.position % bs for it in items], dtype=torch.long
+            )
+            src_slot = slot_for_step(self.cfg.kv_policy, step, self.slots)
+            for layer in range(layers):
+                dst = [t * layers + layer for t in range(src_slot + 1, self.slots)]
+                if dst:
+                    self.model.copy_rows(src_slot * layers + layer, dst, rows)
+
+    def _prelude(self, items: list[Item]) -> None:
+        if not items:
+            return
+        emb = self.model.embed([it.token for it in items])
+        for i, it in enumerate(items):
+            it.hidden = emb[i]
+
+    def _run_coda(self, items: list[Item]) -> list[int]:
+        self.launches.append({"kind": "coda", "items": [[it.req.idx, it.position, it.step] for it in items]})
+        for it in items:
+            it.req.in_flight_tokens += 1
+        logits = self.model.lm_head(torch.stack([it.hidden for it in items]))
+        self.logits.append(("coda", logits))
+        self.stats["coda_batches"] += 1
+        self.stats["coda_tokens"] += len(items)
+        return torch.argmax(logits, dim=-1).tolist()
+
+    # ------------------------------------------------------------------ loops
+    def _consume_prefill(self, results: list[tuple[Req, int]], stage: bool) -> None:
+        new_items = []
+        for r, tok in results:
+            if r.status == FINISHED:
+                continue
+            if self._update(r, self._next_token(r, tok)):
+                self._retire(r)
+                continue
+            if stage:
+                new_items.append(self._stage_decode(r))
+        self._prelude(new_items)
+        for it in new_items:
+            self._enqueue(it)
+
+    def _consume_coda(self, items: list[Item], toks: list[int], stage: bool) -> None:
+        new_items = []
+        for it, tok in zip(items, toks, strict=True):
+            r = it.req
+            if r.status == FINISHED:
+                continue
+            r.position += 1
+            if self._update(r, self._next_token(r, tok)):
+                self._retire(r)
+                continue
+            if stage:
+                new_items.append(self._stage_decode(r))
+        self._prelude(new_items)
+        self._enqueue_front(new_items)
+
+    def _refill_loop(self) -> None:
+        pending_prefill: list[list[tuple[Req, int]]] = []
+        pending_coda: list[tuple[list[Item], list[int]]] = []
+        while self._has_pending() or pending_prefill or pending_coda:
+            for res in pending_prefill:
+                self._consume_prefill(res, stage=True)
+            pending_prefill = []
+            for items, toks in pending_coda:
+                self._consume_coda(items, toks, stage=True)
+            pending_coda = []
+            if not self._has_pending():
+                continue
+            self.stats["ticks"] += 1
+            if len(self.coda_q) >= self.cfg.min_coda_batch_size:
+                batch = [self.coda_q.popleft() for _ in range(min(self.max_num_seqs, len(self.coda_q)))]
+                pending_coda.append((batch, self._run_coda(batch)))
+                continue
+            if self._admit_prefill():
+                pb = self._schedule_prefill()
+                if pb is not None:
+                    self.stats["prefill_batches"] += 1
+                    pending_prefill.append(self._run_prefill(pb))
+                    for r, _past, _q, has in pb:
+                        if not has:
+                            self.in_flight.discard(r.idx)
+                    continue
+            items = self._pop_recurrent()
+            if items:
+                gate = self._run_recurrent(items)
+                refills = []
+                for i, it in enumerate(items):
+                    if self._should_exit(it, it.step, gate, i):
+                        self._record_exit(it, it.step)
+                        self.in_flight.add(it.req.idx)
+                        self.coda_q.append(it)
+                    else:
+                        it.step += 1
+                        refills.append(it)
+                self._enqueue_front(refills)
+                self._flush_exit_copies()
+                continue
+            if self.coda_q:
+                batch = [self.coda_q.popleft() for _ in range(min(self.max_num_seqs, len(self.coda_q)))]
+                pending_coda.append((batch, self._run_coda(batch)))
+                continue
+            raise RuntimeError("oracle: scheduler stalled (KV cache too small for the workload)")
+
+    def _pop_recurrent(self) -> list[Item]:
+        n = min(self.max_num_seqs, len(self.ready))
+        if n == 0:
+            return []
+        first = self.ready.popleft()
+        batch = [first]
+        if self.slots > 1:
+            target = slot_for_step(self.cfg.kv_policy, first.step, self.slots)
+            deferred: deque[Item] = deque()
+            while self.ready and len(batch) < n:
+                it = self.ready.popleft()
+                if slot_for_step(self.cfg.kv_policy, it.step, self.slots) == target:
+                    batch.append(it)
+                else:
+                    deferred.append(it)
+            deferred.extend(self.ready)
+            self.ready = deferred
+        else:
+            while self.ready and len(batch) < n:
+                batch.append(self.ready.popleft())
+        return batch
+
+    def _no_refill_loop(self) -> None:
+        while self._has_pending():
+            did_prefill = False
+            while self._admit_prefill():
+                pb = self._schedule_prefill()
+                if pb is None:
+                    break
+                self.stats["prefill_batches"] += 1
+                res = self._run_prefill(pb)
+                for r, *_ in pb:
+                    self.in_flight.discard(r.idx)
+                self._consume_prefill(res, stage=False)
+                did_prefill = True
+            cohort = [r for r in self.active.values() if r.status == DECODING and r.to_process and r.to_process[0] >= 0]
+            cohort = cohort[: self.max_num_seqs]
+            items = [self._stage_decode(r) for r in cohort]
+            if not items:
+                if not did_prefill and self._has_pending():
+                    raise RuntimeError("oracle: no-refill loop stalled")
+                continue
+            self._prelude(items)
+            survivors, exited = items, []
+            for step in range(self.cfg.max_recurrent_steps):
+                for it in survivors:
+                    it.step = step
+                gate = self._run_recurrent(survivors)
+                forced = step == self.cfg.max_recurrent_steps - 1
+                cont = []
+                for i, it in enumerate(survivors):
+                    if forced or self._should_exit(it, step, gate, i):
+                        self._record_exit(it, step)
+                        exited.append(it)
+                    else:
+                        cont.append(it)
+                self._flush_exit_copies()
+                survivors = cont
+                if not survivors:
+                    break
+            toks = self._run_coda(exited)
+            self._consume_coda(exited, toks, stage=False)
+
+    def generate(
+        self,
+        prompts: list[list[int]],
+        max_new_tokens: list[int],
+        exit_depths: list[list[int]] | None = None,
+        forced_tokens: list[list[int]] | None = None,
+    ) -> list[list[int]]:
+        cfg = self.cfg
+        caps = [min(m, cfg.max_model_len - len(p)) for m, p in zip(max_new_tokens, prompts, strict=True)]
+        self.free: deque[int] = deque(range(cfg.num_blocks))
+        self.tables: dict[int, list[int]] = {}
+        self.model = OuroOracle(
+            self.weights, OracleKVCache(self.shape, self.num_cache_layers, cfg.num_blocks, cfg.block_size, self.dtype)
+        )
+        self.waiting: OrderedDict[int, Req] = OrderedDict()
+        self.active: OrderedDict[int, Req] = OrderedDict()
+        self.in_flight: set[int] = set()
+        self.ready: deque[Item] = deque()
+        self.coda_q: deque[Item] = deque()
+        self.backlog: list[tuple[Item, int]] = []
+        self.finished: dict[int, list[int]] = {}
+        self.launches: list[dict] = []
+        self.logits: list[tuple[str, torch.Tensor]] = []
+        self.refills = 0
+        self.hist: Counter[int] = Counter()
+        self.stats = Counter()
+        self.forced = forced_tokens
+        reqs = []
+        for i, (p, m) in enumerate(zip(prompts, caps, strict=True)):
+            r = Req(idx=i, prompt=list(p), max_new=m, depths=list(exit_depths[i]) if exit_depths else [])
+            r.remaining = list(p)
+            reqs.append(r)
+            self.waiting[i] = r
+        with torch.no_grad():
+            if cfg.refill:
+                self._refill_loop()
+            else:
+                self._no_refill_loop()
+        self.requests = reqs
+        self.stats["generated_tokens"] = sum(len(v) for v in self.finished.values())
+        self.stats["scheduler_refills"] = self.refills
+        return [self.finished[i] for i in range(len(prompts))]
+
+
+def exit_depth_histogram(engine: OracleEngine) -> dict[str, int]:
+    return {str(k): v for k, v in sorted(engine.hist.items())}
+
+
+def isclose_tokens(a: list[list[int]], b: list[list[int]]) -> float:
+    """Fraction of equal token positions between two generations (same shapes)."""
+
+    total = sum(len(x) for x in a)
+    same = sum(int(p == q) for x, y in zip(a, b, strict=True) for p, q in zip(x, y, strict=True))
+    return same / total if total else 1.0
+
+
+__all__ = ["OracleConfig", "OracleEngine", "exit_depth_histogram", "isclose_tokens"]

@@ -1,0 +1,267 @@
+"""Generate the golden fixtures by running the reference engine itself on CPU.
+
+Run in a container that has the reference checkout (read-only) at ``$CDB_REFERENCE_SRC``
+(default ``/root/reference/src``)::
+
+    python tests/golden/make_golden.py
+
+It builds the reference's own ``OuroForCausalLM`` at BASELINE config 0's shape, loads the
+seeded weights from :func:`continuous_depth_batching_b200.ouro.random_ouro_state_dict`,
+registers the CPU restatement of the paged FlashAttention contract
+(:mod:`oracle.paged_attention`; FlashAttention-3 is a binary the image does not have) and
+drives the reference ``ContinuousDepthBatchingEngine.generate_batch`` in its synchronous mode
+(``use_async_batching=False``). Each run records the generated tokens, per-token exit depths,
+engine stats, the launch trace (every prefill, recurrent and coda launch with its items,
+positions, recurrent steps and block-table rows) and the logits of every LM-head call.
+
+Outputs: ``tests/golden/ouro_cfg0.json`` (traces) and ``tests/golden/ouro_cfg0_logits.npz``.
+The GPU box has no reference checkout; the tests only read these files.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO))
+sys.path.insert(0, os.environ.get("CDB_REFERENCE_SRC", "/root/reference/src"))
+
+from continuous_depth_batching_b200.ouro import OuroShape, random_ouro_state_dict  # noqa: E402
+from oracle.paged_attention import cpu_paged_attention_forward  # noqa: E402
+from oracle.workloads import config0_workload  # noqa: E402
+
+CFG0 = OuroShape(
+    vocab_size=1024,
+    hidden_size=256,
+    intermediate_size=704,
+    num_hidden_layers=4,
+    num_attention_heads=4,
+    num_key_value_heads=4,
+    head_dim=64,
+    rope_theta=10000.0,
+    rms_norm_eps=1e-6,
+    max_position_embeddings=2048,
+    total_ut_steps=4,
+)
+# A gate wide enough that the live hazard policy is not decided by the sign of a logit
+# that sits within rounding of zero.
+GATE_STD = 0.12
+
+
+def build_reference_model(shape: OuroShape, kv_policy: str):
+    from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
+
+    from looped_cdb.models.ouro.configuration_ouro import OuroConfig
+    from looped_cdb.models.ouro.kv_cache_policy import configure_kv_cache_policy
+    from looped_cdb.models.ouro.modeling_ouro import OuroForCausalLM
+
+    ALL_ATTENTION_FUNCTIONS["paged|flash_attention_3"] = cpu_paged_attention_forward
+    config = OuroConfig(
+        vocab_size=shape.vocab_size,
+        hidden_size=shape.hidden_size,
+        intermediate_size=shape.intermediate_size,
+        num_hidden_layers=shape.num_hidden_layers,
+        num_attention_heads=shape.num_attention_heads,
+        num_key_value_heads=shape.num_key_value_heads,
+        max_position_embeddings=shape.max_position_embeddings,
+        rope_theta=shape.rope_theta,
+        rms_norm_eps=shape.rms_norm_eps,
+        total_ut_steps=shape.total_ut_steps,
+        layer_types=["full_attention"] * shape.num_hidden_layers,
+        pad_token_id=None,
+    )
+    torch.manual_seed(0)
+    model = OuroForCausalLM(config)
+    model.config._attn_implementation = "paged|flash_attention_3"
+    state = random_ouro_state_dict(shape, seed=0, gate_std=GATE_STD)
+    missing, unexpected = model.load_state_dict(state, strict=False)
+    assert not unexpected, unexpected
+    assert all("lookahead" in m or "preloop" in m for m in missing), missing
+    model.eval()
+    configure_kv_cache_policy(model, kv_policy=kv_policy)
+    return model
+
+
+class Recorder:
+    """Wraps the reference runner to log every launch, in order."""
+
+    def __init__(self, engine) -> None:
+        self.engine = engine
+        self.launches: list[dict] = []
+        self.logits: list[np.ndarray] = []
+        runner = engine.runner
+        cache = engine.cache
+        bs = cache.block_size
+        rid_index = lambda rid: int(rid.split("-")[1])  # noqa: E731
+
+        def blocks_of(rid: str, length: int) -> list[int]:
+            blocks = cache.cache_allocator.block_table[rid]
+            return [int(b) for b in blocks[: -(-length // bs)]]
+
+        orig_rec = runner.compute_recurrent_batch
+
+        def compute_recurrent_batch(items, recurrent_kwargs=None):
+            self.launches.append(
+                {
+                    "kind": "recurrent",
+                    "items": [
+                        [rid_index(it.state.request_id), it.token_position, it.recurrent_step] for it in items
+                    ],
+                    "blocks": [blocks_of(it.state.request_id, it.token_position + 1) for it in items],
+                }
+            )
+            return orig_rec(items, recurrent_kwargs=recurrent_kwargs)
+
+        orig_pre = runner.stage_prefill_batch
+
+        def stage_prefill_batch(model, requests, **kw):
+            entries = []
+            for fut in requests:
+                st = fut.state
+                entries.append([rid_index(st.request_id), st.position_offset, fut.query_length, int(fut.has_new_token)])
+            launch = {"kind": "prefill", "items": entries}
+            self.launches.append(launch)
+            out = orig_pre(model, requests, **kw)
+            launch["blocks"] = [blocks_of(fut.state.request_id, fut.state.position_offset) for fut in requests]
+            return out
+
+        orig_coda = runner.stage_coda_batch
+
+        def stage_coda_batch(items, allow_async=True):
+            self.launches.append(
+                {
+                    "kind": "coda",
+                    "items": [[rid_index(it.state.request_id), it.token_position, it.recurrent_step] for it in items],
+                }
+            )
+            return orig_coda(items, allow_async=allow_async)
+
+        runner.compute_recurrent_batch = compute_recurrent_batch
+        runner.stage_prefill_batch = stage_prefill_batch
+        runner.stage_coda_batch = stage_coda_batch
+
+        lm_head = engine.model.lm_head
+        orig_fwd = lm_head.forward
+
+        def lm_forward(x):
+            y = orig_fwd(x)
+            self.logits.append(y.detach().reshape(-1, y.shape[-1]).float().numpy().copy())
+            return y
+
+        lm_head.forward = lm_forward
+
+
+def run_case(name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_depths=None, num_blocks=4096):
+    from looped_cdb.continuous_depth_batching import ContinuousDepthBatchingConfig, ContinuousDepthBatchingEngine
+
+    model = build_reference_model(CFG0, kv_policy)
+    prompts, max_new = config0_workload()
+    cfg = ContinuousDepthBatchingConfig(
+        block_size=16,
+        num_blocks=num_blocks,
+        max_recurrent_steps=CFG0.total_ut_steps,
+        exit_threshold=0.5 if live_gate else None,
+        synthetic_exit_replay=not live_gate,
+        use_async_batching=False,
+        use_cuda_graph=False,
+        use_cuda_graph_prefill=False,
+        refill=refill,
+        kv_policy=kv_policy,
+        kv_pressure_mode="reserve" if kv_policy == "last_exited" else "recompute",
+        max_model_len=2048,
+    )
+    engine = ContinuousDepthBatchingEngine.from_model(model, cfg)
+    rec = Recorder(engine)
+    with torch.no_grad():
+        outs = engine.generate_batch(
+            prompts, max_new_tokens=max_new, eos_token_id=None, warmup=False, exit_depths=exit_depths
+        )
+    states_exit = {}
+    for st in list(engine.scheduler.active_requests.values()):
+        states_exit[st.request_id] = st.exit_depths
+    stats = engine.last_stats
+    result = {
+        "name": name,
+        "kv_policy": kv_policy,
+        "refill": refill,
+        "live_gate": live_gate,
+        "tokens": [o.generated_tokens for o in outs],
+        "exit_depths": exit_depths,
+        "stats": {
+            "prefill_batches": stats.prefill_batches,
+            "recurrent_batches": stats.recurrent_batches,
+            "coda_batches": stats.coda_batches,
+            "recurrent_steps": stats.recurrent_steps,
+            "coda_tokens": stats.coda_tokens,
+            "generated_tokens": stats.generated_tokens,
+            "scheduler_refills": stats.scheduler_refills,
+            "exit_depth_histogram": {str(k): v for k, v in sorted(stats.exit_depth_histogram.items())},
+        },
+        "launches": rec.launches,
+    }
+    return result, rec.logits
+
+
+def recorded_exit_depths(result: dict) -> list[list[int]]:
+    """Per-request exit steps of a live-gate run, read back from its recurrent trace."""
+
+    n = len(result["tokens"])
+    last_step: dict[tuple[int, int], int] = {}
+    for launch in result["launches"]:
+        if launch["kind"] == "coda":
+            for rid, pos, step in launch["items"]:
+                last_step[(rid, pos)] = step
+    depths = [[] for _ in range(n)]
+    for (rid, pos), step in sorted(last_step.items()):
+        depths[rid].append(step)
+    return depths
+
+
+def main() -> None:
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    runs = []
+    logits_out: dict[str, np.ndarray] = {}
+
+    live, live_logits = run_case("live_gate_refill", kv_policy="single", refill=True, live_gate=True)
+    runs.append(live)
+    depths = recorded_exit_depths(live)
+
+    replay, replay_logits = run_case(
+        "replay_refill", kv_policy="single", refill=True, live_gate=False, exit_depths=depths
+    )
+    runs.append(replay)
+    norefill, _ = run_case("replay_norefill", kv_policy="single", refill=False, live_gate=False, exit_depths=depths)
+    runs.append(norefill)
+    lastx, _ = run_case("replay_last_exited", kv_policy="last_exited", refill=True, live_gate=False, exit_depths=depths)
+    runs.append(lastx)
+
+    for i, arr in enumerate(live_logits[:6]):
+        logits_out[f"live_gate_refill_{i}"] = arr.astype(np.float32)
+    prompts, max_new = config0_workload()
+    payload = {
+        "generator": "tests/golden/make_golden.py",
+        "shape": CFG0.__dict__,
+        "gate_std": GATE_STD,
+        "weights_seed": 0,
+        "prompts": prompts,
+        "max_new_tokens": max_new,
+        "block_size": 16,
+        "num_blocks": 4096,
+        "runs": runs,
+    }
+    (HERE / "ouro_cfg0.json").write_text(json.dumps(payload, separators=(",", ":")))
+    np.savez_compressed(HERE / "ouro_cfg0_logits.npz", **logits_out)
+    print("wrote", HERE / "ouro_cfg0.json", "runs:", [r["name"] for r in runs])
+    for r in runs:
+        print(r["name"], r["stats"])
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,66 @@
+"""Pin the CPU oracle against fixtures recorded from the reference engine itself.
+
+``tests/golden/make_golden.py`` ran the reference ``ContinuousDepthBatchingEngine`` (BASELINE
+config 0 shape, seeded weights, synchronous mode) and recorded every launch. The oracle must
+reproduce each run exactly: generated tokens, the ordered launch trace with every item's
+(request, position, recurrent step) and block-table row, refill counts, exit histograms, and
+(fp32) the LM-head logits.
+"""
+
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from continuous_depth_batching_b200.ouro import OuroShape, random_ouro_state_dict
+from oracle.engine import OracleConfig, OracleEngine, exit_depth_histogram
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.fixture(scope="module")
+def golden():
+    data = json.loads((GOLDEN / "ouro_cfg0.json").read_text())
+    shape = OuroShape(**data["shape"])
+    sd = random_ouro_state_dict(shape, seed=data["weights_seed"], gate_std=data["gate_std"])
+    return data, shape, sd
+
+
+def _config(run: dict, data: dict) -> OracleConfig:
+    return OracleConfig(
+        block_size=data["block_size"],
+        num_blocks=data["num_blocks"],
+        max_recurrent_steps=4,
+        max_model_len=2048,
+        exit_threshold=0.5 if run["live_gate"] else None,
+        synthetic_exit_replay=not run["live_gate"],
+        refill=run["refill"],
+        kv_policy=run["kv_policy"],
+        kv_pressure_mode="reserve" if run["kv_policy"] == "last_exited" else "recompute",
+    )
+
+
+@pytest.mark.parametrize("name", ["live_gate_refill", "replay_refill", "replay_norefill", "replay_last_exited"])
+def test_oracle_reproduces_reference_run(golden, name):
+    data, shape, sd = golden
+    run = next(r for r in data["runs"] if r["name"] == name)
+    engine = OracleEngine(shape, sd, _config(run, data), torch.float32)
+    tokens = engine.generate(data["prompts"], data["max_new_tokens"], exit_depths=run["exit_depths"])
+    assert tokens == run["tokens"]
+    assert len(engine.launches) == len(run["launches"])
+    for mine, ref in zip(engine.launches, run["launches"], strict=True):
+        assert mine == ref
+    assert exit_depth_histogram(engine) == run["stats"]["exit_depth_histogram"]
+    assert engine.refills == run["stats"]["scheduler_refills"]
+    assert engine.stats["recurrent_batches"] == run["stats"]["recurrent_batches"]
+    assert engine.stats["coda_batches"] == run["stats"]["coda_batches"]
+    if name == "live_gate_refill":
+        logits = np.load(GOLDEN / "ouro_cfg0_logits.npz")
+        for i in range(6):
+            ref = logits[f"live_gate_refill_{i}"]
+            mine = engine.logits[i][1].numpy()
+            np.testing.assert_allclose(mine, ref, rtol=0, atol=1e-5)
