@@ -1,0 +1,388 @@
+"""Benchmark: CDB decode throughput of the B200 engine -> one JSON line.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--requests R]
+
+Workload: Ouro-1.4B architecture (24 layers, hidden 2048, 16x128
+MHA heads, SwiGLU 5632, vocab 49152, 4 recurrent steps), random-init bf16; 256 concurrent
+requests, prompt lengths LogNormal(median 200, sigma 0.8, cap 2048), output lengths
+LogNormal(median 250, sigma 0.9, cap 1024), token ids uniform; per-token exit depths replayed
+from a seeded categorical over {1,2,3,4} with p=(0.2,0.3,0.3,0.2); kv_policy single, block 16,
+refill on. All inputs are seeded synthetic data (numpy default_rng), no dataset.
+
+A step is one ``generate_batch`` over the whole request set (prefill included, as the
+reference's ``generated_tokens / wall_time`` metric, ``benchmarks/metrics.py:274-278``).
+``value`` is generated tokens / device time (CUDA events on the engine stream, max over ranks);
+``e2e`` is the same through the public API measured on the host clock, which includes the prompt
+upload and the token read-back of every step. Under torchrun each rank is an independent replica
+with its own seeded request set (``scaling: weak``); nothing crosses GPUs inside the timed region.
+
+``--impl reference`` times the CPU restatement of the reference engine (``oracle/``, the only
+place bench.py runs it) on the host cores over a bounded prefix of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tokens/s/GPU, Ouro-1.4B CDB; paged-attn HBM GB/s vs 8 TB/s peak"
+UNIT = "tokens/s"
+OURO_1P4B = dict(
+    vocab_size=49152, hidden_size=2048, intermediate_size=5632, num_hidden_layers=24, num_attention_heads=16,
+    num_key_value_heads=16, head_dim=128, rope_theta=10000.0, rms_norm_eps=1e-6, max_position_embeddings=4096,
+    total_ut_steps=4,
+)
+DEPTH_P = (0.2, 0.3, 0.3, 0.2)
+
+
+def parse() -> argparse.Namespace:
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--requests", type=int, default=256)
+    p.add_argument("--out-cap", type=int, default=1024, help="cap on output lengths (smaller = profiling case)")
+    p.add_argument("--no-graph", action="store_true")
+    p.add_argument("--seed", type=int, default=0)
+    return p.parse_args()
+
+
+def dist_env() -> tuple[int, int, int]:
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def workload(seed: int, n: int, out_cap: int):
+    from oracle.workloads import ouro_lognormal_workload
+
+    return ouro_lognormal_workload(n, vocab_size=OURO_1P4B["vocab_size"], seed=seed, out_cap=out_cap, depth_probs=DEPTH_P)
+
+
+class ClockSampler:
+    """nvidia-smi SM clocks / throttle reasons sampled every 200 ms while running."""
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        q = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            out, _ = self.proc.communicate(timeout=10)
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9], strict=True):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": mx or None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+def build_engine(args, device):
+    from continuous_depth_batching_b200 import ContinuousDepthBatchingConfig, ContinuousDepthBatchingEngine, OuroForCausalLM, OuroShape
+
+    shape = OuroShape(**OURO_1P4B)
+    model = OuroForCausalLM.random_init(shape, seed=1234, dtype=torch.bfloat16, device=device)
+    cfg = ContinuousDepthBatchingConfig(
+        block_size=16,
+        num_blocks=16384,
+        max_recurrent_steps=4,
+        synthetic_exit_replay=True,
+        use_async_batching=False,
+        use_cuda_graph=not args.no_graph,
+        refill=True,
+        kv_policy="single",
+        max_model_len=4096,
+        max_num_seqs=256,
+    )
+    eng = ContinuousDepthBatchingEngine.from_model(model, cfg, device=device)
+    del model
+    return eng, shape
+
+
+def attention_roofline(eng, shape, launches: list[tuple[list[int], list[int]]], peak_gbs: float) -> dict:
+    """Time the paged decode-attention kernel alone over recorded launch shapes (CUDA events)."""
+
+    from continuous_depth_batching_b200 import _lib
+
+    r = eng.runner
+    D, H = shape.head_dim, shape.num_attention_heads
+    row_bytes = H * D * 2
+    total_bytes, total_ms, n = 0.0, 0.0, 0
+    stream = r.stream
+    for slots, pos in launches:
+        b = len(pos)
+        meta = r.upload([slots, pos])
+        meta = meta.view(2, b)
+        with torch.cuda.stream(stream):
+            r._plan(meta[1], b, 1)
+        algo = 0
+        for p in pos:
+            algo += 2 * (p + 1) * row_bytes + 2 * row_bytes + 2 * row_bytes + 4 * (-(-(p + 1) // 16))
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        with torch.cuda.stream(stream):
+            r._attention(b, 0, meta[0], meta[1], 1, 1)  # warm
+            start.record(stream)
+            for _ in range(reps):
+                r._attention(b, 0, meta[0], meta[1], 1, 1)
+            end.record(stream)
+        end.synchronize()
+        ms = start.elapsed_time(end) / reps
+        total_bytes += algo
+        total_ms += ms
+        n += 1
+    per_launch_bytes = total_bytes / n
+    per_launch_ms = total_ms / n
+    achieved = per_launch_bytes / (per_launch_ms * 1e-3) / 1e9
+    return {
+        "bound": "hbm",
+        "achieved": round(achieved, 1),
+        "peak": peak_gbs,
+        "unit": "GB/s",
+        "frac": round(achieved / peak_gbs, 4),
+        "traffic": None,
+        "kernel": "cdb::decode_attn_kernel<128,4>",
+        "launch_ms": round(per_launch_ms, 4),
+        "algorithmic_bytes_per_launch": int(per_launch_bytes),
+        "launches_timed": n,
+    }
+
+
+def run_b200(args) -> None:
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+    eng, shape = build_engine(args, device)
+    prompts, max_new, depths = workload(args.seed + rank, args.requests, args.out_cap)
+    stream = eng.runner.stream
+
+    def step():
+        return eng.generate_batch(prompts, max_new_tokens=max_new, eos_token_id=None, exit_depths=depths)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # Record representative attention launch shapes (positions) from the workload for the roofline pass.
+    recorded: list[tuple[list[int], list[int]]] = []
+    orig = eng._run_recurrent
+
+    def recorder(items):
+        if len(recorded) < 400 and eng.last_stats.recurrent_batches % 5 == 0:
+            recorded.append(([it.req.slot for it in items], [it.position for it in items]))
+        return orig(items)
+
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    peak_gbs = json.loads(peaks_path.read_text())["hbm_gbs"] if peaks_path.exists() else 6650.0
+    peak_src = "measured" if peaks_path.exists() else "fallback"
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    gen_tokens = 0
+    launches0 = eng.runner.stats.kernel_launches
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        t0 = time.perf_counter()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            eng._run_recurrent = recorder
+            outs = step()
+            eng._run_recurrent = orig
+            gen_tokens += sum(len(o.generated_tokens) for o in outs)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+    dev_s = ev0.elapsed_time(ev1) / 1e3
+    wall_s = t1 - t0
+    kernel_launches = eng.runner.stats.kernel_launches - launches0
+    stats = eng.last_stats
+    if world > 1:
+        t = torch.tensor([dev_s, wall_s, float(gen_tokens)], device=device, dtype=torch.float64)
+        mx = t.clone()
+        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+        sm = t.clone()
+        torch.distributed.all_reduce(sm, op=torch.distributed.ReduceOp.SUM)
+        dev_s, wall_s, total_tokens = float(mx[0]), float(mx[1]), float(sm[2])
+    else:
+        total_tokens = float(gen_tokens)
+    if rank == 0:
+        roof = attention_roofline(eng, shape, recorded[:60], peak_gbs)
+        roof["peak_source"] = peak_src
+        prompt_bytes = sum(len(p) for p in prompts) * 4 * 3
+        line = {
+            "metric": METRIC,
+            "value": round(total_tokens / dev_s, 1),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(dev_s * 1e3 / args.steps, 2),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded lognormal lengths, uniform token ids, categorical exit depths)",
+            "config": {
+                "workload": "BASELINE config 1: Ouro-1.4B random-init, 256 concurrent requests, lognormal lengths, "
+                "replayed categorical depths (0.2,0.3,0.3,0.2), kv single, block 16, refill on",
+                "requests_per_gpu": args.requests,
+                "out_cap": args.out_cap,
+                "generated_tokens_per_step_per_gpu": gen_tokens // max(args.steps, 1),
+                "recurrent_batches": stats.recurrent_batches,
+                "coda_batches": stats.coda_batches,
+                "prefill_batches": stats.prefill_batches,
+                "mean_recurrent_batch": round(stats.mean_recurrent_batch_size, 1),
+                "exit_depth_histogram": {str(k): v for k, v in sorted(stats.exit_depth_histogram.items())},
+                "l2": "inputs larger than L2 (KV cache tens of GB, weights 2.5 GB)",
+                "cuda_graphs": not args.no_graph,
+                "parallelism": f"{world} independent request-sharded replicas (no collective)",
+            },
+            "e2e": {
+                "value": round(total_tokens / wall_s, 1),
+                "unit": UNIT,
+                "h2d_bytes_per_step": prompt_bytes,
+                "d2h_bytes_per_step": (gen_tokens // max(args.steps, 1)) * 8,
+            },
+            "gpu_launches": kernel_launches,
+            "roofline": roof,
+            "clocks": clocks.summary(),
+        }
+        if world == 1:
+            line["cpu_baseline"] = cpu_baseline(seconds=20.0)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def cpu_sample_workload():
+    """Bounded sample of the config-1 workload for the CPU oracle: first 2 requests, 4 tokens each."""
+
+    prompts, max_new, depths = workload(0, 256, 1024)
+    k, new = 2, 4
+    prompts = [p[:256] for p in prompts[:k]]
+    max_new = [new] * k
+    depths = [d[: new - 1] for d in depths[:k]]
+    return prompts, max_new, depths
+
+
+def cpu_baseline(seconds: float = 20.0) -> dict:
+    """Time the CPU restatement of the reference engine (oracle/) on this host's cores."""
+
+    from continuous_depth_batching_b200.ouro import OuroShape, random_ouro_state_dict
+    from oracle.engine import OracleConfig, OracleEngine
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    shape = OuroShape(**OURO_1P4B)
+    sd = random_ouro_state_dict(shape, seed=1234, dtype=torch.float32)
+    cfg = OracleConfig(num_blocks=1024, max_model_len=4096, synthetic_exit_replay=True, max_recurrent_steps=4)
+    eng = OracleEngine(shape, sd, cfg, torch.float32)
+    prompts, max_new, depths = cpu_sample_workload()
+    tokens, t0 = 0, time.perf_counter()
+    runs = 0
+    while True:
+        out = eng.generate(prompts, max_new, exit_depths=depths)
+        tokens += sum(len(x) for x in out)
+        runs += 1
+        if time.perf_counter() - t0 > seconds or runs >= 3:
+            break
+    dt = time.perf_counter() - t0
+    return {
+        "value": round(tokens / dt, 3),
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{runs} x generate of the first {len(prompts)} config-1 requests (prompts cut to 256 tokens), "
+        f"{max_new[0]} new tokens each, fp32 on the host CPU",
+    }
+
+
+def run_reference(args) -> None:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    t_all = []
+    vals = []
+    for i in range(args.warmup + args.steps):
+        b = cpu_baseline(seconds=5.0)
+        if i >= args.warmup:
+            vals.append(b["value"])
+            t_all.append(b)
+    v = statistics.mean(vals) if vals else 0.0
+    line = {
+        "metric": METRIC,
+        "value": round(v, 3),
+        "unit": UNIT,
+        "impl": "reference",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "BASELINE config 1 (bounded CPU prefix, see cpu_baseline.sample)"},
+        "cpu_baseline": {**t_all[-1], "value": round(v, 3)} if t_all else None,
+        "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

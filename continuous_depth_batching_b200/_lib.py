@@ -1,0 +1,113 @@
+"""ctypes binding of the C ABI in ``include/cdb_b200.h`` (``libcdb_b200.so``).
+
+The library is the only compute path: if it is missing this module raises on first use
+instead of falling back to anything else. Build it with
+``python -m continuous_depth_batching_b200.csrc.build``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_double, c_float, c_int, c_int64, c_void_p
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libcdb_b200.so"
+
+# name -> argtypes (all return int status unless listed in _RESTYPES)
+_SIGNATURES: dict[str, list] = {
+    "cdb_version": [],
+    "cdb_status_string": [c_int],
+    "cdb_attn_plan": [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p],
+    "cdb_paged_decode_attn_append": [
+        c_void_p, c_int64, c_int64, c_int64,  # qkv, stride, k_col, v_col
+        c_void_p, c_int64,  # out, out_stride
+        c_void_p, c_int, c_int64, c_int,  # kv_base, num_cache_layers, kv_rows, cache_layer
+        c_void_p, c_int64, c_void_p, c_void_p,  # block_table, stride, item_slot, item_pos
+        c_int, c_void_p, c_void_p, c_int,  # rope_mode, cos, sin, append
+        c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,  # plan_header, units, part_o, part_ml, counters
+        c_int, c_int, c_int, c_int, c_int,  # scratch_items, num_items, num_heads, head_dim, block_size
+        c_float, c_int, c_void_p, c_void_p,  # scale, num_ctas, status, stream
+    ],
+    "cdb_attn_scratch_bytes": [c_int, c_int, c_int],
+    "cdb_rope_append_kv": [
+        c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int64, c_int,
+        c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
+    ],
+    "cdb_rmsnorm": [
+        c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_float, c_void_p,
+    ],
+    "cdb_add_rmsnorm": [
+        c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
+        c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p,
+    ],
+    "cdb_silu_mul": [c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_void_p],
+    "cdb_argmax": [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
+    "cdb_embed": [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int, c_void_p, c_void_p],
+    "cdb_block_table_update": [c_void_p, c_int64, c_void_p, c_int, c_void_p],
+    "cdb_exit_kv_copy": [c_void_p, c_int, c_int64, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p],
+    "cdb_exit_hazard": [
+        c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_double, c_void_p,
+    ],
+}
+_RESTYPES = {"cdb_status_string": ctypes.c_char_p, "cdb_attn_scratch_bytes": c_int64}
+
+_LIB: ctypes.CDLL | None = None
+
+
+class CDBError(RuntimeError):
+    """A non-zero status from the CUDA library."""
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once and declare every exported symbol's signature."""
+
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not LIB_PATH.exists():
+        raise CDBError(
+            f"{LIB_PATH} is missing: build it with `python -m continuous_depth_batching_b200.csrc.build` "
+            "(the CUDA library is the only compute path; there is no fallback)"
+        )
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, args in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = _RESTYPES.get(name, c_int)
+    _LIB = lib
+    return lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGNATURES)
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load().cdb_status_string(rc).decode()
+        raise CDBError(f"{what} failed: {msg} (status {rc})")
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    """Device address of a tensor (None passes NULL)."""
+
+    return None if t is None else t.data_ptr()
+
+
+def stream_ptr(stream: torch.cuda.Stream | None = None) -> int:
+    s = torch.cuda.current_stream() if stream is None else stream
+    return s.cuda_stream
+
+
+_NO_LAUNCH = {"cdb_version", "cdb_status_string", "cdb_attn_scratch_bytes"}
+# Kernels enqueued through this binding (device work only; graph replays are counted by the runner).
+launch_count = 0
+
+
+def call(name: str, *args) -> None:
+    global launch_count
+    check(getattr(load(), name)(*args), name)
+    if name not in _NO_LAUNCH:
+        launch_count += 1

@@ -1,0 +1,412 @@
+// Row-wise fused kernels of the CDB recurrent step: the sandwich RMSNorms (with the
+// residual add, the exit-gate dot product and the hidden-bank scatter fused in), SwiGLU,
+// greedy argmax, the prelude embedding gather, device block-table edits, the last_exited
+// KV copy and the cumulative-hazard exit decision.
+//
+// All math is fp32; results are rounded to bf16 exactly where the reference's PyTorch bf16
+// ops round (each elementwise op stores a bf16 tensor), so outputs match it up to the
+// summation order of the row reductions.
+#include "cdb_common.cuh"
+
+namespace cdb {
+
+constexpr int kRowThreads = 256;
+constexpr int kMaxChunks = 6;  // rows up to 256 threads x 6 x 8 = 12288 elements
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  float t = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : 0.f;
+  if (w == 0) t = warp_sum(t);
+  if (threadIdx.x == 0) red[0] = t;
+  __syncthreads();
+  return red[0];
+}
+
+// Load up to kMaxChunks 8-element chunks of a bf16 row into fp32 registers.
+struct RowRegs {
+  float v[kMaxChunks][8];
+};
+
+__device__ __forceinline__ void load_row(const __nv_bfloat16* row, int hidden, RowRegs& r) {
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int d = (c * kRowThreads + threadIdx.x) * 8;
+    if (d < hidden) {
+      const uint4 w = *reinterpret_cast<const uint4*>(row + d);
+      r.v[c][0] = bf16lo(w.x);
+      r.v[c][1] = bf16hi(w.x);
+      r.v[c][2] = bf16lo(w.y);
+      r.v[c][3] = bf16hi(w.y);
+      r.v[c][4] = bf16lo(w.z);
+      r.v[c][5] = bf16hi(w.z);
+      r.v[c][6] = bf16lo(w.w);
+      r.v[c][7] = bf16hi(w.w);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) r.v[c][k] = 0.f;
+    }
+  }
+}
+
+__device__ __forceinline__ void store_row(__nv_bfloat16* row, int hidden, const RowRegs& r) {
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int d = (c * kRowThreads + threadIdx.x) * 8;
+    if (d < hidden) {
+      uint4 w;
+      w.x = pack_bf16x2(r.v[c][0], r.v[c][1]);
+      w.y = pack_bf16x2(r.v[c][2], r.v[c][3]);
+      w.z = pack_bf16x2(r.v[c][4], r.v[c][5]);
+      w.w = pack_bf16x2(r.v[c][6], r.v[c][7]);
+      *reinterpret_cast<uint4*>(row + d) = w;
+    }
+  }
+}
+
+// In-register OuroRMSNorm: r <- weight * bf16(r * rsqrt(mean(r^2) + eps)), all rounded to bf16.
+__device__ __forceinline__ void rms_inplace(RowRegs& r, const __nv_bfloat16* weight, int hidden, float eps,
+                                            float* red) {
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ss = fmaf(r.v[c][k], r.v[c][k], ss);
+  const float var = block_sum(ss, red) / (float)hidden;
+  const float inv = rsqrtf(var + eps);
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int d = (c * kRowThreads + threadIdx.x) * 8;
+    if (d < hidden) {
+      const uint4 w = *reinterpret_cast<const uint4*>(weight + d);
+      const float g[8] = {bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y),
+                          bf16lo(w.z), bf16hi(w.z), bf16lo(w.w), bf16hi(w.w)};
+#pragma unroll
+      for (int k = 0; k < 8; ++k) r.v[c][k] = round_bf16(g[k] * round_bf16(r.v[c][k] * inv));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kRowThreads) rmsnorm_kernel(const __nv_bfloat16* x, int64_t xs, const int32_t* x_rows,
+                                                              const __nv_bfloat16* w, __nv_bfloat16* y, int64_t ys,
+                                                              __nv_bfloat16* xc, int64_t xcs, int hidden, float eps) {
+  __shared__ float red[32];
+  const int r = blockIdx.x;
+  const int src = x_rows ? x_rows[r] : r;
+  if (src < 0) return;
+  RowRegs v;
+  load_row(x + (int64_t)src * xs, hidden, v);
+  if (xc) store_row(xc + (int64_t)r * xcs, hidden, v);
+  rms_inplace(v, w, hidden, eps, red);
+  store_row(y + (int64_t)r * ys, hidden, v);
+}
+
+__global__ void __launch_bounds__(kRowThreads) add_rmsnorm_kernel(__nv_bfloat16* x, int64_t xs, const __nv_bfloat16* a,
+                                                                  int64_t as, const __nv_bfloat16* wa,
+                                                                  const __nv_bfloat16* wn, __nv_bfloat16* y, int64_t ys,
+                                                                  const int32_t* y_rows, const __nv_bfloat16* gw,
+                                                                  const __nv_bfloat16* gb, __nv_bfloat16* gout,
+                                                                  int hidden, float eps) {
+  __shared__ float red[32];
+  const int r = blockIdx.x;
+  const int dst = y_rows ? y_rows[r] : r;
+  if (dst < 0) return;
+  RowRegs av, xv;
+  load_row(a + (int64_t)r * as, hidden, av);
+  rms_inplace(av, wa, hidden, eps, red);
+  load_row(x + (int64_t)r * xs, hidden, xv);
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) xv.v[c][k] = round_bf16(xv.v[c][k] + av.v[c][k]);
+  store_row(x + (int64_t)r * xs, hidden, xv);
+  rms_inplace(xv, wn, hidden, eps, red);
+  store_row(y + (int64_t)dst * ys, hidden, xv);
+  if (gw) {
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int d = (c * kRowThreads + threadIdx.x) * 8;
+      if (d < hidden) {
+        const uint4 w = *reinterpret_cast<const uint4*>(gw + d);
+        const float g[8] = {bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y),
+                            bf16lo(w.z), bf16hi(w.z), bf16lo(w.w), bf16hi(w.w)};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) dot = fmaf(g[k], xv.v[c][k], dot);
+      }
+    }
+    dot = block_sum(dot, red);
+    if (threadIdx.x == 0) gout[r] = f_to_bf16(dot + bf16_to_f(gb[0]));
+  }
+}
+
+__global__ void silu_mul_kernel(const __nv_bfloat16* gu, int64_t gs, __nv_bfloat16* act, int64_t as, int inter) {
+  const int r = blockIdx.y;
+  const int d = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (d >= inter) return;
+  const uint4 g = *reinterpret_cast<const uint4*>(gu + (int64_t)r * gs + d);
+  const uint4 u = *reinterpret_cast<const uint4*>(gu + (int64_t)r * gs + inter + d);
+  const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+  const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+  uint32_t ow[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float g0 = bf16lo(gw[k]), g1 = bf16hi(gw[k]);
+    const float s0 = round_bf16(g0 / (1.f + expf(-g0)));
+    const float s1 = round_bf16(g1 / (1.f + expf(-g1)));
+    ow[k] = pack_bf16x2(s0 * bf16lo(uw[k]), s1 * bf16hi(uw[k]));
+  }
+  *reinterpret_cast<uint4*>(act + (int64_t)r * as + d) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+}
+
+__device__ __forceinline__ void better(float v, int i, float& bv, int& bi) {
+  if (v > bv || (v == bv && i < bi)) {
+    bv = v;
+    bi = i;
+  }
+}
+
+__global__ void __launch_bounds__(512) argmax_kernel(const __nv_bfloat16* logits, int64_t stride, int vocab,
+                                                     int64_t* out, const int32_t* out_rows, const int32_t* token_rows,
+                                                     int32_t* token_table) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int r = blockIdx.x;
+  const __nv_bfloat16* row = logits + (int64_t)r * stride;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  if ((vocab & 7) == 0 && (stride & 7) == 0) {
+    for (int d = threadIdx.x * 8; d < vocab; d += blockDim.x * 8) {
+      const uint4 w = *reinterpret_cast<const uint4*>(row + d);
+      better(bf16lo(w.x), d, bv, bi);
+      better(bf16hi(w.x), d + 1, bv, bi);
+      better(bf16lo(w.y), d + 2, bv, bi);
+      better(bf16hi(w.y), d + 3, bv, bi);
+      better(bf16lo(w.z), d + 4, bv, bi);
+      better(bf16hi(w.z), d + 5, bv, bi);
+      better(bf16lo(w.w), d + 6, bv, bi);
+      better(bf16hi(w.w), d + 7, bv, bi);
+    }
+  } else {
+    for (int d = threadIdx.x; d < vocab; d += blockDim.x) better(bf16_to_f(row[d]), d, bv, bi);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    better(ov, oi, bv, bi);
+  }
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (lane == 0) {
+    sv[w] = bv;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (w == 0) {
+    bv = lane < (int)(blockDim.x >> 5) ? sv[lane] : -INFINITY;
+    bi = lane < (int)(blockDim.x >> 5) ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      better(ov, oi, bv, bi);
+    }
+    if (lane == 0) {
+      if (bi == 0x7fffffff) bi = 0;
+      const int orow = out_rows ? out_rows[r] : r;
+      if (orow >= 0) out[orow] = bi;
+      if (token_rows != nullptr && token_rows[r] >= 0) token_table[token_rows[r]] = bi;
+    }
+  }
+}
+
+__global__ void embed_kernel(const __nv_bfloat16* table, int hidden, int vocab, const int32_t* ids,
+                             const int32_t* id_src, const int32_t* token_table, __nv_bfloat16* out, int64_t os,
+                             const int32_t* out_rows, int32_t* status) {
+  const int r = blockIdx.x;
+  const int dst = out_rows ? out_rows[r] : r;
+  if (dst < 0) return;
+  int id = ids ? ids[r] : -1;
+  if (id < 0 && id_src != nullptr) id = token_table[id_src[r]];
+  __nv_bfloat16* o = out + (int64_t)dst * os;
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) set_error(status, CDB_ERR_INDEX);
+    for (int d = threadIdx.x; d < hidden; d += blockDim.x) o[d] = f_to_bf16(0.f);
+    return;
+  }
+  const __nv_bfloat16* src = table + (int64_t)id * hidden;
+  if ((hidden & 7) == 0) {
+    for (int d = threadIdx.x * 8; d < hidden; d += blockDim.x * 8)
+      *reinterpret_cast<uint4*>(o + d) = *reinterpret_cast<const uint4*>(src + d);
+  } else {
+    for (int d = threadIdx.x; d < hidden; d += blockDim.x) o[d] = src[d];
+  }
+}
+
+__global__ void block_table_update_kernel(int32_t* table, int64_t stride, const int32_t* edits, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  table[(int64_t)edits[3 * i] * stride + edits[3 * i + 1]] = edits[3 * i + 2];
+}
+
+__global__ void exit_kv_copy_kernel(__nv_bfloat16* kv, int64_t kv_rows, int64_t row_elems, const int32_t* rows,
+                                    const int32_t* src_layers, const int32_t* dst_layers) {
+  const int64_t row = rows[blockIdx.x];
+  const int pair = blockIdx.y;
+  const int src = src_layers[pair], dst = dst_layers[pair];
+  for (int kvsel = 0; kvsel < 2; ++kvsel) {
+    const uint4* s = reinterpret_cast<const uint4*>(kv + ((int64_t)(2 * src + kvsel) * kv_rows + row) * row_elems);
+    uint4* d = reinterpret_cast<uint4*>(kv + ((int64_t)(2 * dst + kvsel) * kv_rows + row) * row_elems);
+    for (int i = threadIdx.x; i < row_elems / 8; i += blockDim.x) d[i] = s[i];
+  }
+}
+
+__global__ void exit_hazard_kernel(const void* signal, int signal_bf16, const int32_t* slots, const int32_t* steps,
+                                   const int8_t* reset, double* cdf, double* surv, int8_t* exit_out, int n,
+                                   int min_steps, double threshold) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const int s = slots[r];
+  if (s < 0) {
+    exit_out[r] = 0;
+    return;
+  }
+  if (reset != nullptr && reset[r]) {
+    cdf[s] = 0.0;
+    surv[s] = 1.0;
+  }
+  float h;
+  if (signal_bf16) {
+    const float x = bf16_to_f(static_cast<const __nv_bfloat16*>(signal)[r]);
+    h = round_bf16(1.f / (1.f + expf(-x)));
+  } else {
+    const float x = static_cast<const float*>(signal)[r];
+    h = 1.f / (1.f + expf(-x));
+  }
+  const double hd = (double)h;
+  const double c = cdf[s] + hd * surv[s];
+  cdf[s] = c;
+  surv[s] = surv[s] * (1.0 - hd);
+  exit_out[r] = (steps[r] + 1 >= min_steps && c >= threshold) ? 1 : 0;
+}
+
+static inline int check_launch() { return cudaPeekAtLastError() == cudaSuccess ? CDB_OK : CDB_ERR_CUDA; }
+
+}  // namespace cdb
+
+using namespace cdb;
+
+extern "C" int cdb_version(void) { return 100; }
+
+extern "C" const char* cdb_status_string(int status) {
+  switch (status) {
+    case CDB_OK:
+      return "ok";
+    case CDB_ERR_INVALID_ARGUMENT:
+      return "invalid argument";
+    case CDB_ERR_UNSUPPORTED:
+      return "unsupported shape";
+    case CDB_ERR_CUDA:
+      return "CUDA launch error";
+    case CDB_ERR_DEVICE_TIMEOUT:
+      return "device-side wait ran out of iterations";
+    case CDB_ERR_TMA_ENCODE:
+      return "TMA tensor map encoding failed";
+    case CDB_ERR_INDEX:
+      return "device-side index out of range";
+    default:
+      return "unknown status";
+  }
+}
+
+extern "C" int cdb_rmsnorm(const void* x, int64_t x_stride, const int32_t* x_rows, const void* weight, void* y,
+                           int64_t y_stride, void* x_copy, int64_t x_copy_stride, int num_rows, int hidden, float eps,
+                           void* stream) {
+  if (hidden % 8 != 0 || hidden > kRowThreads * kMaxChunks * 8 || num_rows < 0) return CDB_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return CDB_OK;
+  rmsnorm_kernel<<<num_rows, kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), x_stride, x_rows, static_cast<const __nv_bfloat16*>(weight),
+      static_cast<__nv_bfloat16*>(y), y_stride, static_cast<__nv_bfloat16*>(x_copy), x_copy_stride, hidden, eps);
+  return check_launch();
+}
+
+extern "C" int cdb_add_rmsnorm(void* x, int64_t x_stride, const void* a, int64_t a_stride, const void* w_a,
+                               const void* w_next, void* y, int64_t y_stride, const int32_t* y_rows,
+                               const void* gate_w, const void* gate_b, void* gate_out, int num_rows, int hidden,
+                               float eps, void* stream) {
+  if (hidden % 8 != 0 || hidden > kRowThreads * kMaxChunks * 8 || num_rows < 0) return CDB_ERR_INVALID_ARGUMENT;
+  if (gate_w != nullptr && (gate_b == nullptr || gate_out == nullptr)) return CDB_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return CDB_OK;
+  add_rmsnorm_kernel<<<num_rows, kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<__nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(a), a_stride,
+      static_cast<const __nv_bfloat16*>(w_a), static_cast<const __nv_bfloat16*>(w_next),
+      static_cast<__nv_bfloat16*>(y), y_stride, y_rows, static_cast<const __nv_bfloat16*>(gate_w),
+      static_cast<const __nv_bfloat16*>(gate_b), static_cast<__nv_bfloat16*>(gate_out), hidden, eps);
+  return check_launch();
+}
+
+extern "C" int cdb_silu_mul(const void* gu, int64_t gu_stride, void* act, int64_t act_stride, int num_rows, int inter,
+                            void* stream) {
+  if (inter % 8 != 0 || num_rows < 0) return CDB_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return CDB_OK;
+  const int threads = 128;
+  dim3 grid((inter / 8 + threads - 1) / threads, num_rows);
+  silu_mul_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(gu), gu_stride, static_cast<__nv_bfloat16*>(act), act_stride, inter);
+  return check_launch();
+}
+
+extern "C" int cdb_argmax(const void* logits, int64_t stride, int num_rows, int vocab, int64_t* out,
+                          const int32_t* out_rows, const int32_t* token_rows, int32_t* token_table, void* stream) {
+  if (vocab <= 0 || num_rows < 0 || (token_rows != nullptr && token_table == nullptr)) return CDB_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return CDB_OK;
+  argmax_kernel<<<num_rows, 512, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const __nv_bfloat16*>(logits),
+                                                                         stride, vocab, out, out_rows, token_rows, token_table);
+  return check_launch();
+}
+
+extern "C" int cdb_embed(const void* table, int hidden, int vocab, const int32_t* ids, const int32_t* id_src,
+                         const int32_t* token_table, void* out, int64_t out_stride, const int32_t* out_rows,
+                         int num_rows, int32_t* status, void* stream) {
+  if (hidden <= 0 || vocab <= 0 || num_rows < 0 || (ids == nullptr && id_src == nullptr)) return CDB_ERR_INVALID_ARGUMENT;
+  if (id_src != nullptr && token_table == nullptr) return CDB_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return CDB_OK;
+  embed_kernel<<<num_rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(table), hidden, vocab, ids, id_src, token_table,
+      static_cast<__nv_bfloat16*>(out), out_stride, out_rows, status);
+  return check_launch();
+}
+
+extern "C" int cdb_block_table_update(int32_t* table, int64_t stride, const int32_t* edits, int num_edits,
+                                      void* stream) {
+  if (num_edits < 0) return CDB_ERR_INVALID_ARGUMENT;
+  if (num_edits == 0) return CDB_OK;
+  block_table_update_kernel<<<(num_edits + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(table, stride,
+                                                                                                   edits, num_edits);
+  return check_launch();
+}
+
+extern "C" int cdb_exit_kv_copy(void* kv_base, int num_cache_layers, int64_t kv_rows, int num_kv_heads, int head_dim,
+                                const int32_t* rows, int num_rows, const int32_t* src_layers,
+                                const int32_t* dst_layers, int num_pairs, void* stream) {
+  const int64_t row_elems = (int64_t)num_kv_heads * head_dim;
+  if (row_elems % 8 != 0 || num_rows < 0 || num_pairs < 0 || num_cache_layers <= 0) return CDB_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0 || num_pairs == 0) return CDB_OK;
+  dim3 grid(num_rows, num_pairs);
+  exit_kv_copy_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<__nv_bfloat16*>(kv_base), kv_rows, row_elems, rows, src_layers, dst_layers);
+  return check_launch();
+}
+
+extern "C" int cdb_exit_hazard(const void* signal, int signal_bf16, const int32_t* slots, const int32_t* steps,
+                               const int8_t* reset, double* cdf, double* surv, int8_t* exit_out, int num_rows,
+                               int min_steps, double threshold, void* stream) {
+  if (num_rows < 0) return CDB_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return CDB_OK;
+  exit_hazard_kernel<<<(num_rows + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      signal, signal_bf16, slots, steps, reset, cdf, surv, exit_out, num_rows, min_steps, threshold);
+  return check_launch();
+}

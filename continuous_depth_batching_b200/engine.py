@@ -1,0 +1,932 @@
+"""``ContinuousDepthBatchingEngine``: the reference's engine surface over the B200 runner.
+
+Public surface (kept verbatim from ``continuous_depth_batching/continuous_api.py``):
+``from_model(model, cdb_config, *, dtype=None, model_adapter=None)`` (``:275-376``),
+``generate_batch(input_ids, *, max_new_tokens, eos_token_id, stop_sequences=None, warmup=True,
+model_kwargs=None, exit_depths=None, arrival_offsets_s=None, record_token_times=False,
+record_queue_samples=False)`` (``:379-452``) and ``last_stats`` (``:114-228``).
+
+Scheduling follows the reference's synchronous decision timing exactly, so every launch, block
+table and per-step depth assignment is bit-identical to the reference run on the same inputs:
+
+* refill loop ``:503-606`` with ``CDBScheduler.schedule_next`` (``scheduler.py:101-140``):
+  coda when >= ``min_coda_batch_size`` -> prefill when admitted (``scheduler_base.py:129-201``)
+  -> recurrent FIFO (slot-homogeneous under multi-slot KV, ``scheduler.py:322-346``) -> coda flush;
+* recurrent routing ``:1090-1203``: exits go to the coda queue, survivors return to the queue
+  head in order; coda re-entry ``:1378-1448`` puts each successor at the queue head;
+* no-refill lockstep waves ``:608-944``; ``last_exited`` copy-on-exit ``:1205-1245``.
+
+What differs is where the work runs. Token ids stay on the device (the coda's argmax feeds the
+next prelude through the device token table), block tables live on the device and are patched
+with new block ids only, and the host never waits for the device unless a decision needs device
+data (a live exit gate, EOS or stop sequences): with replayed exits it schedules ahead while the
+GPU executes, and reads every sampled token back once at the end.
+"""
+
+from __future__ import annotations
+
+import time
+from collections import Counter, OrderedDict, deque
+from dataclasses import dataclass, field
+from enum import IntEnum
+
+import torch
+
+from .config import ContinuousDepthBatchingConfig
+from .kv_cache import copies_exit_kv, kv_slot_for_step
+from .ouro import OuroShape
+from .runner import OuroRunner
+
+
+class CacheFullError(RuntimeError):
+    """Raised when the KV cache cannot place any work and nothing can relieve the pressure."""
+
+
+class RequestStatus(IntEnum):
+    PENDING = 0
+    PREFILLING = 1
+    DECODING = 2
+    FINISHED = 3
+
+
+@dataclass
+class GenerationOutput:
+    """Mirror of the reference ``GenerationOutput`` (``continuous_batching/requests.py:44-70``)."""
+
+    request_id: str
+    prompt_ids: list[int] = field(default_factory=list)
+    generated_tokens: list[int] = field(default_factory=list)
+    status: RequestStatus = RequestStatus.PENDING
+    created_time: float = field(default_factory=time.perf_counter)
+    lifespan: tuple[float, float] = (-1, -1)
+    first_token_time: float = -1.0
+    token_ready_times: list[float] = field(default_factory=list)
+    exit_depths: list[int] = field(default_factory=list)
+
+    def is_finished(self) -> bool:
+        return self.status == RequestStatus.FINISHED
+
+
+@dataclass
+class ContinuousDepthBatchingStats:
+    """Runtime counters (the reference ``ContinuousDepthBatchingStats`` fields this engine produces)."""
+
+    prefill_batches: int = 0
+    prefill_requests: int = 0
+    recurrent_batches: int = 0
+    coda_batches: int = 0
+    recurrent_steps: int = 0
+    coda_tokens: int = 0
+    generated_tokens: int = 0
+    prefill_recurrent_steps: int = 0
+    prefill_coda_tokens: int = 0
+    fixed_depth_recurrent_steps: int = 0
+    exit_depth_histogram: Counter = field(default_factory=Counter)
+    recurrent_step_histogram: Counter = field(default_factory=Counter)
+    mixed_recurrent_batches: int = 0
+    mixed_recurrent_depth_histogram: Counter = field(default_factory=Counter)
+    max_mixed_depths_per_batch: int = 0
+    scheduler_refills: int = 0
+    max_depth_queue_size: int = 0
+    recurrent_graph_hits: int = 0
+    recurrent_graph_captures: int = 0
+    scheduler_ticks: int = 0
+    prefill_tokens: int = 0
+    exit_kv_copies: int = 0
+    host_syncs: int = 0
+    kv_peak_blocks: int = 0
+
+    @property
+    def skipped_recurrent_steps(self) -> int:
+        return max(0, self.fixed_depth_recurrent_steps - self.recurrent_steps)
+
+    @property
+    def mean_recurrent_batch_size(self) -> float:
+        return self.recurrent_steps / self.recurrent_batches if self.recurrent_batches else 0.0
+
+    @property
+    def mean_coda_batch_size(self) -> float:
+        return self.coda_tokens / self.coda_batches if self.coda_batches else 0.0
+
+
+class _Req:
+    __slots__ = (
+        "idx", "request_id", "prompt", "max_new", "depths", "cursor", "status", "remaining", "chunk",
+        "position", "allocated", "generated", "slot", "log_base", "exit_depths", "eos", "stops",
+        "created", "start", "finish", "first_token", "token_times", "record_times", "pending_token",
+    )
+
+    def __init__(self, idx: int, prompt: list[int], max_new: int, depths: list[int], eos: set[int], stops, rec: bool):
+        self.idx = idx
+        self.request_id = f"request-{idx}"
+        self.prompt = prompt
+        self.max_new = max_new
+        self.depths = depths
+        self.cursor = 0
+        self.status = RequestStatus.PENDING
+        self.remaining = list(prompt)
+        self.chunk: list[int] = []
+        self.position = 0
+        self.allocated = 0
+        self.generated = 0
+        self.slot = -1
+        self.log_base = 0
+        self.exit_depths: list[int] = []
+        self.eos = eos
+        self.stops = stops
+        self.created = time.perf_counter()
+        self.start = -1.0
+        self.finish = -1.0
+        self.first_token = -1.0
+        self.token_times: list[float] = []
+        self.record_times = rec
+        self.pending_token = -1
+
+    def next_depth(self) -> int | None:
+        if not self.depths:
+            return None
+        if self.cursor >= len(self.depths):
+            raise RuntimeError(f"Request {self.request_id}: synthetic exit-depth schedule exhausted")
+        d = self.depths[self.cursor]
+        self.cursor += 1
+        return d
+
+
+class _Item:
+    __slots__ = ("req", "position", "step", "depth", "hidden", "token")
+
+    def __init__(self, req: _Req, position: int, depth: int | None, hidden: int, token: int):
+        self.req = req
+        self.position = position
+        self.step = 0
+        self.depth = depth
+        self.hidden = hidden
+        self.token = token
+
+
+class ContinuousDepthBatchingEngine:
+    """Continuous depth batching over the B200 CUDA library (one engine per GPU)."""
+
+    def __init__(self, model, cdb_config: ContinuousDepthBatchingConfig, runner: OuroRunner, shape: OuroShape):
+        self.model = model
+        self.cdb_config = cdb_config
+        self.runner = runner
+        self.shape = shape
+        self.last_stats = ContinuousDepthBatchingStats()
+        self.record_trace = False
+        self.launch_trace: list[dict] = []
+        self.coda_logits: list[torch.Tensor] = []
+        self.keep_coda_logits = False
+
+    # ------------------------------------------------------------------ construction
+    @classmethod
+    def from_model(
+        cls,
+        model,
+        cdb_config: ContinuousDepthBatchingConfig,
+        *,
+        dtype: torch.dtype | None = None,
+        model_adapter=None,
+        device: torch.device | str | None = None,
+    ) -> ContinuousDepthBatchingEngine:
+        """Build an engine for an Ouro causal LM given by its parameters (reference names).
+
+        ``model`` is the reference's ``OuroForCausalLM`` or any module with its state-dict layout
+        (e.g. :class:`~.ouro.OuroForCausalLM`). Weights are packed to bf16 on ``device``
+        (default: the model's device if CUDA, else ``cuda``). ``dtype`` other than bf16 is rejected:
+        the kernels compute in bf16 with fp32 accumulation.
+        """
+
+        if model_adapter is not None:
+            raise NotImplementedError("custom model adapters are not supported by the B200 engine")
+        if dtype not in (None, torch.bfloat16):
+            raise NotImplementedError(f"the B200 kernels run bf16; got dtype={dtype}")
+        config = getattr(model, "config", None)
+        if config is None or getattr(config, "model_type", None) not in ("ouro",):
+            raise TypeError(f"Continuous depth batching requires an Ouro model; got {type(model)!r}")
+        cfg = cdb_config.get_resolved()
+        shape = OuroShape.from_config(config)
+        shape = OuroShape(**{**shape.__dict__, "total_ut_steps": cfg.max_recurrent_steps})
+        if shape.num_key_value_heads != shape.num_attention_heads:
+            raise NotImplementedError("the paged decode kernel serves MHA (num_key_value_heads == num_attention_heads)")
+        if device is None:
+            p = next(model.parameters())
+            device = p.device if p.device.type == "cuda" else torch.device("cuda")
+        device = torch.device(device)
+        if device.type == "cuda" and device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        if cfg.num_blocks is None:
+            cfg.num_blocks = _auto_num_blocks(shape, cfg, device)
+        state = {k: v for k, v in model.state_dict().items()}
+        runner = OuroRunner(
+            shape,
+            state,
+            device=device,
+            kv_policy=cfg.kv_policy,
+            kv_slots_per_layer=cfg.kv_slots_per_layer,
+            num_blocks=cfg.num_blocks,
+            block_size=cfg.block_size,
+            max_model_len=cfg.max_model_len,
+            max_num_seqs=cfg.max_num_seqs,
+            max_num_batched_tokens=cfg.max_num_batched_tokens,
+            use_cuda_graph=cfg.use_cuda_graph,
+        )
+        return cls(model, cfg, runner, shape)
+
+    # ------------------------------------------------------------------ public API
+    @torch.no_grad()
+    def generate_batch(
+        self,
+        input_ids: list[list[int]],
+        *,
+        max_new_tokens: int | list[int],
+        eos_token_id: int | list[int] | None,
+        stop_sequences: list[list[int]] | None = None,
+        warmup: bool = True,
+        model_kwargs: dict | None = None,
+        exit_depths: list[list[int]] | None = None,
+        arrival_offsets_s: list[float] | None = None,
+        record_token_times: bool = False,
+        record_queue_samples: bool = False,
+        forced_tokens: list[list[int]] | None = None,
+    ) -> list[GenerationOutput]:
+        """Generate from tokenized prompts with decode-time CDB (see the module docstring).
+
+        ``forced_tokens`` (parity harness) continues each request with the given tokens instead of
+        its own samples; the engine still records its own argmax at every position.
+        """
+
+        del warmup, record_queue_samples
+        cfg = self.cdb_config
+        self._validate(input_ids, max_new_tokens, exit_depths, model_kwargs)
+        if isinstance(max_new_tokens, int):
+            max_new_tokens = [max_new_tokens] * len(input_ids)
+        too_long = [i for i, p in enumerate(input_ids) if len(p) >= cfg.max_model_len]
+        if too_long:
+            raise ValueError(f"{len(too_long)} prompt(s) have length >= max_model_len ({cfg.max_model_len})")
+        caps = [min(m, cfg.max_model_len - len(p)) for m, p in zip(max_new_tokens, input_ids, strict=True)]
+        eos = set()
+        if eos_token_id is not None:
+            for t in [eos_token_id] if isinstance(eos_token_id, int) else eos_token_id:
+                if t >= 0:
+                    eos.add(int(t))
+        stops = [list(s) for s in stop_sequences] if stop_sequences else []
+        self._content_finish = bool(eos or stops)
+        self._forced = forced_tokens
+        self._gate_live = cfg.exit_threshold is not None and (
+            model_kwargs is None or model_kwargs.get("use_early_exit_gate", True)
+        )
+        reqs: list[_Req] = []
+        base = 0
+        for i, (p, m) in enumerate(zip(input_ids, caps, strict=True)):
+            r = _Req(i, list(p), m, list(exit_depths[i]) if exit_depths else [], eos, stops, record_token_times)
+            r.log_base = base
+            base += m
+            reqs.append(r)
+        self.runner.reset(max(base, 1))
+        self._reset_state()
+        self._log_total = base
+        arrivals = None
+        if arrival_offsets_s is None:
+            for r in reqs:
+                self.waiting[r.idx] = r
+        else:
+            if len(arrival_offsets_s) != len(reqs):
+                raise ValueError("arrival_offsets_s needs one offset per request")
+            arrivals = deque(sorted(zip(arrival_offsets_s, range(len(reqs))), key=lambda x: (x[0], x[1])))
+        self._reqs = reqs
+        self._t0 = time.perf_counter()
+        if cfg.refill:
+            self._refill_loop(arrivals)
+        else:
+            self._no_refill_loop(arrivals)
+        tokens = self.runner.read_tokens(base) if base else []
+        self.runner.check_status()
+        outs = []
+        for r in reqs:
+            gen = tokens[r.log_base : r.log_base + r.generated]
+            outs.append(
+                GenerationOutput(
+                    request_id=r.request_id,
+                    prompt_ids=r.prompt,
+                    generated_tokens=gen,
+                    status=r.status,
+                    created_time=r.created,
+                    lifespan=(r.start, r.finish),
+                    first_token_time=r.first_token,
+                    token_ready_times=r.token_times,
+                    exit_depths=r.exit_depths,
+                )
+            )
+        st = self.last_stats
+        st.generated_tokens = sum(len(o.generated_tokens) for o in outs)
+        st.scheduler_refills = self.refills
+        st.max_depth_queue_size = self.max_queue
+        st.recurrent_graph_hits = self.runner.stats.recurrent_graph_hits
+        st.recurrent_graph_captures = self.runner.stats.recurrent_graph_captures
+        st.fixed_depth_recurrent_steps = st.coda_tokens * cfg.max_recurrent_steps
+        st.kv_peak_blocks = self.runner.pool.pool.peak
+        return outs
+
+    # ------------------------------------------------------------------ state
+    def _reset_state(self) -> None:
+        cfg = self.cdb_config
+        self.last_stats = ContinuousDepthBatchingStats()
+        self.launch_trace = []
+        self.coda_logits = []
+        self.waiting: OrderedDict[int, _Req] = OrderedDict()
+        self.active: OrderedDict[int, _Req] = OrderedDict()
+        self.in_flight: set[int] = set()
+        self.ready: deque[_Item] = deque()
+        self.coda_q: deque[_Item] = deque()
+        self.backlog: list[tuple[_Item, int]] = []
+        self.refills = 0
+        self.max_queue = 0
+        self.free_slots = list(range(cfg.max_num_seqs - 1, -1, -1))
+        self.free_hidden = list(range(self.runner.bank_slots - 1, -1, -1))
+        self.pool = self.runner.pool.pool
+        self.max_num_seqs = cfg.max_num_seqs
+        self.min_free = max(1, cfg.max_num_seqs // 8) if cfg.min_free_slots is None else min(cfg.min_free_slots, cfg.max_num_seqs)
+        self.safety = 0.0 if cfg.kv_pressure_mode == "reserve" else cfg.safety_margin
+        self.width = cfg.decode_block_table_width()
+        self.slots = cfg.kv_slots_per_layer
+        self.steps = cfg.max_recurrent_steps
+
+    def _slot_of_step(self, step: int) -> int:
+        return kv_slot_for_step(step, policy=self.cdb_config.kv_policy, slots_per_layer=self.slots)
+
+    # ------------------------------------------------------------------ block allocation
+    def _alloc(self, r: _Req, n: int) -> bool:
+        if n <= 0:
+            return True
+        if not self.pool.allocate(r.idx, r.slot, n):
+            return False
+        r.allocated += n
+        return True
+
+    def _alloc_if_needed(self, r: _Req, n_next: int) -> bool:
+        bs = self.cdb_config.block_size
+        if r.allocated * bs - r.position < n_next:
+            return self._alloc(r, -(-(r.position + n_next) // bs) - r.allocated)
+        return True
+
+    def _alloc_one_decode(self, r: _Req) -> bool:
+        bs = self.cdb_config.block_size
+        if r.allocated * bs - r.position >= 1 and r.allocated > 0:
+            return True
+        return self._alloc(r, -(-(r.position + 1) // bs) - r.allocated)
+
+    # ------------------------------------------------------------------ request lifecycle
+    def _retire(self, r: _Req) -> None:
+        r.status = RequestStatus.FINISHED
+        r.finish = time.perf_counter()
+        self.pool.release(r.idx)
+        self.active.pop(r.idx, None)
+        self.in_flight.discard(r.idx)
+        self.free_slots.append(r.slot)
+
+    def _record_token(self, r: _Req) -> bool:
+        """Count one sampled token; True when the request is finished (length, EOS or stop)."""
+
+        now = time.perf_counter()
+        if r.first_token < 0:
+            r.first_token = now
+        if r.record_times:
+            r.token_times.append(now)
+        r.generated += 1
+        if r.generated >= r.max_new:
+            return True
+        if self._content_finish:
+            tok = r.pending_token
+            if tok in r.eos:
+                return True
+            if r.stops:
+                gen = self._host_tokens(r)
+                for s in r.stops:
+                    if s and len(gen) >= len(s) and gen[-len(s):] == s:
+                        return True
+        return False
+
+    def _host_tokens(self, r: _Req) -> list[int]:
+        return self.runner.token_log[r.log_base : r.log_base + r.generated].cpu().tolist()
+
+    def _next_token_id(self, r: _Req) -> int:
+        """Host-known input id of the request's next decode token, or -1 (device token table)."""
+
+        if self._forced is not None:
+            return int(self._forced[r.idx][r.generated - 1])
+        return -1
+
+    def _stage_decode(self, r: _Req) -> _Item:
+        if not self._alloc_one_decode(r):
+            raise CacheFullError(
+                f"KV cache full staging a decode block for request {r.request_id}; the B200 engine runs "
+                "without preemption: increase num_blocks or reduce load"
+            )
+        hidden = self.free_hidden.pop()
+        return _Item(r, r.position, r.next_depth(), hidden, self._next_token_id(r))
+
+    def _prelude(self, items: list[_Item]) -> None:
+        if items:
+            self.runner.prelude([it.token for it in items], [it.req.slot for it in items], [it.hidden for it in items])
+
+    def _enqueue(self, item: _Item, front: bool = False) -> None:
+        self.in_flight.add(item.req.idx)
+        if item.step == 0 and self.ready:
+            self.refills += 1
+        if front:
+            self.ready.appendleft(item)
+        else:
+            self.ready.append(item)
+        if len(self.ready) > self.max_queue:
+            self.max_queue = len(self.ready)
+
+    def _enqueue_front(self, items: list[_Item]) -> None:
+        for it in reversed(items):
+            self._enqueue(it, front=True)
+
+    # ------------------------------------------------------------------ admission
+    def _has_pending(self) -> bool:
+        return bool(self.coda_q or self.ready or self.active or self.waiting)
+
+    def _has_decode_work(self) -> bool:
+        return any(r.status == RequestStatus.DECODING for r in self.active.values())
+
+    def _admit_prefill(self) -> bool:
+        return not self._has_decode_work() or self.pool.num_free > self.safety * self.cdb_config.num_blocks
+
+    def _reserved_peak(self, r: _Req) -> int:
+        total = min(len(r.prompt) + r.max_new, self.cdb_config.max_model_len)
+        return -(-total // self.cdb_config.block_size)
+
+    def _prefill_candidates(self) -> list[_Req]:
+        prefilling = [r for r in self.active.values() if r.status == RequestStatus.PREFILLING and r.idx not in self.in_flight]
+        free_res = max(0, self.max_num_seqs - len(self.active))
+        admissible = []
+        for key in self.waiting:
+            if len(admissible) >= free_res:
+                break
+            admissible.append(self.waiting[key])
+        if self.cdb_config.kv_pressure_mode == "reserve":
+            committed = sum(self._reserved_peak(r) for r in self.active.values())
+            kept = []
+            for r in admissible:
+                need = self._reserved_peak(r)
+                if committed + need > self.cdb_config.num_blocks:
+                    break
+                committed += need
+                kept.append(r)
+            admissible = kept
+        cands = prefilling + admissible
+        if not cands:
+            return []
+        if any(r.status == RequestStatus.PREFILLING for r in cands):
+            return cands
+        return cands if free_res >= self.min_free else []
+
+    def _schedule_prefill(self):
+        """``CDBScheduler.schedule_prefill_batch`` (``scheduler.py:190-320``)."""
+
+        cands = self._prefill_candidates()
+        if not cands:
+            return None
+        cfg = self.cdb_config
+        bs = cfg.block_size
+        token_budget = cfg.max_num_batched_tokens
+        cache_budget = cfg.num_blocks * bs
+        margin = self.safety * cfg.num_blocks
+        fast = True
+        out = []
+        for r in cands:
+            n_free = self.pool.num_free
+            if n_free < margin and out:
+                break
+            toks = r.remaining
+            qlen = min(len(toks), token_budget)
+            if qlen == 0:
+                continue
+            eligible = qlen == 1 and r.position < self.width * bs
+            read_needed = r.position
+            if not (fast and eligible) and cache_budget < read_needed:
+                continue
+            if r.status == RequestStatus.PENDING and r.slot < 0:
+                # A resident slot (block-table row) is bound at admission; undone if allocation fails.
+                r.slot = self.free_slots.pop()
+                bound_here = True
+            else:
+                bound_here = False
+            if not self._alloc_if_needed(r, qlen):
+                if bound_here:
+                    self.free_slots.append(r.slot)
+                    r.slot = -1
+                if n_free == 0 and r.idx in self.waiting:
+                    break
+                continue
+            past = r.position
+            if len(toks) <= qlen:
+                if r.status == RequestStatus.PENDING:
+                    self.active[r.idx] = r
+                    r.start = time.perf_counter()
+                r.chunk = toks
+                r.remaining = []
+                r.status = RequestStatus.DECODING
+            else:
+                if r.status == RequestStatus.PENDING:
+                    self.active[r.idx] = r
+                    r.start = time.perf_counter()
+                    r.status = RequestStatus.PREFILLING
+                r.remaining = toks[qlen:]
+                r.chunk = toks[:qlen]
+            self.in_flight.add(r.idx)
+            qlen = len(r.chunk)
+            fast = fast and qlen == 1 and r.position < self.width * bs
+            token_budget -= qlen
+            cache_budget -= read_needed
+            out.append((r, past, qlen, not r.remaining))
+            self.waiting.pop(r.idx, None)
+            if token_budget == 0 or (cache_budget <= 0 and not fast):
+                break
+        return out or None
+
+    # ------------------------------------------------------------------ launches
+    def _run_prefill(self, batch) -> list[_Req]:
+        st = self.last_stats
+        st.prefill_batches += 1
+        st.prefill_requests += len(batch)
+        ids, slots, pos, logit_rows, log_rows, req_slots, sampled = [], [], [], [], [], [], []
+        for r, past, qlen, has in batch:
+            ids.extend(r.chunk)
+            slots.extend([r.slot] * qlen)
+            pos.extend(range(past, past + qlen))
+            r.position = past + qlen
+            if has:
+                logit_rows.append(len(ids) - 1)
+                log_rows.append(r.log_base + r.generated)
+                req_slots.append(r.slot)
+                sampled.append(r)
+        st.prefill_tokens += len(ids)
+        st.prefill_recurrent_steps += len(ids) * self.steps
+        if self.record_trace:
+            bs = self.cdb_config.block_size
+            self.launch_trace.append(
+                {
+                    "kind": "prefill",
+                    "items": [[r.idx, past, qlen, int(has)] for r, past, qlen, has in batch],
+                    "blocks": [list(self.pool.tables[r.idx][: -(-r.position // bs)]) for r, *_ in batch],
+                }
+            )
+        self.runner.prefill(
+            ids, slots, pos, logit_rows, log_rows, req_slots, [self._slot_of_step(s) for s in range(self.steps)]
+        )
+        st.prefill_coda_tokens += len(sampled)
+        if self._content_finish and sampled:
+            self._sync_tokens(sampled)
+        return sampled
+
+    def _sync_tokens(self, reqs: list[_Req]) -> None:
+        self.last_stats.host_syncs += 1
+        self.runner.stream.synchronize()
+        for r in reqs:
+            r.pending_token = int(self.runner.token_log[r.log_base + r.generated].item())
+
+    def _run_recurrent(self, items: list[_Item]) -> list[bool] | None:
+        st = self.last_stats
+        kv_slot = self._slot_of_step(items[0].step)
+        if self.record_trace:
+            bs = self.cdb_config.block_size
+            self.launch_trace.append(
+                {
+                    "kind": "recurrent",
+                    "items": [[it.req.idx, it.position, it.step] for it in items],
+                    "blocks": [list(self.pool.tables[it.req.idx][: -(-(it.position + 1) // bs)]) for it in items],
+                }
+            )
+        self.runner.recurrent(
+            [it.req.slot for it in items], [it.position for it in items], [it.hidden for it in items], kv_slot,
+            self._gate_live,
+        )
+        st.recurrent_batches += 1
+        st.recurrent_steps += len(items)
+        st.mixed_recurrent_batches += 1
+        depths = Counter(it.step for it in items)
+        st.max_mixed_depths_per_batch = max(st.max_mixed_depths_per_batch, len(depths))
+        for k, v in depths.items():
+            st.mixed_recurrent_depth_histogram[k] += v
+        if not self._gate_live:
+            return None
+        return self._live_decisions(items)
+
+    def _live_decisions(self, items: list[_Item]) -> list[bool]:
+        """Cumulative-hazard decisions (``ExitPolicy.should_exit``, ``exit_policy.py:150-169``) on device."""
+
+        self.last_stats.host_syncs += 1
+        r = self.runner
+        cfg = self.cdb_config
+        n = len(items)
+        meta = r.upload([[it.hidden for it in items], [it.step for it in items], [int(it.step == 0) for it in items]])
+        meta = meta.view(3, n)
+        if not hasattr(self, "_hz"):
+            self._hz = (
+                torch.zeros(r.bank_slots, dtype=torch.float64, device=r.device),
+                torch.ones(r.bank_slots, dtype=torch.float64, device=r.device),
+                torch.zeros(cfg.max_num_seqs, dtype=torch.int8, device=r.device),
+            )
+        cdf, surv, flags = self._hz
+        from . import _lib
+
+        with torch.cuda.stream(r.stream):
+            reset = meta[2].to(torch.int8)
+            _lib.call(
+                "cdb_exit_hazard", _lib.ptr(r.gate_out), 1, _lib.ptr(meta[0]), _lib.ptr(meta[1]), _lib.ptr(reset),
+                _lib.ptr(cdf), _lib.ptr(surv), _lib.ptr(flags), n, cfg.min_recurrent_steps, float(cfg.exit_threshold),
+                r.stream.cuda_stream,
+            )
+            host = flags[:n].cpu()
+        return [bool(x) for x in host.tolist()]
+
+    def _should_exit(self, it: _Item, step: int, live: list[bool] | None, i: int) -> bool:
+        if step == self.steps - 1:
+            return True
+        if it.depth is not None:
+            return step >= it.depth
+        if live is None:
+            return False
+        return live[i]
+
+    def _record_exit(self, it: _Item, step: int) -> None:
+        it.req.exit_depths.append(step)
+        self.last_stats.exit_depth_histogram[step] += 1
+        if copies_exit_kv(self.cdb_config.kv_policy) and step < self.steps - 1:
+            self.backlog.append((it, step))
+
+    def _flush_exit_copies(self) -> None:
+        if not self.backlog:
+            return
+        backlog, self.backlog = self.backlog, []
+        by_step: dict[int, list[_Item]] = {}
+        for it, step in backlog:
+            by_step.setdefault(step, []).append(it)
+        bs, L = self.cdb_config.block_size, self.shape.num_hidden_layers
+        for step, items in sorted(by_step.items()):
+            rows = [self.pool.tables[it.req.idx][it.position // bs] * bs + it.position % bs for it in items]
+            src = self._slot_of_step(step)
+            pairs = [(src * L + l, t * L + l) for l in range(L) for t in range(src + 1, self.slots)]
+            self.runner.exit_kv_copy(rows, pairs)
+            self.last_stats.exit_kv_copies += len(rows)
+
+    def _run_coda(self, items: list[_Item]) -> None:
+        st = self.last_stats
+        if self.record_trace:
+            self.launch_trace.append({"kind": "coda", "items": [[it.req.idx, it.position, it.step] for it in items]})
+        logits = self.runner.coda(
+            [it.hidden for it in items],
+            [it.req.log_base + it.req.generated for it in items],
+            [it.req.slot for it in items],
+            keep_logits=self.keep_coda_logits,
+        )
+        if logits is not None:
+            self.coda_logits.append(logits)
+        st.coda_batches += 1
+        st.coda_tokens += len(items)
+        if self._content_finish:
+            self._sync_tokens([it.req for it in items])
+
+    # ------------------------------------------------------------------ consumption
+    def _consume_prefill(self, sampled: list[_Req], stage: bool) -> None:
+        new_items = []
+        for r in sampled:
+            if r.status == RequestStatus.FINISHED:
+                continue
+            if self._record_token(r):
+                self._retire(r)
+                continue
+            if stage:
+                new_items.append(self._stage_decode(r))
+        self._prelude(new_items)
+        for it in new_items:
+            self._enqueue(it)
+
+    def _consume_coda(self, items: list[_Item], stage: bool) -> None:
+        new_items = []
+        for it in items:
+            r = it.req
+            self.free_hidden.append(it.hidden)
+            if r.status == RequestStatus.FINISHED:
+                continue
+            r.position += 1
+            if self._record_token(r):
+                self._retire(r)
+                continue
+            if stage:
+                new_items.append(self._stage_decode(r))
+        self._prelude(new_items)
+        self._enqueue_front(new_items)
+
+    def _release_arrivals(self, arrivals) -> None:
+        if not arrivals:
+            return
+        self.runner.stream.synchronize()
+        now = time.perf_counter() - self._t0
+        while arrivals and arrivals[0][0] <= now:
+            _, i = arrivals.popleft()
+            self.waiting[i] = self._reqs[i]
+
+    def _wait_next_arrival(self, arrivals) -> None:
+        delay = arrivals[0][0] - (time.perf_counter() - self._t0)
+        if delay > 0:
+            time.sleep(delay)
+
+    # ------------------------------------------------------------------ loops
+    def _refill_loop(self, arrivals) -> None:
+        cfg = self.cdb_config
+        pending_prefill: list[list[_Req]] = []
+        pending_coda: list[list[_Item]] = []
+        while arrivals or self._has_pending() or pending_prefill or pending_coda:
+            self._release_arrivals(arrivals)
+            for sampled in pending_prefill:
+                self._consume_prefill(sampled, stage=True)
+            pending_prefill = []
+            for items in pending_coda:
+                self._consume_coda(items, stage=True)
+            pending_coda = []
+            if not self._has_pending():
+                if arrivals:
+                    self._wait_next_arrival(arrivals)
+                continue
+            self.last_stats.scheduler_ticks += 1
+            if len(self.coda_q) >= cfg.min_coda_batch_size:
+                batch = [self.coda_q.popleft() for _ in range(min(self.max_num_seqs, len(self.coda_q)))]
+                self._run_coda(batch)
+                pending_coda.append(batch)
+                continue
+            if self._admit_prefill():
+                pb = self._schedule_prefill()
+                if pb is not None:
+                    pending_prefill.append(self._run_prefill(pb))
+                    for r, _past, _q, has in pb:
+                        if not has:
+                            self.in_flight.discard(r.idx)
+                    continue
+            items = self._pop_recurrent()
+            if items:
+                live = self._run_recurrent(items)
+                refills = []
+                for i, it in enumerate(items):
+                    step = it.step
+                    self.last_stats.recurrent_step_histogram[step] += 1
+                    if self._should_exit(it, step, live, i):
+                        self._record_exit(it, step)
+                        self.in_flight.add(it.req.idx)
+                        self.coda_q.append(it)
+                    else:
+                        it.step = step + 1
+                        refills.append(it)
+                self._enqueue_front(refills)
+                self._flush_exit_copies()
+                continue
+            if self.coda_q:
+                batch = [self.coda_q.popleft() for _ in range(min(self.max_num_seqs, len(self.coda_q)))]
+                self._run_coda(batch)
+                pending_coda.append(batch)
+                continue
+            if arrivals:
+                self._wait_next_arrival(arrivals)
+                continue
+            raise CacheFullError(
+                "The CDB scheduler could place no work: the KV cache cannot admit the next prompt "
+                "(increase num_blocks or reduce max_model_len)"
+            )
+
+    def _pop_recurrent(self) -> list[_Item]:
+        n = min(self.max_num_seqs, len(self.ready))
+        if n == 0:
+            return []
+        first = self.ready.popleft()
+        batch = [first]
+        if self.slots > 1:
+            target = self._slot_of_step(first.step)
+            deferred: deque[_Item] = deque()
+            while self.ready and len(batch) < n:
+                it = self.ready.popleft()
+                if self._slot_of_step(it.step) == target:
+                    batch.append(it)
+                else:
+                    deferred.append(it)
+            deferred.extend(self.ready)
+            self.ready = deferred
+        else:
+            while self.ready and len(batch) < n:
+                batch.append(self.ready.popleft())
+        return batch
+
+    def _no_refill_loop(self, arrivals) -> None:
+        while arrivals or self._has_pending():
+            self._release_arrivals(arrivals)
+            if not self._has_pending():
+                if arrivals:
+                    self._wait_next_arrival(arrivals)
+                continue
+            self.last_stats.scheduler_ticks += 1
+            did_prefill = False
+            while self._admit_prefill():
+                pb = self._schedule_prefill()
+                if pb is None:
+                    break
+                sampled = self._run_prefill(pb)
+                for r, *_ in pb:
+                    self.in_flight.discard(r.idx)
+                self._consume_prefill(sampled, stage=False)
+                did_prefill = True
+            cohort = [r for r in self.active.values() if r.status == RequestStatus.DECODING and r.generated > 0]
+            cohort = cohort[: self.max_num_seqs]
+            items = [self._stage_decode(r) for r in cohort]
+            if not items:
+                if not did_prefill and self._has_pending() and not arrivals:
+                    raise CacheFullError("No-refill loop stalled with pending work (over-subscribed KV cache)")
+                if arrivals and not did_prefill:
+                    self._wait_next_arrival(arrivals)
+                continue
+            self._prelude(items)
+            survivors, exited = items, []
+            for step in range(self.steps):
+                for it in survivors:
+                    it.step = step
+                live = self._run_recurrent(survivors)
+                forced = step == self.steps - 1
+                cont = []
+                for i, it in enumerate(survivors):
+                    self.last_stats.recurrent_step_histogram[step] += 1
+                    if forced or self._should_exit(it, step, live, i):
+                        self._record_exit(it, step)
+                        exited.append(it)
+                    else:
+                        cont.append(it)
+                self._flush_exit_copies()
+                survivors = cont
+                if not survivors:
+                    break
+            self._run_coda(exited)
+            self._consume_coda(exited, stage=False)
+
+    # ------------------------------------------------------------------ validation
+    def _validate(self, input_ids, max_new_tokens, exit_depths, model_kwargs) -> None:
+        cfg = self.cdb_config
+        if not input_ids:
+            raise ValueError("input_ids must contain at least one prompt")
+        if isinstance(max_new_tokens, list):
+            if len(max_new_tokens) != len(input_ids):
+                raise ValueError(f"max_new_tokens has {len(max_new_tokens)} entries but there are {len(input_ids)} prompts")
+            bad = [i for i, v in enumerate(max_new_tokens) if v < 1]
+            if bad:
+                raise ValueError(f"max_new_tokens must be >= 1 for every request, but got <1 at indices {bad}")
+        elif max_new_tokens <= 0:
+            raise ValueError(f"max_new_tokens must be positive, but got {max_new_tokens}")
+        empty = [i for i, p in enumerate(input_ids) if not p]
+        if empty:
+            raise ValueError(f"input_ids contains empty prompts at indices {empty}")
+        if cfg.exit_threshold is not None and model_kwargs is not None and model_kwargs.get("use_early_exit_gate") is False:
+            raise ValueError("exit_threshold CDB requires use_early_exit_gate to stay enabled")
+        if exit_depths is None:
+            return
+        if not cfg.synthetic_exit_replay:
+            raise ValueError("exit_depths requires cdb_config.synthetic_exit_replay=True")
+        if len(exit_depths) != len(input_ids):
+            raise ValueError(f"exit_depths has {len(exit_depths)} entries but there are {len(input_ids)} requests")
+        mnt = max_new_tokens if isinstance(max_new_tokens, list) else [max_new_tokens] * len(input_ids)
+        mnt = [min(m, cfg.max_model_len - len(p)) for m, p in zip(mnt, input_ids, strict=True)]
+        steps = cfg.max_recurrent_steps
+        for idx, depths in enumerate(exit_depths):
+            if len(depths) != mnt[idx] - 1:
+                raise ValueError(
+                    f"exit_depths[{idx}] has {len(depths)} entries but the request stages {mnt[idx] - 1} decode tokens "
+                    "(max_new_tokens - 1)"
+                )
+            for d in depths:
+                if not 0 <= d < steps:
+                    raise ValueError(f"exit_depths[{idx}] value {d} is out of range [0, {steps}); values are 0-based")
+        if copies_exit_kv(cfg.kv_policy):
+            return
+        for depths in exit_depths:
+            for d in depths:
+                if d + 1 < cfg.kv_slots_per_layer:
+                    raise ValueError(
+                        "Every replay exit depth must write all static KV slots before exit: "
+                        f"kv_slots_per_layer={cfg.kv_slots_per_layer}, exit step {d + 1}"
+                    )
+
+
+def _auto_num_blocks(shape: OuroShape, cfg: ContinuousDepthBatchingConfig, device: torch.device) -> int:
+    """Fill the post-load budget (``kv_cache_sizing.py:34-80``; default static fraction 0.8)."""
+
+    free, total = torch.cuda.mem_get_info(device)
+    frac = 0.8 if cfg.mem_fraction_static is None else cfg.mem_fraction_static
+    # Reserve room for the packed weights, the work buffers and the logits the runner allocates.
+    weights = 2 * (shape.param_count_recurrent() + 2 * shape.vocab_size * shape.hidden_size)
+    work = 2 * cfg.max_num_batched_tokens * (4 * shape.hidden_size + 3 * shape.intermediate_size + 3 * shape.hidden_size)
+    budget = int(free - total * (1 - frac)) - weights - work
+    assert cfg.kv_slots_per_layer is not None
+    per_block = 2 * cfg.kv_slots_per_layer * shape.num_hidden_layers * cfg.block_size * shape.num_key_value_heads * shape.head_dim * 2
+    blocks = budget // per_block - 2
+    if blocks <= 0:
+        raise ValueError("No usable KV blocks fit in device memory")
+    return int(blocks)

@@ -1,0 +1,166 @@
+/*
+ * C ABI of the B200 continuous-depth-batching (CDB) decode library, libcdb_b200.so.
+ *
+ * Every entry point takes raw device pointers, sizes and strides plus a cudaStream_t passed
+ * as void*, returns an int status (CDB_OK or a CDB_ERR_* code below), allocates no device
+ * memory, and only enqueues work on the given stream (safe inside CUDA-graph capture).
+ * Tensors are row-major; "bf16" is IEEE bfloat16; element strides are in elements.
+ *
+ * Device-side failures (a bounded wait that ran out, an out-of-range index caught by a
+ * kernel's own check) are written to the caller's `status` word in device memory (first
+ * error wins) instead of trapping; the host reads it between launches.
+ *
+ * Reference interfaces these replace are cited per entry point as path:line inside the
+ * reference project (ZH-Haoran/continuous-depth-batching, package looped_cdb), or inside
+ * HF transformers 5.x where the reference calls into it.
+ */
+#ifndef CDB_B200_H_
+#define CDB_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CDB_OK 0
+#define CDB_ERR_INVALID_ARGUMENT 1
+#define CDB_ERR_UNSUPPORTED 2
+#define CDB_ERR_CUDA 3
+#define CDB_ERR_DEVICE_TIMEOUT 4
+#define CDB_ERR_TMA_ENCODE 5
+#define CDB_ERR_INDEX 6
+
+/* Library version (major*10000 + minor*100 + patch). */
+int cdb_version(void);
+
+/* Human-readable text for a status code (static storage). */
+const char* cdb_status_string(int status);
+
+/* ---------------------------------------------------------------------------------------
+ * Paged KV pool. One bf16 allocation laid out
+ *   kv[num_cache_layers][2 (K,V)][rows][num_kv_heads][head_dim],  rows = (num_blocks+2)*block_size
+ * i.e. for each cache layer exactly the reference's per-layer key/value tensors
+ * [(num_blocks+2)*block_size, Hkv, D] (continuous_batching/cache.py:131-145), stacked. A token
+ * of request r at position p lives in row block_table[r][p / block_size]*block_size + p % block_size
+ * of every cache layer; cache layer = kv_slot*num_layers + physical layer
+ * (kv_cache_policy.py:106-128).
+ * ------------------------------------------------------------------------------------- */
+
+/* Split-KV work plan for one recurrent (or prefill) launch; run once, reused by every layer.
+ *   item_pos    [num_items] int32: position of each row's query token; -1 = padding row.
+ *   append      1: row p reads cached rows [0,p) and appends its own k/v (decode);
+ *               0: row p reads cached rows [0,p] (its k/v already written, prefill).
+ *   plan_header [4] int32 out: {num_units, blocks_per_split, max_splits, 0}.
+ *   units       [unit_capacity] int4 out: {item, head_group, split, num_splits}.
+ *   scratch_items: rows the split-combine scratch covers; larger launches never split.
+ * Replaces the split decision inside FlashAttention-3's flash_attn_with_kvcache
+ * (transformers integrations/flash_paged.py:107-118). */
+int cdb_attn_plan(const int32_t* item_pos, int num_items, int append, int num_heads, int head_dim,
+                  int block_size, int unit_capacity, int scratch_items, int num_sms, int32_t* plan_header,
+                  void* units, void* stream);
+
+/* Ragged-depth paged decode attention with fused RoPE and KV append (one cache layer).
+ * Replaces paged_attention_forward's decode branch -> flash_attn_with_kvcache
+ * (transformers integrations/flash_paged.py:84-122), reached from OuroAttention.forward
+ * (models/ouro/modeling_ouro.py:377-432) and HuginnAttention.forward
+ * (models/huginn/modeling_huginn.py:244-302).
+ *   qkv        bf16 [num_items, qkv_stride]: q at column 0, k at k_col, v at v_col (H*D each).
+ *   rope_mode  0: q/k already rotated; 1: split-half rotate_half RoPE (Ouro);
+ *              2: interleaved-pair RoPE in fp32 (Huginn), cos/sin tables given in fp32.
+ *   rope_cos/rope_sin  [max_positions, head_dim] tables (bf16 for mode 1, fp32 for mode 2).
+ *   append     1: rotate k, write k/v at the row's position, attend over [0,p] using the
+ *              new k/v from registers; 0: attend over cached rows [0,p] only.
+ *   out        bf16 [num_items, out_stride], heads concatenated.
+ *   part_o/part_ml/counters: split-combine scratch sized for scratch_items rows
+ *              (cdb_attn_scratch_bytes); counters must start zeroed, kernels leave them zeroed.
+ */
+int cdb_paged_decode_attn_append(const void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col,
+                                 void* out, int64_t out_stride, void* kv_base, int num_cache_layers,
+                                 int64_t kv_rows, int cache_layer, const int32_t* block_table,
+                                 int64_t block_table_stride, const int32_t* item_slot, const int32_t* item_pos,
+                                 int rope_mode, const void* rope_cos, const void* rope_sin, int append,
+                                 const int32_t* plan_header, const void* units, float* part_o, float* part_ml,
+                                 int32_t* counters, int scratch_items, int num_items, int num_heads, int head_dim,
+                                 int block_size, float scale, int num_ctas, int32_t* status, void* stream);
+
+/* Bytes of split-combine scratch (part_o + part_ml + counters) for `scratch_items` rows. */
+int64_t cdb_attn_scratch_bytes(int scratch_items, int num_heads, int head_dim);
+
+/* Rotate q in place and rotate+write k and v of every row into its cache row (prefill path).
+ * Replaces apply_rotary_pos_emb (modeling_ouro.py:186-204) + PagedAttentionCache.update's
+ * index_copy_ writes (continuous_batching/cache.py:284-318). */
+int cdb_rope_append_kv(void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col, void* kv_base,
+                       int num_cache_layers, int64_t kv_rows, int cache_layer, const int32_t* block_table,
+                       int64_t block_table_stride, const int32_t* item_slot, const int32_t* item_pos, int rope_mode,
+                       const void* rope_cos, const void* rope_sin, int num_items, int num_heads, int head_dim,
+                       int block_size, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Row-wise fused elementwise kernels (bf16 activations, fp32 math, bf16 rounding at the
+ * points PyTorch rounds). Optional index arrays (nullable) gather input rows / scatter output
+ * rows; an index < 0 marks a padding row that is skipped.
+ * ------------------------------------------------------------------------------------- */
+
+/* y[r] = weight * bf16(x*rsqrt(mean(x^2)+eps)), x read from x[x_rows[r]] (OuroRMSNorm.forward,
+ * modeling_ouro.py:445-450). If x_copy != NULL the gathered x row is also stored there. */
+int cdb_rmsnorm(const void* x, int64_t x_stride, const int32_t* x_rows, const void* weight, void* y,
+                int64_t y_stride, void* x_copy, int64_t x_copy_stride, int num_rows, int hidden, float eps,
+                void* stream);
+
+/* Sandwich-norm residual step of OuroDecoderLayer.forward (modeling_ouro.py:481-502):
+ *   x[r] = x[r] + rmsnorm(a[r]; w_a)     (bf16 add)
+ *   y[r] = rmsnorm(x[r]; w_next)         (next norm: the MLP input norm, the next layer's
+ *                                         input norm, or the final model norm)
+ * If gate_w != NULL also gate_out[r] = bf16(dot(y[r], gate_w) + gate_b[0]) (exit gate
+ * Linear(H,1), adapters/ouro.py:262-291). If y_rows != NULL, y row r is written to
+ * y[y_rows[r]] (the hidden-state bank scatter, model_runner.py:690-693). */
+int cdb_add_rmsnorm(void* x, int64_t x_stride, const void* a, int64_t a_stride, const void* w_a,
+                    const void* w_next, void* y, int64_t y_stride, const int32_t* y_rows, const void* gate_w,
+                    const void* gate_b, void* gate_out, int num_rows, int hidden, float eps, void* stream);
+
+/* act[r] = bf16(bf16(silu(g)) * u) with gu[r] = [g (inter) | u (inter)] (OuroMLP.forward,
+ * modeling_ouro.py:166-169). */
+int cdb_silu_mul(const void* gu, int64_t gu_stride, void* act, int64_t act_stride, int num_rows, int inter,
+                 void* stream);
+
+/* Greedy sampling: id_r = argmax_j logits[r][j] (first index among equal maxima, as
+ * torch.argmax; model_runner.py:1062,1105), stored to out[out_rows[r]] (out[r] when out_rows is
+ * NULL; skipped when out_rows[r] < 0). If token_rows != NULL and token_rows[r] >= 0 the id is
+ * also stored to token_table[token_rows[r]] (device-resident next-token buffer). */
+int cdb_argmax(const void* logits, int64_t stride, int num_rows, int vocab, int64_t* out, const int32_t* out_rows,
+               const int32_t* token_rows, int32_t* token_table, void* stream);
+
+/* Prelude embedding lookup (OuroCDBAdapter.prelude, adapters/ouro.py:199-212):
+ * out[out_rows[r]] = table[id_r]; id_r = ids[r] if ids[r] >= 0 else token_table[id_src[r]]
+ * (the on-device successor-token gather of model_runner.py:439-457). */
+int cdb_embed(const void* table, int hidden, int vocab, const int32_t* ids, const int32_t* id_src,
+              const int32_t* token_table, void* out, int64_t out_stride, const int32_t* out_rows, int num_rows,
+              int32_t* status, void* stream);
+
+/* Apply n block-table edits {row, column, block_id} (int32 triples) to a device block table
+ * [rows, stride]. The device mirror of FullAttentionCacheAllocator.allocate_blocks /
+ * _refresh_cached_block_table (cache_manager.py:150-165, continuous_depth_batching/cache.py:115-144). */
+int cdb_block_table_update(int32_t* table, int64_t stride, const int32_t* edits, int num_edits, void* stream);
+
+/* last_exited copy-on-exit: for each token row in rows[n] copy K and V of cache layer
+ * src_layers[i] into dst_layers[i] (num_pairs pairs). PagedAttentionCache.copy_kv_rows driven by
+ * _flush_exit_kv_copies (continuous_depth_batching/cache.py:105-113, continuous_api.py:1225-1245). */
+int cdb_exit_kv_copy(void* kv_base, int num_cache_layers, int64_t kv_rows, int num_kv_heads, int head_dim,
+                     const int32_t* rows, int num_rows, const int32_t* src_layers, const int32_t* dst_layers,
+                     int num_pairs, void* stream);
+
+/* Cumulative-hazard exit decision on device (ExitPolicy.should_exit, exit_policy.py:150-169):
+ * for row r with hidden slot s = slots[r] (>= 0): h = float(bf16(sigmoid(signal[r]))) when
+ * signal_bf16 else sigmoid in fp32; cdf[s] += h*surv[s]; surv[s] *= 1-h;
+ * exit[r] = (steps[r]+1 >= min_steps) && cdf[s] >= threshold. cdf/surv are fp64 per slot and
+ * must be reset (cdf=0, surv=1) when a slot starts a new token (reset[r] != 0 does that first). */
+int cdb_exit_hazard(const void* signal, int signal_bf16, const int32_t* slots, const int32_t* steps,
+                    const int8_t* reset, double* cdf, double* surv, int8_t* exit_out, int num_rows,
+                    int min_steps, double threshold, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CDB_B200_H_ */

@@ -1,0 +1,158 @@
+"""End-to-end parity of the B200 engine against the reference trace and the CPU oracle.
+
+* Schedule parity (bit-exact): with the replayed exit schedule of the reference run, the
+  engine's ordered launch trace - every prefill/recurrent/coda launch, each item's (request,
+  position, recurrent step) and block-table row - equals the trace recorded from the reference
+  engine itself (``tests/golden/ouro_cfg0.json``), for refill, no-refill and ``last_exited``.
+  The device block table is read back and compared with the host block lists.
+* Numerics: teacher-forced on the oracle's tokens (so one flipped argmax cannot derail the rest
+  of a sequence), every LM-head launch's bf16 logits are within 2e-2 max-abs of the bf16 CPU
+  oracle's and the greedy tokens agree on >= 99% of positions.
+"""
+
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import pytest
+import torch
+
+from continuous_depth_batching_b200 import ContinuousDepthBatchingConfig, ContinuousDepthBatchingEngine, OuroForCausalLM, OuroShape
+from continuous_depth_batching_b200.ouro import random_ouro_state_dict
+from oracle.engine import OracleConfig, OracleEngine
+from oracle.workloads import ouro_lognormal_workload
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _golden():
+    data = json.loads((GOLDEN / "ouro_cfg0.json").read_text())
+    shape = OuroShape(**data["shape"])
+    return data, shape
+
+
+def _engine(shape, sd, *, kv_policy="single", refill=True, live=False, num_blocks=4096, max_model_len=2048, graphs=True):
+    model = OuroForCausalLM(shape)
+    model.load_state_dict({k: v.to(torch.float32) for k, v in sd.items()})
+    cfg = ContinuousDepthBatchingConfig(
+        block_size=16,
+        num_blocks=num_blocks,
+        max_recurrent_steps=shape.total_ut_steps,
+        exit_threshold=0.5 if live else None,
+        synthetic_exit_replay=not live,
+        use_async_batching=False,
+        use_cuda_graph=graphs,
+        refill=refill,
+        kv_policy=kv_policy,
+        kv_pressure_mode="reserve" if kv_policy == "last_exited" else "recompute",
+        max_model_len=max_model_len,
+    )
+    return ContinuousDepthBatchingEngine.from_model(model, cfg, device="cuda")
+
+
+@pytest.mark.parametrize("name", ["replay_refill", "replay_norefill", "replay_last_exited"])
+@pytest.mark.parametrize("graphs", [True, False])
+def test_schedule_and_block_tables_match_reference(name, graphs):
+    data, shape = _golden()
+    run = next(r for r in data["runs"] if r["name"] == name)
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+    eng = _engine(shape, sd, kv_policy=run["kv_policy"], refill=run["refill"], graphs=graphs)
+    eng.record_trace = True
+    outs = eng.generate_batch(data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"])
+    assert len(eng.launch_trace) == len(run["launches"])
+    for mine, ref in zip(eng.launch_trace, run["launches"], strict=True):
+        assert mine == ref
+    assert [len(o.generated_tokens) for o in outs] == data["max_new_tokens"]
+    assert {str(k): v for k, v in sorted(eng.last_stats.exit_depth_histogram.items())} == run["stats"]["exit_depth_histogram"]
+    assert eng.last_stats.scheduler_refills == run["stats"]["scheduler_refills"]
+
+
+def test_device_block_table_mirrors_host_lists():
+    """At every recurrent launch the device table row of each item equals its host block list."""
+
+    data, shape = _golden()
+    run = next(r for r in data["runs"] if r["name"] == "replay_refill")
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+    eng = _engine(shape, sd)
+    checked = []
+    orig = eng._run_recurrent
+
+    def run_and_check(items):
+        out = orig(items)
+        eng.runner.stream.synchronize()
+        table = eng.runner.pool.block_table.cpu()
+        for it in items:
+            host = eng.pool.tables[it.req.idx]
+            assert table[it.req.slot, : len(host)].tolist() == host
+        checked.append(len(items))
+        return out
+
+    eng._run_recurrent = run_and_check
+    eng.generate_batch(data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"])
+    assert sum(checked) == run["stats"]["recurrent_steps"]
+    assert eng.pool.tables == {}  # every request retired and released its blocks
+
+
+def _oracle(shape, sd, prompts, max_new, depths, dtype, forced=None, kv_policy="single"):
+    cfg = OracleConfig(
+        block_size=16, num_blocks=4096, max_recurrent_steps=shape.total_ut_steps, max_model_len=4096,
+        synthetic_exit_replay=True, kv_policy=kv_policy,
+        kv_pressure_mode="reserve" if kv_policy == "last_exited" else "recompute",
+    )
+    eng = OracleEngine(shape, sd, cfg, dtype)
+    toks = eng.generate(prompts, max_new, exit_depths=depths, forced_tokens=forced)
+    return eng, toks
+
+
+def _compare_teacher_forced(shape, sd, prompts, max_new, depths, kv_policy="single"):
+    oracle, otoks = _oracle(shape, sd, prompts, max_new, depths, torch.bfloat16, kv_policy=kv_policy)
+    eng = _engine(shape, sd, kv_policy=kv_policy, max_model_len=4096)
+    eng.record_trace = True
+    eng.keep_coda_logits = True
+    outs = eng.generate_batch(prompts, max_new_tokens=max_new, eos_token_id=None, exit_depths=depths, forced_tokens=otoks)
+    assert eng.launch_trace == oracle.launches
+    mine = [o.generated_tokens for o in outs]
+    total = sum(len(t) for t in otoks)
+    same = sum(int(a == b) for x, y in zip(mine, otoks, strict=True) for a, b in zip(x, y, strict=True))
+    coda_ref = [lg for kind, lg in oracle.logits if kind == "coda"]
+    assert len(coda_ref) == len(eng.coda_logits)
+    worst = max((a.float().cpu() - b.float()).abs().max().item() for a, b in zip(eng.coda_logits, coda_ref, strict=True))
+    return same / total, worst
+
+
+def test_teacher_forced_tokens_and_logits_config0_shape():
+    data, shape = _golden()
+    run = next(r for r in data["runs"] if r["name"] == "replay_refill")
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+    agree, worst = _compare_teacher_forced(shape, sd, data["prompts"], data["max_new_tokens"], run["exit_depths"])
+    assert worst <= 2e-2, worst
+    assert agree >= 0.99, agree
+
+
+def test_teacher_forced_ouro_1p4b_width_two_layers():
+    """Ouro-1.4B layer widths (H 2048, 16x128 heads, I 5632, V 49152) with 2 layers on a small mix."""
+
+    shape = OuroShape(
+        vocab_size=49152, hidden_size=2048, intermediate_size=5632, num_hidden_layers=2, num_attention_heads=16,
+        num_key_value_heads=16, head_dim=128, total_ut_steps=4, max_position_embeddings=4096,
+    )
+    sd = random_ouro_state_dict(shape, seed=1)
+    prompts, max_new, depths = ouro_lognormal_workload(6, vocab_size=shape.vocab_size, seed=3, prompt_median=40,
+                                                       prompt_cap=200, out_median=8, out_cap=12)
+    agree, worst = _compare_teacher_forced(shape, sd, prompts, max_new, depths)
+    assert worst <= 2e-2, worst
+    assert agree >= 0.99, agree
+
+
+def test_last_exited_copy_teacher_forced():
+    data, shape = _golden()
+    run = next(r for r in data["runs"] if r["name"] == "replay_last_exited")
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+    prompts = data["prompts"][:6]
+    max_new = data["max_new_tokens"][:6]
+    depths = run["exit_depths"][:6]
+    agree, worst = _compare_teacher_forced(shape, sd, prompts, max_new, depths, kv_policy="last_exited")
+    assert worst <= 2e-2, worst
+    assert agree >= 0.99, agree
