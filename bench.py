@@ -56,12 +56,36 @@ def parse() -> argparse.Namespace:
     p.add_argument("--requests", type=int, default=256)
     p.add_argument("--out-cap", type=int, default=1024, help="cap on output lengths (smaller = profiling case)")
     p.add_argument("--no-graph", action="store_true")
+    p.add_argument("--gemm", default="cublas", choices=["tcgen05", "cublas"], help="dense GEMM backend")
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
 
 
 def dist_env() -> tuple[int, int, int]:
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def aggregate(dev_s: float, wall_s: float, tokens: float, device) -> tuple[float, float, float]:
+    """Whole-job numbers across replicas: max over ranks of the times, sum of generated tokens.
+
+    Runs after the timed region; with one process it returns its inputs.
+    """
+
+    import torch.distributed as dist
+
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return dev_s, wall_s, tokens
+    t = torch.tensor([dev_s, wall_s], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    n = torch.tensor([tokens], dtype=torch.float64, device=device)
+    dist.all_reduce(n, op=dist.ReduceOp.SUM)
+    return float(t[0]), float(t[1]), float(n[0])
+
+
+def replica_seed(seed: int, rank: int) -> int:
+    """Each replica serves its own seeded request set (request-sharded, weak scaling)."""
+
+    return seed + 1000 * rank
 
 
 def workload(seed: int, n: int, out_cap: int):
@@ -135,7 +159,7 @@ def build_engine(args, device):
         max_model_len=4096,
         max_num_seqs=256,
     )
-    eng = ContinuousDepthBatchingEngine.from_model(model, cfg, device=device)
+    eng = ContinuousDepthBatchingEngine.from_model(model, cfg, device=device, gemm_backend=args.gemm)
     del model
     return eng, shape
 
@@ -200,7 +224,7 @@ def run_b200(args) -> None:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
     eng, shape = build_engine(args, device)
-    prompts, max_new, depths = workload(args.seed + rank, args.requests, args.out_cap)
+    prompts, max_new, depths = workload(replica_seed(args.seed, rank), args.requests, args.out_cap)
     stream = eng.runner.stream
 
     def step():
@@ -228,6 +252,7 @@ def run_b200(args) -> None:
     launches0 = eng.runner.stats.kernel_launches
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        torch.cuda.nvtx.range_push("bench.timed")
         t0 = time.perf_counter()
         ev0.record(stream)
         for _ in range(args.steps):
@@ -238,19 +263,12 @@ def run_b200(args) -> None:
         ev1.record(stream)
         torch.cuda.synchronize()
         t1 = time.perf_counter()
+        torch.cuda.nvtx.range_pop()
     dev_s = ev0.elapsed_time(ev1) / 1e3
     wall_s = t1 - t0
     kernel_launches = eng.runner.stats.kernel_launches - launches0
     stats = eng.last_stats
-    if world > 1:
-        t = torch.tensor([dev_s, wall_s, float(gen_tokens)], device=device, dtype=torch.float64)
-        mx = t.clone()
-        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
-        sm = t.clone()
-        torch.distributed.all_reduce(sm, op=torch.distributed.ReduceOp.SUM)
-        dev_s, wall_s, total_tokens = float(mx[0]), float(mx[1]), float(sm[2])
-    else:
-        total_tokens = float(gen_tokens)
+    dev_s, wall_s, total_tokens = aggregate(dev_s, wall_s, float(gen_tokens), device)
     if rank == 0:
         roof = attention_roofline(eng, shape, recorded[:60], peak_gbs)
         roof["peak_source"] = peak_src
@@ -281,6 +299,7 @@ def run_b200(args) -> None:
                 "exit_depth_histogram": {str(k): v for k, v in sorted(stats.exit_depth_histogram.items())},
                 "l2": "inputs larger than L2 (KV cache tens of GB, weights 2.5 GB)",
                 "cuda_graphs": not args.no_graph,
+                "gemm_backend": args.gemm,
                 "parallelism": f"{world} independent request-sharded replicas (no collective)",
             },
             "e2e": {

@@ -35,6 +35,11 @@ _SIGNATURES: dict[str, list] = {
         c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int64, c_int,
         c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
     ],
+    "cdb_gemm_bf16": [
+        c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_int,
+        c_int, c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_void_p,
+    ],
+    "cdb_gemm_workspace_elems": [c_int, c_int, c_int, c_int],
     "cdb_rmsnorm": [
         c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_float, c_void_p,
     ],
@@ -51,7 +56,7 @@ _SIGNATURES: dict[str, list] = {
         c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_double, c_void_p,
     ],
 }
-_RESTYPES = {"cdb_status_string": ctypes.c_char_p, "cdb_attn_scratch_bytes": c_int64}
+_RESTYPES = {"cdb_status_string": ctypes.c_char_p, "cdb_attn_scratch_bytes": c_int64, "cdb_gemm_workspace_elems": c_int64}
 
 _LIB: ctypes.CDLL | None = None
 
@@ -101,7 +106,7 @@ def stream_ptr(stream: torch.cuda.Stream | None = None) -> int:
     return s.cuda_stream
 
 
-_NO_LAUNCH = {"cdb_version", "cdb_status_string", "cdb_attn_scratch_bytes"}
+_NO_LAUNCH = {"cdb_version", "cdb_status_string", "cdb_attn_scratch_bytes", "cdb_gemm_workspace_elems"}
 # Kernels enqueued through this binding (device work only; graph replays are counted by the runner).
 launch_count = 0
 

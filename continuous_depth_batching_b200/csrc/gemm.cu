@@ -1,0 +1,398 @@
+// bf16 tensor-core GEMM for sm_100a on tcgen05/TMEM: C[M,N] = X[M,K] * W[N,K]^T.
+//
+// Decode-shaped problems have few token rows (M <= 256) and wide weights (N up to 49152), so
+// the weight is the MMA "A" operand (128 weight rows per tile, UMMA M=128) and the token rows
+// are the MMA "B" operand (UMMA N = BN in {32,64,128,256}); the fp32 accumulator lives in
+// tensor memory as [128 lanes = weight rows] x [BN columns = token rows].
+//
+// One CTA = one (weight tile, token tile, K split), warp specialised:
+//   warp 0      TMA producer: 2-D tile loads of W[128 x 64] and X[BN x 64] (128-byte swizzle)
+//               into a STAGES-deep ring, completion on "full" mbarriers;
+//   warp 1      allocates TMEM and issues tcgen05.mma (one elected thread), releasing each
+//               stage with tcgen05.commit onto its "empty" mbarrier;
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp reads its 32-lane quarter),
+//               round to bf16 and store; consecutive lanes hold consecutive output columns,
+//               so every store instruction writes 64 contiguous bytes.
+// Split-K (for the small-N projections that cannot fill 148 SMs otherwise) is deterministic:
+// every split stores fp32 partials to L2-resident scratch and the last CTA of the tile (atomic
+// counter) sums them in split order, stores bf16 and resets its counter.
+#include <cuda.h>
+
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "cdb_common.cuh"
+
+namespace cdb {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // one 128-byte swizzle atom of bf16
+constexpr int THREADS = 192;
+
+template <int BN, int STAGES>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  // kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both K-major, M=128, N=BN.
+  static constexpr uint32_t IDESC =
+      (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+};
+
+struct Params {
+  __nv_bfloat16* c;
+  int64_t ldc;
+  float* ws;
+  int32_t* counters;
+  int M, N, K;
+  int splits, kb_per_split, num_kb;
+  int32_t* status;
+};
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of 128 B,
+// 8-row groups 1024 B apart (SBO), sm100 descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  const uint32_t mask0 = 0, mask1 = 0, mask2 = 0, mask3 = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(mask0), "r"(mask1), "r"(mask2), "r"(mask3)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, Params p) {
+  using C = Cfg<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accum = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int wtile = blockIdx.x, mtile = blockIdx.y, split = blockIdx.z;
+  const int kb0 = split * p.kb_per_split;
+  const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tensormap(&map_w);
+      prefetch_tensormap(&map_x);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) break;
+        uint8_t* a = smem + stage * C::STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+        tma_load_2d(a, &map_w, &full[stage], kb * BK, wtile * BM);
+        tma_load_2d(a + C::A_BYTES, &map_x, &full[stage], kb * BK, mtile * BN);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full[stage], phase, p.status)) break;
+        tc_fence_after();
+        const uint32_t a = smem_u32(smem + stage * C::STAGE_BYTES);
+        const uint32_t b = a + C::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          umma_bf16(tmem, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), C::IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      umma_commit(accum);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int n = wtile * BM + q * 32 + lane;
+    const bool ok = mbar_wait(accum, 0, p.status);
+    tc_fence_after();
+    const bool split_k = p.splits > 1;
+    const int m_base = mtile * BN;
+    if (ok) {
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, r);
+        if (n < p.N) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int m = m_base + c0 + j;
+            if (m < p.M) {
+              const float v = __uint_as_float(r[j]);
+              if (split_k)
+                p.ws[((int64_t)split * gridDim.y * BN + m) * p.N + n] = v;
+              else
+                p.c[(int64_t)m * p.ldc + n] = f_to_bf16(v);
+            }
+          }
+        }
+      }
+    }
+    if (split_k) {
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64) {
+        int32_t* ctr = p.counters + (int64_t)mtile * gridDim.x + wtile;
+        const int prev = atomicAdd(ctr, 1);
+        const int last = prev == p.splits - 1;
+        if (last) atomicExch(ctr, 0);
+        *last_flag = last;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (*last_flag && n < p.N) {
+        __threadfence();
+        const int m_end = min(m_base + BN, p.M);
+        for (int m = m_base; m < m_end; ++m) {
+          float acc = 0.f;
+          for (int s = 0; s < p.splits; ++s) acc += __ldcg(p.ws + ((int64_t)s * gridDim.y * BN + m) * p.N + n);
+          p.c[(int64_t)m * p.ldc + n] = f_to_bf16(acc);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeFn encoder() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(ptr);
+  });
+  return fn;
+}
+
+struct Key {
+  const void* ptr;
+  int64_t rows, cols, ld;
+  int box_rows;
+  bool operator==(const Key& o) const {
+    return ptr == o.ptr && rows == o.rows && cols == o.cols && ld == o.ld && box_rows == o.box_rows;
+  }
+};
+struct KeyHash {
+  size_t operator()(const Key& k) const {
+    return std::hash<const void*>()(k.ptr) ^ (std::hash<int64_t>()(k.rows) * 31) ^ (std::hash<int64_t>()(k.cols) * 131) ^
+           (std::hash<int64_t>()(k.ld) * 1313) ^ ((size_t)k.box_rows << 40);
+  }
+};
+
+// 2-D row-major bf16 matrix [rows, cols] with leading dimension ld, tile box {64 cols, box_rows}.
+static int matrix_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  static std::mutex mu;
+  static std::unordered_map<Key, CUtensorMap, KeyHash> cache;
+  const Key key{ptr, rows, cols, ld, box_rows};
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *out = it->second;
+    return CDB_OK;
+  }
+  EncodeFn enc = encoder();
+  if (enc == nullptr) return CDB_ERR_TMA_ENCODE;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUtensorMap map;
+  std::memset(&map, 0, sizeof(map));
+  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return CDB_ERR_TMA_ENCODE;
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(key, map);
+  *out = map;
+  return CDB_OK;
+}
+
+template <int BN, int STAGES>
+static int launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, dim3 grid, cudaStream_t st) {
+  using C = Cfg<BN, STAGES>;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(gemm_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+        cudaSuccess)
+      return CDB_ERR_CUDA;
+    attr = true;
+  }
+  gemm_kernel<BN, STAGES><<<grid, THREADS, C::SMEM, st>>>(mw, mx, p);
+  return cudaPeekAtLastError() == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
+}
+
+}  // namespace gemm
+}  // namespace cdb
+
+using namespace cdb;
+
+extern "C" int cdb_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int M,
+                             int N, int K, int splits, float* workspace, int64_t workspace_elems, int32_t* counters,
+                             int num_counters, int num_sms, int32_t* status, void* stream) {
+  using namespace cdb::gemm;
+  if (M <= 0 || N <= 0 || K <= 0) return M == 0 ? CDB_OK : CDB_ERR_INVALID_ARGUMENT;
+  if (K % 8 != 0 || ldx % 8 != 0 || ldw % 8 != 0 || ldx < K || ldw < K || ldc < N) return CDB_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return CDB_ERR_INVALID_ARGUMENT;
+  const int bn = M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  const int tiles_n = (N + BM - 1) / BM;
+  const int tiles_m = (M + bn - 1) / bn;
+  const int num_kb = (K + BK - 1) / BK;
+  if (num_sms <= 0) num_sms = 148;
+  int s = splits;
+  if (s <= 0) {
+    const int tiles = tiles_n * tiles_m;
+    s = tiles >= num_sms ? 1 : num_sms / tiles;
+    s = min(s, max(1, num_kb / 4));
+    s = min(s, 16);
+  }
+  s = max(1, min(s, num_kb));
+  int kb_per = (num_kb + s - 1) / s;
+  s = (num_kb + kb_per - 1) / kb_per;
+  if (s > 1) {
+    const int64_t need = (int64_t)s * tiles_m * bn * N;
+    if (workspace == nullptr || counters == nullptr || need > workspace_elems || tiles_n * tiles_m > num_counters) {
+      s = 1;
+      kb_per = num_kb;
+    }
+  }
+  CUtensorMap mw, mx;
+  int rc = matrix_map(&mw, w, N, K, ldw, BM);
+  if (rc != CDB_OK) return rc;
+  rc = matrix_map(&mx, x, M, K, ldx, bn);
+  if (rc != CDB_OK) return rc;
+  Params p;
+  p.c = static_cast<__nv_bfloat16*>(c);
+  p.ldc = ldc;
+  p.ws = workspace;
+  p.counters = counters;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.splits = s;
+  p.kb_per_split = kb_per;
+  p.num_kb = num_kb;
+  p.status = status;
+  const dim3 grid(tiles_n, tiles_m, s);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (bn) {
+    case 32:
+      return launch<32, 8>(mw, mx, p, grid, st);
+    case 64:
+      return launch<64, 8>(mw, mx, p, grid, st);
+    case 128:
+      return launch<128, 6>(mw, mx, p, grid, st);
+    default:
+      return launch<256, 4>(mw, mx, p, grid, st);
+  }
+}
+
+extern "C" int64_t cdb_gemm_workspace_elems(int M, int N, int K, int num_sms) {
+  using namespace cdb::gemm;
+  const int bn = M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  const int tiles = ((N + BM - 1) / BM) * ((M + bn - 1) / bn);
+  const int num_kb = (K + BK - 1) / BK;
+  if (num_sms <= 0) num_sms = 148;
+  int s = tiles >= num_sms ? 1 : num_sms / tiles;
+  s = min(min(s, max(1, num_kb / 4)), 16);
+  return s > 1 ? (int64_t)s * ((M + bn - 1) / bn) * bn * N : 0;
+}

@@ -175,8 +175,8 @@ class ContinuousDepthBatchingEngine:
         self.last_stats = ContinuousDepthBatchingStats()
         self.record_trace = False
         self.launch_trace: list[dict] = []
-        self.coda_logits: list[torch.Tensor] = []
-        self.keep_coda_logits = False
+        self.lm_logits: list[tuple[str, torch.Tensor]] = []
+        self.keep_logits = False
 
     # ------------------------------------------------------------------ construction
     @classmethod
@@ -188,6 +188,7 @@ class ContinuousDepthBatchingEngine:
         dtype: torch.dtype | None = None,
         model_adapter=None,
         device: torch.device | str | None = None,
+        gemm_backend: str = "cublas",
     ) -> ContinuousDepthBatchingEngine:
         """Build an engine for an Ouro causal LM given by its parameters (reference names).
 
@@ -230,6 +231,7 @@ class ContinuousDepthBatchingEngine:
             max_num_seqs=cfg.max_num_seqs,
             max_num_batched_tokens=cfg.max_num_batched_tokens,
             use_cuda_graph=cfg.use_cuda_graph,
+            gemm_backend=gemm_backend,
         )
         return cls(model, cfg, runner, shape)
 
@@ -333,7 +335,7 @@ class ContinuousDepthBatchingEngine:
         cfg = self.cdb_config
         self.last_stats = ContinuousDepthBatchingStats()
         self.launch_trace = []
-        self.coda_logits = []
+        self.lm_logits = []
         self.waiting: OrderedDict[int, _Req] = OrderedDict()
         self.active: OrderedDict[int, _Req] = OrderedDict()
         self.in_flight: set[int] = set()
@@ -575,9 +577,12 @@ class ContinuousDepthBatchingEngine:
                     "blocks": [list(self.pool.tables[r.idx][: -(-r.position // bs)]) for r, *_ in batch],
                 }
             )
-        self.runner.prefill(
-            ids, slots, pos, logit_rows, log_rows, req_slots, [self._slot_of_step(s) for s in range(self.steps)]
+        logits = self.runner.prefill(
+            ids, slots, pos, logit_rows, log_rows, req_slots, [self._slot_of_step(s) for s in range(self.steps)],
+            keep_logits=self.keep_logits,
         )
+        if logits is not None:
+            self.lm_logits.append(("prefill", logits))
         st.prefill_coda_tokens += len(sampled)
         if self._content_finish and sampled:
             self._sync_tokens(sampled)
@@ -682,10 +687,10 @@ class ContinuousDepthBatchingEngine:
             [it.hidden for it in items],
             [it.req.log_base + it.req.generated for it in items],
             [it.req.slot for it in items],
-            keep_logits=self.keep_coda_logits,
+            keep_logits=self.keep_logits,
         )
         if logits is not None:
-            self.coda_logits.append(logits)
+            self.lm_logits.append(("coda", logits))
         st.coda_batches += 1
         st.coda_tokens += len(items)
         if self._content_finish:

@@ -132,11 +132,14 @@ def random_ouro_state_dict(
     std: float = 0.02,
     norm_jitter: float = 0.05,
     gate_std: float | None = None,
+    lm_head_std: float | None = None,
 ) -> dict[str, torch.Tensor]:
     """Seeded random-init weights with the reference's parameter names.
 
     Matrices are ``N(0, std)`` (the HF ``initializer_range`` default); RMSNorm gains are
     ``1 + N(0, norm_jitter)`` so the gain multiply is exercised; the exit-gate bias is zero.
+    ``lm_head_std`` widens the LM head alone (a peaked output distribution, as a trained model
+    has, so greedy tokens are not decided by margins below bf16 resolution).
     Tensors are drawn in sorted-name order from one generator on ``device`` so the same seed
     gives the same weights on every machine with the same torch build and device type.
     """
@@ -154,6 +157,8 @@ def random_ouro_state_dict(
             t = torch.zeros(dims, device=device, dtype=torch.float32)
         elif name == "model.early_exit_gate.weight":
             t = gate_std * torch.randn(dims, generator=gen, device=device, dtype=torch.float32)
+        elif name == "lm_head.weight" and lm_head_std is not None:
+            t = lm_head_std * torch.randn(dims, generator=gen, device=device, dtype=torch.float32)
         else:
             t = std * torch.randn(dims, generator=gen, device=device, dtype=torch.float32)
         out[name] = t.to(dtype)

@@ -152,10 +152,13 @@ class OuroRunner:
         max_num_seqs: int,
         max_num_batched_tokens: int,
         use_cuda_graph: bool = True,
+        gemm_backend: str = "tcgen05",
     ) -> None:
         if device.type != "cuda":
             raise RuntimeError("the B200 CDB runner needs a CUDA device; there is no CPU path")
         _lib.load()
+        # cuBLAS may otherwise reduce split-K partial sums of bf16 GEMMs in bf16; keep fp32.
+        torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
         self.shape = shape
         self.device = device
         self.kv_policy = kv_policy
@@ -178,6 +181,12 @@ class OuroRunner:
         self.stream = torch.cuda.Stream(device=device)
         self.uploader = Uploader(device)
         self.num_sms = torch.cuda.get_device_properties(device).multi_processor_count
+        if gemm_backend not in ("tcgen05", "cublas"):
+            raise ValueError(f"gemm_backend must be 'tcgen05' or 'cublas', got {gemm_backend!r}")
+        self.gemm_backend = gemm_backend
+        # split-K scratch of the tcgen05 GEMM (L2-resident partials; counters stay zeroed)
+        self.gemm_ws = torch.zeros(32 << 20, dtype=torch.float32, device=device)
+        self.gemm_ctr = torch.zeros(1 << 14, dtype=torch.int32, device=device)
         self.attn_ctas = 2 * self.num_sms
         H, D = shape.hidden_size, shape.head_dim
         Hq = shape.num_attention_heads * D
@@ -249,7 +258,17 @@ class OuroRunner:
         return torch.cuda.current_stream(self.device).cuda_stream
 
     def _mm(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> None:
-        torch.mm(a, w.t(), out=out)
+        """out = a @ w^T: the tcgen05 GEMM of libcdb (``gemm_backend='tcgen05'``) or cuBLAS."""
+
+        if self.gemm_backend == "cublas":
+            torch.mm(a, w.t(), out=out)
+            return
+        m, k = a.shape
+        _lib.call(
+            "cdb_gemm_bf16", _lib.ptr(a), a.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(out), out.stride(0),
+            m, w.shape[0], k, 0, _lib.ptr(self.gemm_ws), self.gemm_ws.numel(), _lib.ptr(self.gemm_ctr),
+            self.gemm_ctr.numel(), self.num_sms, _lib.ptr(self.status), self._sp(),
+        )
 
     # ------------------------------------------------------------------ stage bodies
     def _plan(self, item_pos: torch.Tensor, n: int, append: int) -> None:
@@ -388,7 +407,8 @@ class OuroRunner:
         log_rows: list[int],
         req_slots: list[int],
         slot_for_step: list[int],
-    ) -> None:
+        keep_logits: bool = False,
+    ) -> torch.Tensor | None:
         """Full-depth monolithic prefill over a varlen batch of prompt chunks (no early exit)."""
 
         s = self.shape
@@ -420,6 +440,9 @@ class OuroRunner:
                     "cdb_argmax", _lib.ptr(self.logits), self.logits.stride(0), k, s.vocab_size,
                     _lib.ptr(self.token_log), _lib.ptr(sel[1]), _lib.ptr(sel[2]), _lib.ptr(self.token_table), sp,
                 )
+                if keep_logits:
+                    return self.logits[:k].clone()
+        return None
 
     def prelude(self, token_ids: list[int], req_slots: list[int], hidden: list[int]) -> None:
         """Embed each item's token into its bank slot; id -1 takes the request's device token."""

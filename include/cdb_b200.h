@@ -96,6 +96,22 @@ int cdb_rope_append_kv(void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_c
                        const void* rope_cos, const void* rope_sin, int num_items, int num_heads, int head_dim,
                        int block_size, void* stream);
 
+/* bf16 tensor-core GEMM on tcgen05/TMEM: c[M,N] = x[M,K] * w[N,K]^T (fp32 accumulation, bf16
+ * store). Replaces the nn.Linear projections of the shared block and the LM head
+ * (OuroAttention q/k/v/o_proj modeling_ouro.py:371-374,431; OuroMLP gate/up/down :162-168;
+ * lm_head adapters/ouro.py:321-329), which the reference runs on cuBLAS through ATen.
+ *   x, w       row-major bf16, leading dimensions ldx, ldw (multiples of 8), 16-byte aligned.
+ *   splits     K splits (<= 0: chosen from the tile count and num_sms); splits > 1 needs
+ *              workspace (fp32, cdb_gemm_workspace_elems) and num_counters zeroed int32 counters
+ *              (left zeroed). Without enough workspace the call runs unsplit.
+ * Deterministic: split partials are summed in split order. */
+int cdb_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int M, int N, int K,
+                  int splits, float* workspace, int64_t workspace_elems, int32_t* counters, int num_counters,
+                  int num_sms, int32_t* status, void* stream);
+
+/* fp32 workspace elements cdb_gemm_bf16 uses for an automatically split problem (0 = unsplit). */
+int64_t cdb_gemm_workspace_elems(int M, int N, int K, int num_sms);
+
 /* ---------------------------------------------------------------------------------------
  * Row-wise fused elementwise kernels (bf16 activations, fp32 math, bf16 rounding at the
  * points PyTorch rounds). Optional index arrays (nullable) gather input rows / scatter output

@@ -1,0 +1,60 @@
+"""Multi-process host logic of the request-sharded replicas, on CPU with the gloo backend.
+
+Each rank of ``bench.py`` is an independent engine replica; the only cross-rank step is the
+aggregation after the timed region (max of the times, sum of the tokens), tested here with two
+gloo ranks. Replicas get distinct seeded request sets.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, out) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import bench
+
+        dev, wall, tok = bench.aggregate(1.0 + rank, 2.0 + 3 * rank, 100.0 * (rank + 1), torch.device("cpu"))
+        prompts, max_new, depths = bench.workload(bench.replica_seed(0, rank), 4, 16)
+        out.put((rank, dev, wall, tok, prompts[0][:5], sum(max_new)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_aggregation_and_distinct_shards():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, dev, wall, tok, _head, _n in results:
+        assert dev == 2.0 and wall == 5.0 and tok == 300.0, rank
+    assert results[0][4] != results[1][4]  # different request sets per replica
+
+
+def test_single_process_aggregation_is_identity():
+    import bench
+
+    if dist.is_initialized():
+        pytest.skip("process group already initialised")
+    assert bench.aggregate(1.5, 2.5, 7.0, torch.device("cpu")) == (1.5, 2.5, 7.0)
