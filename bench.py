@@ -57,6 +57,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--out-cap", type=int, default=1024, help="cap on output lengths (smaller = profiling case)")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--gemm", default="cublas", choices=["tcgen05", "cublas"], help="dense GEMM backend")
+    p.add_argument("--num-blocks", type=int, default=16384, help="KV pool blocks (small for profiler captures)")
+    p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle timing (profiling runs)")
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
 
@@ -149,7 +151,7 @@ def build_engine(args, device):
     model = OuroForCausalLM.random_init(shape, seed=1234, dtype=torch.bfloat16, device=device)
     cfg = ContinuousDepthBatchingConfig(
         block_size=16,
-        num_blocks=16384,
+        num_blocks=args.num_blocks,
         max_recurrent_steps=4,
         synthetic_exit_replay=True,
         use_async_batching=False,
@@ -312,7 +314,7 @@ def run_b200(args) -> None:
             "roofline": roof,
             "clocks": clocks.summary(),
         }
-        if world == 1:
+        if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(seconds=20.0)
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -35,6 +35,10 @@ _SIGNATURES: dict[str, list] = {
         c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int64, c_int,
         c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
     ],
+    "cdb_prefill_attention": [
+        c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int64, c_int,
+        c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_float, c_void_p, c_void_p,
+    ],
     "cdb_gemm_bf16": [
         c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_int,
         c_int, c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_void_p,

@@ -293,6 +293,36 @@ class OuroRunner:
             self.scale, self.attn_ctas, _lib.ptr(self.status), self._sp(),
         )
 
+    def _prefill_attention(self, cache_layer: int) -> None:
+        """Tiled causal attention of the current prefill batch (tiles uploaded by ``prefill``)."""
+
+        s, pool = self.shape, self.pool
+        _lib.call(
+            "cdb_prefill_attention", _lib.ptr(self.qkv), self.qkv.stride(0), self.k_col, self.v_col,
+            _lib.ptr(self.attn), self.attn.stride(0), _lib.ptr(pool.kv), pool.num_cache_layers, pool.rows,
+            cache_layer, _lib.ptr(pool.block_table), pool.block_table.stride(0), _lib.ptr(self._tiles),
+            self._num_tiles, s.num_attention_heads, s.head_dim, self.block_size, self.scale, _lib.ptr(self.status),
+            self._sp(),
+        )
+
+    @staticmethod
+    def prefill_tiles(item_slot: list[int], item_pos: list[int], tile_rows: int = 64) -> list[tuple[int, int, int, int]]:
+        """Split prefill rows into runs of <= 64 consecutive positions of one request."""
+
+        tiles: list[tuple[int, int, int, int]] = []
+        start = 0
+        n = len(item_slot)
+        for i in range(1, n + 1):
+            if (
+                i == n
+                or item_slot[i] != item_slot[start]
+                or item_pos[i] != item_pos[i - 1] + 1
+                or i - start == tile_rows
+            ):
+                tiles.append((start, i - start, item_slot[start], item_pos[start]))
+                start = i
+        return tiles
+
     def _layer_stack(self, n: int, base_layer: int, item_slot, item_pos, append: int, final_dst, final_rows, gate: bool):
         """All shared layers over rows ``[0, n)`` of the work buffers; residual stream in ``xw``."""
 
@@ -312,7 +342,7 @@ class OuroRunner:
                     _lib.ptr(item_pos), 1, _lib.ptr(self.rope_cos), _lib.ptr(self.rope_sin), n,
                     s.num_attention_heads, s.head_dim, self.block_size, sp,
                 )
-                self._attention(n, base_layer + l, item_slot, item_pos, 0, 0)
+                self._prefill_attention(base_layer + l)
             self._mm(self.attn[:n], w.w_o[l], self.o[:n])
             _lib.call(
                 "cdb_add_rmsnorm", _lib.ptr(self.xw), self.xw.stride(0), _lib.ptr(self.o), self.o.stride(0),
@@ -423,7 +453,9 @@ class OuroRunner:
                 "cdb_embed", _lib.ptr(self.w.embed), s.hidden_size, s.vocab_size, _lib.ptr(meta[0]), None, None,
                 _lib.ptr(self.xw), self.xw.stride(0), None, n, _lib.ptr(self.status), sp,
             )
-            self._plan(meta[2], n, 0)
+            tiles = self.prefill_tiles(item_slot, item_pos)
+            self._tiles = self.upload(tiles)
+            self._num_tiles = len(tiles)
             for step in range(s.total_ut_steps):
                 _lib.call(
                     "cdb_rmsnorm", _lib.ptr(self.xw), self.xw.stride(0), None,

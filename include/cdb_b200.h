@@ -87,6 +87,19 @@ int cdb_paged_decode_attn_append(const void* qkv, int64_t qkv_stride, int64_t k_
 /* Bytes of split-combine scratch (part_o + part_ml + counters) for `scratch_items` rows. */
 int64_t cdb_attn_scratch_bytes(int scratch_items, int num_heads, int head_dim);
 
+/* Causal paged prefill attention over prompt-chunk tiles (the varlen branch of
+ * paged_attention_forward, transformers integrations/flash_paged.py:50-81, after
+ * PagedAttentionCache.update, continuous_batching/cache.py:284-318).
+ *   tiles  int4 [num_tiles] {row_start, num_rows <= 64, resident slot, position of row_start}:
+ *          consecutive rows of one request; each row attends to keys [0, its position] of that
+ *          request through the block table. q must already be rotated and the chunk's k/v
+ *          written (cdb_rope_append_kv). head_dim 64 or 128. */
+int cdb_prefill_attention(const void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col, void* out,
+                          int64_t out_stride, const void* kv_base, int num_cache_layers, int64_t kv_rows,
+                          int cache_layer, const int32_t* block_table, int64_t block_table_stride, const void* tiles,
+                          int num_tiles, int num_heads, int head_dim, int block_size, float scale, int32_t* status,
+                          void* stream);
+
 /* Rotate q in place and rotate+write k and v of every row into its cache row (prefill path).
  * Replaces apply_rotary_pos_emb (modeling_ouro.py:186-204) + PagedAttentionCache.update's
  * index_copy_ writes (continuous_batching/cache.py:284-318). */

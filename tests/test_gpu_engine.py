@@ -7,8 +7,9 @@
   The device block table is read back and compared with the host block lists.
 * Numerics: teacher-forced on the fp32 oracle's tokens (so one flipped argmax cannot derail the
   rest of a sequence), every LM-head launch's logits are as accurate against the fp32 oracle as
-  the reference-style bf16 oracle's are, within ``2e-2 * max(1, |logit|max)`` of the bf16
-  oracle's (``tests/numerics.py``), and the greedy tokens agree on >= 99% of positions.
+  the reference-style bf16 oracle's are, closer to the bf16 oracle than it is to fp32, and the
+  greedy tokens agree with the bf16 oracle's at >= 99% of the positions its margin decides
+  (criteria and rationale in ``tests/numerics.py``).
 """
 
 from __future__ import annotations
@@ -23,7 +24,7 @@ from continuous_depth_batching_b200 import ContinuousDepthBatchingConfig, Contin
 from continuous_depth_batching_b200.ouro import random_ouro_state_dict
 from oracle.engine import OracleConfig, OracleEngine
 from oracle.workloads import ouro_lognormal_workload
-from tests.numerics import logit_tolerance, max_abs
+from tests.numerics import assert_report, compare_lm_launches
 
 pytestmark = pytest.mark.gpu
 GOLDEN = Path(__file__).resolve().parent / "golden"
@@ -111,8 +112,7 @@ def _oracle(shape, sd, prompts, max_new, depths, dtype, forced=None, kv_policy="
 def _compare_teacher_forced(shape, sd, prompts, max_new, depths, kv_policy="single"):
     """fp32 oracle -> tokens; bf16 oracle and GPU engine both forced onto those tokens.
 
-    Returns (GPU greedy agreement with the fp32 tokens, worst GPU-vs-bf16 logit diff over the
-    logit tolerance, accuracy errors (gpu, reference-bf16) against fp32).
+    Returns the ``tests.numerics.compare_lm_launches`` report over every LM-head launch.
     """
 
     o32, toks = _oracle(shape, sd, prompts, max_new, depths, torch.float32, kv_policy=kv_policy)
@@ -120,29 +120,13 @@ def _compare_teacher_forced(shape, sd, prompts, max_new, depths, kv_policy="sing
     eng = _engine(shape, sd, kv_policy=kv_policy, max_model_len=4096)
     eng.record_trace = True
     eng.keep_logits = True
-    outs = eng.generate_batch(prompts, max_new_tokens=max_new, eos_token_id=None, exit_depths=depths, forced_tokens=toks)
+    eng.generate_batch(prompts, max_new_tokens=max_new, eos_token_id=None, exit_depths=depths, forced_tokens=toks)
     assert eng.launch_trace == o32.launches == o16.launches
-    mine = [o.generated_tokens for o in outs]
-    total = sum(len(t) for t in toks)
-    same = sum(int(a == b) for x, y in zip(mine, toks, strict=True) for a, b in zip(x, y, strict=True))
     kinds = [k for k, _ in eng.lm_logits]
     assert kinds == [k for k, _ in o16.logits] == [k for k, _ in o32.logits]
-    gpu = [lg for _, lg in eng.lm_logits]
-    ref = [lg for _, lg in o16.logits]
-    truth = [lg for _, lg in o32.logits]
-    worst_ratio = max(max_abs(a, b) / logit_tolerance(b) for a, b in zip(gpu, ref, strict=True))
-    gpu_err = max(max_abs(a, t) for a, t in zip(gpu, truth, strict=True))
-    ref_err = max(max_abs(b, t) for b, t in zip(ref, truth, strict=True))
-    print(f"agreement {same}/{total}; worst gpu-vs-bf16 diff / tolerance {worst_ratio:.3f}; "
-          f"max logit error vs fp32: gpu {gpu_err:.4e}, reference-bf16 {ref_err:.4e}")
-    return same / total, worst_ratio, (gpu_err, ref_err)
-
-
-def _check(result, min_agree):
-    agree, worst_ratio, (gpu_err, ref_err) = result
-    assert gpu_err <= 1.25 * ref_err + 1e-3, (gpu_err, ref_err)
-    assert worst_ratio <= 1.0, worst_ratio
-    assert agree >= min_agree, agree
+    rep = compare_lm_launches([lg for _, lg in eng.lm_logits], [lg for _, lg in o16.logits], [lg for _, lg in o32.logits])
+    print(rep)
+    return rep
 
 
 def test_teacher_forced_logits_config0_shape():
@@ -151,16 +135,16 @@ def test_teacher_forced_logits_config0_shape():
     data, shape = _golden()
     run = next(r for r in data["runs"] if r["name"] == "replay_refill")
     sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
-    _check(_compare_teacher_forced(shape, sd, data["prompts"], data["max_new_tokens"], run["exit_depths"]), 0.0)
+    assert_report(_compare_teacher_forced(shape, sd, data["prompts"], data["max_new_tokens"], run["exit_depths"]))
 
 
 def test_teacher_forced_greedy_tokens_peaked_head():
-    """Greedy tokens agree on >= 99% of positions once the LM head is peaked like a trained one."""
+    """Same criteria with a wide LM head (logit scale ~14 instead of ~1.4)."""
 
     data, shape = _golden()
     run = next(r for r in data["runs"] if r["name"] == "replay_refill")
     sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"], lm_head_std=0.2)
-    _check(_compare_teacher_forced(shape, sd, data["prompts"], data["max_new_tokens"], run["exit_depths"]), 0.99)
+    assert_report(_compare_teacher_forced(shape, sd, data["prompts"], data["max_new_tokens"], run["exit_depths"]))
 
 
 def test_teacher_forced_ouro_1p4b_width_two_layers():
@@ -173,7 +157,7 @@ def test_teacher_forced_ouro_1p4b_width_two_layers():
     sd = random_ouro_state_dict(shape, seed=1, lm_head_std=0.1)
     prompts, max_new, depths = ouro_lognormal_workload(6, vocab_size=shape.vocab_size, seed=3, prompt_median=40,
                                                        prompt_cap=200, out_median=8, out_cap=12)
-    _check(_compare_teacher_forced(shape, sd, prompts, max_new, depths), 0.99)
+    assert_report(_compare_teacher_forced(shape, sd, prompts, max_new, depths))
 
 
 def test_last_exited_copy_teacher_forced():
@@ -183,4 +167,4 @@ def test_last_exited_copy_teacher_forced():
     prompts = data["prompts"][:6]
     max_new = data["max_new_tokens"][:6]
     depths = run["exit_depths"][:6]
-    _check(_compare_teacher_forced(shape, sd, prompts, max_new, depths, kv_policy="last_exited"), 0.99)
+    assert_report(_compare_teacher_forced(shape, sd, prompts, max_new, depths, kv_policy="last_exited"))

@@ -313,3 +313,40 @@ def test_exit_hazard_matches_host_policy():
         assert math.isclose(float(cdf[i]), hz, rel_tol=0, abs_tol=1e-12)
         want = (int(steps[i]) + 1 >= 2) and hz >= 0.5
         assert bool(flags[i]) == want
+
+
+@pytest.mark.parametrize("heads,d", [(16, 128), (4, 64)])
+def test_prefill_attention_tiles_match_fp32(heads, d):
+    """Tiled causal prefill attention == per-row fp32 attention over [0, position]."""
+
+    from continuous_depth_batching_b200.runner import OuroRunner
+
+    gen = torch.Generator().manual_seed(21)
+    h = AttnHarness(8, heads, d, num_blocks=600)
+    table = _make_tables(5, 40, h.num_blocks, gen)
+    # chunks: (slot, past, rows) - cached prefixes, ragged lengths, a 1-row chunk, > 64-row chunks
+    chunks = [(0, 0, 150), (1, 37, 5), (2, 100, 64), (3, 0, 1), (4, 250, 129)]
+    slots, pos = [], []
+    for s, past, rows in chunks:
+        slots += [s] * rows
+        pos += list(range(past, past + rows))
+    n = len(pos)
+    tiles = OuroRunner.prefill_tiles(slots, pos)
+    assert all(t[1] <= 64 for t in tiles) and sum(t[1] for t in tiles) == n
+    tiles_d = torch.tensor(tiles, dtype=torch.int32, device=DEV).reshape(-1)
+    qkv = torch.randn(n, 3 * heads * d, device=DEV).to(torch.bfloat16)
+    out = torch.zeros(n, heads * d, device=DEV, dtype=torch.bfloat16)
+    slots_d = torch.tensor(slots, dtype=torch.int32, device=DEV)
+    pos_d = torch.tensor(pos, dtype=torch.int32, device=DEV)
+    cos, sin = _rope_tables(8, d)
+    ref, _ = _reference_decode(h, qkv, h.kv, 1, table, slots_d, pos_d, cos, sin, append=0)
+    hd = heads * d
+    _lib.call(
+        "cdb_prefill_attention", _lib.ptr(qkv), qkv.stride(0), hd, 2 * hd, _lib.ptr(out), out.stride(0), _lib.ptr(h.kv),
+        h.layers, h.rows, 1, _lib.ptr(table), table.stride(0), _lib.ptr(tiles_d), len(tiles), heads, d, BS, d**-0.5,
+        _lib.ptr(h.status), torch.cuda.current_stream().cuda_stream,
+    )
+    torch.cuda.synchronize()
+    assert int(h.status.item()) == 0
+    err = (out.float() - ref).abs().max().item()
+    assert err < 2e-2, err
