@@ -4,14 +4,16 @@
 // different positions and recurrent steps. Work is split into units (row, head group,
 // KV split) by cdb_attn_plan so CTAs see roughly equal byte counts despite ragged contexts.
 //
-// Each CTA is warp specialised: one producer warp streams K and V pages of the unit
-// through a NSTAGE-deep shared-memory ring with 4-D TMA tile loads (one 16-token x HG-head x
-// D tile per page, completion on an mbarrier); HG consumer warps, one per head, do the
-// QK dot products, the online softmax and the PV accumulation in fp32 from shared memory.
-// The appended token's k/v never round-trip through the cache: the unit holding the last
-// split rotates k, folds the new token in from registers and writes k/v to its cache row.
-// Splits of one (row, head group) combine through scratch: the last CTA to finish (atomic
-// counter) merges the partial (m, l, o) triples and resets its counter.
+// Decode rows first go through rope_append_kernel (rotate q in place, rotate k, write k/v to the
+// row's cache slot), so the attention kernel itself only reads the cache: row p attends over
+// positions [0, p]. Each CTA is warp specialised: one producer warp prefetches a unit's block
+// ids with one coalesced load and streams its K and V pages through an NSTAGE-deep
+// shared-memory ring with 4-D TMA tile loads (one 16-token x HG-head x D tile per page,
+// completion on an mbarrier, no multicast); two consumer warps per head split every page's 16
+// tokens, each keeping its own fp32 online-softmax state (QK dot products from conflict-free
+// 16-byte shared-memory reads, base-2 softmax with warp shuffles, PV accumulation), and merge
+// at the end of the unit. Splits of one (row, head) combine through scratch: the last warp to
+// finish (atomic counter) merges the partial (m, l, o) triples and resets its counter.
 #include <cuda.h>
 
 #include <cstdio>
@@ -30,36 +32,36 @@ constexpr float kLog2e = 1.4426950408889634f;
 template <int D, int HG>
 struct AttnCfg {
   static constexpr int NSTAGE = 3;
+  static constexpr int WPH = 2;                  // consumer warps per head
+  static constexpr int TPW = kBlock / WPH;       // tokens of a page per warp
   static constexpr int LPT = (D == 96) ? 4 : 8;  // lanes cooperating on one token's QK dot
   static constexpr int DPL = D / LPT;            // dims per lane in QK
   static constexpr int TPP = 32 / LPT;           // tokens per pass
-  static constexpr int PASSES = kBlock / TPP;
+  static constexpr int PASSES = TPW / TPP;
   static constexpr int NPAIR = D / 2;
   static constexpr int PPL = (NPAIR + 31) / 32;  // bf16 pairs per lane in PV
-  static constexpr int NCH = DPL / 8;          // 16-byte chunks per lane; lane cq owns chunks cq + c*LPT
+  static constexpr int NCH = DPL / 8;            // 16-byte chunks per lane; lane cq owns chunks cq + c*LPT
   static constexpr int TILE_BYTES = kBlock * HG * D * 2;
   static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-  static constexpr int THREADS = (HG + 1) * 32;
-  static constexpr int SMEM = NSTAGE * STAGE_BYTES + 2 * NSTAGE * 8 + 64;
+  static constexpr int CONSUMERS = HG * WPH;
+  static constexpr int THREADS = (CONSUMERS + 1) * 32;
+  static constexpr int MERGE_FLOATS = D + 2;
+  static constexpr int SMEM = NSTAGE * STAGE_BYTES + 2 * NSTAGE * 8 + HG * MERGE_FLOATS * 4 + 64;
   static_assert(DPL % 8 == 0, "QK lane slice must be whole 16-byte chunks");
+  static_assert(TPW % TPP == 0, "tokens per warp must be whole passes");
 };
 
 struct AttnParams {
   const __nv_bfloat16* qkv;
-  int64_t qkv_stride, k_col, v_col;
+  int64_t qkv_stride;
   __nv_bfloat16* out;
   int64_t out_stride;
-  __nv_bfloat16* kv;
   int64_t kv_rows;
   int cache_layer;
   const int32_t* block_table;
   int64_t bt_stride;
   const int32_t* item_slot;
   const int32_t* item_pos;
-  int rope_mode;
-  const void* rope_cos;
-  const void* rope_sin;
-  int append;
   const int32_t* hdr;
   const int4* units;
   float* part_o;
@@ -72,39 +74,9 @@ struct AttnParams {
 
 // Rotated value of element d of one head vector (Ouro split-half rotate_half RoPE with
 // bf16 cos/sin, every product and the sum rounded to bf16 as PyTorch's bf16 ops round).
-__device__ __forceinline__ float rope_elem(const __nv_bfloat16* x, int d, int D, const __nv_bfloat16* cos_row,
-                                           const __nv_bfloat16* sin_row) {
-  const int half = D / 2;
-  const float xv = bf16_to_f(x[d]);
-  const float rot = d < half ? -bf16_to_f(x[d + half]) : bf16_to_f(x[d - half]);
-  const float a = round_bf16(xv * bf16_to_f(cos_row[d]));
-  const float b = round_bf16(rot * bf16_to_f(sin_row[d]));
-  return round_bf16(a + b);
-}
-
-// Huginn interleaved-pair rotation in fp32 (modeling_huginn.py:178-196): pairs (2i, 2i+1).
-__device__ __forceinline__ float rope_elem_pairs(const __nv_bfloat16* x, int d, const float* cos_row,
-                                                 const float* sin_row) {
-  const int i = d >> 1;
-  const float x0 = bf16_to_f(x[2 * i]);
-  const float x1 = bf16_to_f(x[2 * i + 1]);
-  const float c = cos_row[i], s = sin_row[i];
-  return round_bf16((d & 1) ? (x0 * s + x1 * c) : (x0 * c - x1 * s));
-}
-
-template <int D>
-__device__ __forceinline__ float load_rot(const AttnParams& p, const __nv_bfloat16* x, int d, int pos) {
-  if (p.rope_mode == 1) {
-    const __nv_bfloat16* c = static_cast<const __nv_bfloat16*>(p.rope_cos) + (int64_t)pos * D;
-    const __nv_bfloat16* s = static_cast<const __nv_bfloat16*>(p.rope_sin) + (int64_t)pos * D;
-    return rope_elem(x, d, D, c, s);
-  }
-  if (p.rope_mode == 2) {
-    const float* c = static_cast<const float*>(p.rope_cos) + (int64_t)pos * (D / 2);
-    const float* s = static_cast<const float*>(p.rope_sin) + (int64_t)pos * (D / 2);
-    return rope_elem_pairs(x, d, c, s);
-  }
-  return bf16_to_f(x[d]);
+__device__ __forceinline__ float rope_half(float x_d, float x_partner, bool low_half, float c, float s) {
+  const float rot = low_half ? -x_partner : x_partner;
+  return round_bf16(round_bf16(x_d * c) + round_bf16(rot * s));
 }
 
 template <int D, int HG>
@@ -114,42 +86,56 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NSTAGE * C::STAGE_BYTES);
   uint64_t* empty = full + C::NSTAGE;
+  float* merge = reinterpret_cast<float*>(empty + C::NSTAGE);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NSTAGE; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], HG);
+      mbar_init(&empty[s], C::CONSUMERS);
     }
     fence_barrier_init();
   }
+  if (warp == C::CONSUMERS && lane == 0) prefetch_tensormap(&map);
   __syncthreads();
+  pdl_trigger();
+  pdl_wait();
 
   const int n_units = p.hdr[0];
   const int sb = p.hdr[1];
-  if (warp == HG) {
+
+  if (warp == C::CONSUMERS) {
     // ------------------------------------------------------------- producer warp
-    if (lane == 0) {
-      prefetch_tensormap(&map);
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-        const int4 unit = p.units[u];
-        const int pos = p.item_pos[unit.x];
-        const int n_cached = p.append ? pos : pos + 1;
-        const int nb = (n_cached + kBlock - 1) / kBlock;
-        const int b0 = unit.z * sb;
-        const int b1 = min(b0 + sb, nb);
-        const int32_t* bt = p.block_table + (int64_t)p.item_slot[unit.x] * p.bt_stride;
-        for (int blk = b0; blk < b1; ++blk) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) return;
-          const int block_id = bt[blk];
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-          uint8_t* dst = smem + stage * C::STAGE_BYTES;
-          tma_load_4d(dst, &map, &full[stage], 0, unit.y * HG, block_id * kBlock, 2 * p.cache_layer);
-          tma_load_4d(dst + C::TILE_BYTES, &map, &full[stage], 0, unit.y * HG, block_id * kBlock,
-                      2 * p.cache_layer + 1);
+    if (lane == 0) prefetch_tensormap(&map);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool alive = true;
+    for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
+      const int4 unit = p.units[u];
+      const int pos = p.item_pos[unit.x];
+      const int nb = (pos + kBlock) / kBlock;
+      const int b0 = unit.z * sb;
+      const int b1 = min(b0 + sb, nb);
+      const int32_t* bt = p.block_table + (int64_t)p.item_slot[unit.x] * p.bt_stride;
+      for (int base = b0; base < b1 && alive; base += 32) {
+        const int my = base + lane < b1 ? bt[base + lane] : 0;
+        const int cnt = min(32, b1 - base);
+        for (int i = 0; i < cnt; ++i) {
+          const int block_id = __shfl_sync(0xffffffffu, my, i);
+          if (lane == 0) {
+            if (mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
+              mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+              uint8_t* dst = smem + stage * C::STAGE_BYTES;
+              tma_load_4d(dst, &map, &full[stage], 0, unit.y * HG, block_id * kBlock, 2 * p.cache_layer);
+              tma_load_4d(dst + C::TILE_BYTES, &map, &full[stage], 0, unit.y * HG, block_id * kBlock,
+                          2 * p.cache_layer + 1);
+            } else {
+              alive = false;
+            }
+          }
+          alive = __shfl_sync(0xffffffffu, alive, 0);
+          if (!alive) break;
           if (++stage == C::NSTAGE) {
             stage = 0;
             phase ^= 1u;
@@ -161,11 +147,15 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
   }
 
   // --------------------------------------------------------------- consumer warps
-  const int hh = warp;            // head within the group
+  const int hh = warp / C::WPH;   // head within the group
+  const int sub = warp % C::WPH;  // which half of every page's tokens
   const int tq = lane / C::LPT;   // token slot within a pass
   const int cq = lane % C::LPT;   // dim slice within the token
+  float* mslot = merge + hh * C::MERGE_FLOATS;
+  const int bar_id = 1 + hh;
   int stage = 0;
   uint32_t phase = 0;
+  bool alive = true;
 
   for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
     const int4 unit = p.units[u];
@@ -174,18 +164,23 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
     const int split = unit.z;
     const int nsplit = unit.w;
     const int pos = p.item_pos[item];
-    const int n_cached = p.append ? pos : pos + 1;
+    const int n_cached = pos + 1;
     const int nb = (n_cached + kBlock - 1) / kBlock;
     const int b0 = split * sb;
     const int b1 = min(b0 + sb, nb);
 
-    // q slice for this lane (rotated when RoPE is fused), pre-scaled by softmax_scale*log2(e).
+    // this lane's q slice (already rotated), pre-scaled by softmax_scale*log2(e)
     const __nv_bfloat16* qrow = p.qkv + (int64_t)item * p.qkv_stride + (int64_t)head * D;
     float qf[C::DPL];
 #pragma unroll
-    for (int i = 0; i < C::DPL; ++i) {
-      const int d = ((i / 8) * C::LPT + cq) * 8 + (i % 8);
-      qf[i] = (p.append ? load_rot<D>(p, qrow, d, pos) : bf16_to_f(qrow[d])) * p.scale_log2;
+    for (int c = 0; c < C::NCH; ++c) {
+      const uint4 w = *reinterpret_cast<const uint4*>(qrow + (c * C::LPT + cq) * 8);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        qf[c * 8 + 2 * k] = bf16lo(ws[k]) * p.scale_log2;
+        qf[c * 8 + 2 * k + 1] = bf16hi(ws[k]) * p.scale_log2;
+      }
     }
 
     float m = -INFINITY, l = 0.f;
@@ -193,67 +188,66 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
 #pragma unroll
     for (int i = 0; i < 2 * C::PPL; ++i) o[i] = 0.f;
 
-    bool ok = true;
     for (int blk = b0; blk < b1; ++blk) {
-      if (!mbar_wait(&full[stage], phase, p.status)) {
-        ok = false;
-        break;
-      }
-      const uint8_t* kt = smem + stage * C::STAGE_BYTES;
-      const uint8_t* vt = kt + C::TILE_BYTES;
-      float s[C::PASSES];
+      if (alive && !mbar_wait(&full[stage], phase, p.status)) alive = false;
+      if (alive) {
+        const uint8_t* kt = smem + stage * C::STAGE_BYTES;
+        const uint8_t* vt = kt + C::TILE_BYTES;
+        float s[C::PASSES];
 #pragma unroll
-      for (int ps = 0; ps < C::PASSES; ++ps) {
-        const int t = ps * C::TPP + tq;
-        const uint4* krow = reinterpret_cast<const uint4*>(kt + ((t * HG + hh) * D + cq * 8) * 2);
-        float acc0 = 0.f, acc1 = 0.f;
+        for (int ps = 0; ps < C::PASSES; ++ps) {
+          const int t = sub * C::TPW + ps * C::TPP + tq;
+          const uint4* krow = reinterpret_cast<const uint4*>(kt + ((t * HG + hh) * D + cq * 8) * 2);
+          float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
-        for (int c = 0; c < C::NCH; ++c) {
-          const uint4 w = krow[c * C::LPT];
-          acc0 = fmaf(qf[c * 8 + 0], bf16lo(w.x), acc0);
-          acc1 = fmaf(qf[c * 8 + 1], bf16hi(w.x), acc1);
-          acc0 = fmaf(qf[c * 8 + 2], bf16lo(w.y), acc0);
-          acc1 = fmaf(qf[c * 8 + 3], bf16hi(w.y), acc1);
-          acc0 = fmaf(qf[c * 8 + 4], bf16lo(w.z), acc0);
-          acc1 = fmaf(qf[c * 8 + 5], bf16hi(w.z), acc1);
-          acc0 = fmaf(qf[c * 8 + 6], bf16lo(w.w), acc0);
-          acc1 = fmaf(qf[c * 8 + 7], bf16hi(w.w), acc1);
+          for (int c = 0; c < C::NCH; ++c) {
+            const uint4 w = krow[c * C::LPT];
+            acc0 = fmaf(qf[c * 8 + 0], bf16lo(w.x), acc0);
+            acc1 = fmaf(qf[c * 8 + 1], bf16hi(w.x), acc1);
+            acc0 = fmaf(qf[c * 8 + 2], bf16lo(w.y), acc0);
+            acc1 = fmaf(qf[c * 8 + 3], bf16hi(w.y), acc1);
+            acc0 = fmaf(qf[c * 8 + 4], bf16lo(w.z), acc0);
+            acc1 = fmaf(qf[c * 8 + 5], bf16hi(w.z), acc1);
+            acc0 = fmaf(qf[c * 8 + 6], bf16lo(w.w), acc0);
+            acc1 = fmaf(qf[c * 8 + 7], bf16hi(w.w), acc1);
+          }
+          float acc = acc0 + acc1;
+#pragma unroll
+          for (int off = C::LPT / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+          s[ps] = (blk * kBlock + t < n_cached) ? acc : -INFINITY;
         }
-        float acc = acc0 + acc1;
+        float mb = s[0];
 #pragma unroll
-        for (int off = C::LPT / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-        s[ps] = (blk * kBlock + t < n_cached) ? acc : -INFINITY;
-      }
-      float mb = s[0];
+        for (int ps = 1; ps < C::PASSES; ++ps) mb = fmaxf(mb, s[ps]);
 #pragma unroll
-      for (int ps = 1; ps < C::PASSES; ++ps) mb = fmaxf(mb, s[ps]);
+        for (int off = C::LPT; off < 32; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+        const float m_new = fmaxf(m, mb);
+        const float alpha = (m_new == -INFINITY) ? 1.f : exp2f(m - m_new);
+        float psum = 0.f;
 #pragma unroll
-      for (int off = C::LPT; off < 32; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
-      const float m_new = fmaxf(m, mb);
-      const float alpha = (m_new == -INFINITY) ? 1.f : exp2f(m - m_new);
-      float psum = 0.f;
+        for (int ps = 0; ps < C::PASSES; ++ps) {
+          s[ps] = (s[ps] == -INFINITY) ? 0.f : exp2f(s[ps] - m_new);
+          psum += s[ps];
+        }
 #pragma unroll
-      for (int ps = 0; ps < C::PASSES; ++ps) {
-        s[ps] = (s[ps] == -INFINITY) ? 0.f : exp2f(s[ps] - m_new);
-        psum += s[ps];
-      }
+        for (int off = C::LPT; off < 32; off <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
+        l = l * alpha + psum;
+        m = m_new;
 #pragma unroll
-      for (int off = C::LPT; off < 32; off <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
-      l = l * alpha + psum;
-      m = m_new;
+        for (int i = 0; i < 2 * C::PPL; ++i) o[i] *= alpha;
+        const uint32_t* vrow = reinterpret_cast<const uint32_t*>(vt);
 #pragma unroll
-      for (int i = 0; i < 2 * C::PPL; ++i) o[i] *= alpha;
-      const uint32_t* vrow = reinterpret_cast<const uint32_t*>(vt);
+        for (int tt = 0; tt < C::TPW; ++tt) {
+          const int t = sub * C::TPW + tt;
+          const float pt = __shfl_sync(0xffffffffu, s[tt / C::TPP], (tt % C::TPP) * C::LPT);
 #pragma unroll
-      for (int t = 0; t < kBlock; ++t) {
-        const float pt = __shfl_sync(0xffffffffu, s[t / C::TPP], (t % C::TPP) * C::LPT);
-#pragma unroll
-        for (int i = 0; i < C::PPL; ++i) {
-          const int j = lane + 32 * i;
-          if (j < C::NPAIR) {
-            const uint32_t w = vrow[(t * HG + hh) * C::NPAIR + j];
-            o[2 * i] = fmaf(pt, bf16lo(w), o[2 * i]);
-            o[2 * i + 1] = fmaf(pt, bf16hi(w), o[2 * i + 1]);
+          for (int i = 0; i < C::PPL; ++i) {
+            const int j = lane + 32 * i;
+            if (j < C::NPAIR) {
+              const uint32_t w = vrow[(t * HG + hh) * C::NPAIR + j];
+              o[2 * i] = fmaf(pt, bf16lo(w), o[2 * i]);
+              o[2 * i + 1] = fmaf(pt, bf16hi(w), o[2 * i + 1]);
+            }
           }
         }
       }
@@ -264,47 +258,41 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
         phase ^= 1u;
       }
     }
-    if (!ok) return;
 
-    // The appended token: rotate k, fold it in from registers, write k/v to its cache row.
-    if (p.append && split == nsplit - 1) {
-      const __nv_bfloat16* krow = p.qkv + (int64_t)item * p.qkv_stride + p.k_col + (int64_t)head * D;
-      const __nv_bfloat16* vsrc = p.qkv + (int64_t)item * p.qkv_stride + p.v_col + (int64_t)head * D;
-      float acc = 0.f;
-#pragma unroll
-      for (int i = 0; i < C::DPL; ++i) acc = fmaf(qf[i], load_rot<D>(p, krow, ((i / 8) * C::LPT + cq) * 8 + (i % 8), pos), acc);
-#pragma unroll
-      for (int off = C::LPT / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-      const float m_new = fmaxf(m, acc);
-      const float alpha = (m_new == -INFINITY) ? 1.f : exp2f(m - m_new);
-      const float pn = exp2f(acc - m_new);
-      l = l * alpha + pn;
-      m = m_new;
-      const uint32_t* v32 = reinterpret_cast<const uint32_t*>(vsrc);
+    // merge the two token halves of this head
+    if (sub == 1) {
 #pragma unroll
       for (int i = 0; i < C::PPL; ++i) {
         const int j = lane + 32 * i;
         if (j < C::NPAIR) {
-          const uint32_t w = v32[j];
-          o[2 * i] = fmaf(pn, bf16lo(w), o[2 * i] * alpha);
-          o[2 * i + 1] = fmaf(pn, bf16hi(w), o[2 * i + 1] * alpha);
+          mslot[2 * j] = o[2 * i];
+          mslot[2 * j + 1] = o[2 * i + 1];
         }
       }
-      const int32_t* bt = p.block_table + (int64_t)p.item_slot[item] * p.bt_stride;
-      const int64_t row = (int64_t)bt[pos / kBlock] * kBlock + pos % kBlock;
-      if (row < 0 || row >= p.kv_rows) {
-        if (lane == 0) set_error(p.status, CDB_ERR_INDEX);
-      } else {
-        const int64_t hstride = (int64_t)p.num_heads * D;
-        __nv_bfloat16* kdst = p.kv + ((int64_t)(2 * p.cache_layer) * p.kv_rows + row) * hstride + (int64_t)head * D;
-        __nv_bfloat16* vdst =
-            p.kv + ((int64_t)(2 * p.cache_layer + 1) * p.kv_rows + row) * hstride + (int64_t)head * D;
-        for (int d = lane; d < D; d += 32) {
-          kdst[d] = f_to_bf16(load_rot<D>(p, krow, d, pos));
-          vdst[d] = vsrc[d];
+      if (lane == 0) {
+        mslot[D] = m;
+        mslot[D + 1] = l;
+      }
+    }
+    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(64) : "memory");
+    if (sub == 0) {
+      const float m2 = mslot[D], l2 = mslot[D + 1];
+      const float mm = fmaxf(m, m2);
+      const float w1 = (m == -INFINITY) ? 0.f : exp2f(m - mm);
+      const float w2 = (m2 == -INFINITY) ? 0.f : exp2f(m2 - mm);
+      l = l * w1 + l2 * w2;
+      m = mm;
+#pragma unroll
+      for (int i = 0; i < C::PPL; ++i) {
+        const int j = lane + 32 * i;
+        if (j < C::NPAIR) {
+          o[2 * i] = o[2 * i] * w1 + mslot[2 * j] * w2;
+          o[2 * i + 1] = o[2 * i + 1] * w1 + mslot[2 * j + 1] * w2;
         }
       }
     }
+    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(64) : "memory");
+    if (sub != 0 || !alive) continue;
 
     __nv_bfloat16* orow = p.out + (int64_t)item * p.out_stride + (int64_t)head * D;
     if (nsplit == 1) {
@@ -317,33 +305,29 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
       continue;
     }
 
-    // Split-KV: publish the partial, the last CTA of this (row, head group) merges.
+    // Split-KV: publish the partial; the last warp of this (row, head) merges all splits.
     const int64_t pidx = ((int64_t)item * p.num_heads + head) * kMaxSplits + split;
     float* po = p.part_o + pidx * D;
 #pragma unroll
     for (int i = 0; i < C::PPL; ++i) {
       const int j = lane + 32 * i;
-      if (j < C::NPAIR) {
-        po[2 * j] = o[2 * i];
-        po[2 * j + 1] = o[2 * i + 1];
-      }
+      if (j < C::NPAIR) *reinterpret_cast<float2*>(po + 2 * j) = make_float2(o[2 * i], o[2 * i + 1]);
     }
-    if (lane == 0) {
-      p.part_ml[2 * pidx] = m;
-      p.part_ml[2 * pidx + 1] = l;
-    }
-    __threadfence();
+    if (lane == 0) *reinterpret_cast<float2*>(p.part_ml + 2 * pidx) = make_float2(m, l);
     __syncwarp();
     int last = 0;
     if (lane == 0) {
+      __threadfence();
       int32_t* ctr = p.counters + (int64_t)item * p.num_heads + head;
       const int prev = atomicAdd(ctr, 1);
       last = (prev == nsplit - 1);
-      if (last) atomicExch(ctr, 0);
+      if (last) {
+        atomicExch(ctr, 0);
+        __threadfence();
+      }
     }
     last = __shfl_sync(0xffffffffu, last, 0);
     if (!last) continue;
-    __threadfence();
     const int64_t base = ((int64_t)item * p.num_heads + head) * kMaxSplits;
     float mx = -INFINITY;
     for (int sp = 0; sp < nsplit; ++sp) mx = fmaxf(mx, __ldcg(p.part_ml + 2 * (base + sp)));
@@ -352,16 +336,17 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
 #pragma unroll
     for (int i = 0; i < 2 * C::PPL; ++i) acc[i] = 0.f;
     for (int sp = 0; sp < nsplit; ++sp) {
-      const float ms = __ldcg(p.part_ml + 2 * (base + sp));
-      const float w = (ms == -INFINITY) ? 0.f : exp2f(ms - mx);
-      lsum += w * __ldcg(p.part_ml + 2 * (base + sp) + 1);
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + 2 * (base + sp)));
+      const float w = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - mx);
+      lsum += w * ml.y;
       const float* ps = p.part_o + (base + sp) * D;
 #pragma unroll
       for (int i = 0; i < C::PPL; ++i) {
         const int j = lane + 32 * i;
         if (j < C::NPAIR) {
-          acc[2 * i] = fmaf(w, __ldcg(ps + 2 * j), acc[2 * i]);
-          acc[2 * i + 1] = fmaf(w, __ldcg(ps + 2 * j + 1), acc[2 * i + 1]);
+          const float2 v = __ldcg(reinterpret_cast<const float2*>(ps + 2 * j));
+          acc[2 * i] = fmaf(w, v.x, acc[2 * i]);
+          acc[2 * i + 1] = fmaf(w, v.y, acc[2 * i + 1]);
         }
       }
     }
@@ -380,6 +365,8 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const int32_t* item_pos
                                                          int32_t* hdr, int4* units) {
   __shared__ int s_total, s_max, s_sb;
   __shared__ int s_warp[32];
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x == 0) {
     s_total = 0;
     s_max = 0;
@@ -389,7 +376,7 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const int32_t* item_pos
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int pos = item_pos[i];
     if (pos < 0) continue;
-    const int nc = append ? pos : pos + 1;
+    const int nc = pos + 1;
     const int nb = (nc + kBlock - 1) / kBlock;
     local_total += nb;
     local_max = max(local_max, nb);
@@ -415,7 +402,7 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const int32_t* item_pos
     if (i < n) {
       const int pos = item_pos[i];
       if (pos >= 0) {
-        const int nc = append ? pos : pos + 1;
+        const int nc = pos + 1;
         const int nb = (nc + kBlock - 1) / kBlock;
         ns = max(1, (nb + sb - 1) / sb);
         cnt = ns * nhg;
@@ -461,45 +448,70 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const int32_t* item_pos
   }
 }
 
-// ------------------------------------------------------------------ prefill rope + append
+// ------------------------------------------------------------------ rope + append
+// One CTA per row: rotate q in place, rotate k, write k and v to the row's cache slot. Each
+// thread owns one rotation pair of one head, so the in-place update needs no synchronisation.
 __global__ void rope_append_kernel(__nv_bfloat16* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col,
                                    __nv_bfloat16* kv, int64_t kv_rows, int cache_layer, const int32_t* block_table,
                                    int64_t bt_stride, const int32_t* item_slot, const int32_t* item_pos,
-                                   int rope_mode, const void* rope_cos, const void* rope_sin, int n, int num_heads,
-                                   int D) {
+                                   int rope_mode, const void* rope_cos, const void* rope_sin, int num_heads, int D,
+                                   int32_t* status) {
+  pdl_trigger();
+  pdl_wait();
   const int item = blockIdx.x;
   const int pos = item_pos[item];
   if (pos < 0) return;
-  const int head = blockIdx.y;
-  __nv_bfloat16* q = qkv + (int64_t)item * qkv_stride + (int64_t)head * D;
-  __nv_bfloat16* k = qkv + (int64_t)item * qkv_stride + k_col + (int64_t)head * D;
-  const __nv_bfloat16* v = qkv + (int64_t)item * qkv_stride + v_col + (int64_t)head * D;
-  float qr = 0.f, kr = 0.f;
-  const int d = threadIdx.x;
-  if (d < D) {
-    if (rope_mode == 1) {
-      const __nv_bfloat16* c = static_cast<const __nv_bfloat16*>(rope_cos) + (int64_t)pos * D;
-      const __nv_bfloat16* s = static_cast<const __nv_bfloat16*>(rope_sin) + (int64_t)pos * D;
-      qr = rope_elem(q, d, D, c, s);
-      kr = rope_elem(k, d, D, c, s);
-    } else if (rope_mode == 2) {
-      const float* c = static_cast<const float*>(rope_cos) + (int64_t)pos * (D / 2);
-      const float* s = static_cast<const float*>(rope_sin) + (int64_t)pos * (D / 2);
-      qr = rope_elem_pairs(q, d, c, s);
-      kr = rope_elem_pairs(k, d, c, s);
-    } else {
-      qr = bf16_to_f(q[d]);
-      kr = bf16_to_f(k[d]);
-    }
+  const int32_t* bt = block_table + (int64_t)item_slot[item] * bt_stride;
+  const int blk = bt[pos / kBlock];
+  const int64_t row = (int64_t)blk * kBlock + pos % kBlock;
+  if (blk < 0 || row >= kv_rows) {
+    if (threadIdx.x == 0) set_error(status, CDB_ERR_INDEX);
+    return;
   }
-  __syncthreads();
-  if (d < D) {
-    q[d] = f_to_bf16(qr);
-    const int32_t* bt = block_table + (int64_t)item_slot[item] * bt_stride;
-    const int64_t row = (int64_t)bt[pos / kBlock] * kBlock + pos % kBlock;
-    const int64_t hstride = (int64_t)num_heads * D;
-    kv[((int64_t)(2 * cache_layer) * kv_rows + row) * hstride + (int64_t)head * D + d] = f_to_bf16(kr);
-    kv[((int64_t)(2 * cache_layer + 1) * kv_rows + row) * hstride + (int64_t)head * D + d] = v[d];
+  const int64_t hstride = (int64_t)num_heads * D;
+  __nv_bfloat16* q = qkv + (int64_t)item * qkv_stride;
+  const __nv_bfloat16* k = q + k_col;
+  const __nv_bfloat16* v = q + v_col;
+  __nv_bfloat16* kd = kv + ((int64_t)(2 * cache_layer) * kv_rows + row) * hstride;
+  __nv_bfloat16* vd = kv + ((int64_t)(2 * cache_layer + 1) * kv_rows + row) * hstride;
+  const int half = D / 2;
+  for (int i = threadIdx.x; i < num_heads * half; i += blockDim.x) {
+    const int h = i / half, j = i % half;
+    const int64_t hb = (int64_t)h * D;
+    if (rope_mode == 1) {
+      const __nv_bfloat16* cr = static_cast<const __nv_bfloat16*>(rope_cos) + (int64_t)pos * D;
+      const __nv_bfloat16* sr = static_cast<const __nv_bfloat16*>(rope_sin) + (int64_t)pos * D;
+      const int d0 = j, d1 = j + half;
+      const float q0 = bf16_to_f(q[hb + d0]), q1 = bf16_to_f(q[hb + d1]);
+      const float k0 = bf16_to_f(k[hb + d0]), k1 = bf16_to_f(k[hb + d1]);
+      const float c0 = bf16_to_f(cr[d0]), s0 = bf16_to_f(sr[d0]), c1 = bf16_to_f(cr[d1]), s1 = bf16_to_f(sr[d1]);
+      q[hb + d0] = f_to_bf16(rope_half(q0, q1, true, c0, s0));
+      q[hb + d1] = f_to_bf16(rope_half(q1, q0, false, c1, s1));
+      kd[hb + d0] = f_to_bf16(rope_half(k0, k1, true, c0, s0));
+      kd[hb + d1] = f_to_bf16(rope_half(k1, k0, false, c1, s1));
+      vd[hb + d0] = v[hb + d0];
+      vd[hb + d1] = v[hb + d1];
+    } else if (rope_mode == 2) {
+      // Huginn interleaved pairs (2j, 2j+1) rotated in fp32 (modeling_huginn.py:178-196).
+      const float* cr = static_cast<const float*>(rope_cos) + (int64_t)pos * half;
+      const float* sr = static_cast<const float*>(rope_sin) + (int64_t)pos * half;
+      const int d0 = 2 * j, d1 = 2 * j + 1;
+      const float c = cr[j], s = sr[j];
+      const float q0 = bf16_to_f(q[hb + d0]), q1 = bf16_to_f(q[hb + d1]);
+      const float k0 = bf16_to_f(k[hb + d0]), k1 = bf16_to_f(k[hb + d1]);
+      q[hb + d0] = f_to_bf16(q0 * c - q1 * s);
+      q[hb + d1] = f_to_bf16(q1 * c + q0 * s);
+      kd[hb + d0] = f_to_bf16(k0 * c - k1 * s);
+      kd[hb + d1] = f_to_bf16(k1 * c + k0 * s);
+      vd[hb + d0] = v[hb + d0];
+      vd[hb + d1] = v[hb + d1];
+    } else {
+      const int d0 = 2 * j, d1 = 2 * j + 1;
+      kd[hb + d0] = k[hb + d0];
+      kd[hb + d1] = k[hb + d1];
+      vd[hb + d0] = v[hb + d0];
+      vd[hb + d1] = v[hb + d1];
+    }
   }
 }
 
@@ -575,8 +587,10 @@ static int launch_attn(const CUtensorMap& map, const AttnParams& p, int num_ctas
       return CDB_ERR_CUDA;
     attr_set = true;
   }
-  decode_attn_kernel<D, HG><<<num_ctas, C::THREADS, C::SMEM, stream>>>(map, p);
-  return cudaPeekAtLastError() == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
+  return launch_pdl(decode_attn_kernel<D, HG>, dim3(num_ctas), dim3(C::THREADS), C::SMEM, stream, map, p) ==
+                 cudaSuccess
+             ? CDB_OK
+             : CDB_ERR_CUDA;
 }
 
 static int heads_per_cta(int num_heads, int head_dim) {
@@ -584,6 +598,22 @@ static int heads_per_cta(int num_heads, int head_dim) {
   if (head_dim == 64 && num_heads % 4 == 0) return 4;
   if (head_dim == 96 && num_heads % 5 == 0) return 5;
   return 0;
+}
+
+static int launch_rope_append(void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col, void* kv_base,
+                              int64_t kv_rows, int cache_layer, const int32_t* block_table, int64_t bt_stride,
+                              const int32_t* item_slot, const int32_t* item_pos, int rope_mode, const void* rope_cos,
+                              const void* rope_sin, int num_items, int num_heads, int head_dim, int32_t* status,
+                              cudaStream_t st) {
+  if (num_items == 0) return CDB_OK;
+  const int pairs = num_heads * (head_dim / 2);
+  const int threads = pairs >= 1024 ? 1024 : ((pairs + 31) / 32) * 32;
+  return launch_pdl(rope_append_kernel, dim3(num_items), dim3(threads), 0, st, static_cast<__nv_bfloat16*>(qkv),
+                    qkv_stride, k_col, v_col, static_cast<__nv_bfloat16*>(kv_base), kv_rows, cache_layer, block_table,
+                    bt_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin, num_heads, head_dim,
+                    status) == cudaSuccess
+             ? CDB_OK
+             : CDB_ERR_CUDA;
 }
 
 }  // namespace cdb
@@ -597,10 +627,11 @@ extern "C" int cdb_attn_plan(const int32_t* item_pos, int num_items, int append,
   const int hg = heads_per_cta(num_heads, head_dim);
   if (hg == 0) return CDB_ERR_UNSUPPORTED;
   const int target = 8 * (num_sms > 0 ? num_sms : 148);
-  attn_plan_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(item_pos, num_items, append, num_heads / hg,
-                                                                      unit_capacity, scratch_items, target,
-                                                                      plan_header, static_cast<int4*>(units));
-  return cudaPeekAtLastError() == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
+  return launch_pdl(attn_plan_kernel, dim3(1), dim3(1024), 0, static_cast<cudaStream_t>(stream), item_pos, num_items,
+                    append, num_heads / hg, unit_capacity, scratch_items, target, plan_header,
+                    static_cast<int4*>(units)) == cudaSuccess
+             ? CDB_OK
+             : CDB_ERR_CUDA;
 }
 
 extern "C" int64_t cdb_attn_scratch_bytes(int scratch_items, int num_heads, int head_dim) {
@@ -608,45 +639,46 @@ extern "C" int64_t cdb_attn_scratch_bytes(int scratch_items, int num_heads, int 
   return parts * head_dim * 4 + parts * 2 * 4 + (int64_t)scratch_items * num_heads * 4;
 }
 
-extern "C" int cdb_paged_decode_attn_append(const void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col,
-                                            void* out, int64_t out_stride, void* kv_base, int num_cache_layers,
-                                            int64_t kv_rows, int cache_layer, const int32_t* block_table,
-                                            int64_t block_table_stride, const int32_t* item_slot,
-                                            const int32_t* item_pos, int rope_mode, const void* rope_cos,
-                                            const void* rope_sin, int append, const int32_t* plan_header,
-                                            const void* units, float* part_o, float* part_ml, int32_t* counters,
-                                            int scratch_items, int num_items, int num_heads, int head_dim,
-                                            int block_size, float scale, int num_ctas, int32_t* status,
-                                            void* stream) {
+extern "C" int cdb_paged_decode_attn_append(void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col, void* out,
+                                            int64_t out_stride, void* kv_base, int num_cache_layers, int64_t kv_rows,
+                                            int cache_layer, const int32_t* block_table, int64_t block_table_stride,
+                                            const int32_t* item_slot, const int32_t* item_pos, int rope_mode,
+                                            const void* rope_cos, const void* rope_sin, int append,
+                                            const int32_t* plan_header, const void* units, float* part_o,
+                                            float* part_ml, int32_t* counters, int scratch_items, int num_items,
+                                            int num_heads, int head_dim, int block_size, float scale, int num_ctas,
+                                            int32_t* status, void* stream) {
   if (block_size != kBlock || cache_layer < 0 || cache_layer >= num_cache_layers || num_items < 0)
     return CDB_ERR_INVALID_ARGUMENT;
-  if ((reinterpret_cast<uintptr_t>(kv_base) & 15) != 0 || (qkv_stride & 1) != 0) return CDB_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(kv_base) & 15) || (reinterpret_cast<uintptr_t>(qkv) & 15) || (qkv_stride & 7) ||
+      (k_col & 7) || (v_col & 7) || (out_stride & 1))
+    return CDB_ERR_INVALID_ARGUMENT;
   const int hg = heads_per_cta(num_heads, head_dim);
   if (hg == 0) return CDB_ERR_UNSUPPORTED;
-  if (rope_mode < 0 || rope_mode > 2 || (rope_mode != 0 && (rope_cos == nullptr || rope_sin == nullptr)))
+  if (rope_mode < 0 || rope_mode > 2 || (append && rope_mode != 0 && (rope_cos == nullptr || rope_sin == nullptr)))
     return CDB_ERR_INVALID_ARGUMENT;
   (void)scratch_items;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (append) {
+    const int rc = launch_rope_append(qkv, qkv_stride, k_col, v_col, kv_base, kv_rows, cache_layer, block_table,
+                                      block_table_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin, num_items,
+                                      num_heads, head_dim, status, st);
+    if (rc != CDB_OK) return rc;
+  }
   CUtensorMap map;
   const int rc = kv_tensor_map(&map, kv_base, num_cache_layers, kv_rows, num_heads, head_dim, hg);
   if (rc != CDB_OK) return rc;
   AttnParams p;
   p.qkv = static_cast<const __nv_bfloat16*>(qkv);
   p.qkv_stride = qkv_stride;
-  p.k_col = k_col;
-  p.v_col = v_col;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride = out_stride;
-  p.kv = static_cast<__nv_bfloat16*>(kv_base);
   p.kv_rows = kv_rows;
   p.cache_layer = cache_layer;
   p.block_table = block_table;
   p.bt_stride = block_table_stride;
   p.item_slot = item_slot;
   p.item_pos = item_pos;
-  p.rope_mode = rope_mode;
-  p.rope_cos = rope_cos;
-  p.rope_sin = rope_sin;
-  p.append = append;
   p.hdr = plan_header;
   p.units = static_cast<const int4*>(units);
   p.part_o = part_o;
@@ -655,7 +687,6 @@ extern "C" int cdb_paged_decode_attn_append(const void* qkv, int64_t qkv_stride,
   p.num_heads = num_heads;
   p.scale_log2 = scale * kLog2e;
   p.status = status;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (num_ctas <= 0) num_ctas = 2 * 148;
   if (head_dim == 128) return launch_attn<128, 4>(map, p, num_ctas, st);
   if (head_dim == 64) return launch_attn<64, 4>(map, p, num_ctas, st);
@@ -668,14 +699,10 @@ extern "C" int cdb_rope_append_kv(void* qkv, int64_t qkv_stride, int64_t k_col, 
                                   int64_t block_table_stride, const int32_t* item_slot, const int32_t* item_pos,
                                   int rope_mode, const void* rope_cos, const void* rope_sin, int num_items,
                                   int num_heads, int head_dim, int block_size, void* stream) {
-  if (block_size != kBlock || cache_layer < 0 || cache_layer >= num_cache_layers || head_dim > 1024)
+  if (block_size != kBlock || cache_layer < 0 || cache_layer >= num_cache_layers || head_dim % 2 != 0 ||
+      rope_mode < 0 || rope_mode > 2)
     return CDB_ERR_INVALID_ARGUMENT;
-  if (num_items == 0) return CDB_OK;
-  dim3 grid(num_items, num_heads);
-  const int threads = ((head_dim + 31) / 32) * 32;
-  rope_append_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<__nv_bfloat16*>(qkv), qkv_stride, k_col, v_col, static_cast<__nv_bfloat16*>(kv_base), kv_rows,
-      cache_layer, block_table, block_table_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin, num_items,
-      num_heads, head_dim);
-  return cudaPeekAtLastError() == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
+  return launch_rope_append(qkv, qkv_stride, k_col, v_col, kv_base, kv_rows, cache_layer, block_table,
+                            block_table_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin, num_items,
+                            num_heads, head_dim, nullptr, static_cast<cudaStream_t>(stream));
 }

@@ -93,6 +93,8 @@ __device__ __forceinline__ void rms_inplace(RowRegs& r, const __nv_bfloat16* wei
 __global__ void __launch_bounds__(kRowThreads) rmsnorm_kernel(const __nv_bfloat16* x, int64_t xs, const int32_t* x_rows,
                                                               const __nv_bfloat16* w, __nv_bfloat16* y, int64_t ys,
                                                               __nv_bfloat16* xc, int64_t xcs, int hidden, float eps) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const int r = blockIdx.x;
   const int src = x_rows ? x_rows[r] : r;
@@ -110,6 +112,8 @@ __global__ void __launch_bounds__(kRowThreads) add_rmsnorm_kernel(__nv_bfloat16*
                                                                   const int32_t* y_rows, const __nv_bfloat16* gw,
                                                                   const __nv_bfloat16* gb, __nv_bfloat16* gout,
                                                                   int hidden, float eps) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const int r = blockIdx.x;
   const int dst = y_rows ? y_rows[r] : r;
@@ -144,6 +148,8 @@ __global__ void __launch_bounds__(kRowThreads) add_rmsnorm_kernel(__nv_bfloat16*
 }
 
 __global__ void silu_mul_kernel(const __nv_bfloat16* gu, int64_t gs, __nv_bfloat16* act, int64_t as, int inter) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.y;
   const int d = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (d >= inter) return;
@@ -172,6 +178,8 @@ __device__ __forceinline__ void better(float v, int i, float& bv, int& bi) {
 __global__ void __launch_bounds__(512) argmax_kernel(const __nv_bfloat16* logits, int64_t stride, int vocab,
                                                      int64_t* out, const int32_t* out_rows, const int32_t* token_rows,
                                                      int32_t* token_table) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float sv[32];
   __shared__ int si[32];
   const int r = blockIdx.x;
@@ -226,6 +234,8 @@ __global__ void __launch_bounds__(512) argmax_kernel(const __nv_bfloat16* logits
 __global__ void embed_kernel(const __nv_bfloat16* table, int hidden, int vocab, const int32_t* ids,
                              const int32_t* id_src, const int32_t* token_table, __nv_bfloat16* out, int64_t os,
                              const int32_t* out_rows, int32_t* status) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x;
   const int dst = out_rows ? out_rows[r] : r;
   if (dst < 0) return;
@@ -247,6 +257,8 @@ __global__ void embed_kernel(const __nv_bfloat16* table, int hidden, int vocab, 
 }
 
 __global__ void block_table_update_kernel(int32_t* table, int64_t stride, const int32_t* edits, int n) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   table[(int64_t)edits[3 * i] * stride + edits[3 * i + 1]] = edits[3 * i + 2];
@@ -254,6 +266,8 @@ __global__ void block_table_update_kernel(int32_t* table, int64_t stride, const 
 
 __global__ void exit_kv_copy_kernel(__nv_bfloat16* kv, int64_t kv_rows, int64_t row_elems, const int32_t* rows,
                                     const int32_t* src_layers, const int32_t* dst_layers) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t row = rows[blockIdx.x];
   const int pair = blockIdx.y;
   const int src = src_layers[pair], dst = dst_layers[pair];
@@ -267,6 +281,8 @@ __global__ void exit_kv_copy_kernel(__nv_bfloat16* kv, int64_t kv_rows, int64_t 
 __global__ void exit_hazard_kernel(const void* signal, int signal_bf16, const int32_t* slots, const int32_t* steps,
                                    const int8_t* reset, double* cdf, double* surv, int8_t* exit_out, int n,
                                    int min_steps, double threshold) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= n) return;
   const int s = slots[r];
@@ -327,7 +343,7 @@ extern "C" int cdb_rmsnorm(const void* x, int64_t x_stride, const int32_t* x_row
                            void* stream) {
   if (hidden % 8 != 0 || hidden > kRowThreads * kMaxChunks * 8 || num_rows < 0) return CDB_ERR_INVALID_ARGUMENT;
   if (num_rows == 0) return CDB_OK;
-  rmsnorm_kernel<<<num_rows, kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(rmsnorm_kernel, dim3(num_rows), dim3(kRowThreads), 0, static_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(x), x_stride, x_rows, static_cast<const __nv_bfloat16*>(weight),
       static_cast<__nv_bfloat16*>(y), y_stride, static_cast<__nv_bfloat16*>(x_copy), x_copy_stride, hidden, eps);
   return check_launch();
@@ -340,7 +356,7 @@ extern "C" int cdb_add_rmsnorm(void* x, int64_t x_stride, const void* a, int64_t
   if (hidden % 8 != 0 || hidden > kRowThreads * kMaxChunks * 8 || num_rows < 0) return CDB_ERR_INVALID_ARGUMENT;
   if (gate_w != nullptr && (gate_b == nullptr || gate_out == nullptr)) return CDB_ERR_INVALID_ARGUMENT;
   if (num_rows == 0) return CDB_OK;
-  add_rmsnorm_kernel<<<num_rows, kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(add_rmsnorm_kernel, dim3(num_rows), dim3(kRowThreads), 0, static_cast<cudaStream_t>(stream), 
       static_cast<__nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(a), a_stride,
       static_cast<const __nv_bfloat16*>(w_a), static_cast<const __nv_bfloat16*>(w_next),
       static_cast<__nv_bfloat16*>(y), y_stride, y_rows, static_cast<const __nv_bfloat16*>(gate_w),
@@ -354,7 +370,7 @@ extern "C" int cdb_silu_mul(const void* gu, int64_t gu_stride, void* act, int64_
   if (num_rows == 0) return CDB_OK;
   const int threads = 128;
   dim3 grid((inter / 8 + threads - 1) / threads, num_rows);
-  silu_mul_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(silu_mul_kernel, dim3(grid), dim3(threads), 0, static_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(gu), gu_stride, static_cast<__nv_bfloat16*>(act), act_stride, inter);
   return check_launch();
 }
@@ -363,7 +379,7 @@ extern "C" int cdb_argmax(const void* logits, int64_t stride, int num_rows, int 
                           const int32_t* out_rows, const int32_t* token_rows, int32_t* token_table, void* stream) {
   if (vocab <= 0 || num_rows < 0 || (token_rows != nullptr && token_table == nullptr)) return CDB_ERR_INVALID_ARGUMENT;
   if (num_rows == 0) return CDB_OK;
-  argmax_kernel<<<num_rows, 512, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const __nv_bfloat16*>(logits),
+  launch_pdl(argmax_kernel, dim3(num_rows), dim3(512), 0, static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(logits),
                                                                          stride, vocab, out, out_rows, token_rows, token_table);
   return check_launch();
 }
@@ -374,7 +390,7 @@ extern "C" int cdb_embed(const void* table, int hidden, int vocab, const int32_t
   if (hidden <= 0 || vocab <= 0 || num_rows < 0 || (ids == nullptr && id_src == nullptr)) return CDB_ERR_INVALID_ARGUMENT;
   if (id_src != nullptr && token_table == nullptr) return CDB_ERR_INVALID_ARGUMENT;
   if (num_rows == 0) return CDB_OK;
-  embed_kernel<<<num_rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(embed_kernel, dim3(num_rows), dim3(128), 0, static_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(table), hidden, vocab, ids, id_src, token_table,
       static_cast<__nv_bfloat16*>(out), out_stride, out_rows, status);
   return check_launch();
@@ -384,7 +400,7 @@ extern "C" int cdb_block_table_update(int32_t* table, int64_t stride, const int3
                                       void* stream) {
   if (num_edits < 0) return CDB_ERR_INVALID_ARGUMENT;
   if (num_edits == 0) return CDB_OK;
-  block_table_update_kernel<<<(num_edits + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(table, stride,
+  launch_pdl(block_table_update_kernel, dim3((num_edits + 255) / 256), dim3(256), 0, static_cast<cudaStream_t>(stream), table, stride,
                                                                                                    edits, num_edits);
   return check_launch();
 }
@@ -396,7 +412,7 @@ extern "C" int cdb_exit_kv_copy(void* kv_base, int num_cache_layers, int64_t kv_
   if (row_elems % 8 != 0 || num_rows < 0 || num_pairs < 0 || num_cache_layers <= 0) return CDB_ERR_INVALID_ARGUMENT;
   if (num_rows == 0 || num_pairs == 0) return CDB_OK;
   dim3 grid(num_rows, num_pairs);
-  exit_kv_copy_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(exit_kv_copy_kernel, dim3(grid), dim3(128), 0, static_cast<cudaStream_t>(stream), 
       static_cast<__nv_bfloat16*>(kv_base), kv_rows, row_elems, rows, src_layers, dst_layers);
   return check_launch();
 }
@@ -406,7 +422,7 @@ extern "C" int cdb_exit_hazard(const void* signal, int signal_bf16, const int32_
                                int min_steps, double threshold, void* stream) {
   if (num_rows < 0) return CDB_ERR_INVALID_ARGUMENT;
   if (num_rows == 0) return CDB_OK;
-  exit_hazard_kernel<<<(num_rows + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(exit_hazard_kernel, dim3((num_rows + 127) / 128), dim3(128), 0, static_cast<cudaStream_t>(stream), 
       signal, signal_bf16, slots, steps, reset, cdf, surv, exit_out, num_rows, min_steps, threshold);
   return check_launch();
 }

@@ -146,14 +146,26 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+  if (warp != 0) pdl_wait();  // the producer waits after prefetching weights
 
   if (warp == 0) {
     if (lane == 0) {
       prefetch_tensormap(&map_w);
       prefetch_tensormap(&map_x);
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int kb = kb0; kb < kb1; ++kb) {
+      // Weights do not depend on the previous kernel: fill the first stages' weight tiles
+      // before waiting on it, then add the activation tiles.
+      const int npre = min(STAGES, kb1 - kb0);
+      for (int i = 0; i < npre; ++i) {
+        mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+        tma_load_2d(smem + i * C::STAGE_BYTES, &map_w, &full[i], (kb0 + i) * BK, wtile * BM);
+      }
+      pdl_wait();
+      for (int i = 0; i < npre; ++i)
+        tma_load_2d(smem + i * C::STAGE_BYTES + C::A_BYTES, &map_x, &full[i], (kb0 + i) * BK, mtile * BN);
+      int stage = npre % STAGES;
+      uint32_t phase = (npre == STAGES) ? 1u : 0u;
+      for (int kb = kb0 + npre; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) break;
         uint8_t* a = smem + stage * C::STAGE_BYTES;
         mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
@@ -228,11 +240,26 @@ __global__ void __launch_bounds__(THREADS, 1)
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (*last_flag && n < p.N) {
         __threadfence();
+        // Sum the splits in split order, 8 token rows at a time so 8 independent loads are in
+        // flight per split (the partials sit in L2).
         const int m_end = min(m_base + BN, p.M);
-        for (int m = m_base; m < m_end; ++m) {
-          float acc = 0.f;
-          for (int s = 0; s < p.splits; ++s) acc += __ldcg(p.ws + ((int64_t)s * gridDim.y * BN + m) * p.N + n);
-          p.c[(int64_t)m * p.ldc + n] = f_to_bf16(acc);
+        const float* __restrict__ ws = p.ws;
+        const int64_t split_stride = (int64_t)gridDim.y * BN * p.N;
+        for (int m0 = m_base; m0 < m_end; m0 += 8) {
+          float acc[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+          for (int s = 0; s < p.splits; ++s) {
+            const float* src = ws + s * split_stride + (int64_t)m0 * p.N + n;
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = (m0 + j < m_end) ? __ldcg(src + (int64_t)j * p.N) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] += v[j];
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (m0 + j < m_end) p.c[(int64_t)(m0 + j) * p.ldc + n] = f_to_bf16(acc[j]);
         }
       }
     }
@@ -317,8 +344,9 @@ static int launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p,
       return CDB_ERR_CUDA;
     attr = true;
   }
-  gemm_kernel<BN, STAGES><<<grid, THREADS, C::SMEM, st>>>(mw, mx, p);
-  return cudaPeekAtLastError() == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
+  return launch_pdl(gemm_kernel<BN, STAGES>, grid, dim3(THREADS), C::SMEM, st, mw, mx, p) == cudaSuccess
+             ? CDB_OK
+             : CDB_ERR_CUDA;
 }
 
 }  // namespace gemm

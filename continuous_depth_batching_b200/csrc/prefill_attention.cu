@@ -72,6 +72,8 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
 
 template <int D>
 __global__ void __launch_bounds__(128) prefill_attn_kernel(Params p) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int NCH = D / 8;   // 16-byte chunks per row
   constexpr int KS = D / 16;   // k-steps over the head dim
   constexpr int NT = D / 8;    // n-tiles of the output
@@ -257,7 +259,7 @@ static int launch(const Params& p, int num_tiles, cudaStream_t st) {
     attr = true;
   }
   dim3 grid(num_tiles, p.num_heads);
-  prefill_attn_kernel<D><<<grid, 128, SMEM, st>>>(p);
+  launch_pdl(prefill_attn_kernel<D>, dim3(grid), dim3(128), SMEM, st, p);
   return cudaPeekAtLastError() == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
 }
 

@@ -65,17 +65,18 @@ int cdb_attn_plan(const int32_t* item_pos, int num_items, int append, int num_he
  * (transformers integrations/flash_paged.py:84-122), reached from OuroAttention.forward
  * (models/ouro/modeling_ouro.py:377-432) and HuginnAttention.forward
  * (models/huginn/modeling_huginn.py:244-302).
- *   qkv        bf16 [num_items, qkv_stride]: q at column 0, k at k_col, v at v_col (H*D each).
- *   rope_mode  0: q/k already rotated; 1: split-half rotate_half RoPE (Ouro);
- *              2: interleaved-pair RoPE in fp32 (Huginn), cos/sin tables given in fp32.
- *   rope_cos/rope_sin  [max_positions, head_dim] tables (bf16 for mode 1, fp32 for mode 2).
- *   append     1: rotate k, write k/v at the row's position, attend over [0,p] using the
- *              new k/v from registers; 0: attend over cached rows [0,p] only.
+ *   qkv        bf16 [num_items, qkv_stride]: q at column 0, k at k_col, v at v_col (H*D each);
+ *              16-byte aligned, strides and column offsets multiples of 8 elements.
+ *   rope_mode  0: q/k already rotated; 1: split-half rotate_half RoPE (Ouro, bf16 tables
+ *              [max_positions, head_dim]); 2: interleaved-pair RoPE in fp32 (Huginn, fp32
+ *              tables [max_positions, head_dim/2]).
+ *   append     1: rotate q in place in `qkv`, rotate k, write k/v at the row's position, then
+ *              attend over [0,p]; 0: attend over cached rows [0,p] with q already rotated.
  *   out        bf16 [num_items, out_stride], heads concatenated.
  *   part_o/part_ml/counters: split-combine scratch sized for scratch_items rows
  *              (cdb_attn_scratch_bytes); counters must start zeroed, kernels leave them zeroed.
  */
-int cdb_paged_decode_attn_append(const void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col,
+int cdb_paged_decode_attn_append(void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col,
                                  void* out, int64_t out_stride, void* kv_base, int num_cache_layers,
                                  int64_t kv_rows, int cache_layer, const int32_t* block_table,
                                  int64_t block_table_stride, const int32_t* item_slot, const int32_t* item_pos,
