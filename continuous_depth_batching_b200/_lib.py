@@ -30,6 +30,15 @@ _SIGNATURES: dict[str, list] = {
         c_int, c_int, c_int, c_int, c_int,  # scratch_items, num_items, num_heads, head_dim, block_size
         c_float, c_int, c_void_p, c_void_p,  # scale, num_ctas, status, stream
     ],
+    "cdb_paged_decode_attn_append_static": [
+        c_void_p, c_int64, c_int64, c_int64,  # qkv, stride, k_col, v_col
+        c_void_p, c_int64,  # out, out_stride
+        c_void_p, c_int, c_int64, c_int,  # kv_base, num_cache_layers, kv_rows, cache_layer
+        c_void_p, c_int64, c_void_p, c_void_p,  # block_table, stride, item_slot, item_pos
+        c_int, c_void_p, c_void_p, c_int,  # rope_mode, cos, sin, append
+        c_int, c_int, c_int, c_int,  # num_items, num_heads, head_dim, block_size
+        c_float, c_int, c_void_p, c_void_p,  # scale, num_ctas, status, stream
+    ],
     "cdb_attn_scratch_bytes": [c_int, c_int, c_int],
     "cdb_rope_append_kv": [
         c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int64, c_int,

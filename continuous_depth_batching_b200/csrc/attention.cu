@@ -706,3 +706,146 @@ extern "C" int cdb_rope_append_kv(void* qkv, int64_t qkv_stride, int64_t k_col, 
                             block_table_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin, num_items,
                             num_heads, head_dim, nullptr, static_cast<cudaStream_t>(stream));
 }
+
+// ======================================================================================
+// Allocation-free variant of cdb_paged_decode_attn_append.
+//
+// Some callers cannot call cudaMalloc at all: a function registered as the model's attention
+// hook runs inside the host framework's CUDA-graph capture (allocation is not permitted while a
+// stream is being captured), and a plugin that is handed only tensors has no allocator to ask.
+// For them the work plan and the split-KV combine scratch of this entry point live in one
+// file-scope device array instead of caller buffers. Every GPU that loads the library holds the
+// array (4,784,896 bytes) until the process exits.
+// ======================================================================================
+namespace cdb {
+namespace noalloc {
+constexpr int kRowHeads = 128;    // (rows x heads) the split-combine scratch covers
+constexpr int kMaxUnits = 32768;  // work-plan capacity (units of row x head group x split)
+constexpr int kMaxHeadDim = 128;
+constexpr size_t kPartOFloats = (size_t)kRowHeads * kMaxSplits * kMaxHeadDim;
+constexpr size_t kPartMLFloats = (size_t)kRowHeads * kMaxSplits * 2;
+constexpr size_t kOffPartML = kPartOFloats * 4;
+constexpr size_t kOffCounters = kOffPartML + kPartMLFloats * 4;
+constexpr size_t kOffHeader = kOffCounters + (size_t)kRowHeads * 4;
+constexpr size_t kOffUnits = (kOffHeader + 16 + 255) / 256 * 256;
+constexpr size_t kBytes = kOffUnits + (size_t)kMaxUnits * 16;
+constexpr int kMaxDevices = 64;
+}  // namespace noalloc
+}  // namespace cdb
+
+// The scratch itself. Host code must not use this name as a device address: it resolves to a
+// host-side shadow. Its device address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) uint8_t cdb_noalloc_scratch[cdb::noalloc::kBytes];
+
+namespace cdb {
+namespace noalloc {
+
+// Device address of the scratch array on the current device, looked up once per device with
+// that device current (the first call on a device does this; make it before any stream capture).
+static int scratch_address(uint8_t** out) {
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CDB_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, cdb_noalloc_scratch) != cudaSuccess || p == nullptr) return CDB_ERR_CUDA;
+    addr[dev] = p;
+  }
+  *out = static_cast<uint8_t*>(addr[dev]);
+  return CDB_OK;
+}
+
+// The KV pool tensor map, encoded on the stack (the cached path keeps a host-side table).
+static int encode_kv_map(CUtensorMap* map, const void* base, int layers, int64_t rows, int heads, int d, int hg) {
+  EncodeFn enc = get_encode();
+  if (enc == nullptr) return CDB_ERR_TMA_ENCODE;
+  const cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)heads, (cuuint64_t)rows, (cuuint64_t)(2 * layers)};
+  const cuuint64_t strides[3] = {(cuuint64_t)d * 2, (cuuint64_t)heads * d * 2, (cuuint64_t)rows * heads * d * 2};
+  const cuuint32_t box[4] = {(cuuint32_t)d, (cuuint32_t)hg, (cuuint32_t)kBlock, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  std::memset(map, 0, sizeof(*map));
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? CDB_OK
+             : CDB_ERR_TMA_ENCODE;
+}
+
+}  // namespace noalloc
+}  // namespace cdb
+
+extern "C" int cdb_paged_decode_attn_append_static(void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col,
+                                                   void* out, int64_t out_stride, void* kv_base, int num_cache_layers,
+                                                   int64_t kv_rows, int cache_layer, const int32_t* block_table,
+                                                   int64_t block_table_stride, const int32_t* item_slot,
+                                                   const int32_t* item_pos, int rope_mode, const void* rope_cos,
+                                                   const void* rope_sin, int append, int num_items, int num_heads,
+                                                   int head_dim, int block_size, float scale, int num_ctas,
+                                                   int32_t* status, void* stream) {
+  using namespace cdb::noalloc;
+  if (block_size != kBlock || cache_layer < 0 || cache_layer >= num_cache_layers || num_items < 0)
+    return CDB_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(kv_base) & 15) || (reinterpret_cast<uintptr_t>(qkv) & 15) || (qkv_stride & 7) ||
+      (k_col & 7) || (v_col & 7) || (out_stride & 1))
+    return CDB_ERR_INVALID_ARGUMENT;
+  const int hg = heads_per_cta(num_heads, head_dim);
+  if (hg == 0) return CDB_ERR_UNSUPPORTED;
+  if (rope_mode < 0 || rope_mode > 2 || (append && rope_mode != 0 && (rope_cos == nullptr || rope_sin == nullptr)))
+    return CDB_ERR_INVALID_ARGUMENT;
+  // Limits of the static scratch: head_dim <= 128, num_heads <= 128, and the work plan of an
+  // unsplit launch (num_items x num_heads/heads_per_CTA units) within kMaxUnits.
+  const int scratch_items = kRowHeads / num_heads;
+  if (head_dim > kMaxHeadDim || scratch_items < 1 || (int64_t)num_items * (num_heads / hg) > kMaxUnits)
+    return CDB_ERR_SCRATCH_LIMIT;
+  uint8_t* base = nullptr;
+  int rc = scratch_address(&base);
+  if (rc != CDB_OK) return rc;
+  if (num_items == 0) return CDB_OK;
+  float* part_o = reinterpret_cast<float*>(base);
+  float* part_ml = reinterpret_cast<float*>(base + kOffPartML);
+  int32_t* counters = reinterpret_cast<int32_t*>(base + kOffCounters);
+  int32_t* header = reinterpret_cast<int32_t*>(base + kOffHeader);
+  void* units = base + kOffUnits;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's contents: the split counters must start at zero.
+  if (cudaMemsetAsync(counters, 0, (size_t)kRowHeads * 4, st) != cudaSuccess) return CDB_ERR_CUDA;
+  if (append) {
+    rc = launch_rope_append(qkv, qkv_stride, k_col, v_col, kv_base, kv_rows, cache_layer, block_table,
+                            block_table_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin, num_items,
+                            num_heads, head_dim, status, st);
+    if (rc != CDB_OK) return rc;
+  }
+  const int target = 8 * 148;
+  if (launch_pdl(attn_plan_kernel, dim3(1), dim3(1024), 0, st, item_pos, num_items, 0, num_heads / hg, kMaxUnits,
+                 scratch_items, target, header, static_cast<int4*>(units)) != cudaSuccess)
+    return CDB_ERR_CUDA;
+  CUtensorMap map;
+  rc = encode_kv_map(&map, kv_base, num_cache_layers, kv_rows, num_heads, head_dim, hg);
+  if (rc != CDB_OK) return rc;
+  AttnParams p;
+  p.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  p.qkv_stride = qkv_stride;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride = out_stride;
+  p.kv_rows = kv_rows;
+  p.cache_layer = cache_layer;
+  p.block_table = block_table;
+  p.bt_stride = block_table_stride;
+  p.item_slot = item_slot;
+  p.item_pos = item_pos;
+  p.hdr = header;
+  p.units = static_cast<const int4*>(units);
+  p.part_o = part_o;
+  p.part_ml = part_ml;
+  p.counters = counters;
+  p.num_heads = num_heads;
+  p.scale_log2 = scale * kLog2e;
+  p.status = status;
+  if (num_ctas <= 0) num_ctas = 2 * 148;
+  if (head_dim == 128) return launch_attn<128, 4>(map, p, num_ctas, st);
+  if (head_dim == 64) return launch_attn<64, 4>(map, p, num_ctas, st);
+  if (head_dim == 96) return launch_attn<96, 5>(map, p, num_ctas, st);
+  return CDB_ERR_UNSUPPORTED;
+}

@@ -333,6 +333,8 @@ extern "C" const char* cdb_status_string(int status) {
       return "TMA tensor map encoding failed";
     case CDB_ERR_INDEX:
       return "device-side index out of range";
+    case CDB_ERR_SCRATCH_LIMIT:
+      return "call exceeds the static scratch limits (head_dim <= 128, num_heads <= 128, plan <= 32768 units)";
     default:
       return "unknown status";
   }

@@ -30,6 +30,7 @@ extern "C" {
 #define CDB_ERR_DEVICE_TIMEOUT 4
 #define CDB_ERR_TMA_ENCODE 5
 #define CDB_ERR_INDEX 6
+#define CDB_ERR_SCRATCH_LIMIT 7 /* call exceeds the fixed static scratch of a *_static entry point */
 
 /* Library version (major*10000 + minor*100 + patch). */
 int cdb_version(void);
@@ -84,6 +85,33 @@ int cdb_paged_decode_attn_append(void* qkv, int64_t qkv_stride, int64_t k_col, i
                                  const int32_t* plan_header, const void* units, float* part_o, float* part_ml,
                                  int32_t* counters, int scratch_items, int num_items, int num_heads, int head_dim,
                                  int block_size, float scale, int num_ctas, int32_t* status, void* stream);
+
+/* Same attention as cdb_paged_decode_attn_append (plan included), but needing no scratch from
+ * the caller: no plan buffers, no split-combine buffers. No counterpart in the reference; it
+ * exists for callers that cannot allocate device memory, such as an attention hook that runs
+ * while the host framework captures a CUDA graph (allocation is not permitted during capture)
+ * or a plugin that is handed tensors but no allocator.
+ *   Arguments mean what they mean for cdb_paged_decode_attn_append.
+ *   Scratch: one file-scope device array of 4,784,896 bytes (about 4.8 MB) per GPU, held until
+ *   the process exits.
+ *   Its device address is looked up with cudaGetSymbolAddress on the first call made with that
+ *   device current, so make one call per device (num_items = 0 is enough) before any stream
+ *   capture. Each call clears the split counters (cudaMemsetAsync on `stream`) before using them.
+ *   Limits: head_dim <= 128, num_heads <= 128, num_items * (num_heads / heads_per_CTA) <= 32768
+ *   (heads_per_CTA 4 for head_dim 64/128, 5 for 96); beyond them it returns
+ *   CDB_ERR_SCRATCH_LIMIT and enqueues nothing. KV splitting is used only while
+ *   num_items * num_heads <= 128; larger launches run one unit per (row, head group).
+ *   Every call on a device shares the one array: calls whose work can overlap (different
+ *   streams, or different host threads, without ordering between them) race on it and give
+ *   wrong results. Calls must be ordered, e.g. all on one stream. */
+int cdb_paged_decode_attn_append_static(void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col,
+                                        void* out, int64_t out_stride, void* kv_base, int num_cache_layers,
+                                        int64_t kv_rows, int cache_layer, const int32_t* block_table,
+                                        int64_t block_table_stride, const int32_t* item_slot,
+                                        const int32_t* item_pos, int rope_mode, const void* rope_cos,
+                                        const void* rope_sin, int append, int num_items, int num_heads,
+                                        int head_dim, int block_size, float scale, int num_ctas, int32_t* status,
+                                        void* stream);
 
 /* Bytes of split-combine scratch (part_o + part_ml + counters) for `scratch_items` rows. */
 int64_t cdb_attn_scratch_bytes(int scratch_items, int num_heads, int head_dim);

@@ -1,0 +1,146 @@
+"""cdb_paged_decode_attn_append_static (static scratch, no caller buffers) against the entry point
+with caller-provided scratch, both called through the C ABI.
+
+Tolerance: the attention tests' 2e-2 max-abs on the bf16 output, and exact equality of the
+appended K/V rows and of the rotated q written back into qkv. Each case makes two calls in a row
+on different inputs, so the second call runs on scratch the first one has used.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from continuous_depth_batching_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+BS = 16
+SCRATCH_LIMIT = 7  # CDB_ERR_SCRATCH_LIMIT
+
+
+def _rope_tables(max_pos: int, d: int, theta: float = 10000.0):
+    inv = 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.int64).to(torch.float32) / d))
+    freqs = torch.arange(max_pos, dtype=torch.float32, device=DEV)[:, None] * inv.to(DEV)[None, :]
+    emb = torch.cat((freqs, freqs), dim=-1)
+    return emb.cos().to(torch.bfloat16).contiguous(), emb.sin().to(torch.bfloat16).contiguous()
+
+
+class Case:
+    """One launch's inputs: a paged KV pool, block tables, rows at ragged positions."""
+
+    def __init__(self, heads, d, n_items, max_pos, seed, layers=2):
+        gen = torch.Generator().manual_seed(seed)
+        self.h, self.d, self.layers = heads, d, layers
+        self.max_blocks = max_pos // BS + 2
+        self.num_blocks = n_items * self.max_blocks + 8
+        self.rows = (self.num_blocks + 2) * BS
+        self.kv = torch.randn(layers, 2, self.rows, heads, d, generator=gen).to(torch.bfloat16).to(DEV)
+        perm = torch.randperm(self.num_blocks, generator=gen)[: n_items * self.max_blocks]
+        self.table = perm.view(n_items, self.max_blocks).to(torch.int32).to(DEV)
+        pos = torch.randint(0, max_pos, (n_items,), generator=gen).to(torch.int32)
+        pos[0] = 0
+        if n_items > 3:
+            pos[1] = 15
+            pos[2] = -1  # padding row
+        self.pos = pos.to(DEV)
+        self.slots = torch.arange(n_items, dtype=torch.int32, device=DEV)
+        self.qkv = torch.randn(n_items, 3 * heads * d, generator=gen).to(torch.bfloat16).to(DEV)
+        self.cos, self.sin = _rope_tables(max_pos + 1, d)
+        self.rope_mode = 1 if d != 96 else 0
+        self.n = n_items
+
+
+def _run_scratch(c: Case, qkv, kv, out, layer, append, status, stream):
+    """The existing entry point with caller-provided plan and split-combine buffers."""
+    hg = 5 if c.d == 96 else 4
+    scratch_items = max(1, 128 // c.h)
+    cap = max(scratch_items * (c.h // hg) * 64, c.n * (c.h // hg))
+    hdr = torch.zeros(4, dtype=torch.int32, device=DEV)
+    units = torch.zeros(cap, 4, dtype=torch.int32, device=DEV)
+    part_o = torch.zeros(scratch_items * c.h * 64 * c.d, device=DEV)
+    part_ml = torch.zeros(scratch_items * c.h * 64 * 2, device=DEV)
+    counters = torch.zeros(scratch_items * c.h, dtype=torch.int32, device=DEV)
+    _lib.call(
+        "cdb_attn_plan", _lib.ptr(c.pos), c.n, append, c.h, c.d, BS, cap, scratch_items, 148,
+        _lib.ptr(hdr), _lib.ptr(units), stream,
+    )
+    hd = c.h * c.d
+    _lib.call(
+        "cdb_paged_decode_attn_append", _lib.ptr(qkv), qkv.stride(0), hd, 2 * hd, _lib.ptr(out), out.stride(0),
+        _lib.ptr(kv), c.layers, c.rows, layer, _lib.ptr(c.table), c.table.stride(0), _lib.ptr(c.slots),
+        _lib.ptr(c.pos), c.rope_mode, _lib.ptr(c.cos), _lib.ptr(c.sin), append, _lib.ptr(hdr), _lib.ptr(units),
+        _lib.ptr(part_o), _lib.ptr(part_ml), _lib.ptr(counters), scratch_items, c.n, c.h, c.d, BS, c.d**-0.5, 296,
+        _lib.ptr(status), stream,
+    )
+    torch.cuda.synchronize()
+
+
+def _static_args(c: Case, qkv, kv, out, layer, append, n, status, stream):
+    hd = c.h * c.d
+    return (
+        _lib.ptr(qkv), qkv.stride(0), hd, 2 * hd, _lib.ptr(out), out.stride(0), _lib.ptr(kv), c.layers, c.rows,
+        layer, _lib.ptr(c.table), c.table.stride(0), _lib.ptr(c.slots), _lib.ptr(c.pos), c.rope_mode,
+        _lib.ptr(c.cos), _lib.ptr(c.sin), append, n, c.h, c.d, BS, c.d**-0.5, 296, _lib.ptr(status), stream,
+    )
+
+
+def _run_static(c: Case, qkv, kv, out, layer, append, status, stream):
+    _lib.call("cdb_paged_decode_attn_append_static", *_static_args(c, qkv, kv, out, layer, append, c.n, status, stream))
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize(
+    "heads,d,n_items,max_pos",
+    [
+        (16, 128, 6, 3000),  # 96 row-heads: KV splits through the static combine scratch
+        (16, 128, 80, 600),  # 1280 row-heads: one unit per (row, head group)
+        (4, 64, 24, 400),
+        (55, 96, 2, 900),
+    ],
+)
+def test_static_scratch_matches_scratch_entry_two_calls(heads, d, n_items, max_pos):
+    stream = torch.cuda.current_stream().cuda_stream
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    setup = Case(heads, d, 1, 16, seed=1)
+    # First call with this device current: looks up the scratch address, enqueues nothing.
+    _lib.call(
+        "cdb_paged_decode_attn_append_static",
+        *_static_args(setup, setup.qkv, setup.kv, setup.qkv, 0, 1, 0, status, stream),
+    )
+    for call, (layer, append) in enumerate([(1, 1), (0, 0)]):
+        c = Case(heads, d, n_items, max_pos, seed=100 * call + heads + n_items)
+        qkv_a, qkv_b = c.qkv.clone(), c.qkv.clone()
+        kv_a, kv_b = c.kv.clone(), c.kv.clone()
+        out_a = torch.zeros(c.n, heads * d, device=DEV, dtype=torch.bfloat16)
+        out_b = torch.zeros_like(out_a)
+        _run_scratch(c, qkv_a, kv_a, out_a, layer, append, status, stream)
+        assert int(status.item()) == 0
+        _run_static(c, qkv_b, kv_b, out_b, layer, append, status, stream)
+        assert int(status.item()) == 0
+        err = (out_a.float() - out_b.float()).abs().max().item()
+        assert err < 2e-2, (call, err)
+        assert torch.equal(qkv_a, qkv_b), call
+        assert torch.equal(kv_a, kv_b), call
+        assert out_b[c.pos >= 0].abs().sum().item() > 0
+
+
+def test_static_scratch_limits_rejected():
+    stream = torch.cuda.current_stream().cuda_stream
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    lib = _lib.load()
+    # 132 heads of 128: more row-heads than the split-combine scratch holds for even one row.
+    wide = Case(132, 128, 1, 16, seed=2)
+    rc = lib.cdb_paged_decode_attn_append_static(*_static_args(wide, wide.qkv, wide.kv, wide.qkv, 0, 1, 1, status, stream))
+    assert rc == SCRATCH_LIMIT
+    # 8193 rows x 4 head groups: the work plan would exceed 32768 units. Rejected on the host
+    # before anything is enqueued, so the buffers of a one-row case suffice.
+    small = Case(16, 128, 1, 16, seed=3)
+    rc = lib.cdb_paged_decode_attn_append_static(
+        *_static_args(small, small.qkv, small.kv, small.qkv, 0, 1, 8193, status, stream)
+    )
+    assert rc == SCRATCH_LIMIT
+    assert b"static scratch" in lib.cdb_status_string(SCRATCH_LIMIT)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
