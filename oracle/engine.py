@@ -28,6 +28,12 @@ Every launch is appended to ``launches`` in the golden-fixture format:
 ``forced_tokens`` (teacher forcing) makes the engine continue every request with the given
 tokens instead of its own argmax, so a second engine's per-position predictions can be
 compared against these without autoregressive divergence.
+
+Two model families: Ouro (:class:`OuroOracle`; prelude = embedding, coda = LM head, exit
+signal = gate logit under the cumulative-hazard rule) and Huginn (:class:`HuginnOracle`;
+``HuginnCDBAdapter`` ``adapters/huginn.py``: prelude and coda are attention blocks writing
+their own cache layers, the hidden vector is ``[state | injection]``, the exit signal is the
+latent difference under the direct-threshold rule ``exit_policy.py:167-168``).
 """
 
 from __future__ import annotations
@@ -37,8 +43,10 @@ from dataclasses import dataclass, field
 
 import torch
 
+from continuous_depth_batching_b200.huginn import HuginnShape
 from continuous_depth_batching_b200.ouro import OuroShape
 
+from .huginn_math import HuginnOracle, HuginnWeights
 from .ouro_math import OracleKVCache, OuroOracle, OuroWeights
 
 PENDING, PREFILLING, DECODING, FINISHED = 0, 1, 2, 3
@@ -123,15 +131,24 @@ class Item:
 class OracleEngine:
     """Synchronous-mode CDB engine on CPU over :class:`OuroOracle` math."""
 
-    def __init__(self, shape: OuroShape, state_dict: dict, cfg: OracleConfig, dtype: torch.dtype = torch.float32):
+    def __init__(
+        self, shape: OuroShape | HuginnShape, state_dict: dict, cfg: OracleConfig, dtype: torch.dtype = torch.float32
+    ):
         if cfg.kv_policy not in KV_POLICIES:
             raise ValueError(f"unknown kv_policy {cfg.kv_policy!r}")
         self.shape = shape
         self.cfg = cfg
         self.dtype = dtype
+        self.huginn = isinstance(shape, HuginnShape)
         self.slots = slots_per_layer(cfg.kv_policy, cfg.max_recurrent_steps, cfg.kv_slots_per_layer)
-        self.num_cache_layers = self.slots * shape.num_hidden_layers
-        self.weights = OuroWeights.from_state_dict(shape, state_dict, dtype)
+        if self.huginn:
+            self.core_layers = shape.n_layers_in_recurrent_block
+            self.num_cache_layers = shape.n_layers_in_prelude + self.slots * self.core_layers + shape.n_layers_in_coda
+            self.weights = HuginnWeights.from_state_dict(shape, state_dict, dtype)
+        else:
+            self.core_layers = shape.num_hidden_layers
+            self.num_cache_layers = self.slots * shape.num_hidden_layers
+            self.weights = OuroWeights.from_state_dict(shape, state_dict, dtype)
         self.max_num_seqs = min(cfg.max_num_seqs, cfg.max_num_batched_tokens)
         self.min_free = (
             max(1, self.max_num_seqs // 8) if cfg.min_free_slots is None else min(cfg.min_free_slots, self.max_num_seqs)
@@ -338,9 +355,12 @@ class OracleEngine:
             }
         )
         hidden = torch.stack([it.hidden for it in items])
-        out, gate = self.model.recurrent_step(
-            hidden, [it.position for it in items], blocks, slot * self.shape.num_hidden_layers
-        )
+        if self.huginn:
+            out, gate = self.model.recurrent_step(hidden, [it.position for it in items], blocks, slot)
+        else:
+            out, gate = self.model.recurrent_step(
+                hidden, [it.position for it in items], blocks, slot * self.shape.num_hidden_layers
+            )
         for i, it in enumerate(items):
             it.hidden = out[i]
         self.stats["recurrent_batches"] += 1
@@ -354,10 +374,13 @@ class OracleEngine:
             return step >= item.depth
         if self.cfg.exit_threshold is None:
             return False
+        can_exit = step + 1 >= self.cfg.min_recurrent_steps
+        if self.huginn:
+            return can_exit and float(gate[i].float().item()) < self.cfg.exit_threshold
         hazard = float(torch.sigmoid(gate[i]).float().item())
         item.cdf += hazard * item.survival
         item.survival *= 1.0 - hazard
-        return step + 1 >= self.cfg.min_recurrent_steps and item.cdf >= self.cfg.exit_threshold
+        return can_exit and item.cdf >= self.cfg.exit_threshold
 
     def _record_exit(self, item: Item, step: int) -> None:
         item.req.exit_depths.append(step)
@@ -374,21 +397,30 @@ class OracleEngine:
         by_step: dict[int, list[Item]] = {}
         for item, step in backlog:
             by_step.setdefault(step, []).append(item)
-        bs, layers = self.cfg.block_size, self.shape.num_hidden_layers
+        bs, layers = self.cfg.block_size, self.core_layers
+        first = self.shape.n_layers_in_prelude if self.huginn else 0
         for step, items in sorted(by_step.items()):
             rows = torch.tensor(
                 [self.tables[it.req.idx][it.position // bs] * bs + it.position % bs for it in items], dtype=torch.long
             )
             src_slot = slot_for_step(self.cfg.kv_policy, step, self.slots)
             for layer in range(layers):
-                dst = [t * layers + layer for t in range(src_slot + 1, self.slots)]
+                dst = [first + t * layers + layer for t in range(src_slot + 1, self.slots)]
                 if dst:
-                    self.model.copy_rows(src_slot * layers + layer, dst, rows)
+                    self.model.copy_rows(first + src_slot * layers + layer, dst, rows)
+
+    def _item_blocks(self, it: Item) -> list[int]:
+        return self.tables[it.req.idx][: -(-(it.position + 1) // self.cfg.block_size)]
 
     def _prelude(self, items: list[Item]) -> None:
         if not items:
             return
-        emb = self.model.embed([it.token for it in items])
+        if self.huginn:
+            emb = self.model.prelude(
+                [it.token for it in items], [it.position for it in items], [self._item_blocks(it) for it in items]
+            )
+        else:
+            emb = self.model.embed([it.token for it in items])
         for i, it in enumerate(items):
             it.hidden = emb[i]
 
@@ -396,7 +428,10 @@ class OracleEngine:
         self.launches.append({"kind": "coda", "items": [[it.req.idx, it.position, it.step] for it in items]})
         for it in items:
             it.req.in_flight_tokens += 1
-        logits = self.model.lm_head(torch.stack([it.hidden for it in items]))
+        hidden = torch.stack([it.hidden for it in items])
+        if self.huginn:
+            hidden = self.model.coda(hidden, [it.position for it in items], [self._item_blocks(it) for it in items])
+        logits = self.model.lm_head(hidden)
         self.logits.append(("coda", logits))
         self.stats["coda_batches"] += 1
         self.stats["coda_tokens"] += len(items)
@@ -553,9 +588,11 @@ class OracleEngine:
         caps = [min(m, cfg.max_model_len - len(p)) for m, p in zip(max_new_tokens, prompts, strict=True)]
         self.free: deque[int] = deque(range(cfg.num_blocks))
         self.tables: dict[int, list[int]] = {}
-        self.model = OuroOracle(
-            self.weights, OracleKVCache(self.shape, self.num_cache_layers, cfg.num_blocks, cfg.block_size, self.dtype)
-        )
+        cache = OracleKVCache(self.shape, self.num_cache_layers, cfg.num_blocks, cfg.block_size, self.dtype)
+        if self.huginn:
+            self.model = HuginnOracle(self.weights, cache, self.slots)
+        else:
+            self.model = OuroOracle(self.weights, cache)
         self.waiting: OrderedDict[int, Req] = OrderedDict()
         self.active: OrderedDict[int, Req] = OrderedDict()
         self.in_flight: set[int] = set()

@@ -1,0 +1,184 @@
+"""Generate the Huginn golden fixtures by running the reference engine itself on CPU.
+
+Run in a container that has the reference checkout (read-only) at ``$CDB_REFERENCE_SRC``
+(default ``/root/reference/src``)::
+
+    python tests/golden/make_golden_huginn.py
+
+It builds the reference's own ``HuginnForCausalLM`` at a small shape with Huginn's structure
+(prelude / recurrent core / coda, 96-wide heads, ``qk_bias``, interleaved RoPE, tied LM head),
+loads seeded weights from :func:`continuous_depth_batching_b200.huginn.random_huginn_state_dict`,
+registers the CPU restatement of the paged FlashAttention contract and drives the reference
+``ContinuousDepthBatchingEngine.generate_batch`` (``HuginnCDBAdapter``, synchronous mode).
+Runs: the live latent-difference exit gate (direct threshold) with refill, then its recorded
+exit depths replayed with refill, without refill, and under ``last_exited``.
+
+Outputs ``tests/golden/huginn_small.json`` (tokens, stats, launch traces with block-table rows)
+and ``tests/golden/huginn_small_logits.npz`` (the first LM-head calls of the live run).
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO))
+sys.path.insert(0, str(HERE))
+sys.path.insert(0, os.environ.get("CDB_REFERENCE_SRC", "/root/reference/src"))
+
+from make_golden import Recorder, recorded_exit_depths  # noqa: E402
+
+from continuous_depth_batching_b200.huginn import HuginnShape, random_huginn_state_dict  # noqa: E402
+from oracle.paged_attention import cpu_paged_attention_forward  # noqa: E402
+from oracle.workloads import config0_workload  # noqa: E402
+
+SMALL = HuginnShape(
+    vocab_size=1024,
+    n_embd=480,
+    n_heads=5,
+    intermediate_size=1280,
+    n_layers_in_prelude=1,
+    n_layers_in_recurrent_block=2,
+    n_layers_in_coda=1,
+    total_recurrent_steps=6,
+    rope_base=50000.0,
+    norm_eps=1e-6,
+    qk_bias=True,
+    max_position_embeddings=2048,
+)
+# Relative latent-difference threshold of the live run: a level the random-init states cross
+# after a few steps, so the run mixes exit depths.
+EXIT_THRESHOLD = 0.4
+EMBED_STD = 0.5
+
+
+def build_reference_model(shape: HuginnShape):
+    from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
+
+    from looped_cdb.models.huginn.configuration_huginn import HuginnConfig
+    from looped_cdb.models.huginn.modeling_huginn import HuginnForCausalLM
+
+    ALL_ATTENTION_FUNCTIONS["paged|flash_attention_3"] = cpu_paged_attention_forward
+    config = HuginnConfig(
+        n_embd=shape.n_embd,
+        n_heads=shape.n_heads,
+        n_layers=shape.n_layers_in_prelude + shape.n_layers_in_recurrent_block + shape.n_layers_in_coda,
+        n_layers_in_prelude=shape.n_layers_in_prelude,
+        n_layers_in_recurrent_block=shape.n_layers_in_recurrent_block,
+        n_layers_in_coda=shape.n_layers_in_coda,
+        mean_recurrence=shape.total_recurrent_steps,
+        block_size=shape.max_position_embeddings,
+        vocab_size=shape.vocab_size,
+        intermediate_size=shape.intermediate_size,
+        norm_eps=shape.norm_eps,
+        rope_base=shape.rope_base,
+        qk_bias=shape.qk_bias,
+        bos_token_id=None,
+        eos_token_id=None,
+        pad_token_id=None,
+    )
+    torch.manual_seed(0)
+    model = HuginnForCausalLM(config)
+    model.config._attn_implementation = "paged|flash_attention_3"
+    state = random_huginn_state_dict(shape, seed=0, embed_std=EMBED_STD)
+    missing, unexpected = model.load_state_dict(state, strict=False)
+    assert not unexpected, unexpected
+    assert not missing, missing
+    assert torch.equal(model.lm_head.weight, model.transformer["wte"].weight)
+    model.eval()
+    return model
+
+
+def run_case(name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_depths=None, num_blocks=4096):
+    from looped_cdb.continuous_depth_batching import ContinuousDepthBatchingConfig, ContinuousDepthBatchingEngine
+
+    model = build_reference_model(SMALL)
+    prompts, max_new = config0_workload()
+    cfg = ContinuousDepthBatchingConfig(
+        block_size=16,
+        num_blocks=num_blocks,
+        max_recurrent_steps=SMALL.total_recurrent_steps,
+        exit_threshold=EXIT_THRESHOLD if live_gate else None,
+        synthetic_exit_replay=not live_gate,
+        use_async_batching=False,
+        use_cuda_graph=False,
+        use_cuda_graph_prefill=False,
+        refill=refill,
+        kv_policy=kv_policy,
+        kv_pressure_mode="reserve" if kv_policy == "last_exited" else "recompute",
+        max_model_len=2048,
+    )
+    engine = ContinuousDepthBatchingEngine.from_model(model, cfg)
+    rec = Recorder(engine)
+    with torch.no_grad():
+        outs = engine.generate_batch(
+            prompts, max_new_tokens=max_new, eos_token_id=None, warmup=False, exit_depths=exit_depths
+        )
+    stats = engine.last_stats
+    result = {
+        "name": name,
+        "kv_policy": kv_policy,
+        "refill": refill,
+        "live_gate": live_gate,
+        "tokens": [o.generated_tokens for o in outs],
+        "exit_depths": exit_depths,
+        "stats": {
+            "prefill_batches": stats.prefill_batches,
+            "recurrent_batches": stats.recurrent_batches,
+            "coda_batches": stats.coda_batches,
+            "recurrent_steps": stats.recurrent_steps,
+            "coda_tokens": stats.coda_tokens,
+            "generated_tokens": stats.generated_tokens,
+            "scheduler_refills": stats.scheduler_refills,
+            "exit_depth_histogram": {str(k): v for k, v in sorted(stats.exit_depth_histogram.items())},
+        },
+        "launches": rec.launches,
+    }
+    return result, rec.logits
+
+
+def main() -> None:
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    runs = []
+    logits_out: dict[str, np.ndarray] = {}
+    live, live_logits = run_case("live_gate_refill", kv_policy="single", refill=True, live_gate=True)
+    runs.append(live)
+    depths = recorded_exit_depths(live)
+    replay, _ = run_case("replay_refill", kv_policy="single", refill=True, live_gate=False, exit_depths=depths)
+    runs.append(replay)
+    norefill, _ = run_case("replay_norefill", kv_policy="single", refill=False, live_gate=False, exit_depths=depths)
+    runs.append(norefill)
+    lastx, _ = run_case("replay_last_exited", kv_policy="last_exited", refill=True, live_gate=False, exit_depths=depths)
+    runs.append(lastx)
+    for i, arr in enumerate(live_logits[:6]):
+        logits_out[f"live_gate_refill_{i}"] = arr.astype(np.float32)
+    prompts, max_new = config0_workload()
+    shape = dict(SMALL.__dict__)
+    payload = {
+        "generator": "tests/golden/make_golden_huginn.py",
+        "shape": shape,
+        "embed_std": EMBED_STD,
+        "exit_threshold": EXIT_THRESHOLD,
+        "weights_seed": 0,
+        "prompts": prompts,
+        "max_new_tokens": max_new,
+        "block_size": 16,
+        "num_blocks": 4096,
+        "runs": runs,
+    }
+    (HERE / "huginn_small.json").write_text(json.dumps(payload, separators=(",", ":")))
+    np.savez_compressed(HERE / "huginn_small_logits.npz", **logits_out)
+    print("wrote", HERE / "huginn_small.json", "runs:", [r["name"] for r in runs])
+    for r in runs:
+        print(r["name"], r["stats"])
+
+
+if __name__ == "__main__":
+    main()

@@ -64,3 +64,48 @@ def test_oracle_reproduces_reference_run(golden, name):
             ref = logits[f"live_gate_refill_{i}"]
             mine = engine.logits[i][1].numpy()
             np.testing.assert_allclose(mine, ref, rtol=0, atol=1e-5)
+
+
+# ----------------------------------------------------------------------------- Huginn
+# tests/golden/make_golden_huginn.py ran the reference HuginnForCausalLM + HuginnCDBAdapter at a
+# small shape with Huginn's structure (prelude/core/coda, 96-wide heads, qk_bias, interleaved
+# RoPE, tied LM head) under the live latent-difference gate and three replays.
+
+
+@pytest.fixture(scope="module")
+def golden_huginn():
+    from continuous_depth_batching_b200.huginn import HuginnShape, random_huginn_state_dict
+
+    data = json.loads((GOLDEN / "huginn_small.json").read_text())
+    shape = HuginnShape(**data["shape"])
+    sd = random_huginn_state_dict(shape, seed=data["weights_seed"], embed_std=data["embed_std"])
+    return data, shape, sd
+
+
+@pytest.mark.parametrize("name", ["live_gate_refill", "replay_refill", "replay_norefill", "replay_last_exited"])
+def test_oracle_reproduces_reference_huginn_run(golden_huginn, name):
+    data, shape, sd = golden_huginn
+    run = next(r for r in data["runs"] if r["name"] == name)
+    cfg = OracleConfig(
+        block_size=data["block_size"],
+        num_blocks=data["num_blocks"],
+        max_recurrent_steps=shape.total_recurrent_steps,
+        max_model_len=2048,
+        exit_threshold=data["exit_threshold"] if run["live_gate"] else None,
+        synthetic_exit_replay=not run["live_gate"],
+        refill=run["refill"],
+        kv_policy=run["kv_policy"],
+        kv_pressure_mode="reserve" if run["kv_policy"] == "last_exited" else "recompute",
+    )
+    engine = OracleEngine(shape, sd, cfg, torch.float32)
+    tokens = engine.generate(data["prompts"], data["max_new_tokens"], exit_depths=run["exit_depths"])
+    assert tokens == run["tokens"]
+    assert engine.launches == run["launches"]
+    assert exit_depth_histogram(engine) == run["stats"]["exit_depth_histogram"]
+    assert engine.refills == run["stats"]["scheduler_refills"]
+    assert engine.stats["recurrent_batches"] == run["stats"]["recurrent_batches"]
+    assert engine.stats["coda_batches"] == run["stats"]["coda_batches"]
+    if name == "live_gate_refill":
+        logits = np.load(GOLDEN / "huginn_small_logits.npz")
+        for i in range(len(logits.files)):
+            np.testing.assert_allclose(engine.logits[i][1].numpy(), logits[f"live_gate_refill_{i}"], rtol=0, atol=1e-5)
