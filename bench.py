@@ -166,14 +166,26 @@ def build_engine(args, device):
     return eng, shape
 
 
-def attention_roofline(eng, shape, launches: list[tuple[list[int], list[int]]], peak_gbs: float) -> dict:
-    """Time the paged decode-attention kernel alone over recorded launch shapes (CUDA events)."""
+# DRAM bytes per algorithmic byte of decode_attn_kernel<128,4>, from one ncu capture of a launch
+# of 128 rows x ~1055-token contexts (kernel_bench attention --rows 128 --context 1024):
+# dram__bytes_read.sum 1.117004 GB + dram__bytes_write.sum 9.95 MB over 1,107,100,888 algorithmic
+# bytes. Traffic grows with the pages a launch streams, so a bench launch's traffic is its
+# algorithmic bytes times this ratio.
+ATTN_TRAFFIC_PER_ALGO_BYTE = (1.117004e9 + 9.953536e6) / 1107100888
 
-    from continuous_depth_batching_b200 import _lib
+
+def attention_roofline(eng, shape, launches: list[tuple[list[int], list[int]]], peak_gbs: float) -> dict:
+    """Time the paged decode-attention kernel alone over recorded launch shapes (CUDA events).
+
+    Each recorded recurrent launch (rows' slots and positions) is replayed as the cache-only
+    attention launch of one layer (rows attend over their cached positions 0..p, which the timed
+    step wrote), on the engine stream; achieved = algorithmic bytes / mean launch time.
+    """
+
+    from continuous_depth_batching_b200.kernel_bench import attention_bytes
 
     r = eng.runner
     D, H = shape.head_dim, shape.num_attention_heads
-    row_bytes = H * D * 2
     total_bytes, total_ms, n = 0.0, 0.0, 0
     stream = r.stream
     for slots, pos in launches:
@@ -181,17 +193,15 @@ def attention_roofline(eng, shape, launches: list[tuple[list[int], list[int]]], 
         meta = r.upload([slots, pos])
         meta = meta.view(2, b)
         with torch.cuda.stream(stream):
-            r._plan(meta[1], b, 1)
-        algo = 0
-        for p in pos:
-            algo += 2 * (p + 1) * row_bytes + 2 * row_bytes + 2 * row_bytes + 4 * (-(-(p + 1) // 16))
+            r._plan(meta[1], b, 0)
+        algo = attention_bytes(pos, H, D, append=False)
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = 10
         with torch.cuda.stream(stream):
-            r._attention(b, 0, meta[0], meta[1], 1, 1)  # warm
+            r._attention(b, 0, meta[0], meta[1], 0, 0)  # warm
             start.record(stream)
             for _ in range(reps):
-                r._attention(b, 0, meta[0], meta[1], 1, 1)
+                r._attention(b, 0, meta[0], meta[1], 0, 0)
             end.record(stream)
         end.synchronize()
         ms = start.elapsed_time(end) / reps
@@ -207,8 +217,9 @@ def attention_roofline(eng, shape, launches: list[tuple[list[int], list[int]]], 
         "peak": peak_gbs,
         "unit": "GB/s",
         "frac": round(achieved / peak_gbs, 4),
-        "traffic": None,
-        "kernel": "cdb::decode_attn_kernel<128,4>",
+        "traffic": int(per_launch_bytes * ATTN_TRAFFIC_PER_ALGO_BYTE),
+        "traffic_source": "ncu dram bytes of a 128-row x 1055-token launch scaled by algorithmic bytes (ratio 1.018)",
+        "kernel": f"cdb::decode_attn_kernel<{D},{5 if D == 96 else 4}>",
         "launch_ms": round(per_launch_ms, 4),
         "algorithmic_bytes_per_launch": int(per_launch_bytes),
         "launches_timed": n,
@@ -240,7 +251,7 @@ def run_b200(args) -> None:
     orig = eng._run_recurrent
 
     def recorder(items):
-        if len(recorded) < 400 and eng.last_stats.recurrent_batches % 5 == 0:
+        if eng.last_stats.recurrent_batches % 5 == 0:
             recorded.append(([it.req.slot for it in items], [it.position for it in items]))
         return orig(items)
 
@@ -272,7 +283,9 @@ def run_b200(args) -> None:
     stats = eng.last_stats
     dev_s, wall_s, total_tokens = aggregate(dev_s, wall_s, float(gen_tokens), device)
     if rank == 0:
-        roof = attention_roofline(eng, shape, recorded[:60], peak_gbs)
+        # 60 launches spread evenly over the timed steps (every 5th recurrent launch was recorded)
+        sample = [recorded[int(i * len(recorded) / 60)] for i in range(60)] if len(recorded) > 60 else recorded
+        roof = attention_roofline(eng, shape, sample, peak_gbs)
         roof["peak_source"] = peak_src
         prompt_bytes = sum(len(p) for p in prompts) * 4 * 3
         line = {

@@ -39,6 +39,10 @@ _SIGNATURES: dict[str, list] = {
         c_int, c_int, c_int, c_int,  # num_items, num_heads, head_dim, block_size
         c_float, c_int, c_void_p, c_void_p,  # scale, num_ctas, status, stream
     ],
+    "cdb_mlp_gateup_silu_gemm": [
+        c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,  # x, ldx, w_gate_up, ldw, act, ld_act
+        c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,  # M, inter, K, splits, num_sms, status, stream
+    ],
     "cdb_attn_scratch_bytes": [c_int, c_int, c_int],
     "cdb_rope_append_kv": [
         c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int64, c_int,
@@ -61,6 +65,7 @@ _SIGNATURES: dict[str, list] = {
         c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p,
     ],
     "cdb_silu_mul": [c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_void_p],
+    "cdb_gather_rows": [c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_int64, c_void_p],
     "cdb_argmax": [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
     "cdb_embed": [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int, c_void_p, c_void_p],
     "cdb_block_table_update": [c_void_p, c_int64, c_void_p, c_int, c_void_p],

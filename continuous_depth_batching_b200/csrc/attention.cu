@@ -430,9 +430,11 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const int32_t* item_pos
     __syncthreads();
     const int excl = carry + (w > 0 ? s_warp[w - 1] : 0) + v - cnt;
     if (i < n && cnt > 0) {
-      for (int g = 0; g < nhg; ++g)
-        for (int s = 0; s < ns; ++s) {
-          const int idx = excl + g * ns + s;
+      // Split-major: the head groups of one (row, split) are consecutive units, so CTAs with
+      // consecutive indices read the same pages' K/V rows at the same time.
+      for (int s = 0; s < ns; ++s)
+        for (int g = 0; g < nhg; ++g) {
+          const int idx = excl + s * nhg + g;
           if (idx < capacity) units[idx] = make_int4(i, g, s, ns);
         }
     }

@@ -256,6 +256,27 @@ __global__ void embed_kernel(const __nv_bfloat16* table, int hidden, int vocab, 
   }
 }
 
+// dst[r] = src[rows[r]] for bf16 rows of `hidden` elements (rows[r] < 0: row r is zeroed).
+__global__ void gather_rows_kernel(const __nv_bfloat16* src, int64_t ss, const int32_t* rows, int hidden,
+                                   __nv_bfloat16* dst, int64_t ds) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x;
+  const int sr = rows[r];
+  __nv_bfloat16* o = dst + (int64_t)r * ds;
+  if (sr < 0) {
+    for (int d = threadIdx.x; d < hidden; d += blockDim.x) o[d] = f_to_bf16(0.f);
+    return;
+  }
+  const __nv_bfloat16* x = src + (int64_t)sr * ss;
+  if ((hidden & 7) == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(o)) & 15) == 0) {
+    for (int d = threadIdx.x * 8; d < hidden; d += blockDim.x * 8)
+      *reinterpret_cast<uint4*>(o + d) = *reinterpret_cast<const uint4*>(x + d);
+  } else {
+    for (int d = threadIdx.x; d < hidden; d += blockDim.x) o[d] = x[d];
+  }
+}
+
 __global__ void block_table_update_kernel(int32_t* table, int64_t stride, const int32_t* edits, int n) {
   pdl_trigger();
   pdl_wait();
@@ -374,6 +395,16 @@ extern "C" int cdb_silu_mul(const void* gu, int64_t gu_stride, void* act, int64_
   dim3 grid((inter / 8 + threads - 1) / threads, num_rows);
   launch_pdl(silu_mul_kernel, dim3(grid), dim3(threads), 0, static_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(gu), gu_stride, static_cast<__nv_bfloat16*>(act), act_stride, inter);
+  return check_launch();
+}
+
+extern "C" int cdb_gather_rows(const void* src, int64_t src_stride, const int32_t* rows, int num_rows, int hidden,
+                               void* dst, int64_t dst_stride, void* stream) {
+  if (hidden <= 0 || num_rows < 0 || rows == nullptr) return CDB_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return CDB_OK;
+  launch_pdl(gather_rows_kernel, dim3(num_rows), dim3(128), 0, static_cast<cudaStream_t>(stream),
+             static_cast<const __nv_bfloat16*>(src), src_stride, rows, hidden, static_cast<__nv_bfloat16*>(dst),
+             dst_stride);
   return check_launch();
 }
 

@@ -10,12 +10,14 @@
 //               into a STAGES-deep ring, completion on "full" mbarriers;
 //   warp 1      allocates TMEM and issues tcgen05.mma (one elected thread), releasing each
 //               stage with tcgen05.commit onto its "empty" mbarrier;
-//   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp reads its 32-lane quarter),
-//               round to bf16 and store; consecutive lanes hold consecutive output columns,
-//               so every store instruction writes 64 contiguous bytes.
-// Split-K (for the small-N projections that cannot fill 148 SMs otherwise) is deterministic:
-// every split stores fp32 partials to L2-resident scratch and the last CTA of the tile (atomic
-// counter) sums them in split order, stores bf16 and resets its counter.
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp reads its 32-lane quarter)
+//               into an fp32 tile in the drained stage ring.
+// Split-K (for the projections whose weight tiles cannot fill 148 SMs otherwise) keeps the
+// splits of one tile in one thread-block cluster (grid z = cluster z = splits <= 8): after a
+// cluster barrier every CTA reduces one slice of the tile from all ranks' shared memory
+// (distributed shared memory loads, rank order, so the sum is deterministic) and stores it as
+// bf16 with 8-byte vector stores. No global partials, counters or second pass.
+#include <cooperative_groups.h>
 #include <cuda.h>
 
 #include <cstring>
@@ -30,6 +32,7 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle atom of bf16
 constexpr int THREADS = 192;
+constexpr int kMaxClusterSplits = 8;  // portable cluster size
 
 template <int BN, int STAGES>
 struct Cfg {
@@ -43,15 +46,15 @@ struct Cfg {
   static constexpr uint32_t IDESC =
       (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+  static_assert(BN * BM * 4 <= STAGES * STAGE_BYTES, "fp32 partial tile must fit in the stage ring");
 };
 
 struct Params {
   __nv_bfloat16* c;
   int64_t ldc;
-  float* ws;
-  int32_t* counters;
   int M, N, K;
-  int splits, kb_per_split, num_kb;
+  int splits, kb_per_split, num_kb;  // splits == cluster size along z
+  int vec_store;                     // c 8-byte aligned and ldc % 4 == 0
   int32_t* status;
 };
 
@@ -112,7 +115,10 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-template <int BN, int STAGES>
+// EPI 0: store c[m, n] = bf16(acc). EPI 1 (SwiGLU): weight rows are gate/up pairs
+// (row 2j = gate_j, row 2j+1 = up_j) and c[m, j] = bf16(bf16(silu(bf16(g))) * bf16(u)), the
+// rounding of OuroMLP's act_fn(gate_proj(x)) * up_proj(x) in bf16.
+template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, Params p) {
   using C = Cfg<BN, STAGES>;
@@ -122,7 +128,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* empty = full + STAGES;
   uint64_t* accum = empty + STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  float* red = reinterpret_cast<float*>(smem);  // [BN][BM] fp32 partial tile, after the mainloop
+  cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -165,17 +172,24 @@ __global__ void __launch_bounds__(THREADS, 1)
         tma_load_2d(smem + i * C::STAGE_BYTES + C::A_BYTES, &map_x, &full[i], (kb0 + i) * BK, mtile * BN);
       int stage = npre % STAGES;
       uint32_t phase = (npre == STAGES) ? 1u : 0u;
+      int issued = npre;
       for (int kb = kb0 + npre; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) break;
         uint8_t* a = smem + stage * C::STAGE_BYTES;
         mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
         tma_load_2d(a, &map_w, &full[stage], kb * BK, wtile * BM);
         tma_load_2d(a + C::A_BYTES, &map_x, &full[stage], kb * BK, mtile * BN);
+        ++issued;
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
         }
       }
+      // Load j lands in stage j % STAGES and completes that barrier's phase of parity
+      // (j / STAGES) & 1. Wait (bounded) for the last load of every stage, so that no copy is
+      // still in flight when the ring is reused for the partial tile or the CTA exits.
+      for (int j = max(0, issued - STAGES); j < issued; ++j)
+        mbar_wait(&full[j % STAGES], (uint32_t)((j / STAGES) & 1), p.status);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -199,73 +213,81 @@ __global__ void __launch_bounds__(THREADS, 1)
       umma_commit(accum);
     }
     __syncwarp();
-  } else {
+  }
+  // The producer's loads have all landed and the MMA warp has issued its final commit.
+  __syncthreads();
+  if (warp >= 2) {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
+    // TMEM -> this CTA's fp32 partial tile red[token][weight row] in the stage ring, which is
+    // free once the accumulator barrier fires (every MMA, the ring's only reader, completed).
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int n = wtile * BM + q * 32 + lane;
     const bool ok = mbar_wait(accum, 0, p.status);
     tc_fence_after();
-    const bool split_k = p.splits > 1;
-    const int m_base = mtile * BN;
     if (ok) {
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, r);
-        if (n < p.N) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int m = m_base + c0 + j;
-            if (m < p.M) {
-              const float v = __uint_as_float(r[j]);
-              if (split_k)
-                p.ws[((int64_t)split * gridDim.y * BN + m) * p.N + n] = v;
-              else
-                p.c[(int64_t)m * p.ldc + n] = f_to_bf16(v);
-            }
-          }
-        }
-      }
-    }
-    if (split_k) {
-      __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (threadIdx.x == 64) {
-        int32_t* ctr = p.counters + (int64_t)mtile * gridDim.x + wtile;
-        const int prev = atomicAdd(ctr, 1);
-        const int last = prev == p.splits - 1;
-        if (last) atomicExch(ctr, 0);
-        *last_flag = last;
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (*last_flag && n < p.N) {
-        __threadfence();
-        // Sum the splits in split order, 8 token rows at a time so 8 independent loads are in
-        // flight per split (the partials sit in L2).
-        const int m_end = min(m_base + BN, p.M);
-        const float* __restrict__ ws = p.ws;
-        const int64_t split_stride = (int64_t)gridDim.y * BN * p.N;
-        for (int m0 = m_base; m0 < m_end; m0 += 8) {
-          float acc[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-          for (int s = 0; s < p.splits; ++s) {
-            const float* src = ws + s * split_stride + (int64_t)m0 * p.N + n;
-            float v[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = (m0 + j < m_end) ? __ldcg(src + (int64_t)j * p.N) : 0.f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc[j] += v[j];
-          }
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            if (m0 + j < m_end) p.c[(int64_t)(m0 + j) * p.ldc + n] = f_to_bf16(acc[j]);
-        }
+        for (int j = 0; j < 32; ++j) red[(c0 + j) * BM + q * 32 + lane] = __uint_as_float(r[j]);
       }
     }
   }
   tc_fence_before();
-  __syncthreads();
+  // Every thread of every CTA of the cluster passes both cluster barriers exactly once, error
+  // paths included, so no CTA can wait on one that has left.
+  cluster.sync();
+
+  // Deterministic K-split reduction through distributed shared memory: the cluster holds the
+  // tile's `splits` CTAs; rank r sums slice r of the tile over all ranks in rank order and
+  // stores it as bf16 (4 consecutive weight rows = 4 consecutive output columns per thread).
+  {
+    const int ns = p.splits;
+    const int rank = (int)cluster.block_rank();
+    constexpr int kVec = BM / 4;
+    constexpr int kTotal = BN * kVec;
+    const int per = (kTotal + ns - 1) / ns;
+    const int e_end = min((rank + 1) * per, kTotal);
+    const int m_base = mtile * BN;
+    const bool vec_store = p.vec_store;
+    for (int e = rank * per + (int)threadIdx.x; e < e_end; e += THREADS) {
+      const int m = e / kVec;
+      const int n4 = (e % kVec) * 4;
+      const int gm = m_base + m;
+      const int gn = wtile * BM + n4;
+      if (gm >= p.M || gn >= p.N) continue;
+      float4 v[kMaxClusterSplits];
+#pragma unroll
+      for (int sp = 0; sp < kMaxClusterSplits; ++sp)
+        if (sp < ns) v[sp] = *(cluster.map_shared_rank(reinterpret_cast<float4*>(red), sp) + (m * BM + n4) / 4);
+      float4 acc = v[0];
+#pragma unroll
+      for (int sp = 1; sp < kMaxClusterSplits; ++sp)
+        if (sp < ns) {
+          acc.x += v[sp].x;
+          acc.y += v[sp].y;
+          acc.z += v[sp].z;
+          acc.w += v[sp].w;
+        }
+      if constexpr (EPI == 1) {
+        // N % 4 == 0 here: (gate_j, up_j, gate_j+1, up_j+1) -> act[j], act[j+1], j = gn / 2.
+        const float g0 = round_bf16(acc.x), u0 = round_bf16(acc.y);
+        const float g1 = round_bf16(acc.z), u1 = round_bf16(acc.w);
+        const float s0 = round_bf16(g0 / (1.f + expf(-g0)));
+        const float s1 = round_bf16(g1 / (1.f + expf(-g1)));
+        *reinterpret_cast<uint32_t*>(p.c + (int64_t)gm * p.ldc + gn / 2) = pack_bf16x2(s0 * u0, s1 * u1);
+      } else {
+        __nv_bfloat16* dst = p.c + (int64_t)gm * p.ldc + gn;
+        if (vec_store && gn + 3 < p.N) {
+          *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
+        } else {
+          const float a[4] = {acc.x, acc.y, acc.z, acc.w};
+          for (int j = 0; j < 4 && gn + j < p.N; ++j) dst[j] = f_to_bf16(a[j]);
+        }
+      }
+    }
+  }
+  cluster.sync();  // peers finished reading this CTA's partial tile
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
@@ -335,54 +357,98 @@ static int matrix_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t c
 }
 
 template <int BN, int STAGES>
-static int launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, dim3 grid, cudaStream_t st) {
+static cudaLaunchConfig_t launch_config(dim3 grid, int splits, cudaStream_t st, cudaLaunchAttribute (&attr)[2]) {
   using C = Cfg<BN, STAGES>;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(gemm_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = splits;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cfg;
+}
+
+// Largest cluster size <= want that the device can schedule for this configuration (checked
+// once per size with cudaOccupancyMaxActiveClusters and remembered).
+template <int BN, int STAGES, int EPI>
+static int schedulable_splits(int want) {
+  static std::mutex mu;
+  static int ok[kMaxClusterSplits + 1] = {};  // 0 unknown, 1 fits, -1 does not
+  std::lock_guard<std::mutex> lock(mu);
+  for (int s = want; s > 1; --s) {
+    if (ok[s] == 0) {
+      cudaLaunchAttribute attr[2];
+      cudaLaunchConfig_t cfg = launch_config<BN, STAGES>(dim3(1, 1, s), s, nullptr, attr);
+      int n = 0;
+      ok[s] = (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<BN, STAGES, EPI>, &cfg) == cudaSuccess && n > 0) ? 1 : -1;
+      cudaGetLastError();
+    }
+    if (ok[s] == 1) return s;
+  }
+  return 1;
+}
+
+template <int BN, int STAGES, int EPI>
+static int launch(const CUtensorMap& mw, const CUtensorMap& mx, Params p, int tiles_n, int tiles_m, int splits,
+                  cudaStream_t st) {
+  using C = Cfg<BN, STAGES>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(gemm_kernel<BN, STAGES, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
         cudaSuccess)
       return CDB_ERR_CUDA;
-    attr = true;
+    attr_set = true;
   }
-  return launch_pdl(gemm_kernel<BN, STAGES>, grid, dim3(THREADS), C::SMEM, st, mw, mx, p) == cudaSuccess
-             ? CDB_OK
-             : CDB_ERR_CUDA;
+  int s = schedulable_splits<BN, STAGES, EPI>(splits);
+  int kb_per = (p.num_kb + s - 1) / s;
+  s = (p.num_kb + kb_per - 1) / kb_per;  // no empty split
+  p.splits = s;
+  p.kb_per_split = kb_per;
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = launch_config<BN, STAGES>(dim3(tiles_n, tiles_m, s), s, st, attr);
+  return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, STAGES, EPI>, mw, mx, p) == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
 }
+
+// Token-tile width for M token rows, and CTAs of that configuration resident per SM.
+static int tile_n_for(int M) { return M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256; }
+static int ctas_per_sm(int bn) { return bn <= 64 ? 2 : 1; }
 
 }  // namespace gemm
 }  // namespace cdb
 
 using namespace cdb;
 
-extern "C" int cdb_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int M,
-                             int N, int K, int splits, float* workspace, int64_t workspace_elems, int32_t* counters,
-                             int num_counters, int num_sms, int32_t* status, void* stream) {
-  using namespace cdb::gemm;
-  if (M <= 0 || N <= 0 || K <= 0) return M == 0 ? CDB_OK : CDB_ERR_INVALID_ARGUMENT;
-  if (K % 8 != 0 || ldx % 8 != 0 || ldw % 8 != 0 || ldx < K || ldw < K || ldc < N) return CDB_ERR_INVALID_ARGUMENT;
+namespace cdb {
+namespace gemm {
+
+// Shared host path of the plain and SwiGLU GEMMs: c = epilogue(x[M,K] * w[N,K]^T).
+template <int EPI>
+static int run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int M, int N, int K,
+               int splits, int num_sms, int32_t* status, cudaStream_t st) {
+  if (K % 8 != 0 || ldx % 8 != 0 || ldw % 8 != 0 || ldx < K || ldw < K) return CDB_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return CDB_ERR_INVALID_ARGUMENT;
-  const int bn = M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  const int bn = tile_n_for(M);
   const int tiles_n = (N + BM - 1) / BM;
   const int tiles_m = (M + bn - 1) / bn;
   const int num_kb = (K + BK - 1) / BK;
   if (num_sms <= 0) num_sms = 148;
   int s = splits;
   if (s <= 0) {
+    // Fill the resident CTA slots with (weight tile, token tile, K split) CTAs, at least two
+    // k-blocks per split.
     const int tiles = tiles_n * tiles_m;
-    s = tiles >= num_sms ? 1 : num_sms / tiles;
-    s = min(s, max(1, num_kb / 4));
-    s = min(s, 16);
+    const int slots = num_sms * ctas_per_sm(bn);
+    s = tiles >= slots ? 1 : slots / tiles;
+    s = min(s, max(1, num_kb / 2));
   }
-  s = max(1, min(s, num_kb));
-  int kb_per = (num_kb + s - 1) / s;
-  s = (num_kb + kb_per - 1) / kb_per;
-  if (s > 1) {
-    const int64_t need = (int64_t)s * tiles_m * bn * N;
-    if (workspace == nullptr || counters == nullptr || need > workspace_elems || tiles_n * tiles_m > num_counters) {
-      s = 1;
-      kb_per = num_kb;
-    }
-  }
+  s = max(1, min(min(s, kMaxClusterSplits), num_kb));
   CUtensorMap mw, mx;
   int rc = matrix_map(&mw, w, N, K, ldw, BM);
   if (rc != CDB_OK) return rc;
@@ -391,36 +457,55 @@ extern "C" int cdb_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t 
   Params p;
   p.c = static_cast<__nv_bfloat16*>(c);
   p.ldc = ldc;
-  p.ws = workspace;
-  p.counters = counters;
   p.M = M;
   p.N = N;
   p.K = K;
   p.splits = s;
-  p.kb_per_split = kb_per;
+  p.kb_per_split = num_kb;
   p.num_kb = num_kb;
+  p.vec_store = ((reinterpret_cast<uintptr_t>(c) & 7) == 0 && ldc % 4 == 0) ? 1 : 0;
   p.status = status;
-  const dim3 grid(tiles_n, tiles_m, s);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (bn) {
     case 32:
-      return launch<32, 8>(mw, mx, p, grid, st);
+      return launch<32, 5, EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
     case 64:
-      return launch<64, 8>(mw, mx, p, grid, st);
+      return launch<64, 4, EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
     case 128:
-      return launch<128, 6>(mw, mx, p, grid, st);
+      return launch<128, 6, EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
     default:
-      return launch<256, 4>(mw, mx, p, grid, st);
+      return launch<256, 4, EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
   }
 }
 
+}  // namespace gemm
+}  // namespace cdb
+
+extern "C" int cdb_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int M,
+                             int N, int K, int splits, float* workspace, int64_t workspace_elems, int32_t* counters,
+                             int num_counters, int num_sms, int32_t* status, void* stream) {
+  (void)workspace;
+  (void)workspace_elems;
+  (void)counters;
+  (void)num_counters;
+  if (M <= 0 || N <= 0 || K <= 0) return M == 0 ? CDB_OK : CDB_ERR_INVALID_ARGUMENT;
+  if (ldc < N) return CDB_ERR_INVALID_ARGUMENT;
+  return cdb::gemm::run<0>(x, ldx, w, ldw, c, ldc, M, N, K, splits, num_sms, status, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cdb_mlp_gateup_silu_gemm(const void* x, int64_t ldx, const void* w_gate_up, int64_t ldw, void* act,
+                                        int64_t ld_act, int M, int inter, int K, int splits, int num_sms,
+                                        int32_t* status, void* stream) {
+  if (M <= 0 || inter <= 0 || K <= 0) return M == 0 ? CDB_OK : CDB_ERR_INVALID_ARGUMENT;
+  if (inter % 2 != 0 || ld_act < inter || ld_act % 2 != 0 || (reinterpret_cast<uintptr_t>(act) & 3))
+    return CDB_ERR_INVALID_ARGUMENT;
+  return cdb::gemm::run<1>(x, ldx, w_gate_up, ldw, act, ld_act, M, 2 * inter, K, splits, num_sms, status,
+                           static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int64_t cdb_gemm_workspace_elems(int M, int N, int K, int num_sms) {
-  using namespace cdb::gemm;
-  const int bn = M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
-  const int tiles = ((N + BM - 1) / BM) * ((M + bn - 1) / bn);
-  const int num_kb = (K + BK - 1) / BK;
-  if (num_sms <= 0) num_sms = 148;
-  int s = tiles >= num_sms ? 1 : num_sms / tiles;
-  s = min(min(s, max(1, num_kb / 4)), 16);
-  return s > 1 ? (int64_t)s * ((M + bn - 1) / bn) * bn * N : 0;
+  (void)M;
+  (void)N;
+  (void)K;
+  (void)num_sms;
+  return 0;  // K splits reduce inside a thread-block cluster; no global workspace
 }

@@ -1,0 +1,192 @@
+"""Single-kernel timing on synthetic inputs, through the C ABI, for roofline and profiler runs.
+
+    python -m continuous_depth_batching_b200.kernel_bench attention --rows 128 --context 1024
+    python -m continuous_depth_batching_b200.kernel_bench gemm --m 80 --n 2048 --k 2048
+
+``attention`` builds a one-cache-layer paged KV pool with the Ouro-1.4B head shape (16 heads x
+128), gives each row a context drawn uniformly from [context/2, 3*context/2), and times the
+cache-only decode attention kernel (the launch a recurrent step makes per layer after the
+rope/append kernel) with CUDA events on the launching stream. Algorithmic bytes per launch are
+``attention_bytes`` below. ``gemm`` times ``cdb_gemm_bf16`` against ``torch.mm`` (cuBLAS) on one
+shape, flushing L2 between launches so weights stream from HBM as they do in a decode step.
+Each prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import _lib
+
+BLOCK = 16
+
+
+def attention_bytes(positions, num_heads: int, head_dim: int, append: bool) -> int:
+    """Algorithmic HBM bytes of one decode-attention launch over rows at ``positions``.
+
+    Per row at position p: K and V rows 0..p read (2*(p+1)*H*D*2 bytes), q read and o written
+    (2*H*D*2), the block-table entries (4 bytes per page), and when appending the new k and v
+    rows written (2*H*D*2). Padding rows (p < 0) cost nothing.
+    """
+    row = num_heads * head_dim * 2
+    total = 0
+    for p in positions:
+        if p < 0:
+            continue
+        total += 2 * (p + 1) * row + 2 * row + 4 * (-(-(p + 1) // BLOCK))
+        if append:
+            total += 2 * row
+    return total
+
+
+def _events_ms(fn, reps: int, stream, flush: torch.Tensor | None = None) -> float:
+    """Median device time of ``fn`` in ms over ``reps`` launches (CUDA events on ``stream``)."""
+    times = []
+    for _ in range(reps):
+        if flush is not None:
+            flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def run_attention(args) -> dict:
+    dev = torch.device("cuda")
+    gen = torch.Generator().manual_seed(args.seed)
+    heads, dim = args.heads, args.head_dim
+    ctx = torch.randint(args.context // 2, args.context * 3 // 2, (args.rows,), generator=gen)
+    pos = (ctx - 1).to(torch.int32)
+    nb = (ctx + BLOCK - 1) // BLOCK
+    width = int(nb.max())
+    num_blocks = int(nb.sum())
+    perm = torch.randperm(num_blocks, generator=gen).to(torch.int32)
+    table = torch.zeros(args.rows, width, dtype=torch.int32)
+    k = 0
+    for r in range(args.rows):
+        n = int(nb[r])
+        table[r, :n] = perm[k : k + n]
+        k += n
+    kv_rows = (num_blocks + 2) * BLOCK
+    kv = torch.empty(1, 2, kv_rows, heads, dim, device=dev, dtype=torch.bfloat16).normal_()
+    table = table.to(dev)
+    pos_d = pos.to(dev)
+    slots = torch.arange(args.rows, dtype=torch.int32, device=dev)
+    hd = heads * dim
+    qkv = torch.randn(args.rows, 3 * hd, device=dev).to(torch.bfloat16)
+    out = torch.empty(args.rows, hd, device=dev, dtype=torch.bfloat16)
+    hg = 5 if dim == 96 else 4
+    scratch_items = args.scratch_items
+    cap = max(scratch_items * (heads // hg) * 64, args.rows * (heads // hg))
+    hdr = torch.zeros(4, dtype=torch.int32, device=dev)
+    units = torch.zeros(cap, 4, dtype=torch.int32, device=dev)
+    part_o = torch.zeros(scratch_items * heads * 64 * dim, device=dev)
+    part_ml = torch.zeros(scratch_items * heads * 64 * 2, device=dev)
+    counters = torch.zeros(scratch_items * heads, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    _lib.call(
+        "cdb_attn_plan", _lib.ptr(pos_d), args.rows, 0, heads, dim, BLOCK, cap, scratch_items, 148,
+        _lib.ptr(hdr), _lib.ptr(units), sp,
+    )
+
+    def launch():
+        _lib.call(
+            "cdb_paged_decode_attn_append", _lib.ptr(qkv), qkv.stride(0), hd, 2 * hd, _lib.ptr(out), out.stride(0),
+            _lib.ptr(kv), 1, kv_rows, 0, _lib.ptr(table), table.stride(0), _lib.ptr(slots), _lib.ptr(pos_d), 0,
+            None, None, 0, _lib.ptr(hdr), _lib.ptr(units), _lib.ptr(part_o), _lib.ptr(part_ml), _lib.ptr(counters),
+            scratch_items, args.rows, heads, dim, BLOCK, dim**-0.5, args.ctas, _lib.ptr(status), sp,
+        )
+
+    for _ in range(args.warmup):
+        launch()
+    torch.cuda.synchronize()
+    ms = _events_ms(launch, args.iters, stream)
+    if int(status.item()) != 0:
+        raise RuntimeError(_lib.load().cdb_status_string(int(status.item())).decode())
+    algo = attention_bytes(pos.tolist(), heads, dim, append=False)
+    return {
+        "kernel": f"cdb::decode_attn_kernel<{dim},{hg}>",
+        "rows": args.rows,
+        "mean_context": float(ctx.float().mean()),
+        "kv_pool_bytes": kv.numel() * 2,
+        "plan": [int(x) for x in hdr.tolist()],
+        "launch_us": round(ms * 1e3, 2),
+        "algorithmic_bytes": algo,
+        "achieved_gbs": round(algo / (ms * 1e-3) / 1e9, 1),
+    }
+
+
+def run_gemm(args) -> dict:
+    dev = torch.device("cuda")
+    torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+    m, n, k = args.m, args.n, args.k
+    x = torch.randn(m, k, device=dev).to(torch.bfloat16)
+    w = (0.02 * torch.randn(n, k, device=dev)).to(torch.bfloat16)
+    c = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    ws = torch.zeros(32 << 20, dtype=torch.float32, device=dev)
+    ctr = torch.zeros(1 << 14, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def tc():
+        _lib.call(
+            "cdb_gemm_bf16", _lib.ptr(x), x.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(c), c.stride(0), m, n, k,
+            args.splits, _lib.ptr(ws), ws.numel(), _lib.ptr(ctr), ctr.numel(), 148, _lib.ptr(status), stream.cuda_stream,
+        )
+
+    def cublas():
+        torch.mm(x, w.t(), out=c)
+
+    res = {"m": m, "n": n, "k": k, "weight_bytes": 2 * n * k}
+    for name, fn in (("tcgen05", tc), ("cublas", cublas)):
+        if args.only and name != args.only:
+            continue
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        ms = _events_ms(fn, args.iters, stream, flush)
+        byts = 2 * (n * k + m * k + m * n)
+        res[name] = {"us": round(ms * 1e3, 2), "gbs": round(byts / (ms * 1e-3) / 1e9, 1),
+                     "tflops": round(2 * m * n * k / (ms * 1e-3) / 1e12, 1)}
+    if int(status.item()) != 0:
+        raise RuntimeError(_lib.load().cdb_status_string(int(status.item())).decode())
+    return res
+
+
+def main(argv=None) -> None:
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    sub = p.add_subparsers(dest="kernel", required=True)
+    a = sub.add_parser("attention")
+    a.add_argument("--rows", type=int, default=128)
+    a.add_argument("--context", type=int, default=1024)
+    a.add_argument("--heads", type=int, default=16)
+    a.add_argument("--head-dim", type=int, default=128)
+    a.add_argument("--scratch-items", type=int, default=256)
+    a.add_argument("--ctas", type=int, default=296)
+    g = sub.add_parser("gemm")
+    g.add_argument("--m", type=int, default=80)
+    g.add_argument("--n", type=int, default=2048)
+    g.add_argument("--k", type=int, default=2048)
+    g.add_argument("--splits", type=int, default=0)
+    g.add_argument("--only", choices=["tcgen05", "cublas"], default=None)
+    for s in (a, g):
+        s.add_argument("--warmup", type=int, default=3)
+        s.add_argument("--iters", type=int, default=20)
+        s.add_argument("--seed", type=int, default=0)
+    args = p.parse_args(argv)
+    res = run_attention(args) if args.kernel == "attention" else run_gemm(args)
+    print(json.dumps(res))
+
+
+if __name__ == "__main__":
+    main()

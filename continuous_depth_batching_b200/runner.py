@@ -77,7 +77,11 @@ class Uploader:
 
 @dataclass
 class PackedOuroWeights:
-    """bf16 device weights with the projections the kernels fuse concatenated."""
+    """bf16 device weights with the projections the kernels fuse concatenated.
+
+    ``w_gu`` is ``[gate; up]`` stacked (the cuBLAS path then runs ``cdb_silu_mul``) or, with
+    ``gu_interleaved``, row pairs ``(gate_j, up_j)`` as ``cdb_mlp_gateup_silu_gemm`` reads them.
+    """
 
     embed: torch.Tensor
     w_qkv: list[torch.Tensor]
@@ -91,9 +95,17 @@ class PackedOuroWeights:
     lm_head: torch.Tensor
 
     @classmethod
-    def from_state_dict(cls, shape: OuroShape, sd: dict[str, torch.Tensor], device: torch.device) -> PackedOuroWeights:
+    def from_state_dict(
+        cls, shape: OuroShape, sd: dict[str, torch.Tensor], device: torch.device, gu_interleaved: bool = False
+    ) -> PackedOuroWeights:
         def g(name: str) -> torch.Tensor:
             return sd[name].detach().to(device=device, dtype=torch.bfloat16).contiguous()
+
+        def gate_up(p: str) -> torch.Tensor:
+            gate, up = g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")
+            if gu_interleaved:
+                return torch.stack([gate, up], dim=1).reshape(2 * gate.shape[0], gate.shape[1]).contiguous()
+            return torch.cat([gate, up]).contiguous()
 
         L = shape.num_hidden_layers
         pre = [f"model.layers.{i}." for i in range(L)]
@@ -104,7 +116,7 @@ class PackedOuroWeights:
                 for p in pre
             ],
             w_o=[g(p + "self_attn.o_proj.weight") for p in pre],
-            w_gu=[torch.cat([g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")]).contiguous() for p in pre],
+            w_gu=[gate_up(p) for p in pre],
             w_down=[g(p + "mlp.down_proj.weight") for p in pre],
             norms={n: [g(p + n + ".weight") for p in pre] for n in LAYER_NORM_NAMES},
             final_norm=g("model.norm.weight"),
@@ -166,7 +178,7 @@ class OuroRunner:
         self.block_size = block_size
         self.max_num_seqs = max_num_seqs
         self.use_cuda_graph = use_cuda_graph
-        self.w = PackedOuroWeights.from_state_dict(shape, state_dict, device)
+        self.w = PackedOuroWeights.from_state_dict(shape, state_dict, device, gu_interleaved=gemm_backend == "tcgen05")
         L = shape.num_hidden_layers
         self.pool = PagedKVPool(
             num_cache_layers=self.slots * L,
@@ -212,7 +224,7 @@ class OuroRunner:
         self.token_log = torch.zeros(1, dtype=torch.int64, device=device)
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
         self.logits = torch.zeros(max_num_seqs, shape.vocab_size, **bf)
-        self.gather_idx = torch.zeros(max_num_seqs, dtype=torch.int64, device=device)
+        self.lm_in = torch.zeros(max_num_seqs, shape.hidden_size, **bf)  # gathered LM-head input rows
         # attention plan + split-combine scratch
         nh = shape.num_attention_heads
         hg = 5 if D == 96 else 4
@@ -349,8 +361,17 @@ class OuroRunner:
                 _lib.ptr(w.norms["input_layernorm_2"][l]), _lib.ptr(w.norms["post_attention_layernorm"][l]),
                 _lib.ptr(self.h), self.h.stride(0), None, None, None, None, n, H, eps, sp,
             )
-            self._mm(self.h[:n], w.w_gu[l], self.gu[:n])
-            _lib.call("cdb_silu_mul", _lib.ptr(self.gu), self.gu.stride(0), _lib.ptr(self.act), self.act.stride(0), n, I, sp)
+            if self.gemm_backend == "tcgen05":
+                _lib.call(
+                    "cdb_mlp_gateup_silu_gemm", _lib.ptr(self.h), self.h.stride(0), _lib.ptr(w.w_gu[l]),
+                    w.w_gu[l].stride(0), _lib.ptr(self.act), self.act.stride(0), n, I, H, 0, self.num_sms,
+                    _lib.ptr(self.status), sp,
+                )
+            else:
+                self._mm(self.h[:n], w.w_gu[l], self.gu[:n])
+                _lib.call(
+                    "cdb_silu_mul", _lib.ptr(self.gu), self.gu.stride(0), _lib.ptr(self.act), self.act.stride(0), n, I, sp
+                )
             self._mm(self.act[:n], w.w_down[l], self.m[:n])
             if l < L - 1:
                 _lib.call(
@@ -465,9 +486,11 @@ class OuroRunner:
                 base = slot_for_step[step] * s.num_hidden_layers
                 self._layer_stack(n, base, meta[1], meta[2], 0, self.xw, None, False)
             if k:
-                self.gather_idx[:k].copy_(sel[0].to(torch.int64))
-                hl = self.xw.index_select(0, self.gather_idx[:k])
-                self._mm(hl, self.w.lm_head, self.logits[:k])
+                _lib.call(
+                    "cdb_gather_rows", _lib.ptr(self.xw), self.xw.stride(0), _lib.ptr(sel[0]), k, s.hidden_size,
+                    _lib.ptr(self.lm_in), self.lm_in.stride(0), sp,
+                )
+                self._mm(self.lm_in[:k], self.w.lm_head, self.logits[:k])
                 _lib.call(
                     "cdb_argmax", _lib.ptr(self.logits), self.logits.stride(0), k, s.vocab_size,
                     _lib.ptr(self.token_log), _lib.ptr(sel[1]), _lib.ptr(sel[2]), _lib.ptr(self.token_table), sp,
@@ -498,9 +521,11 @@ class OuroRunner:
         n = len(hidden)
         meta = self.upload([hidden, log_rows, req_slots]).view(3, n)
         with torch.cuda.stream(self.stream):
-            self.gather_idx[:n].copy_(meta[0].to(torch.int64))
-            hl = self.bank.index_select(0, self.gather_idx[:n])
-            self._mm(hl, self.w.lm_head, self.logits[:n])
+            _lib.call(
+                "cdb_gather_rows", _lib.ptr(self.bank), self.bank.stride(0), _lib.ptr(meta[0]), n, s.hidden_size,
+                _lib.ptr(self.lm_in), self.lm_in.stride(0), self.stream.cuda_stream,
+            )
+            self._mm(self.lm_in[:n], self.w.lm_head, self.logits[:n])
             _lib.call(
                 "cdb_argmax", _lib.ptr(self.logits), self.logits.stride(0), n, s.vocab_size, _lib.ptr(self.token_log),
                 _lib.ptr(meta[1]), _lib.ptr(meta[2]), _lib.ptr(self.token_table), self.stream.cuda_stream,

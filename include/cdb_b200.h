@@ -143,15 +143,27 @@ int cdb_rope_append_kv(void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_c
  * (OuroAttention q/k/v/o_proj modeling_ouro.py:371-374,431; OuroMLP gate/up/down :162-168;
  * lm_head adapters/ouro.py:321-329), which the reference runs on cuBLAS through ATen.
  *   x, w       row-major bf16, leading dimensions ldx, ldw (multiples of 8), 16-byte aligned.
- *   splits     K splits (<= 0: chosen from the tile count and num_sms); splits > 1 needs
- *              workspace (fp32, cdb_gemm_workspace_elems) and num_counters zeroed int32 counters
- *              (left zeroed). Without enough workspace the call runs unsplit.
+ *   splits     K splits, clamped to [1, 8] (<= 0: chosen from the tile count and num_sms).
+ *              The splits of one output tile run as one thread-block cluster and reduce
+ *              through distributed shared memory, so no global scratch is used:
+ *              workspace/workspace_elems/counters/num_counters are ignored (may be NULL/0).
  * Deterministic: split partials are summed in split order. */
 int cdb_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int M, int N, int K,
                   int splits, float* workspace, int64_t workspace_elems, int32_t* counters, int num_counters,
                   int num_sms, int32_t* status, void* stream);
 
-/* fp32 workspace elements cdb_gemm_bf16 uses for an automatically split problem (0 = unsplit). */
+/* Fused MLP input half: act[M, inter] = silu(x * Wg^T) * (x * Wu^T) with the reference's bf16
+ * rounding (gate and up rounded to bf16, silu rounded to bf16, product rounded to bf16), in one
+ * tcgen05 GEMM whose epilogue applies SwiGLU. Replaces OuroMLP.forward's
+ * act_fn(gate_proj(x)) * up_proj(x) (modeling_ouro.py:162-168).
+ *   w_gate_up  bf16 [2*inter, K] with rows interleaved: row 2j = gate_proj row j,
+ *              row 2j+1 = up_proj row j. inter even; act 4-byte aligned, ld_act even.
+ *   splits, num_sms, status: as cdb_gemm_bf16. */
+int cdb_mlp_gateup_silu_gemm(const void* x, int64_t ldx, const void* w_gate_up, int64_t ldw, void* act,
+                             int64_t ld_act, int M, int inter, int K, int splits, int num_sms, int32_t* status,
+                             void* stream);
+
+/* fp32 workspace elements cdb_gemm_bf16 needs: always 0 (kept for callers sizing a buffer). */
 int64_t cdb_gemm_workspace_elems(int M, int N, int K, int num_sms);
 
 /* ---------------------------------------------------------------------------------------
@@ -207,6 +219,13 @@ int cdb_block_table_update(int32_t* table, int64_t stride, const int32_t* edits,
 int cdb_exit_kv_copy(void* kv_base, int num_cache_layers, int64_t kv_rows, int num_kv_heads, int head_dim,
                      const int32_t* rows, int num_rows, const int32_t* src_layers, const int32_t* dst_layers,
                      int num_pairs, void* stream);
+
+/* dst[r] = src[rows[r]] for bf16 rows of `hidden` elements; rows[r] < 0 zeroes row r. The
+ * gather of exited tokens' hidden states from the bank before the LM head
+ * (`_run_coda_forward_graphed`, model_runner.py:1064-1125) and of the prefill rows whose logits
+ * are kept (`logits_to_keep`, continuous_batching/model_runner.py:304-333). */
+int cdb_gather_rows(const void* src, int64_t src_stride, const int32_t* rows, int num_rows, int hidden, void* dst,
+                    int64_t dst_stride, void* stream);
 
 /* Cumulative-hazard exit decision on device (ExitPolicy.should_exit, exit_policy.py:150-169):
  * for row r with hidden slot s = slots[r] (>= 0): h = float(bf16(sigmoid(signal[r]))) when

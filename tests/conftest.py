@@ -1,9 +1,13 @@
-"""Shared pytest setup: the ``gpu`` marker and the repo root on ``sys.path``."""
+"""Shared pytest setup: the ``gpu`` marker, the repo root on ``sys.path``, and a fixed torch
+seed before every test, so a test sees the same random inputs whichever tests ran before it."""
 
 from __future__ import annotations
 
 import sys
 from pathlib import Path
+
+import pytest
+import torch
 
 ROOT = Path(__file__).resolve().parent.parent
 if str(ROOT) not in sys.path:
@@ -12,3 +16,9 @@ if str(ROOT) not in sys.path:
 
 def pytest_configure(config) -> None:
     config.addinivalue_line("markers", "gpu: needs a CUDA B200 and the built sm_100a library")
+
+
+@pytest.fixture(autouse=True)
+def _fixed_torch_seed():
+    torch.manual_seed(0)
+    yield

@@ -4,8 +4,9 @@ c = x @ w^T with bf16 x, w; the reference multiplies the same bf16 values in fp3
 accumulates in fp32 and rounds once, so every element is within one bf16 rounding of the
 reference plus fp32 summation-order noise: |c - ref| <= 2^-8 |ref| + 2^-12 * ||x_row|| ||w_row||.
 Shapes cover the Ouro-1.4B projections (N 6144/2048/11264/2048, K 2048/5632, LM head 49152),
-token counts from 1 to prefill sizes, M/N/K tails, automatic and forced K splits, and
-repeated calls (split-K counters must return to zero).
+token counts from 1 to prefill sizes, M/N/K tails (odd output widths take the scalar store
+path), automatic and forced K splits (clamped to the 8-CTA cluster), and repeated calls (the
+cluster reduction must give bit-identical results).
 """
 
 from __future__ import annotations
@@ -55,6 +56,7 @@ def _check(c, x, w):
         (1, 6144, 2048), (7, 2048, 2048), (33, 11264, 2048), (64, 2048, 5632), (100, 6144, 2048),
         (256, 6144, 2048), (256, 2048, 2048), (256, 11264, 2048), (256, 2048, 5632), (96, 49152, 2048),
         (300, 768, 256), (1024, 1408, 256), (2048, 6144, 2048), (16, 256, 704), (130, 1000, 520),
+        (5, 1001, 512), (40, 130, 4096), (24, 2048, 5632),
     ],
 )
 def test_gemm_matches_fp32_reference(gemm, m, n, k):
@@ -67,17 +69,17 @@ def test_gemm_matches_fp32_reference(gemm, m, n, k):
     _check(c, x, w)
 
 
+@pytest.mark.parametrize("m", [200, 24, 60])
 @pytest.mark.parametrize("splits", [1, 2, 5, 16])
-def test_gemm_forced_splits_and_repeat(gemm, splits):
+def test_gemm_forced_splits_and_repeat(gemm, splits, m):
     g = torch.Generator(device=DEV).manual_seed(splits)
-    x = torch.randn(200, 2048, device=DEV, generator=g).to(torch.bfloat16)
+    x = torch.randn(m, 2048, device=DEV, generator=g).to(torch.bfloat16)
     w = (0.05 * torch.randn(2048, 2048, device=DEV, generator=g)).to(torch.bfloat16)
     first = gemm(x, w, splits=splits)
     for _ in range(3):
         again = gemm(x, w, splits=splits)
         torch.cuda.synchronize()
         assert torch.equal(first, again)  # deterministic across calls
-    assert int(gemm.ctr.abs().sum().item()) == 0
     _check(first, x, w)
 
 
@@ -91,3 +93,44 @@ def test_gemm_strided_operands_and_output(gemm):
     torch.cuda.synchronize()
     _check(out[:, :512], x, w)
     assert out[:, 512:].abs().sum().item() == 0
+
+
+@pytest.mark.parametrize("m,inter,k", [(1, 5632, 2048), (80, 5632, 2048), (256, 5632, 2048), (700, 704, 256), (33, 504, 520)])
+def test_gateup_silu_gemm(gemm, m, inter, k):
+    """cdb_mlp_gateup_silu_gemm == plain GEMM on the same interleaved weight + cdb_silu_mul
+    (bit-exact: same tiles and splits), and within one bf16 rounding of gate/up of the fp32
+    reference act_fn(x Wg^T) * (x Wu^T) with the reference's bf16 rounding points."""
+
+    g = torch.Generator(device=DEV).manual_seed(m + inter + k)
+    x = torch.randn(m, k, device=DEV, generator=g).to(torch.bfloat16)
+    wg = (0.05 * torch.randn(inter, k, device=DEV, generator=g)).to(torch.bfloat16)
+    wu = (0.05 * torch.randn(inter, k, device=DEV, generator=g)).to(torch.bfloat16)
+    w_il = torch.stack([wg, wu], dim=1).reshape(2 * inter, k).contiguous()
+    act = torch.zeros(m, inter, dtype=torch.bfloat16, device=DEV)
+    sp = torch.cuda.current_stream().cuda_stream
+    _lib.call(
+        "cdb_mlp_gateup_silu_gemm", _lib.ptr(x), x.stride(0), _lib.ptr(w_il), w_il.stride(0), _lib.ptr(act),
+        act.stride(0), m, inter, k, 0, 148, _lib.ptr(gemm.status), sp,
+    )
+    gu_il = gemm(x, w_il)
+    gu = torch.cat([gu_il[:, 0::2], gu_il[:, 1::2]], dim=1).contiguous()
+    act2 = torch.zeros_like(act)
+    _lib.call("cdb_silu_mul", _lib.ptr(gu), gu.stride(0), _lib.ptr(act2), act2.stride(0), m, inter, sp)
+    torch.cuda.synchronize()
+    assert int(gemm.status.item()) == 0
+    assert torch.equal(act, act2)
+    gf = x.float() @ wg.float().t()
+    uf = x.float() @ wu.float().t()
+    gb, ub = gf.to(torch.bfloat16), uf.to(torch.bfloat16)
+    ref = (torch.nn.functional.silu(gb.float()).to(torch.bfloat16).float() * ub.float()).to(torch.bfloat16).float()
+    # gate and up each carry the plain GEMM's error bound (one bf16 rounding plus fp32
+    # summation-order noise, as in _check): E = 2^-7 |v| + 2^-12 ||x_row|| ||w_row||. Through
+    # silu(g)*u (|silu'| <= 1.1, |silu(g)| <= |g|) that moves act by at most
+    # 1.1 E_g (|u| + E_u) + (|g| + E_g) E_u, plus the product's own rounding 2^-7 |ref|.
+    # A mis-paired gate/up row is off by O(|ref|).
+    xn = x.float().norm(dim=1)[:, None]
+    e_g = 2**-7 * gf.abs() + 2**-12 * xn * wg.float().norm(dim=1)[None, :]
+    e_u = 2**-7 * uf.abs() + 2**-12 * xn * wu.float().norm(dim=1)[None, :]
+    bound = 1.1 * e_g * (uf.abs() + e_u) + (gf.abs() + e_g) * e_u + 2**-7 * ref.abs() + 1e-6
+    bad = (act.float() - ref).abs() > bound
+    assert not bad.any(), f"{int(bad.sum())} out of bound; max err {(act.float() - ref).abs().max().item():.3e}"

@@ -188,6 +188,7 @@ def _torch_rmsnorm(x, w, eps):
 
 @pytest.mark.parametrize("hidden", [256, 2048, 5280])
 def test_rmsnorm_and_sandwich_add(hidden):
+    torch.manual_seed(hidden)
     n = 33
     eps = 1e-6
     x = torch.randn(n, hidden, device=DEV).to(torch.bfloat16)
@@ -217,7 +218,9 @@ def test_rmsnorm_and_sandwich_add(hidden):
     gr = torch.nn.functional.linear(yr, gw[None], gb)[:, 0]
     assert (x2.float() - xr.float()).abs().max().item() <= 2 ** -6 * xr.float().abs().max().item()
     assert (y.float() - yr.float()).abs().max().item() <= 2 ** -6 * yr.float().abs().max().item()
-    assert (g.float() - gr.float()).abs().max().item() < 2e-2
+    # the gate logit is one bf16 rounding of an fp32 dot product: within 2^-7 of its magnitude
+    # (one ulp), plus summation-order noise near zero
+    assert ((g.float() - gr.float()).abs() <= 2**-7 * gr.float().abs() + 1e-2).all()
 
 
 def test_silu_mul_matches_torch():
@@ -350,3 +353,20 @@ def test_prefill_attention_tiles_match_fp32(heads, d):
     assert int(h.status.item()) == 0
     err = (out.float() - ref).abs().max().item()
     assert err < 2e-2, err
+
+
+@pytest.mark.parametrize("hidden", [2048, 1000])
+def test_gather_rows_exact(hidden):
+    src = torch.randn(20, hidden + 8, device=DEV).to(torch.bfloat16)[:, :hidden]
+    rows = torch.tensor([3, -1, 19, 0, 3], dtype=torch.int32, device=DEV)
+    dst = torch.full((5, hidden), 7.0, device=DEV, dtype=torch.bfloat16)
+    _lib.call(
+        "cdb_gather_rows", _lib.ptr(src), src.stride(0), _lib.ptr(rows), 5, hidden, _lib.ptr(dst), dst.stride(0),
+        torch.cuda.current_stream().cuda_stream,
+    )
+    torch.cuda.synchronize()
+    for i, r in enumerate(rows.tolist()):
+        if r < 0:
+            assert dst[i].abs().sum().item() == 0
+        else:
+            assert torch.equal(dst[i], src[r])
