@@ -15,6 +15,10 @@ import torch
 
 LIB_PATH = Path(__file__).resolve().parent / "libcdb_b200.so"
 
+# int32 entries of an attention work-plan header (CDB_ATTN_PLAN_HEADER_INTS in the C header)
+ATTN_PLAN_MAX_CHUNKS = 1024
+ATTN_PLAN_HEADER_INTS = 4 + ATTN_PLAN_MAX_CHUNKS + 1
+
 # name -> argtypes (all return int status unless listed in _RESTYPES)
 _SIGNATURES: dict[str, list] = {
     "cdb_version": [],
@@ -25,7 +29,7 @@ _SIGNATURES: dict[str, list] = {
         c_void_p, c_int64,  # out, out_stride
         c_void_p, c_int, c_int64, c_int,  # kv_base, num_cache_layers, kv_rows, cache_layer
         c_void_p, c_int64, c_void_p, c_void_p,  # block_table, stride, item_slot, item_pos
-        c_int, c_void_p, c_void_p, c_int,  # rope_mode, cos, sin, append
+        c_int, c_void_p, c_void_p, c_void_p, c_int,  # rope_mode, cos, sin, qk_bias, append
         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,  # plan_header, units, part_o, part_ml, counters
         c_int, c_int, c_int, c_int, c_int,  # scratch_items, num_items, num_heads, head_dim, block_size
         c_float, c_int, c_void_p, c_void_p,  # scale, num_ctas, status, stream
@@ -35,7 +39,7 @@ _SIGNATURES: dict[str, list] = {
         c_void_p, c_int64,  # out, out_stride
         c_void_p, c_int, c_int64, c_int,  # kv_base, num_cache_layers, kv_rows, cache_layer
         c_void_p, c_int64, c_void_p, c_void_p,  # block_table, stride, item_slot, item_pos
-        c_int, c_void_p, c_void_p, c_int,  # rope_mode, cos, sin, append
+        c_int, c_void_p, c_void_p, c_void_p, c_int,  # rope_mode, cos, sin, qk_bias, append
         c_int, c_int, c_int, c_int,  # num_items, num_heads, head_dim, block_size
         c_float, c_int, c_void_p, c_void_p,  # scale, num_ctas, status, stream
     ],
@@ -46,7 +50,8 @@ _SIGNATURES: dict[str, list] = {
     "cdb_attn_scratch_bytes": [c_int, c_int, c_int],
     "cdb_rope_append_kv": [
         c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int64, c_int,
-        c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
+        c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p,  # ... cos, sin, qk_bias
+        c_int, c_int, c_int, c_int, c_void_p,
     ],
     "cdb_prefill_attention": [
         c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int64, c_int,
@@ -67,7 +72,15 @@ _SIGNATURES: dict[str, list] = {
     "cdb_silu_mul": [c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_void_p],
     "cdb_gather_rows": [c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_int64, c_void_p],
     "cdb_argmax": [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
-    "cdb_embed": [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int, c_void_p, c_void_p],
+    "cdb_embed": [
+        c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int, c_float, c_void_p,
+        c_void_p,
+    ],
+    "cdb_sandwich_norm": [
+        c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
+        c_void_p, c_int64, c_int, c_int, c_float, c_void_p,
+    ],
+    "cdb_latent_diff": [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_void_p],
     "cdb_block_table_update": [c_void_p, c_int64, c_void_p, c_int, c_void_p],
     "cdb_exit_kv_copy": [c_void_p, c_int, c_int64, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p],
     "cdb_exit_hazard": [

@@ -26,7 +26,8 @@
 namespace cdb {
 
 constexpr int kMaxSplits = 64;
-constexpr int kBlock = 16;  // tokens per page (block_size)
+constexpr int kBlock = 16;           // tokens per page (block_size)
+constexpr int kMaxPlanChunks = CDB_ATTN_PLAN_MAX_CHUNKS;
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D, int HG>
@@ -72,6 +73,24 @@ struct AttnParams {
   int32_t* status;
 };
 
+// A work unit: `row`'s head group `hg`, pages [b0, b1) of its cache, split `split` of `nsplit`.
+struct Unit {
+  int row, hg, split, nsplit, b0, b1;
+};
+__device__ __forceinline__ Unit decode_unit(int4 u) {
+  return Unit{u.x, u.y >> 16, u.y & 0xffff, u.w, u.z >> 16, u.z & 0xffff};
+}
+// Units of chunk c: a range from the plan header, or unit c alone when segments are whole.
+__device__ __forceinline__ void chunk_units(const int32_t* hdr, int c, int& u0, int& u1) {
+  if (hdr[3]) {
+    u0 = c;
+    u1 = c + 1;
+  } else {
+    u0 = hdr[4 + c];
+    u1 = hdr[5 + c];
+  }
+}
+
 // Rotated value of element d of one head vector (Ouro split-half rotate_half RoPE with
 // bf16 cos/sin, every product and the sum rounded to bf16 as PyTorch's bf16 ops round).
 __device__ __forceinline__ float rope_half(float x_d, float x_partner, bool low_half, float c, float s) {
@@ -102,8 +121,7 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
   pdl_trigger();
   pdl_wait();
 
-  const int n_units = p.hdr[0];
-  const int sb = p.hdr[1];
+  const int n_chunks = p.hdr[1];
 
   if (warp == C::CONSUMERS) {
     // ------------------------------------------------------------- producer warp
@@ -111,13 +129,14 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
     int stage = 0;
     uint32_t phase = 0;
     bool alive = true;
-    for (int u = blockIdx.x; u < n_units && alive; u += gridDim.x) {
-      const int4 unit = p.units[u];
-      const int pos = p.item_pos[unit.x];
-      const int nb = (pos + kBlock) / kBlock;
-      const int b0 = unit.z * sb;
-      const int b1 = min(b0 + sb, nb);
-      const int32_t* bt = p.block_table + (int64_t)p.item_slot[unit.x] * p.bt_stride;
+    for (int c = blockIdx.x; c < n_chunks && alive; c += gridDim.x) {
+    int u0, u1;
+    chunk_units(p.hdr, c, u0, u1);
+    for (int u = u0; u < u1 && alive; ++u) {
+      const Unit unit = decode_unit(p.units[u]);
+      const int b0 = unit.b0;
+      const int b1 = unit.b1;
+      const int32_t* bt = p.block_table + (int64_t)p.item_slot[unit.row] * p.bt_stride;
       for (int base = b0; base < b1 && alive; base += 32) {
         const int my = base + lane < b1 ? bt[base + lane] : 0;
         const int cnt = min(32, b1 - base);
@@ -127,8 +146,8 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
             if (mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
               mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
               uint8_t* dst = smem + stage * C::STAGE_BYTES;
-              tma_load_4d(dst, &map, &full[stage], 0, unit.y * HG, block_id * kBlock, 2 * p.cache_layer);
-              tma_load_4d(dst + C::TILE_BYTES, &map, &full[stage], 0, unit.y * HG, block_id * kBlock,
+              tma_load_4d(dst, &map, &full[stage], 0, unit.hg * HG, block_id * kBlock, 2 * p.cache_layer);
+              tma_load_4d(dst + C::TILE_BYTES, &map, &full[stage], 0, unit.hg * HG, block_id * kBlock,
                           2 * p.cache_layer + 1);
             } else {
               alive = false;
@@ -142,6 +161,7 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
           }
         }
       }
+    }
     }
     return;
   }
@@ -157,17 +177,19 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
   uint32_t phase = 0;
   bool alive = true;
 
-  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-    const int4 unit = p.units[u];
-    const int item = unit.x;
-    const int head = unit.y * HG + hh;
-    const int split = unit.z;
-    const int nsplit = unit.w;
+  for (int c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+  int u0, u1;
+  chunk_units(p.hdr, c, u0, u1);
+  for (int u = u0; u < u1; ++u) {
+    const Unit unit = decode_unit(p.units[u]);
+    const int item = unit.row;
+    const int head = unit.hg * HG + hh;
+    const int split = unit.split;
+    const int nsplit = unit.nsplit;
     const int pos = p.item_pos[item];
     const int n_cached = pos + 1;
-    const int nb = (n_cached + kBlock - 1) / kBlock;
-    const int b0 = split * sb;
-    const int b1 = min(b0 + sb, nb);
+    const int b0 = unit.b0;
+    const int b1 = unit.b1;
 
     // this lane's q slice (already rotated), pre-scaled by softmax_scale*log2(e)
     const __nv_bfloat16* qrow = p.qkv + (int64_t)item * p.qkv_stride + (int64_t)head * D;
@@ -357,13 +379,49 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
       if (j < C::NPAIR) reinterpret_cast<uint32_t*>(orow)[j] = pack_bf16x2(acc[2 * i] * inv, acc[2 * i + 1] * inv);
     }
   }
+  }
 }
 
 // ------------------------------------------------------------------ work plan (one CTA)
-__global__ void __launch_bounds__(1024) attn_plan_kernel(const int32_t* item_pos, int n, int append, int nhg,
-                                                         int capacity, int scratch_items, int target_units,
-                                                         int32_t* hdr, int4* units) {
-  __shared__ int s_total, s_max, s_sb;
+// Exclusive block-wide scan of one int per thread (blockDim.x == 1024); `total` gets the sum.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int& total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += t;
+  }
+  if (lane == 31) s_warp[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    int y = s_warp[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, y, o);
+      if (lane >= o) y += t;
+    }
+    s_warp[lane] = y;
+  }
+  __syncthreads();
+  const int excl = (w > 0 ? s_warp[w - 1] : 0) + x - v;
+  total = s_warp[31];
+  __syncthreads();
+  return excl;
+}
+
+// Balanced plan. The launch's work is the sequence of pages of every (row, head group) segment,
+// rows in order and head groups inner, cut into n_chunks equal chunks of `ch` pages (about one
+// chunk per CTA). A segment crossing chunk boundaries becomes one unit per chunk it touches
+// (split-KV pieces, merged by the last warp to finish); chunk c's units are
+// [hdr[4 + c], hdr[5 + c]). Every CTA streams the same number of pages, so no CTA is left with
+// a whole extra segment at the end. When the rows exceed the split-combine scratch
+// (n > scratch_items) segments are not split: one unit each, dealt round-robin (hdr[3] = 1).
+// Units: int4 {row, head_group << 16 | split, first_page << 16 | end_page, num_splits}.
+__global__ void __launch_bounds__(1024) attn_plan_kernel(const int32_t* item_pos, int n, int nhg, int capacity,
+                                                         int scratch_items, int target_chunks, int32_t* hdr,
+                                                         int4* units) {
+  __shared__ int s_total, s_max, s_ch, s_nch;
   __shared__ int s_warp[32];
   pdl_trigger();
   pdl_wait();
@@ -376,88 +434,93 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const int32_t* item_pos
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int pos = item_pos[i];
     if (pos < 0) continue;
-    const int nc = pos + 1;
-    const int nb = (nc + kBlock - 1) / kBlock;
+    const int nb = (pos + kBlock) / kBlock;  // pages of the cached positions 0..pos
     local_total += nb;
     local_max = max(local_max, nb);
   }
   atomicAdd(&s_total, local_total);
   atomicMax(&s_max, local_max);
   __syncthreads();
+  const bool whole = n > scratch_items;
   if (threadIdx.x == 0) {
-    const long long work = (long long)s_total * nhg;
-    int sb = (int)((work + target_units - 1) / target_units);
-    sb = max(sb, 4);
-    sb = max(sb, (s_max + kMaxSplits - 1) / kMaxSplits);
-    if (n > scratch_items) sb = max(sb, s_max);
-    s_sb = max(sb, 1);
+    const long long T = (long long)s_total * nhg;
+    const int C = max(1, min(target_chunks, kMaxPlanChunks));
+    long long ch = (T + C - 1) / C;
+    ch = max(ch, (long long)((s_max + kMaxSplits - 3) / (kMaxSplits - 2)));  // <= kMaxSplits pieces a segment
+    ch = max(ch, 2LL);
+    s_ch = (int)ch;
+    s_nch = T > 0 ? (int)((T + ch - 1) / ch) : 0;
   }
   __syncthreads();
-  const int sb = s_sb;
-  // Exclusive scan of per-item unit counts, in chunks of blockDim.x items.
-  int carry = 0;
+  const long long ch = s_ch;
+  const int nch = s_nch;
+  int carry_p = 0, carry_u = 0;
   for (int start = 0; start < n; start += blockDim.x) {
     const int i = start + threadIdx.x;
-    int cnt = 0, ns = 0;
+    int p = 0;
     if (i < n) {
       const int pos = item_pos[i];
-      if (pos >= 0) {
-        const int nc = pos + 1;
-        const int nb = (nc + kBlock - 1) / kBlock;
-        ns = max(1, (nb + sb - 1) / sb);
-        cnt = ns * nhg;
-      }
+      if (pos >= 0) p = (pos + kBlock) / kBlock;
     }
-    // warp inclusive scan
-    int v = cnt;
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(0xffffffffu, v, o);
-      if (lane >= o) v += t;
-    }
-    if (lane == 31) s_warp[w] = v;
-    __syncthreads();
-    if (w == 0) {
-      int x = (lane < (int)(blockDim.x >> 5)) ? s_warp[lane] : 0;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += t;
-      }
-      s_warp[lane] = x;
-    }
-    __syncthreads();
-    const int excl = carry + (w > 0 ? s_warp[w - 1] : 0) + v - cnt;
-    if (i < n && cnt > 0) {
-      // Split-major: the head groups of one (row, split) are consecutive units, so CTAs with
-      // consecutive indices read the same pages' K/V rows at the same time.
-      for (int s = 0; s < ns; ++s)
+    int tile_pages;
+    const int ep = block_exclusive_scan(p, s_warp, tile_pages);
+    const long long S0 = (long long)(carry_p + ep) * nhg;  // first page of segment (i, 0)
+    int pieces = 0;
+    if (p > 0) {
+      if (whole) {
+        pieces = nhg;
+      } else {
         for (int g = 0; g < nhg; ++g) {
-          const int idx = excl + s * nhg + g;
-          if (idx < capacity) units[idx] = make_int4(i, g, s, ns);
+          const long long S = S0 + (long long)g * p;
+          pieces += (int)((S + p - 1) / ch - S / ch + 1);
         }
+      }
     }
-    const int chunk_total = s_warp[(blockDim.x >> 5) - 1];
-    __syncthreads();
-    carry += chunk_total;
+    int tile_units;
+    int u = carry_u + block_exclusive_scan(pieces, s_warp, tile_units);
+    if (p > 0) {
+      for (int g = 0; g < nhg; ++g) {
+        if (whole) {
+          if (u < capacity) units[u] = make_int4(i, g << 16, p, 1);
+          ++u;
+          continue;
+        }
+        const long long S = S0 + (long long)g * p;
+        const long long fc = S / ch;
+        const int ns = (int)((S + p - 1) / ch - fc + 1);
+        for (int k = 0; k < ns; ++k) {
+          const long long c = fc + k;
+          const int b0 = (int)max(0LL, c * ch - S);
+          const int b1 = (int)min((long long)p, (c + 1) * ch - S);
+          if (u < capacity) units[u] = make_int4(i, (g << 16) | k, (b0 << 16) | b1, ns);
+          if (c * ch >= S && c < nch) hdr[4 + c] = min(u, capacity);  // chunk c starts in this segment
+          ++u;
+        }
+      }
+    }
+    carry_p += tile_pages;
+    carry_u += tile_units;
   }
   if (threadIdx.x == 0) {
-    hdr[0] = min(carry, capacity);
-    hdr[1] = sb;
+    const int n_units = min(carry_u, capacity);
+    hdr[0] = n_units;
+    hdr[1] = whole ? n_units : nch;
     hdr[2] = kMaxSplits;
-    hdr[3] = 0;
+    hdr[3] = whole ? 1 : 0;
+    if (!whole) hdr[4 + nch] = n_units;
   }
 }
 
 // ------------------------------------------------------------------ rope + append
 // One CTA per row: rotate q in place, rotate k, write k and v to the row's cache slot. Each
 // thread owns one rotation pair of one head, so the in-place update needs no synchronisation.
+// qk_bias (bf16 [2][heads][D], q bias then k bias; may be null) is added to q and k in bf16
+// before the rotation (HuginnAttention.forward, modeling_huginn.py:261-264).
 __global__ void rope_append_kernel(__nv_bfloat16* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col,
                                    __nv_bfloat16* kv, int64_t kv_rows, int cache_layer, const int32_t* block_table,
                                    int64_t bt_stride, const int32_t* item_slot, const int32_t* item_pos,
-                                   int rope_mode, const void* rope_cos, const void* rope_sin, int num_heads, int D,
-                                   int32_t* status) {
+                                   int rope_mode, const void* rope_cos, const void* rope_sin,
+                                   const __nv_bfloat16* qk_bias, int num_heads, int D, int32_t* status) {
   pdl_trigger();
   pdl_wait();
   const int item = blockIdx.x;
@@ -477,6 +540,16 @@ __global__ void rope_append_kernel(__nv_bfloat16* qkv, int64_t qkv_stride, int64
   __nv_bfloat16* kd = kv + ((int64_t)(2 * cache_layer) * kv_rows + row) * hstride;
   __nv_bfloat16* vd = kv + ((int64_t)(2 * cache_layer + 1) * kv_rows + row) * hstride;
   const int half = D / 2;
+  const __nv_bfloat16* kb = qk_bias ? qk_bias + (int64_t)num_heads * D : nullptr;
+  // element d of head h of q (or k), with the bias added in bf16 when present
+  auto qval = [&](int64_t hb, int d) {
+    const float x = bf16_to_f(q[hb + d]);
+    return qk_bias ? round_bf16(x + bf16_to_f(qk_bias[hb + d])) : x;
+  };
+  auto kval = [&](int64_t hb, int d) {
+    const float x = bf16_to_f(k[hb + d]);
+    return kb ? round_bf16(x + bf16_to_f(kb[hb + d])) : x;
+  };
   for (int i = threadIdx.x; i < num_heads * half; i += blockDim.x) {
     const int h = i / half, j = i % half;
     const int64_t hb = (int64_t)h * D;
@@ -484,8 +557,8 @@ __global__ void rope_append_kernel(__nv_bfloat16* qkv, int64_t qkv_stride, int64
       const __nv_bfloat16* cr = static_cast<const __nv_bfloat16*>(rope_cos) + (int64_t)pos * D;
       const __nv_bfloat16* sr = static_cast<const __nv_bfloat16*>(rope_sin) + (int64_t)pos * D;
       const int d0 = j, d1 = j + half;
-      const float q0 = bf16_to_f(q[hb + d0]), q1 = bf16_to_f(q[hb + d1]);
-      const float k0 = bf16_to_f(k[hb + d0]), k1 = bf16_to_f(k[hb + d1]);
+      const float q0 = qval(hb, d0), q1 = qval(hb, d1);
+      const float k0 = kval(hb, d0), k1 = kval(hb, d1);
       const float c0 = bf16_to_f(cr[d0]), s0 = bf16_to_f(sr[d0]), c1 = bf16_to_f(cr[d1]), s1 = bf16_to_f(sr[d1]);
       q[hb + d0] = f_to_bf16(rope_half(q0, q1, true, c0, s0));
       q[hb + d1] = f_to_bf16(rope_half(q1, q0, false, c1, s1));
@@ -497,20 +570,25 @@ __global__ void rope_append_kernel(__nv_bfloat16* qkv, int64_t qkv_stride, int64
       // Huginn interleaved pairs (2j, 2j+1) rotated in fp32 (modeling_huginn.py:178-196).
       const float* cr = static_cast<const float*>(rope_cos) + (int64_t)pos * half;
       const float* sr = static_cast<const float*>(rope_sin) + (int64_t)pos * half;
+      // Each product and the sum rounded separately (no contraction), as the fp32 tensor ops do.
       const int d0 = 2 * j, d1 = 2 * j + 1;
       const float c = cr[j], s = sr[j];
-      const float q0 = bf16_to_f(q[hb + d0]), q1 = bf16_to_f(q[hb + d1]);
-      const float k0 = bf16_to_f(k[hb + d0]), k1 = bf16_to_f(k[hb + d1]);
-      q[hb + d0] = f_to_bf16(q0 * c - q1 * s);
-      q[hb + d1] = f_to_bf16(q1 * c + q0 * s);
-      kd[hb + d0] = f_to_bf16(k0 * c - k1 * s);
-      kd[hb + d1] = f_to_bf16(k1 * c + k0 * s);
+      const float q0 = qval(hb, d0), q1 = qval(hb, d1);
+      const float k0 = kval(hb, d0), k1 = kval(hb, d1);
+      q[hb + d0] = f_to_bf16(__fsub_rn(__fmul_rn(q0, c), __fmul_rn(q1, s)));
+      q[hb + d1] = f_to_bf16(__fadd_rn(__fmul_rn(q1, c), __fmul_rn(q0, s)));
+      kd[hb + d0] = f_to_bf16(__fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, s)));
+      kd[hb + d1] = f_to_bf16(__fadd_rn(__fmul_rn(k1, c), __fmul_rn(k0, s)));
       vd[hb + d0] = v[hb + d0];
       vd[hb + d1] = v[hb + d1];
     } else {
       const int d0 = 2 * j, d1 = 2 * j + 1;
-      kd[hb + d0] = k[hb + d0];
-      kd[hb + d1] = k[hb + d1];
+      if (qk_bias) {
+        q[hb + d0] = f_to_bf16(qval(hb, d0));
+        q[hb + d1] = f_to_bf16(qval(hb, d1));
+      }
+      kd[hb + d0] = f_to_bf16(kval(hb, d0));
+      kd[hb + d1] = f_to_bf16(kval(hb, d1));
       vd[hb + d0] = v[hb + d0];
       vd[hb + d1] = v[hb + d1];
     }
@@ -605,15 +683,15 @@ static int heads_per_cta(int num_heads, int head_dim) {
 static int launch_rope_append(void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col, void* kv_base,
                               int64_t kv_rows, int cache_layer, const int32_t* block_table, int64_t bt_stride,
                               const int32_t* item_slot, const int32_t* item_pos, int rope_mode, const void* rope_cos,
-                              const void* rope_sin, int num_items, int num_heads, int head_dim, int32_t* status,
-                              cudaStream_t st) {
+                              const void* rope_sin, const void* qk_bias, int num_items, int num_heads, int head_dim,
+                              int32_t* status, cudaStream_t st) {
   if (num_items == 0) return CDB_OK;
   const int pairs = num_heads * (head_dim / 2);
   const int threads = pairs >= 1024 ? 1024 : ((pairs + 31) / 32) * 32;
   return launch_pdl(rope_append_kernel, dim3(num_items), dim3(threads), 0, st, static_cast<__nv_bfloat16*>(qkv),
                     qkv_stride, k_col, v_col, static_cast<__nv_bfloat16*>(kv_base), kv_rows, cache_layer, block_table,
-                    bt_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin, num_heads, head_dim,
-                    status) == cudaSuccess
+                    bt_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin,
+                    static_cast<const __nv_bfloat16*>(qk_bias), num_heads, head_dim, status) == cudaSuccess
              ? CDB_OK
              : CDB_ERR_CUDA;
 }
@@ -628,9 +706,11 @@ extern "C" int cdb_attn_plan(const int32_t* item_pos, int num_items, int append,
   if (block_size != kBlock || num_items < 0 || unit_capacity <= 0) return CDB_ERR_INVALID_ARGUMENT;
   const int hg = heads_per_cta(num_heads, head_dim);
   if (hg == 0) return CDB_ERR_UNSUPPORTED;
-  const int target = 8 * (num_sms > 0 ? num_sms : 148);
+  (void)append;  // the attention kernel reads only cached rows; append happens before it
+  // one chunk per attention CTA: the decode launch runs 2 CTAs per SM
+  const int target = 2 * (num_sms > 0 ? num_sms : 148);
   return launch_pdl(attn_plan_kernel, dim3(1), dim3(1024), 0, static_cast<cudaStream_t>(stream), item_pos, num_items,
-                    append, num_heads / hg, unit_capacity, scratch_items, target, plan_header,
+                    num_heads / hg, unit_capacity, scratch_items, target, plan_header,
                     static_cast<int4*>(units)) == cudaSuccess
              ? CDB_OK
              : CDB_ERR_CUDA;
@@ -645,8 +725,8 @@ extern "C" int cdb_paged_decode_attn_append(void* qkv, int64_t qkv_stride, int64
                                             int64_t out_stride, void* kv_base, int num_cache_layers, int64_t kv_rows,
                                             int cache_layer, const int32_t* block_table, int64_t block_table_stride,
                                             const int32_t* item_slot, const int32_t* item_pos, int rope_mode,
-                                            const void* rope_cos, const void* rope_sin, int append,
-                                            const int32_t* plan_header, const void* units, float* part_o,
+                                            const void* rope_cos, const void* rope_sin, const void* qk_bias,
+                                            int append, const int32_t* plan_header, const void* units, float* part_o,
                                             float* part_ml, int32_t* counters, int scratch_items, int num_items,
                                             int num_heads, int head_dim, int block_size, float scale, int num_ctas,
                                             int32_t* status, void* stream) {
@@ -663,8 +743,8 @@ extern "C" int cdb_paged_decode_attn_append(void* qkv, int64_t qkv_stride, int64
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (append) {
     const int rc = launch_rope_append(qkv, qkv_stride, k_col, v_col, kv_base, kv_rows, cache_layer, block_table,
-                                      block_table_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin, num_items,
-                                      num_heads, head_dim, status, st);
+                                      block_table_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin, qk_bias,
+                                      num_items, num_heads, head_dim, status, st);
     if (rc != CDB_OK) return rc;
   }
   CUtensorMap map;
@@ -699,13 +779,13 @@ extern "C" int cdb_paged_decode_attn_append(void* qkv, int64_t qkv_stride, int64
 extern "C" int cdb_rope_append_kv(void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col, void* kv_base,
                                   int num_cache_layers, int64_t kv_rows, int cache_layer, const int32_t* block_table,
                                   int64_t block_table_stride, const int32_t* item_slot, const int32_t* item_pos,
-                                  int rope_mode, const void* rope_cos, const void* rope_sin, int num_items,
-                                  int num_heads, int head_dim, int block_size, void* stream) {
+                                  int rope_mode, const void* rope_cos, const void* rope_sin, const void* qk_bias,
+                                  int num_items, int num_heads, int head_dim, int block_size, void* stream) {
   if (block_size != kBlock || cache_layer < 0 || cache_layer >= num_cache_layers || head_dim % 2 != 0 ||
       rope_mode < 0 || rope_mode > 2)
     return CDB_ERR_INVALID_ARGUMENT;
   return launch_rope_append(qkv, qkv_stride, k_col, v_col, kv_base, kv_rows, cache_layer, block_table,
-                            block_table_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin, num_items,
+                            block_table_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin, qk_bias, num_items,
                             num_heads, head_dim, nullptr, static_cast<cudaStream_t>(stream));
 }
 
@@ -717,7 +797,7 @@ extern "C" int cdb_rope_append_kv(void* qkv, int64_t qkv_stride, int64_t k_col, 
 // stream is being captured), and a plugin that is handed only tensors has no allocator to ask.
 // For them the work plan and the split-KV combine scratch of this entry point live in one
 // file-scope device array instead of caller buffers. Every GPU that loads the library holds the
-// array (4,784,896 bytes) until the process exits.
+// array (4,788,992 bytes) until the process exits.
 // ======================================================================================
 namespace cdb {
 namespace noalloc {
@@ -729,7 +809,7 @@ constexpr size_t kPartMLFloats = (size_t)kRowHeads * kMaxSplits * 2;
 constexpr size_t kOffPartML = kPartOFloats * 4;
 constexpr size_t kOffCounters = kOffPartML + kPartMLFloats * 4;
 constexpr size_t kOffHeader = kOffCounters + (size_t)kRowHeads * 4;
-constexpr size_t kOffUnits = (kOffHeader + 16 + 255) / 256 * 256;
+constexpr size_t kOffUnits = (kOffHeader + CDB_ATTN_PLAN_HEADER_INTS * 4 + 255) / 256 * 256;
 constexpr size_t kBytes = kOffUnits + (size_t)kMaxUnits * 16;
 constexpr int kMaxDevices = 64;
 }  // namespace noalloc
@@ -783,7 +863,8 @@ extern "C" int cdb_paged_decode_attn_append_static(void* qkv, int64_t qkv_stride
                                                    int64_t kv_rows, int cache_layer, const int32_t* block_table,
                                                    int64_t block_table_stride, const int32_t* item_slot,
                                                    const int32_t* item_pos, int rope_mode, const void* rope_cos,
-                                                   const void* rope_sin, int append, int num_items, int num_heads,
+                                                   const void* rope_sin, const void* qk_bias, int append,
+                                                   int num_items, int num_heads,
                                                    int head_dim, int block_size, float scale, int num_ctas,
                                                    int32_t* status, void* stream) {
   using namespace cdb::noalloc;
@@ -815,13 +896,13 @@ extern "C" int cdb_paged_decode_attn_append_static(void* qkv, int64_t qkv_stride
   if (cudaMemsetAsync(counters, 0, (size_t)kRowHeads * 4, st) != cudaSuccess) return CDB_ERR_CUDA;
   if (append) {
     rc = launch_rope_append(qkv, qkv_stride, k_col, v_col, kv_base, kv_rows, cache_layer, block_table,
-                            block_table_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin, num_items,
-                            num_heads, head_dim, status, st);
+                            block_table_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin, qk_bias,
+                            num_items, num_heads, head_dim, status, st);
     if (rc != CDB_OK) return rc;
   }
-  const int target = 8 * 148;
-  if (launch_pdl(attn_plan_kernel, dim3(1), dim3(1024), 0, st, item_pos, num_items, 0, num_heads / hg, kMaxUnits,
-                 scratch_items, target, header, static_cast<int4*>(units)) != cudaSuccess)
+  if (num_ctas <= 0) num_ctas = 2 * 148;
+  if (launch_pdl(attn_plan_kernel, dim3(1), dim3(1024), 0, st, item_pos, num_items, num_heads / hg, kMaxUnits,
+                 scratch_items, num_ctas, header, static_cast<int4*>(units)) != cudaSuccess)
     return CDB_ERR_CUDA;
   CUtensorMap map;
   rc = encode_kv_map(&map, kv_base, num_cache_layers, kv_rows, num_heads, head_dim, hg);

@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(512) argmax_kernel(const __nv_bfloat16* logits
 
 __global__ void embed_kernel(const __nv_bfloat16* table, int hidden, int vocab, const int32_t* ids,
                              const int32_t* id_src, const int32_t* token_table, __nv_bfloat16* out, int64_t os,
-                             const int32_t* out_rows, int32_t* status) {
+                             const int32_t* out_rows, float scale, int32_t* status) {
   pdl_trigger();
   pdl_wait();
   const int r = blockIdx.x;
@@ -248,11 +248,85 @@ __global__ void embed_kernel(const __nv_bfloat16* table, int hidden, int vocab, 
     return;
   }
   const __nv_bfloat16* src = table + (int64_t)id * hidden;
-  if ((hidden & 7) == 0) {
+  if (scale != 1.f) {
+    // wte(ids) * scale in bf16: fp32 product rounded once (modeling_huginn.py:431)
+    for (int d = threadIdx.x; d < hidden; d += blockDim.x) o[d] = f_to_bf16(bf16_to_f(src[d]) * scale);
+  } else if ((hidden & 7) == 0) {
     for (int d = threadIdx.x * 8; d < hidden; d += blockDim.x * 8)
       *reinterpret_cast<uint4*>(o + d) = *reinterpret_cast<const uint4*>(src + d);
   } else {
     for (int d = threadIdx.x; d < hidden; d += blockDim.x) o[d] = src[d];
+  }
+}
+
+// Huginn's sandwich-norm row step, general enough for every block boundary and stage edge:
+//   v = xs[x_rows ? x_rows[r] : r]; if a: v = bf16(v + a[r]); if w1: v = rmsnorm(v; w1);
+//   if xd: xd[xd_rows ? xd_rows[r] : r] = v (skipped when that index < 0);
+//   if w2: y[r] = rmsnorm(v; w2).
+// (HuginnBlock.forward modeling_huginn.py:333-336: x = norm_2(attn + x), norm_3(x); x = norm_4(mlp
+// + x), then the next block's norm_1; run_coda :454-460: ln_f before and after the coda blocks.)
+__global__ void __launch_bounds__(kRowThreads) sandwich_norm_kernel(
+    const __nv_bfloat16* xs, int64_t xss, const int32_t* x_rows, const __nv_bfloat16* a, int64_t as,
+    const __nv_bfloat16* w1, __nv_bfloat16* xd, int64_t xds, const int32_t* xd_rows, const __nv_bfloat16* w2,
+    __nv_bfloat16* y, int64_t ys, int hidden, float eps) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[32];
+  const int r = blockIdx.x;
+  const int src = x_rows ? x_rows[r] : r;
+  if (src < 0) return;
+  RowRegs v;
+  load_row(xs + (int64_t)src * xss, hidden, v);
+  if (a) {
+    RowRegs av;
+    load_row(a + (int64_t)r * as, hidden, av);
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v.v[c][k] = round_bf16(av.v[c][k] + v.v[c][k]);
+  }
+  if (w1) rms_inplace(v, w1, hidden, eps, red);
+  if (xd) {
+    const int dst = xd_rows ? xd_rows[r] : r;
+    if (dst >= 0) store_row(xd + (int64_t)dst * xds, hidden, v);
+  }
+  if (w2) {
+    rms_inplace(v, w2, hidden, eps, red);
+    store_row(y + (int64_t)r * ys, hidden, v);
+  }
+}
+
+// latent_diff (models/huginn/exit_gates.py:33-40) in bf16 tensors, as the adapter computes it:
+// d = bf16(new - old); out[r] = bf16(bf16(||d||) / max(bf16(||new||), 1e-9)), norms accumulated
+// in fp32. new row rows[r] (r when rows == NULL), old row r; rows[r] < 0 skips row r.
+__global__ void __launch_bounds__(kRowThreads) latent_diff_kernel(const __nv_bfloat16* nw, int64_t ns,
+                                                                  const __nv_bfloat16* old, int64_t os,
+                                                                  const int32_t* rows, int hidden,
+                                                                  __nv_bfloat16* out) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[32];
+  const int r = blockIdx.x;
+  const int nr = rows ? rows[r] : r;
+  if (nr < 0) return;
+  RowRegs a, b;
+  load_row(nw + (int64_t)nr * ns, hidden, a);
+  load_row(old + (int64_t)r * os, hidden, b);
+  float sd = 0.f, sn = 0.f;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float d = round_bf16(a.v[c][k] - b.v[c][k]);
+      sd = fmaf(d, d, sd);
+      sn = fmaf(a.v[c][k], a.v[c][k], sn);
+    }
+  sd = block_sum(sd, red);
+  sn = block_sum(sn, red);
+  if (threadIdx.x == 0) {
+    const float nd = round_bf16(sqrtf(sd));
+    const float nn = fmaxf(round_bf16(sqrtf(sn)), 1e-9f);
+    out[r] = f_to_bf16(nd / nn);
   }
 }
 
@@ -419,13 +493,37 @@ extern "C" int cdb_argmax(const void* logits, int64_t stride, int num_rows, int 
 
 extern "C" int cdb_embed(const void* table, int hidden, int vocab, const int32_t* ids, const int32_t* id_src,
                          const int32_t* token_table, void* out, int64_t out_stride, const int32_t* out_rows,
-                         int num_rows, int32_t* status, void* stream) {
+                         int num_rows, float scale, int32_t* status, void* stream) {
   if (hidden <= 0 || vocab <= 0 || num_rows < 0 || (ids == nullptr && id_src == nullptr)) return CDB_ERR_INVALID_ARGUMENT;
   if (id_src != nullptr && token_table == nullptr) return CDB_ERR_INVALID_ARGUMENT;
   if (num_rows == 0) return CDB_OK;
   launch_pdl(embed_kernel, dim3(num_rows), dim3(128), 0, static_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(table), hidden, vocab, ids, id_src, token_table,
-      static_cast<__nv_bfloat16*>(out), out_stride, out_rows, status);
+      static_cast<__nv_bfloat16*>(out), out_stride, out_rows, scale, status);
+  return check_launch();
+}
+
+extern "C" int cdb_sandwich_norm(const void* x_src, int64_t x_src_stride, const int32_t* x_rows, const void* add,
+                                 int64_t add_stride, const void* w1, void* x_dst, int64_t x_dst_stride,
+                                 const int32_t* x_dst_rows, const void* w2, void* y, int64_t y_stride, int num_rows,
+                                 int hidden, float eps, void* stream) {
+  if (hidden % 8 != 0 || hidden > kRowThreads * kMaxChunks * 8 || num_rows < 0 || (w2 != nullptr && y == nullptr))
+    return CDB_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return CDB_OK;
+  launch_pdl(sandwich_norm_kernel, dim3(num_rows), dim3(kRowThreads), 0, static_cast<cudaStream_t>(stream),
+             static_cast<const __nv_bfloat16*>(x_src), x_src_stride, x_rows, static_cast<const __nv_bfloat16*>(add),
+             add_stride, static_cast<const __nv_bfloat16*>(w1), static_cast<__nv_bfloat16*>(x_dst), x_dst_stride,
+             x_dst_rows, static_cast<const __nv_bfloat16*>(w2), static_cast<__nv_bfloat16*>(y), y_stride, hidden, eps);
+  return check_launch();
+}
+
+extern "C" int cdb_latent_diff(const void* new_state, int64_t new_stride, const void* old_state, int64_t old_stride,
+                               const int32_t* rows, int num_rows, int hidden, void* out, void* stream) {
+  if (hidden % 8 != 0 || hidden > kRowThreads * kMaxChunks * 8 || num_rows < 0) return CDB_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return CDB_OK;
+  launch_pdl(latent_diff_kernel, dim3(num_rows), dim3(kRowThreads), 0, static_cast<cudaStream_t>(stream),
+             static_cast<const __nv_bfloat16*>(new_state), new_stride, static_cast<const __nv_bfloat16*>(old_state),
+             old_stride, rows, hidden, static_cast<__nv_bfloat16*>(out));
   return check_launch();
 }
 

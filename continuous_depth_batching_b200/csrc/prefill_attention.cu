@@ -34,10 +34,19 @@ struct Params {
   int32_t* status;
 };
 
-// Row r, 16-byte chunk c of a [rows][D] bf16 tile with the chunk index XOR-swizzled by r % 8.
+// Shared-memory row pitch of a [rows][D] bf16 tile. D = 64/128: rows of D*2 bytes with the
+// 16-byte chunk index XOR-swizzled by r % 8 (rows hold whole groups of 8 chunks). D = 96: 12
+// chunks per row do not form whole groups, so rows are padded to 13 chunks (208 bytes) instead;
+// the 8 rows one ldmatrix phase reads then start in distinct bank groups ((13 r + c) mod 8).
+template <int D>
+struct RowPitch {
+  static constexpr int BYTES = (D == 96) ? 208 : D * 2;
+  static constexpr bool XOR = (D != 96);
+};
+
 template <int D>
 __device__ __forceinline__ uint32_t swz(int r, int c) {
-  return (uint32_t)(r * D * 2 + ((c ^ (r & 7)) << 4));
+  return (uint32_t)(r * RowPitch<D>::BYTES + ((RowPitch<D>::XOR ? (c ^ (r & 7)) : c) << 4));
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
@@ -79,8 +88,9 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(Params p) {
   constexpr int NT = D / 8;    // n-tiles of the output
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* sq = smem;
-  uint8_t* sk = smem + TQ * D * 2;          // [2][TK][D]
-  uint8_t* sv = sk + 2 * TK * D * 2;        // [2][TK][D]
+  constexpr int PITCH = RowPitch<D>::BYTES;
+  uint8_t* sk = smem + TQ * PITCH;          // [2][TK][D]
+  uint8_t* sv = sk + 2 * TK * PITCH;        // [2][TK][D]
   const uint32_t sq_u = smem_u32(sq), sk_u = smem_u32(sk), sv_u = smem_u32(sv);
 
   const int4 tile = p.tiles[blockIdx.x];
@@ -111,7 +121,7 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(Params p) {
         row = (int64_t)blk * kBlock + key % kBlock;
         if (blk < 0 || row >= p.kv_rows) row = 0;
       }
-      const uint32_t off = (uint32_t)(buf * TK * D * 2) + swz<D>(r, c);
+      const uint32_t off = (uint32_t)(buf * TK * PITCH) + swz<D>(r, c);
       cp_async16(sk_u + off, kbase + row * hstride + c * 8, valid);
       cp_async16(sv_u + off, vbase + row * hstride + c * 8, valid);
     }
@@ -143,8 +153,8 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(Params p) {
     cp_commit();
     cp_wait<1>();
     __syncthreads();
-    const uint32_t kb = sk_u + (uint32_t)(buf * TK * D * 2);
-    const uint32_t vb = sv_u + (uint32_t)(buf * TK * D * 2);
+    const uint32_t kb = sk_u + (uint32_t)(buf * TK * PITCH);
+    const uint32_t vb = sv_u + (uint32_t)(buf * TK * PITCH);
 
     float s[TK / 8][4];
 #pragma unroll
@@ -250,7 +260,7 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(Params p) {
 
 template <int D>
 static int launch(const Params& p, int num_tiles, cudaStream_t st) {
-  constexpr int SMEM = TQ * D * 2 + 4 * TK * D * 2;
+  constexpr int SMEM = TQ * RowPitch<D>::BYTES + 4 * TK * RowPitch<D>::BYTES;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(prefill_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) !=
@@ -295,5 +305,6 @@ extern "C" int cdb_prefill_attention(const void* qkv, int64_t qkv_stride, int64_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (head_dim == 128) return launch<128>(p, num_tiles, st);
   if (head_dim == 64) return launch<64>(p, num_tiles, st);
+  if (head_dim == 96) return launch<96>(p, num_tiles, st);
   return CDB_ERR_UNSUPPORTED;
 }

@@ -34,6 +34,8 @@ import torch
 
 from .config import ContinuousDepthBatchingConfig
 from .kv_cache import copies_exit_kv, kv_slot_for_step
+from .huginn import HuginnShape
+from .huginn_runner import HuginnRunner
 from .ouro import OuroShape
 from .runner import OuroRunner
 
@@ -167,7 +169,9 @@ class _Item:
 class ContinuousDepthBatchingEngine:
     """Continuous depth batching over the B200 CUDA library (one engine per GPU)."""
 
-    def __init__(self, model, cdb_config: ContinuousDepthBatchingConfig, runner: OuroRunner, shape: OuroShape):
+    def __init__(
+        self, model, cdb_config: ContinuousDepthBatchingConfig, runner: OuroRunner, shape: OuroShape | HuginnShape
+    ):
         self.model = model
         self.cdb_config = cdb_config
         self.runner = runner
@@ -190,10 +194,12 @@ class ContinuousDepthBatchingEngine:
         device: torch.device | str | None = None,
         gemm_backend: str = "cublas",
     ) -> ContinuousDepthBatchingEngine:
-        """Build an engine for an Ouro causal LM given by its parameters (reference names).
+        """Build an engine for an Ouro or Huginn causal LM given by its parameters (reference names).
 
-        ``model`` is the reference's ``OuroForCausalLM`` or any module with its state-dict layout
-        (e.g. :class:`~.ouro.OuroForCausalLM`). Weights are packed to bf16 on ``device``
+        ``model`` is the reference's ``OuroForCausalLM`` / ``HuginnForCausalLM`` or any module with
+        its state-dict layout (e.g. :class:`~.ouro.OuroForCausalLM`,
+        :class:`~.huginn.HuginnForCausalLM`); ``config.model_type`` picks the family, as
+        ``resolve_cdb_model_adapter`` does (``model_adapter.py:105-122``). Weights are packed to bf16 on ``device``
         (default: the model's device if CUDA, else ``cuda``). ``dtype`` other than bf16 is rejected:
         the kernels compute in bf16 with fp32 accumulation.
         """
@@ -203,11 +209,18 @@ class ContinuousDepthBatchingEngine:
         if dtype not in (None, torch.bfloat16):
             raise NotImplementedError(f"the B200 kernels run bf16; got dtype={dtype}")
         config = getattr(model, "config", None)
-        if config is None or getattr(config, "model_type", None) not in ("ouro",):
-            raise TypeError(f"Continuous depth batching requires an Ouro model; got {type(model)!r}")
+        model_type = getattr(config, "model_type", None) if config is not None else None
+        if model_type not in ("ouro", "huginn"):
+            raise TypeError(f"Continuous depth batching requires an Ouro or Huginn model; got {type(model)!r}")
         cfg = cdb_config.get_resolved()
-        shape = OuroShape.from_config(config)
-        shape = OuroShape(**{**shape.__dict__, "total_ut_steps": cfg.max_recurrent_steps})
+        if model_type == "huginn":
+            hshape = HuginnShape.from_config(config)
+            shape = HuginnShape(**{**hshape.__dict__, "total_recurrent_steps": cfg.max_recurrent_steps})
+            runner_cls = HuginnRunner
+        else:
+            oshape = OuroShape.from_config(config)
+            shape = OuroShape(**{**oshape.__dict__, "total_ut_steps": cfg.max_recurrent_steps})
+            runner_cls = OuroRunner
         if shape.num_key_value_heads != shape.num_attention_heads:
             raise NotImplementedError("the paged decode kernel serves MHA (num_key_value_heads == num_attention_heads)")
         if device is None:
@@ -219,7 +232,7 @@ class ContinuousDepthBatchingEngine:
         if cfg.num_blocks is None:
             cfg.num_blocks = _auto_num_blocks(shape, cfg, device)
         state = {k: v for k, v in model.state_dict().items()}
-        runner = OuroRunner(
+        runner = runner_cls(
             shape,
             state,
             device=device,
@@ -430,7 +443,12 @@ class ContinuousDepthBatchingEngine:
 
     def _prelude(self, items: list[_Item]) -> None:
         if items:
-            self.runner.prelude([it.token for it in items], [it.req.slot for it in items], [it.hidden for it in items])
+            self.runner.prelude(
+                [it.token for it in items],
+                [it.req.slot for it in items],
+                [it.hidden for it in items],
+                positions=[it.position for it in items],
+            )
 
     def _enqueue(self, item: _Item, front: bool = False) -> None:
         self.in_flight.add(item.req.idx)
@@ -608,7 +626,7 @@ class ContinuousDepthBatchingEngine:
             )
         self.runner.recurrent(
             [it.req.slot for it in items], [it.position for it in items], [it.hidden for it in items], kv_slot,
-            self._gate_live,
+            self._gate_live, steps=[it.step for it in items],
         )
         st.recurrent_batches += 1
         st.recurrent_steps += len(items)
@@ -622,12 +640,23 @@ class ContinuousDepthBatchingEngine:
         return self._live_decisions(items)
 
     def _live_decisions(self, items: list[_Item]) -> list[bool]:
-        """Cumulative-hazard decisions (``ExitPolicy.should_exit``, ``exit_policy.py:150-169``) on device."""
+        """Live exit decisions (``ExitPolicy.should_exit``, ``exit_policy.py:150-169``).
+
+        Ouro: cumulative hazard of the gate logit on device (``cdb_exit_hazard``). Huginn: direct
+        threshold on the latent difference (``signal < exit_threshold`` once ``step + 1 >=
+        min_recurrent_steps``), read back with one synchronisation.
+        """
 
         self.last_stats.host_syncs += 1
         r = self.runner
         cfg = self.cdb_config
         n = len(items)
+        if isinstance(self.shape, HuginnShape):
+            signals = r.gate_signals(n).tolist()
+            return [
+                it.step + 1 >= cfg.min_recurrent_steps and sig < float(cfg.exit_threshold)
+                for it, sig in zip(items, signals, strict=True)
+            ]
         meta = r.upload([[it.hidden for it in items], [it.step for it in items], [int(it.step == 0) for it in items]])
         meta = meta.view(3, n)
         if not hasattr(self, "_hz"):
@@ -671,11 +700,12 @@ class ContinuousDepthBatchingEngine:
         by_step: dict[int, list[_Item]] = {}
         for it, step in backlog:
             by_step.setdefault(step, []).append(it)
-        bs, L = self.cdb_config.block_size, self.shape.num_hidden_layers
+        bs, L = self.cdb_config.block_size, self.runner.num_core_layers
+        layer_of = self.runner.core_cache_layer
         for step, items in sorted(by_step.items()):
             rows = [self.pool.tables[it.req.idx][it.position // bs] * bs + it.position % bs for it in items]
             src = self._slot_of_step(step)
-            pairs = [(src * L + l, t * L + l) for l in range(L) for t in range(src + 1, self.slots)]
+            pairs = [(layer_of(src, l), layer_of(t, l)) for l in range(L) for t in range(src + 1, self.slots)]
             self.runner.exit_kv_copy(rows, pairs)
             self.last_stats.exit_kv_copies += len(rows)
 
@@ -688,6 +718,7 @@ class ContinuousDepthBatchingEngine:
             [it.req.log_base + it.req.generated for it in items],
             [it.req.slot for it in items],
             keep_logits=self.keep_logits,
+            positions=[it.position for it in items],
         )
         if logits is not None:
             self.lm_logits.append(("coda", logits))
@@ -920,17 +951,24 @@ class ContinuousDepthBatchingEngine:
                     )
 
 
-def _auto_num_blocks(shape: OuroShape, cfg: ContinuousDepthBatchingConfig, device: torch.device) -> int:
+def _auto_num_blocks(shape: OuroShape | HuginnShape, cfg: ContinuousDepthBatchingConfig, device: torch.device) -> int:
     """Fill the post-load budget (``kv_cache_sizing.py:34-80``; default static fraction 0.8)."""
 
     free, total = torch.cuda.mem_get_info(device)
     frac = 0.8 if cfg.mem_fraction_static is None else cfg.mem_fraction_static
-    # Reserve room for the packed weights, the work buffers and the logits the runner allocates.
-    weights = 2 * (shape.param_count_recurrent() + 2 * shape.vocab_size * shape.hidden_size)
-    work = 2 * cfg.max_num_batched_tokens * (4 * shape.hidden_size + 3 * shape.intermediate_size + 3 * shape.hidden_size)
-    budget = int(free - total * (1 - frac)) - weights - work
     assert cfg.kv_slots_per_layer is not None
-    per_block = 2 * cfg.kv_slots_per_layer * shape.num_hidden_layers * cfg.block_size * shape.num_key_value_heads * shape.head_dim * 2
+    h, i = shape.hidden_size, shape.intermediate_size
+    # Reserve room for the packed weights, the work buffers and the logits the runner allocates.
+    if isinstance(shape, HuginnShape):
+        extra = shape.n_layers_in_prelude + shape.n_layers_in_coda
+        weights = 2 * (shape.param_count_core_step() + extra * (4 * h * h + 3 * h * i) + shape.vocab_size * h)
+        cache_layers = extra + cfg.kv_slots_per_layer * shape.n_layers_in_recurrent_block
+    else:
+        weights = 2 * (shape.param_count_recurrent() + 2 * shape.vocab_size * h)
+        cache_layers = cfg.kv_slots_per_layer * shape.num_hidden_layers
+    work = 2 * cfg.max_num_batched_tokens * (9 * h + 3 * i)
+    budget = int(free - total * (1 - frac)) - weights - work
+    per_block = 2 * cache_layers * cfg.block_size * shape.num_key_value_heads * shape.head_dim * 2
     blocks = budget // per_block - 2
     if blocks <= 0:
         raise ValueError("No usable KV blocks fit in device memory")

@@ -85,7 +85,7 @@ def run_attention(args) -> dict:
     hg = 5 if dim == 96 else 4
     scratch_items = args.scratch_items
     cap = max(scratch_items * (heads // hg) * 64, args.rows * (heads // hg))
-    hdr = torch.zeros(4, dtype=torch.int32, device=dev)
+    hdr = torch.zeros(_lib.ATTN_PLAN_HEADER_INTS, dtype=torch.int32, device=dev)
     units = torch.zeros(cap, 4, dtype=torch.int32, device=dev)
     part_o = torch.zeros(scratch_items * heads * 64 * dim, device=dev)
     part_ml = torch.zeros(scratch_items * heads * 64 * 2, device=dev)
@@ -102,7 +102,7 @@ def run_attention(args) -> dict:
         _lib.call(
             "cdb_paged_decode_attn_append", _lib.ptr(qkv), qkv.stride(0), hd, 2 * hd, _lib.ptr(out), out.stride(0),
             _lib.ptr(kv), 1, kv_rows, 0, _lib.ptr(table), table.stride(0), _lib.ptr(slots), _lib.ptr(pos_d), 0,
-            None, None, 0, _lib.ptr(hdr), _lib.ptr(units), _lib.ptr(part_o), _lib.ptr(part_ml), _lib.ptr(counters),
+            None, None, None, 0, _lib.ptr(hdr), _lib.ptr(units), _lib.ptr(part_o), _lib.ptr(part_ml), _lib.ptr(counters),
             scratch_items, args.rows, heads, dim, BLOCK, dim**-0.5, args.ctas, _lib.ptr(status), sp,
         )
 
@@ -118,7 +118,7 @@ def run_attention(args) -> dict:
         "rows": args.rows,
         "mean_context": float(ctx.float().mean()),
         "kv_pool_bytes": kv.numel() * 2,
-        "plan": [int(x) for x in hdr.tolist()],
+        "plan": [int(x) for x in hdr[:4].tolist()],
         "launch_us": round(ms * 1e3, 2),
         "algorithmic_bytes": algo,
         "achieved_gbs": round(algo / (ms * 1e-3) / 1e9, 1),

@@ -150,6 +150,9 @@ class RunnerStats:
 class OuroRunner:
     """Owns the device side of one engine replica (one GPU)."""
 
+    #: int32 rows of a recurrent launch's metadata block (resident slot, position, bank slot)
+    meta_rows = 3
+
     def __init__(
         self,
         shape: OuroShape,
@@ -166,48 +169,28 @@ class OuroRunner:
         use_cuda_graph: bool = True,
         gemm_backend: str = "tcgen05",
     ) -> None:
-        if device.type != "cuda":
-            raise RuntimeError("the B200 CDB runner needs a CUDA device; there is no CPU path")
-        _lib.load()
-        # cuBLAS may otherwise reduce split-K partial sums of bf16 GEMMs in bf16; keep fp32.
-        torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
-        self.shape = shape
-        self.device = device
-        self.kv_policy = kv_policy
-        self.slots = kv_slots_per_layer
-        self.block_size = block_size
-        self.max_num_seqs = max_num_seqs
-        self.use_cuda_graph = use_cuda_graph
-        self.w = PackedOuroWeights.from_state_dict(shape, state_dict, device, gu_interleaved=gemm_backend == "tcgen05")
-        L = shape.num_hidden_layers
-        self.pool = PagedKVPool(
-            num_cache_layers=self.slots * L,
+        self._init_device(
+            shape,
+            device=device,
+            kv_policy=kv_policy,
+            kv_slots_per_layer=kv_slots_per_layer,
+            num_cache_layers=kv_slots_per_layer * shape.num_hidden_layers,
             num_blocks=num_blocks,
             block_size=block_size,
-            num_kv_heads=shape.num_key_value_heads,
-            head_dim=shape.head_dim,
             max_model_len=max_model_len,
-            resident_slots=max_num_seqs,
-            device=device,
+            max_num_seqs=max_num_seqs,
+            max_num_batched_tokens=max_num_batched_tokens,
+            use_cuda_graph=use_cuda_graph,
+            gemm_backend=gemm_backend,
         )
-        self.stream = torch.cuda.Stream(device=device)
-        self.uploader = Uploader(device)
-        self.num_sms = torch.cuda.get_device_properties(device).multi_processor_count
-        if gemm_backend not in ("tcgen05", "cublas"):
-            raise ValueError(f"gemm_backend must be 'tcgen05' or 'cublas', got {gemm_backend!r}")
-        self.gemm_backend = gemm_backend
-        # split-K scratch of the tcgen05 GEMM (L2-resident partials; counters stay zeroed)
-        self.gemm_ws = torch.zeros(32 << 20, dtype=torch.float32, device=device)
-        self.gemm_ctr = torch.zeros(1 << 14, dtype=torch.int32, device=device)
-        self.attn_ctas = 2 * self.num_sms
+        self.w = PackedOuroWeights.from_state_dict(shape, state_dict, device, gu_interleaved=gemm_backend == "tcgen05")
         H, D = shape.hidden_size, shape.head_dim
         Hq = shape.num_attention_heads * D
         Hk = shape.num_key_value_heads * D
         self.qkv_width = Hq + 2 * Hk
         self.k_col, self.v_col = Hq, Hq + Hk
         I = shape.intermediate_size
-        rows = max(max_num_seqs, max_num_batched_tokens)
-        self.rows = rows
+        rows = self.rows
         bf = dict(dtype=torch.bfloat16, device=device)
         self.xw = torch.zeros(rows, H, **bf)
         self.h = torch.zeros(rows, H, **bf)
@@ -220,20 +203,8 @@ class OuroRunner:
         self.gate_out = torch.zeros(max_num_seqs, **bf)
         self.bank_slots = 2 * max_num_seqs + 8
         self.bank = torch.zeros(self.bank_slots, H, **bf)
-        self.token_table = torch.zeros(max_num_seqs, dtype=torch.int32, device=device)
-        self.token_log = torch.zeros(1, dtype=torch.int64, device=device)
-        self.status = torch.zeros(1, dtype=torch.int32, device=device)
         self.logits = torch.zeros(max_num_seqs, shape.vocab_size, **bf)
         self.lm_in = torch.zeros(max_num_seqs, shape.hidden_size, **bf)  # gathered LM-head input rows
-        # attention plan + split-combine scratch
-        nh = shape.num_attention_heads
-        hg = 5 if D == 96 else 4
-        self.unit_capacity = max(SCRATCH_ITEMS * (nh // hg) * 64, rows * (nh // hg))
-        self.plan_hdr = torch.zeros(4, dtype=torch.int32, device=device)
-        self.units = torch.zeros(self.unit_capacity, 4, dtype=torch.int32, device=device)
-        self.part_o = torch.zeros(SCRATCH_ITEMS * nh * 64 * D, dtype=torch.float32, device=device)
-        self.part_ml = torch.zeros(SCRATCH_ITEMS * nh * 64 * 2, dtype=torch.float32, device=device)
-        self.counters = torch.zeros(SCRATCH_ITEMS * nh, dtype=torch.int32, device=device)
         # RoPE tables: fp32 inv_freq x position, cos/sin in fp32, cast to bf16 (modeling_ouro.py:560-573)
         max_pos = max_model_len + 1
         inv = 1.0 / (shape.rope_theta ** (torch.arange(0, D, 2, dtype=torch.int64).to(torch.float32) / D))
@@ -241,11 +212,88 @@ class OuroRunner:
         emb = torch.cat((freqs, freqs), dim=-1)
         self.rope_cos = emb.cos().to(torch.bfloat16).contiguous()
         self.rope_sin = emb.sin().to(torch.bfloat16).contiguous()
+
+    def _init_device(
+        self,
+        shape,
+        *,
+        device: torch.device,
+        kv_policy: str,
+        kv_slots_per_layer: int,
+        num_cache_layers: int,
+        num_blocks: int,
+        block_size: int,
+        max_model_len: int,
+        max_num_seqs: int,
+        max_num_batched_tokens: int,
+        use_cuda_graph: bool,
+        gemm_backend: str,
+    ) -> None:
+        """Model-independent device state: KV pool, stream, uploads, attention scratch, graphs."""
+
+        if device.type != "cuda":
+            raise RuntimeError("the B200 CDB runner needs a CUDA device; there is no CPU path")
+        _lib.load()
+        # cuBLAS may otherwise reduce split-K partial sums of bf16 GEMMs in bf16; keep fp32.
+        torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+        if gemm_backend not in ("tcgen05", "cublas"):
+            raise ValueError(f"gemm_backend must be 'tcgen05' or 'cublas', got {gemm_backend!r}")
+        self.shape = shape
+        self.device = device
+        self.kv_policy = kv_policy
+        self.slots = kv_slots_per_layer
+        self.block_size = block_size
+        self.max_num_seqs = max_num_seqs
+        self.use_cuda_graph = use_cuda_graph
+        self.gemm_backend = gemm_backend
+        self.pool = PagedKVPool(
+            num_cache_layers=num_cache_layers,
+            num_blocks=num_blocks,
+            block_size=block_size,
+            num_kv_heads=shape.num_key_value_heads,
+            head_dim=shape.head_dim,
+            max_model_len=max_model_len,
+            resident_slots=max_num_seqs,
+            device=device,
+        )
+        self.stream = torch.cuda.Stream(device=device)
+        self.uploader = Uploader(device)
+        self.num_sms = torch.cuda.get_device_properties(device).multi_processor_count
+        # kept for cdb_gemm_bf16's (unused) workspace arguments
+        self.gemm_ws = torch.zeros(1, dtype=torch.float32, device=device)
+        self.gemm_ctr = torch.zeros(1, dtype=torch.int32, device=device)
+        self.attn_ctas = 2 * self.num_sms
+        D = shape.head_dim
+        self.rows = max(max_num_seqs, max_num_batched_tokens)
+        self.token_table = torch.zeros(max_num_seqs, dtype=torch.int32, device=device)
+        self.token_log = torch.zeros(1, dtype=torch.int64, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        # attention plan + split-combine scratch
+        nh = shape.num_attention_heads
+        hg = 5 if D == 96 else 4
+        self.unit_capacity = max(SCRATCH_ITEMS * (nh // hg) * 64, self.rows * (nh // hg)) + _lib.ATTN_PLAN_MAX_CHUNKS
+        self.plan_hdr = torch.zeros(_lib.ATTN_PLAN_HEADER_INTS, dtype=torch.int32, device=device)
+        self.units = torch.zeros(self.unit_capacity, 4, dtype=torch.int32, device=device)
+        self.part_o = torch.zeros(SCRATCH_ITEMS * nh * 64 * D, dtype=torch.float32, device=device)
+        self.part_ml = torch.zeros(SCRATCH_ITEMS * nh * 64 * 2, dtype=torch.float32, device=device)
+        self.counters = torch.zeros(SCRATCH_ITEMS * nh, dtype=torch.int32, device=device)
         self.scale = float(D) ** -0.5
         self.buckets = decode_graph_buckets(max_num_seqs)
         self.graphs: dict[tuple[int, int, bool], _Graph] = {}
         self.graph_pool = None
         self.stats = RunnerStats()
+
+    # ------------------------------------------------------------------ cache-layer layout
+    @property
+    def num_core_layers(self) -> int:
+        """Physical layers one recurrent step runs (the ones whose KV is replicated per slot)."""
+
+        return self.shape.num_hidden_layers
+
+    def core_cache_layer(self, slot: int, layer: int) -> int:
+        """Cache layer of a recurrent layer at a KV slot (``kv_cache_policy.py:106-128``)."""
+
+        return slot * self.shape.num_hidden_layers + layer
 
     # ------------------------------------------------------------------ small helpers
     def reset(self, log_capacity: int) -> None:
@@ -299,7 +347,7 @@ class OuroRunner:
             _lib.ptr(self.attn), self.attn.stride(0),
             _lib.ptr(pool.kv), pool.num_cache_layers, pool.rows, cache_layer,
             _lib.ptr(pool.block_table), pool.block_table.stride(0), _lib.ptr(item_slot), _lib.ptr(item_pos),
-            rope_mode, _lib.ptr(self.rope_cos), _lib.ptr(self.rope_sin), append,
+            rope_mode, _lib.ptr(self.rope_cos), _lib.ptr(self.rope_sin), None, append,
             _lib.ptr(self.plan_hdr), _lib.ptr(self.units), _lib.ptr(self.part_o), _lib.ptr(self.part_ml),
             _lib.ptr(self.counters), SCRATCH_ITEMS, n, s.num_attention_heads, s.head_dim, self.block_size,
             self.scale, self.attn_ctas, _lib.ptr(self.status), self._sp(),
@@ -351,7 +399,7 @@ class OuroRunner:
                     "cdb_rope_append_kv", _lib.ptr(self.qkv), self.qkv.stride(0), self.k_col, self.v_col,
                     _lib.ptr(self.pool.kv), self.pool.num_cache_layers, self.pool.rows, base_layer + l,
                     _lib.ptr(self.pool.block_table), self.pool.block_table.stride(0), _lib.ptr(item_slot),
-                    _lib.ptr(item_pos), 1, _lib.ptr(self.rope_cos), _lib.ptr(self.rope_sin), n,
+                    _lib.ptr(item_pos), 1, _lib.ptr(self.rope_cos), _lib.ptr(self.rope_sin), None, n,
                     s.num_attention_heads, s.head_dim, self.block_size, sp,
                 )
                 self._prefill_attention(base_layer + l)
@@ -400,13 +448,27 @@ class OuroRunner:
         self._layer_stack(n, kv_slot * s.num_hidden_layers, item_slot, item_pos, 1, self.bank, hid, gate)
 
     # ------------------------------------------------------------------ public stages
-    def recurrent(self, item_slot: list[int], item_pos: list[int], hidden: list[int], kv_slot: int, gate: bool) -> None:
+    def _recurrent_meta(self, item_slot: list[int], item_pos: list[int], hidden: list[int], steps) -> list[list[int]]:
+        """The int32 metadata rows of a recurrent launch (``meta_rows`` of them)."""
+
+        return [item_slot, item_pos, hidden]
+
+    def recurrent(
+        self,
+        item_slot: list[int],
+        item_pos: list[int],
+        hidden: list[int],
+        kv_slot: int,
+        gate: bool,
+        steps: list[int] | None = None,
+    ) -> None:
         """One mixed-depth recurrent launch over ``len(item_slot)`` rows (each at its own step)."""
 
         n = len(item_slot)
         self.flush_block_edits()
+        rows = self._recurrent_meta(item_slot, item_pos, hidden, steps)
         if not self.use_cuda_graph:
-            meta = self.upload([item_slot, item_pos, hidden]).view(3, n)
+            meta = self.upload(rows).view(self.meta_rows, n)
             with torch.cuda.stream(self.stream):
                 self._recurrent_body(meta, n, kv_slot, gate)
             return
@@ -418,20 +480,17 @@ class OuroRunner:
             self.stats.recurrent_graph_captures += 1
         else:
             self.stats.recurrent_graph_hits += 1
-        pad = bucket - n
-        meta_host = np.full((3, bucket), -1, dtype=np.int32)
-        meta_host[0, :n] = item_slot
-        meta_host[1, :n] = item_pos
-        meta_host[2, :n] = hidden
+        meta_host = np.full((self.meta_rows, bucket), -1, dtype=np.int32)
+        for i, row in enumerate(rows):
+            meta_host[i, :n] = row
         meta_host[0, n:] = 0
-        del pad
         self.uploader.upload(meta_host, self.stream, out=g.meta)
         with torch.cuda.stream(self.stream):
             g.graph.replay()
         self.stats.replayed_launches += g.launches
 
     def _capture(self, bucket: int, kv_slot: int, gate: bool) -> _Graph:
-        meta = torch.full((3, bucket), -1, dtype=torch.int32, device=self.device)
+        meta = torch.full((self.meta_rows, bucket), -1, dtype=torch.int32, device=self.device)
         meta[0].zero_()
         # Warm up on a fully padded batch (every kernel skips padding rows), then capture.
         with torch.cuda.stream(self.stream):
@@ -472,7 +531,7 @@ class OuroRunner:
         with torch.cuda.stream(self.stream):
             _lib.call(
                 "cdb_embed", _lib.ptr(self.w.embed), s.hidden_size, s.vocab_size, _lib.ptr(meta[0]), None, None,
-                _lib.ptr(self.xw), self.xw.stride(0), None, n, _lib.ptr(self.status), sp,
+                _lib.ptr(self.xw), self.xw.stride(0), None, n, 1.0, _lib.ptr(self.status), sp,
             )
             tiles = self.prefill_tiles(item_slot, item_pos)
             self._tiles = self.upload(tiles)
@@ -499,8 +558,10 @@ class OuroRunner:
                     return self.logits[:k].clone()
         return None
 
-    def prelude(self, token_ids: list[int], req_slots: list[int], hidden: list[int]) -> None:
-        """Embed each item's token into its bank slot; id -1 takes the request's device token."""
+    def prelude(self, token_ids: list[int], req_slots: list[int], hidden: list[int], positions=None) -> None:
+        """Embed each item's token into its bank slot; id -1 takes the request's device token.
+
+        ``positions`` is unused: Ouro's prelude is a lookup with no attention."""
 
         s = self.shape
         n = len(token_ids)
@@ -511,11 +572,15 @@ class OuroRunner:
             _lib.call(
                 "cdb_embed", _lib.ptr(self.w.embed), s.hidden_size, s.vocab_size, _lib.ptr(meta[0]),
                 _lib.ptr(meta[1]), _lib.ptr(self.token_table), _lib.ptr(self.bank), self.bank.stride(0),
-                _lib.ptr(meta[2]), n, _lib.ptr(self.status), self.stream.cuda_stream,
+                _lib.ptr(meta[2]), n, 1.0, _lib.ptr(self.status), self.stream.cuda_stream,
             )
 
-    def coda(self, hidden: list[int], log_rows: list[int], req_slots: list[int], keep_logits: bool = False):
-        """LM head + greedy argmax for exited tokens; ids go to the token log and token table."""
+    def coda(
+        self, hidden: list[int], log_rows: list[int], req_slots: list[int], keep_logits: bool = False, positions=None
+    ):
+        """LM head + greedy argmax for exited tokens; ids go to the token log and token table.
+
+        ``positions`` is unused: Ouro's coda is the LM head alone."""
 
         s = self.shape
         n = len(hidden)

@@ -32,6 +32,10 @@ extern "C" {
 #define CDB_ERR_INDEX 6
 #define CDB_ERR_SCRATCH_LIMIT 7 /* call exceeds the fixed static scratch of a *_static entry point */
 
+/* Attention work plan header: 4 ints + the first unit of each chunk (+ one end entry). */
+#define CDB_ATTN_PLAN_MAX_CHUNKS 1024
+#define CDB_ATTN_PLAN_HEADER_INTS (4 + CDB_ATTN_PLAN_MAX_CHUNKS + 1)
+
 /* Library version (major*10000 + minor*100 + patch). */
 int cdb_version(void);
 
@@ -48,13 +52,19 @@ const char* cdb_status_string(int status);
  * (kv_cache_policy.py:106-128).
  * ------------------------------------------------------------------------------------- */
 
-/* Split-KV work plan for one recurrent (or prefill) launch; run once, reused by every layer.
+/* Balanced split-KV work plan for one recurrent launch; run once, reused by every layer.
+ * The pages of every (row, head group) segment, rows in order and head groups inner, are cut
+ * into about 2*num_sms equal chunks (one per attention CTA); a segment crossing chunk boundaries
+ * becomes split-KV pieces that the attention kernel merges (the last warp of a (row, head)).
  *   item_pos    [num_items] int32: position of each row's query token; -1 = padding row.
- *   append      1: row p reads cached rows [0,p) and appends its own k/v (decode);
- *               0: row p reads cached rows [0,p] (its k/v already written, prefill).
- *   plan_header [4] int32 out: {num_units, blocks_per_split, max_splits, 0}.
- *   units       [unit_capacity] int4 out: {item, head_group, split, num_splits}.
- *   scratch_items: rows the split-combine scratch covers; larger launches never split.
+ *               Row p attends over cached rows [0, p].
+ *   append      accepted for compatibility, no effect (the append runs before the attention).
+ *   plan_header [CDB_ATTN_PLAN_HEADER_INTS] int32 out: {num_units, num_chunks, max_splits,
+ *               whole_segments, first unit of chunk 0 .. num_chunks}.
+ *   units       [unit_capacity] int4 out: {row, head_group << 16 | split, first_page << 16 |
+ *               end_page, num_splits}; unit_capacity >= rows * heads/heads_per_CTA + 2*num_sms.
+ *   scratch_items: rows the split-combine scratch covers; larger launches never split (whole
+ *               segments dealt round-robin).
  * Replaces the split decision inside FlashAttention-3's flash_attn_with_kvcache
  * (transformers integrations/flash_paged.py:107-118). */
 int cdb_attn_plan(const int32_t* item_pos, int num_items, int append, int num_heads, int head_dim,
@@ -70,7 +80,10 @@ int cdb_attn_plan(const int32_t* item_pos, int num_items, int append, int num_he
  *              16-byte aligned, strides and column offsets multiples of 8 elements.
  *   rope_mode  0: q/k already rotated; 1: split-half rotate_half RoPE (Ouro, bf16 tables
  *              [max_positions, head_dim]); 2: interleaved-pair RoPE in fp32 (Huginn, fp32
- *              tables [max_positions, head_dim/2]).
+ *              tables [max_positions, head_dim/2], apply_rotary_emb_complex_like
+ *              modeling_huginn.py:175-197).
+ *   qk_bias    NULL, or bf16 [2, num_heads, head_dim] (q bias, then k bias) added to q and k in
+ *              bf16 before the rotation (Huginn's learned qk_bias, modeling_huginn.py:261-264).
  *   append     1: rotate q in place in `qkv`, rotate k, write k/v at the row's position, then
  *              attend over [0,p]; 0: attend over cached rows [0,p] with q already rotated.
  *   out        bf16 [num_items, out_stride], heads concatenated.
@@ -81,8 +94,9 @@ int cdb_paged_decode_attn_append(void* qkv, int64_t qkv_stride, int64_t k_col, i
                                  void* out, int64_t out_stride, void* kv_base, int num_cache_layers,
                                  int64_t kv_rows, int cache_layer, const int32_t* block_table,
                                  int64_t block_table_stride, const int32_t* item_slot, const int32_t* item_pos,
-                                 int rope_mode, const void* rope_cos, const void* rope_sin, int append,
-                                 const int32_t* plan_header, const void* units, float* part_o, float* part_ml,
+                                 int rope_mode, const void* rope_cos, const void* rope_sin, const void* qk_bias,
+                                 int append, const int32_t* plan_header, const void* units, float* part_o,
+                                 float* part_ml,
                                  int32_t* counters, int scratch_items, int num_items, int num_heads, int head_dim,
                                  int block_size, float scale, int num_ctas, int32_t* status, void* stream);
 
@@ -92,7 +106,7 @@ int cdb_paged_decode_attn_append(void* qkv, int64_t qkv_stride, int64_t k_col, i
  * while the host framework captures a CUDA graph (allocation is not permitted during capture)
  * or a plugin that is handed tensors but no allocator.
  *   Arguments mean what they mean for cdb_paged_decode_attn_append.
- *   Scratch: one file-scope device array of 4,784,896 bytes (about 4.8 MB) per GPU, held until
+ *   Scratch: one file-scope device array of 4,788,992 bytes (about 4.8 MB) per GPU, held until
  *   the process exits.
  *   Its device address is looked up with cudaGetSymbolAddress on the first call made with that
  *   device current, so make one call per device (num_items = 0 is enough) before any stream
@@ -109,7 +123,8 @@ int cdb_paged_decode_attn_append_static(void* qkv, int64_t qkv_stride, int64_t k
                                         int64_t kv_rows, int cache_layer, const int32_t* block_table,
                                         int64_t block_table_stride, const int32_t* item_slot,
                                         const int32_t* item_pos, int rope_mode, const void* rope_cos,
-                                        const void* rope_sin, int append, int num_items, int num_heads,
+                                        const void* rope_sin, const void* qk_bias, int append, int num_items,
+                                        int num_heads,
                                         int head_dim, int block_size, float scale, int num_ctas, int32_t* status,
                                         void* stream);
 
@@ -122,7 +137,7 @@ int64_t cdb_attn_scratch_bytes(int scratch_items, int num_heads, int head_dim);
  *   tiles  int4 [num_tiles] {row_start, num_rows <= 64, resident slot, position of row_start}:
  *          consecutive rows of one request; each row attends to keys [0, its position] of that
  *          request through the block table. q must already be rotated and the chunk's k/v
- *          written (cdb_rope_append_kv). head_dim 64 or 128. */
+ *          written (cdb_rope_append_kv). head_dim 64, 96 or 128. */
 int cdb_prefill_attention(const void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col, void* out,
                           int64_t out_stride, const void* kv_base, int num_cache_layers, int64_t kv_rows,
                           int cache_layer, const int32_t* block_table, int64_t block_table_stride, const void* tiles,
@@ -135,8 +150,8 @@ int cdb_prefill_attention(const void* qkv, int64_t qkv_stride, int64_t k_col, in
 int cdb_rope_append_kv(void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col, void* kv_base,
                        int num_cache_layers, int64_t kv_rows, int cache_layer, const int32_t* block_table,
                        int64_t block_table_stride, const int32_t* item_slot, const int32_t* item_pos, int rope_mode,
-                       const void* rope_cos, const void* rope_sin, int num_items, int num_heads, int head_dim,
-                       int block_size, void* stream);
+                       const void* rope_cos, const void* rope_sin, const void* qk_bias, int num_items, int num_heads,
+                       int head_dim, int block_size, void* stream);
 
 /* bf16 tensor-core GEMM on tcgen05/TMEM: c[M,N] = x[M,K] * w[N,K]^T (fp32 accumulation, bf16
  * store). Replaces the nn.Linear projections of the shared block and the LM head
@@ -201,12 +216,32 @@ int cdb_silu_mul(const void* gu, int64_t gu_stride, void* act, int64_t act_strid
 int cdb_argmax(const void* logits, int64_t stride, int num_rows, int vocab, int64_t* out, const int32_t* out_rows,
                const int32_t* token_rows, int32_t* token_table, void* stream);
 
-/* Prelude embedding lookup (OuroCDBAdapter.prelude, adapters/ouro.py:199-212):
- * out[out_rows[r]] = table[id_r]; id_r = ids[r] if ids[r] >= 0 else token_table[id_src[r]]
- * (the on-device successor-token gather of model_runner.py:439-457). */
+/* Prelude embedding lookup (OuroCDBAdapter.prelude, adapters/ouro.py:199-212; Huginn's
+ * wte(ids) * embed_scale, modeling_huginn.py:431):
+ * out[out_rows[r]] = bf16(table[id_r] * scale); id_r = ids[r] if ids[r] >= 0 else
+ * token_table[id_src[r]] (the on-device successor-token gather of model_runner.py:439-457).
+ * scale = 1 copies the row exactly (Ouro). */
 int cdb_embed(const void* table, int hidden, int vocab, const int32_t* ids, const int32_t* id_src,
               const int32_t* token_table, void* out, int64_t out_stride, const int32_t* out_rows, int num_rows,
-              int32_t* status, void* stream);
+              float scale, int32_t* status, void* stream);
+
+/* Huginn sandwich-norm row step (HuginnBlock.forward, modeling_huginn.py:333-336; run_coda :454-460):
+ *   v = x_src[x_rows ? x_rows[r] : r];  if add: v = bf16(v + add[r]);  if w1: v = rmsnorm(v; w1);
+ *   if x_dst: x_dst[x_dst_rows ? x_dst_rows[r] : r] = v  (skipped when that index < 0);
+ *   if w2: y[r] = rmsnorm(v; w2).
+ * Every pointer but x_src may be NULL; rmsnorm is HuginnRMSNorm (fp32 normalise, bf16 cast, bf16
+ * gain multiply). A row whose x_rows entry is < 0 is skipped. hidden % 8 == 0, <= 12288. */
+int cdb_sandwich_norm(const void* x_src, int64_t x_src_stride, const int32_t* x_rows, const void* add,
+                      int64_t add_stride, const void* w1, void* x_dst, int64_t x_dst_stride,
+                      const int32_t* x_dst_rows, const void* w2, void* y, int64_t y_stride, int num_rows, int hidden,
+                      float eps, void* stream);
+
+/* Huginn exit signal (latent_diff, models/huginn/exit_gates.py:33-40, as HuginnCDBAdapter.exit_signal
+ * computes it in bf16, adapters/huginn.py:171-175): out[r] = bf16(bf16(||bf16(new-old)||) /
+ * max(bf16(||new||), 1e-9)) with new = new_state[rows[r]] (row r when rows is NULL) and
+ * old = old_state[r]; rows[r] < 0 skips row r. */
+int cdb_latent_diff(const void* new_state, int64_t new_stride, const void* old_state, int64_t old_stride,
+                    const int32_t* rows, int num_rows, int hidden, void* out, void* stream);
 
 /* Apply n block-table edits {row, column, block_id} (int32 triples) to a device block table
  * [rows, stride]. The device mirror of FullAttentionCacheAllocator.allocate_blocks /

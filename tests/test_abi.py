@@ -24,6 +24,43 @@ def test_header_and_binding_agree():
     assert declared_symbols() == sorted(_lib.exported_symbols())
 
 
+def test_plan_header_size_matches_binding():
+    text = (ROOT / "include" / "cdb_b200.h").read_text()
+    chunks = int(re.search(r"#define CDB_ATTN_PLAN_MAX_CHUNKS (\d+)", text).group(1))
+    assert chunks == _lib.ATTN_PLAN_MAX_CHUNKS
+    assert "#define CDB_ATTN_PLAN_HEADER_INTS (4 + CDB_ATTN_PLAN_MAX_CHUNKS + 1)" in text
+    assert _lib.ATTN_PLAN_HEADER_INTS == 4 + chunks + 1
+
+
+def _param_kind(decl: str) -> str:
+    decl = decl.strip()
+    if "*" in decl:
+        return "ptr"
+    for kind in ("int64_t", "double", "float", "int"):
+        if re.search(rf"\b{kind}\b", decl):
+            return kind
+    raise AssertionError(f"unrecognised parameter {decl!r}")
+
+
+def test_binding_argument_kinds_match_header_prototypes():
+    """Each ctypes argtype has the kind (pointer / int / int64 / float / double) of the header
+    parameter in the same position, so a binding cannot shift or retype an argument."""
+
+    import ctypes
+
+    text = (ROOT / "include" / "cdb_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    kinds = {ctypes.c_void_p: "ptr", ctypes.c_int: "int", ctypes.c_int64: "int64_t", ctypes.c_float: "float",
+             ctypes.c_double: "double"}
+    protos = re.findall(r"\b(cdb_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text)
+    assert len(protos) == len(_lib.exported_symbols())
+    for name, params in protos:
+        params = params.strip()
+        header = [] if params in ("", "void") else [_param_kind(p) for p in params.split(",")]
+        binding = [kinds[t] for t in _lib._SIGNATURES[name]]
+        assert header == binding, (name, header, binding)
+
+
 def test_library_loads_and_exports_every_symbol():
     lib = _lib.load()
     for name in declared_symbols():

@@ -43,7 +43,7 @@ class AttnHarness:
         self.kv = torch.randn(layers, 2, self.rows, heads, d, device=DEV).to(torch.bfloat16)
         self.hg = 5 if d == 96 else 4
         self.cap = max(scratch * (heads // self.hg) * 64, n_items * (heads // self.hg))
-        self.hdr = torch.zeros(4, dtype=torch.int32, device=DEV)
+        self.hdr = torch.zeros(_lib.ATTN_PLAN_HEADER_INTS, dtype=torch.int32, device=DEV)
         self.units = torch.zeros(self.cap, 4, dtype=torch.int32, device=DEV)
         self.part_o = torch.zeros(scratch * heads * 64 * d, device=DEV)
         self.part_ml = torch.zeros(scratch * heads * 64 * 2, device=DEV)
@@ -52,7 +52,7 @@ class AttnHarness:
         self.scratch = scratch
         self.num_blocks = num_blocks
 
-    def run(self, qkv, out, layer, block_table, item_slot, item_pos, append, rope_mode, cos, sin):
+    def run(self, qkv, out, layer, block_table, item_slot, item_pos, append, rope_mode, cos, sin, qk_bias=None):
         n = item_pos.numel()
         sp = torch.cuda.current_stream().cuda_stream
         _lib.call(
@@ -63,7 +63,7 @@ class AttnHarness:
         _lib.call(
             "cdb_paged_decode_attn_append", _lib.ptr(qkv), qkv.stride(0), hd, 2 * hd, _lib.ptr(out), out.stride(0),
             _lib.ptr(self.kv), self.layers, self.rows, layer, _lib.ptr(block_table), block_table.stride(0),
-            _lib.ptr(item_slot), _lib.ptr(item_pos), rope_mode, _lib.ptr(cos), _lib.ptr(sin), append,
+            _lib.ptr(item_slot), _lib.ptr(item_pos), rope_mode, _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(qk_bias), append,
             _lib.ptr(self.hdr), _lib.ptr(self.units), _lib.ptr(self.part_o), _lib.ptr(self.part_ml),
             _lib.ptr(self.counters), self.scratch, n, self.h, self.d, BS, self.d**-0.5, 296, _lib.ptr(self.status), sp,
         )
@@ -267,12 +267,20 @@ def test_embed_gathers_host_and_device_ids():
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
     _lib.call(
         "cdb_embed", _lib.ptr(table), hidden, vocab, _lib.ptr(ids), _lib.ptr(src), _lib.ptr(tok), _lib.ptr(out), hidden,
-        _lib.ptr(rows), n, _lib.ptr(status), torch.cuda.current_stream().cuda_stream,
+        _lib.ptr(rows), n, 1.0, _lib.ptr(status), torch.cuda.current_stream().cuda_stream,
     )
     torch.cuda.synchronize()
     want = torch.where(ids >= 0, ids, tok).long()
     assert torch.equal(out[::2], table[want])
     assert int(status.item()) == 0
+    # Huginn's scaled embedding: bf16(table[id] * sqrt(n_embd)), one rounding (torch's bf16 * float)
+    scale = math.sqrt(5280)
+    _lib.call(
+        "cdb_embed", _lib.ptr(table), hidden, vocab, _lib.ptr(ids), _lib.ptr(src), _lib.ptr(tok), _lib.ptr(out), hidden,
+        _lib.ptr(rows), n, scale, _lib.ptr(status), torch.cuda.current_stream().cuda_stream,
+    )
+    torch.cuda.synchronize()
+    assert torch.equal(out[::2], table[want] * scale)
 
 
 def test_block_table_edits_and_exit_copy():
@@ -318,7 +326,7 @@ def test_exit_hazard_matches_host_policy():
         assert bool(flags[i]) == want
 
 
-@pytest.mark.parametrize("heads,d", [(16, 128), (4, 64)])
+@pytest.mark.parametrize("heads,d", [(16, 128), (4, 64), (5, 96)])
 def test_prefill_attention_tiles_match_fp32(heads, d):
     """Tiled causal prefill attention == per-row fp32 attention over [0, position]."""
 
@@ -370,3 +378,104 @@ def test_gather_rows_exact(hidden):
             assert dst[i].abs().sum().item() == 0
         else:
             assert torch.equal(dst[i], src[r])
+
+
+# ----------------------------------------------------------------------------- Huginn kernels
+def _huginn_rotate(x, cos, sin):
+    """apply_rotary_emb_complex_like (modeling_huginn.py:175-197) on [T, H, D] bf16."""
+
+    x2 = x.unflatten(-1, (-1, 2)).float()
+    c, s_ = cos[:, None, :], sin[:, None, :]
+    return torch.stack([x2[..., 0] * c - x2[..., 1] * s_, x2[..., 1] * c + x2[..., 0] * s_], dim=-1).flatten(2).type_as(x)
+
+
+def test_huginn_rope_bias_append_exact():
+    """rope_mode 2 + qk_bias: q rotated in place and k/v appended equal the reference's op sequence
+    bit for bit (bf16 bias add, fp32 products and sums each rounded, one cast back)."""
+
+    heads, d, n = 5, 96, 7
+    gen = torch.Generator().manual_seed(5)
+    h = AttnHarness(n, heads, d, num_blocks=64)
+    table = _make_tables(n, 4, h.num_blocks, gen)
+    pos = torch.tensor([0, 3, 15, 16, 40, 17, 2], dtype=torch.int32, device=DEV)
+    slots = torch.arange(n, dtype=torch.int32, device=DEV)
+    qkv = torch.randn(n, 3 * heads * d, device=DEV).to(torch.bfloat16)
+    bias = (0.1 * torch.randn(2, heads, d, device=DEV)).to(torch.bfloat16)
+    inv = 1.0 / (50000.0 ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+    freqs = torch.arange(64, device=DEV).float().unsqueeze(-1) * inv.to(DEV)
+    cos, sin = freqs.cos().contiguous(), freqs.sin().contiguous()
+    hd = heads * d
+    q0 = qkv[:, :hd].reshape(n, heads, d).clone()
+    k0 = qkv[:, hd : 2 * hd].reshape(n, heads, d).clone()
+    v0 = qkv[:, 2 * hd :].reshape(n, heads, d).clone()
+    p = pos.long()
+    q_ref = _huginn_rotate((q0 + bias[0]).to(torch.bfloat16), cos[p], sin[p])
+    k_ref = _huginn_rotate((k0 + bias[1]).to(torch.bfloat16), cos[p], sin[p])
+    out = torch.zeros(n, hd, device=DEV, dtype=torch.bfloat16)
+    h.run(qkv, out, 1, table, slots, pos, 1, 2, cos, sin, qk_bias=bias)
+    assert torch.equal(qkv[:, :hd].reshape(n, heads, d), q_ref)
+    for i in range(n):
+        pi = int(pos[i])
+        row = int(table[i, pi // BS]) * BS + pi % BS
+        assert torch.equal(h.kv[1, 0, row], k_ref[i]), i
+        assert torch.equal(h.kv[1, 1, row], v0[i]), i
+    # the attention output over the cache (now holding the appended rows) against fp32
+    ref, _ = _reference_decode(h, qkv, h.kv, 1, table, slots, pos, cos, sin, append=0)
+    assert (out.float() - ref).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("hidden", [480, 5280])
+def test_sandwich_norm_matches_torch(hidden):
+    n, eps = 9, 1e-6
+    x = (4 * torch.randn(12, hidden, device=DEV)).to(torch.bfloat16)
+    a = torch.randn(n, hidden, device=DEV).to(torch.bfloat16)
+    w1 = (1 + 0.1 * torch.randn(hidden, device=DEV)).to(torch.bfloat16)
+    w2 = (1 + 0.1 * torch.randn(hidden, device=DEV)).to(torch.bfloat16)
+    rows = torch.tensor([3, 0, -1, 11, 5, 6, 7, 8, 2], dtype=torch.int32, device=DEV)
+    drows = torch.tensor([1, -1, 0, 2, 3, 4, 5, 6, 7], dtype=torch.int32, device=DEV)
+    xd = torch.zeros(8, hidden, device=DEV, dtype=torch.bfloat16)
+    y = torch.zeros(n, hidden, device=DEV, dtype=torch.bfloat16)
+    _lib.call(
+        "cdb_sandwich_norm", _lib.ptr(x), x.stride(0), _lib.ptr(rows), _lib.ptr(a), a.stride(0), _lib.ptr(w1),
+        _lib.ptr(xd), xd.stride(0), _lib.ptr(drows), _lib.ptr(w2), _lib.ptr(y), y.stride(0), n, hidden, eps,
+        torch.cuda.current_stream().cuda_stream,
+    )
+    torch.cuda.synchronize()
+    for r in range(n):
+        src, dst = int(rows[r]), int(drows[r])
+        if src < 0:
+            continue
+        v = _torch_rmsnorm(a[r] + x[src], w1, eps)  # norm_2(attn + x)
+        yr = _torch_rmsnorm(v, w2, eps)  # norm_3(x)
+        if dst >= 0:
+            assert (xd[dst].float() - v.float()).abs().max().item() <= 2**-7 * v.float().abs().max().item()
+        assert (y[r].float() - yr.float()).abs().max().item() <= 2**-7 * yr.float().abs().max().item()
+    # no add, no first norm: a pure gather + norm (coda entry is ln_f of the gathered state)
+    y2 = torch.zeros_like(y)
+    _lib.call(
+        "cdb_sandwich_norm", _lib.ptr(x), x.stride(0), _lib.ptr(rows), None, 0, None, None, 0, None, _lib.ptr(w2),
+        _lib.ptr(y2), y2.stride(0), n, hidden, eps, torch.cuda.current_stream().cuda_stream,
+    )
+    torch.cuda.synchronize()
+    r = 0
+    ref = _torch_rmsnorm(x[int(rows[r])], w2, eps)
+    assert (y2[r].float() - ref.float()).abs().max().item() <= 2**-7 * ref.float().abs().max().item()
+
+
+def test_latent_diff_matches_torch():
+    n, hidden = 11, 5280
+    new = torch.randn(n, hidden, device=DEV).to(torch.bfloat16)
+    old = (new.float() + 0.3 * torch.randn(n, hidden, device=DEV)).to(torch.bfloat16)
+    old[3] = new[3]  # converged row: exactly zero
+    rows = torch.arange(n, dtype=torch.int32, device=DEV)
+    rows[5] = -1
+    out = torch.full((n,), 7.0, device=DEV, dtype=torch.bfloat16)
+    _lib.call(
+        "cdb_latent_diff", _lib.ptr(new), new.stride(0), _lib.ptr(old), old.stride(0), _lib.ptr(rows), n, hidden,
+        _lib.ptr(out), torch.cuda.current_stream().cuda_stream,
+    )
+    torch.cuda.synchronize()
+    ref = ((new - old).norm(dim=-1) / new.norm(dim=-1).clamp_min(1e-9)).to(torch.bfloat16)
+    keep = rows >= 0
+    assert ((out.float() - ref.float()).abs()[keep] <= 2**-7 * ref.float().abs()[keep]).all()
+    assert float(out[3]) == 0.0 and float(out[5]) == 7.0

@@ -49,6 +49,8 @@ class Case:
         self.qkv = torch.randn(n_items, 3 * heads * d, generator=gen).to(torch.bfloat16).to(DEV)
         self.cos, self.sin = _rope_tables(max_pos + 1, d)
         self.rope_mode = 1 if d != 96 else 0
+        # the 96-wide (Huginn) case also exercises the q/k bias
+        self.qk_bias = (0.1 * torch.randn(2, heads, d, generator=gen)).to(torch.bfloat16).to(DEV) if d == 96 else None
         self.n = n_items
 
 
@@ -57,7 +59,7 @@ def _run_scratch(c: Case, qkv, kv, out, layer, append, status, stream):
     hg = 5 if c.d == 96 else 4
     scratch_items = max(1, 128 // c.h)
     cap = max(scratch_items * (c.h // hg) * 64, c.n * (c.h // hg))
-    hdr = torch.zeros(4, dtype=torch.int32, device=DEV)
+    hdr = torch.zeros(_lib.ATTN_PLAN_HEADER_INTS, dtype=torch.int32, device=DEV)
     units = torch.zeros(cap, 4, dtype=torch.int32, device=DEV)
     part_o = torch.zeros(scratch_items * c.h * 64 * c.d, device=DEV)
     part_ml = torch.zeros(scratch_items * c.h * 64 * 2, device=DEV)
@@ -70,7 +72,8 @@ def _run_scratch(c: Case, qkv, kv, out, layer, append, status, stream):
     _lib.call(
         "cdb_paged_decode_attn_append", _lib.ptr(qkv), qkv.stride(0), hd, 2 * hd, _lib.ptr(out), out.stride(0),
         _lib.ptr(kv), c.layers, c.rows, layer, _lib.ptr(c.table), c.table.stride(0), _lib.ptr(c.slots),
-        _lib.ptr(c.pos), c.rope_mode, _lib.ptr(c.cos), _lib.ptr(c.sin), append, _lib.ptr(hdr), _lib.ptr(units),
+        _lib.ptr(c.pos), c.rope_mode, _lib.ptr(c.cos), _lib.ptr(c.sin), _lib.ptr(c.qk_bias), append, _lib.ptr(hdr),
+        _lib.ptr(units),
         _lib.ptr(part_o), _lib.ptr(part_ml), _lib.ptr(counters), scratch_items, c.n, c.h, c.d, BS, c.d**-0.5, 296,
         _lib.ptr(status), stream,
     )
@@ -82,7 +85,8 @@ def _static_args(c: Case, qkv, kv, out, layer, append, n, status, stream):
     return (
         _lib.ptr(qkv), qkv.stride(0), hd, 2 * hd, _lib.ptr(out), out.stride(0), _lib.ptr(kv), c.layers, c.rows,
         layer, _lib.ptr(c.table), c.table.stride(0), _lib.ptr(c.slots), _lib.ptr(c.pos), c.rope_mode,
-        _lib.ptr(c.cos), _lib.ptr(c.sin), append, n, c.h, c.d, BS, c.d**-0.5, 296, _lib.ptr(status), stream,
+        _lib.ptr(c.cos), _lib.ptr(c.sin), _lib.ptr(c.qk_bias), append, n, c.h, c.d, BS, c.d**-0.5, 296,
+        _lib.ptr(status), stream,
     )
 
 
