@@ -168,10 +168,10 @@ def build_engine(args, device):
 
 # DRAM bytes per algorithmic byte of decode_attn_kernel<128,4>, from one ncu capture of a launch
 # of 128 rows x ~1055-token contexts (kernel_bench attention --rows 128 --context 1024):
-# dram__bytes_read.sum 1.117004 GB + dram__bytes_write.sum 9.95 MB over 1,107,100,888 algorithmic
+# dram__bytes_read.sum 1.116279 GB + dram__bytes_write.sum 4.74 MB over 1,107,100,888 algorithmic
 # bytes. Traffic grows with the pages a launch streams, so a bench launch's traffic is its
 # algorithmic bytes times this ratio.
-ATTN_TRAFFIC_PER_ALGO_BYTE = (1.117004e9 + 9.953536e6) / 1107100888
+ATTN_TRAFFIC_PER_ALGO_BYTE = (1.116279e9 + 4.741632e6) / 1107100888
 
 
 def attention_roofline(eng, shape, launches: list[tuple[list[int], list[int]]], peak_gbs: float) -> dict:
@@ -218,7 +218,7 @@ def attention_roofline(eng, shape, launches: list[tuple[list[int], list[int]]], 
         "unit": "GB/s",
         "frac": round(achieved / peak_gbs, 4),
         "traffic": int(per_launch_bytes * ATTN_TRAFFIC_PER_ALGO_BYTE),
-        "traffic_source": "ncu dram bytes of a 128-row x 1055-token launch scaled by algorithmic bytes (ratio 1.018)",
+        "traffic_source": "ncu dram bytes of a 128-row x 1055-token launch scaled by algorithmic bytes (ratio 1.013)",
         "kernel": f"cdb::decode_attn_kernel<{D},{5 if D == 96 else 4}>",
         "launch_ms": round(per_launch_ms, 4),
         "algorithmic_bytes_per_launch": int(per_launch_bytes),

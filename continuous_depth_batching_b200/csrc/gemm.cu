@@ -34,6 +34,15 @@ constexpr int BK = 64;  // one 128-byte swizzle atom of bf16
 constexpr int THREADS = 192;
 constexpr int kMaxClusterSplits = 8;  // portable cluster size
 
+// Token-tile widths of at most 128 run two CTAs per SM (stage ring within ~110 KB), wider ones one
+// (ring within ~220 KB); the ring depth follows from the stage size, capped at 8.
+constexpr int ctas_per_sm_for(int bn) { return bn <= 128 ? 2 : 1; }
+constexpr int stages_for(int bn) {
+  const int stage = BM * BK * 2 + bn * BK * 2;
+  const int budget = (bn <= 128 ? 110 : 220) * 1024;
+  return budget / stage < 8 ? budget / stage : 8;
+}
+
 template <int BN, int STAGES>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
@@ -41,7 +50,8 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
-  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  // tcgen05.alloc takes a power of two >= 32 columns
+  static constexpr uint32_t TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   // kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both K-major, M=128, N=BN.
   static constexpr uint32_t IDESC =
       (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
@@ -229,7 +239,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, r);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) red[(c0 + j) * BM + q * 32 + lane] = __uint_as_float(r[j]);
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < BN) red[(c0 + j) * BM + q * 32 + lane] = __uint_as_float(r[j]);
       }
     }
   }
@@ -244,45 +255,62 @@ __global__ void __launch_bounds__(THREADS, 1)
   {
     const int ns = p.splits;
     const int rank = (int)cluster.block_rank();
-    constexpr int kVec = BM / 4;
+    constexpr int kVec = BM / 4;  // float4 per token row of the partial tile
     constexpr int kTotal = BN * kVec;
     const int per = (kTotal + ns - 1) / ns;
-    const int e_end = min((rank + 1) * per, kTotal);
+    const int e_beg = rank * per;
+    const int e_end = min(e_beg + per, kTotal);
     const int m_base = mtile * BN;
     const bool vec_store = p.vec_store;
-    for (int e = rank * per + (int)threadIdx.x; e < e_end; e += THREADS) {
-      const int m = e / kVec;
-      const int n4 = (e % kVec) * 4;
-      const int gm = m_base + m;
-      const int gn = wtile * BM + n4;
-      if (gm >= p.M || gn >= p.N) continue;
-      float4 v[kMaxClusterSplits];
+    // Element e of the tile is float4 e of every rank's partial (token e / kVec, weight rows
+    // 4 * (e % kVec) ..). Without a split the partial is this CTA's own shared memory.
+    const float4* src[kMaxClusterSplits];
 #pragma unroll
-      for (int sp = 0; sp < kMaxClusterSplits; ++sp)
-        if (sp < ns) v[sp] = *(cluster.map_shared_rank(reinterpret_cast<float4*>(red), sp) + (m * BM + n4) / 4);
-      float4 acc = v[0];
+    for (int sp = 0; sp < kMaxClusterSplits; ++sp)
+      src[sp] = ns == 1 ? reinterpret_cast<const float4*>(red)
+                        : cluster.map_shared_rank(reinterpret_cast<const float4*>(red), sp < ns ? sp : 0);
+    constexpr int U = 4;  // elements in flight per thread
+    for (int e0 = e_beg + (int)threadIdx.x; e0 < e_end; e0 += U * THREADS) {
+      float4 acc[U];
 #pragma unroll
-      for (int sp = 1; sp < kMaxClusterSplits; ++sp)
-        if (sp < ns) {
-          acc.x += v[sp].x;
-          acc.y += v[sp].y;
-          acc.z += v[sp].z;
-          acc.w += v[sp].w;
+      for (int q = 0; q < U; ++q) {
+        const int e = e0 + q * THREADS;
+        if (e < e_end) {
+          acc[q] = src[0][e];
+#pragma unroll
+          for (int sp = 1; sp < kMaxClusterSplits; ++sp)
+            if (sp < ns) {
+              const float4 t = src[sp][e];
+              acc[q].x += t.x;
+              acc[q].y += t.y;
+              acc[q].z += t.z;
+              acc[q].w += t.w;
+            }
         }
-      if constexpr (EPI == 1) {
-        // N % 4 == 0 here: (gate_j, up_j, gate_j+1, up_j+1) -> act[j], act[j+1], j = gn / 2.
-        const float g0 = round_bf16(acc.x), u0 = round_bf16(acc.y);
-        const float g1 = round_bf16(acc.z), u1 = round_bf16(acc.w);
-        const float s0 = round_bf16(g0 / (1.f + expf(-g0)));
-        const float s1 = round_bf16(g1 / (1.f + expf(-g1)));
-        *reinterpret_cast<uint32_t*>(p.c + (int64_t)gm * p.ldc + gn / 2) = pack_bf16x2(s0 * u0, s1 * u1);
-      } else {
-        __nv_bfloat16* dst = p.c + (int64_t)gm * p.ldc + gn;
-        if (vec_store && gn + 3 < p.N) {
-          *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
+      }
+#pragma unroll
+      for (int q = 0; q < U; ++q) {
+        const int e = e0 + q * THREADS;
+        if (e >= e_end) continue;
+        const int gm = m_base + e / kVec;
+        const int gn = wtile * BM + (e % kVec) * 4;
+        if (gm >= p.M || gn >= p.N) continue;
+        if constexpr (EPI == 1) {
+          // N % 4 == 0 here: (gate_j, up_j, gate_j+1, up_j+1) -> act[j], act[j+1], j = gn / 2.
+          const float g0 = round_bf16(acc[q].x), u0 = round_bf16(acc[q].y);
+          const float g1 = round_bf16(acc[q].z), u1 = round_bf16(acc[q].w);
+          const float s0 = round_bf16(g0 / (1.f + expf(-g0)));
+          const float s1 = round_bf16(g1 / (1.f + expf(-g1)));
+          *reinterpret_cast<uint32_t*>(p.c + (int64_t)gm * p.ldc + gn / 2) = pack_bf16x2(s0 * u0, s1 * u1);
         } else {
-          const float a[4] = {acc.x, acc.y, acc.z, acc.w};
-          for (int j = 0; j < 4 && gn + j < p.N; ++j) dst[j] = f_to_bf16(a[j]);
+          __nv_bfloat16* dst = p.c + (int64_t)gm * p.ldc + gn;
+          if (vec_store && gn + 3 < p.N) {
+            *reinterpret_cast<uint2*>(dst) =
+                make_uint2(pack_bf16x2(acc[q].x, acc[q].y), pack_bf16x2(acc[q].z, acc[q].w));
+          } else {
+            const float a4[4] = {acc[q].x, acc[q].y, acc[q].z, acc[q].w};
+            for (int j = 0; j < 4 && gn + j < p.N; ++j) dst[j] = f_to_bf16(a4[j]);
+          }
         }
       }
     }
@@ -375,24 +403,37 @@ static cudaLaunchConfig_t launch_config(dim3 grid, int splits, cudaStream_t st, 
   return cfg;
 }
 
-// Largest cluster size <= want that the device can schedule for this configuration (checked
-// once per size with cudaOccupancyMaxActiveClusters and remembered).
+// Split s <= want with the least estimated time. A launch of `clusters` clusters of s CTAs (one
+// cluster per output tile) runs in ceil(clusters / max_active(s)) waves, max_active from
+// cudaOccupancyMaxActiveClusters (queried once per size and remembered), and each CTA does 1/s of
+// the tile's K work: time ~ waves / s. Ties go to fewer waves (less fixed cost per wave).
 template <int BN, int STAGES, int EPI>
-static int schedulable_splits(int want) {
+static int schedulable_splits(int want, int clusters) {
   static std::mutex mu;
-  static int ok[kMaxClusterSplits + 1] = {};  // 0 unknown, 1 fits, -1 does not
+  static int max_active[kMaxClusterSplits + 1];
+  static bool known[kMaxClusterSplits + 1] = {};
   std::lock_guard<std::mutex> lock(mu);
-  for (int s = want; s > 1; --s) {
-    if (ok[s] == 0) {
+  int best = 1, best_waves = 0;
+  double best_cost = 0.0;
+  for (int s = 1; s <= want; ++s) {
+    if (!known[s]) {
       cudaLaunchAttribute attr[2];
       cudaLaunchConfig_t cfg = launch_config<BN, STAGES>(dim3(1, 1, s), s, nullptr, attr);
       int n = 0;
-      ok[s] = (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<BN, STAGES, EPI>, &cfg) == cudaSuccess && n > 0) ? 1 : -1;
+      max_active[s] = cudaOccupancyMaxActiveClusters(&n, gemm_kernel<BN, STAGES, EPI>, &cfg) == cudaSuccess ? n : 0;
       cudaGetLastError();
+      known[s] = true;
     }
-    if (ok[s] == 1) return s;
+    if (max_active[s] <= 0) continue;
+    const int waves = (clusters + max_active[s] - 1) / max_active[s];
+    const double cost = (double)waves / s;
+    if (best_waves == 0 || cost < best_cost - 1e-9 || (cost < best_cost + 1e-9 && waves < best_waves)) {
+      best = s;
+      best_waves = waves;
+      best_cost = cost;
+    }
   }
-  return 1;
+  return best;
 }
 
 template <int BN, int STAGES, int EPI>
@@ -406,7 +447,8 @@ static int launch(const CUtensorMap& mw, const CUtensorMap& mx, Params p, int ti
       return CDB_ERR_CUDA;
     attr_set = true;
   }
-  int s = schedulable_splits<BN, STAGES, EPI>(splits);
+  prefer_max_shared(reinterpret_cast<const void*>(gemm_kernel<BN, STAGES, EPI>));
+  int s = schedulable_splits<BN, STAGES, EPI>(splits, tiles_n * tiles_m);
   int kb_per = (p.num_kb + s - 1) / s;
   s = (p.num_kb + kb_per - 1) / kb_per;  // no empty split
   p.splits = s;
@@ -416,9 +458,10 @@ static int launch(const CUtensorMap& mw, const CUtensorMap& mx, Params p, int ti
   return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, STAGES, EPI>, mw, mx, p) == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
 }
 
-// Token-tile width for M token rows, and CTAs of that configuration resident per SM.
-static int tile_n_for(int M) { return M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256; }
-static int ctas_per_sm(int bn) { return bn <= 64 ? 2 : 1; }
+// Token-tile width for M token rows: M rounded up to a multiple of 16 (the UMMA N step for
+// M = 128) up to 256; wider problems tile the tokens by 256.
+static int tile_n_for(int M) { return M >= 256 ? 256 : ((max(M, 16) + 15) / 16) * 16; }
+static int ctas_per_sm(int bn) { return ctas_per_sm_for(bn); }
 
 }  // namespace gemm
 }  // namespace cdb
@@ -466,14 +509,40 @@ static int run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, 
   p.vec_store = ((reinterpret_cast<uintptr_t>(c) & 7) == 0 && ldc % 4 == 0) ? 1 : 0;
   p.status = status;
   switch (bn) {
+    case 16:
+      return launch<16, stages_for(16), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
     case 32:
-      return launch<32, 5, EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+      return launch<32, stages_for(32), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+    case 48:
+      return launch<48, stages_for(48), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
     case 64:
-      return launch<64, 4, EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+      return launch<64, stages_for(64), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+    case 80:
+      return launch<80, stages_for(80), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+    case 96:
+      return launch<96, stages_for(96), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+    case 112:
+      return launch<112, stages_for(112), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
     case 128:
-      return launch<128, 6, EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+      return launch<128, stages_for(128), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+    case 144:
+      return launch<144, stages_for(144), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+    case 160:
+      return launch<160, stages_for(160), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+    case 176:
+      return launch<176, stages_for(176), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+    case 192:
+      return launch<192, stages_for(192), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+    case 208:
+      return launch<208, stages_for(208), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+    case 224:
+      return launch<224, stages_for(224), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+    case 240:
+      return launch<240, stages_for(240), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+    case 256:
+      return launch<256, stages_for(256), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
     default:
-      return launch<256, 4, EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+      return CDB_ERR_UNSUPPORTED;
   }
 }
 
