@@ -235,7 +235,9 @@ def run_b200(args) -> None:
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+        # ranks wait for one another only at the start/end barriers and the result reduction;
+        # a rank that never arrives ends the others' collective with an error after this timeout
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     eng, shape = build_engine(args, device)
     prompts, max_new, depths = workload(replica_seed(args.seed, rank), args.requests, args.out_cap)
     stream = eng.runner.stream
