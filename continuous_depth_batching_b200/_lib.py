@@ -62,6 +62,11 @@ _SIGNATURES: dict[str, list] = {
         c_int, c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_void_p,
     ],
     "cdb_gemm_workspace_elems": [c_int, c_int, c_int, c_int],
+    "cdb_lm_head_argmax": [
+        c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_int,  # x, ldx, w, ldw, M, vocab, K
+        c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,  # out_ids, out_rows, token_rows, table, keys, done
+        c_int, c_void_p, c_void_p,  # num_sms, status, stream
+    ],
     "cdb_rmsnorm": [
         c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_float, c_void_p,
     ],

@@ -66,7 +66,23 @@ struct Params {
   int splits, kb_per_split, num_kb;  // splits == cluster size along z
   int vec_store;                     // c 8-byte aligned and ldc % 4 == 0
   int32_t* status;
+  // EPI 2 (LM head + argmax): per-token running keys, completion counter, outputs
+  unsigned long long* keys;
+  int32_t* done;
+  int total_ctas;
+  int64_t* out_ids;
+  const int32_t* out_rows;
+  const int32_t* token_rows;
+  int32_t* token_table;
 };
+
+// Orderable 64-bit key of (bf16 logit v, vocab index n): larger v wins, then the smaller index
+// (torch.argmax returns the first maximum).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)ord << 32) | (0xFFFFFFFFu - (uint32_t)n);
+}
 
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of 128 B,
 // 8-row groups 1024 B apart (SBO), sm100 descriptor version 1.
@@ -127,7 +143,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 // EPI 0: store c[m, n] = bf16(acc). EPI 1 (SwiGLU): weight rows are gate/up pairs
 // (row 2j = gate_j, row 2j+1 = up_j) and c[m, j] = bf16(bf16(silu(bf16(g))) * bf16(u)), the
-// rounding of OuroMLP's act_fn(gate_proj(x)) * up_proj(x) in bf16.
+// rounding of OuroMLP's act_fn(gate_proj(x)) * up_proj(x) in bf16. EPI 2 (LM head + greedy
+// argmax, unsplit): no logits are stored; each token's argmax over the bf16 logits of the tile's
+// vocab rows is folded into keys[m] with atomicMax, and the last CTA writes the token ids.
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, Params p) {
@@ -249,6 +267,48 @@ __global__ void __launch_bounds__(THREADS, 1)
   // paths included, so no CTA can wait on one that has left.
   cluster.sync();
 
+  if constexpr (EPI == 2) {
+    // One warp per token: the max over this tile's 128 vocab rows, then one atomic per token.
+    __shared__ int s_last;
+    const int m_base = mtile * BN;
+    for (int m = warp; m < BN && m_base + m < p.M; m += THREADS / 32) {
+      const float4 v = reinterpret_cast<const float4*>(red)[m * (BM / 4) + lane];
+      const float vals[4] = {v.x, v.y, v.z, v.w};
+      unsigned long long best = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int n = wtile * BM + lane * 4 + j;
+        if (n < p.N) {
+          const unsigned long long k = argmax_key(round_bf16(vals[j]), n);
+          best = k > best ? k : best;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+        best = t > best ? t : best;
+      }
+      if (lane == 0 && best != 0) atomicMax(p.keys + m_base + m, best);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      s_last = atomicAdd(p.done, 1) == p.total_ctas - 1;
+    }
+    __syncthreads();
+    if (s_last) {
+      // every other CTA's atomics precede its counter increment: read and reset the keys
+      __threadfence();
+      for (int m = threadIdx.x; m < p.M; m += THREADS) {
+        const unsigned long long k = atomicExch(p.keys + m, 0ull);
+        const int64_t id = (int64_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+        const int orow = p.out_rows ? p.out_rows[m] : m;
+        if (orow >= 0) p.out_ids[orow] = id;
+        if (p.token_rows != nullptr && p.token_rows[m] >= 0) p.token_table[p.token_rows[m]] = (int32_t)id;
+      }
+      if (threadIdx.x == 0) atomicExch(p.done, 0);
+    }
+  } else
   // Deterministic K-split reduction through distributed shared memory: the cluster holds the
   // tile's `splits` CTAs; rank r sums slice r of the tile over all ranks in rank order and
   // stores it as bf16 (4 consecutive weight rows = 4 consecutive output columns per thread).
@@ -453,6 +513,7 @@ static int launch(const CUtensorMap& mw, const CUtensorMap& mx, Params p, int ti
   s = (p.num_kb + kb_per - 1) / kb_per;  // no empty split
   p.splits = s;
   p.kb_per_split = kb_per;
+  p.total_ctas = tiles_n * tiles_m * s;
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = launch_config<BN, STAGES>(dim3(tiles_n, tiles_m, s), s, st, attr);
   return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, STAGES, EPI>, mw, mx, p) == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
@@ -474,7 +535,7 @@ namespace gemm {
 // Shared host path of the plain and SwiGLU GEMMs: c = epilogue(x[M,K] * w[N,K]^T).
 template <int EPI>
 static int run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int M, int N, int K,
-               int splits, int num_sms, int32_t* status, cudaStream_t st) {
+               int splits, int num_sms, int32_t* status, cudaStream_t st, const Params* epi2 = nullptr) {
   if (K % 8 != 0 || ldx % 8 != 0 || ldw % 8 != 0 || ldx < K || ldw < K) return CDB_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return CDB_ERR_INVALID_ARGUMENT;
   const int bn = tile_n_for(M);
@@ -492,6 +553,7 @@ static int run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, 
     s = min(s, max(1, num_kb / 2));
   }
   s = max(1, min(min(s, kMaxClusterSplits), num_kb));
+  if (EPI == 2) s = 1;  // the argmax epilogue reads whole (unsplit) logit tiles
   CUtensorMap mw, mx;
   int rc = matrix_map(&mw, w, N, K, ldw, BM);
   if (rc != CDB_OK) return rc;
@@ -508,6 +570,13 @@ static int run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, 
   p.num_kb = num_kb;
   p.vec_store = ((reinterpret_cast<uintptr_t>(c) & 7) == 0 && ldc % 4 == 0) ? 1 : 0;
   p.status = status;
+  p.keys = epi2 ? epi2->keys : nullptr;
+  p.done = epi2 ? epi2->done : nullptr;
+  p.total_ctas = 0;
+  p.out_ids = epi2 ? epi2->out_ids : nullptr;
+  p.out_rows = epi2 ? epi2->out_rows : nullptr;
+  p.token_rows = epi2 ? epi2->token_rows : nullptr;
+  p.token_table = epi2 ? epi2->token_table : nullptr;
   switch (bn) {
     case 16:
       return launch<16, stages_for(16), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
@@ -569,6 +638,24 @@ extern "C" int cdb_mlp_gateup_silu_gemm(const void* x, int64_t ldx, const void* 
     return CDB_ERR_INVALID_ARGUMENT;
   return cdb::gemm::run<1>(x, ldx, w_gate_up, ldw, act, ld_act, M, 2 * inter, K, splits, num_sms, status,
                            static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cdb_lm_head_argmax(const void* x, int64_t ldx, const void* w, int64_t ldw, int M, int vocab, int K,
+                                  int64_t* out_ids, const int32_t* out_rows, const int32_t* token_rows,
+                                  int32_t* token_table, uint64_t* keys, int32_t* done, int num_sms,
+                                  int32_t* status, void* stream) {
+  if (M <= 0 || vocab <= 0 || K <= 0) return M == 0 ? CDB_OK : CDB_ERR_INVALID_ARGUMENT;
+  if (out_ids == nullptr || keys == nullptr || done == nullptr || (token_rows != nullptr && token_table == nullptr))
+    return CDB_ERR_INVALID_ARGUMENT;
+  cdb::gemm::Params e;
+  e.keys = reinterpret_cast<unsigned long long*>(keys);
+  e.done = done;
+  e.out_ids = out_ids;
+  e.out_rows = out_rows;
+  e.token_rows = token_rows;
+  e.token_table = token_table;
+  return cdb::gemm::run<2>(x, ldx, w, ldw, nullptr, 0, M, vocab, K, 1, num_sms, status,
+                           static_cast<cudaStream_t>(stream), &e);
 }
 
 extern "C" int64_t cdb_gemm_workspace_elems(int M, int N, int K, int num_sms) {

@@ -311,14 +311,7 @@ class HuginnRunner(OuroRunner):
             first = self.w.blocks["coda"][0]["norm_1"]
             self._sandwich(n, self.state_bank, x_rows=meta[0], w1=self.w.ln_f, xd=self.xw, w2=first, y=self.h)
             self._blocks("coda", n, self.coda_cache_layer, meta[2], meta[3], True, self.xw, None, self.w.ln_f)
-            self._mm(self.h[:n], self.w.lm_head, self.logits[:n])
-            _lib.call(
-                "cdb_argmax", _lib.ptr(self.logits), self.logits.stride(0), n, s.vocab_size, _lib.ptr(self.token_log),
-                _lib.ptr(meta[1]), _lib.ptr(meta[2]), _lib.ptr(self.token_table), self._sp(),
-            )
-            if keep_logits:
-                return self.logits[:n].clone()
-        return None
+            return self._lm_head_argmax(self.h, n, self.w.lm_head, meta[1], meta[2], keep_logits)
 
     def prefill(
         self,
@@ -364,12 +357,5 @@ class HuginnRunner(OuroRunner):
             self._blocks("coda", n, self.coda_cache_layer, meta[1], meta[2], False, self.xw, None, self.w.ln_f)
             if k:
                 self._gather(self.h, sel[0], k, self.lm_in)
-                self._mm(self.lm_in[:k], self.w.lm_head, self.logits[:k])
-                _lib.call(
-                    "cdb_argmax", _lib.ptr(self.logits), self.logits.stride(0), k, s.vocab_size,
-                    _lib.ptr(self.token_log), _lib.ptr(sel[1]), _lib.ptr(sel[2]), _lib.ptr(self.token_table),
-                    self._sp(),
-                )
-                if keep_logits:
-                    return self.logits[:k].clone()
+                return self._lm_head_argmax(self.lm_in, k, self.w.lm_head, sel[1], sel[2], keep_logits)
         return None

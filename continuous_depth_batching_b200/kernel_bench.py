@@ -2,6 +2,7 @@
 
     python -m continuous_depth_batching_b200.kernel_bench attention --rows 128 --context 1024
     python -m continuous_depth_batching_b200.kernel_bench gemm --m 80 --n 2048 --k 2048
+    python -m continuous_depth_batching_b200.kernel_bench lm_head --m 32 --vocab 49152 --k 2048
 
 ``attention`` builds a one-cache-layer paged KV pool with the Ouro-1.4B head shape (16 heads x
 128), gives each row a context drawn uniformly from [context/2, 3*context/2), and times the
@@ -163,6 +164,44 @@ def run_gemm(args) -> dict:
     return res
 
 
+def run_lm_head(args) -> dict:
+    """cdb_lm_head_argmax against torch.mm (cuBLAS) + cdb_argmax on the same rows."""
+
+    dev = torch.device("cuda")
+    m, v, k = args.m, args.vocab, args.k
+    x = torch.randn(m, k, device=dev).to(torch.bfloat16)
+    w = (0.02 * torch.randn(v, k, device=dev)).to(torch.bfloat16)
+    logits = torch.empty(m, v, device=dev, dtype=torch.bfloat16)
+    ids = torch.zeros(m, dtype=torch.int64, device=dev)
+    keys = torch.zeros(m, dtype=torch.int64, device=dev)
+    done = torch.zeros(1, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def fused():
+        _lib.call(
+            "cdb_lm_head_argmax", _lib.ptr(x), k, _lib.ptr(w), k, m, v, k, _lib.ptr(ids), None, None, None,
+            _lib.ptr(keys), _lib.ptr(done), 148, _lib.ptr(status), sp,
+        )
+
+    def unfused():
+        torch.mm(x, w.t(), out=logits)
+        _lib.call("cdb_argmax", _lib.ptr(logits), v, m, v, _lib.ptr(ids), None, None, None, sp)
+
+    res = {"m": m, "vocab": v, "k": k, "weight_bytes": 2 * v * k}
+    for name, fn in (("fused_tcgen05", fused), ("cublas_plus_argmax", unfused)):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        ms = _events_ms(fn, args.iters, stream, flush)
+        res[name] = {"us": round(ms * 1e3, 2), "gbs": round(2 * v * k / (ms * 1e-3) / 1e9, 1)}
+    if int(status.item()) != 0:
+        raise RuntimeError(_lib.load().cdb_status_string(int(status.item())).decode())
+    return res
+
+
 def main(argv=None) -> None:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     sub = p.add_subparsers(dest="kernel", required=True)
@@ -179,12 +218,16 @@ def main(argv=None) -> None:
     g.add_argument("--k", type=int, default=2048)
     g.add_argument("--splits", type=int, default=0)
     g.add_argument("--only", choices=["tcgen05", "cublas"], default=None)
-    for s in (a, g):
+    lm = sub.add_parser("lm_head")
+    lm.add_argument("--m", type=int, default=32)
+    lm.add_argument("--vocab", type=int, default=49152)
+    lm.add_argument("--k", type=int, default=2048)
+    for s in (a, g, lm):
         s.add_argument("--warmup", type=int, default=3)
         s.add_argument("--iters", type=int, default=20)
         s.add_argument("--seed", type=int, default=0)
     args = p.parse_args(argv)
-    res = run_attention(args) if args.kernel == "attention" else run_gemm(args)
+    res = {"attention": run_attention, "gemm": run_gemm, "lm_head": run_lm_head}[args.kernel](args)
     print(json.dumps(res))
 
 

@@ -278,10 +278,33 @@ class OuroRunner:
         self.part_ml = torch.zeros(SCRATCH_ITEMS * nh * 64 * 2, dtype=torch.float32, device=device)
         self.counters = torch.zeros(SCRATCH_ITEMS * nh, dtype=torch.int32, device=device)
         self.scale = float(D) ** -0.5
+        # LM head + argmax in one GEMM (no logits in HBM) unless logits are kept for inspection
+        self.fused_lm_head = gemm_backend == "tcgen05"
+        self.lm_keys = torch.zeros(max_num_seqs, dtype=torch.int64, device=device)
+        self.lm_done = torch.zeros(1, dtype=torch.int32, device=device)
         self.buckets = decode_graph_buckets(max_num_seqs)
         self.graphs: dict[tuple[int, int, bool], _Graph] = {}
         self.graph_pool = None
         self.stats = RunnerStats()
+
+    def _lm_head_argmax(self, x: torch.Tensor, n: int, w: torch.Tensor, out_rows, token_rows, keep_logits: bool):
+        """Greedy next tokens of rows [0, n) of ``x`` into the token log / table; the logits when kept."""
+
+        s = self.shape
+        if self.fused_lm_head and not keep_logits:
+            _lib.call(
+                "cdb_lm_head_argmax", _lib.ptr(x), x.stride(0), _lib.ptr(w), w.stride(0), n, s.vocab_size,
+                x.shape[1], _lib.ptr(self.token_log), _lib.ptr(out_rows), _lib.ptr(token_rows),
+                _lib.ptr(self.token_table), _lib.ptr(self.lm_keys), _lib.ptr(self.lm_done), self.num_sms,
+                _lib.ptr(self.status), self._sp(),
+            )
+            return None
+        self._mm(x[:n], w, self.logits[:n])
+        _lib.call(
+            "cdb_argmax", _lib.ptr(self.logits), self.logits.stride(0), n, s.vocab_size, _lib.ptr(self.token_log),
+            _lib.ptr(out_rows), _lib.ptr(token_rows), _lib.ptr(self.token_table), self._sp(),
+        )
+        return self.logits[:n].clone() if keep_logits else None
 
     # ------------------------------------------------------------------ cache-layer layout
     @property
@@ -549,13 +572,7 @@ class OuroRunner:
                     "cdb_gather_rows", _lib.ptr(self.xw), self.xw.stride(0), _lib.ptr(sel[0]), k, s.hidden_size,
                     _lib.ptr(self.lm_in), self.lm_in.stride(0), sp,
                 )
-                self._mm(self.lm_in[:k], self.w.lm_head, self.logits[:k])
-                _lib.call(
-                    "cdb_argmax", _lib.ptr(self.logits), self.logits.stride(0), k, s.vocab_size,
-                    _lib.ptr(self.token_log), _lib.ptr(sel[1]), _lib.ptr(sel[2]), _lib.ptr(self.token_table), sp,
-                )
-                if keep_logits:
-                    return self.logits[:k].clone()
+                return self._lm_head_argmax(self.lm_in, k, self.w.lm_head, sel[1], sel[2], keep_logits)
         return None
 
     def prelude(self, token_ids: list[int], req_slots: list[int], hidden: list[int], positions=None) -> None:
@@ -590,14 +607,7 @@ class OuroRunner:
                 "cdb_gather_rows", _lib.ptr(self.bank), self.bank.stride(0), _lib.ptr(meta[0]), n, s.hidden_size,
                 _lib.ptr(self.lm_in), self.lm_in.stride(0), self.stream.cuda_stream,
             )
-            self._mm(self.lm_in[:n], self.w.lm_head, self.logits[:n])
-            _lib.call(
-                "cdb_argmax", _lib.ptr(self.logits), self.logits.stride(0), n, s.vocab_size, _lib.ptr(self.token_log),
-                _lib.ptr(meta[1]), _lib.ptr(meta[2]), _lib.ptr(self.token_table), self.stream.cuda_stream,
-            )
-            if keep_logits:
-                return self.logits[:n].clone()
-        return None
+            return self._lm_head_argmax(self.lm_in, n, self.w.lm_head, meta[1], meta[2], keep_logits)
 
     def exit_kv_copy(self, rows: list[int], pairs: list[tuple[int, int]]) -> None:
         if not rows or not pairs:

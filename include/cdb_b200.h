@@ -178,6 +178,17 @@ int cdb_mlp_gateup_silu_gemm(const void* x, int64_t ldx, const void* w_gate_up, 
                              int64_t ld_act, int M, int inter, int K, int splits, int num_sms, int32_t* status,
                              void* stream);
 
+/* LM head + greedy argmax in one tcgen05 GEMM, without storing logits (the coda's lm_head,
+ * adapters/ouro.py:321-329, then argmax, _run_coda_forward_graphed model_runner.py:1064-1125):
+ * id[r] = argmax_v bf16(x[r] . w[v]) over v < vocab, first index on ties (as torch.argmax).
+ *   out_ids[out_rows ? out_rows[r] : r] = id[r] (skipped when out_rows[r] < 0); if token_rows is
+ *   not NULL and token_rows[r] >= 0, also token_table[token_rows[r]] = id[r].
+ *   keys [M] uint64 and done [1] int32: scratch that must start zeroed; the call leaves it zeroed.
+ *   Calls sharing keys/done must be ordered (one stream). x/w as cdb_gemm_bf16. */
+int cdb_lm_head_argmax(const void* x, int64_t ldx, const void* w, int64_t ldw, int M, int vocab, int K,
+                       int64_t* out_ids, const int32_t* out_rows, const int32_t* token_rows, int32_t* token_table,
+                       uint64_t* keys, int32_t* done, int num_sms, int32_t* status, void* stream);
+
 /* fp32 workspace elements cdb_gemm_bf16 needs: always 0 (kept for callers sizing a buffer). */
 int64_t cdb_gemm_workspace_elems(int M, int N, int K, int num_sms);
 

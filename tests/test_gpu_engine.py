@@ -36,7 +36,8 @@ def _golden():
     return data, shape
 
 
-def _engine(shape, sd, *, kv_policy="single", refill=True, live=False, num_blocks=4096, max_model_len=2048, graphs=True):
+def _engine(shape, sd, *, kv_policy="single", refill=True, live=False, num_blocks=4096, max_model_len=2048, graphs=True,
+            gemm="cublas"):
     model = OuroForCausalLM(shape)
     model.load_state_dict({k: v.to(torch.float32) for k, v in sd.items()})
     cfg = ContinuousDepthBatchingConfig(
@@ -52,7 +53,7 @@ def _engine(shape, sd, *, kv_policy="single", refill=True, live=False, num_block
         kv_pressure_mode="reserve" if kv_policy == "last_exited" else "recompute",
         max_model_len=max_model_len,
     )
-    return ContinuousDepthBatchingEngine.from_model(model, cfg, device="cuda")
+    return ContinuousDepthBatchingEngine.from_model(model, cfg, device="cuda", gemm_backend=gemm)
 
 
 @pytest.mark.parametrize("name", ["replay_refill", "replay_norefill", "replay_last_exited"])
@@ -168,3 +169,34 @@ def test_last_exited_copy_teacher_forced():
     max_new = data["max_new_tokens"][:6]
     depths = run["exit_depths"][:6]
     assert_report(_compare_teacher_forced(shape, sd, prompts, max_new, depths, kv_policy="last_exited"))
+
+
+def test_tcgen05_backend_schedule_and_fused_lm_head():
+    """The all-library GEMM path (tcgen05 projections, fused SwiGLU, LM head + argmax in one GEMM):
+    bit-exact schedule vs the reference trace, and, teacher-forced on the reference tokens, the
+    fused LM head's greedy tokens equal the argmax of the same engine's stored logits (unfused
+    LM head) at >= 99% of positions."""
+
+    data, shape = _golden()
+    run = next(r for r in data["runs"] if r["name"] == "replay_refill")
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"], lm_head_std=0.2)
+    fused = _engine(shape, sd, gemm="tcgen05")
+    assert fused.runner.fused_lm_head
+    fused.record_trace = True
+    outs_a = fused.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"],
+        forced_tokens=run["tokens"],
+    )
+    assert fused.launch_trace == run["launches"]
+    plain = _engine(shape, sd, gemm="tcgen05")
+    plain.keep_logits = True
+    outs_b = plain.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"],
+        forced_tokens=run["tokens"],
+    )
+    a = [t for o in outs_a for t in o.generated_tokens]
+    b = [t for o in outs_b for t in o.generated_tokens]
+    assert len(a) == len(b) == sum(data["max_new_tokens"])
+    agree = sum(int(x == y) for x, y in zip(a, b, strict=True)) / len(a)
+    print({"fused_vs_unfused_agreement": agree})
+    assert agree >= 0.99

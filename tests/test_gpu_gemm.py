@@ -134,3 +134,36 @@ def test_gateup_silu_gemm(gemm, m, inter, k):
     bound = 1.1 * e_g * (uf.abs() + e_u) + (gf.abs() + e_g) * e_u + 2**-7 * ref.abs() + 1e-6
     bad = (act.float() - ref).abs() > bound
     assert not bad.any(), f"{int(bad.sum())} out of bound; max err {(act.float() - ref).abs().max().item():.3e}"
+
+
+@pytest.mark.parametrize("m,vocab,k", [(1, 49152, 2048), (7, 1000, 512), (80, 49152, 2048), (130, 65536, 480), (300, 4096, 256)])
+def test_lm_head_argmax_matches_logits_argmax(gemm, m, vocab, k):
+    """cdb_lm_head_argmax == torch.argmax (first maximum) of the unsplit GEMM's bf16 logits, exactly
+    (same tiles, same accumulation), with the output-row and token-table scatters, twice in a row
+    (the key/counter scratch must come back zeroed)."""
+
+    g = torch.Generator(device=DEV).manual_seed(m + vocab)
+    x = torch.randn(m, k, device=DEV, generator=g).to(torch.bfloat16)
+    w = (0.05 * torch.randn(vocab, k, device=DEV, generator=g)).to(torch.bfloat16)
+    keys = torch.zeros(m, dtype=torch.int64, device=DEV)
+    done = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = torch.full((2 * m + 1,), -7, dtype=torch.int64, device=DEV)
+    out_rows = (torch.arange(m, dtype=torch.int32, device=DEV) * 2 + 1)
+    out_rows[0] = -1  # skipped row
+    table = torch.full((m + 3,), -5, dtype=torch.int32, device=DEV)
+    token_rows = torch.arange(m, dtype=torch.int32, device=DEV) + 3
+    sp = torch.cuda.current_stream().cuda_stream
+    logits = gemm(x, w, splits=1)
+    ref = logits.float().argmax(dim=-1)
+    for _ in range(2):
+        _lib.call(
+            "cdb_lm_head_argmax", _lib.ptr(x), x.stride(0), _lib.ptr(w), w.stride(0), m, vocab, k, _lib.ptr(out),
+            _lib.ptr(out_rows), _lib.ptr(token_rows), _lib.ptr(table), _lib.ptr(keys), _lib.ptr(done), 148,
+            _lib.ptr(gemm.status), sp,
+        )
+        torch.cuda.synchronize()
+        assert int(gemm.status.item()) == 0
+        assert torch.equal(out[out_rows[1:].long()], ref[1:])
+        assert int(out[1]) == -7  # row 0 was skipped
+        assert torch.equal(table[3:].long(), ref)
+        assert int(keys.abs().sum()) == 0 and int(done.item()) == 0
