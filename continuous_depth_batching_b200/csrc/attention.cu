@@ -4,9 +4,13 @@
 // different positions and recurrent steps. Work is split into units (row, head group,
 // KV split) by cdb_attn_plan so CTAs see roughly equal byte counts despite ragged contexts.
 //
-// Decode rows first go through rope_append_kernel (rotate q in place, rotate k, write k/v to the
-// row's cache slot), so the attention kernel itself only reads the cache: row p attends over
-// positions [0, p]. Each CTA is warp specialised: one producer warp prefetches a unit's block
+// The new token of each row is appended in one of two ways. append == 1: rope_append_kernel
+// first rotates q in place, rotates k and writes k/v to the row's cache slot, and the attention
+// kernel then only reads the cache. append == 2 (fused, one launch): the attention kernel rotates
+// q in registers, and the warp that reads position p of a row's last staged page computes the
+// rotated k and v itself, writes them to the cache and uses them for position p from registers
+// (the bytes TMA staged for that row are not used). Either way row p attends over [0, p].
+// Each CTA is warp specialised: one producer warp prefetches a unit's block
 // ids with one coalesced load and streams its K and V pages through an NSTAGE-deep
 // shared-memory ring with 4-D TMA tile loads (one 16-token x HG-head x D tile per page,
 // completion on an mbarrier, no multicast); two consumer warps per head split every page's 16
@@ -71,6 +75,15 @@ struct AttnParams {
   int num_heads;
   float scale_log2;
   int32_t* status;
+  // Fused append (append == 2): q is read unrotated and rotated in registers; the warp that
+  // owns a row's newest token writes the rotated k and v to the cache and into its staged page.
+  int fused;
+  int rope_mode;
+  const void* rope_cos;
+  const void* rope_sin;
+  const __nv_bfloat16* qk_bias;
+  __nv_bfloat16* kv;
+  int64_t k_col, v_col;
 };
 
 // A work unit: `row`'s head group `hg`, pages [b0, b1) of its cache, split `split` of `nsplit`.
@@ -96,6 +109,184 @@ __device__ __forceinline__ void chunk_units(const int32_t* hdr, int c, int& u0, 
 __device__ __forceinline__ float rope_half(float x_d, float x_partner, bool low_half, float c, float s) {
   const float rot = low_half ? -x_partner : x_partner;
   return round_bf16(round_bf16(x_d * c) + round_bf16(rot * s));
+}
+
+// Element d of head vector x with the bias added in bf16 when present.
+__device__ __forceinline__ float biased(const __nv_bfloat16* x, const __nv_bfloat16* b, int d) {
+  const float v = bf16_to_f(x[d]);
+  return b ? round_bf16(v + bf16_to_f(b[d])) : v;
+}
+
+// Rotation pair j of head vector x (bias b or null) at position pos: its element indices and
+// rotated values, rounded to bf16 where the reference's ops round. Mode 1: Ouro split-half
+// rotate_half with bf16 tables [pos][D]; mode 2: Huginn interleaved pairs in fp32 with fp32
+// tables [pos][D/2] (modeling_huginn.py:178-196), each product and the sum rounded separately;
+// mode 0: no rotation.
+__device__ __forceinline__ void rope_pair(int mode, const void* rcos, const void* rsin, int pos, int D, int j,
+                                          const __nv_bfloat16* x, const __nv_bfloat16* b, int& d0, int& d1,
+                                          float& y0, float& y1) {
+  if (mode == 1) {
+    const int half = D / 2;
+    d0 = j;
+    d1 = j + half;
+    const __nv_bfloat16* cr = static_cast<const __nv_bfloat16*>(rcos) + (int64_t)pos * D;
+    const __nv_bfloat16* sr = static_cast<const __nv_bfloat16*>(rsin) + (int64_t)pos * D;
+    const float x0 = biased(x, b, d0), x1 = biased(x, b, d1);
+    y0 = rope_half(x0, x1, true, bf16_to_f(cr[d0]), bf16_to_f(sr[d0]));
+    y1 = rope_half(x1, x0, false, bf16_to_f(cr[d1]), bf16_to_f(sr[d1]));
+  } else if (mode == 2) {
+    d0 = 2 * j;
+    d1 = 2 * j + 1;
+    const float c = static_cast<const float*>(rcos)[(int64_t)pos * (D / 2) + j];
+    const float s = static_cast<const float*>(rsin)[(int64_t)pos * (D / 2) + j];
+    const float x0 = biased(x, b, d0), x1 = biased(x, b, d1);
+    y0 = round_bf16(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s)));
+    y1 = round_bf16(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s)));
+  } else {
+    d0 = 2 * j;
+    d1 = 2 * j + 1;
+    y0 = biased(x, b, d0);
+    y1 = biased(x, b, d1);
+  }
+}
+
+// The raw 16-byte operands of one 8-element RoPE chunk: the chunk, its bias, the split-half
+// partner chunk and its bias (mode 1), and the cos/sin entries (8 bf16 for mode 1, 4 fp32 for
+// mode 2). Loading and rotating are separate so the loads can be issued well before use.
+struct RopeRaw {
+  uint4 x, xb, px, pb, c, s;
+};
+
+__device__ __forceinline__ uint4 ld16(const void* ptr) { return *reinterpret_cast<const uint4*>(ptr); }
+
+// Loads for dims [x0, x0 + 8) of head vector x (x0 a multiple of 8, so a chunk never straddles
+// the split-half boundary or an interleaved pair; x, b and the tables 16-byte aligned).
+__device__ __forceinline__ void rope_load(int mode, const void* rcos, const void* rsin, int pos, int D,
+                                          const __nv_bfloat16* x, const __nv_bfloat16* b, int x0, RopeRaw& r) {
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  r.x = ld16(x + x0);
+  r.xb = b ? ld16(b + x0) : z;
+  r.px = r.pb = r.c = r.s = z;
+  if (mode == 1) {
+    const int px = x0 < D / 2 ? x0 + D / 2 : x0 - D / 2;
+    r.px = ld16(x + px);
+    r.pb = b ? ld16(b + px) : z;
+    r.c = ld16(static_cast<const __nv_bfloat16*>(rcos) + (int64_t)pos * D + x0);
+    r.s = ld16(static_cast<const __nv_bfloat16*>(rsin) + (int64_t)pos * D + x0);
+  } else if (mode == 2) {
+    r.c = ld16(static_cast<const float*>(rcos) + (int64_t)pos * (D / 2) + x0 / 2);
+    r.s = ld16(static_cast<const float*>(rsin) + (int64_t)pos * (D / 2) + x0 / 2);
+  }
+}
+
+__device__ __forceinline__ void unpack8(const uint4 w, float a[8]) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    a[2 * k] = bf16lo(ws[k]);
+    a[2 * k + 1] = bf16hi(ws[k]);
+  }
+}
+
+__device__ __forceinline__ void add_bias8(float a[8], const uint4 b) {
+  float t[8];
+  unpack8(b, t);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) a[e] = round_bf16(a[e] + t[e]);
+}
+
+// The rotated (and bias-added) chunk, exactly as rope_pair rotates each element. `low`: the
+// chunk lies in the first half of the head vector.
+__device__ __forceinline__ void rope_apply(int mode, bool has_bias, bool low, const RopeRaw& r, float y[8]) {
+  float a[8];
+  unpack8(r.x, a);
+  if (has_bias) add_bias8(a, r.xb);
+  if (mode == 1) {
+    float pa[8], c[8], sn[8];
+    unpack8(r.px, pa);
+    if (has_bias) add_bias8(pa, r.pb);
+    unpack8(r.c, c);
+    unpack8(r.s, sn);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = rope_half(a[e], pa[e], low, c[e], sn[e]);
+  } else if (mode == 2) {
+    const float cc[4] = {__uint_as_float(r.c.x), __uint_as_float(r.c.y), __uint_as_float(r.c.z), __uint_as_float(r.c.w)};
+    const float sc[4] = {__uint_as_float(r.s.x), __uint_as_float(r.s.y), __uint_as_float(r.s.z), __uint_as_float(r.s.w)};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      y[2 * i] = round_bf16(__fsub_rn(__fmul_rn(a[2 * i], cc[i]), __fmul_rn(a[2 * i + 1], sc[i])));
+      y[2 * i + 1] = round_bf16(__fadd_rn(__fmul_rn(a[2 * i + 1], cc[i]), __fmul_rn(a[2 * i], sc[i])));
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = a[e];
+  }
+}
+
+__device__ __forceinline__ void rope_chunk8(int mode, const void* rcos, const void* rsin, int pos, int D,
+                                            const __nv_bfloat16* x, const __nv_bfloat16* b, int x0, float y[8]) {
+  RopeRaw r;
+  rope_load(mode, rcos, rsin, pos, D, x, b, x0, r);
+  rope_apply(mode, b != nullptr, x0 < D / 2, r, y);
+}
+
+// Fused append, producer side. A unit holding row `item`'s last page also writes the row's
+// rotated k and its v for head group hg to cache row (last page, pos % 16): the producer warp
+// issues the loads when it starts the unit (append_load), streams the unit's pages, then rotates
+// and stores (append_store), so the load latency overlaps the page stream. The producer runs
+// NSTAGE pages ahead of the consumers, so this costs them nothing.
+template <int D, int HG>
+struct AppendRegs {
+  static constexpr int kChunks = HG * D / 8;  // 8-element chunks of the head group's k (and v)
+  static constexpr int kPer = (kChunks + 31) / 32;
+  RopeRaw k[kPer];
+  uint4 v[kPer];
+  int blk_id;
+};
+
+template <int D, int HG>
+__device__ __forceinline__ void append_load(const AttnParams& p, int item, int hg, int pos, int blk_id,
+                                            AppendRegs<D, HG>& a) {
+  using A = AppendRegs<D, HG>;
+  const int lane = threadIdx.x & 31;
+  const __nv_bfloat16* row = p.qkv + (int64_t)item * p.qkv_stride;
+  a.blk_id = blk_id;
+#pragma unroll
+  for (int i = 0; i < A::kPer; ++i) {
+    const int q = lane + 32 * i;
+    if (q < A::kChunks) {
+      const int head = hg * HG + q * 8 / D, x0 = q * 8 % D;
+      const __nv_bfloat16* kb = p.qk_bias ? p.qk_bias + (int64_t)(p.num_heads + head) * D : nullptr;
+      rope_load(p.rope_mode, p.rope_cos, p.rope_sin, pos, D, row + p.k_col + (int64_t)head * D, kb, x0, a.k[i]);
+      a.v[i] = ld16(row + p.v_col + (int64_t)head * D + x0);
+    }
+  }
+}
+
+template <int D, int HG>
+__device__ __forceinline__ void append_store(const AttnParams& p, int hg, int pos, const AppendRegs<D, HG>& a) {
+  using A = AppendRegs<D, HG>;
+  const int lane = threadIdx.x & 31;
+  const int64_t crow = (int64_t)a.blk_id * kBlock + pos % kBlock;
+  if (a.blk_id < 0 || crow >= p.kv_rows) {
+    if (lane == 0) set_error(p.status, CDB_ERR_INDEX);
+    return;
+  }
+  const int64_t hstride = (int64_t)p.num_heads * D;
+  __nv_bfloat16* kd = p.kv + ((int64_t)(2 * p.cache_layer) * p.kv_rows + crow) * hstride + (int64_t)hg * HG * D;
+  __nv_bfloat16* vd = kd + p.kv_rows * hstride;  // the V slice (cache index 2 * layer + 1), same row
+#pragma unroll
+  for (int i = 0; i < A::kPer; ++i) {
+    const int q = lane + 32 * i;
+    if (q < A::kChunks) {
+      const int off = q * 8, x0 = off % D;  // head-group-relative offset; dim within the head
+      float y[8];
+      rope_apply(p.rope_mode, p.qk_bias != nullptr, x0 < D / 2, a.k[i], y);
+      *reinterpret_cast<uint4*>(kd + off) = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
+                                                       pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
+      *reinterpret_cast<uint4*>(vd + off) = a.v[i];
+    }
+  }
 }
 
 template <int D, int HG>
@@ -137,6 +328,15 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
       const int b0 = unit.b0;
       const int b1 = unit.b1;
       const int32_t* bt = p.block_table + (int64_t)p.item_slot[unit.row] * p.bt_stride;
+      AppendRegs<D, HG> app;
+      int app_pos = -1;
+      if (p.fused) {
+        const int pos = p.item_pos[unit.row];
+        if (b1 == pos / kBlock + 1) {
+          app_pos = pos;
+          append_load<D, HG>(p, unit.row, unit.hg, pos, bt[b1 - 1], app);
+        }
+      }
       for (int base = b0; base < b1 && alive; base += 32) {
         const int my = base + lane < b1 ? bt[base + lane] : 0;
         const int cnt = min(32, b1 - base);
@@ -161,6 +361,7 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
           }
         }
       }
+      if (app_pos >= 0 && alive) append_store<D, HG>(p, unit.hg, app_pos, app);
     }
     }
     return;
@@ -191,17 +392,66 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
     const int b0 = unit.b0;
     const int b1 = unit.b1;
 
-    // this lane's q slice (already rotated), pre-scaled by softmax_scale*log2(e)
+    // this lane's q slice, rotated, pre-scaled by softmax_scale*log2(e)
     const __nv_bfloat16* qrow = p.qkv + (int64_t)item * p.qkv_stride + (int64_t)head * D;
     float qf[C::DPL];
+    if (p.fused) {
+      const __nv_bfloat16* qb = p.qk_bias ? p.qk_bias + (int64_t)head * D : nullptr;
 #pragma unroll
-    for (int c = 0; c < C::NCH; ++c) {
-      const uint4 w = *reinterpret_cast<const uint4*>(qrow + (c * C::LPT + cq) * 8);
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+      for (int c = 0; c < C::NCH; ++c) {
+        float y[8];
+        rope_chunk8(p.rope_mode, p.rope_cos, p.rope_sin, pos, D, qrow, qb, (c * C::LPT + cq) * 8, y);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        qf[c * 8 + 2 * k] = bf16lo(ws[k]) * p.scale_log2;
-        qf[c * 8 + 2 * k + 1] = bf16hi(ws[k]) * p.scale_log2;
+        for (int e = 0; e < 8; ++e) qf[c * 8 + e] = y[e] * p.scale_log2;
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < C::NCH; ++c) {
+        const uint4 w = *reinterpret_cast<const uint4*>(qrow + (c * C::LPT + cq) * 8);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          qf[c * 8 + 2 * k] = bf16lo(ws[k]) * p.scale_log2;
+          qf[c * 8 + 2 * k + 1] = bf16hi(ws[k]) * p.scale_log2;
+        }
+      }
+    }
+
+    // Fused append: the piece holding the row's last page stages that page before position pos
+    // is written, so the warp whose token half holds pos takes that token from registers: its
+    // score is q . k_new summed in the page loop's order (bit-identical to reading k_new from the
+    // page) and its value pairs are v_new. The producer warp writes k_new and v_new to the cache
+    // row (append_load / append_store); no unit of the launch reads that row from the cache.
+    const int t_new = pos % kBlock;
+    const bool owner = p.fused && b1 == pos / kBlock + 1 && sub == t_new / C::TPW;
+    float kdot_new = 0.f;
+    uint32_t vnew[C::PPL];
+#pragma unroll
+    for (int i = 0; i < C::PPL; ++i) vnew[i] = 0u;
+    if (owner) {
+      const __nv_bfloat16* krow_g = p.qkv + (int64_t)item * p.qkv_stride + p.k_col + (int64_t)head * D;
+      const __nv_bfloat16* vrow_g = p.qkv + (int64_t)item * p.qkv_stride + p.v_col + (int64_t)head * D;
+      const __nv_bfloat16* kb = p.qk_bias ? p.qk_bias + (int64_t)(p.num_heads + head) * D : nullptr;
+      float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < C::NCH; ++c) {
+        const int x0 = (c * C::LPT + cq) * 8;
+        float y[8];
+        rope_chunk8(p.rope_mode, p.rope_cos, p.rope_sin, pos, D, krow_g, kb, x0, y);
+        acc0 = fmaf(qf[c * 8 + 0], y[0], acc0);
+        acc1 = fmaf(qf[c * 8 + 1], y[1], acc1);
+        acc0 = fmaf(qf[c * 8 + 2], y[2], acc0);
+        acc1 = fmaf(qf[c * 8 + 3], y[3], acc1);
+        acc0 = fmaf(qf[c * 8 + 4], y[4], acc0);
+        acc1 = fmaf(qf[c * 8 + 5], y[5], acc1);
+        acc0 = fmaf(qf[c * 8 + 6], y[6], acc0);
+        acc1 = fmaf(qf[c * 8 + 7], y[7], acc1);
+      }
+      kdot_new = acc0 + acc1;
+#pragma unroll
+      for (int i = 0; i < C::PPL; ++i) {
+        const int j = lane + 32 * i;
+        if (j < C::NPAIR) vnew[i] = *reinterpret_cast<const uint32_t*>(vrow_g + 2 * j);
       }
     }
 
@@ -215,6 +465,7 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
       if (alive) {
         const uint8_t* kt = smem + stage * C::STAGE_BYTES;
         const uint8_t* vt = kt + C::TILE_BYTES;
+        const bool last_own = owner && blk == b1 - 1;
         float s[C::PASSES];
 #pragma unroll
         for (int ps = 0; ps < C::PASSES; ++ps) {
@@ -234,6 +485,7 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
             acc1 = fmaf(qf[c * 8 + 7], bf16hi(w.w), acc1);
           }
           float acc = acc0 + acc1;
+          if (last_own && t == t_new) acc = kdot_new;
 #pragma unroll
           for (int off = C::LPT / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
           s[ps] = (blk * kBlock + t < n_cached) ? acc : -INFINITY;
@@ -266,7 +518,7 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
           for (int i = 0; i < C::PPL; ++i) {
             const int j = lane + 32 * i;
             if (j < C::NPAIR) {
-              const uint32_t w = vrow[(t * HG + hh) * C::NPAIR + j];
+              const uint32_t w = (last_own && t == t_new) ? vnew[i] : vrow[(t * HG + hh) * C::NPAIR + j];
               o[2 * i] = fmaf(pt, bf16lo(w), o[2 * i]);
               o[2 * i + 1] = fmaf(pt, bf16hi(w), o[2 * i + 1]);
             }
@@ -541,57 +793,21 @@ __global__ void rope_append_kernel(__nv_bfloat16* qkv, int64_t qkv_stride, int64
   __nv_bfloat16* vd = kv + ((int64_t)(2 * cache_layer + 1) * kv_rows + row) * hstride;
   const int half = D / 2;
   const __nv_bfloat16* kb = qk_bias ? qk_bias + (int64_t)num_heads * D : nullptr;
-  // element d of head h of q (or k), with the bias added in bf16 when present
-  auto qval = [&](int64_t hb, int d) {
-    const float x = bf16_to_f(q[hb + d]);
-    return qk_bias ? round_bf16(x + bf16_to_f(qk_bias[hb + d])) : x;
-  };
-  auto kval = [&](int64_t hb, int d) {
-    const float x = bf16_to_f(k[hb + d]);
-    return kb ? round_bf16(x + bf16_to_f(kb[hb + d])) : x;
-  };
   for (int i = threadIdx.x; i < num_heads * half; i += blockDim.x) {
     const int h = i / half, j = i % half;
     const int64_t hb = (int64_t)h * D;
-    if (rope_mode == 1) {
-      const __nv_bfloat16* cr = static_cast<const __nv_bfloat16*>(rope_cos) + (int64_t)pos * D;
-      const __nv_bfloat16* sr = static_cast<const __nv_bfloat16*>(rope_sin) + (int64_t)pos * D;
-      const int d0 = j, d1 = j + half;
-      const float q0 = qval(hb, d0), q1 = qval(hb, d1);
-      const float k0 = kval(hb, d0), k1 = kval(hb, d1);
-      const float c0 = bf16_to_f(cr[d0]), s0 = bf16_to_f(sr[d0]), c1 = bf16_to_f(cr[d1]), s1 = bf16_to_f(sr[d1]);
-      q[hb + d0] = f_to_bf16(rope_half(q0, q1, true, c0, s0));
-      q[hb + d1] = f_to_bf16(rope_half(q1, q0, false, c1, s1));
-      kd[hb + d0] = f_to_bf16(rope_half(k0, k1, true, c0, s0));
-      kd[hb + d1] = f_to_bf16(rope_half(k1, k0, false, c1, s1));
-      vd[hb + d0] = v[hb + d0];
-      vd[hb + d1] = v[hb + d1];
-    } else if (rope_mode == 2) {
-      // Huginn interleaved pairs (2j, 2j+1) rotated in fp32 (modeling_huginn.py:178-196).
-      const float* cr = static_cast<const float*>(rope_cos) + (int64_t)pos * half;
-      const float* sr = static_cast<const float*>(rope_sin) + (int64_t)pos * half;
-      // Each product and the sum rounded separately (no contraction), as the fp32 tensor ops do.
-      const int d0 = 2 * j, d1 = 2 * j + 1;
-      const float c = cr[j], s = sr[j];
-      const float q0 = qval(hb, d0), q1 = qval(hb, d1);
-      const float k0 = kval(hb, d0), k1 = kval(hb, d1);
-      q[hb + d0] = f_to_bf16(__fsub_rn(__fmul_rn(q0, c), __fmul_rn(q1, s)));
-      q[hb + d1] = f_to_bf16(__fadd_rn(__fmul_rn(q1, c), __fmul_rn(q0, s)));
-      kd[hb + d0] = f_to_bf16(__fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, s)));
-      kd[hb + d1] = f_to_bf16(__fadd_rn(__fmul_rn(k1, c), __fmul_rn(k0, s)));
-      vd[hb + d0] = v[hb + d0];
-      vd[hb + d1] = v[hb + d1];
-    } else {
-      const int d0 = 2 * j, d1 = 2 * j + 1;
-      if (qk_bias) {
-        q[hb + d0] = f_to_bf16(qval(hb, d0));
-        q[hb + d1] = f_to_bf16(qval(hb, d1));
-      }
-      kd[hb + d0] = f_to_bf16(kval(hb, d0));
-      kd[hb + d1] = f_to_bf16(kval(hb, d1));
-      vd[hb + d0] = v[hb + d0];
-      vd[hb + d1] = v[hb + d1];
+    int d0, d1;
+    float y0, y1;
+    if (rope_mode != 0 || qk_bias) {
+      rope_pair(rope_mode, rope_cos, rope_sin, pos, D, j, q + hb, qk_bias ? qk_bias + hb : nullptr, d0, d1, y0, y1);
+      q[hb + d0] = f_to_bf16(y0);
+      q[hb + d1] = f_to_bf16(y1);
     }
+    rope_pair(rope_mode, rope_cos, rope_sin, pos, D, j, k + hb, kb ? kb + hb : nullptr, d0, d1, y0, y1);
+    kd[hb + d0] = f_to_bf16(y0);
+    kd[hb + d1] = f_to_bf16(y1);
+    vd[hb + d0] = v[hb + d0];
+    vd[hb + d1] = v[hb + d1];
   }
 }
 
@@ -737,11 +953,16 @@ extern "C" int cdb_paged_decode_attn_append(void* qkv, int64_t qkv_stride, int64
     return CDB_ERR_INVALID_ARGUMENT;
   const int hg = heads_per_cta(num_heads, head_dim);
   if (hg == 0) return CDB_ERR_UNSUPPORTED;
-  if (rope_mode < 0 || rope_mode > 2 || (append && rope_mode != 0 && (rope_cos == nullptr || rope_sin == nullptr)))
+  if (rope_mode < 0 || rope_mode > 2 || append < 0 || append > 2 ||
+      (append && rope_mode != 0 && (rope_cos == nullptr || rope_sin == nullptr)))
+    return CDB_ERR_INVALID_ARGUMENT;
+  // the fused append reads tables and bias in 16-byte vectors
+  if (append == 2 && ((reinterpret_cast<uintptr_t>(qk_bias) & 15) ||
+                      (rope_mode != 0 && ((reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin)) & 15))))
     return CDB_ERR_INVALID_ARGUMENT;
   (void)scratch_items;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (append) {
+  if (append == 1) {
     const int rc = launch_rope_append(qkv, qkv_stride, k_col, v_col, kv_base, kv_rows, cache_layer, block_table,
                                       block_table_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin, qk_bias,
                                       num_items, num_heads, head_dim, status, st);
@@ -769,6 +990,14 @@ extern "C" int cdb_paged_decode_attn_append(void* qkv, int64_t qkv_stride, int64
   p.num_heads = num_heads;
   p.scale_log2 = scale * kLog2e;
   p.status = status;
+  p.fused = append == 2;
+  p.rope_mode = rope_mode;
+  p.rope_cos = rope_cos;
+  p.rope_sin = rope_sin;
+  p.qk_bias = static_cast<const __nv_bfloat16*>(qk_bias);
+  p.kv = static_cast<__nv_bfloat16*>(kv_base);
+  p.k_col = k_col;
+  p.v_col = v_col;
   if (num_ctas <= 0) num_ctas = 2 * 148;
   if (head_dim == 128) return launch_attn<128, 4>(map, p, num_ctas, st);
   if (head_dim == 64) return launch_attn<64, 4>(map, p, num_ctas, st);
@@ -875,7 +1104,12 @@ extern "C" int cdb_paged_decode_attn_append_static(void* qkv, int64_t qkv_stride
     return CDB_ERR_INVALID_ARGUMENT;
   const int hg = heads_per_cta(num_heads, head_dim);
   if (hg == 0) return CDB_ERR_UNSUPPORTED;
-  if (rope_mode < 0 || rope_mode > 2 || (append && rope_mode != 0 && (rope_cos == nullptr || rope_sin == nullptr)))
+  if (rope_mode < 0 || rope_mode > 2 || append < 0 || append > 2 ||
+      (append && rope_mode != 0 && (rope_cos == nullptr || rope_sin == nullptr)))
+    return CDB_ERR_INVALID_ARGUMENT;
+  // the fused append reads tables and bias in 16-byte vectors
+  if (append == 2 && ((reinterpret_cast<uintptr_t>(qk_bias) & 15) ||
+                      (rope_mode != 0 && ((reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin)) & 15))))
     return CDB_ERR_INVALID_ARGUMENT;
   // Limits of the static scratch: head_dim <= 128, num_heads <= 128, and the work plan of an
   // unsplit launch (num_items x num_heads/heads_per_CTA units) within kMaxUnits.
@@ -894,7 +1128,7 @@ extern "C" int cdb_paged_decode_attn_append_static(void* qkv, int64_t qkv_stride
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // The array keeps the previous call's contents: the split counters must start at zero.
   if (cudaMemsetAsync(counters, 0, (size_t)kRowHeads * 4, st) != cudaSuccess) return CDB_ERR_CUDA;
-  if (append) {
+  if (append == 1) {
     rc = launch_rope_append(qkv, qkv_stride, k_col, v_col, kv_base, kv_rows, cache_layer, block_table,
                             block_table_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin, qk_bias,
                             num_items, num_heads, head_dim, status, st);
@@ -926,6 +1160,14 @@ extern "C" int cdb_paged_decode_attn_append_static(void* qkv, int64_t qkv_stride
   p.num_heads = num_heads;
   p.scale_log2 = scale * kLog2e;
   p.status = status;
+  p.fused = append == 2;
+  p.rope_mode = rope_mode;
+  p.rope_cos = rope_cos;
+  p.rope_sin = rope_sin;
+  p.qk_bias = static_cast<const __nv_bfloat16*>(qk_bias);
+  p.kv = static_cast<__nv_bfloat16*>(kv_base);
+  p.k_col = k_col;
+  p.v_col = v_col;
   if (num_ctas <= 0) num_ctas = 2 * 148;
   if (head_dim == 128) return launch_attn<128, 4>(map, p, num_ctas, st);
   if (head_dim == 64) return launch_attn<64, 4>(map, p, num_ctas, st);

@@ -6,6 +6,8 @@
 // All math is fp32; results are rounded to bf16 exactly where the reference's PyTorch bf16
 // ops round (each elementwise op stores a bf16 tensor), so outputs match it up to the
 // summation order of the row reductions.
+#include <type_traits>
+
 #include "cdb_common.cuh"
 
 namespace cdb {
@@ -26,35 +28,55 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return red[0];
 }
 
-// Load up to kMaxChunks 8-element chunks of a bf16 row into fp32 registers.
+// A bf16 row held as NC 8-element chunks per thread (chunk c of thread t covers elements
+// (c * kRowThreads + t) * 8 ..). NC is the smallest count that covers the row, so registers
+// scale with the row width.
+template <int NC>
 struct RowRegs {
-  float v[kMaxChunks][8];
+  float v[NC][8];
 };
 
-__device__ __forceinline__ void load_row(const __nv_bfloat16* row, int hidden, RowRegs& r) {
+template <int NC>
+struct RowRaw {
+  uint4 w[NC];
+};
+
+// Raw 16-byte chunks of a bf16 row (zeros past `hidden`); issued early, converted later.
+template <int NC>
+__device__ __forceinline__ void load_raw(const __nv_bfloat16* row, int hidden, RowRaw<NC>& r) {
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < NC; ++c) {
     const int d = (c * kRowThreads + threadIdx.x) * 8;
-    if (d < hidden) {
-      const uint4 w = *reinterpret_cast<const uint4*>(row + d);
-      r.v[c][0] = bf16lo(w.x);
-      r.v[c][1] = bf16hi(w.x);
-      r.v[c][2] = bf16lo(w.y);
-      r.v[c][3] = bf16hi(w.y);
-      r.v[c][4] = bf16lo(w.z);
-      r.v[c][5] = bf16hi(w.z);
-      r.v[c][6] = bf16lo(w.w);
-      r.v[c][7] = bf16hi(w.w);
-    } else {
-#pragma unroll
-      for (int k = 0; k < 8; ++k) r.v[c][k] = 0.f;
-    }
+    r.w[c] = d < hidden ? *reinterpret_cast<const uint4*>(row + d) : make_uint4(0u, 0u, 0u, 0u);
   }
 }
 
-__device__ __forceinline__ void store_row(__nv_bfloat16* row, int hidden, const RowRegs& r) {
+template <int NC>
+__device__ __forceinline__ void unpack_row(const RowRaw<NC>& w, RowRegs<NC>& r) {
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < NC; ++c) {
+    r.v[c][0] = bf16lo(w.w[c].x);
+    r.v[c][1] = bf16hi(w.w[c].x);
+    r.v[c][2] = bf16lo(w.w[c].y);
+    r.v[c][3] = bf16hi(w.w[c].y);
+    r.v[c][4] = bf16lo(w.w[c].z);
+    r.v[c][5] = bf16hi(w.w[c].z);
+    r.v[c][6] = bf16lo(w.w[c].w);
+    r.v[c][7] = bf16hi(w.w[c].w);
+  }
+}
+
+template <int NC>
+__device__ __forceinline__ void load_row(const __nv_bfloat16* row, int hidden, RowRegs<NC>& r) {
+  RowRaw<NC> w;
+  load_raw(row, hidden, w);
+  unpack_row(w, r);
+}
+
+template <int NC>
+__device__ __forceinline__ void store_row(__nv_bfloat16* row, int hidden, const RowRegs<NC>& r) {
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
     const int d = (c * kRowThreads + threadIdx.x) * 8;
     if (d < hidden) {
       uint4 w;
@@ -67,45 +89,49 @@ __device__ __forceinline__ void store_row(__nv_bfloat16* row, int hidden, const 
   }
 }
 
-// In-register OuroRMSNorm: r <- weight * bf16(r * rsqrt(mean(r^2) + eps)), all rounded to bf16.
-__device__ __forceinline__ void rms_inplace(RowRegs& r, const __nv_bfloat16* weight, int hidden, float eps,
+// In-register OuroRMSNorm with preloaded weights: r <- weight * bf16(r * rsqrt(mean(r^2) + eps)),
+// all rounded to bf16.
+template <int NC>
+__device__ __forceinline__ void rms_inplace(RowRegs<NC>& r, const RowRaw<NC>& weight, int hidden, float eps,
                                             float* red) {
   float ss = 0.f;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c)
+  for (int c = 0; c < NC; ++c)
 #pragma unroll
     for (int k = 0; k < 8; ++k) ss = fmaf(r.v[c][k], r.v[c][k], ss);
   const float var = block_sum(ss, red) / (float)hidden;
   const float inv = rsqrtf(var + eps);
+  RowRegs<NC> g;
+  unpack_row(weight, g);
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
-    const int d = (c * kRowThreads + threadIdx.x) * 8;
-    if (d < hidden) {
-      const uint4 w = *reinterpret_cast<const uint4*>(weight + d);
-      const float g[8] = {bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y),
-                          bf16lo(w.z), bf16hi(w.z), bf16lo(w.w), bf16hi(w.w)};
+  for (int c = 0; c < NC; ++c)
 #pragma unroll
-      for (int k = 0; k < 8; ++k) r.v[c][k] = round_bf16(g[k] * round_bf16(r.v[c][k] * inv));
-    }
-  }
+    for (int k = 0; k < 8; ++k) r.v[c][k] = round_bf16(g.v[c][k] * round_bf16(r.v[c][k] * inv));
 }
 
+// Norm kernels load their weights before pdl_wait() (weights never depend on the preceding
+// kernel) and issue every row load before the first reduction, so a launch costs one memory
+// round trip after its predecessor finishes instead of one per operand.
+template <int NC>
 __global__ void __launch_bounds__(kRowThreads) rmsnorm_kernel(const __nv_bfloat16* x, int64_t xs, const int32_t* x_rows,
                                                               const __nv_bfloat16* w, __nv_bfloat16* y, int64_t ys,
                                                               __nv_bfloat16* xc, int64_t xcs, int hidden, float eps) {
   pdl_trigger();
+  RowRaw<NC> wr;
+  load_raw(w, hidden, wr);
   pdl_wait();
   __shared__ float red[32];
   const int r = blockIdx.x;
   const int src = x_rows ? x_rows[r] : r;
   if (src < 0) return;
-  RowRegs v;
+  RowRegs<NC> v;
   load_row(x + (int64_t)src * xs, hidden, v);
   if (xc) store_row(xc + (int64_t)r * xcs, hidden, v);
-  rms_inplace(v, w, hidden, eps, red);
+  rms_inplace(v, wr, hidden, eps, red);
   store_row(y + (int64_t)r * ys, hidden, v);
 }
 
+template <int NC>
 __global__ void __launch_bounds__(kRowThreads) add_rmsnorm_kernel(__nv_bfloat16* x, int64_t xs, const __nv_bfloat16* a,
                                                                   int64_t as, const __nv_bfloat16* wa,
                                                                   const __nv_bfloat16* wn, __nv_bfloat16* y, int64_t ys,
@@ -113,35 +139,37 @@ __global__ void __launch_bounds__(kRowThreads) add_rmsnorm_kernel(__nv_bfloat16*
                                                                   const __nv_bfloat16* gb, __nv_bfloat16* gout,
                                                                   int hidden, float eps) {
   pdl_trigger();
+  RowRaw<NC> war, wnr, gwr;
+  load_raw(wa, hidden, war);
+  load_raw(wn, hidden, wnr);
+  if (gw) load_raw(gw, hidden, gwr);
   pdl_wait();
   __shared__ float red[32];
   const int r = blockIdx.x;
   const int dst = y_rows ? y_rows[r] : r;
   if (dst < 0) return;
-  RowRegs av, xv;
-  load_row(a + (int64_t)r * as, hidden, av);
-  rms_inplace(av, wa, hidden, eps, red);
-  load_row(x + (int64_t)r * xs, hidden, xv);
+  RowRaw<NC> ar, xr;
+  load_raw(a + (int64_t)r * as, hidden, ar);
+  load_raw(x + (int64_t)r * xs, hidden, xr);
+  RowRegs<NC> av, xv;
+  unpack_row(ar, av);
+  rms_inplace(av, war, hidden, eps, red);
+  unpack_row(xr, xv);
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c)
+  for (int c = 0; c < NC; ++c)
 #pragma unroll
     for (int k = 0; k < 8; ++k) xv.v[c][k] = round_bf16(xv.v[c][k] + av.v[c][k]);
   store_row(x + (int64_t)r * xs, hidden, xv);
-  rms_inplace(xv, wn, hidden, eps, red);
+  rms_inplace(xv, wnr, hidden, eps, red);
   store_row(y + (int64_t)dst * ys, hidden, xv);
   if (gw) {
+    RowRegs<NC> g;
+    unpack_row(gwr, g);
     float dot = 0.f;
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
-      const int d = (c * kRowThreads + threadIdx.x) * 8;
-      if (d < hidden) {
-        const uint4 w = *reinterpret_cast<const uint4*>(gw + d);
-        const float g[8] = {bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y),
-                            bf16lo(w.z), bf16hi(w.z), bf16lo(w.w), bf16hi(w.w)};
+    for (int c = 0; c < NC; ++c)
 #pragma unroll
-        for (int k = 0; k < 8; ++k) dot = fmaf(g[k], xv.v[c][k], dot);
-      }
-    }
+      for (int k = 0; k < 8; ++k) dot = fmaf(g.v[c][k], xv.v[c][k], dot);
     dot = block_sum(dot, red);
     if (threadIdx.x == 0) gout[r] = f_to_bf16(dot + bf16_to_f(gb[0]));
   }
@@ -265,33 +293,40 @@ __global__ void embed_kernel(const __nv_bfloat16* table, int hidden, int vocab, 
 //   if w2: y[r] = rmsnorm(v; w2).
 // (HuginnBlock.forward modeling_huginn.py:333-336: x = norm_2(attn + x), norm_3(x); x = norm_4(mlp
 // + x), then the next block's norm_1; run_coda :454-460: ln_f before and after the coda blocks.)
+template <int NC>
 __global__ void __launch_bounds__(kRowThreads) sandwich_norm_kernel(
     const __nv_bfloat16* xs, int64_t xss, const int32_t* x_rows, const __nv_bfloat16* a, int64_t as,
     const __nv_bfloat16* w1, __nv_bfloat16* xd, int64_t xds, const int32_t* xd_rows, const __nv_bfloat16* w2,
     __nv_bfloat16* y, int64_t ys, int hidden, float eps) {
   pdl_trigger();
+  RowRaw<NC> w1r, w2r;
+  if (w1) load_raw(w1, hidden, w1r);
+  if (w2) load_raw(w2, hidden, w2r);
   pdl_wait();
   __shared__ float red[32];
   const int r = blockIdx.x;
   const int src = x_rows ? x_rows[r] : r;
   if (src < 0) return;
-  RowRegs v;
-  load_row(xs + (int64_t)src * xss, hidden, v);
+  RowRaw<NC> xr, ar;
+  load_raw(xs + (int64_t)src * xss, hidden, xr);
+  if (a) load_raw(a + (int64_t)r * as, hidden, ar);
+  RowRegs<NC> v;
+  unpack_row(xr, v);
   if (a) {
-    RowRegs av;
-    load_row(a + (int64_t)r * as, hidden, av);
+    RowRegs<NC> av;
+    unpack_row(ar, av);
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c)
+    for (int c = 0; c < NC; ++c)
 #pragma unroll
       for (int k = 0; k < 8; ++k) v.v[c][k] = round_bf16(av.v[c][k] + v.v[c][k]);
   }
-  if (w1) rms_inplace(v, w1, hidden, eps, red);
+  if (w1) rms_inplace(v, w1r, hidden, eps, red);
   if (xd) {
     const int dst = xd_rows ? xd_rows[r] : r;
     if (dst >= 0) store_row(xd + (int64_t)dst * xds, hidden, v);
   }
   if (w2) {
-    rms_inplace(v, w2, hidden, eps, red);
+    rms_inplace(v, w2r, hidden, eps, red);
     store_row(y + (int64_t)r * ys, hidden, v);
   }
 }
@@ -299,6 +334,7 @@ __global__ void __launch_bounds__(kRowThreads) sandwich_norm_kernel(
 // latent_diff (models/huginn/exit_gates.py:33-40) in bf16 tensors, as the adapter computes it:
 // d = bf16(new - old); out[r] = bf16(bf16(||d||) / max(bf16(||new||), 1e-9)), norms accumulated
 // in fp32. new row rows[r] (r when rows == NULL), old row r; rows[r] < 0 skips row r.
+template <int NC>
 __global__ void __launch_bounds__(kRowThreads) latent_diff_kernel(const __nv_bfloat16* nw, int64_t ns,
                                                                   const __nv_bfloat16* old, int64_t os,
                                                                   const int32_t* rows, int hidden,
@@ -309,12 +345,12 @@ __global__ void __launch_bounds__(kRowThreads) latent_diff_kernel(const __nv_bfl
   const int r = blockIdx.x;
   const int nr = rows ? rows[r] : r;
   if (nr < 0) return;
-  RowRegs a, b;
+  RowRegs<NC> a, b;
   load_row(nw + (int64_t)nr * ns, hidden, a);
   load_row(old + (int64_t)r * os, hidden, b);
   float sd = 0.f, sn = 0.f;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c)
+  for (int c = 0; c < NC; ++c)
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const float d = round_bf16(a.v[c][k] - b.v[c][k]);
@@ -435,14 +471,30 @@ extern "C" const char* cdb_status_string(int status) {
   }
 }
 
+// Calls f(std::integral_constant<int, NC>) with NC = the chunks per thread covering `hidden`.
+template <typename F>
+static void with_row_chunks(int hidden, F&& f) {
+  switch (max(1, (hidden + kRowThreads * 8 - 1) / (kRowThreads * 8))) {
+    case 1: f(std::integral_constant<int, 1>{}); break;
+    case 2: f(std::integral_constant<int, 2>{}); break;
+    case 3: f(std::integral_constant<int, 3>{}); break;
+    case 4: f(std::integral_constant<int, 4>{}); break;
+    case 5: f(std::integral_constant<int, 5>{}); break;
+    default: f(std::integral_constant<int, kMaxChunks>{}); break;
+  }
+}
+
 extern "C" int cdb_rmsnorm(const void* x, int64_t x_stride, const int32_t* x_rows, const void* weight, void* y,
                            int64_t y_stride, void* x_copy, int64_t x_copy_stride, int num_rows, int hidden, float eps,
                            void* stream) {
   if (hidden % 8 != 0 || hidden > kRowThreads * kMaxChunks * 8 || num_rows < 0) return CDB_ERR_INVALID_ARGUMENT;
   if (num_rows == 0) return CDB_OK;
-  launch_pdl(rmsnorm_kernel, dim3(num_rows), dim3(kRowThreads), 0, static_cast<cudaStream_t>(stream), 
-      static_cast<const __nv_bfloat16*>(x), x_stride, x_rows, static_cast<const __nv_bfloat16*>(weight),
-      static_cast<__nv_bfloat16*>(y), y_stride, static_cast<__nv_bfloat16*>(x_copy), x_copy_stride, hidden, eps);
+  with_row_chunks(hidden, [&](auto nc) {
+    launch_pdl(rmsnorm_kernel<decltype(nc)::value>, dim3(num_rows), dim3(kRowThreads), 0,
+               static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x), x_stride, x_rows,
+               static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(y), y_stride,
+               static_cast<__nv_bfloat16*>(x_copy), x_copy_stride, hidden, eps);
+  });
   return check_launch();
 }
 
@@ -453,11 +505,14 @@ extern "C" int cdb_add_rmsnorm(void* x, int64_t x_stride, const void* a, int64_t
   if (hidden % 8 != 0 || hidden > kRowThreads * kMaxChunks * 8 || num_rows < 0) return CDB_ERR_INVALID_ARGUMENT;
   if (gate_w != nullptr && (gate_b == nullptr || gate_out == nullptr)) return CDB_ERR_INVALID_ARGUMENT;
   if (num_rows == 0) return CDB_OK;
-  launch_pdl(add_rmsnorm_kernel, dim3(num_rows), dim3(kRowThreads), 0, static_cast<cudaStream_t>(stream), 
-      static_cast<__nv_bfloat16*>(x), x_stride, static_cast<const __nv_bfloat16*>(a), a_stride,
-      static_cast<const __nv_bfloat16*>(w_a), static_cast<const __nv_bfloat16*>(w_next),
-      static_cast<__nv_bfloat16*>(y), y_stride, y_rows, static_cast<const __nv_bfloat16*>(gate_w),
-      static_cast<const __nv_bfloat16*>(gate_b), static_cast<__nv_bfloat16*>(gate_out), hidden, eps);
+  with_row_chunks(hidden, [&](auto nc) {
+    launch_pdl(add_rmsnorm_kernel<decltype(nc)::value>, dim3(num_rows), dim3(kRowThreads), 0,
+               static_cast<cudaStream_t>(stream), static_cast<__nv_bfloat16*>(x), x_stride,
+               static_cast<const __nv_bfloat16*>(a), a_stride, static_cast<const __nv_bfloat16*>(w_a),
+               static_cast<const __nv_bfloat16*>(w_next), static_cast<__nv_bfloat16*>(y), y_stride, y_rows,
+               static_cast<const __nv_bfloat16*>(gate_w), static_cast<const __nv_bfloat16*>(gate_b),
+               static_cast<__nv_bfloat16*>(gate_out), hidden, eps);
+  });
   return check_launch();
 }
 
@@ -510,10 +565,13 @@ extern "C" int cdb_sandwich_norm(const void* x_src, int64_t x_src_stride, const 
   if (hidden % 8 != 0 || hidden > kRowThreads * kMaxChunks * 8 || num_rows < 0 || (w2 != nullptr && y == nullptr))
     return CDB_ERR_INVALID_ARGUMENT;
   if (num_rows == 0) return CDB_OK;
-  launch_pdl(sandwich_norm_kernel, dim3(num_rows), dim3(kRowThreads), 0, static_cast<cudaStream_t>(stream),
-             static_cast<const __nv_bfloat16*>(x_src), x_src_stride, x_rows, static_cast<const __nv_bfloat16*>(add),
-             add_stride, static_cast<const __nv_bfloat16*>(w1), static_cast<__nv_bfloat16*>(x_dst), x_dst_stride,
-             x_dst_rows, static_cast<const __nv_bfloat16*>(w2), static_cast<__nv_bfloat16*>(y), y_stride, hidden, eps);
+  with_row_chunks(hidden, [&](auto nc) {
+    launch_pdl(sandwich_norm_kernel<decltype(nc)::value>, dim3(num_rows), dim3(kRowThreads), 0,
+               static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x_src), x_src_stride, x_rows,
+               static_cast<const __nv_bfloat16*>(add), add_stride, static_cast<const __nv_bfloat16*>(w1),
+               static_cast<__nv_bfloat16*>(x_dst), x_dst_stride, x_dst_rows, static_cast<const __nv_bfloat16*>(w2),
+               static_cast<__nv_bfloat16*>(y), y_stride, hidden, eps);
+  });
   return check_launch();
 }
 
@@ -521,9 +579,12 @@ extern "C" int cdb_latent_diff(const void* new_state, int64_t new_stride, const 
                                const int32_t* rows, int num_rows, int hidden, void* out, void* stream) {
   if (hidden % 8 != 0 || hidden > kRowThreads * kMaxChunks * 8 || num_rows < 0) return CDB_ERR_INVALID_ARGUMENT;
   if (num_rows == 0) return CDB_OK;
-  launch_pdl(latent_diff_kernel, dim3(num_rows), dim3(kRowThreads), 0, static_cast<cudaStream_t>(stream),
-             static_cast<const __nv_bfloat16*>(new_state), new_stride, static_cast<const __nv_bfloat16*>(old_state),
-             old_stride, rows, hidden, static_cast<__nv_bfloat16*>(out));
+  with_row_chunks(hidden, [&](auto nc) {
+    launch_pdl(latent_diff_kernel<decltype(nc)::value>, dim3(num_rows), dim3(kRowThreads), 0,
+               static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(new_state), new_stride,
+               static_cast<const __nv_bfloat16*>(old_state), old_stride, rows, hidden,
+               static_cast<__nv_bfloat16*>(out));
+  });
   return check_launch();
 }
 

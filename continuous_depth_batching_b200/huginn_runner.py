@@ -171,7 +171,7 @@ class HuginnRunner(OuroRunner):
             _lib.ptr(self.attn), self.attn.stride(0),
             _lib.ptr(pool.kv), pool.num_cache_layers, pool.rows, cache_layer,
             _lib.ptr(pool.block_table), pool.block_table.stride(0), _lib.ptr(item_slot), _lib.ptr(item_pos),
-            2, _lib.ptr(self.rope_cos), _lib.ptr(self.rope_sin), _lib.ptr(qk_bias), 1,
+            2, _lib.ptr(self.rope_cos), _lib.ptr(self.rope_sin), _lib.ptr(qk_bias), 2,  # fused append
             _lib.ptr(self.plan_hdr), _lib.ptr(self.units), _lib.ptr(self.part_o), _lib.ptr(self.part_ml),
             _lib.ptr(self.counters), SCRATCH_ITEMS, n, s.n_heads, s.head_dim, self.block_size,
             self.scale, self.attn_ctas, _lib.ptr(self.status), self._sp(),

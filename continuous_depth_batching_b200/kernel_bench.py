@@ -6,8 +6,9 @@
 
 ``attention`` builds a one-cache-layer paged KV pool with the Ouro-1.4B head shape (16 heads x
 128), gives each row a context drawn uniformly from [context/2, 3*context/2), and times the
-cache-only decode attention kernel (the launch a recurrent step makes per layer after the
-rope/append kernel) with CUDA events on the launching stream. Algorithmic bytes per launch are
+decode attention with CUDA events on the launching stream: cache-only (``--append 0``, the
+default), the rope/append kernel followed by the attention kernel (``--append 1``), or the fused
+single launch the engine uses (``--append 2``, split-half RoPE). Algorithmic bytes per launch are
 ``attention_bytes`` below. ``gemm`` times ``cdb_gemm_bf16`` against ``torch.mm`` (cuBLAS) on one
 shape, flushing L2 between launches so weights stream from HBM as they do in a decode step.
 Each prints one JSON line.
@@ -94,17 +95,24 @@ def run_attention(args) -> dict:
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
+    append = args.append
+    rope_mode = 1 if append else 0
+    tab = torch.arange(int(pos.max()) + 1, device=dev, dtype=torch.float32)[:, None] * torch.linspace(
+        1.0, 1e-4, dim, device=dev
+    )[None, :]
+    cos, sin = tab.cos().to(torch.bfloat16).contiguous(), tab.sin().to(torch.bfloat16).contiguous()
     _lib.call(
-        "cdb_attn_plan", _lib.ptr(pos_d), args.rows, 0, heads, dim, BLOCK, cap, scratch_items, 148,
+        "cdb_attn_plan", _lib.ptr(pos_d), args.rows, append, heads, dim, BLOCK, cap, scratch_items, 148,
         _lib.ptr(hdr), _lib.ptr(units), sp,
     )
 
     def launch():
         _lib.call(
             "cdb_paged_decode_attn_append", _lib.ptr(qkv), qkv.stride(0), hd, 2 * hd, _lib.ptr(out), out.stride(0),
-            _lib.ptr(kv), 1, kv_rows, 0, _lib.ptr(table), table.stride(0), _lib.ptr(slots), _lib.ptr(pos_d), 0,
-            None, None, None, 0, _lib.ptr(hdr), _lib.ptr(units), _lib.ptr(part_o), _lib.ptr(part_ml), _lib.ptr(counters),
-            scratch_items, args.rows, heads, dim, BLOCK, dim**-0.5, args.ctas, _lib.ptr(status), sp,
+            _lib.ptr(kv), 1, kv_rows, 0, _lib.ptr(table), table.stride(0), _lib.ptr(slots), _lib.ptr(pos_d), rope_mode,
+            _lib.ptr(cos), _lib.ptr(sin), None, append, _lib.ptr(hdr), _lib.ptr(units), _lib.ptr(part_o),
+            _lib.ptr(part_ml), _lib.ptr(counters), scratch_items, args.rows, heads, dim, BLOCK, dim**-0.5, args.ctas,
+            _lib.ptr(status), sp,
         )
 
     for _ in range(args.warmup):
@@ -113,9 +121,10 @@ def run_attention(args) -> dict:
     ms = _events_ms(launch, args.iters, stream)
     if int(status.item()) != 0:
         raise RuntimeError(_lib.load().cdb_status_string(int(status.item())).decode())
-    algo = attention_bytes(pos.tolist(), heads, dim, append=False)
+    algo = attention_bytes(pos.tolist(), heads, dim, append=bool(append))
     return {
         "kernel": f"cdb::decode_attn_kernel<{dim},{hg}>",
+        "append": append,
         "rows": args.rows,
         "mean_context": float(ctx.float().mean()),
         "kv_pool_bytes": kv.numel() * 2,
@@ -212,6 +221,7 @@ def main(argv=None) -> None:
     a.add_argument("--head-dim", type=int, default=128)
     a.add_argument("--scratch-items", type=int, default=256)
     a.add_argument("--ctas", type=int, default=296)
+    a.add_argument("--append", type=int, choices=[0, 1, 2], default=0)
     g = sub.add_parser("gemm")
     g.add_argument("--m", type=int, default=80)
     g.add_argument("--n", type=int, default=2048)

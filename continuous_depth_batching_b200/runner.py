@@ -416,7 +416,7 @@ class OuroRunner:
         for l in range(L):
             self._mm(self.h[:n], w.w_qkv[l], self.qkv[:n])
             if append:
-                self._attention(n, base_layer + l, item_slot, item_pos, 1, 1)
+                self._attention(n, base_layer + l, item_slot, item_pos, 2, 1)  # RoPE + KV append fused
             else:
                 _lib.call(
                     "cdb_rope_append_kv", _lib.ptr(self.qkv), self.qkv.stride(0), self.k_col, self.v_col,

@@ -84,8 +84,11 @@ int cdb_attn_plan(const int32_t* item_pos, int num_items, int append, int num_he
  *              modeling_huginn.py:175-197).
  *   qk_bias    NULL, or bf16 [2, num_heads, head_dim] (q bias, then k bias) added to q and k in
  *              bf16 before the rotation (Huginn's learned qk_bias, modeling_huginn.py:261-264).
- *   append     1: rotate q in place in `qkv`, rotate k, write k/v at the row's position, then
- *              attend over [0,p]; 0: attend over cached rows [0,p] with q already rotated.
+ *   append     1: rotate q in place in `qkv`, rotate k, write k/v at the row's position (a
+ *              separate kernel), then attend over [0,p]; 2: the same result in one kernel (q
+ *              rotated in registers and `qkv` left unchanged; k/v written to the cache and used
+ *              for position p directly; tables and qk_bias 16-byte aligned); 0: attend over
+ *              cached rows [0,p] with q already rotated.
  *   out        bf16 [num_items, out_stride], heads concatenated.
  *   part_o/part_ml/counters: split-combine scratch sized for scratch_items rows
  *              (cdb_attn_scratch_bytes); counters must start zeroed, kernels leave them zeroed.

@@ -114,11 +114,12 @@ def _reference_decode(h, qkv, kv, layer, table, slots, pos, cos, sin, append, ro
     return out, new_k
 
 
+@pytest.mark.parametrize("append", [1, 2])
 @pytest.mark.parametrize(
     "heads,d,n_items,max_pos",
     [(16, 128, 37, 700), (16, 128, 256, 300), (4, 64, 16, 120), (16, 128, 3, 3000), (55, 96, 9, 200)],
 )
-def test_decode_attention_append_matches_fp32(heads, d, n_items, max_pos):
+def test_decode_attention_append_matches_fp32(heads, d, n_items, max_pos, append):
     gen = torch.Generator().manual_seed(heads * 1000 + n_items)
     h = AttnHarness(n_items, heads, d, num_blocks=max(512, n_items * (max_pos // BS + 2)))
     max_blocks = max_pos // BS + 2
@@ -137,7 +138,10 @@ def test_decode_attention_append_matches_fp32(heads, d, n_items, max_pos):
     # head_dim 96 is the Huginn shape, whose interleaved RoPE is not the Ouro table: run it unrotated.
     rope_mode = 1 if d != 96 else 0
     ref, new_k = _reference_decode(h, qkv, h.kv.clone(), 1, table, slots, pos, cos, sin, append=1, rope=rope_mode == 1)
-    h.run(qkv, out, 1, table, slots, pos, 1, rope_mode, cos, sin)
+    qkv_in = qkv.clone()
+    h.run(qkv, out, 1, table, slots, pos, append, rope_mode, cos, sin)
+    if append == 2:  # fused: q is rotated in registers, qkv is left as it was
+        assert torch.equal(qkv, qkv_in)
     valid = pos >= 0
     err = (out.float()[valid] - ref[valid]).abs().max().item()
     assert err < 2e-2, err
@@ -147,6 +151,57 @@ def test_decode_attention_append_matches_fp32(heads, d, n_items, max_pos):
     # padding row untouched
     if n_items > 4:
         assert out[3].abs().sum().item() == 0.0
+
+
+@pytest.mark.parametrize(
+    "heads,d,rope_mode,bias,n_items,max_pos,scratch",
+    [
+        (16, 128, 1, False, 37, 700, 256),  # split-KV pieces; the last piece appends
+        (16, 128, 1, False, 300, 200, 256),  # rows > scratch rows: whole segments, round-robin
+        (16, 128, 1, True, 5, 3000, 256),  # long contexts: many pieces per segment
+        (4, 64, 1, False, 33, 90, 256),
+        (5, 96, 2, True, 21, 400, 256),  # Huginn: qk_bias + interleaved fp32 RoPE
+        (55, 96, 2, True, 4, 150, 256),
+        (16, 128, 0, True, 12, 100, 256),  # bias without rotation
+    ],
+)
+def test_fused_append_bit_exact_vs_two_kernels(heads, d, rope_mode, bias, n_items, max_pos, scratch):
+    """append=2 (one launch) against append=1 (rope_append kernel, then attention): the same
+    output bits and the same cache contents, at every position within a page (both token halves
+    of the page own the new row somewhere in the batch) and with padding rows."""
+
+    gen = torch.Generator().manual_seed(heads + 17 * n_items + rope_mode)
+    max_blocks = max_pos // BS + 2
+    h = AttnHarness(n_items, heads, d, num_blocks=max(512, n_items * max_blocks), scratch=scratch)
+    table = _make_tables(n_items, max_blocks, h.num_blocks, gen)
+    pos = torch.randint(0, max_pos, (n_items,), generator=gen).to(torch.int32)
+    for i in range(min(n_items, 16)):
+        pos[i] = (pos[i] // BS) * BS + i  # every offset within a page
+    if n_items > 4:
+        pos[4] = -1
+    pos = pos.to(DEV)
+    slots = torch.arange(n_items, dtype=torch.int32, device=DEV)
+    qkv = torch.randn(n_items, 3 * heads * d, device=DEV).to(torch.bfloat16)
+    qk_bias = (0.1 * torch.randn(2, heads, d, device=DEV)).to(torch.bfloat16) if bias else None
+    if rope_mode == 2:
+        inv = 1.0 / (50000.0 ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+        freqs = torch.arange(max_pos + BS, device=DEV).float().unsqueeze(-1) * inv.to(DEV)
+        cos, sin = freqs.cos().contiguous(), freqs.sin().contiguous()
+    else:
+        cos, sin = _rope_tables(max_pos + BS, d)  # positions reach max_pos + 14
+    kv0 = h.kv.clone()
+    out1 = torch.zeros(n_items, heads * d, device=DEV, dtype=torch.bfloat16)
+    out2 = torch.zeros_like(out1)
+    qkv1 = qkv.clone()
+    h.run(qkv1, out1, 1, table, slots, pos, 1, rope_mode, cos, sin, qk_bias=qk_bias)
+    kv1 = h.kv.clone()
+    h.kv.copy_(kv0)
+    qkv2 = qkv.clone()
+    h.run(qkv2, out2, 1, table, slots, pos, 2, rope_mode, cos, sin, qk_bias=qk_bias)
+    assert torch.equal(qkv2, qkv)
+    assert torch.equal(h.kv, kv1)
+    assert torch.equal(out2, out1)
+    assert int(h.counters.abs().sum().item()) == 0
 
 
 @pytest.mark.parametrize("heads,d", [(16, 128), (4, 64), (55, 96)])

@@ -2,8 +2,9 @@
 with caller-provided scratch, both called through the C ABI.
 
 Tolerance: the attention tests' 2e-2 max-abs on the bf16 output, and exact equality of the
-appended K/V rows and of the rotated q written back into qkv. Each case makes two calls in a row
-on different inputs, so the second call runs on scratch the first one has used.
+appended K/V rows and of qkv (q rotated in place with append 1, left unchanged with the fused
+append 2). Each case makes three calls in a row on different inputs, so later calls run on
+scratch an earlier one has used.
 """
 
 from __future__ import annotations
@@ -113,7 +114,7 @@ def test_static_scratch_matches_scratch_entry_two_calls(heads, d, n_items, max_p
         "cdb_paged_decode_attn_append_static",
         *_static_args(setup, setup.qkv, setup.kv, setup.qkv, 0, 1, 0, status, stream),
     )
-    for call, (layer, append) in enumerate([(1, 1), (0, 0)]):
+    for call, (layer, append) in enumerate([(1, 1), (0, 0), (1, 2)]):
         c = Case(heads, d, n_items, max_pos, seed=100 * call + heads + n_items)
         qkv_a, qkv_b = c.qkv.clone(), c.qkv.clone()
         kv_a, kv_b = c.kv.clone(), c.kv.clone()
