@@ -155,7 +155,7 @@ class _Req:
 
 
 class _Item:
-    __slots__ = ("req", "position", "step", "depth", "hidden", "token")
+    __slots__ = ("req", "position", "step", "depth", "hidden", "token", "pending")
 
     def __init__(self, req: _Req, position: int, depth: int | None, hidden: int, token: int):
         self.req = req
@@ -164,6 +164,30 @@ class _Item:
         self.depth = depth
         self.hidden = hidden
         self.token = token
+        # Delayed gate consumption: the live decision of the item's previous step, as
+        # (staged launch decisions, row), consumed at the routing after the following launch.
+        self.pending: tuple[_StagedDecisions, int] | None = None
+
+
+class _StagedDecisions:
+    """One recurrent launch's live exit decisions, copied to pinned host memory on the engine
+    stream without waiting (``stage_delayed_exit_signals``, ``continuous_api.py:1117-1122``).
+    The host reads them one launch later, by which time the copy has normally landed."""
+
+    def __init__(self, values: torch.Tensor, stream: torch.cuda.Stream, decide) -> None:
+        self.host = torch.empty(values.shape, dtype=values.dtype, pin_memory=True)
+        with torch.cuda.stream(stream):
+            self.host.copy_(values, non_blocking=True)
+            self.event = torch.cuda.Event()
+            self.event.record(stream)
+        self.decide = decide  # (row, host values) -> bool
+        self._vals: list | None = None
+
+    def get(self, row: int) -> bool:
+        if self._vals is None:
+            self.event.synchronize()
+            self._vals = self.host.tolist()
+        return self.decide(row, self._vals)
 
 
 class ContinuousDepthBatchingEngine:
@@ -291,6 +315,10 @@ class ContinuousDepthBatchingEngine:
         self._gate_live = cfg.exit_threshold is not None and (
             model_kwargs is None or model_kwargs.get("use_early_exit_gate", True)
         )
+        # The reference's default timing (use_async_batching with delay_gate_consumption): a step's
+        # exit decision is applied at the routing after the item's next launch
+        # (ExitPolicy.delayed_transport_enabled, exit_policy.py:76-80).
+        self._delayed = bool(cfg.use_async_batching and cfg.delay_gate_consumption)
         reqs: list[_Req] = []
         base = 0
         for i, (p, m) in enumerate(zip(input_ids, caps, strict=True)):
@@ -637,7 +665,53 @@ class ContinuousDepthBatchingEngine:
             st.mixed_recurrent_depth_histogram[k] += v
         if not self._gate_live:
             return None
+        if self._delayed:
+            return self._stage_live_decisions(items)
         return self._live_decisions(items)
+
+    def _hazard_flags(self, items: list[_Item]) -> torch.Tensor:
+        """Cumulative-hazard decisions of this launch's gate logits, on device (``cdb_exit_hazard``)."""
+
+        r = self.runner
+        cfg = self.cdb_config
+        n = len(items)
+        meta = r.upload([[it.hidden for it in items], [it.step for it in items], [int(it.step == 0) for it in items]])
+        meta = meta.view(3, n)
+        if not hasattr(self, "_hz"):
+            self._hz = (
+                torch.zeros(r.bank_slots, dtype=torch.float64, device=r.device),
+                torch.ones(r.bank_slots, dtype=torch.float64, device=r.device),
+                torch.zeros(cfg.max_num_seqs, dtype=torch.int8, device=r.device),
+            )
+        cdf, surv, flags = self._hz
+        from . import _lib
+
+        with torch.cuda.stream(r.stream):
+            reset = meta[2].to(torch.int8)
+            _lib.call(
+                "cdb_exit_hazard", _lib.ptr(r.gate_out), 1, _lib.ptr(meta[0]), _lib.ptr(meta[1]), _lib.ptr(reset),
+                _lib.ptr(cdf), _lib.ptr(surv), _lib.ptr(flags), n, cfg.min_recurrent_steps, float(cfg.exit_threshold),
+                r.stream.cuda_stream,
+            )
+        return flags[:n]
+
+    def _stage_live_decisions(self, items: list[_Item]) -> _StagedDecisions:
+        """Delayed consumption: decide this launch's signals on device now (the per-token policy
+        state advances in step order, as the reference's deferred ``should_exit`` calls advance
+        it) and stage them to the host; routing reads them after the next launch."""
+
+        r = self.runner
+        cfg = self.cdb_config
+        n = len(items)
+        if isinstance(self.shape, HuginnShape):
+            steps = [it.step for it in items]
+            tau, min_steps = float(cfg.exit_threshold), cfg.min_recurrent_steps
+            with torch.cuda.stream(r.stream):
+                sig = r.gate_out[:n].float()
+            return _StagedDecisions(
+                sig, r.stream, lambda i, v: steps[i] + 1 >= min_steps and v[i] < tau
+            )
+        return _StagedDecisions(self._hazard_flags(items), r.stream, lambda i, v: bool(v[i]))
 
     def _live_decisions(self, items: list[_Item]) -> list[bool]:
         """Live exit decisions (``ExitPolicy.should_exit``, ``exit_policy.py:150-169``).
@@ -657,28 +731,22 @@ class ContinuousDepthBatchingEngine:
                 it.step + 1 >= cfg.min_recurrent_steps and sig < float(cfg.exit_threshold)
                 for it, sig in zip(items, signals, strict=True)
             ]
-        meta = r.upload([[it.hidden for it in items], [it.step for it in items], [int(it.step == 0) for it in items]])
-        meta = meta.view(3, n)
-        if not hasattr(self, "_hz"):
-            self._hz = (
-                torch.zeros(r.bank_slots, dtype=torch.float64, device=r.device),
-                torch.ones(r.bank_slots, dtype=torch.float64, device=r.device),
-                torch.zeros(cfg.max_num_seqs, dtype=torch.int8, device=r.device),
-            )
-        cdf, surv, flags = self._hz
-        from . import _lib
-
         with torch.cuda.stream(r.stream):
-            reset = meta[2].to(torch.int8)
-            _lib.call(
-                "cdb_exit_hazard", _lib.ptr(r.gate_out), 1, _lib.ptr(meta[0]), _lib.ptr(meta[1]), _lib.ptr(reset),
-                _lib.ptr(cdf), _lib.ptr(surv), _lib.ptr(flags), n, cfg.min_recurrent_steps, float(cfg.exit_threshold),
-                r.stream.cuda_stream,
-            )
-            host = flags[:n].cpu()
+            host = self._hazard_flags(items).cpu()
         return [bool(x) for x in host.tolist()]
 
-    def _should_exit(self, it: _Item, step: int, live: list[bool] | None, i: int) -> bool:
+    def _should_exit(self, it: _Item, step: int, live, i: int) -> bool:
+        if self._delayed:
+            # Delayed consumption (continuous_api.py:1124-1160, 1250-1280): route on the decision
+            # of the item's previous step; this step's live decision is kept for the next routing.
+            pend, it.pending = it.pending, None
+            if isinstance(live, _StagedDecisions):
+                it.pending = (live, i)
+            if step == self.steps - 1:
+                return True
+            if it.depth is not None:
+                return step >= it.depth + 1  # the pending replay step (step - 1) reached the depth
+            return pend is not None and pend[0].get(pend[1])
         if step == self.steps - 1:
             return True
         if it.depth is not None:
@@ -855,7 +923,50 @@ class ContinuousDepthBatchingEngine:
                 batch.append(self.ready.popleft())
         return batch
 
+    def _carry_successor(self, r: _Req) -> _Item | None:
+        """Stage the next decode token of ``r`` ahead of its wave (eager re-entry,
+        ``_select_eager_reentries``, ``continuous_api.py:1304-1327``): allocate its KV block now;
+        None when no block is free (a later wave's cohort scan picks it up)."""
+
+        if not self._alloc_one_decode(r):
+            return None
+        return _Item(r, r.position, r.next_depth(), self.free_hidden.pop(), self._next_token_id(r))
+
+    def _carry_after_prefill(self, sampled: list[_Req], budget: int) -> list[_Item]:
+        """Delayed no-refill path: each prefilled request's first decode token is carried into
+        this iteration's wave, up to ``budget`` items (``continuous_api.py:763-781``)."""
+
+        carried = []
+        for r in sampled:
+            if r.status == RequestStatus.FINISHED:
+                continue
+            if self._record_token(r):
+                self._retire(r)
+                continue
+            if len(carried) < budget and (it := self._carry_successor(r)) is not None:
+                carried.append(it)
+        return carried
+
+    def _carry_after_coda(self, items: list[_Item]) -> list[_Item]:
+        """Delayed no-refill path: the wave's exiters' successors, staged at the boundary coda in
+        exit order, lead the next wave (``continuous_api.py:929-940``)."""
+
+        carried = []
+        for it in items:
+            r = it.req
+            self.free_hidden.append(it.hidden)
+            if r.status == RequestStatus.FINISHED:
+                continue
+            r.position += 1
+            if self._record_token(r):
+                self._retire(r)
+                continue
+            if (nxt := self._carry_successor(r)) is not None:
+                carried.append(nxt)
+        return carried
+
     def _no_refill_loop(self, arrivals) -> None:
+        carried: list[_Item] = []  # delayed path: successors staged before their wave
         while arrivals or self._has_pending():
             self._release_arrivals(arrivals)
             if not self._has_pending():
@@ -871,11 +982,20 @@ class ContinuousDepthBatchingEngine:
                 sampled = self._run_prefill(pb)
                 for r, *_ in pb:
                     self.in_flight.discard(r.idx)
-                self._consume_prefill(sampled, stage=False)
+                if self._delayed:
+                    carried += self._carry_after_prefill(sampled, max(0, self.max_num_seqs - len(carried)))
+                else:
+                    self._consume_prefill(sampled, stage=False)
                 did_prefill = True
-            cohort = [r for r in self.active.values() if r.status == RequestStatus.DECODING and r.generated > 0]
-            cohort = cohort[: self.max_num_seqs]
-            items = [self._stage_decode(r) for r in cohort]
+            carried_ids = {it.req.idx for it in carried}
+            cohort = [
+                r
+                for r in self.active.values()
+                if r.status == RequestStatus.DECODING and r.generated > 0 and r.idx not in carried_ids
+            ]
+            cohort = cohort[: max(0, self.max_num_seqs - len(carried))]
+            items = carried + [self._stage_decode(r) for r in cohort]
+            carried = []
             if not items:
                 if not did_prefill and self._has_pending() and not arrivals:
                     raise CacheFullError("No-refill loop stalled with pending work (over-subscribed KV cache)")
@@ -902,7 +1022,10 @@ class ContinuousDepthBatchingEngine:
                 if not survivors:
                     break
             self._run_coda(exited)
-            self._consume_coda(exited, stage=False)
+            if self._delayed:
+                carried = self._carry_after_coda(exited)
+            else:
+                self._consume_coda(exited, stage=False)
 
     # ------------------------------------------------------------------ validation
     def _validate(self, input_ids, max_new_tokens, exit_depths, model_kwargs) -> None:
@@ -942,12 +1065,13 @@ class ContinuousDepthBatchingEngine:
                     raise ValueError(f"exit_depths[{idx}] value {d} is out of range [0, {steps}); values are 0-based")
         if copies_exit_kv(cfg.kv_policy):
             return
+        extra = int(cfg.use_async_batching and cfg.delay_gate_consumption)  # continuous_api.py:1826
         for depths in exit_depths:
             for d in depths:
-                if d + 1 < cfg.kv_slots_per_layer:
+                if d + 1 + extra < cfg.kv_slots_per_layer:
                     raise ValueError(
                         "Every replay exit depth must write all static KV slots before exit: "
-                        f"kv_slots_per_layer={cfg.kv_slots_per_layer}, exit step {d + 1}"
+                        f"kv_slots_per_layer={cfg.kv_slots_per_layer}, exit step {d + 1 + extra}"
                     )
 
 

@@ -1,10 +1,11 @@
-"""CPU restatement of the reference CDB engine in its synchronous mode.
+"""CPU restatement of the reference CDB engine (synchronous and delayed-gate timing).
 
 TEST INFRASTRUCTURE ONLY: the checker for the CUDA engine's schedules, block tables and
 logits. Nothing in the product imports this module.
 
 It restates ``ContinuousDepthBatchingEngine`` with ``use_async_batching=False`` (every
-stage synchronous, the mode the reference's CPU tests and replay parity use):
+stage synchronous), and with ``OracleConfig.delayed`` the reference's default timing
+(``use_async_batching`` + ``delay_gate_consumption``: decisions applied one launch late):
 
 * refill loop ``continuous_depth_batching/continuous_api.py:503-606`` with
   ``CDBScheduler.schedule_next`` ``scheduler.py:101-140`` (coda >= min -> prefill if admitted
@@ -90,6 +91,9 @@ class OracleConfig:
     kv_policy: str = "single"
     kv_slots_per_layer: int | None = None
     kv_pressure_mode: str = "recompute"
+    # use_async_batching and delay_gate_consumption both on (the reference's defaults): every
+    # exit decision is applied at the routing after the item's next launch.
+    delayed: bool = False
 
 
 @dataclass
@@ -126,6 +130,8 @@ class Item:
     hidden: torch.Tensor | None = None
     cdf: float = 0.0
     survival: float = 1.0
+    pending_step: int | None = None  # delayed: the step whose decision is still to be applied
+    pending_signal: torch.Tensor | None = None
 
 
 class OracleEngine:
@@ -368,19 +374,42 @@ class OracleEngine:
         return gate
 
     def _should_exit(self, item: Item, step: int, gate: torch.Tensor | None, i: int) -> bool:
+        if self.cfg.delayed:
+            return self._should_exit_delayed(item, step, gate, i)
         if step == self.cfg.max_recurrent_steps - 1:
             return True
         if item.depth is not None:
             return step >= item.depth
         if self.cfg.exit_threshold is None:
             return False
-        can_exit = step + 1 >= self.cfg.min_recurrent_steps
+        return self._policy(item, step, gate[i])
+
+    def _policy(self, item: Item, source_step: int, signal: torch.Tensor) -> bool:
+        """``ExitPolicy.should_exit`` (``exit_policy.py:150-169``) for one signal of ``source_step``."""
+
+        can_exit = source_step + 1 >= self.cfg.min_recurrent_steps
         if self.huginn:
-            return can_exit and float(gate[i].float().item()) < self.cfg.exit_threshold
-        hazard = float(torch.sigmoid(gate[i]).float().item())
+            return can_exit and float(signal.float().item()) < self.cfg.exit_threshold
+        hazard = float(torch.sigmoid(signal).float().item())
         item.cdf += hazard * item.survival
         item.survival *= 1.0 - hazard
         return can_exit and item.cdf >= self.cfg.exit_threshold
+
+    def _should_exit_delayed(self, item: Item, step: int, gate: torch.Tensor | None, i: int) -> bool:
+        """Delayed consumption: ``_consume_delayed_gate`` / ``_consume_delayed_synthetic_exit``
+        (``continuous_api.py:1699-1724``) route on the previous step's pending decision, then
+        ``_schedule_after_delayed_*_step`` (``:1250-1280``) keep this step's for the next routing."""
+
+        pend_step, pend_sig = item.pending_step, item.pending_signal
+        item.pending_step = step
+        item.pending_signal = gate[i] if gate is not None else None
+        if step == self.cfg.max_recurrent_steps - 1:
+            return True
+        if item.depth is not None:
+            return pend_step is not None and pend_step >= item.depth
+        if self.cfg.exit_threshold is None or pend_sig is None:
+            return False
+        return self._policy(item, pend_step, pend_sig)
 
     def _record_exit(self, item: Item, step: int) -> None:
         item.req.exit_depths.append(step)
@@ -536,7 +565,18 @@ class OracleEngine:
                 batch.append(self.ready.popleft())
         return batch
 
+    def _carry_successor(self, r: Req) -> Item | None:
+        """Eager re-entry (``_select_eager_reentries``, ``continuous_api.py:1304-1327``)."""
+
+        if not self._alloc_one_decode(r):
+            return None
+        return Item(req=r, token=r.to_process[0], position=r.position, step=0, depth=r.next_depth())
+
     def _no_refill_loop(self) -> None:
+        # Delayed mode carries a wave's exiters' successors (staged at its boundary coda, in exit
+        # order) and each prefilled request's first decode token (up to the launch width) into
+        # the next wave ahead of the cohort scan (``continuous_api.py:721-790, 815-944``).
+        carried: list[Item] = []
         while self._has_pending():
             did_prefill = False
             while self._admit_prefill():
@@ -547,11 +587,29 @@ class OracleEngine:
                 res = self._run_prefill(pb)
                 for r, *_ in pb:
                     self.in_flight.discard(r.idx)
-                self._consume_prefill(res, stage=False)
+                if self.cfg.delayed:
+                    budget = max(0, self.max_num_seqs - len(carried))
+                    for r, tok in res:
+                        if r.status == FINISHED:
+                            continue
+                        if self._update(r, self._next_token(r, tok)):
+                            self._retire(r)
+                            continue
+                        if budget > 0 and (it := self._carry_successor(r)) is not None:
+                            carried.append(it)
+                            budget -= 1
+                else:
+                    self._consume_prefill(res, stage=False)
                 did_prefill = True
-            cohort = [r for r in self.active.values() if r.status == DECODING and r.to_process and r.to_process[0] >= 0]
-            cohort = cohort[: self.max_num_seqs]
-            items = [self._stage_decode(r) for r in cohort]
+            carried_ids = {it.req.idx for it in carried}
+            cohort = [
+                r
+                for r in self.active.values()
+                if r.status == DECODING and r.to_process and r.to_process[0] >= 0 and r.idx not in carried_ids
+            ]
+            cohort = cohort[: max(0, self.max_num_seqs - len(carried))]
+            items = carried + [self._stage_decode(r) for r in cohort]
+            carried = []
             if not items:
                 if not did_prefill and self._has_pending():
                     raise RuntimeError("oracle: no-refill loop stalled")
@@ -575,7 +633,19 @@ class OracleEngine:
                 if not survivors:
                     break
             toks = self._run_coda(exited)
-            self._consume_coda(exited, toks, stage=False)
+            if self.cfg.delayed:
+                for it, tok in zip(exited, toks, strict=True):
+                    r = it.req
+                    if r.status == FINISHED:
+                        continue
+                    r.position += 1
+                    if self._update(r, self._next_token(r, tok)):
+                        self._retire(r)
+                        continue
+                    if (nxt := self._carry_successor(r)) is not None:
+                        carried.append(nxt)
+            else:
+                self._consume_coda(exited, toks, stage=False)
 
     def generate(
         self,

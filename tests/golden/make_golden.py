@@ -10,11 +10,13 @@ seeded weights from :func:`continuous_depth_batching_b200.ouro.random_ouro_state
 registers the CPU restatement of the paged FlashAttention contract
 (:mod:`oracle.paged_attention`; FlashAttention-3 is a binary the image does not have) and
 drives the reference ``ContinuousDepthBatchingEngine.generate_batch`` in its synchronous mode
-(``use_async_batching=False``). Each run records the generated tokens, per-token exit depths,
+(``use_async_batching=False``) or, with ``--async``, its default delayed-gate mode. Each run records the generated tokens, per-token exit depths,
 engine stats, the launch trace (every prefill, recurrent and coda launch with its items,
 positions, recurrent steps and block-table rows) and the logits of every LM-head call.
 
-Outputs: ``tests/golden/ouro_cfg0.json`` (traces) and ``tests/golden/ouro_cfg0_logits.npz``.
+Outputs: ``tests/golden/ouro_cfg0.json`` (traces) and ``tests/golden/ouro_cfg0_logits.npz``;
+with ``--async`` the reference's default timing (``use_async_batching=True``,
+``delay_gate_consumption=True``) into ``ouro_cfg0_async.json`` / ``ouro_cfg0_async_logits.npz``.
 The GPU box has no reference checkout; the tests only read these files.
 """
 
@@ -158,7 +160,9 @@ class Recorder:
         lm_head.forward = lm_forward
 
 
-def run_case(name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_depths=None, num_blocks=4096):
+def run_case(
+    name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_depths=None, num_blocks=4096, async_mode=False
+):
     from looped_cdb.continuous_depth_batching import ContinuousDepthBatchingConfig, ContinuousDepthBatchingEngine
 
     model = build_reference_model(CFG0, kv_policy)
@@ -169,7 +173,7 @@ def run_case(name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_d
         max_recurrent_steps=CFG0.total_ut_steps,
         exit_threshold=0.5 if live_gate else None,
         synthetic_exit_replay=not live_gate,
-        use_async_batching=False,
+        use_async_batching=async_mode,
         use_cuda_graph=False,
         use_cuda_graph_prefill=False,
         refill=refill,
@@ -192,6 +196,7 @@ def run_case(name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_d
         "kv_policy": kv_policy,
         "refill": refill,
         "live_gate": live_gate,
+        "async": async_mode,
         "tokens": [o.generated_tokens for o in outs],
         "exit_depths": exit_depths,
         "stats": {
@@ -224,26 +229,53 @@ def recorded_exit_depths(result: dict) -> list[list[int]]:
     return depths
 
 
+def replay_depths(result: dict, async_mode: bool) -> list[list[int]]:
+    """Replay depths that reproduce a live run. With delayed gate consumption (async mode) a
+    replayed depth d exits at step d + 1, so the depths are the recorded exit steps minus one."""
+
+    depths = recorded_exit_depths(result)
+    return [[s - 1 for s in ds] for ds in depths] if async_mode else depths
+
+
 def main() -> None:
+    """``python tests/golden/make_golden.py [--async]``: the synchronous runs, or with ``--async``
+    the same runs under the reference's default timing (use_async_batching=True,
+    delay_gate_consumption=True) plus a live-gate no-refill run, into ``ouro_cfg0_async.*``."""
+
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    async_mode = "--async" in sys.argv[1:]
+    sfx = "_async" if async_mode else ""
     runs = []
     logits_out: dict[str, np.ndarray] = {}
 
-    live, live_logits = run_case("live_gate_refill", kv_policy="single", refill=True, live_gate=True)
+    live, live_logits = run_case(
+        "live_gate_refill" + sfx, kv_policy="single", refill=True, live_gate=True, async_mode=async_mode
+    )
     runs.append(live)
-    depths = recorded_exit_depths(live)
+    depths = replay_depths(live, async_mode)
 
     replay, replay_logits = run_case(
-        "replay_refill", kv_policy="single", refill=True, live_gate=False, exit_depths=depths
+        "replay_refill" + sfx, kv_policy="single", refill=True, live_gate=False, exit_depths=depths,
+        async_mode=async_mode,
     )
     runs.append(replay)
-    norefill, _ = run_case("replay_norefill", kv_policy="single", refill=False, live_gate=False, exit_depths=depths)
+    norefill, _ = run_case(
+        "replay_norefill" + sfx, kv_policy="single", refill=False, live_gate=False, exit_depths=depths,
+        async_mode=async_mode,
+    )
     runs.append(norefill)
-    lastx, _ = run_case("replay_last_exited", kv_policy="last_exited", refill=True, live_gate=False, exit_depths=depths)
+    lastx, _ = run_case(
+        "replay_last_exited" + sfx, kv_policy="last_exited", refill=True, live_gate=False, exit_depths=depths,
+        async_mode=async_mode,
+    )
     runs.append(lastx)
+    if async_mode:
+        live_nr, _ = run_case("live_gate_norefill" + sfx, kv_policy="single", refill=False, live_gate=True,
+                              async_mode=True)
+        runs.append(live_nr)
 
     for i, arr in enumerate(live_logits[:6]):
-        logits_out[f"live_gate_refill_{i}"] = arr.astype(np.float32)
+        logits_out[f"live_gate_refill{sfx}_{i}"] = arr.astype(np.float32)
     prompts, max_new = config0_workload()
     payload = {
         "generator": "tests/golden/make_golden.py",
@@ -256,9 +288,9 @@ def main() -> None:
         "num_blocks": 4096,
         "runs": runs,
     }
-    (HERE / "ouro_cfg0.json").write_text(json.dumps(payload, separators=(",", ":")))
-    np.savez_compressed(HERE / "ouro_cfg0_logits.npz", **logits_out)
-    print("wrote", HERE / "ouro_cfg0.json", "runs:", [r["name"] for r in runs])
+    (HERE / f"ouro_cfg0{sfx}.json").write_text(json.dumps(payload, separators=(",", ":")))
+    np.savez_compressed(HERE / f"ouro_cfg0{sfx}_logits.npz", **logits_out)
+    print("wrote", HERE / f"ouro_cfg0{sfx}.json", "runs:", [r["name"] for r in runs])
     for r in runs:
         print(r["name"], r["stats"])
 

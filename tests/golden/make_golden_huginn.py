@@ -33,7 +33,7 @@ sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(HERE))
 sys.path.insert(0, os.environ.get("CDB_REFERENCE_SRC", "/root/reference/src"))
 
-from make_golden import Recorder, recorded_exit_depths  # noqa: E402
+from make_golden import Recorder, replay_depths  # noqa: E402
 
 from continuous_depth_batching_b200.huginn import HuginnShape, random_huginn_state_dict  # noqa: E402
 from oracle.paged_attention import cpu_paged_attention_forward  # noqa: E402
@@ -96,7 +96,9 @@ def build_reference_model(shape: HuginnShape):
     return model
 
 
-def run_case(name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_depths=None, num_blocks=4096):
+def run_case(
+    name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_depths=None, num_blocks=4096, async_mode=False
+):
     from looped_cdb.continuous_depth_batching import ContinuousDepthBatchingConfig, ContinuousDepthBatchingEngine
 
     model = build_reference_model(SMALL)
@@ -107,7 +109,7 @@ def run_case(name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_d
         max_recurrent_steps=SMALL.total_recurrent_steps,
         exit_threshold=EXIT_THRESHOLD if live_gate else None,
         synthetic_exit_replay=not live_gate,
-        use_async_batching=False,
+        use_async_batching=async_mode,
         use_cuda_graph=False,
         use_cuda_graph_prefill=False,
         refill=refill,
@@ -127,6 +129,7 @@ def run_case(name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_d
         "kv_policy": kv_policy,
         "refill": refill,
         "live_gate": live_gate,
+        "async": async_mode,
         "tokens": [o.generated_tokens for o in outs],
         "exit_depths": exit_depths,
         "stats": {
@@ -145,20 +148,34 @@ def run_case(name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_d
 
 
 def main() -> None:
+    """``python tests/golden/make_golden_huginn.py [--async]`` (``--async``: the reference's default
+    delayed-gate timing, plus a live-gate no-refill run, into ``huginn_small_async.*``)."""
+
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    async_mode = "--async" in sys.argv[1:]
+    sfx = "_async" if async_mode else ""
     runs = []
     logits_out: dict[str, np.ndarray] = {}
-    live, live_logits = run_case("live_gate_refill", kv_policy="single", refill=True, live_gate=True)
+    live, live_logits = run_case(
+        "live_gate_refill" + sfx, kv_policy="single", refill=True, live_gate=True, async_mode=async_mode
+    )
     runs.append(live)
-    depths = recorded_exit_depths(live)
-    replay, _ = run_case("replay_refill", kv_policy="single", refill=True, live_gate=False, exit_depths=depths)
-    runs.append(replay)
-    norefill, _ = run_case("replay_norefill", kv_policy="single", refill=False, live_gate=False, exit_depths=depths)
-    runs.append(norefill)
-    lastx, _ = run_case("replay_last_exited", kv_policy="last_exited", refill=True, live_gate=False, exit_depths=depths)
-    runs.append(lastx)
+    depths = replay_depths(live, async_mode)
+    for name, policy, refill in (
+        ("replay_refill", "single", True),
+        ("replay_norefill", "single", False),
+        ("replay_last_exited", "last_exited", True),
+    ):
+        res, _ = run_case(
+            name + sfx, kv_policy=policy, refill=refill, live_gate=False, exit_depths=depths, async_mode=async_mode
+        )
+        runs.append(res)
+    if async_mode:
+        live_nr, _ = run_case("live_gate_norefill" + sfx, kv_policy="single", refill=False, live_gate=True,
+                              async_mode=True)
+        runs.append(live_nr)
     for i, arr in enumerate(live_logits[:6]):
-        logits_out[f"live_gate_refill_{i}"] = arr.astype(np.float32)
+        logits_out[f"live_gate_refill{sfx}_{i}"] = arr.astype(np.float32)
     prompts, max_new = config0_workload()
     shape = dict(SMALL.__dict__)
     payload = {
@@ -173,9 +190,9 @@ def main() -> None:
         "num_blocks": 4096,
         "runs": runs,
     }
-    (HERE / "huginn_small.json").write_text(json.dumps(payload, separators=(",", ":")))
-    np.savez_compressed(HERE / "huginn_small_logits.npz", **logits_out)
-    print("wrote", HERE / "huginn_small.json", "runs:", [r["name"] for r in runs])
+    (HERE / f"huginn_small{sfx}.json").write_text(json.dumps(payload, separators=(",", ":")))
+    np.savez_compressed(HERE / f"huginn_small{sfx}_logits.npz", **logits_out)
+    print("wrote", HERE / f"huginn_small{sfx}.json", "runs:", [r["name"] for r in runs])
     for r in runs:
         print(r["name"], r["stats"])
 

@@ -37,7 +37,7 @@ def _golden():
 
 
 def _engine(shape, sd, *, kv_policy="single", refill=True, live=False, num_blocks=4096, max_model_len=2048, graphs=True,
-            gemm="cublas"):
+            gemm="cublas", async_mode=False):
     model = OuroForCausalLM(shape)
     model.load_state_dict({k: v.to(torch.float32) for k, v in sd.items()})
     cfg = ContinuousDepthBatchingConfig(
@@ -46,7 +46,7 @@ def _engine(shape, sd, *, kv_policy="single", refill=True, live=False, num_block
         max_recurrent_steps=shape.total_ut_steps,
         exit_threshold=0.5 if live else None,
         synthetic_exit_replay=not live,
-        use_async_batching=False,
+        use_async_batching=async_mode,
         use_cuda_graph=graphs,
         refill=refill,
         kv_policy=kv_policy,
@@ -97,6 +97,67 @@ def test_device_block_table_mirrors_host_lists():
     eng.generate_batch(data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"])
     assert sum(checked) == run["stats"]["recurrent_steps"]
     assert eng.pool.tables == {}  # every request retired and released its blocks
+
+
+@pytest.mark.parametrize("name", ["replay_refill_async", "replay_norefill_async", "replay_last_exited_async"])
+def test_async_schedule_matches_reference(name):
+    """The reference's default timing (use_async_batching + delay_gate_consumption): decisions
+    applied one launch late, no-refill waves led by the previous wave's exiters in exit order.
+    Launch traces and block tables equal ``tests/golden/ouro_cfg0_async.json`` bit for bit."""
+
+    data = json.loads((GOLDEN / "ouro_cfg0_async.json").read_text())
+    shape = OuroShape(**data["shape"])
+    run = next(r for r in data["runs"] if r["name"] == name)
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+    eng = _engine(shape, sd, kv_policy=run["kv_policy"], refill=run["refill"], async_mode=True)
+    eng.record_trace = True
+    outs = eng.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"]
+    )
+    assert eng.launch_trace == run["launches"]
+    assert [len(o.generated_tokens) for o in outs] == data["max_new_tokens"]
+    hist = {str(k): v for k, v in sorted(eng.last_stats.exit_depth_histogram.items())}
+    assert hist == run["stats"]["exit_depth_histogram"]
+    assert eng.last_stats.scheduler_refills == run["stats"]["scheduler_refills"]
+
+
+def exit_agreement(outs, run) -> float:
+    """Fraction of tokens whose exit step equals the reference run's (read from its coda launches)."""
+
+    ref = [[] for _ in run["tokens"]]
+    for launch in run["launches"]:
+        if launch["kind"] == "coda":
+            for req, _pos, step in launch["items"]:
+                ref[req].append(step)
+    pairs = [(a, b) for o, r in zip(outs, ref, strict=True) for a, b in zip(o.exit_depths, r, strict=True)]
+    assert len(pairs) == sum(len(r) for r in ref)
+    return sum(int(a == b) for a, b in pairs) / len(pairs)
+
+
+@pytest.mark.parametrize(
+    "fixture,name,refill",
+    [
+        ("ouro_cfg0.json", "live_gate_refill", True),
+        ("ouro_cfg0_async.json", "live_gate_refill_async", True),
+        ("ouro_cfg0_async.json", "live_gate_norefill_async", False),
+    ],
+)
+def test_live_hazard_gate_matches_reference_decisions(fixture, name, refill):
+    """Live cumulative-hazard gate on device, teacher-forced on the reference's tokens: the exit
+    step of each token equals the reference's at >= 95% of tokens (a gate logit within bf16
+    noise of the threshold may flip). Async runs consume each decision one launch late."""
+
+    data = json.loads((GOLDEN / fixture).read_text())
+    shape = OuroShape(**data["shape"])
+    run = next(r for r in data["runs"] if r["name"] == name)
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+    eng = _engine(shape, sd, refill=refill, live=True, async_mode=run.get("async", False))
+    outs = eng.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, forced_tokens=run["tokens"]
+    )
+    agree = exit_agreement(outs, run)
+    print({"run": name, "exit_agreement": agree})
+    assert agree >= 0.95
 
 
 def _oracle(shape, sd, prompts, max_new, depths, dtype, forced=None, kv_policy="single"):

@@ -38,7 +38,7 @@ def _golden():
 
 
 def _engine(shape, sd, *, kv_policy="single", refill=True, threshold=None, num_blocks=4096, max_model_len=2048,
-            graphs=True):
+            graphs=True, async_mode=False):
     model = HuginnForCausalLM(shape)
     model.load_state_dict({k: v.to(torch.float32) for k, v in sd.items()})
     cfg = ContinuousDepthBatchingConfig(
@@ -47,7 +47,7 @@ def _engine(shape, sd, *, kv_policy="single", refill=True, threshold=None, num_b
         max_recurrent_steps=shape.total_recurrent_steps,
         exit_threshold=threshold,
         synthetic_exit_replay=threshold is None,
-        use_async_batching=False,
+        use_async_batching=async_mode,
         use_cuda_graph=graphs,
         refill=refill,
         kv_policy=kv_policy,
@@ -148,4 +148,43 @@ def test_huginn_live_latent_gate_matches_reference_decisions():
     assert len(pairs) == sum(len(x) for x in ref_depths)
     agree = sum(int(a == b) for a, b in pairs) / len(pairs)
     print({"exit_agreement": agree, "tokens": len(pairs)})
+    assert agree >= 0.95
+
+
+def _golden_async():
+    data = json.loads((GOLDEN / "huginn_small_async.json").read_text())
+    return data, HuginnShape(**data["shape"])
+
+
+@pytest.mark.parametrize("name", ["replay_refill_async", "replay_norefill_async", "replay_last_exited_async"])
+def test_huginn_async_schedule_matches_reference(name):
+    """The reference's default delayed-gate timing, bit-exact against huginn_small_async.json."""
+
+    data, shape = _golden_async()
+    run = next(r for r in data["runs"] if r["name"] == name)
+    sd = random_huginn_state_dict(shape, seed=0, embed_std=data["embed_std"])
+    eng = _engine(shape, sd, kv_policy=run["kv_policy"], refill=run["refill"], async_mode=True)
+    eng.record_trace = True
+    eng.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"]
+    )
+    assert eng.launch_trace == run["launches"]
+    hist = {str(k): v for k, v in sorted(eng.last_stats.exit_depth_histogram.items())}
+    assert hist == run["stats"]["exit_depth_histogram"]
+    assert eng.last_stats.scheduler_refills == run["stats"]["scheduler_refills"]
+
+
+@pytest.mark.parametrize("name,refill", [("live_gate_refill_async", True), ("live_gate_norefill_async", False)])
+def test_huginn_async_live_gate_matches_reference_decisions(name, refill):
+    from tests.test_gpu_engine import exit_agreement
+
+    data, shape = _golden_async()
+    run = next(r for r in data["runs"] if r["name"] == name)
+    sd = random_huginn_state_dict(shape, seed=0, embed_std=data["embed_std"])
+    eng = _engine(shape, sd, refill=refill, threshold=data["exit_threshold"], async_mode=True)
+    outs = eng.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, forced_tokens=run["tokens"]
+    )
+    agree = exit_agreement(outs, run)
+    print({"run": name, "exit_agreement": agree})
     assert agree >= 0.95

@@ -1,7 +1,9 @@
 """Pin the CPU oracle against fixtures recorded from the reference engine itself.
 
 ``tests/golden/make_golden.py`` ran the reference ``ContinuousDepthBatchingEngine`` (BASELINE
-config 0 shape, seeded weights, synchronous mode) and recorded every launch. The oracle must
+config 0 shape, seeded weights) and recorded every launch, in the synchronous mode
+(``ouro_cfg0.json``) and in the reference's default delayed-gate mode (``use_async_batching`` +
+``delay_gate_consumption``, ``ouro_cfg0_async.json``). The oracle must
 reproduce each run exactly: generated tokens, the ordered launch trace with every item's
 (request, position, recurrent step) and block-table row, refill counts, exit histograms, and
 (fp32) the LM-head logits.
@@ -22,12 +24,21 @@ from oracle.engine import OracleConfig, OracleEngine, exit_depth_histogram
 GOLDEN = Path(__file__).resolve().parent / "golden"
 
 
-@pytest.fixture(scope="module")
-def golden():
-    data = json.loads((GOLDEN / "ouro_cfg0.json").read_text())
+def _load_ouro(name: str):
+    data = json.loads((GOLDEN / name).read_text())
     shape = OuroShape(**data["shape"])
     sd = random_ouro_state_dict(shape, seed=data["weights_seed"], gate_std=data["gate_std"])
     return data, shape, sd
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return _load_ouro("ouro_cfg0.json")
+
+
+@pytest.fixture(scope="module")
+def golden_async():
+    return _load_ouro("ouro_cfg0_async.json")
 
 
 def _config(run: dict, data: dict) -> OracleConfig:
@@ -41,7 +52,38 @@ def _config(run: dict, data: dict) -> OracleConfig:
         refill=run["refill"],
         kv_policy=run["kv_policy"],
         kv_pressure_mode="reserve" if run["kv_policy"] == "last_exited" else "recompute",
+        delayed=run.get("async", False),
     )
+
+
+ASYNC_RUNS = [
+    "live_gate_refill_async",
+    "replay_refill_async",
+    "replay_norefill_async",
+    "replay_last_exited_async",
+    "live_gate_norefill_async",
+]
+
+
+@pytest.mark.parametrize("name", ASYNC_RUNS)
+def test_oracle_reproduces_reference_async_run(golden_async, name):
+    """Delayed gate consumption: every decision applied one launch late; no-refill waves lead
+    with the previous wave's exiters in exit order."""
+
+    data, shape, sd = golden_async
+    run = next(r for r in data["runs"] if r["name"] == name)
+    engine = OracleEngine(shape, sd, _config(run, data), torch.float32)
+    tokens = engine.generate(data["prompts"], data["max_new_tokens"], exit_depths=run["exit_depths"])
+    assert tokens == run["tokens"]
+    assert engine.launches == run["launches"]
+    assert exit_depth_histogram(engine) == run["stats"]["exit_depth_histogram"]
+    assert engine.refills == run["stats"]["scheduler_refills"]
+    assert engine.stats["recurrent_batches"] == run["stats"]["recurrent_batches"]
+    assert engine.stats["coda_batches"] == run["stats"]["coda_batches"]
+    if name == "live_gate_refill_async":
+        logits = np.load(GOLDEN / "ouro_cfg0_async_logits.npz")
+        for i in range(6):
+            np.testing.assert_allclose(engine.logits[i][1].numpy(), logits[f"{name}_{i}"], rtol=0, atol=1e-5)
 
 
 @pytest.mark.parametrize("name", ["live_gate_refill", "replay_refill", "replay_norefill", "replay_last_exited"])
@@ -72,19 +114,37 @@ def test_oracle_reproduces_reference_run(golden, name):
 # RoPE, tied LM head) under the live latent-difference gate and three replays.
 
 
-@pytest.fixture(scope="module")
-def golden_huginn():
+def _load_huginn(name: str):
     from continuous_depth_batching_b200.huginn import HuginnShape, random_huginn_state_dict
 
-    data = json.loads((GOLDEN / "huginn_small.json").read_text())
+    data = json.loads((GOLDEN / name).read_text())
     shape = HuginnShape(**data["shape"])
     sd = random_huginn_state_dict(shape, seed=data["weights_seed"], embed_std=data["embed_std"])
     return data, shape, sd
 
 
+@pytest.fixture(scope="module")
+def golden_huginn():
+    return _load_huginn("huginn_small.json")
+
+
+@pytest.fixture(scope="module")
+def golden_huginn_async():
+    return _load_huginn("huginn_small_async.json")
+
+
 @pytest.mark.parametrize("name", ["live_gate_refill", "replay_refill", "replay_norefill", "replay_last_exited"])
 def test_oracle_reproduces_reference_huginn_run(golden_huginn, name):
-    data, shape, sd = golden_huginn
+    _check_huginn(golden_huginn, name, "huginn_small_logits.npz")
+
+
+@pytest.mark.parametrize("name", ASYNC_RUNS)
+def test_oracle_reproduces_reference_huginn_async_run(golden_huginn_async, name):
+    _check_huginn(golden_huginn_async, name, "huginn_small_async_logits.npz")
+
+
+def _check_huginn(golden, name, logits_file):
+    data, shape, sd = golden
     run = next(r for r in data["runs"] if r["name"] == name)
     cfg = OracleConfig(
         block_size=data["block_size"],
@@ -96,6 +156,7 @@ def test_oracle_reproduces_reference_huginn_run(golden_huginn, name):
         refill=run["refill"],
         kv_policy=run["kv_policy"],
         kv_pressure_mode="reserve" if run["kv_policy"] == "last_exited" else "recompute",
+        delayed=run.get("async", False),
     )
     engine = OracleEngine(shape, sd, cfg, torch.float32)
     tokens = engine.generate(data["prompts"], data["max_new_tokens"], exit_depths=run["exit_depths"])
@@ -105,7 +166,7 @@ def test_oracle_reproduces_reference_huginn_run(golden_huginn, name):
     assert engine.refills == run["stats"]["scheduler_refills"]
     assert engine.stats["recurrent_batches"] == run["stats"]["recurrent_batches"]
     assert engine.stats["coda_batches"] == run["stats"]["coda_batches"]
-    if name == "live_gate_refill":
-        logits = np.load(GOLDEN / "huginn_small_logits.npz")
+    if name.startswith("live_gate_refill"):
+        logits = np.load(GOLDEN / logits_file)
         for i in range(len(logits.files)):
-            np.testing.assert_allclose(engine.logits[i][1].numpy(), logits[f"live_gate_refill_{i}"], rtol=0, atol=1e-5)
+            np.testing.assert_allclose(engine.logits[i][1].numpy(), logits[f"{name}_{i}"], rtol=0, atol=1e-5)
