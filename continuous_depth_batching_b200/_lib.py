@@ -91,6 +91,19 @@ _SIGNATURES: dict[str, list] = {
     "cdb_exit_hazard": [
         c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_double, c_void_p,
     ],
+    "cdb_exit_gate_route": [
+        c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+        c_int, c_int, c_double, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+    ],
+    "cdb_block_pool_init": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p],
+    "cdb_block_alloc": [
+        c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
+    ],
+    "cdb_block_free": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int, c_void_p],
+    "cdb_build_tables": [
+        c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_int64, c_void_p,
+        c_void_p, c_void_p, c_void_p,
+    ],
 }
 _RESTYPES = {"cdb_status_string": ctypes.c_char_p, "cdb_attn_scratch_bytes": c_int64, "cdb_gemm_workspace_elems": c_int64}
 

@@ -285,6 +285,63 @@ int cdb_exit_hazard(const void* signal, int signal_bf16, const int32_t* slots, c
                     const int8_t* reset, double* cdf, double* surv, int8_t* exit_out, int num_rows,
                     int min_steps, double threshold, void* stream);
 
+/* ---------------------------------------------------------------- device scheduling primitives */
+
+/* Exit-gate evaluation plus routing and compaction of one recurrent launch on device: the
+ * decision of ExitPolicy.should_exit (exit_policy.py:150-169) and the routing of
+ * _run_mixed_recurrent_batch / the delayed consumption path (continuous_api.py:1090-1203,
+ * 1250-1280, 1699-1724). Row r: policy-state slot hidden[r] (< 0: padding, not routed), step[r],
+ * replay depth depth[r] (NULL or < 0: none), reset[r] (NULL, or nonzero when the row starts a
+ * new token: its slot's state is cleared first), signal = bf16 signal[r * signal_stride].
+ *   policy 0 none, 1 cumulative hazard (h = bf16(sigmoid(x)); cdf += h*surv; surv *= 1-h;
+ *          d = step+1 >= min_steps && cdf >= threshold), 2 direct threshold (d = step+1 >=
+ *          min_steps && x < threshold). cdf/surv fp64 per slot.
+ *   delayed 0: exit = step == max_steps-1 || (replay ? step >= depth : d).
+ *   delayed 1 (use_async_batching with delay_gate_consumption): exit = step == max_steps-1 ||
+ *          (replay ? step >= depth+1 : pending[slot] == 1); then pending[slot] = d (-1 without a
+ *          policy). pending is int8 per slot, -1 = none.
+ * Outputs: exit_flag[r] (1 exit, 0 continue, -1 padding); survivors / exits: row indices in row
+ * order (survivors return to the depth-queue head in that order, exits join the coda queue in
+ * it); counts = {num_survivors, num_exits}. One CTA; n any size. */
+int cdb_exit_gate_route(const void* signal, int64_t signal_stride, const int32_t* hidden, const int32_t* step,
+                        const int32_t* depth, const int8_t* reset, double* cdf, double* surv, int8_t* pending,
+                        int num_rows, int policy, int delayed, int min_steps, int max_steps, double threshold,
+                        int8_t* exit_flag, int32_t* survivors, int32_t* exits, int32_t* counts, void* stream);
+
+/* Device FIFO KV block allocator, the order-exact mirror of BlockManager
+ * (continuous_batching/cache_manager.py:33-91): ring[num_blocks] of free ids, popped at the head
+ * and appended at the tail; state int32[4] = {head, free count, num_blocks, peak allocated};
+ * row_len[num_rows] = blocks held by each block-table row. cdb_block_pool_init fills the ring
+ * with 0..num_blocks-1 (the deque(range(num_blocks)) start) and zeroes row_len. */
+int cdb_block_pool_init(int32_t* ring, int32_t* state, int32_t* row_len, int num_rows, int num_blocks, void* stream);
+
+/* Requests in order: request j appends counts[j] blocks from the ring's head to block-table row
+ * slots[j] (after its row_len blocks), or, when fewer blocks are free than it asks for or the row
+ * would pass `width`, takes none and gets granted[j] = 0 while later requests still try
+ * (get_free_blocks, cache_manager.py:72-81; exact-ceil counts as in _allocate_blocks_if_needed,
+ * scheduler_base.py:416-433). slots must lie in [0, num_rows). */
+int cdb_block_alloc(int32_t* ring, int32_t* state, int32_t* row_len, int32_t* block_table,
+                    int64_t block_table_stride, int width, const int32_t* slots, const int32_t* counts,
+                    int num_requests, int32_t* granted, void* stream);
+
+/* Rows slots[j], in the order given: their blocks in column order are appended at the ring's tail
+ * (a finished request's block list released, BlockManager.free_blocks), the row is reset to -1
+ * and its row_len to 0. Each slot at most once per call. */
+int cdb_block_free(int32_t* ring, int32_t* state, int32_t* row_len, int32_t* block_table,
+                   int64_t block_table_stride, const int32_t* slots, int num_slots, void* stream);
+
+/* The per-launch metadata FlashAttention's kvcache branch takes (_prepare_recurrent_stage_buffers,
+ * model_runner.py:704-754, gather_block_table_host_rows, continuous_depth_batching/cache.py:66-91):
+ * out_table[i] = the full block row of slot item_slot[i] (-1 past its row_len blocks, `width`
+ * columns), cu_seq_lens_q = 0,1,..,num_items then plateaued, cu_seq_lens_k[i+1] =
+ * cu_seq_lens_k[i] + item_pos[i] + 1 then plateaued; padding rows num_items <= i < bucket get
+ * all -1. cu arrays hold bucket+1 entries. A row whose position lies past its blocks sets
+ * CDB_ERR_INDEX in *status (the reference raises ValueError). */
+int cdb_build_tables(const int32_t* block_table, int64_t block_table_stride, const int32_t* row_len, int width,
+                     int block_size, const int32_t* item_slot, const int32_t* item_pos, int num_items, int bucket,
+                     int32_t* out_table, int64_t out_stride, int32_t* cu_seq_lens_q, int32_t* cu_seq_lens_k,
+                     int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
