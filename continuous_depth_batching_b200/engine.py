@@ -669,70 +669,53 @@ class ContinuousDepthBatchingEngine:
             return self._stage_live_decisions(items)
         return self._live_decisions(items)
 
-    def _hazard_flags(self, items: list[_Item]) -> torch.Tensor:
-        """Cumulative-hazard decisions of this launch's gate logits, on device (``cdb_exit_hazard``)."""
+    def _live_flags(self, items: list[_Item]) -> torch.Tensor:
+        """This launch's live exit decisions on device (``cdb_exit_gate_route``, synchronous rule):
+        Ouro's cumulative hazard of the gate logit, Huginn's direct threshold on the latent
+        difference. Policy state (fp64 cdf/survival) lives per hidden-bank slot on the device."""
 
         r = self.runner
         cfg = self.cdb_config
         n = len(items)
         meta = r.upload([[it.hidden for it in items], [it.step for it in items], [int(it.step == 0) for it in items]])
         meta = meta.view(3, n)
-        if not hasattr(self, "_hz"):
-            self._hz = (
+        if not hasattr(self, "_route"):
+            m = cfg.max_num_seqs
+            self._route = (
                 torch.zeros(r.bank_slots, dtype=torch.float64, device=r.device),
                 torch.ones(r.bank_slots, dtype=torch.float64, device=r.device),
-                torch.zeros(cfg.max_num_seqs, dtype=torch.int8, device=r.device),
+                torch.zeros(m, dtype=torch.int8, device=r.device),
+                torch.zeros(2, m, dtype=torch.int32, device=r.device),
+                torch.zeros(2, dtype=torch.int32, device=r.device),
             )
-        cdf, surv, flags = self._hz
+        cdf, surv, flags, lists, counts = self._route
+        policy = 2 if isinstance(self.shape, HuginnShape) else 1
         from . import _lib
 
         with torch.cuda.stream(r.stream):
             reset = meta[2].to(torch.int8)
             _lib.call(
-                "cdb_exit_hazard", _lib.ptr(r.gate_out), 1, _lib.ptr(meta[0]), _lib.ptr(meta[1]), _lib.ptr(reset),
-                _lib.ptr(cdf), _lib.ptr(surv), _lib.ptr(flags), n, cfg.min_recurrent_steps, float(cfg.exit_threshold),
-                r.stream.cuda_stream,
+                "cdb_exit_gate_route", _lib.ptr(r.gate_out), r.gate_out.stride(0), _lib.ptr(meta[0]),
+                _lib.ptr(meta[1]), None, _lib.ptr(reset), _lib.ptr(cdf), _lib.ptr(surv), None, n, policy, 0,
+                cfg.min_recurrent_steps, self.steps, float(cfg.exit_threshold), _lib.ptr(flags), _lib.ptr(lists[0]),
+                _lib.ptr(lists[1]), _lib.ptr(counts), r.stream.cuda_stream,
             )
         return flags[:n]
 
     def _stage_live_decisions(self, items: list[_Item]) -> _StagedDecisions:
         """Delayed consumption: decide this launch's signals on device now (the per-token policy
         state advances in step order, as the reference's deferred ``should_exit`` calls advance
-        it) and stage them to the host; routing reads them after the next launch."""
+        it) and stage the flags to the host; routing reads them after the next launch."""
 
-        r = self.runner
-        cfg = self.cdb_config
-        n = len(items)
-        if isinstance(self.shape, HuginnShape):
-            steps = [it.step for it in items]
-            tau, min_steps = float(cfg.exit_threshold), cfg.min_recurrent_steps
-            with torch.cuda.stream(r.stream):
-                sig = r.gate_out[:n].float()
-            return _StagedDecisions(
-                sig, r.stream, lambda i, v: steps[i] + 1 >= min_steps and v[i] < tau
-            )
-        return _StagedDecisions(self._hazard_flags(items), r.stream, lambda i, v: bool(v[i]))
+        return _StagedDecisions(self._live_flags(items), self.runner.stream, lambda i, v: bool(v[i]))
 
     def _live_decisions(self, items: list[_Item]) -> list[bool]:
-        """Live exit decisions (``ExitPolicy.should_exit``, ``exit_policy.py:150-169``).
-
-        Ouro: cumulative hazard of the gate logit on device (``cdb_exit_hazard``). Huginn: direct
-        threshold on the latent difference (``signal < exit_threshold`` once ``step + 1 >=
-        min_recurrent_steps``), read back with one synchronisation.
-        """
+        """Live exit decisions (``ExitPolicy.should_exit``, ``exit_policy.py:150-169``) decided on
+        device and read back with one synchronisation (the synchronous timing)."""
 
         self.last_stats.host_syncs += 1
-        r = self.runner
-        cfg = self.cdb_config
-        n = len(items)
-        if isinstance(self.shape, HuginnShape):
-            signals = r.gate_signals(n).tolist()
-            return [
-                it.step + 1 >= cfg.min_recurrent_steps and sig < float(cfg.exit_threshold)
-                for it, sig in zip(items, signals, strict=True)
-            ]
-        with torch.cuda.stream(r.stream):
-            host = self._hazard_flags(items).cpu()
+        with torch.cuda.stream(self.runner.stream):
+            host = self._live_flags(items).cpu()
         return [bool(x) for x in host.tolist()]
 
     def _should_exit(self, it: _Item, step: int, live, i: int) -> bool:
