@@ -57,6 +57,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--out-cap", type=int, default=1024, help="cap on output lengths (smaller = profiling case)")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--gemm", default="cublas", choices=["tcgen05", "cublas"], help="dense GEMM backend")
+    p.add_argument("--lm-head", default="fused", choices=["fused", "gemm"],
+                   help="LM head + argmax as one tcgen05 GEMM (fused) or a GEMM then an argmax kernel")
     p.add_argument("--num-blocks", type=int, default=16384, help="KV pool blocks (small for profiler captures)")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle timing (profiling runs)")
     p.add_argument("--seed", type=int, default=0)
@@ -161,7 +163,9 @@ def build_engine(args, device):
         max_model_len=4096,
         max_num_seqs=256,
     )
-    eng = ContinuousDepthBatchingEngine.from_model(model, cfg, device=device, gemm_backend=args.gemm)
+    eng = ContinuousDepthBatchingEngine.from_model(
+        model, cfg, device=device, gemm_backend=args.gemm, fused_lm_head=getattr(args, "lm_head", "fused") == "fused"
+    )
     del model
     return eng, shape
 
@@ -317,6 +321,7 @@ def run_b200(args) -> None:
                 "l2": "inputs larger than L2 (KV cache tens of GB, weights 2.5 GB)",
                 "cuda_graphs": not args.no_graph,
                 "gemm_backend": args.gemm,
+                "lm_head": args.lm_head,
                 "parallelism": f"{world} independent request-sharded replicas (no collective)",
             },
             "e2e": {

@@ -104,6 +104,7 @@ class HuginnRunner(OuroRunner):
         max_num_batched_tokens: int,
         use_cuda_graph: bool = True,
         gemm_backend: str = "tcgen05",
+        fused_lm_head: bool = True,
     ) -> None:
         P, C, Dc = shape.n_layers_in_prelude, shape.n_layers_in_recurrent_block, shape.n_layers_in_coda
         self._init_device(
@@ -119,6 +120,7 @@ class HuginnRunner(OuroRunner):
             max_num_batched_tokens=max_num_batched_tokens,
             use_cuda_graph=use_cuda_graph,
             gemm_backend=gemm_backend,
+            fused_lm_head=fused_lm_head,
         )
         self.w = PackedHuginnWeights.from_state_dict(shape, state_dict, device, fc_interleaved=gemm_backend == "tcgen05")
         E, I = shape.n_embd, shape.intermediate_size

@@ -168,6 +168,7 @@ class OuroRunner:
         max_num_batched_tokens: int,
         use_cuda_graph: bool = True,
         gemm_backend: str = "tcgen05",
+        fused_lm_head: bool = True,
     ) -> None:
         self._init_device(
             shape,
@@ -182,6 +183,7 @@ class OuroRunner:
             max_num_batched_tokens=max_num_batched_tokens,
             use_cuda_graph=use_cuda_graph,
             gemm_backend=gemm_backend,
+            fused_lm_head=fused_lm_head,
         )
         self.w = PackedOuroWeights.from_state_dict(shape, state_dict, device, gu_interleaved=gemm_backend == "tcgen05")
         H, D = shape.hidden_size, shape.head_dim
@@ -228,6 +230,7 @@ class OuroRunner:
         max_num_batched_tokens: int,
         use_cuda_graph: bool,
         gemm_backend: str,
+        fused_lm_head: bool = True,
     ) -> None:
         """Model-independent device state: KV pool, stream, uploads, attention scratch, graphs."""
 
@@ -278,8 +281,9 @@ class OuroRunner:
         self.part_ml = torch.zeros(SCRATCH_ITEMS * nh * 64 * 2, dtype=torch.float32, device=device)
         self.counters = torch.zeros(SCRATCH_ITEMS * nh, dtype=torch.int32, device=device)
         self.scale = float(D) ** -0.5
-        # LM head + argmax in one GEMM (no logits in HBM) unless logits are kept for inspection
-        self.fused_lm_head = gemm_backend == "tcgen05"
+        # LM head + greedy argmax in one tcgen05 GEMM (no logits in HBM; cdb_lm_head_argmax) with
+        # either projection backend, unless logits are kept for inspection
+        self.fused_lm_head = fused_lm_head
         self.lm_keys = torch.zeros(max_num_seqs, dtype=torch.int64, device=device)
         self.lm_done = torch.zeros(1, dtype=torch.int32, device=device)
         self.buckets = decode_graph_buckets(max_num_seqs)
