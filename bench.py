@@ -170,20 +170,21 @@ def build_engine(args, device):
     return eng, shape
 
 
-# DRAM bytes per algorithmic byte of decode_attn_kernel<128,4>, from one ncu capture of a launch
-# of 128 rows x ~1055-token contexts (kernel_bench attention --rows 128 --context 1024):
-# dram__bytes_read.sum 1.116279 GB + dram__bytes_write.sum 4.74 MB over 1,107,100,888 algorithmic
-# bytes. Traffic grows with the pages a launch streams, so a bench launch's traffic is its
-# algorithmic bytes times this ratio.
-ATTN_TRAFFIC_PER_ALGO_BYTE = (1.116279e9 + 4.741632e6) / 1107100888
+# DRAM bytes per algorithmic byte of decode_attn_kernel<128,4> with the fused append, from one ncu
+# capture of a launch of 128 rows x ~1055-token contexts (kernel_bench attention --rows 128
+# --context 1024 --append 2): dram__bytes_read.sum 1.117724 GB + dram__bytes_write.sum 5.687 MB
+# over 1,108,149,464 algorithmic bytes. Traffic grows with the pages a launch streams, so a bench
+# launch's traffic is its algorithmic bytes times this ratio.
+ATTN_TRAFFIC_PER_ALGO_BYTE = (1.117724e9 + 5.687296e6) / 1108149464
 
 
 def attention_roofline(eng, shape, launches: list[tuple[list[int], list[int]]], peak_gbs: float) -> dict:
     """Time the paged decode-attention kernel alone over recorded launch shapes (CUDA events).
 
-    Each recorded recurrent launch (rows' slots and positions) is replayed as the cache-only
-    attention launch of one layer (rows attend over their cached positions 0..p, which the timed
-    step wrote), on the engine stream; achieved = algorithmic bytes / mean launch time.
+    Each recorded recurrent launch (rows' slots and positions) is replayed as the per-layer
+    attention launch the engine makes: RoPE of q and k, the KV append at position p and attention
+    over 0..p in one kernel (append=2), on the engine stream; achieved = algorithmic bytes (cache
+    rows 0..p-1 read, the new k/v read and written, q read, o written) / mean launch time.
     """
 
     from continuous_depth_batching_b200.kernel_bench import attention_bytes
@@ -197,15 +198,15 @@ def attention_roofline(eng, shape, launches: list[tuple[list[int], list[int]]], 
         meta = r.upload([slots, pos])
         meta = meta.view(2, b)
         with torch.cuda.stream(stream):
-            r._plan(meta[1], b, 0)
-        algo = attention_bytes(pos, H, D, append=False)
+            r._plan(meta[1], b, 1)
+        algo = attention_bytes(pos, H, D, append=True)
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = 10
         with torch.cuda.stream(stream):
-            r._attention(b, 0, meta[0], meta[1], 0, 0)  # warm
+            r._attention(b, 0, meta[0], meta[1], 2, 1)  # warm
             start.record(stream)
             for _ in range(reps):
-                r._attention(b, 0, meta[0], meta[1], 0, 0)
+                r._attention(b, 0, meta[0], meta[1], 2, 1)
             end.record(stream)
         end.synchronize()
         ms = start.elapsed_time(end) / reps
@@ -222,7 +223,7 @@ def attention_roofline(eng, shape, launches: list[tuple[list[int], list[int]]], 
         "unit": "GB/s",
         "frac": round(achieved / peak_gbs, 4),
         "traffic": int(per_launch_bytes * ATTN_TRAFFIC_PER_ALGO_BYTE),
-        "traffic_source": "ncu dram bytes of a 128-row x 1055-token launch scaled by algorithmic bytes (ratio 1.013)",
+        "traffic_source": "ncu dram bytes of a 128-row x 1055-token fused-append launch scaled by algorithmic bytes (ratio 1.014)",
         "kernel": f"cdb::decode_attn_kernel<{D},{5 if D == 96 else 4}>",
         "launch_ms": round(per_launch_ms, 4),
         "algorithmic_bytes_per_launch": int(per_launch_bytes),
