@@ -95,6 +95,19 @@ _SIGNATURES: dict[str, list] = {
         c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
         c_int, c_int, c_double, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
     ],
+    "cdb_qkv_rope_append_gemm": [
+        c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int, c_int, c_void_p, c_int,
+        c_int64, c_int, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int,
+        c_int, c_int, c_void_p, c_void_p,
+    ],
+    "cdb_o_proj_residual_norm_gemm": [
+        c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+        c_int64, c_int, c_int, c_int, c_float, c_int, c_void_p, c_void_p,
+    ],
+    "cdb_down_residual_norm_gemm": [
+        c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+        c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_int, c_void_p, c_void_p,
+    ],
     "cdb_block_pool_init": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p],
     "cdb_block_alloc": [
         c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p,

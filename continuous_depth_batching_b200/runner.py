@@ -430,12 +430,21 @@ class OuroRunner:
                     s.num_attention_heads, s.head_dim, self.block_size, sp,
                 )
                 self._prefill_attention(base_layer + l)
-            self._mm(self.attn[:n], w.w_o[l], self.o[:n])
-            _lib.call(
-                "cdb_add_rmsnorm", _lib.ptr(self.xw), self.xw.stride(0), _lib.ptr(self.o), self.o.stride(0),
-                _lib.ptr(w.norms["input_layernorm_2"][l]), _lib.ptr(w.norms["post_attention_layernorm"][l]),
-                _lib.ptr(self.h), self.h.stride(0), None, None, None, None, n, H, eps, sp,
-            )
+            if self.gemm_backend == "tcgen05":
+                _lib.call(
+                    "cdb_o_proj_residual_norm_gemm", _lib.ptr(self.attn), self.attn.stride(0), _lib.ptr(w.w_o[l]),
+                    w.w_o[l].stride(0), _lib.ptr(self.o), self.o.stride(0), _lib.ptr(self.xw), self.xw.stride(0),
+                    _lib.ptr(w.norms["input_layernorm_2"][l]), _lib.ptr(w.norms["post_attention_layernorm"][l]),
+                    _lib.ptr(self.h), self.h.stride(0), n, H, w.w_o[l].shape[1], eps, self.num_sms,
+                    _lib.ptr(self.status), sp,
+                )
+            else:
+                self._mm(self.attn[:n], w.w_o[l], self.o[:n])
+                _lib.call(
+                    "cdb_add_rmsnorm", _lib.ptr(self.xw), self.xw.stride(0), _lib.ptr(self.o), self.o.stride(0),
+                    _lib.ptr(w.norms["input_layernorm_2"][l]), _lib.ptr(w.norms["post_attention_layernorm"][l]),
+                    _lib.ptr(self.h), self.h.stride(0), None, None, None, None, n, H, eps, sp,
+                )
             if self.gemm_backend == "tcgen05":
                 _lib.call(
                     "cdb_mlp_gateup_silu_gemm", _lib.ptr(self.h), self.h.stride(0), _lib.ptr(w.w_gu[l]),
@@ -447,20 +456,28 @@ class OuroRunner:
                 _lib.call(
                     "cdb_silu_mul", _lib.ptr(self.gu), self.gu.stride(0), _lib.ptr(self.act), self.act.stride(0), n, I, sp
                 )
-            self._mm(self.act[:n], w.w_down[l], self.m[:n])
-            if l < L - 1:
+            # x += norm(m); then the next layer's input norm, or after the last layer the final norm
+            # scattered into the bank (and the exit-gate logit)
+            last = l == L - 1
+            w_next = w.final_norm if last else w.norms["input_layernorm"][l + 1]
+            y, y_rows = (final_dst, final_rows) if last else (self.h, None)
+            g = last and gate
+            if self.gemm_backend == "tcgen05":
                 _lib.call(
-                    "cdb_add_rmsnorm", _lib.ptr(self.xw), self.xw.stride(0), _lib.ptr(self.m), self.m.stride(0),
-                    _lib.ptr(w.norms["post_attention_layernorm_2"][l]), _lib.ptr(w.norms["input_layernorm"][l + 1]),
-                    _lib.ptr(self.h), self.h.stride(0), None, None, None, None, n, H, eps, sp,
+                    "cdb_down_residual_norm_gemm", _lib.ptr(self.act), self.act.stride(0), _lib.ptr(w.w_down[l]),
+                    w.w_down[l].stride(0), _lib.ptr(self.m), self.m.stride(0), _lib.ptr(self.xw), self.xw.stride(0),
+                    _lib.ptr(w.norms["post_attention_layernorm_2"][l]), _lib.ptr(w_next), _lib.ptr(y), y.stride(0),
+                    _lib.ptr(y_rows), _lib.ptr(w.gate_w) if g else None, _lib.ptr(w.gate_b) if g else None,
+                    _lib.ptr(self.gate_out) if g else None, n, H, w.w_down[l].shape[1], eps, self.num_sms,
+                    _lib.ptr(self.status), sp,
                 )
             else:
+                self._mm(self.act[:n], w.w_down[l], self.m[:n])
                 _lib.call(
                     "cdb_add_rmsnorm", _lib.ptr(self.xw), self.xw.stride(0), _lib.ptr(self.m), self.m.stride(0),
-                    _lib.ptr(w.norms["post_attention_layernorm_2"][l]), _lib.ptr(w.final_norm),
-                    _lib.ptr(final_dst), final_dst.stride(0), _lib.ptr(final_rows),
-                    _lib.ptr(w.gate_w) if gate else None, _lib.ptr(w.gate_b) if gate else None,
-                    _lib.ptr(self.gate_out) if gate else None, n, H, eps, sp,
+                    _lib.ptr(w.norms["post_attention_layernorm_2"][l]), _lib.ptr(w_next), _lib.ptr(y), y.stride(0),
+                    _lib.ptr(y_rows), _lib.ptr(w.gate_w) if g else None, _lib.ptr(w.gate_b) if g else None,
+                    _lib.ptr(self.gate_out) if g else None, n, H, eps, sp,
                 )
 
     def _recurrent_body(self, meta: torch.Tensor, n: int, kv_slot: int, gate: bool) -> None:

@@ -218,6 +218,40 @@ int cdb_add_rmsnorm(void* x, int64_t x_stride, const void* a, int64_t a_stride, 
                     const void* w_next, void* y, int64_t y_stride, const int32_t* y_rows, const void* gate_w,
                     const void* gate_b, void* gate_out, int num_rows, int hidden, float eps, void* stream);
 
+/* QKV projection with RoPE and the KV append: qkv[M, v_col + H*D] = x * w_qkv^T (cdb_gemm_bf16),
+ * then q rotated in place, k rotated, and k/v written at each row's position (cdb_rope_append_kv;
+ * same arguments). Replaces OuroAttention.forward's q/k/v_proj + apply_rotary_pos_emb + the
+ * cache write of paged_attention_forward (modeling_ouro.py:377-410, flash_paged.py:84-106); the
+ * cache-only attention (append 0) then reads the new row. Two launches chained with programmatic
+ * dependent launch. */
+int cdb_qkv_rope_append_gemm(const void* x, int64_t ldx, const void* w_qkv, int64_t ldw, void* qkv,
+                             int64_t qkv_stride, int64_t k_col, int64_t v_col, int num_items, int K, void* kv_base,
+                             int num_cache_layers, int64_t kv_rows, int cache_layer, const int32_t* block_table,
+                             int64_t block_table_stride, const int32_t* item_slot, const int32_t* item_pos,
+                             int rope_mode, const void* rope_cos, const void* rope_sin, const void* qk_bias,
+                             int num_heads, int head_dim, int block_size, int num_sms, int32_t* status,
+                             void* stream);
+
+/* O projection with Ouro's post-attention sandwich: proj = attn * w_o^T; x <- bf16(x +
+ * norm_post(proj)); y = norm_next(x) (OuroDecoderLayer.forward, modeling_ouro.py:470-490:
+ * input_layernorm_2 on the attention output, the residual add, post_attention_layernorm). The
+ * tcgen05 GEMM, then cdb_add_rmsnorm, chained with programmatic dependent launch. */
+int cdb_o_proj_residual_norm_gemm(const void* attn, int64_t ld_attn, const void* w_o, int64_t ldw, void* proj,
+                                  int64_t ld_proj, void* x, int64_t x_stride, const void* w_norm_post,
+                                  const void* w_norm_next, void* y, int64_t y_stride, int num_rows, int hidden,
+                                  int K, float eps, int num_sms, int32_t* status, void* stream);
+
+/* Down projection with the MLP sandwich: proj = act * w_down^T; x <- bf16(x + norm_post(proj));
+ * y[y_rows[r]] = norm_next(x[r]) (y_rows NULL: y[r]; rows with y_rows[r] < 0 skipped) and, with
+ * gate_w, gate_out[r] = bf16(gate_w . y + gate_b) - the layer end of OuroDecoderLayer.forward
+ * (modeling_ouro.py:492-503) and, after the last layer, the final norm, bank scatter and exit-gate
+ * logit of OuroCDBAdapter.recurrent_step (adapters/ouro.py:240-262). */
+int cdb_down_residual_norm_gemm(const void* act, int64_t ld_act, const void* w_down, int64_t ldw, void* proj,
+                                int64_t ld_proj, void* x, int64_t x_stride, const void* w_norm_post,
+                                const void* w_norm_next, void* y, int64_t y_stride, const int32_t* y_rows,
+                                const void* gate_w, const void* gate_b, void* gate_out, int num_rows, int hidden,
+                                int K, float eps, int num_sms, int32_t* status, void* stream);
+
 /* act[r] = bf16(bf16(silu(g)) * u) with gu[r] = [g (inter) | u (inter)] (OuroMLP.forward,
  * modeling_ouro.py:166-169). */
 int cdb_silu_mul(const void* gu, int64_t gu_stride, void* act, int64_t act_stride, int num_rows, int inter,

@@ -167,3 +167,106 @@ def test_lm_head_argmax_matches_logits_argmax(gemm, m, vocab, k):
         assert int(out[1]) == -7  # row 0 was skipped
         assert torch.equal(table[3:].long(), ref)
         assert int(keys.abs().sum()) == 0 and int(done.item()) == 0
+
+
+def _sp():
+    return torch.cuda.current_stream().cuda_stream
+
+
+@pytest.mark.parametrize("m,hidden,k,last", [(80, 2048, 2048, False), (37, 2048, 5632, True), (256, 512, 1408, True)])
+def test_residual_norm_gemms_match_separate_calls(gemm, m, hidden, k, last):
+    """cdb_o_proj_residual_norm_gemm / cdb_down_residual_norm_gemm equal cdb_gemm_bf16 followed by
+    cdb_add_rmsnorm bit for bit (projection, residual stream, normed output, gate logit)."""
+
+    torch.manual_seed(m + hidden)
+    a = torch.randn(m, k, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(hidden, k, device=DEV) * k**-0.5).to(torch.bfloat16)
+    x0 = torch.randn(m, hidden, device=DEV).to(torch.bfloat16)
+    wa = (1 + 0.1 * torch.randn(hidden, device=DEV)).to(torch.bfloat16)
+    wn = (1 + 0.1 * torch.randn(hidden, device=DEV)).to(torch.bfloat16)
+    gw = (0.05 * torch.randn(hidden, device=DEV)).to(torch.bfloat16)
+    gb = torch.tensor([0.25], device=DEV).to(torch.bfloat16)
+    rows = torch.randperm(2 * m, device=DEV)[:m].to(torch.int32) if last else None
+    if last:
+        rows[m // 3] = -1
+    out_rows = 2 * m if last else m
+    results = []
+    for fused in (False, True):
+        x = x0.clone()
+        proj = torch.zeros(m, hidden, dtype=torch.bfloat16, device=DEV)
+        y = torch.zeros(out_rows, hidden, dtype=torch.bfloat16, device=DEV)
+        gout = torch.zeros(m, dtype=torch.bfloat16, device=DEV)
+        g = (_lib.ptr(gw), _lib.ptr(gb), _lib.ptr(gout)) if last else (None, None, None)
+        if fused and last:
+            _lib.call(
+                "cdb_down_residual_norm_gemm", _lib.ptr(a), a.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(proj),
+                proj.stride(0), _lib.ptr(x), x.stride(0), _lib.ptr(wa), _lib.ptr(wn), _lib.ptr(y), y.stride(0),
+                _lib.ptr(rows), *g, m, hidden, k, 1e-6, 148, _lib.ptr(gemm.status), _sp(),
+            )
+        elif fused:
+            _lib.call(
+                "cdb_o_proj_residual_norm_gemm", _lib.ptr(a), a.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(proj),
+                proj.stride(0), _lib.ptr(x), x.stride(0), _lib.ptr(wa), _lib.ptr(wn), _lib.ptr(y), y.stride(0), m,
+                hidden, k, 1e-6, 148, _lib.ptr(gemm.status), _sp(),
+            )
+        else:
+            gemm(a, w, out=proj)
+            _lib.call(
+                "cdb_add_rmsnorm", _lib.ptr(x), x.stride(0), _lib.ptr(proj), proj.stride(0), _lib.ptr(wa), _lib.ptr(wn),
+                _lib.ptr(y), y.stride(0), _lib.ptr(rows), *g, m, hidden, 1e-6, _sp(),
+            )
+        torch.cuda.synchronize()
+        assert int(gemm.status.item()) == 0
+        results.append((proj, x, y, gout))
+    for ref, got in zip(results[0], results[1], strict=True):
+        assert torch.equal(ref, got)
+    assert results[1][1].abs().sum().item() > 0
+
+
+@pytest.mark.parametrize("heads,d,rope_mode,bias", [(16, 128, 1, False), (5, 96, 2, True)])
+def test_qkv_rope_append_gemm_matches_separate_calls(gemm, heads, d, rope_mode, bias):
+    """cdb_qkv_rope_append_gemm equals cdb_gemm_bf16 followed by cdb_rope_append_kv bit for bit
+    (rotated q in the qkv buffer, rotated k and v in the cache rows)."""
+
+    torch.manual_seed(heads)
+    n, k, bs, nb = 21, 512, 16, 64
+    hd = heads * d
+    x = torch.randn(n, k, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(3 * hd, k, device=DEV) * k**-0.5).to(torch.bfloat16)
+    kv0 = torch.randn(2, 2, (nb + 2) * bs, heads, d, device=DEV).to(torch.bfloat16)
+    table = torch.randperm(nb, device=DEV)[: n * 3].view(n, 3).to(torch.int32)
+    slots = torch.arange(n, dtype=torch.int32, device=DEV)
+    pos = torch.randint(0, 3 * bs, (n,), device=DEV).to(torch.int32)
+    pos[2] = -1  # padding row: nothing written
+    qk_bias = (0.1 * torch.randn(2, heads, d, device=DEV)).to(torch.bfloat16) if bias else None
+    if rope_mode == 2:
+        inv = 1.0 / (50000.0 ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+        f = torch.arange(3 * bs, device=DEV).float().unsqueeze(-1) * inv.to(DEV)
+        cos, sin = f.cos().contiguous(), f.sin().contiguous()
+    else:
+        inv = 1.0 / (10000.0 ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+        f = torch.arange(3 * bs, device=DEV).float().unsqueeze(-1) * inv.to(DEV)
+        emb = torch.cat((f, f), dim=-1)
+        cos, sin = emb.cos().to(torch.bfloat16).contiguous(), emb.sin().to(torch.bfloat16).contiguous()
+    outs = []
+    for fused in (False, True):
+        qkv = torch.zeros(n, 3 * hd, dtype=torch.bfloat16, device=DEV)
+        kv = kv0.clone()
+        common = (
+            _lib.ptr(kv), 2, (nb + 2) * bs, 1, _lib.ptr(table), table.stride(0), _lib.ptr(slots), _lib.ptr(pos),
+            rope_mode, _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(qk_bias),
+        )
+        if fused:
+            _lib.call(
+                "cdb_qkv_rope_append_gemm", _lib.ptr(x), x.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(qkv),
+                qkv.stride(0), hd, 2 * hd, n, k, *common, heads, d, bs, 148, _lib.ptr(gemm.status), _sp(),
+            )
+        else:
+            gemm(x, w, out=qkv)
+            _lib.call("cdb_rope_append_kv", _lib.ptr(qkv), qkv.stride(0), hd, 2 * hd, *common, n, heads, d, bs, _sp())
+        torch.cuda.synchronize()
+        assert int(gemm.status.item()) == 0
+        outs.append((qkv, kv))
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert torch.equal(outs[0][1], outs[1][1])
+    assert not torch.equal(outs[1][1], kv0)
