@@ -3,6 +3,7 @@
     python -m continuous_depth_batching_b200.kernel_bench attention --rows 128 --context 1024
     python -m continuous_depth_batching_b200.kernel_bench gemm --m 80 --n 2048 --k 2048
     python -m continuous_depth_batching_b200.kernel_bench lm_head --m 32 --vocab 49152 --k 2048
+    python -m continuous_depth_batching_b200.kernel_bench gemm_chain --m 80 --n 6144 --k 2048
 
 ``attention`` builds a one-cache-layer paged KV pool with the Ouro-1.4B head shape (16 heads x
 128), gives each row a context drawn uniformly from [context/2, 3*context/2), and times the
@@ -173,6 +174,48 @@ def run_gemm(args) -> dict:
     return res
 
 
+def run_gemm_chain(args) -> dict:
+    """Per-GEMM time inside a CUDA graph of ``--layers`` GEMMs of one shape on different weights
+    (the shape of a decode step's projections, launch gaps and PDL overlap included), for cuBLAS
+    and for cdb_gemm_bf16 at each K split (0 = the automatic choice)."""
+
+    dev = torch.device("cuda")
+    torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+    m, n, k, layers = args.m, args.n, args.k, args.layers
+    w = (0.02 * torch.randn(layers, n, k, device=dev)).to(torch.bfloat16)
+    x = torch.randn(m, k, device=dev).to(torch.bfloat16)
+    out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream()
+    res = {"m": m, "n": n, "k": k, "layers": layers, "us_per_gemm": {}}
+    for split in ["cublas", 0, 1, 2, 4, 8]:
+        def body(split=split):
+            for layer in range(layers):
+                if split == "cublas":
+                    torch.mm(x, w[layer].t(), out=out)
+                else:
+                    _lib.call(
+                        "cdb_gemm_bf16", _lib.ptr(x), x.stride(0), _lib.ptr(w[layer]), w.stride(1), _lib.ptr(out),
+                        out.stride(0), m, n, k, split, None, 0, None, 0, 148, _lib.ptr(status), stream.cuda_stream,
+                    )
+
+        with torch.cuda.stream(stream):
+            body()
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            body()
+        with torch.cuda.stream(stream):  # replays run on the current stream: make it the timed one
+            for _ in range(args.warmup):
+                graph.replay()
+            ms = _events_ms(graph.replay, args.iters, stream)
+        res["us_per_gemm"][str(split)] = round(ms * 1e3 / layers, 2)
+        del graph
+    if int(status.item()) != 0:
+        raise RuntimeError(_lib.load().cdb_status_string(int(status.item())).decode())
+    return res
+
+
 def run_lm_head(args) -> dict:
     """cdb_lm_head_argmax against torch.mm (cuBLAS) + cdb_argmax on the same rows."""
 
@@ -232,12 +275,19 @@ def main(argv=None) -> None:
     lm.add_argument("--m", type=int, default=32)
     lm.add_argument("--vocab", type=int, default=49152)
     lm.add_argument("--k", type=int, default=2048)
-    for s in (a, g, lm):
+    gc = sub.add_parser("gemm_chain")
+    gc.add_argument("--m", type=int, default=80)
+    gc.add_argument("--n", type=int, default=2048)
+    gc.add_argument("--k", type=int, default=2048)
+    gc.add_argument("--layers", type=int, default=24)
+    for s in (a, g, lm, gc):
         s.add_argument("--warmup", type=int, default=3)
         s.add_argument("--iters", type=int, default=20)
         s.add_argument("--seed", type=int, default=0)
     args = p.parse_args(argv)
-    res = {"attention": run_attention, "gemm": run_gemm, "lm_head": run_lm_head}[args.kernel](args)
+    res = {"attention": run_attention, "gemm": run_gemm, "lm_head": run_lm_head, "gemm_chain": run_gemm_chain}[
+        args.kernel
+    ](args)
     print(json.dumps(res))
 
 
