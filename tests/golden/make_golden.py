@@ -1,9 +1,9 @@
 """Generate the golden fixtures by running the reference engine itself on CPU.
 
-Run in a container that has the reference checkout (read-only) at ``$CDB_REFERENCE_SRC``
-(default ``/root/reference/src``)::
+Run in a container that has the reference checkout (read-only), with ``CDB_REFERENCE_SRC``
+pointing at its ``src`` directory::
 
-    python tests/golden/make_golden.py
+    CDB_REFERENCE_SRC=<reference checkout>/src python tests/golden/make_golden.py [--async]
 
 It builds the reference's own ``OuroForCausalLM`` at BASELINE config 0's shape, loads the
 seeded weights from :func:`continuous_depth_batching_b200.ouro.random_ouro_state_dict`,
@@ -33,7 +33,9 @@ import torch
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO))
-sys.path.insert(0, os.environ.get("CDB_REFERENCE_SRC", "/root/reference/src"))
+if not os.environ.get("CDB_REFERENCE_SRC"):
+    raise SystemExit("set CDB_REFERENCE_SRC to the reference checkout's src directory")
+sys.path.insert(0, os.environ["CDB_REFERENCE_SRC"])
 
 from continuous_depth_batching_b200.ouro import OuroShape, random_ouro_state_dict  # noqa: E402
 from oracle.paged_attention import cpu_paged_attention_forward  # noqa: E402

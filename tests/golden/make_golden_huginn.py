@@ -1,9 +1,9 @@
 """Generate the Huginn golden fixtures by running the reference engine itself on CPU.
 
-Run in a container that has the reference checkout (read-only) at ``$CDB_REFERENCE_SRC``
-(default ``/root/reference/src``)::
+Run in a container that has the reference checkout (read-only), with ``CDB_REFERENCE_SRC``
+pointing at its ``src`` directory::
 
-    python tests/golden/make_golden_huginn.py
+    CDB_REFERENCE_SRC=<reference checkout>/src python tests/golden/make_golden_huginn.py [--async]
 
 It builds the reference's own ``HuginnForCausalLM`` at a small shape with Huginn's structure
 (prelude / recurrent core / coda, 96-wide heads, ``qk_bias``, interleaved RoPE, tied LM head),
@@ -31,7 +31,9 @@ HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(HERE))
-sys.path.insert(0, os.environ.get("CDB_REFERENCE_SRC", "/root/reference/src"))
+if not os.environ.get("CDB_REFERENCE_SRC"):
+    raise SystemExit("set CDB_REFERENCE_SRC to the reference checkout's src directory")
+sys.path.insert(0, os.environ["CDB_REFERENCE_SRC"])
 
 from make_golden import Recorder, replay_depths  # noqa: E402
 
