@@ -811,6 +811,59 @@ __global__ void rope_append_kernel(__nv_bfloat16* qkv, int64_t qkv_stride, int64
   }
 }
 
+// Vectorised rope + append: one CTA per row, one thread per 8-element chunk of the H*D q (and k, v)
+// vector, 16-byte loads and stores. Every q chunk is read before any is rewritten in place (the
+// split-half rotation reads a partner chunk another thread owns). Same arithmetic as
+// rope_append_kernel (rope_load / rope_apply restate rope_pair per chunk).
+__global__ void rope_append_vec_kernel(__nv_bfloat16* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col,
+                                       __nv_bfloat16* kv, int64_t kv_rows, int cache_layer, const int32_t* block_table,
+                                       int64_t bt_stride, const int32_t* item_slot, const int32_t* item_pos,
+                                       int rope_mode, const void* rope_cos, const void* rope_sin,
+                                       const __nv_bfloat16* qk_bias, int num_heads, int D, int32_t* status) {
+  pdl_trigger();
+  pdl_wait();
+  const int item = blockIdx.x;
+  const int pos = item_pos[item];
+  if (pos < 0) return;
+  const int32_t* bt = block_table + (int64_t)item_slot[item] * bt_stride;
+  const int blk = bt[pos / kBlock];
+  const int64_t row = (int64_t)blk * kBlock + pos % kBlock;
+  if (blk < 0 || row >= kv_rows) {
+    if (threadIdx.x == 0) set_error(status, CDB_ERR_INDEX);
+    return;
+  }
+  const int64_t hstride = (int64_t)num_heads * D;
+  __nv_bfloat16* q = qkv + (int64_t)item * qkv_stride;
+  const __nv_bfloat16* k = q + k_col;
+  const __nv_bfloat16* v = q + v_col;
+  __nv_bfloat16* kd = kv + ((int64_t)(2 * cache_layer) * kv_rows + row) * hstride;
+  __nv_bfloat16* vd = kv + ((int64_t)(2 * cache_layer + 1) * kv_rows + row) * hstride;
+  const int c = threadIdx.x;
+  const bool active = c < num_heads * D / 8;
+  const int head = active ? c * 8 / D : 0, x0 = active ? c * 8 % D : 0;
+  const int64_t hb = (int64_t)head * D;
+  const bool rot_q = rope_mode != 0 || qk_bias != nullptr;
+  RopeRaw rq, rk;
+  uint4 vv = make_uint4(0u, 0u, 0u, 0u);
+  if (active) {
+    if (rot_q) rope_load(rope_mode, rope_cos, rope_sin, pos, D, q + hb, qk_bias ? qk_bias + hb : nullptr, x0, rq);
+    rope_load(rope_mode, rope_cos, rope_sin, pos, D, k + hb, qk_bias ? qk_bias + hstride + hb : nullptr, x0, rk);
+    vv = ld16(v + hb + x0);
+  }
+  __syncthreads();
+  if (!active) return;
+  float y[8];
+  if (rot_q) {
+    rope_apply(rope_mode, qk_bias != nullptr, x0 < D / 2, rq, y);
+    *reinterpret_cast<uint4*>(q + hb + x0) = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
+                                                        pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
+  }
+  rope_apply(rope_mode, qk_bias != nullptr, x0 < D / 2, rk, y);
+  *reinterpret_cast<uint4*>(kd + hb + x0) = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
+                                                       pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
+  *reinterpret_cast<uint4*>(vd + hb + x0) = vv;
+}
+
 // ------------------------------------------------------------------ tensor-map cache (host)
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -902,6 +955,20 @@ static int launch_rope_append(void* qkv, int64_t qkv_stride, int64_t k_col, int6
                               const void* rope_sin, const void* qk_bias, int num_items, int num_heads, int head_dim,
                               int32_t* status, cudaStream_t st) {
   if (num_items == 0) return CDB_OK;
+  const int chunks = num_heads * head_dim / 8;
+  const bool aligned16 = ((reinterpret_cast<uintptr_t>(qk_bias) | reinterpret_cast<uintptr_t>(kv_base) |
+                           reinterpret_cast<uintptr_t>(qkv)) & 15) == 0 &&
+                         (rope_mode == 0 ||
+                          ((reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin)) & 15) == 0) &&
+                         (qkv_stride & 7) == 0 && (k_col & 7) == 0 && (v_col & 7) == 0;
+  if (head_dim % 8 == 0 && chunks <= 1024 && aligned16) {
+    return launch_pdl(rope_append_vec_kernel, dim3(num_items), dim3(((chunks + 31) / 32) * 32), 0, st,
+                      static_cast<__nv_bfloat16*>(qkv), qkv_stride, k_col, v_col, static_cast<__nv_bfloat16*>(kv_base),
+                      kv_rows, cache_layer, block_table, bt_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin,
+                      static_cast<const __nv_bfloat16*>(qk_bias), num_heads, head_dim, status) == cudaSuccess
+               ? CDB_OK
+               : CDB_ERR_CUDA;
+  }
   const int pairs = num_heads * (head_dim / 2);
   const int threads = pairs >= 1024 ? 1024 : ((pairs + 31) / 32) * 32;
   return launch_pdl(rope_append_kernel, dim3(num_items), dim3(threads), 0, st, static_cast<__nv_bfloat16*>(qkv),
