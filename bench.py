@@ -231,6 +231,44 @@ def attention_roofline(eng, shape, launches: list[tuple[list[int], list[int]]], 
     }
 
 
+def step_roofline(shape, recurrent_positions, coda_sizes, prefill_batches, measured_s: float, hbm_gbs: float,
+                  tflops: float) -> dict:
+    """Whole-step roofline: the sum over the step's launches of max(bytes / HBM bandwidth,
+    FLOPs / tensor peak), against the measured step time.
+
+    Per recurrent launch of B rows: the decode-attention bytes of every layer (kernel_bench
+    attention_bytes with the append) plus the shared block's weights (2 P bytes, P = L (4 H^2 +
+    3 H I) parameters), and 2 B P GEMM FLOPs. Per coda launch: the LM head's weights (2 V H bytes)
+    and 2 B H V FLOPs. Per prefill batch of T prompt tokens, S recurrent steps: 2 T P S FLOPs (plus
+    the LM head of its sampled rows) against the weights read once per step.
+    """
+
+    from continuous_depth_batching_b200.kernel_bench import attention_bytes
+
+    H, I, L, V = shape.hidden_size, shape.intermediate_size, shape.num_hidden_layers, shape.vocab_size
+    heads, D, S = shape.num_attention_heads, shape.head_dim, shape.total_ut_steps
+    P = L * (4 * H * H + 3 * H * I)
+    bw, fl = hbm_gbs * 1e9, tflops * 1e12
+    parts = {"recurrent": 0.0, "coda": 0.0, "prefill": 0.0}
+    for pos in recurrent_positions:
+        byts = L * attention_bytes(pos, heads, D, append=True) + 2 * P
+        parts["recurrent"] += max(byts / bw, 2 * len(pos) * P / fl)
+    for b in coda_sizes:
+        parts["coda"] += max(2 * V * H / bw, 2 * b * H * V / fl)
+    for tokens, sampled in prefill_batches:
+        parts["prefill"] += max((2 * P * S + 2 * V * H) / bw, (2 * tokens * P * S + 2 * sampled * H * V) / fl)
+    total = sum(parts.values())
+    return {
+        "roofline_s": round(total, 4),
+        "measured_s": round(measured_s, 4),
+        "frac": round(total / measured_s, 4),
+        "parts_s": {k: round(v, 4) for k, v in parts.items()},
+        "hbm_gbs": hbm_gbs,
+        "tflops": tflops,
+        "launches": {"recurrent": len(recurrent_positions), "coda": len(coda_sizes), "prefill": len(prefill_batches)},
+    }
+
+
 def run_b200(args) -> None:
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -255,12 +293,31 @@ def run_b200(args) -> None:
     torch.cuda.synchronize()
     # Record representative attention launch shapes (positions) from the workload for the roofline pass.
     recorded: list[tuple[list[int], list[int]]] = []
+    rec_positions: list[list[int]] = []
+    coda_sizes: list[int] = []
+    prefill_batches: list[tuple[int, int]] = []
+    prefill_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
     orig = eng._run_recurrent
+    orig_coda, orig_prefill = eng._run_coda, eng._run_prefill
 
     def recorder(items):
         if eng.last_stats.recurrent_batches % 5 == 0:
             recorded.append(([it.req.slot for it in items], [it.position for it in items]))
+        rec_positions.append([it.position for it in items])
         return orig(items)
+
+    def coda_recorder(items):
+        coda_sizes.append(len(items))
+        return orig_coda(items)
+
+    def prefill_recorder(batch):
+        prefill_batches.append((sum(q for _r, _p, q, _h in batch), sum(int(h) for *_x, h in batch)))
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        out = orig_prefill(batch)
+        b.record(stream)
+        prefill_events.append((a, b))
+        return out
 
     peaks_path = ROOT / "MEASURED_PEAKS.json"
     peak_gbs = json.loads(peaks_path.read_text())["hbm_gbs"] if peaks_path.exists() else 6650.0
@@ -276,9 +333,9 @@ def run_b200(args) -> None:
         t0 = time.perf_counter()
         ev0.record(stream)
         for _ in range(args.steps):
-            eng._run_recurrent = recorder
+            eng._run_recurrent, eng._run_coda, eng._run_prefill = recorder, coda_recorder, prefill_recorder
             outs = step()
-            eng._run_recurrent = orig
+            eng._run_recurrent, eng._run_coda, eng._run_prefill = orig, orig_coda, orig_prefill
             gen_tokens += sum(len(o.generated_tokens) for o in outs)
         ev1.record(stream)
         torch.cuda.synchronize()
@@ -286,14 +343,23 @@ def run_b200(args) -> None:
         torch.cuda.nvtx.range_pop()
     dev_s = ev0.elapsed_time(ev1) / 1e3
     wall_s = t1 - t0
+    prefill_s = sum(a.elapsed_time(b) for a, b in prefill_events) / 1e3
+    local_dev_s = dev_s
     kernel_launches = eng.runner.stats.kernel_launches - launches0
     stats = eng.last_stats
+    decode_s, _, _ = aggregate(dev_s - prefill_s, 0.0, 0.0, device)
     dev_s, wall_s, total_tokens = aggregate(dev_s, wall_s, float(gen_tokens), device)
     if rank == 0:
         # 60 launches spread evenly over the timed steps (every 5th recurrent launch was recorded)
         sample = [recorded[int(i * len(recorded) / 60)] for i in range(60)] if len(recorded) > 60 else recorded
         roof = attention_roofline(eng, shape, sample, peak_gbs)
         roof["peak_source"] = peak_src
+        peaks = json.loads(peaks_path.read_text()) if peaks_path.exists() else {}
+        whole = step_roofline(
+            shape, rec_positions, coda_sizes, prefill_batches, local_dev_s, peak_gbs,
+            peaks.get("bf16_tflops_sustained", 1400.0),
+        )
+        whole["scope"] = "rank 0, all timed steps; peaks: measured HBM copy and sustained cuBLAS bf16"
         prompt_bytes = sum(len(p) for p in prompts) * 4 * 3
         line = {
             "metric": METRIC,
@@ -331,8 +397,15 @@ def run_b200(args) -> None:
                 "h2d_bytes_per_step": prompt_bytes,
                 "d2h_bytes_per_step": (gen_tokens // max(args.steps, 1)) * 8,
             },
+            "decode_only": {
+                "value": round(total_tokens / decode_s, 1),
+                "unit": UNIT,
+                "prefill_ms_per_step_rank0": round(prefill_s * 1e3 / args.steps, 2),
+                "definition": "generated tokens / (device time minus prefill launch time), max over ranks",
+            },
             "gpu_launches": kernel_launches,
             "roofline": roof,
+            "step_roofline": whole,
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -376,10 +449,20 @@ def cpu_baseline(seconds: float = 20.0) -> dict:
         if time.perf_counter() - t0 > seconds or runs >= 3:
             break
     dt = time.perf_counter() - t0
+    cpu_model = ""
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                cpu_model = ln.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
     return {
         "value": round(tokens / dt, 3),
         "unit": UNIT,
         "cores": threads,
+        "cpu_model": cpu_model,
+        "dtype": "fp32",
         "kind": "port",
         "sample": f"{runs} x generate of the first {len(prompts)} config-1 requests (prompts cut to 256 tokens), "
         f"{max_new[0]} new tokens each, fp32 on the host CPU",
