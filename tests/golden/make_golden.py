@@ -239,6 +239,41 @@ def replay_depths(result: dict, async_mode: bool) -> list[list[int]]:
     return [[s - 1 for s in ds] for ds in depths] if async_mode else depths
 
 
+def policies_main() -> None:
+    """``--policies``: the replayed schedule under the other KV layouts, into
+    ``ouro_cfg0_policies.json``: ``first_then_shared`` (2 slots, step s -> slot min(s, 1)) in both
+    timings, and ``depth_indexed`` at full depth (it only admits exits that wrote every slot)."""
+
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    gold = json.loads((HERE / "ouro_cfg0.json").read_text())
+    depths = next(r for r in gold["runs"] if r["name"] == "replay_refill")["exit_depths"]
+    at_least_1 = [[max(d, 1) for d in ds] for ds in depths]
+    full = [[CFG0.total_ut_steps - 1 for _ in ds] for ds in depths]
+    runs = []
+    for name, policy, dep, async_mode in (
+        ("replay_first_then_shared", "first_then_shared", at_least_1, False),
+        ("replay_first_then_shared_async", "first_then_shared", depths, True),
+        ("replay_depth_indexed_full", "depth_indexed", full, False),
+    ):
+        res, _ = run_case(name, kv_policy=policy, refill=True, live_gate=False, exit_depths=dep, async_mode=async_mode)
+        runs.append(res)
+    prompts, max_new = config0_workload()
+    payload = {
+        "generator": "tests/golden/make_golden.py --policies",
+        "shape": CFG0.__dict__,
+        "gate_std": GATE_STD,
+        "weights_seed": 0,
+        "prompts": prompts,
+        "max_new_tokens": max_new,
+        "block_size": 16,
+        "num_blocks": 4096,
+        "runs": runs,
+    }
+    (HERE / "ouro_cfg0_policies.json").write_text(json.dumps(payload, separators=(",", ":")))
+    for r in runs:
+        print(r["name"], r["stats"])
+
+
 def main() -> None:
     """``python tests/golden/make_golden.py [--async]``: the synchronous runs, or with ``--async``
     the same runs under the reference's default timing (use_async_batching=True,
@@ -298,4 +333,4 @@ def main() -> None:
 
 
 if __name__ == "__main__":
-    main()
+    policies_main() if "--policies" in sys.argv[1:] else main()

@@ -121,6 +121,28 @@ def test_async_schedule_matches_reference(name):
     assert eng.last_stats.scheduler_refills == run["stats"]["scheduler_refills"]
 
 
+@pytest.mark.parametrize(
+    "name", ["replay_first_then_shared", "replay_first_then_shared_async", "replay_depth_indexed_full"]
+)
+def test_kv_policy_schedule_matches_reference(name):
+    """The other KV layouts (``tests/golden/ouro_cfg0_policies.json``): first_then_shared, whose
+    recurrent batches are slot-homogeneous over 2 slots, in both timings, and depth_indexed at
+    full depth over 4 slots; launches and block tables bit-exact."""
+
+    data = json.loads((GOLDEN / "ouro_cfg0_policies.json").read_text())
+    shape = OuroShape(**data["shape"])
+    run = next(r for r in data["runs"] if r["name"] == name)
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+    eng = _engine(shape, sd, kv_policy=run["kv_policy"], refill=run["refill"], async_mode=run["async"])
+    eng.record_trace = True
+    eng.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"]
+    )
+    assert eng.launch_trace == run["launches"]
+    hist = {str(k): v for k, v in sorted(eng.last_stats.exit_depth_histogram.items())}
+    assert hist == run["stats"]["exit_depth_histogram"]
+
+
 def exit_agreement(outs, run) -> float:
     """Fraction of tokens whose exit step equals the reference run's (read from its coda launches)."""
 

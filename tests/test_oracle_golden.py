@@ -41,6 +41,11 @@ def golden_async():
     return _load_ouro("ouro_cfg0_async.json")
 
 
+@pytest.fixture(scope="module")
+def golden_policies():
+    return _load_ouro("ouro_cfg0_policies.json")
+
+
 def _config(run: dict, data: dict) -> OracleConfig:
     return OracleConfig(
         block_size=data["block_size"],
@@ -84,6 +89,23 @@ def test_oracle_reproduces_reference_async_run(golden_async, name):
         logits = np.load(GOLDEN / "ouro_cfg0_async_logits.npz")
         for i in range(6):
             np.testing.assert_allclose(engine.logits[i][1].numpy(), logits[f"{name}_{i}"], rtol=0, atol=1e-5)
+
+
+@pytest.mark.parametrize(
+    "name", ["replay_first_then_shared", "replay_first_then_shared_async", "replay_depth_indexed_full"]
+)
+def test_oracle_reproduces_reference_kv_policy_run(golden_policies, name):
+    """The other KV layouts: first_then_shared (2 slots, step s -> slot min(s, 1); slot-homogeneous
+    recurrent batches) in both timings, and depth_indexed at full depth (4 slots)."""
+
+    data, shape, sd = golden_policies
+    run = next(r for r in data["runs"] if r["name"] == name)
+    engine = OracleEngine(shape, sd, _config(run, data), torch.float32)
+    tokens = engine.generate(data["prompts"], data["max_new_tokens"], exit_depths=run["exit_depths"])
+    assert tokens == run["tokens"]
+    assert engine.launches == run["launches"]
+    assert exit_depth_histogram(engine) == run["stats"]["exit_depth_histogram"]
+    assert engine.refills == run["stats"]["scheduler_refills"]
 
 
 @pytest.mark.parametrize("name", ["live_gate_refill", "replay_refill", "replay_norefill", "replay_last_exited"])
