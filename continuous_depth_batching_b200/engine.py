@@ -32,8 +32,8 @@ from enum import IntEnum
 
 import torch
 
-from .config import ContinuousDepthBatchingConfig
-from .kv_cache import copies_exit_kv, kv_slot_for_step
+from .config import ContinuousDepthBatchingConfig, validate_exit_threshold
+from .kv_cache import copies_exit_kv, kv_slot_for_step, resolve_kv_slots_per_layer
 from .huginn import HuginnShape
 from .huginn_runner import HuginnRunner
 from .ouro import OuroShape
@@ -249,6 +249,9 @@ class ContinuousDepthBatchingEngine:
             oshape = OuroShape.from_config(config)
             shape = OuroShape(**{**oshape.__dict__, "total_ut_steps": cfg.max_recurrent_steps})
             runner_cls = OuroRunner
+        # The adapters' exit specs: Ouro's gate is a cumulative hazard, Huginn's a direct threshold
+        # on the latent difference (adapters/ouro.py:293-299, adapters/huginn.py:63-66).
+        validate_exit_threshold(cfg.exit_threshold, "direct" if model_type == "huginn" else "hazard")
         if shape.num_key_value_heads != shape.num_attention_heads:
             raise NotImplementedError("the paged decode kernel serves MHA (num_key_value_heads == num_attention_heads)")
         if device is None:
@@ -1018,11 +1021,24 @@ class ContinuousDepthBatchingEngine:
     # ------------------------------------------------------------------ validation
     def _validate(self, input_ids, max_new_tokens, exit_depths, model_kwargs) -> None:
         cfg = self.cdb_config
+        self._validate_generate_inputs(input_ids, max_new_tokens)
+        if cfg.exit_threshold is not None and model_kwargs is not None and model_kwargs.get("use_early_exit_gate") is False:
+            raise ValueError("exit_threshold CDB requires use_early_exit_gate to stay enabled")
+        mnt = max_new_tokens if isinstance(max_new_tokens, list) else [max_new_tokens] * len(input_ids)
+        mnt = [min(m, cfg.max_model_len - len(p)) for m, p in zip(mnt, input_ids, strict=True)]
+        self._validate_exit_depths(input_ids, mnt, exit_depths)
+
+    @staticmethod
+    def _validate_generate_inputs(input_ids: list[list[int]], max_new_tokens: int | list[int]) -> None:
+        """Token-level input checks before scheduling (``continuous_api.py:1766-1785``)."""
+
         if not input_ids:
             raise ValueError("input_ids must contain at least one prompt")
         if isinstance(max_new_tokens, list):
             if len(max_new_tokens) != len(input_ids):
-                raise ValueError(f"max_new_tokens has {len(max_new_tokens)} entries but there are {len(input_ids)} prompts")
+                raise ValueError(
+                    f"max_new_tokens has {len(max_new_tokens)} entries but there are {len(input_ids)} prompts"
+                )
             bad = [i for i, v in enumerate(max_new_tokens) if v < 1]
             if bad:
                 raise ValueError(f"max_new_tokens must be >= 1 for every request, but got <1 at indices {bad}")
@@ -1031,35 +1047,46 @@ class ContinuousDepthBatchingEngine:
         empty = [i for i, p in enumerate(input_ids) if not p]
         if empty:
             raise ValueError(f"input_ids contains empty prompts at indices {empty}")
-        if cfg.exit_threshold is not None and model_kwargs is not None and model_kwargs.get("use_early_exit_gate") is False:
-            raise ValueError("exit_threshold CDB requires use_early_exit_gate to stay enabled")
+
+    def _validate_exit_depths(self, input_ids, max_new_tokens: list[int], exit_depths) -> None:
+        """A replay schedule against the config and lengths (``continuous_api.py:1787-1836``);
+        ``max_new_tokens`` is per request, already capped by ``max_model_len``."""
+
+        cfg = self.cdb_config
         if exit_depths is None:
             return
         if not cfg.synthetic_exit_replay:
             raise ValueError("exit_depths requires cdb_config.synthetic_exit_replay=True")
+        if cfg.exit_threshold is not None:
+            raise ValueError("exit_depths cannot be combined with exit_threshold")
         if len(exit_depths) != len(input_ids):
             raise ValueError(f"exit_depths has {len(exit_depths)} entries but there are {len(input_ids)} requests")
-        mnt = max_new_tokens if isinstance(max_new_tokens, list) else [max_new_tokens] * len(input_ids)
-        mnt = [min(m, cfg.max_model_len - len(p)) for m, p in zip(mnt, input_ids, strict=True)]
         steps = cfg.max_recurrent_steps
         for idx, depths in enumerate(exit_depths):
-            if len(depths) != mnt[idx] - 1:
+            if len(depths) != max_new_tokens[idx] - 1:
                 raise ValueError(
-                    f"exit_depths[{idx}] has {len(depths)} entries but the request stages {mnt[idx] - 1} decode tokens "
-                    "(max_new_tokens - 1)"
+                    f"exit_depths[{idx}] has {len(depths)} entries but the request stages {max_new_tokens[idx] - 1} "
+                    "decode tokens (max_new_tokens - 1)"
                 )
             for d in depths:
                 if not 0 <= d < steps:
-                    raise ValueError(f"exit_depths[{idx}] value {d} is out of range [0, {steps}); values are 0-based")
+                    raise ValueError(
+                        f"exit_depths[{idx}] value {d} is out of range [0, {steps}); values are 0-based "
+                        "recurrent steps"
+                    )
         if copies_exit_kv(cfg.kv_policy):
+            # copy-on-exit routing fills the deeper slots at exit time, so any replay depth is safe
             return
+        slots = resolve_kv_slots_per_layer(
+            cfg.kv_policy, total_recurrent_steps=steps, requested_slots=cfg.kv_slots_per_layer
+        )
         extra = int(cfg.use_async_batching and cfg.delay_gate_consumption)  # continuous_api.py:1826
         for depths in exit_depths:
             for d in depths:
-                if d + 1 + extra < cfg.kv_slots_per_layer:
+                if d + 1 + extra < slots:
                     raise ValueError(
                         "Every replay exit depth must write all static KV slots before exit: "
-                        f"kv_slots_per_layer={cfg.kv_slots_per_layer}, exit step {d + 1 + extra}"
+                        f"kv_slots_per_layer={slots}, exit step {d + 1 + extra}"
                     )
 
 

@@ -37,8 +37,10 @@ def resolve_kv_slots_per_layer(policy: str, *, total_recurrent_steps: int, reque
             raise ValueError(f"Policy {policy!r} uses exactly {slots} KV slot(s) per layer, got {requested_slots}")
         return slots
     slots = 2 if requested_slots is None else requested_slots
-    if slots <= 0 or slots > total_recurrent_steps:
-        raise ValueError(f"kv_slots_per_layer={slots} must be in [1, {total_recurrent_steps}]")
+    if slots <= 0:
+        raise ValueError(f"kv_slots_per_layer must be positive, got {slots}")
+    if slots > total_recurrent_steps:
+        raise ValueError(f"kv_slots_per_layer={slots} exceeds total_recurrent_steps={total_recurrent_steps}")
     return slots
 
 
