@@ -759,12 +759,11 @@ class ContinuousDepthBatchingEngine:
         by_step: dict[int, list[_Item]] = {}
         for it, step in backlog:
             by_step.setdefault(step, []).append(it)
-        bs, L = self.cdb_config.block_size, self.runner.num_core_layers
-        layer_of = self.runner.core_cache_layer
+        bs = self.cdb_config.block_size
+        layout = self.runner.layout
         for step, items in sorted(by_step.items()):
             rows = [self.pool.tables[it.req.idx][it.position // bs] * bs + it.position % bs for it in items]
-            src = self._slot_of_step(step)
-            pairs = [(layer_of(src, l), layer_of(t, l)) for l in range(L) for t in range(src + 1, self.slots)]
+            pairs = [(src_layer, t) for src_layer, targets in layout.exit_copy_layer_groups(step) for t in targets]
             self.runner.exit_kv_copy(rows, pairs)
             self.last_stats.exit_kv_copies += len(rows)
 

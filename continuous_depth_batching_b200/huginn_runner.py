@@ -32,6 +32,7 @@ import torch
 
 from . import _lib
 from .huginn import BLOCK_NORM_NAMES, STAGES, HuginnShape, huginn_rope_tables
+from .kv_cache import LoopedKvLayout
 from .runner import SCRATCH_ITEMS, OuroRunner
 
 
@@ -106,13 +107,17 @@ class HuginnRunner(OuroRunner):
         gemm_backend: str = "tcgen05",
         fused_lm_head: bool = True,
     ) -> None:
-        P, C, Dc = shape.n_layers_in_prelude, shape.n_layers_in_recurrent_block, shape.n_layers_in_coda
+        layout = LoopedKvLayout(
+            num_prelude_layers=shape.n_layers_in_prelude, num_core_layers=shape.n_layers_in_recurrent_block,
+            num_coda_layers=shape.n_layers_in_coda, total_recurrent_steps=shape.total_recurrent_steps,
+            policy=kv_policy, requested_slots=kv_slots_per_layer,
+        )
         self._init_device(
             shape,
             device=device,
             kv_policy=kv_policy,
             kv_slots_per_layer=kv_slots_per_layer,
-            num_cache_layers=P + kv_slots_per_layer * C + Dc,
+            layout=layout,
             num_blocks=num_blocks,
             block_size=block_size,
             max_model_len=max_model_len,
@@ -148,21 +153,10 @@ class HuginnRunner(OuroRunner):
         self.rope_cos, self.rope_sin = huginn_rope_tables(shape, max_model_len + 1, device)
 
     # ------------------------------------------------------------------ cache-layer layout
-    @property
-    def num_core_layers(self) -> int:
-        return self.shape.n_layers_in_recurrent_block
-
-    def core_cache_layer(self, slot: int, layer: int) -> int:
-        """``LoopedKvLayout.core_layer_index`` (``kv_cache_policy.py:214-227``)."""
-
-        s = self.shape
-        return s.n_layers_in_prelude + slot * s.n_layers_in_recurrent_block + layer
-
     def coda_cache_layer(self, layer: int) -> int:
         """``LoopedKvLayout.coda_layer_index`` (``kv_cache_policy.py:229-233``)."""
 
-        s = self.shape
-        return s.n_layers_in_prelude + self.slots * s.n_layers_in_recurrent_block + layer
+        return self.layout.coda_layer_index(layer)
 
     # ------------------------------------------------------------------ launch helpers
     def _attention_biased(self, n: int, cache_layer: int, item_slot, item_pos, qk_bias) -> None:

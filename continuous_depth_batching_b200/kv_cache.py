@@ -2,7 +2,7 @@
 
 * Slot arithmetic restates ``looped_cdb/kv_cache_policy.py`` (``resolve_kv_slots_per_layer``
   ``:52-79``, ``kv_slot_for_step`` ``:82-103``, ``kv_layer_index`` ``:106-128``,
-  ``LoopedKvLayout.exit_copy_layer_groups`` ``:235-258``) for the four policies.
+  ``LoopedKvLayout`` ``:135-258``) for the four policies.
 * :class:`BlockPool` is the host owner of physical block ids with the reference's FIFO order
   (``continuous_batching/cache_manager.py:33-91``: allocate pops the left of a deque, free
   appends in the request's block order), so block ids - and every block table - come out
@@ -54,6 +54,74 @@ def kv_slot_for_step(recurrent_step: int, *, policy: str, slots_per_layer: int) 
 
 def copies_exit_kv(policy: str) -> bool:
     return policy == "last_exited"
+
+
+class LoopedKvLayout:
+    """Cache-layer numbering of a looped model (``LoopedKvLayout``, ``kv_cache_policy.py:135-258``):
+    prelude layers first (one slot each), then the core layers slot-major (slot s, layer l ->
+    prelude + s * core + l), then the coda layers. Ouro is all core; Huginn has all three stages."""
+
+    def __init__(self, *, num_prelude_layers: int, num_core_layers: int, num_coda_layers: int,
+                 total_recurrent_steps: int, policy: str, requested_slots: int | None = None) -> None:
+        if num_prelude_layers < 0 or num_coda_layers < 0:
+            raise ValueError("prelude and coda layer counts must be non-negative")
+        if num_core_layers <= 0:
+            raise ValueError(f"num_core_layers must be positive, got {num_core_layers}")
+        self.num_prelude_layers = num_prelude_layers
+        self.num_core_layers = num_core_layers
+        self.num_coda_layers = num_coda_layers
+        self.total_recurrent_steps = total_recurrent_steps
+        self.policy = policy
+        self.slots_per_layer = resolve_kv_slots_per_layer(
+            policy, total_recurrent_steps=total_recurrent_steps, requested_slots=requested_slots
+        )
+
+    @property
+    def num_cache_layers(self) -> int:
+        return self.num_prelude_layers + self.slots_per_layer * self.num_core_layers + self.num_coda_layers
+
+    def slot_for_step(self, recurrent_step: int) -> int:
+        if not 0 <= recurrent_step < self.total_recurrent_steps:
+            raise ValueError(f"recurrent_step must be in [0, {self.total_recurrent_steps}), got {recurrent_step}")
+        return kv_slot_for_step(recurrent_step, policy=self.policy, slots_per_layer=self.slots_per_layer)
+
+    @staticmethod
+    def _check(layer: int, count: int, stage: str) -> None:
+        if not 0 <= layer < count:
+            raise ValueError(f"{stage} layer must be in [0, {count}), got {layer}")
+
+    def prelude_layer_index(self, layer: int) -> int:
+        self._check(layer, self.num_prelude_layers, "prelude")
+        return layer
+
+    def core_slot_layer_index(self, slot: int, layer: int) -> int:
+        """Cache layer of core layer ``layer`` in KV slot ``slot``."""
+
+        self._check(layer, self.num_core_layers, "core")
+        if not 0 <= slot < self.slots_per_layer:
+            raise ValueError(f"slot must be in [0, {self.slots_per_layer}), got {slot}")
+        return self.num_prelude_layers + slot * self.num_core_layers + layer
+
+    def core_layer_index(self, layer: int, recurrent_step: int) -> int:
+        return self.core_slot_layer_index(self.slot_for_step(recurrent_step), layer)
+
+    def coda_layer_index(self, layer: int) -> int:
+        self._check(layer, self.num_coda_layers, "coda")
+        return self.num_prelude_layers + self.slots_per_layer * self.num_core_layers + layer
+
+    def exit_copy_layer_groups(self, exit_step: int) -> list[tuple[int, list[int]]]:
+        """Per core layer: (the cache layer the exit step wrote, the same layer in every deeper
+        slot). Empty when no deeper slot exists; only ``last_exited`` copies."""
+
+        src = self.slot_for_step(exit_step)
+        return [
+            (
+                self.core_slot_layer_index(src, layer),
+                [self.core_slot_layer_index(t, layer) for t in range(src + 1, self.slots_per_layer)],
+            )
+            for layer in range(self.num_core_layers)
+            if src + 1 < self.slots_per_layer
+        ]
 
 
 class BlockPool:

@@ -26,7 +26,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from .kv_cache import PagedKVPool, kv_slot_for_step
+from .kv_cache import LoopedKvLayout, PagedKVPool, kv_slot_for_step
 from .ouro import LAYER_NORM_NAMES, OuroShape
 
 SCRATCH_ITEMS = 256
@@ -175,7 +175,10 @@ class OuroRunner:
             device=device,
             kv_policy=kv_policy,
             kv_slots_per_layer=kv_slots_per_layer,
-            num_cache_layers=kv_slots_per_layer * shape.num_hidden_layers,
+            layout=LoopedKvLayout(
+                num_prelude_layers=0, num_core_layers=shape.num_hidden_layers, num_coda_layers=0,
+                total_recurrent_steps=shape.total_ut_steps, policy=kv_policy, requested_slots=kv_slots_per_layer,
+            ),
             num_blocks=num_blocks,
             block_size=block_size,
             max_model_len=max_model_len,
@@ -222,7 +225,7 @@ class OuroRunner:
         device: torch.device,
         kv_policy: str,
         kv_slots_per_layer: int,
-        num_cache_layers: int,
+        layout: LoopedKvLayout,
         num_blocks: int,
         block_size: int,
         max_model_len: int,
@@ -249,8 +252,9 @@ class OuroRunner:
         self.max_num_seqs = max_num_seqs
         self.use_cuda_graph = use_cuda_graph
         self.gemm_backend = gemm_backend
+        self.layout = layout
         self.pool = PagedKVPool(
-            num_cache_layers=num_cache_layers,
+            num_cache_layers=layout.num_cache_layers,
             num_blocks=num_blocks,
             block_size=block_size,
             num_kv_heads=shape.num_key_value_heads,
@@ -315,12 +319,13 @@ class OuroRunner:
     def num_core_layers(self) -> int:
         """Physical layers one recurrent step runs (the ones whose KV is replicated per slot)."""
 
-        return self.shape.num_hidden_layers
+        return self.layout.num_core_layers
 
     def core_cache_layer(self, slot: int, layer: int) -> int:
-        """Cache layer of a recurrent layer at a KV slot (``kv_cache_policy.py:106-128``)."""
+        """Cache layer of a recurrent layer at a KV slot (``LoopedKvLayout.core_layer_index``,
+        ``kv_cache_policy.py:214-227``)."""
 
-        return slot * self.shape.num_hidden_layers + layer
+        return self.layout.core_slot_layer_index(slot, layer)
 
     # ------------------------------------------------------------------ small helpers
     def reset(self, log_capacity: int) -> None:
