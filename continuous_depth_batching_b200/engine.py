@@ -459,6 +459,10 @@ class ContinuousDepthBatchingEngine:
         return False
 
     def _host_tokens(self, r: _Req) -> list[int]:
+        """The tokens the request has continued with so far (the forced ones under teacher forcing)."""
+
+        if self._forced is not None:
+            return list(self._forced[r.idx][: r.generated])
         return self.runner.token_log[r.log_base : r.log_base + r.generated].cpu().tolist()
 
     def _next_token_id(self, r: _Req) -> int:
@@ -643,6 +647,13 @@ class ContinuousDepthBatchingEngine:
         return sampled
 
     def _sync_tokens(self, reqs: list[_Req]) -> None:
+        """Host copies of the tokens about to be recorded, for the EOS / stop-sequence checks. Under
+        teacher forcing the sequence continues with the forced token, so that one decides."""
+
+        if self._forced is not None:
+            for r in reqs:
+                r.pending_token = int(self._forced[r.idx][r.generated])
+            return
         self.last_stats.host_syncs += 1
         self.runner.stream.synchronize()
         for r in reqs:

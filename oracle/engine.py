@@ -190,13 +190,17 @@ class OracleEngine:
 
     # ------------------------------------------------------------------ request bookkeeping
     def _update(self, r: Req, token: int) -> bool:
-        """``RequestState.update_and_check_completion`` (``continuous_batching/requests.py:185-218``), eos=None."""
+        """``RequestState.update_and_check_completion`` (``continuous_batching/requests.py:209-250``):
+        an EOS id is kept and finishes the request, as does the length limit or a generated tail
+        equal to a stop sequence."""
 
         r.in_flight_tokens = max(0, r.in_flight_tokens - 1)
-        if len(r.generated) < r.max_new:
+        is_eos = token in self.eos
+        if is_eos or len(r.generated) < r.max_new:
             r.generated.append(token)
             r.to_process = [token]
-        if len(r.generated) >= r.max_new:
+        stop = any(len(q) and len(r.generated) >= len(q) and r.generated[-len(q):] == q for q in self.stops)
+        if is_eos or len(r.generated) >= r.max_new or stop:
             r.status = FINISHED
             return True
         return False
@@ -653,8 +657,12 @@ class OracleEngine:
         max_new_tokens: list[int],
         exit_depths: list[list[int]] | None = None,
         forced_tokens: list[list[int]] | None = None,
+        eos_token_ids: list[int] | None = None,
+        stop_sequences: list[list[int]] | None = None,
     ) -> list[list[int]]:
         cfg = self.cfg
+        self.eos = set(eos_token_ids or [])
+        self.stops = [list(q) for q in (stop_sequences or [])]
         caps = [min(m, cfg.max_model_len - len(p)) for m, p in zip(max_new_tokens, prompts, strict=True)]
         self.free: deque[int] = deque(range(cfg.num_blocks))
         self.tables: dict[int, list[int]] = {}

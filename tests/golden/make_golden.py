@@ -163,7 +163,8 @@ class Recorder:
 
 
 def run_case(
-    name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_depths=None, num_blocks=4096, async_mode=False
+    name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_depths=None, num_blocks=4096, async_mode=False,
+    eos_token_id=None, stop_sequences=None,
 ):
     from looped_cdb.continuous_depth_batching import ContinuousDepthBatchingConfig, ContinuousDepthBatchingEngine
 
@@ -187,7 +188,8 @@ def run_case(
     rec = Recorder(engine)
     with torch.no_grad():
         outs = engine.generate_batch(
-            prompts, max_new_tokens=max_new, eos_token_id=None, warmup=False, exit_depths=exit_depths
+            prompts, max_new_tokens=max_new, eos_token_id=eos_token_id, stop_sequences=stop_sequences, warmup=False,
+            exit_depths=exit_depths,
         )
     states_exit = {}
     for st in list(engine.scheduler.active_requests.values()):
@@ -199,6 +201,8 @@ def run_case(
         "refill": refill,
         "live_gate": live_gate,
         "async": async_mode,
+        "eos_token_id": eos_token_id,
+        "stop_sequences": stop_sequences,
         "tokens": [o.generated_tokens for o in outs],
         "exit_depths": exit_depths,
         "stats": {
@@ -237,6 +241,38 @@ def replay_depths(result: dict, async_mode: bool) -> list[list[int]]:
 
     depths = recorded_exit_depths(result)
     return [[s - 1 for s in ds] for ds in depths] if async_mode else depths
+
+
+def finish_main() -> None:
+    """``--finish``: the replayed schedule with requests finishing early on EOS ids [363, 924] or
+    the stop sequences [[314, 314], [585, 585]] (ids the seeded model emits), refill on and off,
+    into ``ouro_cfg0_finish.json``."""
+
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    gold = json.loads((HERE / "ouro_cfg0.json").read_text())
+    depths = next(r for r in gold["runs"] if r["name"] == "replay_refill")["exit_depths"]
+    runs = []
+    for name, refill in (("replay_refill_eos_stop", True), ("replay_norefill_eos_stop", False)):
+        res, _ = run_case(
+            name, kv_policy="single", refill=refill, live_gate=False, exit_depths=depths,
+            eos_token_id=[363, 924], stop_sequences=[[314, 314], [585, 585]],
+        )
+        runs.append(res)
+    prompts, max_new = config0_workload()
+    payload = {
+        "generator": "tests/golden/make_golden.py --finish",
+        "shape": CFG0.__dict__,
+        "gate_std": GATE_STD,
+        "weights_seed": 0,
+        "prompts": prompts,
+        "max_new_tokens": max_new,
+        "block_size": 16,
+        "num_blocks": 4096,
+        "runs": runs,
+    }
+    (HERE / "ouro_cfg0_finish.json").write_text(json.dumps(payload, separators=(",", ":")))
+    for r in runs:
+        print(r["name"], r["stats"], [len(t) for t in r["tokens"]])
 
 
 def policies_main() -> None:
@@ -333,4 +369,9 @@ def main() -> None:
 
 
 if __name__ == "__main__":
-    policies_main() if "--policies" in sys.argv[1:] else main()
+    if "--policies" in sys.argv[1:]:
+        policies_main()
+    elif "--finish" in sys.argv[1:]:
+        finish_main()
+    else:
+        main()

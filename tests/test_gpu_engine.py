@@ -143,6 +143,26 @@ def test_kv_policy_schedule_matches_reference(name):
     assert hist == run["stats"]["exit_depth_histogram"]
 
 
+@pytest.mark.parametrize("name", ["replay_refill_eos_stop", "replay_norefill_eos_stop"])
+def test_early_finish_schedule_matches_reference(name):
+    """Requests ending on EOS ids or stop sequences (``tests/golden/ouro_cfg0_finish.json``),
+    teacher-forced on the reference's tokens so that the finishing tokens are the reference's:
+    the launch trace, block tables and output lengths equal the reference's."""
+
+    data = json.loads((GOLDEN / "ouro_cfg0_finish.json").read_text())
+    shape = OuroShape(**data["shape"])
+    run = next(r for r in data["runs"] if r["name"] == name)
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+    eng = _engine(shape, sd, refill=run["refill"])
+    eng.record_trace = True
+    outs = eng.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=run["eos_token_id"],
+        stop_sequences=run["stop_sequences"], exit_depths=run["exit_depths"], forced_tokens=run["tokens"],
+    )
+    assert eng.launch_trace == run["launches"]
+    assert [len(o.generated_tokens) for o in outs] == [len(t) for t in run["tokens"]]
+
+
 def exit_agreement(outs, run) -> float:
     """Fraction of tokens whose exit step equals the reference run's (read from its coda launches)."""
 

@@ -108,6 +108,22 @@ def test_oracle_reproduces_reference_kv_policy_run(golden_policies, name):
     assert engine.refills == run["stats"]["scheduler_refills"]
 
 
+@pytest.mark.parametrize("name", ["replay_refill_eos_stop", "replay_norefill_eos_stop"])
+def test_oracle_reproduces_reference_early_finish_run(name):
+    """Requests finishing on EOS ids (kept in the output) or on stop sequences, refill on and off."""
+
+    data, shape, sd = _load_ouro("ouro_cfg0_finish.json")
+    run = next(r for r in data["runs"] if r["name"] == name)
+    engine = OracleEngine(shape, sd, _config(run, data), torch.float32)
+    tokens = engine.generate(
+        data["prompts"], data["max_new_tokens"], exit_depths=run["exit_depths"], eos_token_ids=run["eos_token_id"],
+        stop_sequences=run["stop_sequences"],
+    )
+    assert tokens == run["tokens"]
+    assert engine.launches == run["launches"]
+    assert exit_depth_histogram(engine) == run["stats"]["exit_depth_histogram"]
+
+
 @pytest.mark.parametrize("name", ["live_gate_refill", "replay_refill", "replay_norefill", "replay_last_exited"])
 def test_oracle_reproduces_reference_run(golden, name):
     data, shape, sd = golden
