@@ -305,13 +305,7 @@ class ContinuousDepthBatchingEngine:
 
         del warmup, record_queue_samples
         cfg = self.cdb_config
-        self._validate(input_ids, max_new_tokens, exit_depths, model_kwargs)
-        if isinstance(max_new_tokens, int):
-            max_new_tokens = [max_new_tokens] * len(input_ids)
-        too_long = [i for i, p in enumerate(input_ids) if len(p) >= cfg.max_model_len]
-        if too_long:
-            raise ValueError(f"{len(too_long)} prompt(s) have length >= max_model_len ({cfg.max_model_len})")
-        caps = [min(m, cfg.max_model_len - len(p)) for m, p in zip(max_new_tokens, input_ids, strict=True)]
+        caps = self._validate(input_ids, max_new_tokens, exit_depths, model_kwargs)
         eos = set()
         if eos_token_id is not None:
             for t in [eos_token_id] if isinstance(eos_token_id, int) else eos_token_id:
@@ -1029,14 +1023,17 @@ class ContinuousDepthBatchingEngine:
                 self._consume_coda(exited, stage=False)
 
     # ------------------------------------------------------------------ validation
-    def _validate(self, input_ids, max_new_tokens, exit_depths, model_kwargs) -> None:
+    def _validate(self, input_ids, max_new_tokens, exit_depths, model_kwargs) -> list[int]:
+        """All checks of generate_batch's arguments; returns the per-request token caps."""
+
         cfg = self.cdb_config
         self._validate_generate_inputs(input_ids, max_new_tokens)
         if cfg.exit_threshold is not None and model_kwargs is not None and model_kwargs.get("use_early_exit_gate") is False:
             raise ValueError("exit_threshold CDB requires use_early_exit_gate to stay enabled")
         mnt = max_new_tokens if isinstance(max_new_tokens, list) else [max_new_tokens] * len(input_ids)
-        mnt = [min(m, cfg.max_model_len - len(p)) for m, p in zip(mnt, input_ids, strict=True)]
-        self._validate_exit_depths(input_ids, mnt, exit_depths)
+        caps = cap_max_new_tokens_to_model_len(input_ids, mnt, cfg.max_model_len)
+        self._validate_exit_depths(input_ids, caps, exit_depths)
+        return caps
 
     @staticmethod
     def _validate_generate_inputs(input_ids: list[list[int]], max_new_tokens: int | list[int]) -> None:
@@ -1098,6 +1095,25 @@ class ContinuousDepthBatchingEngine:
                         "Every replay exit depth must write all static KV slots before exit: "
                         f"kv_slots_per_layer={slots}, exit step {d + 1 + extra}"
                     )
+
+
+def cap_max_new_tokens_to_model_len(input_ids: list[list[int]], max_new_tokens: list[int],
+                                    max_model_len: int | None) -> list[int]:
+    """Prompt + generation within ``max_model_len`` (``utils.py:70-97``): a prompt with no room for
+    a single generated token is refused (the whole batch), every other request's budget is clamped
+    to ``max_model_len - len(prompt)`` (a length finish); no-op without a limit."""
+
+    if max_model_len is None:
+        return max_new_tokens
+    over = [(i, len(p)) for i, p in enumerate(input_ids) if len(p) >= max_model_len]
+    if over:
+        shown = ", ".join(f"request {i} (len {n})" for i, n in over[:5])
+        more = " ..." if len(over) > 5 else ""
+        raise ValueError(
+            f"{len(over)} prompt(s) have length >= max_model_len ({max_model_len}) and leave no room "
+            f"for a generated token: {shown}{more}. Filter or truncate them before serving."
+        )
+    return [min(m, max_model_len - len(p)) for m, p in zip(max_new_tokens, input_ids, strict=True)]
 
 
 def _auto_num_blocks(shape: OuroShape | HuginnShape, cfg: ContinuousDepthBatchingConfig, device: torch.device) -> int:

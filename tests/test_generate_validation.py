@@ -67,3 +67,24 @@ def test_replay_schedules_accepted():
         [[5]], [3], [[0, 0]]
     )
     _engine(synthetic_exit_replay=True)._validate_exit_depths([[5]], [3], None)
+
+
+def test_model_len_caps_and_refusals():
+    from continuous_depth_batching_b200.engine import cap_max_new_tokens_to_model_len as cap
+
+    mnt = [4, 4, 4]
+    assert cap([[1], [2], [3]], mnt, None) is mnt
+    assert cap([[0] * 2, [0] * 8, [0] * 3], [5, 5, 5], 10) == [5, 2, 5]
+    assert cap([[0] * 9], [16], 10) == [1]  # one below the limit: exactly one token
+    with pytest.raises(ValueError, match=r"1 prompt\(s\) have length >= max_model_len \(10\).*request 1 \(len 10\)"):
+        cap([[0] * 5, [0] * 10], [4, 4], 10)
+    with pytest.raises(ValueError, match="max_model_len"):
+        cap([[0] * 11], [4], 10)
+
+
+def test_replay_schedule_checked_against_capped_lengths():
+    eng = _engine(synthetic_exit_replay=True, max_model_len=12)
+    # the 10-token prompt leaves 2 tokens, so its schedule holds max_new - 1 = 1 depth
+    assert eng._validate([[1] * 10], 5, [[0]], None) == [2]
+    with pytest.raises(ValueError, match="stages 1 decode tokens"):
+        eng._validate([[1] * 10], 5, [[0, 0, 0, 0]], None)
