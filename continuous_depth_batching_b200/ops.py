@@ -12,7 +12,9 @@ tensors (there is no CPU path). Each wraps one ``include/cdb_b200.h`` entry poin
 * ``cdb::add_rmsnorm(x, a, w_a, w_next, y)``: ``x += norm_a(a)``, ``y = norm_next(x)``
   (``cdb_add_rmsnorm``);
 * ``cdb::paged_decode_attention(...)``: RoPE, KV append and paged decode attention in one
-  launch (``cdb_paged_decode_attn_append_static``, which needs no caller scratch);
+  launch (``cdb_paged_decode_attn_append_static``, which needs no caller scratch: its plan and
+  split scratch are one static array per GPU, so calls on one GPU must be ordered, e.g. one
+  stream);
 * ``cdb::exit_gate_route(...)``: exit decision, routing and compaction of one recurrent launch
   (``cdb_exit_gate_route``).
 """
