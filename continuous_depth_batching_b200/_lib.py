@@ -108,6 +108,11 @@ _SIGNATURES: dict[str, list] = {
         c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
         c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_int, c_void_p, c_void_p,
     ],
+    "cdb_schedule_tick": [
+        c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int,
+        c_int, c_int, c_int, c_void_p, c_void_p,
+    ],
+    "cdb_schedule_queues_init": [c_void_p, c_int, c_void_p],
     "cdb_block_pool_init": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p],
     "cdb_block_alloc": [
         c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
@@ -168,7 +173,9 @@ def stream_ptr(stream: torch.cuda.Stream | None = None) -> int:
     return s.cuda_stream
 
 
-_NO_LAUNCH = {"cdb_version", "cdb_status_string", "cdb_attn_scratch_bytes", "cdb_gemm_workspace_elems"}
+_NO_LAUNCH = {
+    "cdb_version", "cdb_status_string", "cdb_attn_scratch_bytes", "cdb_gemm_workspace_elems", "cdb_schedule_queues_init",
+}
 # Kernels enqueued through this binding (device work only; graph replays are counted by the runner).
 launch_count = 0
 

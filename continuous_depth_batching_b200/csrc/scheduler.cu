@@ -324,3 +324,170 @@ extern "C" int cdb_build_tables(const int32_t* block_table, int64_t block_table_
              out_stride, cu_seq_lens_q, cu_seq_lens_k, status);
   return sched_launched();
 }
+
+// ------------------------------------------------------------------ scheduler tick on device queues
+namespace cdb {
+
+constexpr int kTickCap = 2048;  // items a queue may hold (both rings staged in shared memory)
+
+// One CDBScheduler tick on device-resident queues (CDBScheduler.schedule_next, scheduler.py:101-140,
+// with the queue operations of enqueue_depth / enqueue_depth_front / enqueue_coda, :142-186, and the
+// slot-homogeneous FIFO pop of _schedule_recurrent_batch, :322-346), in the order the engine applies
+// them between two launches: the last recurrent batch's survivors return to the head of the depth
+// queue in batch order with their step advanced and its exits join the coda queue; prefill successors
+// are appended; coda successors go to the head in order. Then the tick's work is chosen: a coda batch
+// when the coda queue holds min_coda items, else prefill when the host admits it, else a recurrent
+// batch of up to max_seqs items sharing the head item's KV slot (the others keep their order), else a
+// coda flush. The rings are staged in shared memory and the order-dependent part runs on one thread:
+// it is a few hundred integer steps.
+__global__ void __launch_bounds__(kSchedThreads) schedule_tick_kernel(
+    int32_t* state, int32_t* ready, int32_t* coda, int32_t* item_step, const int32_t* routed,
+    const int8_t* exit_flag, int n_routed, const int32_t* back, int n_back, const int32_t* front, int n_front,
+    int min_coda, int max_seqs, int prefill_admit, int slots, int32_t* out) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ int32_t R[2][kTickCap], Q[2][kTickCap];
+  __shared__ int s_rc, s_cc, s_kind, s_n, s_err;
+  const int cap = state[4];
+  const int rh = state[0], rc = state[1], ch = state[2], cc = state[3];
+  if (cap <= 0 || cap > kTickCap || rc < 0 || rc > cap || cc < 0 || cc > cap || rh < 0 || ch < 0) {
+    if (threadIdx.x == 0) {  // a ring the shared-memory staging cannot hold: report, change nothing
+      out[0] = -1;
+      out[1] = 0;
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < rc; i += blockDim.x) R[0][i] = ready[(rh + i) % cap];
+  for (int i = threadIdx.x; i < cc; i += blockDim.x) Q[0][i] = coda[(ch + i) % cap];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int err = 0;
+    int nr = rc, nc = cc, refills = state[5];
+    int32_t* r = R[0];
+    int32_t* rn = R[1];
+    // survivors to the head in batch order (step + 1), exits to the coda queue
+    int ns = 0;
+    for (int i = 0; i < n_routed; ++i)
+      if (!exit_flag[i]) ++ns;
+    if (nr + ns + n_back + n_front > cap || nc + n_routed > cap) {
+      err = 1;
+    } else {
+      int k = 0;
+      for (int i = 0; i < n_routed; ++i) {
+        const int id = routed[i];
+        if (exit_flag[i]) {
+          Q[0][nc++] = id;
+        } else {
+          item_step[id] += 1;
+          rn[k++] = id;
+        }
+      }
+      for (int i = 0; i < nr; ++i) rn[k++] = r[i];
+      nr = k;
+      int32_t* t = r;
+      r = rn;
+      rn = t;
+      // prefill successors at the back (a step-0 item joining a non-empty queue is a refill)
+      for (int i = 0; i < n_back; ++i) {
+        if (item_step[back[i]] == 0 && nr > 0) ++refills;
+        r[nr++] = back[i];
+      }
+      // coda successors to the head, in order (pushed one by one from the last)
+      for (int i = n_front - 1; i >= 0; --i)
+        if (item_step[front[i]] == 0 && nr + (n_front - 1 - i) > 0) ++refills;
+      k = 0;
+      for (int i = 0; i < n_front; ++i) rn[k++] = front[i];
+      for (int i = 0; i < nr; ++i) rn[k++] = r[i];
+      nr = k;
+      t = r;
+      r = rn;
+      rn = t;
+    }
+    // the tick's work
+    int kind = 0, n = 0;
+    if (!err) {
+      if (nc >= min_coda && nc > 0) {
+        kind = 1;
+      } else if (prefill_admit) {
+        kind = 2;
+      } else if (nr > 0) {
+        kind = 3;
+      } else if (nc > 0) {
+        kind = 1;
+      }
+      if (kind == 1) {
+        n = nc < max_seqs ? nc : max_seqs;
+        for (int i = 0; i < n; ++i) out[2 + i] = Q[0][i];
+        for (int i = n; i < nc; ++i) Q[0][i - n] = Q[0][i];
+        nc -= n;
+      } else if (kind == 3) {
+        const int want = nr < max_seqs ? nr : max_seqs;
+        const int target = min(item_step[r[0]], slots - 1);
+        int d = 0, i = 0;
+        for (; i < nr && n < want; ++i) {
+          const int id = r[i];
+          if (min(item_step[id], slots - 1) == target) {
+            out[2 + n++] = id;
+          } else {
+            rn[d++] = id;
+          }
+        }
+        for (; i < nr; ++i) rn[d++] = r[i];
+        nr = d;
+        r = rn;
+      }
+    }
+    s_kind = kind;
+    s_n = n;
+    s_err = err;
+    s_rc = nr;
+    s_cc = nc;
+    // publish the staged ready ring through buffer 0 for the parallel write-back
+    if (!err && r != R[0])
+      for (int i = 0; i < nr; ++i) R[0][i] = r[i];
+    if (!err) state[5] = refills;
+  }
+  __syncthreads();
+  const int nr = s_rc, nc = s_cc;
+  if (!s_err) {  // on overflow the queues stay exactly as they were
+    for (int i = threadIdx.x; i < nr; i += blockDim.x) ready[i] = R[0][i];
+    for (int i = threadIdx.x; i < nc; i += blockDim.x) coda[i] = Q[0][i];
+  }
+  if (threadIdx.x == 0) {
+    out[0] = s_err ? -1 : s_kind;
+    out[1] = s_n;
+    if (!s_err) {
+      state[0] = 0;
+      state[1] = nr;
+      state[2] = 0;
+      state[3] = nc;
+    }
+  }
+}
+
+}  // namespace cdb
+
+extern "C" int cdb_schedule_tick(int32_t* queue_state, int32_t* ready, int32_t* coda, int32_t* item_step,
+                                 const int32_t* routed, const int8_t* exit_flag, int num_routed, const int32_t* back,
+                                 int num_back, const int32_t* front, int num_front, int min_coda_batch_size,
+                                 int max_num_seqs, int prefill_admit, int kv_slots_per_layer, int32_t* out,
+                                 void* stream) {
+  if (queue_state == nullptr || ready == nullptr || coda == nullptr || item_step == nullptr || out == nullptr ||
+      num_routed < 0 || num_back < 0 || num_front < 0 || min_coda_batch_size <= 0 || max_num_seqs <= 0 ||
+      kv_slots_per_layer <= 0 || (num_routed > 0 && (routed == nullptr || exit_flag == nullptr)) ||
+      (num_back > 0 && back == nullptr) || (num_front > 0 && front == nullptr))
+    return CDB_ERR_INVALID_ARGUMENT;
+  launch_pdl(schedule_tick_kernel, dim3(1), dim3(kSchedThreads), 0, static_cast<cudaStream_t>(stream), queue_state,
+             ready, coda, item_step, routed, exit_flag, num_routed, back, num_back, front, num_front,
+             min_coda_batch_size, max_num_seqs, prefill_admit, kv_slots_per_layer, out);
+  return sched_launched();
+}
+
+extern "C" int cdb_schedule_queues_init(int32_t* queue_state, int capacity, void* stream) {
+  if (queue_state == nullptr || capacity <= 0 || capacity > cdb::kTickCap) return CDB_ERR_INVALID_ARGUMENT;
+  const int32_t init[8] = {0, 0, 0, 0, capacity, 0, 0, 0};
+  return cudaMemcpyAsync(queue_state, init, sizeof(init), cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? CDB_OK
+             : CDB_ERR_CUDA;
+}

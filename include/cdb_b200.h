@@ -364,6 +364,30 @@ int cdb_block_alloc(int32_t* ring, int32_t* state, int32_t* row_len, int32_t* bl
 int cdb_block_free(int32_t* ring, int32_t* state, int32_t* row_len, int32_t* block_table,
                    int64_t block_table_stride, const int32_t* slots, int num_slots, void* stream);
 
+/* One CDB scheduler tick on device-resident queues (CDBScheduler.schedule_next, scheduler.py:101-140,
+ * with enqueue_depth / enqueue_depth_front / enqueue_coda, :142-186, and the slot-homogeneous FIFO
+ * pop of _schedule_recurrent_batch, :322-346), applied in the engine's order:
+ *   1. routed[i] (the last recurrent batch, in batch order): exit_flag[i] != 0 joins the coda
+ *      queue; the others return to the head of the depth queue in batch order, item_step += 1;
+ *   2. back[]: appended to the depth queue (prefill successors);
+ *   3. front[]: to the head of the depth queue, in order (coda successors);
+ *   then the work: a coda batch (up to max_num_seqs from the coda queue's head) when it holds
+ *   min_coda_batch_size items, else prefill when prefill_admit (the host's admission), else a
+ *   recurrent batch of up to max_num_seqs items whose KV slot min(step, kv_slots_per_layer - 1)
+ *   equals the head item's (the others keep their order), else a coda flush.
+ * queue_state int32[8] = {ready head, ready count, coda head, coda count, capacity, refill events,
+ * 0, 0} (cdb_schedule_queues_init); ready / coda: int32 rings of `capacity` <= 2048 item ids;
+ * item_step: int32 per item id. A step-0 item joining a non-empty depth queue counts a refill.
+ * out: int32 [2 + max_num_seqs] = {kind (0 idle, 1 coda, 2 prefill, 3 recurrent; -1 a queue would
+ * overflow or the state is invalid, nothing changed), count, item ids of the batch}. */
+int cdb_schedule_tick(int32_t* queue_state, int32_t* ready, int32_t* coda, int32_t* item_step, const int32_t* routed,
+                      const int8_t* exit_flag, int num_routed, const int32_t* back, int num_back, const int32_t* front,
+                      int num_front, int min_coda_batch_size, int max_num_seqs, int prefill_admit,
+                      int kv_slots_per_layer, int32_t* out, void* stream);
+
+/* Empty queues of `capacity` (<= 2048) items each for cdb_schedule_tick. */
+int cdb_schedule_queues_init(int32_t* queue_state, int capacity, void* stream);
+
 /* The per-launch metadata FlashAttention's kvcache branch takes (_prepare_recurrent_stage_buffers,
  * model_runner.py:704-754, gather_block_table_host_rows, continuous_depth_batching/cache.py:66-91):
  * out_table[i] = the full block row of slot item_slot[i] (-1 past its row_len blocks, `width`

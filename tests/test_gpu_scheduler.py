@@ -222,3 +222,91 @@ def test_build_tables_matches_reference_layout():
               _sp())
     torch.cuda.synchronize()
     assert int(status.item()) == 6  # CDB_ERR_INDEX
+
+
+@pytest.mark.parametrize("policy,slots", [("single", 1), ("first_then_shared", 2), ("depth_indexed", 4)])
+def test_schedule_tick_matches_engine_queues(policy, slots):
+    """cdb_schedule_tick against the engine's own queue operations (_enqueue, _enqueue_front,
+    _pop_recurrent, the coda-first decision), the ones the reference traces pin: 150 ticks of
+    routed batches with random exits, prefill and coda successors, and host prefill admissions.
+    Every tick's kind and batch, both queues and the refill count must be equal."""
+
+    from collections import deque
+
+    from continuous_depth_batching_b200 import ContinuousDepthBatchingEngine
+    from continuous_depth_batching_b200.engine import _Item
+
+    rng = random.Random(slots)
+    max_seqs, min_coda, cap, n_items = 12, 3, 256, 4000
+    eng = ContinuousDepthBatchingEngine.__new__(ContinuousDepthBatchingEngine)
+    eng.cdb_config = SimpleNamespace(kv_policy=policy)
+    eng.slots, eng.max_num_seqs = slots, max_seqs
+    eng.ready, eng.in_flight, eng.refills, eng.max_queue = deque(), set(), 0, 0
+    coda_q: deque = deque()
+    items: dict[int, _Item] = {}
+    state = torch.zeros(8, dtype=torch.int32, device=DEV)
+    ready = torch.zeros(cap, dtype=torch.int32, device=DEV)
+    coda = torch.zeros(cap, dtype=torch.int32, device=DEV)
+    step = torch.zeros(n_items, dtype=torch.int32, device=DEV)
+    out = torch.zeros(2 + max_seqs, dtype=torch.int32, device=DEV)
+    _lib.call("cdb_schedule_queues_init", _lib.ptr(state), cap, _sp())
+    next_id = 0
+
+    def new_items(k):
+        nonlocal next_id
+        made = []
+        for _ in range(k):
+            it = _Item(SimpleNamespace(idx=next_id), 0, None, next_id, -1)
+            items[next_id] = it
+            made.append(it)
+            next_id += 1
+        return made
+
+    last_batch: list[_Item] = []
+    for tick in range(150):
+        exits = [int(rng.random() < 0.35 or it.step == 3) for it in last_batch]
+        back = new_items(rng.randrange(0, 4) if tick % 7 == 0 else 0)
+        front = new_items(rng.randrange(0, 3))
+        admit = int(rng.random() < 0.1)
+        # host: the engine's own queue operations in the engine's order
+        surv = []
+        for it, ex in zip(last_batch, exits, strict=True):
+            if ex:
+                coda_q.append(it)
+            else:
+                it.step += 1
+                surv.append(it)
+        eng._enqueue_front(surv)
+        for it in back:
+            eng._enqueue(it)
+        eng._enqueue_front(front)
+        if len(coda_q) >= min_coda:
+            kind, batch = 1, [coda_q.popleft() for _ in range(min(max_seqs, len(coda_q)))]
+        elif admit:
+            kind, batch = 2, []
+        elif eng.ready:
+            kind, batch = 3, eng._pop_recurrent()
+        elif coda_q:
+            kind, batch = 1, [coda_q.popleft() for _ in range(min(max_seqs, len(coda_q)))]
+        else:
+            kind, batch = 0, []
+        # device
+        d = lambda v, dt=torch.int32: torch.tensor(v if v else [0], dtype=dt, device=DEV)  # noqa: E731
+        routed = d([it.hidden for it in last_batch])
+        ex_d = d(exits, torch.int8)
+        back_d, front_d = d([it.hidden for it in back]), d([it.hidden for it in front])
+        _lib.call(
+            "cdb_schedule_tick", _lib.ptr(state), _lib.ptr(ready), _lib.ptr(coda), _lib.ptr(step), _lib.ptr(routed),
+            _lib.ptr(ex_d), len(last_batch), _lib.ptr(back_d), len(back), _lib.ptr(front_d), len(front), min_coda,
+            max_seqs, admit, slots, _lib.ptr(out), _sp(),
+        )
+        torch.cuda.synchronize()
+        o = out.tolist()
+        assert o[0] == kind, tick
+        assert o[2 : 2 + o[1]] == [it.hidden for it in batch], tick
+        st = state.tolist()
+        assert ready[: st[1]].tolist() == [it.hidden for it in eng.ready], tick
+        assert coda[: st[3]].tolist() == [it.hidden for it in coda_q], tick
+        assert st[5] == eng.refills, tick
+        assert step[: next_id].tolist() == [items[i].step for i in range(next_id)], tick
+        last_batch = batch if kind == 3 else []
