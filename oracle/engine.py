@@ -209,12 +209,58 @@ class OracleEngine:
         self._free(r)
         self.active.pop(r.idx, None)
         self.in_flight.discard(r.idx)
+        self.stalled.pop(r.idx, None)
         self.finished[r.idx] = list(r.generated)
+        self.block_new = False  # a finish frees blocks: admission resumes (continuous_api.py:1436-1448)
 
-    def _stage_decode(self, r: Req) -> Item:
+    def _stage_decode(self, r: Req) -> Item | None:
+        """``_stage_decode_token`` (``continuous_api.py:1584-1610``): a request whose next token
+        cannot get a KV block stalls (retried each tick, preempted only when nothing can run)."""
+
         if not self._alloc_one_decode(r):
-            raise RuntimeError("oracle: KV cache full (size num_blocks to fit the workload)")
+            if self.cfg.kv_pressure_mode in ("none", "reserve"):
+                raise RuntimeError("oracle: KV cache full (size num_blocks to fit the workload)")
+            self.stalled[r.idx] = r
+            return None
+        self.stalled.pop(r.idx, None)
         return Item(req=r, token=r.to_process[0], position=r.position, step=0, depth=r.next_depth())
+
+    def _restage_stalled(self) -> list[Item]:
+        """``_restage_stalled_decoders`` (``:1612-1623``): retry in stall order, stop at the first
+        request that still cannot allocate."""
+
+        items = []
+        for r in list(self.stalled.values()):
+            it = self._stage_decode(r)
+            if it is None:
+                break
+            items.append(it)
+        return items
+
+    def _preempt_stalled(self) -> None:
+        """``_preempt_stalled_decoder`` (``:1625-1652``) with recompute (soft reset,
+        ``create_equivalent_initial_request``, ``requests.py:290-315`` and the CDB slice of the replay
+        schedule): the stalled request with the fewest cached tokens (ties: the latest staller)
+        gives up its KV; its generated tokens join its prompt for a full-depth re-prefill; it waits
+        behind every other waiting prompt, and no new prompt is admitted until a request finishes."""
+
+        if len(self.active) <= 1:
+            raise RuntimeError("oracle: a single request's KV cache does not fit")
+        victim = min(reversed(list(self.stalled)), key=lambda i: self.stalled[i].position)
+        r = self.stalled.pop(victim)
+        self._free(r)
+        self.active.pop(r.idx, None)
+        self.in_flight.discard(r.idx)
+        self.waiting.pop(r.idx, None)
+        r.remaining = list(r.prompt) + list(r.generated)
+        r.to_process = []
+        r.position = 0
+        r.allocated = 0
+        r.status = PENDING
+        r.cursor += 1  # the pending token's depth is spent: it is recomputed at full depth
+        self.waiting[r.idx] = r
+        self.block_new = True
+        self.stats["recompute_preemptions"] += 1
 
     def _next_token(self, r: Req, computed: int) -> int:
         if self.forced is not None:
@@ -251,7 +297,7 @@ class OracleEngine:
     def _prefill_candidates(self) -> list[Req]:
         prefilling = [r for r in self.active.values() if r.status == PREFILLING and r.idx not in self.in_flight]
         free_slots = max(0, self.max_num_seqs - len(self.active))
-        admissible = [self.waiting[i] for i in list(self.waiting)[:free_slots]]
+        admissible = [] if self.block_new else [self.waiting[i] for i in list(self.waiting)[:free_slots]]
         if self.cfg.kv_pressure_mode == "reserve":
             committed = sum(self._reserved_peak(r) for r in self.active.values())
             kept = []
@@ -479,8 +525,8 @@ class OracleEngine:
             if self._update(r, self._next_token(r, tok)):
                 self._retire(r)
                 continue
-            if stage:
-                new_items.append(self._stage_decode(r))
+            if stage and (it := self._stage_decode(r)) is not None:
+                new_items.append(it)
         self._prelude(new_items)
         for it in new_items:
             self._enqueue(it)
@@ -495,8 +541,8 @@ class OracleEngine:
             if self._update(r, self._next_token(r, tok)):
                 self._retire(r)
                 continue
-            if stage:
-                new_items.append(self._stage_decode(r))
+            if stage and (it := self._stage_decode(r)) is not None:
+                new_items.append(it)
         self._prelude(new_items)
         self._enqueue_front(new_items)
 
@@ -512,6 +558,10 @@ class OracleEngine:
             pending_coda = []
             if not self._has_pending():
                 continue
+            # decode tokens that could not get a KV block last tick go first, at the queue head
+            resumed = self._restage_stalled()
+            self._prelude(resumed)
+            self._enqueue_front(resumed)
             self.stats["ticks"] += 1
             if len(self.coda_q) >= self.cfg.min_coda_batch_size:
                 batch = [self.coda_q.popleft() for _ in range(min(self.max_num_seqs, len(self.coda_q)))]
@@ -544,6 +594,9 @@ class OracleEngine:
             if self.coda_q:
                 batch = [self.coda_q.popleft() for _ in range(min(self.max_num_seqs, len(self.coda_q)))]
                 pending_coda.append((batch, self._run_coda(batch)))
+                continue
+            if self.stalled:
+                self._preempt_stalled()
                 continue
             raise RuntimeError("oracle: scheduler stalled (KV cache too small for the workload)")
 
@@ -677,6 +730,8 @@ class OracleEngine:
         self.ready: deque[Item] = deque()
         self.coda_q: deque[Item] = deque()
         self.backlog: list[tuple[Item, int]] = []
+        self.stalled: OrderedDict[int, Req] = OrderedDict()
+        self.block_new = False
         self.finished: dict[int, list[int]] = {}
         self.launches: list[dict] = []
         self.logits: list[tuple[str, torch.Tensor]] = []

@@ -214,6 +214,7 @@ def run_case(
             "generated_tokens": stats.generated_tokens,
             "scheduler_refills": stats.scheduler_refills,
             "exit_depth_histogram": {str(k): v for k, v in sorted(stats.exit_depth_histogram.items())},
+            "recompute_preemptions": getattr(engine.offloading_manager, "num_recompute_preemptions", 0),
         },
         "launches": rec.launches,
     }
@@ -273,6 +274,39 @@ def finish_main() -> None:
     (HERE / "ouro_cfg0_finish.json").write_text(json.dumps(payload, separators=(",", ":")))
     for r in runs:
         print(r["name"], r["stats"], [len(t) for t in r["tokens"]])
+
+
+def pressure_main() -> None:
+    """``--pressure``: the replayed schedule (refill on, synchronous) in KV pools too small for the
+    workload, under the default ``kv_pressure_mode="recompute"``: 56 blocks (decoders stall and are
+    restaged), 48 and 40 blocks (stalled decoders are preempted by soft reset and re-prefilled),
+    into ``ouro_cfg0_pressure.json``."""
+
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    gold = json.loads((HERE / "ouro_cfg0.json").read_text())
+    depths = next(r for r in gold["runs"] if r["name"] == "replay_refill")["exit_depths"]
+    runs = []
+    for nb in (56, 48, 40):
+        res, _ = run_case(
+            f"replay_refill_blocks{nb}", kv_policy="single", refill=True, live_gate=False, exit_depths=depths,
+            num_blocks=nb,
+        )
+        res["num_blocks"] = nb
+        runs.append(res)
+    prompts, max_new = config0_workload()
+    payload = {
+        "generator": "tests/golden/make_golden.py --pressure",
+        "shape": CFG0.__dict__,
+        "gate_std": GATE_STD,
+        "weights_seed": 0,
+        "prompts": prompts,
+        "max_new_tokens": max_new,
+        "block_size": 16,
+        "runs": runs,
+    }
+    (HERE / "ouro_cfg0_pressure.json").write_text(json.dumps(payload, separators=(",", ":")))
+    for r in runs:
+        print(r["name"], r["stats"])
 
 
 def policies_main() -> None:
@@ -373,5 +407,7 @@ if __name__ == "__main__":
         policies_main()
     elif "--finish" in sys.argv[1:]:
         finish_main()
+    elif "--pressure" in sys.argv[1:]:
+        pressure_main()
     else:
         main()

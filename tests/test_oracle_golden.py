@@ -124,6 +124,26 @@ def test_oracle_reproduces_reference_early_finish_run(name):
     assert exit_depth_histogram(engine) == run["stats"]["exit_depth_histogram"]
 
 
+@pytest.mark.parametrize(
+    "name,preemptions",
+    [("replay_refill_blocks56", 0), ("replay_refill_blocks48", 3), ("replay_refill_blocks40", 2)],
+)
+def test_oracle_reproduces_reference_pressure_run(name, preemptions):
+    """KV pressure under recompute: a decoder whose next block cannot be had stalls, is restaged
+    at the head of the next tick, and when nothing can run the stalled request with the shortest
+    context is reset to prompt + generated text and re-queued, blocking new admissions until a
+    request retires."""
+
+    data, shape, sd = _load_ouro("ouro_cfg0_pressure.json")
+    run = next(r for r in data["runs"] if r["name"] == name)
+    engine = OracleEngine(shape, sd, _config(run, {**data, "num_blocks": run["num_blocks"]}), torch.float32)
+    tokens = engine.generate(data["prompts"], data["max_new_tokens"], exit_depths=run["exit_depths"])
+    assert tokens == run["tokens"]
+    assert engine.launches == run["launches"]
+    assert engine.stats["recompute_preemptions"] == run["stats"]["recompute_preemptions"] == preemptions
+    assert exit_depth_histogram(engine) == run["stats"]["exit_depth_histogram"]
+
+
 @pytest.mark.parametrize("name", ["live_gate_refill", "replay_refill", "replay_norefill", "replay_last_exited"])
 def test_oracle_reproduces_reference_run(golden, name):
     data, shape, sd = golden
