@@ -97,6 +97,7 @@ class ContinuousDepthBatchingStats:
     exit_kv_copies: int = 0
     host_syncs: int = 0
     kv_peak_blocks: int = 0
+    recompute_preemptions: int = 0
 
     @property
     def skipped_recurrent_steps(self) -> int:
@@ -385,6 +386,8 @@ class ContinuousDepthBatchingEngine:
         self.ready: deque[_Item] = deque()
         self.coda_q: deque[_Item] = deque()
         self.backlog: list[tuple[_Item, int]] = []
+        self.stalled: OrderedDict[int, _Req] = OrderedDict()
+        self.block_new = False
         self.refills = 0
         self.max_queue = 0
         self.free_slots = list(range(cfg.max_num_seqs - 1, -1, -1))
@@ -428,7 +431,10 @@ class ContinuousDepthBatchingEngine:
         self.pool.release(r.idx)
         self.active.pop(r.idx, None)
         self.in_flight.discard(r.idx)
+        self.stalled.pop(r.idx, None)
         self.free_slots.append(r.slot)
+        # a finish frees blocks, so admission resumes (``continuous_api.py:1436-1448``)
+        self.block_new = False
 
     def _record_token(self, r: _Req) -> bool:
         """Count one sampled token; True when the request is finished (length, EOS or stop)."""
@@ -466,14 +472,84 @@ class ContinuousDepthBatchingEngine:
             return int(self._forced[r.idx][r.generated - 1])
         return -1
 
-    def _stage_decode(self, r: _Req) -> _Item:
+    def _stage_decode(self, r: _Req) -> _Item | None:
+        """``_stage_decode_token`` (``continuous_api.py:1584-1610``): the request's next decode
+        item, or None when no KV block is free for its token: the request then stalls at a token
+        boundary, is retried each tick and is preempted only when nothing else can run."""
+
         if not self._alloc_one_decode(r):
-            raise CacheFullError(
-                f"KV cache full staging a decode block for request {r.request_id}; the B200 engine runs "
-                "without preemption: increase num_blocks or reduce load"
-            )
+            mode = self.cdb_config.kv_pressure_mode
+            if mode == "none":
+                raise CacheFullError(
+                    f"KV cache full staging a decode block for request {r.request_id} and "
+                    "kv_pressure_mode='none' does no preemption. Increase num_blocks, reduce load, or select "
+                    "kv_pressure_mode='reserve'/'recompute'."
+                )
+            if mode == "reserve":
+                raise CacheFullError(
+                    f"Reserve admission over-committed the KV cache: request {r.request_id} could not "
+                    "allocate a decode block. This is a bug in reservation accounting."
+                )
+            self.stalled[r.idx] = r
+            return None
+        self.stalled.pop(r.idx, None)
         hidden = self.free_hidden.pop()
         return _Item(r, r.position, r.next_depth(), hidden, self._next_token_id(r))
+
+    def _restage_stalled(self) -> list[_Item]:
+        """``_restage_stalled_decoders`` (``continuous_api.py:1612-1623``): retry the stalled
+        requests in stall order; every one needs one new block, so the first failure ends the scan."""
+
+        items = []
+        for r in list(self.stalled.values()):
+            it = self._stage_decode(r)
+            if it is None:
+                break
+            items.append(it)
+        return items
+
+    def _preempt_stalled(self) -> None:
+        """``_preempt_stalled_decoder`` (``continuous_api.py:1625-1652``) with the recompute soft
+        reset (``create_equivalent_initial_request``, ``requests.py:290-315``).
+
+        The victim is the stalled request with the fewest cached tokens, ties going to the latest
+        staller. Its blocks and block-table row are released. Its generated tokens are appended to its
+        prompt for a full-depth re-prefill, and it re-enters the waiting queue at the back. The depth
+        its pending token would have replayed is skipped. No new prompt is admitted until a request
+        finishes."""
+
+        if self.cdb_config.kv_pressure_mode == "offload":
+            raise NotImplementedError(
+                "kv_pressure_mode='offload' (swapping a stalled request's KV blocks to host memory) is not "
+                "built in the B200 engine; use 'recompute' or 'reserve'"
+            )
+        if len(self.active) <= 1:
+            rid = next(iter(self.stalled.values())).request_id
+            raise CacheFullError(
+                f"A single request's KV cache does not fit: request {rid} could not allocate a decode block "
+                "and no other request can be preempted (increase num_blocks or reduce max_model_len)."
+            )
+        victim = min(reversed(list(self.stalled)), key=lambda i: self.stalled[i].position)
+        r = self.stalled.pop(victim)
+        if self._forced is None:
+            self.last_stats.host_syncs += 1
+            self.runner.stream.synchronize()
+        generated = self._host_tokens(r)
+        self.pool.release(r.idx)
+        self.active.pop(r.idx, None)
+        self.in_flight.discard(r.idx)
+        self.waiting.pop(r.idx, None)
+        self.free_slots.append(r.slot)
+        r.slot = -1
+        r.remaining = list(r.prompt) + generated
+        r.chunk = []
+        r.position = 0
+        r.allocated = 0
+        r.status = RequestStatus.PENDING
+        r.cursor += 1
+        self.waiting[r.idx] = r
+        self.block_new = True
+        self.last_stats.recompute_preemptions += 1
 
     def _prelude(self, items: list[_Item]) -> None:
         if items:
@@ -518,7 +594,8 @@ class ContinuousDepthBatchingEngine:
         free_res = max(0, self.max_num_seqs - len(self.active))
         admissible = []
         for key in self.waiting:
-            if len(admissible) >= free_res:
+            # after a preemption no new prompt is admitted until a request finishes
+            if self.block_new or len(admissible) >= free_res:
                 break
             admissible.append(self.waiting[key])
         if self.cdb_config.kv_pressure_mode == "reserve":
@@ -580,14 +657,16 @@ class ContinuousDepthBatchingEngine:
             if len(toks) <= qlen:
                 if r.status == RequestStatus.PENDING:
                     self.active[r.idx] = r
-                    r.start = time.perf_counter()
+                    if r.start < 0:
+                        r.start = time.perf_counter()
                 r.chunk = toks
                 r.remaining = []
                 r.status = RequestStatus.DECODING
             else:
                 if r.status == RequestStatus.PENDING:
                     self.active[r.idx] = r
-                    r.start = time.perf_counter()
+                    if r.start < 0:
+                        r.start = time.perf_counter()
                     r.status = RequestStatus.PREFILLING
                 r.remaining = toks[qlen:]
                 r.chunk = toks[:qlen]
@@ -799,8 +878,8 @@ class ContinuousDepthBatchingEngine:
             if self._record_token(r):
                 self._retire(r)
                 continue
-            if stage:
-                new_items.append(self._stage_decode(r))
+            if stage and (it := self._stage_decode(r)) is not None:
+                new_items.append(it)
         self._prelude(new_items)
         for it in new_items:
             self._enqueue(it)
@@ -816,8 +895,8 @@ class ContinuousDepthBatchingEngine:
             if self._record_token(r):
                 self._retire(r)
                 continue
-            if stage:
-                new_items.append(self._stage_decode(r))
+            if stage and (nxt := self._stage_decode(r)) is not None:
+                new_items.append(nxt)
         self._prelude(new_items)
         self._enqueue_front(new_items)
 
@@ -852,6 +931,11 @@ class ContinuousDepthBatchingEngine:
                 if arrivals:
                     self._wait_next_arrival(arrivals)
                 continue
+            # decode tokens that found no KV block last tick go first, at the queue head
+            if self.stalled:
+                resumed = self._restage_stalled()
+                self._prelude(resumed)
+                self._enqueue_front(resumed)
             self.last_stats.scheduler_ticks += 1
             if len(self.coda_q) >= cfg.min_coda_batch_size:
                 batch = [self.coda_q.popleft() for _ in range(min(self.max_num_seqs, len(self.coda_q)))]
@@ -887,6 +971,9 @@ class ContinuousDepthBatchingEngine:
                 batch = [self.coda_q.popleft() for _ in range(min(self.max_num_seqs, len(self.coda_q)))]
                 self._run_coda(batch)
                 pending_coda.append(batch)
+                continue
+            if self.stalled:
+                self._preempt_stalled()
                 continue
             if arrivals:
                 self._wait_next_arrival(arrivals)
@@ -989,9 +1076,13 @@ class ContinuousDepthBatchingEngine:
                 if r.status == RequestStatus.DECODING and r.generated > 0 and r.idx not in carried_ids
             ]
             cohort = cohort[: max(0, self.max_num_seqs - len(carried))]
-            items = carried + [self._stage_decode(r) for r in cohort]
+            # a request whose token finds no KV block stalls out of this wave (``continuous_api.py:840-843``)
+            items = carried + [it for r in cohort if (it := self._stage_decode(r)) is not None]
             carried = []
             if not items:
+                if not did_prefill and self.stalled:
+                    self._preempt_stalled()
+                    continue
                 if not did_prefill and self._has_pending() and not arrivals:
                     raise CacheFullError("No-refill loop stalled with pending work (over-subscribed KV cache)")
                 if arrivals and not did_prefill:

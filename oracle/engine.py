@@ -665,9 +665,14 @@ class OracleEngine:
                 if r.status == DECODING and r.to_process and r.to_process[0] >= 0 and r.idx not in carried_ids
             ]
             cohort = cohort[: max(0, self.max_num_seqs - len(carried))]
-            items = carried + [self._stage_decode(r) for r in cohort]
+            # a token that finds no KV block stalls its request out of this wave
+            # (continuous_api.py:840-843); a wave-less pass preempts one staller (:672-677)
+            items = carried + [it for r in cohort if (it := self._stage_decode(r)) is not None]
             carried = []
             if not items:
+                if not did_prefill and self.stalled:
+                    self._preempt_stalled()
+                    continue
                 if not did_prefill and self._has_pending():
                     raise RuntimeError("oracle: no-refill loop stalled")
                 continue

@@ -277,22 +277,24 @@ def finish_main() -> None:
 
 
 def pressure_main() -> None:
-    """``--pressure``: the replayed schedule (refill on, synchronous) in KV pools too small for the
-    workload, under the default ``kv_pressure_mode="recompute"``: 56 blocks (decoders stall and are
-    restaged), 48 and 40 blocks (stalled decoders are preempted by soft reset and re-prefilled),
-    into ``ouro_cfg0_pressure.json``."""
+    """``--pressure``: the replayed schedules (synchronous) in KV pools too small for the workload,
+    under the default ``kv_pressure_mode="recompute"``: refill at 56 blocks (decoders stall and are
+    restaged), 48 and 40 blocks (stalled decoders are preempted by soft reset and re-prefilled), and
+    no-refill at 48 and 40 blocks, into ``ouro_cfg0_pressure.json``."""
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     gold = json.loads((HERE / "ouro_cfg0.json").read_text())
-    depths = next(r for r in gold["runs"] if r["name"] == "replay_refill")["exit_depths"]
     runs = []
-    for nb in (56, 48, 40):
-        res, _ = run_case(
-            f"replay_refill_blocks{nb}", kv_policy="single", refill=True, live_gate=False, exit_depths=depths,
-            num_blocks=nb,
-        )
-        res["num_blocks"] = nb
-        runs.append(res)
+    for refill, nbs in ((True, (56, 48, 40)), (False, (48, 40))):
+        tag = "refill" if refill else "norefill"
+        depths = next(r for r in gold["runs"] if r["name"] == f"replay_{tag}")["exit_depths"]
+        for nb in nbs:
+            res, _ = run_case(
+                f"replay_{tag}_blocks{nb}", kv_policy="single", refill=refill, live_gate=False, exit_depths=depths,
+                num_blocks=nb,
+            )
+            res["num_blocks"] = nb
+            runs.append(res)
     prompts, max_new = config0_workload()
     payload = {
         "generator": "tests/golden/make_golden.py --pressure",

@@ -1,0 +1,227 @@
+"""The engine's host scheduler, run on the CPU against the reference's recorded schedules.
+
+The B200 engine keeps its queues, block allocator and request lifecycle on the host and launches
+device work through its runner. Here the runner is replaced by a host stand-in that launches
+nothing: it hands out the same block pool and KV layout, and each LM-head row it would sample
+gets a deterministic token. Everything else, from admission and chunked prefill through the
+recurrent queue, exit routing, codas, stalls and recompute preemption, is the engine's own code.
+With the replayed exit schedules of the reference runs, its launch trace (each launch's kind,
+items and block-table rows) must equal the trace recorded from the reference engine. The GPU tests
+repeat these comparisons through the real runner.
+"""
+
+from __future__ import annotations
+
+import json
+from pathlib import Path
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+from continuous_depth_batching_b200 import ContinuousDepthBatchingConfig, ContinuousDepthBatchingEngine, OuroShape
+from continuous_depth_batching_b200.kv_cache import BlockPool, LoopedKvLayout
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _token(log_row: int, vocab: int) -> int:
+    return (7 * log_row + 3) % vocab
+
+
+class _HostRunner:
+    """The runner surface the engine drives, with no device work behind it."""
+
+    def __init__(self, cfg: ContinuousDepthBatchingConfig, shape: OuroShape) -> None:
+        self.vocab = shape.vocab_size
+        self.pool = SimpleNamespace(pool=BlockPool(cfg.num_blocks, cfg.block_size, cfg.decode_block_table_width()))
+        self.layout = LoopedKvLayout(
+            num_prelude_layers=0, num_core_layers=shape.num_hidden_layers, num_coda_layers=0,
+            total_recurrent_steps=cfg.max_recurrent_steps, policy=cfg.kv_policy,
+            requested_slots=cfg.kv_slots_per_layer,
+        )
+        self.bank_slots = 2 * cfg.max_num_seqs + 8
+        self.stats = SimpleNamespace(recurrent_graph_hits=0, recurrent_graph_captures=0)
+        self.stream = SimpleNamespace(synchronize=lambda: None)
+        self.prefill_ids: list[list[int]] = []
+        self.token_log = torch.zeros(1, dtype=torch.int64)
+
+    def reset(self, log_len: int) -> None:
+        self.pool.pool.reset()
+        self.token_log = torch.zeros(log_len, dtype=torch.int64)
+        self.prefill_ids = []
+
+    def _sample(self, log_rows) -> None:
+        for row in log_rows:
+            self.token_log[row] = _token(row, self.vocab)
+
+    def prefill(self, ids, slots, pos, logit_rows, log_rows, req_slots, kv_slots, keep_logits=False):
+        self.prefill_ids.append(list(ids))
+        self._sample(log_rows)
+        return None
+
+    def coda(self, hidden, log_rows, slots, keep_logits=False, positions=None):
+        self._sample(log_rows)
+        return None
+
+    def prelude(self, *args, **kwargs) -> None:
+        pass
+
+    def recurrent(self, *args, **kwargs) -> None:
+        pass
+
+    def exit_kv_copy(self, rows, pairs) -> None:
+        pass
+
+    def read_tokens(self, n: int) -> list[int]:
+        return self.token_log[:n].tolist()
+
+    def check_status(self) -> None:
+        pass
+
+
+def _engine(data: dict, run: dict, num_blocks: int) -> ContinuousDepthBatchingEngine:
+    shape = OuroShape(**data["shape"])
+    kv_policy = run.get("kv_policy", "single")
+    cfg = ContinuousDepthBatchingConfig(
+        block_size=16,
+        num_blocks=num_blocks,
+        max_recurrent_steps=shape.total_ut_steps,
+        synthetic_exit_replay=True,
+        use_async_batching=run.get("async", False),
+        refill=run["refill"],
+        kv_policy=kv_policy,
+        kv_pressure_mode="reserve" if kv_policy == "last_exited" else "recompute",
+        max_model_len=2048,
+    ).get_resolved()
+    eng = ContinuousDepthBatchingEngine(None, cfg, _HostRunner(cfg, shape), shape)
+    eng.record_trace = True
+    return eng
+
+
+def _check_prefill_contents(eng: ContinuousDepthBatchingEngine, prompts, outs) -> None:
+    """Every prefill chunk holds the request's prompt followed by its generated tokens at the
+    chunk's positions, so a re-prefill after a preemption recomputes exactly the tokens it had."""
+
+    prefills = [t for t in eng.launch_trace if t["kind"] == "prefill"]
+    assert len(prefills) == len(eng.runner.prefill_ids)
+    for trace, ids in zip(prefills, eng.runner.prefill_ids, strict=True):
+        k = 0
+        for idx, past, qlen, _ in trace["items"]:
+            seq = list(prompts[idx]) + list(outs[idx].generated_tokens)
+            assert ids[k : k + qlen] == seq[past : past + qlen]
+            k += qlen
+        assert k == len(ids)
+
+
+def _run(data: dict, run: dict, num_blocks: int, forced=None, eos=None, stops=None):
+    eng = _engine(data, run, num_blocks)
+    outs = eng.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=eos, stop_sequences=stops,
+        exit_depths=run["exit_depths"], forced_tokens=forced,
+    )
+    return eng, outs
+
+
+def _load(name: str) -> dict:
+    return json.loads((GOLDEN / name).read_text())
+
+
+PRESSURE = [
+    ("replay_refill_blocks56", 0),
+    ("replay_refill_blocks48", 3),
+    ("replay_refill_blocks40", 2),
+    ("replay_norefill_blocks48", 2),
+    ("replay_norefill_blocks40", 1),
+]
+
+
+@pytest.mark.parametrize("name,preemptions", PRESSURE)
+def test_kv_pressure_schedule_matches_reference(name, preemptions):
+    """Recompute mode in pools too small for the workload: stalls, restaging, preemption of the
+    shortest stalled request, its re-prefill and the admission hold equal the reference's."""
+
+    data = _load("ouro_cfg0_pressure.json")
+    run = next(r for r in data["runs"] if r["name"] == name)
+    eng, outs = _run(data, run, run["num_blocks"])
+    assert eng.launch_trace == run["launches"]
+    assert eng.last_stats.recompute_preemptions == run["stats"]["recompute_preemptions"] == preemptions
+    assert [len(o.generated_tokens) for o in outs] == data["max_new_tokens"]
+    assert [o.generated_tokens for o in outs] == [
+        [_token(r_base + g, OuroShape(**data["shape"]).vocab_size) for g in range(m)]
+        for r_base, m in zip(_log_bases(data["max_new_tokens"]), data["max_new_tokens"], strict=True)
+    ]
+    _check_prefill_contents(eng, data["prompts"], outs)
+    assert not eng.stalled and not eng.block_new
+
+
+def _log_bases(max_new: list[int]) -> list[int]:
+    out, base = [], 0
+    for m in max_new:
+        out.append(base)
+        base += m
+    return out
+
+
+@pytest.mark.parametrize("name", ["replay_refill", "replay_norefill", "replay_last_exited"])
+def test_schedule_matches_reference(name):
+    data = _load("ouro_cfg0.json")
+    run = next(r for r in data["runs"] if r["name"] == name)
+    eng, _ = _run(data, run, data["num_blocks"])
+    assert eng.launch_trace == run["launches"]
+    assert eng.last_stats.scheduler_refills == run["stats"]["scheduler_refills"]
+    assert eng.last_stats.recompute_preemptions == 0
+
+
+@pytest.mark.parametrize("name", ["replay_refill_async", "replay_norefill_async", "replay_last_exited_async"])
+def test_async_schedule_matches_reference(name):
+    data = _load("ouro_cfg0_async.json")
+    run = next(r for r in data["runs"] if r["name"] == name)
+    eng, _ = _run(data, run, data["num_blocks"])
+    assert eng.launch_trace == run["launches"]
+
+
+@pytest.mark.parametrize("name", ["replay_first_then_shared", "replay_first_then_shared_async", "replay_depth_indexed_full"])
+def test_kv_policy_schedule_matches_reference(name):
+    data = _load("ouro_cfg0_policies.json")
+    run = next(r for r in data["runs"] if r["name"] == name)
+    eng, _ = _run(data, run, data["num_blocks"])
+    assert eng.launch_trace == run["launches"]
+
+
+@pytest.mark.parametrize("name", ["replay_refill_eos_stop", "replay_norefill_eos_stop"])
+def test_early_finish_schedule_matches_reference(name):
+    data = _load("ouro_cfg0_finish.json")
+    run = next(r for r in data["runs"] if r["name"] == name)
+    eng, outs = _run(
+        data, run, data["num_blocks"], forced=run["tokens"], eos=run["eos_token_id"], stops=run["stop_sequences"]
+    )
+    assert eng.launch_trace == run["launches"]
+    assert [len(o.generated_tokens) for o in outs] == [len(t) for t in run["tokens"]]
+
+
+def test_single_request_that_cannot_fit_raises():
+    """With one active request left and no block for its next token, preemption cannot help: the
+    reference raises ``CacheFullError`` (``continuous_api.py:1640-1646``)."""
+
+    from continuous_depth_batching_b200.engine import CacheFullError
+
+    data = _load("ouro_cfg0_pressure.json")
+    run = {"refill": True, "exit_depths": [[0] * 63]}
+    one = {**data, "prompts": [list(range(30))], "max_new_tokens": [64]}
+    eng = _engine(one, run, 2)
+    with pytest.raises(CacheFullError, match="single request's KV cache does not fit"):
+        eng.generate_batch(one["prompts"], max_new_tokens=[64], eos_token_id=None, exit_depths=run["exit_depths"])
+
+
+def test_pressure_none_mode_raises_instead_of_stalling():
+    data = _load("ouro_cfg0_pressure.json")
+    run = next(r for r in data["runs"] if r["name"] == "replay_refill_blocks48")
+    eng = _engine(data, run, run["num_blocks"])
+    eng.cdb_config.kv_pressure_mode = "none"
+    from continuous_depth_batching_b200.engine import CacheFullError
+
+    with pytest.raises(CacheFullError, match="kv_pressure_mode='none' does no preemption"):
+        eng.generate_batch(
+            data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"]
+        )

@@ -202,9 +202,9 @@ def test_live_hazard_gate_matches_reference_decisions(fixture, name, refill):
     assert agree >= 0.95
 
 
-def _oracle(shape, sd, prompts, max_new, depths, dtype, forced=None, kv_policy="single"):
+def _oracle(shape, sd, prompts, max_new, depths, dtype, forced=None, kv_policy="single", num_blocks=4096):
     cfg = OracleConfig(
-        block_size=16, num_blocks=4096, max_recurrent_steps=shape.total_ut_steps, max_model_len=4096,
+        block_size=16, num_blocks=num_blocks, max_recurrent_steps=shape.total_ut_steps, max_model_len=4096,
         synthetic_exit_replay=True, kv_policy=kv_policy,
         kv_pressure_mode="reserve" if kv_policy == "last_exited" else "recompute",
     )
@@ -213,15 +213,17 @@ def _oracle(shape, sd, prompts, max_new, depths, dtype, forced=None, kv_policy="
     return eng, toks
 
 
-def _compare_teacher_forced(shape, sd, prompts, max_new, depths, kv_policy="single"):
+def _compare_teacher_forced(shape, sd, prompts, max_new, depths, kv_policy="single", num_blocks=4096):
     """fp32 oracle -> tokens; bf16 oracle and GPU engine both forced onto those tokens.
 
     Returns the ``tests.numerics.compare_lm_launches`` report over every LM-head launch.
     """
 
-    o32, toks = _oracle(shape, sd, prompts, max_new, depths, torch.float32, kv_policy=kv_policy)
-    o16, _ = _oracle(shape, sd, prompts, max_new, depths, torch.bfloat16, forced=toks, kv_policy=kv_policy)
-    eng = _engine(shape, sd, kv_policy=kv_policy, max_model_len=4096)
+    o32, toks = _oracle(shape, sd, prompts, max_new, depths, torch.float32, kv_policy=kv_policy, num_blocks=num_blocks)
+    o16, _ = _oracle(
+        shape, sd, prompts, max_new, depths, torch.bfloat16, forced=toks, kv_policy=kv_policy, num_blocks=num_blocks
+    )
+    eng = _engine(shape, sd, kv_policy=kv_policy, max_model_len=4096, num_blocks=num_blocks)
     eng.record_trace = True
     eng.keep_logits = True
     eng.generate_batch(prompts, max_new_tokens=max_new, eos_token_id=None, exit_depths=depths, forced_tokens=toks)
@@ -240,6 +242,53 @@ def test_teacher_forced_logits_config0_shape():
     run = next(r for r in data["runs"] if r["name"] == "replay_refill")
     sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
     assert_report(_compare_teacher_forced(shape, sd, data["prompts"], data["max_new_tokens"], run["exit_depths"]))
+
+
+PRESSURE_RUNS = [
+    ("replay_refill_blocks56", 0),
+    ("replay_refill_blocks48", 3),
+    ("replay_refill_blocks40", 2),
+    ("replay_norefill_blocks48", 2),
+    ("replay_norefill_blocks40", 1),
+]
+
+
+@pytest.mark.parametrize("name,preemptions", PRESSURE_RUNS)
+def test_kv_pressure_schedule_matches_reference(name, preemptions):
+    """KV pools too small for the workload (``tests/golden/ouro_cfg0_pressure.json``, recompute
+    mode): decoders stall and are restaged, stalled requests are preempted, re-prefilled from their
+    prompt plus the tokens read back from the device, and admission is held until a request
+    finishes. The launch trace, block tables and preemption count equal the reference's."""
+
+    data = json.loads((GOLDEN / "ouro_cfg0_pressure.json").read_text())
+    shape = OuroShape(**data["shape"])
+    run = next(r for r in data["runs"] if r["name"] == name)
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+    eng = _engine(shape, sd, refill=run["refill"], num_blocks=run["num_blocks"])
+    eng.record_trace = True
+    outs = eng.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"]
+    )
+    assert eng.launch_trace == run["launches"]
+    assert eng.last_stats.recompute_preemptions == run["stats"]["recompute_preemptions"] == preemptions
+    assert [len(o.generated_tokens) for o in outs] == data["max_new_tokens"]
+    hist = {str(k): v for k, v in sorted(eng.last_stats.exit_depth_histogram.items())}
+    assert hist == run["stats"]["exit_depth_histogram"]
+
+
+def test_kv_pressure_teacher_forced_logits():
+    """After a recompute preemption the re-prefilled requests (prompt + generated tokens at full
+    depth) continue with logits as accurate as the reference-style bf16 path (40-block pool)."""
+
+    data = json.loads((GOLDEN / "ouro_cfg0_pressure.json").read_text())
+    shape = OuroShape(**data["shape"])
+    run = next(r for r in data["runs"] if r["name"] == "replay_refill_blocks40")
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+    assert_report(
+        _compare_teacher_forced(
+            shape, sd, data["prompts"], data["max_new_tokens"], run["exit_depths"], num_blocks=run["num_blocks"]
+        )
+    )
 
 
 def test_teacher_forced_greedy_tokens_peaked_head():

@@ -126,7 +126,13 @@ def test_oracle_reproduces_reference_early_finish_run(name):
 
 @pytest.mark.parametrize(
     "name,preemptions",
-    [("replay_refill_blocks56", 0), ("replay_refill_blocks48", 3), ("replay_refill_blocks40", 2)],
+    [
+        ("replay_refill_blocks56", 0),
+        ("replay_refill_blocks48", 3),
+        ("replay_refill_blocks40", 2),
+        ("replay_norefill_blocks48", 2),
+        ("replay_norefill_blocks40", 1),
+    ],
 )
 def test_oracle_reproduces_reference_pressure_run(name, preemptions):
     """KV pressure under recompute: a decoder whose next block cannot be had stalls, is restaged
