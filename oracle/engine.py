@@ -91,6 +91,9 @@ class OracleConfig:
     kv_policy: str = "single"
     kv_slots_per_layer: int | None = None
     kv_pressure_mode: str = "recompute"
+    # host swap pool for kv_pressure_mode="offload", in blocks (the reference sizes it from
+    # cpu_offload_space GiB over the bytes of one block in every cache layer)
+    num_cpu_blocks: int = 0
     # use_async_batching and delay_gate_consumption both on (the reference's defaults): every
     # exit decision is applied at the routing after the item's next launch.
     delayed: bool = False
@@ -111,6 +114,7 @@ class Req:
     in_flight_tokens: int = 0
     cursor: int = 0
     exit_depths: list[int] = field(default_factory=list)
+    offloaded: bool = False
 
     def next_depth(self) -> int | None:
         if not self.depths:
@@ -248,19 +252,76 @@ class OracleEngine:
             raise RuntimeError("oracle: a single request's KV cache does not fit")
         victim = min(reversed(list(self.stalled)), key=lambda i: self.stalled[i].position)
         r = self.stalled.pop(victim)
+        offloaded = self._offload(r)
+        if not offloaded and self.cfg.kv_pressure_mode == "offload" and self.cfg.kv_policy == "last_exited":
+            raise RuntimeError("oracle: host pool full and the recompute fallback is off under last_exited")
         self._free(r)
         self.active.pop(r.idx, None)
         self.in_flight.discard(r.idx)
         self.waiting.pop(r.idx, None)
-        r.remaining = list(r.prompt) + list(r.generated)
-        r.to_process = []
-        r.position = 0
-        r.allocated = 0
-        r.status = PENDING
-        r.cursor += 1  # the pending token's depth is spent: it is recomputed at full depth
+        if offloaded:
+            # ``prepare_for_offload_requeue`` (``requests.py:275-288``): still decoding, same
+            # position and pending token; only the block allocation is dropped
+            r.allocated = 0
+            self.stats["offload_preemptions"] += 1
+        else:
+            r.remaining = list(r.prompt) + list(r.generated)
+            r.to_process = []
+            r.position = 0
+            r.allocated = 0
+            r.status = PENDING
+            r.cursor += 1  # the pending token's depth is spent: it is recomputed at full depth
+            self.stats["recompute_preemptions"] += 1
         self.waiting[r.idx] = r
         self.block_new = True
-        self.stats["recompute_preemptions"] += 1
+
+    def _offload(self, r: Req) -> bool:
+        """``OffloadingManager._offload_to_cpu`` (``offloading_manager.py:269-306``): copy every
+        block of the request (all cache layers, K and V) into the host pool; False when the pool
+        has too few free blocks (the caller then soft-resets instead)."""
+
+        if self.cfg.kv_pressure_mode != "offload" or self.cfg.num_cpu_blocks <= 0:
+            return False
+        blocks = self.tables.get(r.idx, [])
+        if not blocks or len(self.cpu_free) < len(blocks):
+            return False
+        host = [self.cpu_free.popleft() for _ in blocks]
+        rows = self.cache.rows_for(blocks, 0, len(blocks) * self.cfg.block_size)
+        saved = ([k[rows].clone() for k in self.cache.k], [v[rows].clone() for v in self.cache.v])
+        self.host_store[r.idx] = (host, saved)
+        r.offloaded = True
+        return True
+
+    def _restore_offloaded(self) -> list[Req]:
+        """``admit_offloaded_restores`` (``scheduler_base.py:434-460``) then
+        ``restore_scheduled_requests`` (``offloading_manager.py:216-267``): offloaded waiting
+        requests return to the active set in queue order, ahead of fresh prompts, while a resident
+        slot and blocks for their cached tokens plus the pending one are free; their KV is copied
+        into the new blocks and their host blocks are released."""
+
+        if self.block_new or self.cfg.kv_pressure_mode != "offload" or self.cfg.num_cpu_blocks <= 0:
+            return []
+        admitted = []
+        for i in list(self.waiting):
+            r = self.waiting[i]
+            if not r.offloaded:
+                continue
+            if max(0, self.max_num_seqs - len(self.active)) == 0 or not self._alloc_if_needed(r, 1):
+                break
+            self.active[i] = r
+            del self.waiting[i]
+            admitted.append(r)
+        for r in admitted:
+            host, (ks, vs) = self.host_store.pop(r.idx)
+            blocks = self.tables[r.idx][: len(host)]
+            rows = self.cache.rows_for(blocks, 0, len(blocks) * self.cfg.block_size)
+            for k, v, sk, sv in zip(self.cache.k, self.cache.v, ks, vs, strict=True):
+                k[rows] = sk
+                v[rows] = sv
+            self.cpu_free.extend(host)
+            r.offloaded = False
+            self.stats["restores"] += 1
+        return admitted
 
     def _next_token(self, r: Req, computed: int) -> int:
         if self.forced is not None:
@@ -297,7 +358,9 @@ class OracleEngine:
     def _prefill_candidates(self) -> list[Req]:
         prefilling = [r for r in self.active.values() if r.status == PREFILLING and r.idx not in self.in_flight]
         free_slots = max(0, self.max_num_seqs - len(self.active))
-        admissible = [] if self.block_new else [self.waiting[i] for i in list(self.waiting)[:free_slots]]
+        # fresh prompts only: offloaded requests come back through the restore path
+        fresh = [r for r in self.waiting.values() if not r.offloaded]
+        admissible = [] if self.block_new else fresh[:free_slots]
         if self.cfg.kv_pressure_mode == "reserve":
             committed = sum(self._reserved_peak(r) for r in self.active.values())
             kept = []
@@ -558,8 +621,10 @@ class OracleEngine:
             pending_coda = []
             if not self._has_pending():
                 continue
-            # decode tokens that could not get a KV block last tick go first, at the queue head
-            resumed = self._restage_stalled()
+            # restored requests, then decode tokens that could not get a KV block last tick, go
+            # first, at the queue head
+            resumed = [it for r in self._restore_offloaded() if (it := self._stage_decode(r)) is not None]
+            resumed += self._restage_stalled()
             self._prelude(resumed)
             self._enqueue_front(resumed)
             self.stats["ticks"] += 1
@@ -635,6 +700,9 @@ class OracleEngine:
         # the next wave ahead of the cohort scan (``continuous_api.py:721-790, 815-944``).
         carried: list[Item] = []
         while self._has_pending():
+            # offloaded requests come back before admission, so the prefill gate sees them as
+            # decoders, and join this wave's cohort (``continuous_api.py:656-658``)
+            self._restore_offloaded()
             did_prefill = False
             while self._admit_prefill():
                 pb = self._schedule_prefill()
@@ -725,6 +793,9 @@ class OracleEngine:
         self.free: deque[int] = deque(range(cfg.num_blocks))
         self.tables: dict[int, list[int]] = {}
         cache = OracleKVCache(self.shape, self.num_cache_layers, cfg.num_blocks, cfg.block_size, self.dtype)
+        self.cache = cache
+        self.cpu_free: deque[int] = deque(range(cfg.num_cpu_blocks))
+        self.host_store: dict[int, tuple[list[int], tuple[list[torch.Tensor], list[torch.Tensor]]]] = {}
         if self.huginn:
             self.model = HuginnOracle(self.weights, cache, self.slots)
         else:

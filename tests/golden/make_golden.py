@@ -164,7 +164,7 @@ class Recorder:
 
 def run_case(
     name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_depths=None, num_blocks=4096, async_mode=False,
-    eos_token_id=None, stop_sequences=None,
+    eos_token_id=None, stop_sequences=None, pressure_mode=None, cpu_offload_space=None,
 ):
     from looped_cdb.continuous_depth_batching import ContinuousDepthBatchingConfig, ContinuousDepthBatchingEngine
 
@@ -181,7 +181,8 @@ def run_case(
         use_cuda_graph_prefill=False,
         refill=refill,
         kv_policy=kv_policy,
-        kv_pressure_mode="reserve" if kv_policy == "last_exited" else "recompute",
+        kv_pressure_mode=pressure_mode or ("reserve" if kv_policy == "last_exited" else "recompute"),
+        cpu_offload_space=cpu_offload_space,
         max_model_len=2048,
     )
     engine = ContinuousDepthBatchingEngine.from_model(model, cfg)
@@ -215,6 +216,9 @@ def run_case(
             "scheduler_refills": stats.scheduler_refills,
             "exit_depth_histogram": {str(k): v for k, v in sorted(stats.exit_depth_histogram.items())},
             "recompute_preemptions": getattr(engine.offloading_manager, "num_recompute_preemptions", 0),
+            "offload_preemptions": getattr(engine.offloading_manager, "num_offload_preemptions", 0),
+            "restores": getattr(engine.offloading_manager, "num_restores", 0),
+            "num_cpu_blocks": getattr(engine.offloading_manager, "_num_cpu_blocks", 0),
         },
         "launches": rec.launches,
     }
@@ -404,8 +408,52 @@ def main() -> None:
         print(r["name"], r["stats"])
 
 
+def offload_main() -> None:
+    """``--offload``: the replayed schedules in KV pools too small for the workload under
+    ``kv_pressure_mode="offload"``. A stalled victim's blocks are swapped to a host pool of
+    ``num_cpu_blocks`` blocks and restored (admitted ahead of fresh prompts) once blocks free up;
+    a victim that does not fit the host pool falls back to recompute. Host pools of 64 blocks
+    (every victim fits), 2 and 1 (offload and recompute mixed), refill and no-refill, into
+    ``ouro_cfg0_offload.json``.
+    The host pool is given in GiB, as the reference's config takes it: ``num_cpu_blocks`` times
+    the bytes of one block over all cache layers (K and V) in the cache dtype."""
+
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    gold = json.loads((HERE / "ouro_cfg0.json").read_text())
+    block_bytes = 2 * CFG0.num_hidden_layers * 16 * CFG0.num_key_value_heads * CFG0.head_dim * 4
+    runs = []
+    for refill, nb, cpu_blocks in ((True, 48, 64), (True, 40, 2), (True, 48, 1), (False, 40, 64), (False, 48, 2)):
+        tag = "refill" if refill else "norefill"
+        depths = next(r for r in gold["runs"] if r["name"] == f"replay_{tag}")["exit_depths"]
+        res, _ = run_case(
+            f"replay_{tag}_blocks{nb}_host{cpu_blocks}", kv_policy="single", refill=refill, live_gate=False,
+            exit_depths=depths, num_blocks=nb, pressure_mode="offload",
+            cpu_offload_space=cpu_blocks * block_bytes / 1024**3,
+        )
+        assert res["stats"]["num_cpu_blocks"] == cpu_blocks, res["stats"]
+        res["num_blocks"] = nb
+        res["num_cpu_blocks"] = cpu_blocks
+        runs.append(res)
+    prompts, max_new = config0_workload()
+    payload = {
+        "generator": "tests/golden/make_golden.py --offload",
+        "shape": CFG0.__dict__,
+        "gate_std": GATE_STD,
+        "weights_seed": 0,
+        "prompts": prompts,
+        "max_new_tokens": max_new,
+        "block_size": 16,
+        "runs": runs,
+    }
+    (HERE / "ouro_cfg0_offload.json").write_text(json.dumps(payload, separators=(",", ":")))
+    for r in runs:
+        print(r["name"], r["stats"])
+
+
 if __name__ == "__main__":
-    if "--policies" in sys.argv[1:]:
+    if "--offload" in sys.argv[1:]:
+        offload_main()
+    elif "--policies" in sys.argv[1:]:
         policies_main()
     elif "--finish" in sys.argv[1:]:
         finish_main()

@@ -150,6 +150,38 @@ def test_oracle_reproduces_reference_pressure_run(name, preemptions):
     assert exit_depth_histogram(engine) == run["stats"]["exit_depth_histogram"]
 
 
+OFFLOAD_RUNS = [
+    # name, (recompute, offload, restores)
+    ("replay_refill_blocks48_host64", (0, 3, 3)),
+    ("replay_refill_blocks40_host2", (0, 2, 2)),
+    ("replay_refill_blocks48_host1", (2, 1, 1)),
+    ("replay_norefill_blocks40_host64", (0, 1, 1)),
+    ("replay_norefill_blocks48_host2", (1, 1, 1)),
+]
+
+
+@pytest.mark.parametrize("name,counts", OFFLOAD_RUNS)
+def test_oracle_reproduces_reference_offload_run(name, counts):
+    """KV pressure under offload: a stalled victim's blocks go to a host pool of ``num_cpu_blocks``
+    blocks (recompute when they do not fit) and come back, ahead of fresh prompts, into newly
+    allocated blocks. Tokens equal the reference's, so the restored KV is the victim's own."""
+
+    data, shape, sd = _load_ouro("ouro_cfg0_offload.json")
+    run = next(r for r in data["runs"] if r["name"] == name)
+    cfg = _config(run, {**data, "num_blocks": run["num_blocks"]})
+    cfg.kv_pressure_mode = "offload"
+    cfg.num_cpu_blocks = run["num_cpu_blocks"]
+    engine = OracleEngine(shape, sd, cfg, torch.float32)
+    tokens = engine.generate(data["prompts"], data["max_new_tokens"], exit_depths=run["exit_depths"])
+    assert tokens == run["tokens"]
+    assert engine.launches == run["launches"]
+    st = run["stats"]
+    assert (st["recompute_preemptions"], st["offload_preemptions"], st["restores"]) == counts
+    assert (
+        engine.stats["recompute_preemptions"], engine.stats["offload_preemptions"], engine.stats["restores"]
+    ) == counts
+
+
 @pytest.mark.parametrize("name", ["live_gate_refill", "replay_refill", "replay_norefill", "replay_last_exited"])
 def test_oracle_reproduces_reference_run(golden, name):
     data, shape, sd = golden
