@@ -88,6 +88,9 @@ _SIGNATURES: dict[str, list] = {
     "cdb_latent_diff": [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_void_p],
     "cdb_block_table_update": [c_void_p, c_int64, c_void_p, c_int, c_void_p],
     "cdb_exit_kv_copy": [c_void_p, c_int, c_int64, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p],
+    "cdb_kv_blocks_host_copy": [
+        c_void_p, c_int, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p,
+    ],
     "cdb_exit_hazard": [
         c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_double, c_void_p,
     ],
@@ -175,6 +178,7 @@ def stream_ptr(stream: torch.cuda.Stream | None = None) -> int:
 
 _NO_LAUNCH = {
     "cdb_version", "cdb_status_string", "cdb_attn_scratch_bytes", "cdb_gemm_workspace_elems", "cdb_schedule_queues_init",
+    "cdb_kv_blocks_host_copy",
 }
 # Kernels enqueued through this binding (device work only; graph replays are counted by the runner).
 launch_count = 0

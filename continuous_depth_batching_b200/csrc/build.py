@@ -18,7 +18,7 @@ CSRC = Path(__file__).resolve().parent
 PKG = CSRC.parent
 REPO = PKG.parent
 LIB_NAME = "libcdb_b200.so"
-SOURCES = ["attention.cu", "prefill_attention.cu", "elementwise.cu", "gemm.cu", "scheduler.cu", "fused_ops.cu"]
+SOURCES = ["attention.cu", "prefill_attention.cu", "elementwise.cu", "gemm.cu", "scheduler.cu", "fused_ops.cu", "kv_swap.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -98,6 +98,8 @@ class ContinuousDepthBatchingStats:
     host_syncs: int = 0
     kv_peak_blocks: int = 0
     recompute_preemptions: int = 0
+    offload_preemptions: int = 0
+    restores: int = 0
 
     @property
     def skipped_recurrent_steps(self) -> int:
@@ -116,7 +118,7 @@ class _Req:
     __slots__ = (
         "idx", "request_id", "prompt", "max_new", "depths", "cursor", "status", "remaining", "chunk",
         "position", "allocated", "generated", "slot", "log_base", "exit_depths", "eos", "stops",
-        "created", "start", "finish", "first_token", "token_times", "record_times", "pending_token",
+        "created", "start", "finish", "first_token", "token_times", "record_times", "pending_token", "offloaded",
     )
 
     def __init__(self, idx: int, prompt: list[int], max_new: int, depths: list[int], eos: set[int], stops, rec: bool):
@@ -144,6 +146,7 @@ class _Req:
         self.token_times: list[float] = []
         self.record_times = rec
         self.pending_token = -1
+        self.offloaded = False
 
     def next_depth(self) -> int | None:
         if not self.depths:
@@ -279,6 +282,9 @@ class ContinuousDepthBatchingEngine:
             gemm_backend=gemm_backend,
             fused_lm_head=fused_lm_head,
         )
+        if cfg.kv_pressure_mode == "offload" and cfg.cpu_offload_space:
+            # ``OffloadingManager._compute_num_cpu_blocks`` (``offloading_manager.py:134-144``)
+            runner.pool.attach_host_pool(int(cfg.cpu_offload_space * 1024**3) // runner.pool.block_bytes)
         return cls(model, cfg, runner, shape)
 
     # ------------------------------------------------------------------ public API
@@ -388,6 +394,9 @@ class ContinuousDepthBatchingEngine:
         self.backlog: list[tuple[_Item, int]] = []
         self.stalled: OrderedDict[int, _Req] = OrderedDict()
         self.block_new = False
+        self.num_host_blocks = self.runner.pool.num_host_blocks if cfg.kv_pressure_mode == "offload" else 0
+        self.host_free: deque[int] = deque(range(self.num_host_blocks))
+        self.host_tables: dict[int, list[int]] = {}
         self.refills = 0
         self.max_queue = 0
         self.free_slots = list(range(cfg.max_num_seqs - 1, -1, -1))
@@ -509,20 +518,18 @@ class ContinuousDepthBatchingEngine:
         return items
 
     def _preempt_stalled(self) -> None:
-        """``_preempt_stalled_decoder`` (``continuous_api.py:1625-1652``) with the recompute soft
-        reset (``create_equivalent_initial_request``, ``requests.py:290-315``).
+        """``_preempt_stalled_decoder`` (``continuous_api.py:1625-1652``) and
+        ``OffloadingManager._preempt`` (``offloading_manager.py:180-214``).
 
         The victim is the stalled request with the fewest cached tokens, ties going to the latest
-        staller. Its blocks and block-table row are released. Its generated tokens are appended to its
-        prompt for a full-depth re-prefill, and it re-enters the waiting queue at the back. The depth
-        its pending token would have replayed is skipped. No new prompt is admitted until a request
-        finishes."""
+        staller. Under ``offload`` its blocks are first copied to the host pool if they fit there;
+        it then waits, still decoding, until :meth:`_restore_offloaded` brings it back. Otherwise
+        (``recompute``, or a full host pool) it is soft-reset (``create_equivalent_initial_request``,
+        ``requests.py:290-315``): its generated tokens are appended to its prompt for a full-depth
+        re-prefill, and the depth its pending token would have replayed is skipped. Either way its
+        blocks and block-table row are released, it re-enters the waiting queue at the back, and no
+        new prompt is admitted until a request finishes."""
 
-        if self.cdb_config.kv_pressure_mode == "offload":
-            raise NotImplementedError(
-                "kv_pressure_mode='offload' (swapping a stalled request's KV blocks to host memory) is not "
-                "built in the B200 engine; use 'recompute' or 'reserve'"
-            )
         if len(self.active) <= 1:
             rid = next(iter(self.stalled.values())).request_id
             raise CacheFullError(
@@ -531,25 +538,90 @@ class ContinuousDepthBatchingEngine:
             )
         victim = min(reversed(list(self.stalled)), key=lambda i: self.stalled[i].position)
         r = self.stalled.pop(victim)
-        if self._forced is None:
-            self.last_stats.host_syncs += 1
-            self.runner.stream.synchronize()
-        generated = self._host_tokens(r)
+        offloaded = self._offload(r)
+        if not offloaded:
+            if self.num_host_blocks and copies_exit_kv(self.cdb_config.kv_policy):
+                raise RuntimeError(
+                    f"CPU swap pool cannot hold request {r.request_id} ({r.allocated} blocks needed, "
+                    f"{len(self.host_free)} free) and the soft-reset fallback is disabled: re-prefilling at "
+                    "full depth would replace the KV this cache policy rewrote on early exit. Increase "
+                    "cpu_offload_space or reduce load."
+                )
+            if self._forced is None:
+                self.last_stats.host_syncs += 1
+                self.runner.stream.synchronize()
+            generated = self._host_tokens(r)
         self.pool.release(r.idx)
         self.active.pop(r.idx, None)
         self.in_flight.discard(r.idx)
         self.waiting.pop(r.idx, None)
         self.free_slots.append(r.slot)
         r.slot = -1
-        r.remaining = list(r.prompt) + generated
-        r.chunk = []
-        r.position = 0
         r.allocated = 0
-        r.status = RequestStatus.PENDING
-        r.cursor += 1
+        if offloaded:
+            # ``prepare_for_offload_requeue`` (``requests.py:275-288``): still decoding, with its
+            # position and pending token; only the blocks are given up
+            self.last_stats.offload_preemptions += 1
+        else:
+            r.remaining = list(r.prompt) + generated
+            r.chunk = []
+            r.position = 0
+            r.status = RequestStatus.PENDING
+            r.cursor += 1
+            self.last_stats.recompute_preemptions += 1
         self.waiting[r.idx] = r
         self.block_new = True
-        self.last_stats.recompute_preemptions += 1
+
+    def _offload(self, r: _Req) -> bool:
+        """``OffloadingManager._offload_to_cpu`` (``offloading_manager.py:269-306``): queue the copy of
+        every block of ``r`` into free host blocks; False when the host pool has too few."""
+
+        if not self.num_host_blocks:
+            return False
+        blocks = self.pool.tables.get(r.idx, [])
+        if not blocks or len(self.host_free) < len(blocks):
+            return False
+        host = [self.host_free.popleft() for _ in blocks]
+        self.runner.pool.host_copy(blocks, host, True, self.runner.stream)
+        self.host_tables[r.idx] = host
+        r.offloaded = True
+        return True
+
+    def _restore_offloaded(self) -> list[_Req]:
+        """``admit_offloaded_restores`` (``scheduler_base.py:434-460``) and
+        ``restore_scheduled_requests`` (``offloading_manager.py:216-267``).
+
+        Offloaded waiting requests return to the active set in queue order, ahead of fresh prompts,
+        while a resident slot and blocks for their cached tokens plus the pending one are free (the
+        first that does not fit ends the scan; nothing returns while admission is held). Each gets a
+        block-table row, its host blocks are copied into its new blocks, and its pending token is
+        rebound to the new row."""
+
+        if self.block_new or not self.num_host_blocks:
+            return []
+        admitted = []
+        for i in list(self.waiting):
+            r = self.waiting[i]
+            if not r.offloaded:
+                continue
+            if max(0, self.max_num_seqs - len(self.active)) == 0:
+                break
+            r.slot = self.free_slots.pop()
+            if not self._alloc_if_needed(r, 1):
+                self.free_slots.append(r.slot)
+                r.slot = -1
+                break
+            self.active[i] = r
+            del self.waiting[i]
+            admitted.append(r)
+        for r in admitted:
+            host = self.host_tables.pop(r.idx)
+            self.runner.pool.host_copy(self.pool.tables[r.idx][: len(host)], host, False, self.runner.stream)
+            self.host_free.extend(host)
+            self.runner.rebind_token(r.slot, r.log_base + r.generated - 1)
+            r.offloaded = False
+            self.last_stats.restores += 1
+        return admitted
 
     def _prelude(self, items: list[_Item]) -> None:
         if items:
@@ -597,7 +669,8 @@ class ContinuousDepthBatchingEngine:
             # after a preemption no new prompt is admitted until a request finishes
             if self.block_new or len(admissible) >= free_res:
                 break
-            admissible.append(self.waiting[key])
+            if not self.waiting[key].offloaded:  # offloaded requests return through the restore path
+                admissible.append(self.waiting[key])
         if self.cdb_config.kv_pressure_mode == "reserve":
             committed = sum(self._reserved_peak(r) for r in self.active.values())
             kept = []
@@ -931,9 +1004,12 @@ class ContinuousDepthBatchingEngine:
                 if arrivals:
                     self._wait_next_arrival(arrivals)
                 continue
-            # decode tokens that found no KV block last tick go first, at the queue head
+            # restored requests, then decode tokens that found no KV block last tick, go first, at
+            # the queue head
+            resumed = [it for r in self._restore_offloaded() if (it := self._stage_decode(r)) is not None]
             if self.stalled:
-                resumed = self._restage_stalled()
+                resumed += self._restage_stalled()
+            if resumed:
                 self._prelude(resumed)
                 self._enqueue_front(resumed)
             self.last_stats.scheduler_ticks += 1
@@ -1056,6 +1132,9 @@ class ContinuousDepthBatchingEngine:
                     self._wait_next_arrival(arrivals)
                 continue
             self.last_stats.scheduler_ticks += 1
+            # offloaded requests come back before admission, so the prefill gate counts them as
+            # decoders, and join this wave's cohort (``continuous_api.py:656-658``)
+            self._restore_offloaded()
             did_prefill = False
             while self._admit_prefill():
                 pb = self._schedule_prefill()

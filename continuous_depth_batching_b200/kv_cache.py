@@ -195,6 +195,47 @@ class PagedKVPool:
         )
         self.block_table = torch.full((resident_slots, self.width), -1, dtype=torch.int32, device=device)
         self.pool = BlockPool(num_blocks, block_size, self.width)
+        self.row_bytes = num_kv_heads * head_dim * self.kv.element_size()
+        self.num_host_blocks = 0
+        self.host_pool: torch.Tensor | None = None
+
+    @property
+    def block_bytes(self) -> int:
+        """Bytes of one block over every cache layer, K and V (``OffloadingManager._bytes_per_block``,
+        ``offloading_manager.py:146-157``)."""
+
+        return 2 * self.num_cache_layers * self.block_size * self.row_bytes
+
+    def attach_host_pool(self, num_host_blocks: int) -> None:
+        """Pinned host swap pool of ``num_host_blocks`` blocks for offload preemption, laid out
+        ``[host_blocks, cache_layers * 2, block_size * row_bytes]``."""
+
+        self.num_host_blocks = max(0, int(num_host_blocks))
+        self.host_pool = None
+        if self.num_host_blocks:
+            self.host_pool = torch.empty(
+                (self.num_host_blocks, 2 * self.num_cache_layers, self.block_size * self.row_bytes),
+                dtype=torch.uint8,
+                pin_memory=True,
+            )
+
+    def host_copy(self, device_blocks: list[int], host_blocks: list[int], to_host: bool, stream) -> None:
+        """Copy whole blocks (every cache layer, K and V) between the device pool and the host pool
+        on ``stream`` (``cdb_kv_blocks_host_copy``)."""
+
+        if len(device_blocks) != len(host_blocks):
+            raise ValueError("device_blocks and host_blocks must pair up")
+        if not device_blocks:
+            return
+        if self.host_pool is None:
+            raise RuntimeError("no host swap pool is attached")
+        dev = torch.tensor(device_blocks, dtype=torch.int32)
+        host = torch.tensor(host_blocks, dtype=torch.int32)
+        _lib.call(
+            "cdb_kv_blocks_host_copy", _lib.ptr(self.kv), self.num_cache_layers, self.rows, self.row_bytes,
+            self.block_size, self.num_blocks, dev.data_ptr(), self.host_pool.data_ptr(), self.num_host_blocks,
+            host.data_ptr(), len(device_blocks), int(to_host), stream.cuda_stream,
+        )
 
     def key_cache(self, cache_layer: int) -> torch.Tensor:
         return self.kv[cache_layer, 0]

@@ -338,6 +338,14 @@ class OuroRunner:
     def upload(self, values) -> torch.Tensor:
         return self.uploader.upload(values, self.stream)
 
+    def rebind_token(self, req_slot: int, log_row: int) -> None:
+        """Set a request's device token (token table row ``req_slot``) to the token at ``log_row``
+        of the token log: a request restored from the host pool resumes in a new block-table row,
+        and its pending decode token must follow it there."""
+
+        with torch.cuda.stream(self.stream):
+            self.token_table[req_slot : req_slot + 1].copy_(self.token_log[log_row : log_row + 1])
+
     def flush_block_edits(self) -> None:
         self.pool.flush_edits(self.upload, self.stream)
 

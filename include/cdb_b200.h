@@ -296,6 +296,19 @@ int cdb_latent_diff(const void* new_state, int64_t new_stride, const void* old_s
  * _refresh_cached_block_table (cache_manager.py:150-165, continuous_depth_batching/cache.py:115-144). */
 int cdb_block_table_update(int32_t* table, int64_t stride, const int32_t* edits, int num_edits, void* stream);
 
+/* Offload preemption: copy num KV blocks between the paged device pool kv_base
+ * [num_cache_layers][2][kv_rows][row_bytes] and a host pool host_pool
+ * [num_host_blocks][2 * num_cache_layers][block_size * row_bytes] (pinned, so the copies run
+ * asynchronously). Block i moves between device block device_blocks[i] and host block
+ * host_blocks[i], all cache layers, K and V; to_host = 1 copies device -> host, 0 host -> device.
+ * device_blocks and host_blocks are HOST arrays; every id is range-checked (CDB_ERR_INDEX, nothing
+ * queued) before the copies are queued on stream. Enqueues copies only, no kernel.
+ * Replaces OffloadingManager._offload_to_cpu / restore_scheduled_requests
+ * (offloading_manager.py:216-306), whose per-block, per-layer copy_ loops become one 2-D copy per block. */
+int cdb_kv_blocks_host_copy(void* kv_base, int num_cache_layers, int64_t kv_rows, int64_t row_bytes, int block_size,
+                            int num_device_blocks, const int32_t* device_blocks, void* host_pool, int num_host_blocks,
+                            const int32_t* host_blocks, int num, int to_host, void* stream);
+
 /* last_exited copy-on-exit: for each token row in rows[n] copy K and V of cache layer
  * src_layers[i] into dst_layers[i] (num_pairs pairs). PagedAttentionCache.copy_kv_rows driven by
  * _flush_exit_kv_copies (continuous_depth_batching/cache.py:105-113, continuous_api.py:1225-1245). */

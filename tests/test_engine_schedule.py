@@ -34,7 +34,13 @@ class _HostRunner:
 
     def __init__(self, cfg: ContinuousDepthBatchingConfig, shape: OuroShape) -> None:
         self.vocab = shape.vocab_size
-        self.pool = SimpleNamespace(pool=BlockPool(cfg.num_blocks, cfg.block_size, cfg.decode_block_table_width()))
+        self.pool = SimpleNamespace(
+            pool=BlockPool(cfg.num_blocks, cfg.block_size, cfg.decode_block_table_width()),
+            num_host_blocks=0,
+            host_copies=[],
+            host_copy=lambda dev, host, to_host, stream: self.pool.host_copies.append((list(dev), list(host), to_host)),
+        )
+        self.rebinds: list[tuple[int, int]] = []
         self.layout = LoopedKvLayout(
             num_prelude_layers=0, num_core_layers=shape.num_hidden_layers, num_coda_layers=0,
             total_recurrent_steps=cfg.max_recurrent_steps, policy=cfg.kv_policy,
@@ -73,6 +79,9 @@ class _HostRunner:
     def exit_kv_copy(self, rows, pairs) -> None:
         pass
 
+    def rebind_token(self, req_slot: int, log_row: int) -> None:
+        self.rebinds.append((req_slot, log_row))
+
     def read_tokens(self, n: int) -> list[int]:
         return self.token_log[:n].tolist()
 
@@ -80,9 +89,10 @@ class _HostRunner:
         pass
 
 
-def _engine(data: dict, run: dict, num_blocks: int) -> ContinuousDepthBatchingEngine:
+def _engine(data: dict, run: dict, num_blocks: int, host_blocks: int = 0) -> ContinuousDepthBatchingEngine:
     shape = OuroShape(**data["shape"])
     kv_policy = run.get("kv_policy", "single")
+    pressure = "offload" if host_blocks else ("reserve" if kv_policy == "last_exited" else "recompute")
     cfg = ContinuousDepthBatchingConfig(
         block_size=16,
         num_blocks=num_blocks,
@@ -91,10 +101,13 @@ def _engine(data: dict, run: dict, num_blocks: int) -> ContinuousDepthBatchingEn
         use_async_batching=run.get("async", False),
         refill=run["refill"],
         kv_policy=kv_policy,
-        kv_pressure_mode="reserve" if kv_policy == "last_exited" else "recompute",
+        kv_pressure_mode=pressure,
+        cpu_offload_space=1.0 if host_blocks else None,
         max_model_len=2048,
     ).get_resolved()
-    eng = ContinuousDepthBatchingEngine(None, cfg, _HostRunner(cfg, shape), shape)
+    runner = _HostRunner(cfg, shape)
+    runner.pool.num_host_blocks = host_blocks
+    eng = ContinuousDepthBatchingEngine(None, cfg, runner, shape)
     eng.record_trace = True
     return eng
 
@@ -114,8 +127,8 @@ def _check_prefill_contents(eng: ContinuousDepthBatchingEngine, prompts, outs) -
         assert k == len(ids)
 
 
-def _run(data: dict, run: dict, num_blocks: int, forced=None, eos=None, stops=None):
-    eng = _engine(data, run, num_blocks)
+def _run(data: dict, run: dict, num_blocks: int, forced=None, eos=None, stops=None, host_blocks: int = 0):
+    eng = _engine(data, run, num_blocks, host_blocks)
     outs = eng.generate_batch(
         data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=eos, stop_sequences=stops,
         exit_depths=run["exit_depths"], forced_tokens=forced,
@@ -153,6 +166,42 @@ def test_kv_pressure_schedule_matches_reference(name, preemptions):
     ]
     _check_prefill_contents(eng, data["prompts"], outs)
     assert not eng.stalled and not eng.block_new
+
+
+OFFLOAD = [
+    # name, (recompute, offload, restores)
+    ("replay_refill_blocks48_host64", (0, 3, 3)),
+    ("replay_refill_blocks40_host2", (0, 2, 2)),
+    ("replay_refill_blocks48_host1", (2, 1, 1)),
+    ("replay_norefill_blocks40_host64", (0, 1, 1)),
+    ("replay_norefill_blocks48_host2", (1, 1, 1)),
+]
+
+
+@pytest.mark.parametrize("name,counts", OFFLOAD)
+def test_kv_offload_schedule_matches_reference(name, counts):
+    """Offload mode: victims' blocks go to the host pool (recompute when it is full) and return
+    ahead of fresh prompts; the launch trace, block tables and counters equal the reference's. Each
+    restore copies back exactly the host blocks its offload filled, into the first of the request's
+    new blocks, and rebinds its pending token to its new block-table row."""
+
+    data = _load("ouro_cfg0_offload.json")
+    run = next(r for r in data["runs"] if r["name"] == name)
+    eng, outs = _run(data, run, run["num_blocks"], host_blocks=run["num_cpu_blocks"])
+    assert eng.launch_trace == run["launches"]
+    st = eng.last_stats
+    assert (st.recompute_preemptions, st.offload_preemptions, st.restores) == counts
+    assert [len(o.generated_tokens) for o in outs] == data["max_new_tokens"]
+    _check_prefill_contents(eng, data["prompts"], outs)
+    copies = eng.runner.pool.host_copies
+    outs_ = [c for c in copies if c[2]]
+    ins = [c for c in copies if not c[2]]
+    assert len(outs_) == counts[1] and len(ins) == counts[2]
+    for (dev_out, host_out, _), (dev_in, host_in, _) in zip(outs_, ins, strict=True):
+        assert host_in == host_out and len(dev_in) == len(dev_out)
+        assert max(host_out) < run["num_cpu_blocks"]
+    assert len(eng.runner.rebinds) == counts[2]
+    assert not eng.host_tables and len(eng.host_free) == run["num_cpu_blocks"]
 
 
 def _log_bases(max_new: list[int]) -> list[int]:

@@ -36,8 +36,16 @@ def _golden():
     return data, shape
 
 
+def _host_space(shape, host_blocks: int) -> float | None:
+    """``cpu_offload_space`` (GiB) that sizes the host pool at ``host_blocks`` bf16 blocks."""
+
+    if not host_blocks:
+        return None
+    return host_blocks * 2 * shape.num_hidden_layers * 16 * shape.num_key_value_heads * shape.head_dim * 2 / 1024**3
+
+
 def _engine(shape, sd, *, kv_policy="single", refill=True, live=False, num_blocks=4096, max_model_len=2048, graphs=True,
-            gemm="cublas", async_mode=False):
+            gemm="cublas", async_mode=False, host_blocks=0):
     model = OuroForCausalLM(shape)
     model.load_state_dict({k: v.to(torch.float32) for k, v in sd.items()})
     cfg = ContinuousDepthBatchingConfig(
@@ -50,10 +58,13 @@ def _engine(shape, sd, *, kv_policy="single", refill=True, live=False, num_block
         use_cuda_graph=graphs,
         refill=refill,
         kv_policy=kv_policy,
-        kv_pressure_mode="reserve" if kv_policy == "last_exited" else "recompute",
+        kv_pressure_mode="offload" if host_blocks else ("reserve" if kv_policy == "last_exited" else "recompute"),
+        cpu_offload_space=_host_space(shape, host_blocks),
         max_model_len=max_model_len,
     )
-    return ContinuousDepthBatchingEngine.from_model(model, cfg, device="cuda", gemm_backend=gemm)
+    eng = ContinuousDepthBatchingEngine.from_model(model, cfg, device="cuda", gemm_backend=gemm)
+    assert eng.runner.pool.num_host_blocks == host_blocks
+    return eng
 
 
 @pytest.mark.parametrize("name", ["replay_refill", "replay_norefill", "replay_last_exited"])
@@ -202,11 +213,13 @@ def test_live_hazard_gate_matches_reference_decisions(fixture, name, refill):
     assert agree >= 0.95
 
 
-def _oracle(shape, sd, prompts, max_new, depths, dtype, forced=None, kv_policy="single", num_blocks=4096):
+def _oracle(shape, sd, prompts, max_new, depths, dtype, forced=None, kv_policy="single", num_blocks=4096,
+            host_blocks=0, refill=True):
     cfg = OracleConfig(
         block_size=16, num_blocks=num_blocks, max_recurrent_steps=shape.total_ut_steps, max_model_len=4096,
-        synthetic_exit_replay=True, kv_policy=kv_policy,
-        kv_pressure_mode="reserve" if kv_policy == "last_exited" else "recompute",
+        synthetic_exit_replay=True, kv_policy=kv_policy, refill=refill,
+        kv_pressure_mode="offload" if host_blocks else ("reserve" if kv_policy == "last_exited" else "recompute"),
+        num_cpu_blocks=host_blocks,
     )
     eng = OracleEngine(shape, sd, cfg, dtype)
     toks = eng.generate(prompts, max_new, exit_depths=depths, forced_tokens=forced)
@@ -289,6 +302,67 @@ def test_kv_pressure_teacher_forced_logits():
             shape, sd, data["prompts"], data["max_new_tokens"], run["exit_depths"], num_blocks=run["num_blocks"]
         )
     )
+
+
+OFFLOAD_RUNS = [
+    # name, (recompute, offload, restores)
+    ("replay_refill_blocks48_host64", (0, 3, 3)),
+    ("replay_refill_blocks40_host2", (0, 2, 2)),
+    ("replay_refill_blocks48_host1", (2, 1, 1)),
+    ("replay_norefill_blocks40_host64", (0, 1, 1)),
+    ("replay_norefill_blocks48_host2", (1, 1, 1)),
+]
+
+
+def _offload_golden(name):
+    data = json.loads((GOLDEN / "ouro_cfg0_offload.json").read_text())
+    shape = OuroShape(**data["shape"])
+    run = next(r for r in data["runs"] if r["name"] == name)
+    return data, shape, run, random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+
+
+@pytest.mark.parametrize("name,counts", OFFLOAD_RUNS)
+def test_kv_offload_schedule_matches_reference(name, counts):
+    """Offload mode (``tests/golden/ouro_cfg0_offload.json``): stalled victims' blocks are copied
+    to the pinned host pool (recompute when it is full) and back into new blocks ahead of fresh
+    prompts. The launch trace, block tables and counters equal the reference's."""
+
+    data, shape, run, sd = _offload_golden(name)
+    eng = _engine(shape, sd, refill=run["refill"], num_blocks=run["num_blocks"], host_blocks=run["num_cpu_blocks"])
+    eng.record_trace = True
+    outs = eng.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"]
+    )
+    assert eng.launch_trace == run["launches"]
+    st = eng.last_stats
+    assert (st.recompute_preemptions, st.offload_preemptions, st.restores) == counts
+    assert [len(o.generated_tokens) for o in outs] == data["max_new_tokens"]
+
+
+@pytest.mark.parametrize("name", ["replay_refill_blocks48_host1", "replay_norefill_blocks48_host2"])
+def test_kv_offload_logits_on_own_tokens(name):
+    """The engine runs on its own tokens through offloads, restores and a recompute; the fp32 and
+    bf16 oracles are then forced onto those tokens. Every LM-head launch must meet the numerics
+    criteria. A restored request whose KV or pending token came back wrong would miss them by far."""
+
+    data, shape, run, sd = _offload_golden(name)
+    hb = run["num_cpu_blocks"]
+    eng = _engine(shape, sd, refill=run["refill"], num_blocks=run["num_blocks"], max_model_len=4096, host_blocks=hb)
+    eng.record_trace = True
+    eng.keep_logits = True
+    outs = eng.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"]
+    )
+    assert eng.last_stats.restores >= 1
+    toks = [o.generated_tokens for o in outs]
+    args = (shape, sd, data["prompts"], data["max_new_tokens"], run["exit_depths"])
+    kw = {"forced": toks, "num_blocks": run["num_blocks"], "host_blocks": hb, "refill": run["refill"]}
+    o32, _ = _oracle(*args, torch.float32, **kw)
+    o16, _ = _oracle(*args, torch.bfloat16, **kw)
+    assert eng.launch_trace == o32.launches == o16.launches
+    rep = compare_lm_launches([lg for _, lg in eng.lm_logits], [lg for _, lg in o16.logits], [lg for _, lg in o32.logits])
+    print(rep)
+    assert_report(rep)
 
 
 def test_teacher_forced_greedy_tokens_peaked_head():

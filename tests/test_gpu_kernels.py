@@ -360,6 +360,47 @@ def test_block_table_edits_and_exit_copy():
     assert torch.equal(kv[2][:, untouched], before[2][:, untouched])
 
 
+def test_kv_blocks_host_copy_round_trip():
+    """Offload swap (``cdb_kv_blocks_host_copy``): whole blocks (every cache layer, K and V) go out
+    to a pinned host pool and come back into other blocks bit for bit; block ids out of range are
+    refused before anything is queued."""
+
+    from continuous_depth_batching_b200.kv_cache import PagedKVPool
+
+    pool = PagedKVPool(
+        num_cache_layers=3, num_blocks=12, block_size=16, num_kv_heads=4, head_dim=64, max_model_len=256,
+        resident_slots=4, device=torch.device(DEV),
+    )
+    pool.kv.copy_(torch.randn(pool.kv.shape, device=DEV).to(torch.bfloat16))
+    before = pool.kv.clone()
+    pool.attach_host_pool(8)
+    assert pool.host_pool.is_pinned() and pool.block_bytes == 2 * 3 * 16 * 4 * 64 * 2
+    stream = torch.cuda.current_stream()
+    pool.host_copy([5, 2, 9], [3, 0, 7], True, stream)
+    torch.cuda.synchronize()
+    host = pool.host_pool.view(torch.bfloat16).view(8, 3, 2, 16, 4, 64)
+
+    def blk(t, b):
+        return t[:, :, b * 16 : (b + 1) * 16]
+
+    for d, h in ((5, 3), (2, 0), (9, 7)):
+        assert torch.equal(host[h], blk(before, d).cpu())
+    pool.kv.zero_()
+    pool.host_copy([1, 11, 4], [3, 0, 7], False, stream)
+    torch.cuda.synchronize()
+    for d, src in ((1, 5), (11, 2), (4, 9)):
+        assert torch.equal(blk(pool.kv, d), blk(before, src))
+    others = [b for b in range(14) if b not in (1, 11, 4)]
+    assert all(int(blk(pool.kv, b).abs().sum()) == 0 for b in others)
+    snapshot = pool.kv.clone()
+    with pytest.raises(_lib.CDBError):
+        pool.host_copy([3, 12], [0, 1], True, stream)
+    with pytest.raises(_lib.CDBError):
+        pool.host_copy([3], [8], False, stream)
+    torch.cuda.synchronize()
+    assert torch.equal(pool.kv, snapshot)
+
+
 def test_exit_hazard_matches_host_policy():
     n = 6
     logits = torch.tensor([0.3, -2.0, 4.0, 0.0, -0.1, 1.5], device=DEV).to(torch.bfloat16)
