@@ -18,6 +18,10 @@ with its own seeded request set (``scaling: weak``); nothing crosses GPUs inside
 
 ``--impl reference`` times the CPU restatement of the reference engine (``oracle/``, the only
 place bench.py runs it) on the host cores over a bounded prefix of the same workload.
+
+``--engine cb`` times the full-depth continuous-batching baseline (``ContinuousBatchingEngine``,
+the reference's CB comparison engine) on the same kernels, graphs and workload, and prints its
+own line with ``"engine": "cb"``; every token then runs all 4 recurrent steps.
 """
 
 from __future__ import annotations
@@ -62,6 +66,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--num-blocks", type=int, default=16384, help="KV pool blocks (small for profiler captures)")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle timing (profiling runs)")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--engine", default="cdb", choices=["cdb", "cb"],
+                   help="cdb: the CDB engine (the headline); cb: the full-depth continuous-batching baseline")
     return p.parse_args()
 
 
@@ -501,10 +507,75 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_cb(args) -> None:
+    """The full-depth CB baseline on one GPU: generated tokens / device time over K timed steps."""
+
+    from continuous_depth_batching_b200 import ContinuousBatchingConfig, ContinuousBatchingEngine, OuroForCausalLM, OuroShape
+
+    rank, world, local = dist_env()
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"engine": "cb", "unavailable": "the CB baseline line is measured on one GPU"}))
+        return
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    shape = OuroShape(**OURO_1P4B)
+    model = OuroForCausalLM.random_init(shape, seed=1234, dtype=torch.bfloat16, device=device)
+    cfg = ContinuousBatchingConfig(
+        block_size=16, num_blocks=args.num_blocks, use_async_batching=True, use_cuda_graph=not args.no_graph,
+        max_model_len=4096, max_num_seqs=256,
+    )
+    eng = ContinuousBatchingEngine.from_model(
+        model, cfg, device=device, kv_policy="single", gemm_backend=args.gemm,
+        fused_lm_head=getattr(args, "lm_head", "fused") == "fused",
+    )
+    del model
+    prompts, max_new, _depths = workload(replica_seed(args.seed, rank), args.requests, args.out_cap)
+    stream = eng.runner.stream
+
+    def step():
+        return eng.generate_batch(prompts, max_new_tokens=max_new, eos_token_id=None)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    tokens = 0
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            outs = step()
+            tokens += sum(len(o.generated_tokens) for o in outs)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    st = eng.last_stats
+    print(json.dumps({
+        "metric": "decode tokens/s/GPU, Ouro-1.4B full-depth continuous batching (baseline engine, same kernels)",
+        "engine": "cb",
+        "value": round(tokens / (ms / 1e3), 1),
+        "unit": UNIT,
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 2),
+        "higher_is_better": True,
+        "dtype": "bf16",
+        "data": "synthetic (the CDB line's seeded requests; every token at full depth)",
+        "config": {"workload": "BASELINE config 1 requests, full-depth CB baseline", "requests": args.requests,
+                   "kv_policy": "single", "gemm": args.gemm, "use_async_batching": True},
+        "batches": {"prefill": st.prefill_batches, "decode": st.decode_batches,
+                    "mean_decode_batch": round(st.mean_decode_batch_size, 1)},
+        "clocks": clocks.summary(),
+    }))
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.engine == "cb":
+        run_cb(args)
     else:
         run_b200(args)
 

@@ -2,10 +2,12 @@
 
 Drop-in surface of ``looped_cdb.continuous_depth_batching``: build an engine with
 ``ContinuousDepthBatchingEngine.from_model(model, ContinuousDepthBatchingConfig(...))`` and call
-``generate_batch``. Ouro and Huginn models are served. Compute runs in ``libcdb_b200.so`` (hand-written sm_100a kernels behind the C
+``generate_batch``. Ouro and Huginn models are served. ``ContinuousBatchingEngine`` is the
+full-depth continuous-batching baseline on the same kernels. Compute runs in ``libcdb_b200.so`` (hand-written sm_100a kernels behind the C
 ABI in ``include/cdb_b200.h``) plus cuBLAS GEMMs; there is no CPU path.
 """
 
+from .cb_engine import ContinuousBatchingConfig, ContinuousBatchingEngine, ContinuousBatchingStats
 from .config import ContinuousDepthBatchingConfig
 from .engine import (
     CacheFullError,
@@ -19,6 +21,9 @@ from .ouro import OuroForCausalLM, OuroShape, random_ouro_state_dict
 
 __all__ = [
     "CacheFullError",
+    "ContinuousBatchingConfig",
+    "ContinuousBatchingEngine",
+    "ContinuousBatchingStats",
     "ContinuousDepthBatchingConfig",
     "ContinuousDepthBatchingEngine",
     "ContinuousDepthBatchingStats",

@@ -119,6 +119,7 @@ class _Req:
         "idx", "request_id", "prompt", "max_new", "depths", "cursor", "status", "remaining", "chunk",
         "position", "allocated", "generated", "slot", "log_base", "exit_depths", "eos", "stops",
         "created", "start", "finish", "first_token", "token_times", "record_times", "pending_token", "offloaded",
+        "in_flight_tokens",
     )
 
     def __init__(self, idx: int, prompt: list[int], max_new: int, depths: list[int], eos: set[int], stops, rec: bool):
@@ -147,6 +148,7 @@ class _Req:
         self.record_times = rec
         self.pending_token = -1
         self.offloaded = False
+        self.in_flight_tokens = 0  # sampled tokens launched but not yet consumed (CB pipelining)
 
     def next_depth(self) -> int | None:
         if not self.depths:

@@ -249,6 +249,38 @@ def test_early_finish_schedule_matches_reference(name):
     assert [len(o.generated_tokens) for o in outs] == [len(t) for t in run["tokens"]]
 
 
+CB_RUNS = [("cb_async", 0), ("cb_sync", 0), ("cb_async_blocks40", 1), ("cb_sync_blocks48", 2)]
+
+
+@pytest.mark.parametrize("name,preemptions", CB_RUNS)
+def test_cb_schedule_matches_reference(name, preemptions):
+    """The full-depth continuous-batching baseline: its FIFO prefill-or-decode ticks, pipelined
+    (batch k+1 launched before batch k is consumed) and serialized, with the recompute eviction
+    under a short KV pool, equal the reference CB engine's batches and block tables."""
+
+    from continuous_depth_batching_b200 import ContinuousBatchingConfig, ContinuousBatchingEngine
+    from continuous_depth_batching_b200.config import ContinuousDepthBatchingConfig as CDBConfig
+
+    data = _load("ouro_cfg0_cb.json")
+    run = next(r for r in data["runs"] if r["name"] == name)
+    shape = OuroShape(**data["shape"])
+    cfg = CDBConfig(
+        block_size=16, num_blocks=run["num_blocks"], max_recurrent_steps=shape.total_ut_steps,
+        use_async_batching=run["async"], kv_policy="single", max_model_len=2048,
+    ).get_resolved()
+    eng = ContinuousBatchingEngine(None, cfg, _HostRunner(cfg, shape), shape)
+    eng.cb_config = ContinuousBatchingConfig(num_blocks=run["num_blocks"], use_async_batching=run["async"])
+    eng.record_trace = True
+    outs = eng.generate_batch(data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None)
+    assert eng.launch_trace == run["launches"]
+    st, ref = eng.last_stats, run["stats"]
+    assert st.recompute_preemptions == ref["recompute_preemptions"] == preemptions
+    for k in ("prefill_batches", "prefill_requests", "prefill_query_tokens", "decode_batches", "decode_tokens"):
+        assert getattr(st, k) == ref[k], k
+    assert [len(o.generated_tokens) for o in outs] == data["max_new_tokens"]
+    _check_prefill_contents(eng, data["prompts"], outs)
+
+
 def test_single_request_that_cannot_fit_raises():
     """With one active request left and no block for its next token, preemption cannot help: the
     reference raises ``CacheFullError`` (``continuous_api.py:1640-1646``)."""

@@ -365,6 +365,63 @@ def test_kv_offload_logits_on_own_tokens(name):
     assert_report(rep)
 
 
+def _cb_engine(shape, sd, run):
+    from continuous_depth_batching_b200 import ContinuousBatchingConfig, ContinuousBatchingEngine
+
+    model = OuroForCausalLM(shape)
+    model.load_state_dict({k: v.to(torch.float32) for k, v in sd.items()})
+    cfg = ContinuousBatchingConfig(
+        block_size=16, num_blocks=run["num_blocks"], use_async_batching=run["async"], max_model_len=2048,
+    )
+    return ContinuousBatchingEngine.from_model(model, cfg, device="cuda", kv_policy="single")
+
+
+@pytest.mark.parametrize("name", ["cb_async", "cb_sync", "cb_async_blocks40", "cb_sync_blocks48"])
+def test_cb_schedule_matches_reference(name):
+    """The full-depth continuous-batching baseline on the B200 runner: its prefill and decode
+    batches (pipelined and serialized, with recompute eviction in short pools) and block tables
+    equal the reference CB engine's (``tests/golden/ouro_cfg0_cb.json``)."""
+
+    data = json.loads((GOLDEN / "ouro_cfg0_cb.json").read_text())
+    shape = OuroShape(**data["shape"])
+    run = next(r for r in data["runs"] if r["name"] == name)
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+    eng = _cb_engine(shape, sd, run)
+    eng.record_trace = True
+    outs = eng.generate_batch(data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None)
+    assert eng.launch_trace == run["launches"]
+    assert eng.last_stats.recompute_preemptions == run["stats"]["recompute_preemptions"]
+    assert eng.last_stats.decode_batches == run["stats"]["decode_batches"]
+    assert [len(o.generated_tokens) for o in outs] == data["max_new_tokens"]
+
+
+def test_cb_teacher_forced_logits():
+    """Full depth on the B200 kernels (decode = prelude, 4 recurrent launches, coda), through a
+    recompute eviction: teacher-forced on the fp32 CB oracle's tokens, every LM-head launch meets
+    the numerics criteria against the fp32 and bf16 oracles."""
+
+    from oracle.cb_engine import OracleCBEngine
+
+    data = json.loads((GOLDEN / "ouro_cfg0_cb.json").read_text())
+    shape = OuroShape(**data["shape"])
+    run = next(r for r in data["runs"] if r["name"] == "cb_async_blocks40")
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+    ocfg = OracleConfig(block_size=16, num_blocks=run["num_blocks"], max_recurrent_steps=4, max_model_len=2048)
+    o32 = OracleCBEngine(shape, sd, ocfg, torch.float32, async_mode=True)
+    toks = o32.generate(data["prompts"], data["max_new_tokens"])
+    o16 = OracleCBEngine(shape, sd, ocfg, torch.bfloat16, async_mode=True)
+    o16.generate(data["prompts"], data["max_new_tokens"], forced_tokens=toks)
+    eng = _cb_engine(shape, sd, run)
+    eng.record_trace = True
+    eng.keep_logits = True
+    eng.generate_batch(data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, forced_tokens=toks)
+    assert eng.launch_trace == o32.launches == o16.launches
+    assert [k for k, _ in eng.lm_logits] == [k for k, _ in o16.logits] == [k for k, _ in o32.logits]
+    rep = compare_lm_launches([lg for _, lg in eng.lm_logits], [lg for _, lg in o16.logits], [lg for _, lg in o32.logits])
+    print(rep)
+    assert_report(rep)
+
+
 def test_teacher_forced_greedy_tokens_peaked_head():
     """Same criteria with a wide LM head (logit scale ~14 instead of ~1.4)."""
 
