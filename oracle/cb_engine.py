@@ -175,7 +175,9 @@ class OracleCBEngine(OracleEngine):
         toks = torch.argmax(logits, dim=-1).tolist()
         out = []
         for (r, gen_idx), tok in zip(sampled, toks, strict=True):
-            if self.forced is not None:
+            if self.forced is not None and gen_idx < len(self.forced[r.idx]):
+                # (a row past the forced sequence is the extra token of a request whose finish the
+                # pipelined loop has not seen yet; it is dropped when consumed)
                 tok = self.forced[r.idx][gen_idx]
             r.last_sampled = tok
             out.append((r, tok))
@@ -185,14 +187,10 @@ class OracleCBEngine(OracleEngine):
         """``_consume_batch`` (``continuous_api.py:450-489``)."""
 
         for r, tok in results:
+            # a row whose request finished (EOS seen one tick late) or was evicted is dropped
             if r.status in (FINISHED, PENDING):
                 continue
-            r.in_flight_tokens = max(0, r.in_flight_tokens - 1)
-            if len(r.generated) < r.max_new:
-                r.generated.append(tok)
-                r.to_process = [tok]
-            if len(r.generated) >= r.max_new:
-                r.status = FINISHED
+            if self._update(r, tok):
                 self._free(r)
                 self.active.pop(r.idx, None)
                 self.finished[r.idx] = list(r.generated)
@@ -236,9 +234,11 @@ class OracleCBEngine(OracleEngine):
 
     def generate(self, prompts, max_new_tokens, exit_depths=None, forced_tokens=None, eos_token_ids=None,
                  stop_sequences=None) -> list[list[int]]:
-        if exit_depths is not None or eos_token_ids or stop_sequences:
-            raise NotImplementedError("the CB oracle serves full-depth, length-limited requests")
+        if exit_depths is not None:
+            raise NotImplementedError("the CB engine serves every token at full depth")
         cfg = self.cfg
+        self.eos = set(eos_token_ids or [])
+        self.stops = [list(q) for q in (stop_sequences or [])]
         caps = [min(m, cfg.max_model_len - len(p)) for m, p in zip(max_new_tokens, prompts, strict=True)]
         self.free = deque(range(cfg.num_blocks))
         self.tables = {}

@@ -12,7 +12,9 @@ token per decoding request). This script drives it over BASELINE config 0's mode
 and CPU attention restatement of ``make_golden.py``, kv_policy ``single``) and workload in its
 default pipelined mode (``use_async_batching=True``: batch k+1 is scheduled before batch k's
 tokens are consumed) and in its serialized mode, with an ample cache and with KV pools too small for
-the workload (recompute preemption). Every launched batch is recorded in order: its kind, each
+the workload (recompute preemption), and with requests ending early on EOS ids or stop sequences
+(pipelined, the finish is seen one tick late and the extra token computed meanwhile is dropped).
+Every launched batch is recorded in order: its kind, each
 request's (index, cached length, query length, samples-a-token flag) and block-table row, plus
 the logits of the LM-head rows. Output: ``tests/golden/ouro_cfg0_cb.json`` and
 ``ouro_cfg0_cb_logits.npz``.
@@ -74,7 +76,7 @@ class CBRecorder:
         lm_head.forward = lm_forward
 
 
-def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096):
+def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096, eos_token_id=None, stop_sequences=None):
     from looped_cdb.continuous_batching.config import ContinuousBatchingConfig
     from looped_cdb.continuous_batching.continuous_api import ContinuousBatchingEngine
 
@@ -92,12 +94,16 @@ def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096):
     engine = ContinuousBatchingEngine.from_model(model, cfg)
     rec = CBRecorder(engine)
     with torch.no_grad():
-        outs = engine.generate_batch(prompts, max_new_tokens=max_new, eos_token_id=None, warmup=False)
+        outs = engine.generate_batch(
+            prompts, max_new_tokens=max_new, eos_token_id=eos_token_id, stop_sequences=stop_sequences, warmup=False
+        )
     st = engine.last_stats
     result = {
         "name": name,
         "async": async_mode,
         "num_blocks": num_blocks,
+        "eos_token_id": eos_token_id,
+        "stop_sequences": stop_sequences,
         "tokens": [o.generated_tokens for o in outs],
         "stats": {
             "prefill_batches": st.prefill_batches,
@@ -115,13 +121,18 @@ def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096):
 def main() -> None:
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     runs, logits_out = [], {}
-    for name, async_mode, nb in (
-        ("cb_async", True, 4096),
-        ("cb_sync", False, 4096),
-        ("cb_async_blocks40", True, 40),
-        ("cb_sync_blocks48", False, 48),
+    # EOS ids 1009 and 23 and stop sequences [657, 657] and [475, 475] occur mid-generation in the
+    # seeded model's full-depth output, so several requests end early
+    finish = {"eos_token_id": [1009, 23], "stop_sequences": [[657, 657], [475, 475]]}
+    for name, async_mode, nb, kw in (
+        ("cb_async", True, 4096, {}),
+        ("cb_sync", False, 4096, {}),
+        ("cb_async_blocks40", True, 40, {}),
+        ("cb_sync_blocks48", False, 48, {}),
+        ("cb_async_eos_stop", True, 4096, finish),
+        ("cb_sync_eos_stop", False, 4096, finish),
     ):
-        res, logits = run_case(name, async_mode=async_mode, num_blocks=nb)
+        res, logits = run_case(name, async_mode=async_mode, num_blocks=nb, **kw)
         runs.append(res)
         print(name, res["stats"], len(res["launches"]), "launches", flush=True)
         if name == "cb_async":

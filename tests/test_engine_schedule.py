@@ -249,7 +249,14 @@ def test_early_finish_schedule_matches_reference(name):
     assert [len(o.generated_tokens) for o in outs] == [len(t) for t in run["tokens"]]
 
 
-CB_RUNS = [("cb_async", 0), ("cb_sync", 0), ("cb_async_blocks40", 1), ("cb_sync_blocks48", 2)]
+CB_RUNS = [
+    ("cb_async", 0),
+    ("cb_sync", 0),
+    ("cb_async_blocks40", 1),
+    ("cb_sync_blocks48", 2),
+    ("cb_async_eos_stop", 0),
+    ("cb_sync_eos_stop", 0),
+]
 
 
 @pytest.mark.parametrize("name,preemptions", CB_RUNS)
@@ -271,13 +278,17 @@ def test_cb_schedule_matches_reference(name, preemptions):
     eng = ContinuousBatchingEngine(None, cfg, _HostRunner(cfg, shape), shape)
     eng.cb_config = ContinuousBatchingConfig(num_blocks=run["num_blocks"], use_async_batching=run["async"])
     eng.record_trace = True
-    outs = eng.generate_batch(data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None)
+    finish = run["eos_token_id"] is not None
+    outs = eng.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=run["eos_token_id"],
+        stop_sequences=run["stop_sequences"], forced_tokens=run["tokens"] if finish else None,
+    )
     assert eng.launch_trace == run["launches"]
     st, ref = eng.last_stats, run["stats"]
     assert st.recompute_preemptions == ref["recompute_preemptions"] == preemptions
     for k in ("prefill_batches", "prefill_requests", "prefill_query_tokens", "decode_batches", "decode_tokens"):
         assert getattr(st, k) == ref[k], k
-    assert [len(o.generated_tokens) for o in outs] == data["max_new_tokens"]
+    assert [len(o.generated_tokens) for o in outs] == [len(t) for t in run["tokens"]]
     _check_prefill_contents(eng, data["prompts"], outs)
 
 

@@ -376,11 +376,15 @@ def _cb_engine(shape, sd, run):
     return ContinuousBatchingEngine.from_model(model, cfg, device="cuda", kv_policy="single")
 
 
-@pytest.mark.parametrize("name", ["cb_async", "cb_sync", "cb_async_blocks40", "cb_sync_blocks48"])
+@pytest.mark.parametrize(
+    "name", ["cb_async", "cb_sync", "cb_async_blocks40", "cb_sync_blocks48", "cb_async_eos_stop", "cb_sync_eos_stop"]
+)
 def test_cb_schedule_matches_reference(name):
     """The full-depth continuous-batching baseline on the B200 runner: its prefill and decode
-    batches (pipelined and serialized, with recompute eviction in short pools) and block tables
-    equal the reference CB engine's (``tests/golden/ouro_cfg0_cb.json``)."""
+    batches (pipelined and serialized, with recompute eviction in short pools, with early finishes
+    on EOS ids and stop sequences, teacher-forced on the reference's tokens so the finishing tokens
+    are its own) and block tables equal the reference CB engine's
+    (``tests/golden/ouro_cfg0_cb.json``)."""
 
     data = json.loads((GOLDEN / "ouro_cfg0_cb.json").read_text())
     shape = OuroShape(**data["shape"])
@@ -388,11 +392,16 @@ def test_cb_schedule_matches_reference(name):
     sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
     eng = _cb_engine(shape, sd, run)
     eng.record_trace = True
-    outs = eng.generate_batch(data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None)
+    finish = run["eos_token_id"] is not None
+    outs = eng.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=run["eos_token_id"],
+        stop_sequences=run["stop_sequences"], forced_tokens=run["tokens"] if finish else None,
+    )
     assert eng.launch_trace == run["launches"]
     assert eng.last_stats.recompute_preemptions == run["stats"]["recompute_preemptions"]
     assert eng.last_stats.decode_batches == run["stats"]["decode_batches"]
-    assert [len(o.generated_tokens) for o in outs] == data["max_new_tokens"]
+    assert eng.last_stats.decode_tokens == run["stats"]["decode_tokens"]
+    assert [len(o.generated_tokens) for o in outs] == [len(t) for t in run["tokens"]]
 
 
 def test_cb_teacher_forced_logits():

@@ -183,12 +183,21 @@ def test_oracle_reproduces_reference_offload_run(name, counts):
 
 
 @pytest.mark.parametrize(
-    "name,preemptions", [("cb_async", 0), ("cb_sync", 0), ("cb_async_blocks40", 1), ("cb_sync_blocks48", 2)]
+    "name,preemptions",
+    [
+        ("cb_async", 0),
+        ("cb_sync", 0),
+        ("cb_async_blocks40", 1),
+        ("cb_sync_blocks48", 2),
+        ("cb_async_eos_stop", 0),
+        ("cb_sync_eos_stop", 0),
+    ],
 )
 def test_cb_oracle_reproduces_reference_run(name, preemptions):
     """The full-depth continuous-batching baseline (pipelined and serialized, ample and short KV
-    pools): tokens, the ordered prefill/decode batches with their block-table rows, and (pipelined,
-    ample cache) every LM-head launch's logits equal the reference engine's."""
+    pools, early finishes on EOS ids and stop sequences): tokens, the ordered prefill/decode
+    batches with their block-table rows, and (pipelined, ample cache) every LM-head launch's
+    logits equal the reference engine's."""
 
     from oracle.cb_engine import OracleCBEngine
 
@@ -196,13 +205,17 @@ def test_cb_oracle_reproduces_reference_run(name, preemptions):
     run = next(r for r in data["runs"] if r["name"] == name)
     cfg = OracleConfig(block_size=16, num_blocks=run["num_blocks"], max_recurrent_steps=4, max_model_len=2048)
     engine = OracleCBEngine(shape, sd, cfg, torch.float32, async_mode=run["async"])
-    tokens = engine.generate(data["prompts"], data["max_new_tokens"])
+    tokens = engine.generate(
+        data["prompts"], data["max_new_tokens"], eos_token_ids=run["eos_token_id"],
+        stop_sequences=run["stop_sequences"],
+    )
     assert tokens == run["tokens"]
     assert engine.launches == run["launches"]
     st = run["stats"]
     assert engine.stats["recompute_preemptions"] == st["recompute_preemptions"] == preemptions
     assert engine.stats["decode_batches"] == st["decode_batches"]
     assert engine.stats["prefill_batches"] == st["prefill_batches"]
+    assert sum(len(it["items"]) for it in engine.launches if it["kind"] == "decode") == st["decode_tokens"]
     if name == "cb_async":
         logits = np.load(GOLDEN / "ouro_cfg0_cb_logits.npz")
         assert len(engine.logits) == len(logits.files)
