@@ -10,7 +10,9 @@ finish, up to ``max_num_seqs``. With ``use_async_batching`` (the default) the ti
 k+1 before it consumes batch k, so the scheduler sees the resident set and the free blocks one
 tick late, exactly as the reference's pipelined loop does. When nothing fits and nothing is in
 flight, the active request with the fewest cached tokens is soft-reset and re-queued, and
-admission is held until a request finishes (``kv_pressure_mode="recompute"``).
+admission is held until a request finishes (``kv_pressure_mode="recompute"``); under ``"offload"``
+its blocks go to the pinned host pool when they fit and come back, ahead of fresh prompts, at
+the start of a later tick.
 
 The device work is the CDB engine's, on the same runner, graphs and kernels:
 * a prompt batch is one full-depth prefill launch (``OuroRunner.prefill``: tiled prefill
@@ -66,6 +68,8 @@ class ContinuousBatchingStats:
     decode_tokens: int = 0
     generated_tokens: int = 0
     recompute_preemptions: int = 0
+    offload_preemptions: int = 0
+    restores: int = 0
     host_syncs: int = 0
     kv_peak_blocks: int = 0
 
@@ -105,8 +109,6 @@ class ContinuousBatchingEngine(ContinuousDepthBatchingEngine):
         is what the reference's paged cache assumes for a model that does not name one
         (``continuous_batching/cache.py:160-163``)."""
 
-        if cb_config.kv_pressure_mode == "offload":
-            raise NotImplementedError("the B200 CB baseline preempts by recompute; kv_pressure_mode='offload' is CDB-only")
         config = getattr(model, "config", None)
         steps = getattr(config, "total_ut_steps", None) or getattr(config, "mean_recurrence", None)
         if steps is None:
@@ -128,6 +130,7 @@ class ContinuousBatchingEngine(ContinuousDepthBatchingEngine):
             min_free_slots=cb_config.min_free_slots,
             kv_policy=policy,
             kv_pressure_mode=cb_config.kv_pressure_mode,
+            cpu_offload_space=cb_config.cpu_offload_space,
         )
         eng = super().from_model(
             model, cdb, dtype=dtype, device=device, gemm_backend=gemm_backend, fused_lm_head=fused_lm_head
@@ -232,7 +235,8 @@ class ContinuousBatchingEngine(ContinuousDepthBatchingEngine):
 
         prefilling = [r for r in self.active.values() if r.status == RequestStatus.PREFILLING]
         free_res = max(0, self.max_num_seqs - len(self.active))
-        admissible = [] if self.block_new else list(self.waiting.values())[:free_res]
+        fresh = [r for r in self.waiting.values() if not r.offloaded]  # offloaded ones return by restore
+        admissible = [] if self.block_new else fresh[:free_res]
         if self.cdb_config.kv_pressure_mode == "reserve":
             committed = sum(self._reserved_peak(r) for r in self.active.values())
             kept = []
@@ -311,6 +315,8 @@ class ContinuousBatchingEngine(ContinuousDepthBatchingEngine):
         """``FIFOScheduler.schedule_batch`` (``scheduler.py:82-141``): ``(entries, cache_exhausted)``."""
 
         cfg = self.cdb_config
+        # offloaded requests come back first, into new blocks with their KV (``scheduler.py:97-100``)
+        self._restore_offloaded()
         decode = [r for r in self.active.values() if r.status == RequestStatus.DECODING and not self._will_finish(r)]
         prefill = self._cb_prefill_candidates()
         if prefill and (not decode or self.pool.num_free > self.safety * cfg.num_blocks):
@@ -421,28 +427,37 @@ class ContinuousBatchingEngine(ContinuousDepthBatchingEngine):
                 self._retire(r)
 
     def _evict(self) -> None:
-        """``offload_one_request`` with the recompute soft reset (``offloading_manager.py:165-214``,
-        ``requests.py:290-315``): the active request with the fewest cached tokens (ties: the latest
-        admitted) gives up its KV and re-queues as prompt + generated tokens."""
+        """``offload_one_request`` (``offloading_manager.py:165-214``): the active request with the
+        fewest cached tokens (ties: the latest admitted) gives up its KV. Under ``offload`` its blocks
+        are copied to the host pool if they fit there, and it waits with its status, position and
+        pending token until it is restored. Otherwise it is soft-reset (``requests.py:290-315``) and
+        re-queued as prompt + generated tokens."""
 
         victim = min(reversed(list(self.active)), key=lambda i: self.active[i].position)
         r = self.active.pop(victim)
-        if self._forced is None:
-            self.last_stats.host_syncs += 1
-            self.runner.stream.synchronize()
-        generated = self._host_tokens(r)
+        offloaded = self._offload(r)
+        if not offloaded:
+            if self._forced is None:
+                self.last_stats.host_syncs += 1
+                self.runner.stream.synchronize()
+            generated = self._host_tokens(r)
         self.pool.release(r.idx)
         self.free_slots.append(r.slot)
         r.slot = -1
-        r.remaining = list(r.prompt) + generated
-        r.chunk = []
-        r.position = 0
         r.allocated = 0
-        r.in_flight_tokens = 0
-        r.status = RequestStatus.PENDING
+        r.chunk = []
+        if offloaded:
+            if r.status == RequestStatus.DECODING:
+                r.remaining = []
+            self.last_stats.offload_preemptions += 1
+        else:
+            r.remaining = list(r.prompt) + generated
+            r.position = 0
+            r.in_flight_tokens = 0
+            r.status = RequestStatus.PENDING
+            self.last_stats.recompute_preemptions += 1
         self.waiting[r.idx] = r
         self.block_new = True
-        self.last_stats.recompute_preemptions += 1
 
     def _tick(self, in_flight):
         """``_execute_tick`` (``continuous_api.py:306-448``)."""

@@ -620,7 +620,8 @@ class ContinuousDepthBatchingEngine:
             host = self.host_tables.pop(r.idx)
             self.runner.pool.host_copy(self.pool.tables[r.idx][: len(host)], host, False, self.runner.stream)
             self.host_free.extend(host)
-            self.runner.rebind_token(r.slot, r.log_base + r.generated - 1)
+            if r.generated:  # a request offloaded mid-prompt has no sampled token to carry
+                self.runner.rebind_token(r.slot, r.log_base + r.generated - 1)
             r.offloaded = False
             self.last_stats.restores += 1
         return admitted

@@ -56,7 +56,8 @@ class OracleCBEngine(OracleEngine):
 
         prefilling = [r for r in self.active.values() if r.status == PREFILLING]
         free_slots = max(0, self.max_num_seqs - len(self.active))
-        admissible = [] if self.block_new else list(self.waiting.values())[:free_slots]
+        fresh = [r for r in self.waiting.values() if not r.offloaded]
+        admissible = [] if self.block_new else fresh[:free_slots]
         if self.cfg.kv_pressure_mode == "reserve":
             committed = sum(self._reserved_peak(r) for r in self.active.values())
             kept = []
@@ -128,6 +129,8 @@ class OracleCBEngine(OracleEngine):
     def _schedule_batch(self):
         """``FIFOScheduler.schedule_batch`` (``scheduler.py:82-141``): ``(entries, cache_exhausted)``."""
 
+        # offloaded requests come back first, with their KV (``scheduler.py:97-100``)
+        self._restore_offloaded()
         decode = [r for r in self.active.values() if r.status == DECODING and not self._will_finish(r)]
         prefill = self._cb_prefill_candidates()
         if prefill and (not decode or len(self.free) > self.safety * self.cfg.num_blocks):
@@ -197,20 +200,28 @@ class OracleCBEngine(OracleEngine):
                 self.block_new = False
 
     def _evict(self) -> None:
-        """``offload_one_request`` with the recompute soft reset (``offloading_manager.py:165-214``)."""
+        """``offload_one_request`` (``offloading_manager.py:165-214``): the victim's blocks go to the
+        host pool when they fit (``offload`` mode; it keeps its status, position and pending token),
+        otherwise it is soft-reset to prompt + generated tokens."""
 
         victim = min(reversed(list(self.active)), key=lambda i: self.active[i].position)
         r = self.active.pop(victim)
+        offloaded = self._offload(r)
         self._free(r)
-        r.remaining = list(r.prompt) + list(r.generated)
-        r.to_process = []
-        r.position = 0
         r.allocated = 0
-        r.in_flight_tokens = 0
-        r.status = PENDING
+        if offloaded:
+            if r.status == DECODING:
+                r.remaining = []
+            self.stats["offload_preemptions"] += 1
+        else:
+            r.remaining = list(r.prompt) + list(r.generated)
+            r.to_process = []
+            r.position = 0
+            r.in_flight_tokens = 0
+            r.status = PENDING
+            self.stats["recompute_preemptions"] += 1
         self.waiting[r.idx] = r
         self.block_new = True
-        self.stats["recompute_preemptions"] += 1
 
     def _tick(self, in_flight):
         entries, cache_full = ([], False)
@@ -251,6 +262,8 @@ class OracleCBEngine(OracleEngine):
         self.launches: list[dict] = []
         self.logits: list[tuple[str, torch.Tensor]] = []
         self.stats = Counter()
+        self.cpu_free = deque(range(cfg.num_cpu_blocks))
+        self.host_store = {}
         self.forced = forced_tokens
         for i, (p, m) in enumerate(zip(prompts, caps, strict=True)):
             r = Req(idx=i, prompt=list(p), max_new=m, depths=[])

@@ -13,7 +13,9 @@ and CPU attention restatement of ``make_golden.py``, kv_policy ``single``) and w
 default pipelined mode (``use_async_batching=True``: batch k+1 is scheduled before batch k's
 tokens are consumed) and in its serialized mode, with an ample cache and with KV pools too small for
 the workload (recompute preemption), and with requests ending early on EOS ids or stop sequences
-(pipelined, the finish is seen one tick late and the extra token computed meanwhile is dropped).
+(pipelined, the finish is seen one tick late and the extra token computed meanwhile is dropped),
+and under ``kv_pressure_mode="offload"`` with host pools of 64, 3 and 2 blocks (a victim's blocks go to
+the host pool when they fit there and come back before it is scheduled again; otherwise recompute).
 Every launched batch is recorded in order: its kind, each
 request's (index, cached length, query length, samples-a-token flag) and block-table row, plus
 the logits of the LM-head rows. Output: ``tests/golden/ouro_cfg0_cb.json`` and
@@ -76,7 +78,8 @@ class CBRecorder:
         lm_head.forward = lm_forward
 
 
-def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096, eos_token_id=None, stop_sequences=None):
+def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096, eos_token_id=None, stop_sequences=None,
+             host_blocks: int = 0):
     from looped_cdb.continuous_batching.config import ContinuousBatchingConfig
     from looped_cdb.continuous_batching.continuous_api import ContinuousBatchingEngine
 
@@ -88,7 +91,10 @@ def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096, eos_token_i
         use_async_batching=async_mode,
         use_cuda_graph=False,
         use_cuda_graph_prefill=False,
-        kv_pressure_mode="recompute",
+        kv_pressure_mode="offload" if host_blocks else "recompute",
+        # host pool of `host_blocks` blocks: one block is every cache layer's K and V rows, fp32 here
+        cpu_offload_space=host_blocks * 2 * mg.CFG0.num_hidden_layers * 16 * mg.CFG0.num_key_value_heads
+        * mg.CFG0.head_dim * 4 / 1024**3 if host_blocks else None,
         max_model_len=2048,
     )
     engine = ContinuousBatchingEngine.from_model(model, cfg)
@@ -102,6 +108,7 @@ def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096, eos_token_i
         "name": name,
         "async": async_mode,
         "num_blocks": num_blocks,
+        "num_cpu_blocks": host_blocks,
         "eos_token_id": eos_token_id,
         "stop_sequences": stop_sequences,
         "tokens": [o.generated_tokens for o in outs],
@@ -112,6 +119,9 @@ def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096, eos_token_i
             "decode_batches": st.decode_batches,
             "decode_tokens": st.decode_tokens,
             "recompute_preemptions": engine.offloading_manager.num_recompute_preemptions,
+            "offload_preemptions": engine.offloading_manager.num_offload_preemptions,
+            "restores": engine.offloading_manager.num_restores,
+            "num_cpu_blocks": engine.offloading_manager._num_cpu_blocks,
         },
         "launches": rec.launches,
     }
@@ -131,6 +141,9 @@ def main() -> None:
         ("cb_sync_blocks48", False, 48, {}),
         ("cb_async_eos_stop", True, 4096, finish),
         ("cb_sync_eos_stop", False, 4096, finish),
+        ("cb_async_blocks40_host64", True, 40, {"host_blocks": 64}),
+        ("cb_sync_blocks48_host2", False, 48, {"host_blocks": 2}),
+        ("cb_async_blocks36_host3", True, 36, {"host_blocks": 3}),
     ):
         res, logits = run_case(name, async_mode=async_mode, num_blocks=nb, **kw)
         runs.append(res)

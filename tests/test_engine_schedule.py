@@ -256,6 +256,9 @@ CB_RUNS = [
     ("cb_sync_blocks48", 2),
     ("cb_async_eos_stop", 0),
     ("cb_sync_eos_stop", 0),
+    ("cb_async_blocks40_host64", 0),
+    ("cb_sync_blocks48_host2", 1),
+    ("cb_async_blocks36_host3", 0),
 ]
 
 
@@ -271,11 +274,15 @@ def test_cb_schedule_matches_reference(name, preemptions):
     data = _load("ouro_cfg0_cb.json")
     run = next(r for r in data["runs"] if r["name"] == name)
     shape = OuroShape(**data["shape"])
+    host = run.get("num_cpu_blocks") or 0
     cfg = CDBConfig(
         block_size=16, num_blocks=run["num_blocks"], max_recurrent_steps=shape.total_ut_steps,
         use_async_batching=run["async"], kv_policy="single", max_model_len=2048,
+        kv_pressure_mode="offload" if host else "recompute", cpu_offload_space=1.0 if host else None,
     ).get_resolved()
-    eng = ContinuousBatchingEngine(None, cfg, _HostRunner(cfg, shape), shape)
+    runner = _HostRunner(cfg, shape)
+    runner.pool.num_host_blocks = host
+    eng = ContinuousBatchingEngine(None, cfg, runner, shape)
     eng.cb_config = ContinuousBatchingConfig(num_blocks=run["num_blocks"], use_async_batching=run["async"])
     eng.record_trace = True
     finish = run["eos_token_id"] is not None
@@ -288,6 +295,9 @@ def test_cb_schedule_matches_reference(name, preemptions):
     assert st.recompute_preemptions == ref["recompute_preemptions"] == preemptions
     for k in ("prefill_batches", "prefill_requests", "prefill_query_tokens", "decode_batches", "decode_tokens"):
         assert getattr(st, k) == ref[k], k
+    if host:
+        assert (st.offload_preemptions, st.restores) == (ref["offload_preemptions"], ref["restores"])
+        assert not eng.host_tables and len(eng.host_free) == host
     assert [len(o.generated_tokens) for o in outs] == [len(t) for t in run["tokens"]]
     _check_prefill_contents(eng, data["prompts"], outs)
 

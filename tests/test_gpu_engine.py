@@ -370,14 +370,22 @@ def _cb_engine(shape, sd, run):
 
     model = OuroForCausalLM(shape)
     model.load_state_dict({k: v.to(torch.float32) for k, v in sd.items()})
+    host = run.get("num_cpu_blocks") or 0
     cfg = ContinuousBatchingConfig(
         block_size=16, num_blocks=run["num_blocks"], use_async_batching=run["async"], max_model_len=2048,
+        kv_pressure_mode="offload" if host else "recompute", cpu_offload_space=_host_space(shape, host),
     )
-    return ContinuousBatchingEngine.from_model(model, cfg, device="cuda", kv_policy="single")
+    eng = ContinuousBatchingEngine.from_model(model, cfg, device="cuda", kv_policy="single")
+    assert eng.runner.pool.num_host_blocks == host
+    return eng
 
 
 @pytest.mark.parametrize(
-    "name", ["cb_async", "cb_sync", "cb_async_blocks40", "cb_sync_blocks48", "cb_async_eos_stop", "cb_sync_eos_stop"]
+    "name",
+    [
+        "cb_async", "cb_sync", "cb_async_blocks40", "cb_sync_blocks48", "cb_async_eos_stop", "cb_sync_eos_stop",
+        "cb_async_blocks40_host64", "cb_sync_blocks48_host2", "cb_async_blocks36_host3",
+    ],
 )
 def test_cb_schedule_matches_reference(name):
     """The full-depth continuous-batching baseline on the B200 runner: its prefill and decode
@@ -401,7 +409,41 @@ def test_cb_schedule_matches_reference(name):
     assert eng.last_stats.recompute_preemptions == run["stats"]["recompute_preemptions"]
     assert eng.last_stats.decode_batches == run["stats"]["decode_batches"]
     assert eng.last_stats.decode_tokens == run["stats"]["decode_tokens"]
+    if run.get("num_cpu_blocks"):
+        assert eng.last_stats.offload_preemptions == run["stats"]["offload_preemptions"]
+        assert eng.last_stats.restores == run["stats"]["restores"]
     assert [len(o.generated_tokens) for o in outs] == [len(t) for t in run["tokens"]]
+
+
+def test_cb_offload_logits_on_own_tokens():
+    """CB with two offloads and restores (host pool of 3 blocks): the engine runs on its own tokens,
+    the fp32 and bf16 CB oracles are forced onto them, and every LM-head launch meets the numerics
+    criteria. KV or a pending token that came back wrong from the host pool would miss by far."""
+
+    from oracle.cb_engine import OracleCBEngine
+
+    data = json.loads((GOLDEN / "ouro_cfg0_cb.json").read_text())
+    shape = OuroShape(**data["shape"])
+    run = next(r for r in data["runs"] if r["name"] == "cb_async_blocks36_host3")
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+    eng = _cb_engine(shape, sd, run)
+    eng.record_trace = True
+    eng.keep_logits = True
+    outs = eng.generate_batch(data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None)
+    assert eng.last_stats.restores == 2
+    toks = [o.generated_tokens for o in outs]
+    ocfg = OracleConfig(
+        block_size=16, num_blocks=run["num_blocks"], max_recurrent_steps=4, max_model_len=2048,
+        kv_pressure_mode="offload", num_cpu_blocks=run["num_cpu_blocks"],
+    )
+    o32 = OracleCBEngine(shape, sd, ocfg, torch.float32, async_mode=True)
+    o32.generate(data["prompts"], data["max_new_tokens"], forced_tokens=toks)
+    o16 = OracleCBEngine(shape, sd, ocfg, torch.bfloat16, async_mode=True)
+    o16.generate(data["prompts"], data["max_new_tokens"], forced_tokens=toks)
+    assert eng.launch_trace == o32.launches == o16.launches
+    rep = compare_lm_launches([lg for _, lg in eng.lm_logits], [lg for _, lg in o16.logits], [lg for _, lg in o32.logits])
+    print(rep)
+    assert_report(rep)
 
 
 def test_cb_teacher_forced_logits():

@@ -191,6 +191,9 @@ def test_oracle_reproduces_reference_offload_run(name, counts):
         ("cb_sync_blocks48", 2),
         ("cb_async_eos_stop", 0),
         ("cb_sync_eos_stop", 0),
+        ("cb_async_blocks40_host64", 0),
+        ("cb_sync_blocks48_host2", 1),
+        ("cb_async_blocks36_host3", 0),
     ],
 )
 def test_cb_oracle_reproduces_reference_run(name, preemptions):
@@ -203,7 +206,11 @@ def test_cb_oracle_reproduces_reference_run(name, preemptions):
 
     data, shape, sd = _load_ouro("ouro_cfg0_cb.json")
     run = next(r for r in data["runs"] if r["name"] == name)
-    cfg = OracleConfig(block_size=16, num_blocks=run["num_blocks"], max_recurrent_steps=4, max_model_len=2048)
+    host = run.get("num_cpu_blocks") or 0
+    cfg = OracleConfig(
+        block_size=16, num_blocks=run["num_blocks"], max_recurrent_steps=4, max_model_len=2048,
+        kv_pressure_mode="offload" if host else "recompute", num_cpu_blocks=host,
+    )
     engine = OracleCBEngine(shape, sd, cfg, torch.float32, async_mode=run["async"])
     tokens = engine.generate(
         data["prompts"], data["max_new_tokens"], eos_token_ids=run["eos_token_id"],
@@ -216,6 +223,10 @@ def test_cb_oracle_reproduces_reference_run(name, preemptions):
     assert engine.stats["decode_batches"] == st["decode_batches"]
     assert engine.stats["prefill_batches"] == st["prefill_batches"]
     assert sum(len(it["items"]) for it in engine.launches if it["kind"] == "decode") == st["decode_tokens"]
+    if host:
+        assert (engine.stats["offload_preemptions"], engine.stats["restores"]) == (
+            st["offload_preemptions"], st["restores"]
+        )
     if name == "cb_async":
         logits = np.load(GOLDEN / "ouro_cfg0_cb_logits.npz")
         assert len(engine.logits) == len(logits.files)
