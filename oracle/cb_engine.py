@@ -16,8 +16,9 @@ with the fewest cached tokens (ties: the latest) is soft-reset and re-queued
 (``pop_request_to_evict`` ``scheduler_base.py:406-414``), and admission is held until a request
 finishes.
 
-A batch runs the whole model over its query rows (:meth:`OuroOracle.prefill`: every recurrent
-step, each with its KV slot, then the LM head on the rows that sample). A decode batch is the same
+A batch runs the whole model over its query rows (:meth:`OuroOracle.prefill` /
+:meth:`HuginnOracle.prefill`: every recurrent step, each with its KV slot, then the LM head on the
+rows that sample). A decode batch is the same
 computation with one row per request. Launches are recorded as
 ``{"kind": "prefill" | "decode", "items": [[req, past, q_len, has_new], ...], "blocks": [...]}``.
 """
@@ -28,20 +29,20 @@ from collections import Counter, OrderedDict, deque
 
 import torch
 
+from continuous_depth_batching_b200.huginn import HuginnShape
 from continuous_depth_batching_b200.ouro import OuroShape
 
 from .engine import DECODING, FINISHED, PENDING, PREFILLING, OracleConfig, OracleEngine, Req, slot_for_step
+from .huginn_math import HuginnOracle
 from .ouro_math import OracleKVCache, OuroOracle
 
 
 class OracleCBEngine(OracleEngine):
-    """The reference CB engine on CPU over :class:`OuroOracle` math (Ouro family)."""
+    """The reference CB engine on CPU over :class:`OuroOracle` or :class:`HuginnOracle` math."""
 
-    def __init__(self, shape: OuroShape, state_dict: dict, cfg: OracleConfig, dtype: torch.dtype = torch.float32,
-                 async_mode: bool = True):
+    def __init__(self, shape: OuroShape | HuginnShape, state_dict: dict, cfg: OracleConfig,
+                 dtype: torch.dtype = torch.float32, async_mode: bool = True):
         super().__init__(shape, state_dict, cfg, dtype)
-        if self.huginn:
-            raise NotImplementedError("the CB oracle restates the Ouro family")
         self.async_mode = async_mode
 
     # ------------------------------------------------------------------ scheduling
@@ -254,7 +255,10 @@ class OracleCBEngine(OracleEngine):
         self.free = deque(range(cfg.num_blocks))
         self.tables = {}
         self.cache = OracleKVCache(self.shape, self.num_cache_layers, cfg.num_blocks, cfg.block_size, self.dtype)
-        self.model = OuroOracle(self.weights, self.cache)
+        if self.huginn:
+            self.model = HuginnOracle(self.weights, self.cache, self.slots)
+        else:
+            self.model = OuroOracle(self.weights, self.cache)
         self.waiting: OrderedDict[int, Req] = OrderedDict()
         self.active: OrderedDict[int, Req] = OrderedDict()
         self.block_new = False

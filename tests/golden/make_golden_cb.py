@@ -128,6 +128,55 @@ def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096, eos_token_i
     return result, rec.logits
 
 
+def huginn_main() -> None:
+    """``--huginn``: the small Huginn shape of ``make_golden_huginn.py`` (prelude, recurrent core and
+    coda with their own cache layers; 6 recurrent steps; the model names no KV layout, so the
+    reference cache gives every step its own slot) through the reference CB engine, pipelined and
+    serialized, into ``huginn_small_cb.json``."""
+
+    import make_golden_huginn as mh
+
+    from looped_cdb.continuous_batching.config import ContinuousBatchingConfig
+    from looped_cdb.continuous_batching.continuous_api import ContinuousBatchingEngine
+
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    runs = []
+    for name, async_mode in (("cb_async", True), ("cb_sync", False)):
+        model = mh.build_reference_model(mh.SMALL)
+        prompts, max_new = mh.config0_workload()
+        cfg = ContinuousBatchingConfig(
+            block_size=16, num_blocks=4096, use_async_batching=async_mode, use_cuda_graph=False,
+            use_cuda_graph_prefill=False, kv_pressure_mode="recompute", max_model_len=2048,
+        )
+        engine = ContinuousBatchingEngine.from_model(model, cfg)
+        rec = CBRecorder(engine)
+        with torch.no_grad():
+            outs = engine.generate_batch(prompts, max_new_tokens=max_new, eos_token_id=None, warmup=False)
+        st = engine.last_stats
+        runs.append({
+            "name": name, "async": async_mode, "num_blocks": 4096, "num_cpu_blocks": 0, "eos_token_id": None,
+            "stop_sequences": None, "kv_policy": engine.cache.kv_policy,
+            "tokens": [o.generated_tokens for o in outs],
+            "stats": {"prefill_batches": st.prefill_batches, "prefill_requests": st.prefill_requests,
+                      "prefill_query_tokens": st.prefill_query_tokens, "decode_batches": st.decode_batches,
+                      "decode_tokens": st.decode_tokens, "recompute_preemptions": 0},
+            "launches": rec.launches,
+        })
+        print(name, runs[-1]["kv_policy"], runs[-1]["stats"], flush=True)
+    prompts, max_new = mh.config0_workload()
+    payload = {
+        "generator": "tests/golden/make_golden_cb.py --huginn",
+        "shape": mh.SMALL.__dict__,
+        "embed_std": mh.EMBED_STD,
+        "weights_seed": 0,
+        "prompts": prompts,
+        "max_new_tokens": max_new,
+        "block_size": 16,
+        "runs": runs,
+    }
+    (HERE / "huginn_small_cb.json").write_text(json.dumps(payload, separators=(",", ":")))
+
+
 def main() -> None:
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     runs, logits_out = [], {}
@@ -167,4 +216,7 @@ def main() -> None:
 
 
 if __name__ == "__main__":
-    main()
+    if "--huginn" in sys.argv[1:]:
+        huginn_main()
+    else:
+        main()

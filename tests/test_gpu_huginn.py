@@ -188,3 +188,40 @@ def test_huginn_async_live_gate_matches_reference_decisions(name, refill):
     agree = exit_agreement(outs, run)
     print({"run": name, "exit_agreement": agree})
     assert agree >= 0.95
+
+
+@pytest.mark.parametrize("async_mode", [True, False])
+def test_huginn_cb_baseline_matches_reference_and_oracle(async_mode):
+    """The full-depth CB baseline on a Huginn model (prelude, 6 core steps and coda per decode
+    batch, every step on its own KV slot as the reference cache lays a Huginn model out): batches
+    and block tables equal the reference CB engine's (``tests/golden/huginn_small_cb.json``), and
+    teacher-forced on the fp32 CB oracle's tokens every LM-head launch meets the numerics criteria."""
+
+    from continuous_depth_batching_b200 import ContinuousBatchingConfig, ContinuousBatchingEngine
+    from oracle.cb_engine import OracleCBEngine
+
+    data = json.loads((GOLDEN / "huginn_small_cb.json").read_text())
+    shape = HuginnShape(**data["shape"])
+    run = next(r for r in data["runs"] if r["async"] == async_mode)
+    sd = random_huginn_state_dict(shape, seed=0, embed_std=data["embed_std"])
+    ocfg = OracleConfig(
+        block_size=16, num_blocks=4096, max_recurrent_steps=shape.total_recurrent_steps, max_model_len=2048,
+        kv_policy=run["kv_policy"],
+    )
+    o32 = OracleCBEngine(shape, sd, ocfg, torch.float32, async_mode=async_mode)
+    toks = o32.generate(data["prompts"], data["max_new_tokens"])
+    assert toks == run["tokens"]
+    o16 = OracleCBEngine(shape, sd, ocfg, torch.bfloat16, async_mode=async_mode)
+    o16.generate(data["prompts"], data["max_new_tokens"], forced_tokens=toks)
+    model = HuginnForCausalLM(shape)
+    model.load_state_dict({k: v.to(torch.float32) for k, v in sd.items()})
+    cfg = ContinuousBatchingConfig(block_size=16, num_blocks=4096, use_async_batching=async_mode, max_model_len=2048)
+    eng = ContinuousBatchingEngine.from_model(model, cfg, device="cuda")
+    assert eng.cdb_config.kv_policy == run["kv_policy"]
+    eng.record_trace = True
+    eng.keep_logits = True
+    eng.generate_batch(data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, forced_tokens=toks)
+    assert eng.launch_trace == run["launches"] == o32.launches == o16.launches
+    rep = compare_lm_launches([lg for _, lg in eng.lm_logits], [lg for _, lg in o16.logits], [lg for _, lg in o32.logits])
+    print(rep)
+    assert_report(rep)

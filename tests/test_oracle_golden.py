@@ -18,6 +18,7 @@ import numpy as np
 import pytest
 import torch
 
+from continuous_depth_batching_b200.huginn import HuginnShape, random_huginn_state_dict
 from continuous_depth_batching_b200.ouro import OuroShape, random_ouro_state_dict
 from oracle.engine import OracleConfig, OracleEngine, exit_depth_histogram
 
@@ -232,6 +233,27 @@ def test_cb_oracle_reproduces_reference_run(name, preemptions):
         assert len(engine.logits) == len(logits.files)
         for i, (_kind, lg) in enumerate(engine.logits):
             np.testing.assert_allclose(lg.numpy(), logits[f"{name}_{i}"], rtol=0, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", ["cb_async", "cb_sync"])
+def test_cb_oracle_reproduces_reference_huginn_run(name):
+    """The CB baseline on the small Huginn shape (every recurrent step on its own KV slot, as the
+    reference cache lays out a model that names no layout): tokens and batches equal the
+    reference's."""
+
+    from oracle.cb_engine import OracleCBEngine
+
+    data = json.loads((GOLDEN / "huginn_small_cb.json").read_text())
+    shape = HuginnShape(**data["shape"])
+    sd = random_huginn_state_dict(shape, seed=data["weights_seed"], embed_std=data["embed_std"])
+    run = next(r for r in data["runs"] if r["name"] == name)
+    cfg = OracleConfig(
+        block_size=16, num_blocks=run["num_blocks"], max_recurrent_steps=shape.total_recurrent_steps,
+        max_model_len=2048, kv_policy=run["kv_policy"],
+    )
+    engine = OracleCBEngine(shape, sd, cfg, torch.float32, async_mode=run["async"])
+    assert engine.generate(data["prompts"], data["max_new_tokens"]) == run["tokens"]
+    assert engine.launches == run["launches"]
 
 
 @pytest.mark.parametrize("name", ["live_gate_refill", "replay_refill", "replay_norefill", "replay_last_exited"])
