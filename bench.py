@@ -410,6 +410,7 @@ def run_b200(args) -> None:
                 "definition": "generated tokens / (device time minus prefill launch time), max over ranks",
             },
             "gpu_launches": kernel_launches,
+            "flop_bound": flop_bound_summary(shape, stats),
             "roofline": roof,
             "step_roofline": whole,
             "clocks": clocks.summary(),
@@ -420,6 +421,27 @@ def run_b200(args) -> None:
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+
+
+def flop_bound_summary(shape, stats) -> dict:
+    """The eq. (1) FLOP bound on the speed-up of this run's exit schedule over full depth
+    (``continuous_depth_batching_b200.flop_bound``), from the model's stage weights (counted on a
+    ``meta``-device model) and the mean recurrent steps per decoded token of the last step."""
+
+    from continuous_depth_batching_b200 import OuroForCausalLM
+    from continuous_depth_batching_b200.flop_bound import stage_flops
+
+    with torch.device("meta"):
+        f = stage_flops(OuroForCausalLM(shape))
+    mean_depth = stats.recurrent_steps / stats.coda_tokens if stats.coda_tokens else float(shape.total_ut_steps)
+    return {
+        **f.to_json_dict(),
+        "f0_over_fr": round(f.f0_over_fr, 4),
+        "mean_recurrent_steps": round(mean_depth, 4),
+        "max_depth": shape.total_ut_steps,
+        "ideal_speedup_vs_full_depth": round(f.ideal_speedup(max_depth=shape.total_ut_steps, mean_depth=mean_depth), 4),
+        "note": "compare with this line's value over `bench.py --engine cb` (same kernels, every token at full depth)",
+    }
 
 
 def cpu_sample_workload():
