@@ -164,7 +164,7 @@ class Recorder:
 
 def run_case(
     name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_depths=None, num_blocks=4096, async_mode=False,
-    eos_token_id=None, stop_sequences=None, pressure_mode=None, cpu_offload_space=None,
+    eos_token_id=None, stop_sequences=None, pressure_mode=None, cpu_offload_space=None, max_model_len=2048,
 ):
     from looped_cdb.continuous_depth_batching import ContinuousDepthBatchingConfig, ContinuousDepthBatchingEngine
 
@@ -183,7 +183,7 @@ def run_case(
         kv_policy=kv_policy,
         kv_pressure_mode=pressure_mode or ("reserve" if kv_policy == "last_exited" else "recompute"),
         cpu_offload_space=cpu_offload_space,
-        max_model_len=2048,
+        max_model_len=max_model_len,
     )
     engine = ContinuousDepthBatchingEngine.from_model(model, cfg)
     rec = Recorder(engine)
@@ -284,7 +284,8 @@ def pressure_main() -> None:
     """``--pressure``: the replayed schedules (synchronous) in KV pools too small for the workload,
     under the default ``kv_pressure_mode="recompute"``: refill at 56 blocks (decoders stall and are
     restaged), 48 and 40 blocks (stalled decoders are preempted by soft reset and re-prefilled), and
-    no-refill at 48 and 40 blocks, into ``ouro_cfg0_pressure.json``."""
+    no-refill at 48 and 40 blocks; then both loops at 40 blocks under ``"reserve"`` admission
+    (``max_model_len`` 512), into ``ouro_cfg0_pressure.json``."""
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     gold = json.loads((HERE / "ouro_cfg0.json").read_text())
@@ -299,6 +300,16 @@ def pressure_main() -> None:
             )
             res["num_blocks"] = nb
             runs.append(res)
+        # reserve admission: each admitted request commits its worst-case blocks up front, so
+        # nothing is ever preempted (max_model_len 512 keeps a max-length request within 40 blocks)
+        res, _ = run_case(
+            f"replay_{tag}_reserve_blocks40", kv_policy="single", refill=refill, live_gate=False, exit_depths=depths,
+            num_blocks=40, pressure_mode="reserve", max_model_len=512,
+        )
+        res["num_blocks"] = 40
+        res["kv_pressure_mode"] = "reserve"
+        res["max_model_len"] = 512
+        runs.append(res)
     prompts, max_new = config0_workload()
     payload = {
         "generator": "tests/golden/make_golden.py --pressure",

@@ -15,7 +15,8 @@ tokens are consumed) and in its serialized mode, with an ample cache and with KV
 the workload (recompute preemption), and with requests ending early on EOS ids or stop sequences
 (pipelined, the finish is seen one tick late and the extra token computed meanwhile is dropped),
 and under ``kv_pressure_mode="offload"`` with host pools of 64, 3 and 2 blocks (a victim's blocks go to
-the host pool when they fit there and come back before it is scheduled again; otherwise recompute).
+the host pool when they fit there and come back before it is scheduled again; otherwise recompute),
+and under ``"reserve"`` admission at 40 blocks (``max_model_len`` 512).
 Every launched batch is recorded in order: its kind, each
 request's (index, cached length, query length, samples-a-token flag) and block-table row, plus
 the logits of the LM-head rows. Output: ``tests/golden/ouro_cfg0_cb.json`` and
@@ -79,7 +80,7 @@ class CBRecorder:
 
 
 def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096, eos_token_id=None, stop_sequences=None,
-             host_blocks: int = 0):
+             host_blocks: int = 0, reserve: bool = False):
     from looped_cdb.continuous_batching.config import ContinuousBatchingConfig
     from looped_cdb.continuous_batching.continuous_api import ContinuousBatchingEngine
 
@@ -91,11 +92,11 @@ def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096, eos_token_i
         use_async_batching=async_mode,
         use_cuda_graph=False,
         use_cuda_graph_prefill=False,
-        kv_pressure_mode="offload" if host_blocks else "recompute",
+        kv_pressure_mode="offload" if host_blocks else ("reserve" if reserve else "recompute"),
         # host pool of `host_blocks` blocks: one block is every cache layer's K and V rows, fp32 here
         cpu_offload_space=host_blocks * 2 * mg.CFG0.num_hidden_layers * 16 * mg.CFG0.num_key_value_heads
         * mg.CFG0.head_dim * 4 / 1024**3 if host_blocks else None,
-        max_model_len=2048,
+        max_model_len=512 if reserve else 2048,
     )
     engine = ContinuousBatchingEngine.from_model(model, cfg)
     rec = CBRecorder(engine)
@@ -109,6 +110,8 @@ def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096, eos_token_i
         "async": async_mode,
         "num_blocks": num_blocks,
         "num_cpu_blocks": host_blocks,
+        "kv_pressure_mode": cfg.kv_pressure_mode,
+        "max_model_len": cfg.max_model_len,
         "eos_token_id": eos_token_id,
         "stop_sequences": stop_sequences,
         "tokens": [o.generated_tokens for o in outs],
@@ -193,6 +196,8 @@ def main() -> None:
         ("cb_async_blocks40_host64", True, 40, {"host_blocks": 64}),
         ("cb_sync_blocks48_host2", False, 48, {"host_blocks": 2}),
         ("cb_async_blocks36_host3", True, 36, {"host_blocks": 3}),
+        ("cb_async_reserve_blocks40", True, 40, {"reserve": True}),
+        ("cb_sync_reserve_blocks40", False, 40, {"reserve": True}),
     ):
         res, logits = run_case(name, async_mode=async_mode, num_blocks=nb, **kw)
         runs.append(res)

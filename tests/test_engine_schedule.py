@@ -92,7 +92,9 @@ class _HostRunner:
 def _engine(data: dict, run: dict, num_blocks: int, host_blocks: int = 0) -> ContinuousDepthBatchingEngine:
     shape = OuroShape(**data["shape"])
     kv_policy = run.get("kv_policy", "single")
-    pressure = "offload" if host_blocks else ("reserve" if kv_policy == "last_exited" else "recompute")
+    pressure = run.get("kv_pressure_mode") or (
+        "offload" if host_blocks else ("reserve" if kv_policy == "last_exited" else "recompute")
+    )
     cfg = ContinuousDepthBatchingConfig(
         block_size=16,
         num_blocks=num_blocks,
@@ -103,7 +105,7 @@ def _engine(data: dict, run: dict, num_blocks: int, host_blocks: int = 0) -> Con
         kv_policy=kv_policy,
         kv_pressure_mode=pressure,
         cpu_offload_space=1.0 if host_blocks else None,
-        max_model_len=2048,
+        max_model_len=run.get("max_model_len", 2048),
     ).get_resolved()
     runner = _HostRunner(cfg, shape)
     runner.pool.num_host_blocks = host_blocks
@@ -146,6 +148,8 @@ PRESSURE = [
     ("replay_refill_blocks40", 2),
     ("replay_norefill_blocks48", 2),
     ("replay_norefill_blocks40", 1),
+    ("replay_refill_reserve_blocks40", 0),
+    ("replay_norefill_reserve_blocks40", 0),
 ]
 
 
@@ -259,6 +263,8 @@ CB_RUNS = [
     ("cb_async_blocks40_host64", 0),
     ("cb_sync_blocks48_host2", 1),
     ("cb_async_blocks36_host3", 0),
+    ("cb_async_reserve_blocks40", 0),
+    ("cb_sync_reserve_blocks40", 0),
 ]
 
 
@@ -277,8 +283,8 @@ def test_cb_schedule_matches_reference(name, preemptions):
     host = run.get("num_cpu_blocks") or 0
     cfg = CDBConfig(
         block_size=16, num_blocks=run["num_blocks"], max_recurrent_steps=shape.total_ut_steps,
-        use_async_batching=run["async"], kv_policy="single", max_model_len=2048,
-        kv_pressure_mode="offload" if host else "recompute", cpu_offload_space=1.0 if host else None,
+        use_async_batching=run["async"], kv_policy="single", max_model_len=run["max_model_len"],
+        kv_pressure_mode=run["kv_pressure_mode"], cpu_offload_space=1.0 if host else None,
     ).get_resolved()
     runner = _HostRunner(cfg, shape)
     runner.pool.num_host_blocks = host

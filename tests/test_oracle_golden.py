@@ -11,6 +11,7 @@ reproduce each run exactly: generated tokens, the ordered launch trace with ever
 
 from __future__ import annotations
 
+import dataclasses
 import json
 from pathlib import Path
 
@@ -133,17 +134,24 @@ def test_oracle_reproduces_reference_early_finish_run(name):
         ("replay_refill_blocks40", 2),
         ("replay_norefill_blocks48", 2),
         ("replay_norefill_blocks40", 1),
+        ("replay_refill_reserve_blocks40", 0),
+        ("replay_norefill_reserve_blocks40", 0),
     ],
 )
 def test_oracle_reproduces_reference_pressure_run(name, preemptions):
     """KV pressure under recompute: a decoder whose next block cannot be had stalls, is restaged
     at the head of the next tick, and when nothing can run the stalled request with the shortest
     context is reset to prompt + generated text and re-queued, blocking new admissions until a
-    request retires."""
+    request retires. Under reserve admission the same pool admits a prompt only while every
+    admitted request's worst-case blocks fit, and nothing is preempted."""
 
     data, shape, sd = _load_ouro("ouro_cfg0_pressure.json")
     run = next(r for r in data["runs"] if r["name"] == name)
-    engine = OracleEngine(shape, sd, _config(run, {**data, "num_blocks": run["num_blocks"]}), torch.float32)
+    cfg = dataclasses.replace(
+        _config(run, {**data, "num_blocks": run["num_blocks"]}),
+        kv_pressure_mode=run.get("kv_pressure_mode", "recompute"), max_model_len=run.get("max_model_len", 2048),
+    )
+    engine = OracleEngine(shape, sd, cfg, torch.float32)
     tokens = engine.generate(data["prompts"], data["max_new_tokens"], exit_depths=run["exit_depths"])
     assert tokens == run["tokens"]
     assert engine.launches == run["launches"]
@@ -195,6 +203,8 @@ def test_oracle_reproduces_reference_offload_run(name, counts):
         ("cb_async_blocks40_host64", 0),
         ("cb_sync_blocks48_host2", 1),
         ("cb_async_blocks36_host3", 0),
+        ("cb_async_reserve_blocks40", 0),
+        ("cb_sync_reserve_blocks40", 0),
     ],
 )
 def test_cb_oracle_reproduces_reference_run(name, preemptions):
@@ -209,8 +219,8 @@ def test_cb_oracle_reproduces_reference_run(name, preemptions):
     run = next(r for r in data["runs"] if r["name"] == name)
     host = run.get("num_cpu_blocks") or 0
     cfg = OracleConfig(
-        block_size=16, num_blocks=run["num_blocks"], max_recurrent_steps=4, max_model_len=2048,
-        kv_pressure_mode="offload" if host else "recompute", num_cpu_blocks=host,
+        block_size=16, num_blocks=run["num_blocks"], max_recurrent_steps=4, max_model_len=run["max_model_len"],
+        kv_pressure_mode=run["kv_pressure_mode"], num_cpu_blocks=host,
     )
     engine = OracleCBEngine(shape, sd, cfg, torch.float32, async_mode=run["async"])
     tokens = engine.generate(
