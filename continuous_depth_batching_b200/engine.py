@@ -247,6 +247,10 @@ class ContinuousDepthBatchingEngine:
         if model_type not in ("ouro", "huginn"):
             raise TypeError(f"Continuous depth batching requires an Ouro or Huginn model; got {type(model)!r}")
         cfg = cdb_config.get_resolved()
+        # ``resolve_max_num_seqs`` (``scheduler_base.py:49-66``, applied at ``continuous_api.py:328``):
+        # a decode launch writes one row per resident request into buffers sized by the prefill
+        # token budget, so the resident cap is at most that budget
+        cfg.max_num_seqs = min(cfg.max_num_seqs, cfg.max_num_batched_tokens)
         if model_type == "huginn":
             hshape = HuginnShape.from_config(config)
             shape = HuginnShape(**{**hshape.__dict__, "total_recurrent_steps": cfg.max_recurrent_steps})
@@ -401,11 +405,12 @@ class ContinuousDepthBatchingEngine:
         self.host_tables: dict[int, list[int]] = {}
         self.refills = 0
         self.max_queue = 0
-        self.free_slots = list(range(cfg.max_num_seqs - 1, -1, -1))
+        seqs = min(cfg.max_num_seqs, cfg.max_num_batched_tokens)  # as from_model resolves it
+        self.free_slots = list(range(seqs - 1, -1, -1))
         self.free_hidden = list(range(self.runner.bank_slots - 1, -1, -1))
         self.pool = self.runner.pool.pool
-        self.max_num_seqs = cfg.max_num_seqs
-        self.min_free = max(1, cfg.max_num_seqs // 8) if cfg.min_free_slots is None else min(cfg.min_free_slots, cfg.max_num_seqs)
+        self.max_num_seqs = seqs
+        self.min_free = max(1, seqs // 8) if cfg.min_free_slots is None else min(cfg.min_free_slots, seqs)
         self.safety = 0.0 if cfg.kv_pressure_mode == "reserve" else cfg.safety_margin
         self.width = cfg.decode_block_table_width()
         self.slots = cfg.kv_slots_per_layer

@@ -165,6 +165,7 @@ class Recorder:
 def run_case(
     name: str, *, kv_policy: str, refill: bool, live_gate: bool, exit_depths=None, num_blocks=4096, async_mode=False,
     eos_token_id=None, stop_sequences=None, pressure_mode=None, cpu_offload_space=None, max_model_len=2048,
+    extra_cfg: dict | None = None,
 ):
     from looped_cdb.continuous_depth_batching import ContinuousDepthBatchingConfig, ContinuousDepthBatchingEngine
 
@@ -184,6 +185,7 @@ def run_case(
         kv_pressure_mode=pressure_mode or ("reserve" if kv_policy == "last_exited" else "recompute"),
         cpu_offload_space=cpu_offload_space,
         max_model_len=max_model_len,
+        **(extra_cfg or {}),
     )
     engine = ContinuousDepthBatchingEngine.from_model(model, cfg)
     rec = Recorder(engine)
@@ -461,8 +463,54 @@ def offload_main() -> None:
         print(r["name"], r["stats"])
 
 
+def knobs_main() -> None:
+    """``--knobs``: the replayed schedule under non-default scheduler settings, into
+    ``ouro_cfg0_knobs.json``: a 48-token prefill budget (prompts are chunked and a request is
+    PREFILLING across several batches), refill synchronous and delayed and no-refill; at most 6
+    resident requests (admission waits for open slots); and a coda minimum of 4 exited tokens."""
+
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    gold = json.loads((HERE / "ouro_cfg0.json").read_text())
+    runs = []
+    for name, refill, async_mode, extra in (
+        ("replay_refill_chunked48", True, False, {"max_num_batched_tokens": 48}),
+        ("replay_refill_chunked48_async", True, True, {"max_num_batched_tokens": 48}),
+        ("replay_norefill_chunked48", False, False, {"max_num_batched_tokens": 48}),
+        ("replay_refill_seqs6", True, False, {"max_num_seqs": 6}),
+        ("replay_refill_coda4", True, False, {"min_coda_batch_size": 4}),
+    ):
+        tag = "refill" if refill else "norefill"
+        src = next(r for r in gold["runs"] if r["name"] == f"replay_{tag}")["exit_depths"]
+        if async_mode:
+            src = json.loads((HERE / "ouro_cfg0_async.json").read_text())
+            src = next(r for r in src["runs"] if r["name"] == "replay_refill_async")["exit_depths"]
+        res, _ = run_case(
+            name, kv_policy="single", refill=refill, live_gate=False, exit_depths=src, async_mode=async_mode,
+            extra_cfg=extra,
+        )
+        res["config"] = extra
+        runs.append(res)
+    prompts, max_new = config0_workload()
+    payload = {
+        "generator": "tests/golden/make_golden.py --knobs",
+        "shape": CFG0.__dict__,
+        "gate_std": GATE_STD,
+        "weights_seed": 0,
+        "prompts": prompts,
+        "max_new_tokens": max_new,
+        "block_size": 16,
+        "num_blocks": 4096,
+        "runs": runs,
+    }
+    (HERE / "ouro_cfg0_knobs.json").write_text(json.dumps(payload, separators=(",", ":")))
+    for r in runs:
+        print(r["name"], r["stats"]["prefill_batches"], r["stats"]["coda_batches"], len(r["launches"]))
+
+
 if __name__ == "__main__":
-    if "--offload" in sys.argv[1:]:
+    if "--knobs" in sys.argv[1:]:
+        knobs_main()
+    elif "--offload" in sys.argv[1:]:
         offload_main()
     elif "--policies" in sys.argv[1:]:
         policies_main()

@@ -308,6 +308,45 @@ def test_cb_schedule_matches_reference(name, preemptions):
     _check_prefill_contents(eng, data["prompts"], outs)
 
 
+KNOBS = [
+    "replay_refill_chunked48",
+    "replay_refill_chunked48_async",
+    "replay_norefill_chunked48",
+    "replay_refill_seqs6",
+    "replay_refill_coda4",
+]
+
+
+@pytest.mark.parametrize("name", KNOBS)
+def test_scheduler_settings_match_reference(name):
+    """Non-default scheduler settings (``tests/golden/ouro_cfg0_knobs.json``): a 48-token prefill
+    budget, so prompts are chunked over several batches (refill in both timings, and no-refill);
+    at most 6 resident requests; a coda minimum of 4 exited tokens."""
+
+    data = _load("ouro_cfg0_knobs.json")
+    run = next(r for r in data["runs"] if r["name"] == name)
+    eng = _engine(data, {**run, "kv_policy": "single"}, data["num_blocks"])
+    for key, value in run["config"].items():
+        setattr(eng.cdb_config, key, value)
+    eng.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"]
+    )
+    assert eng.launch_trace == run["launches"]
+    assert eng.last_stats.scheduler_refills == run["stats"]["scheduler_refills"]
+
+
+def test_resident_cap_resolves_to_the_token_budget():
+    """``resolve_max_num_seqs``: a prefill budget below ``max_num_seqs`` caps the resident set,
+    and the default ``min_free_slots`` follows the resolved cap."""
+
+    data = _load("ouro_cfg0_knobs.json")
+    run = next(r for r in data["runs"] if r["name"] == "replay_refill_chunked48")
+    eng = _engine(data, {**run, "kv_policy": "single"}, data["num_blocks"])
+    eng.cdb_config.max_num_batched_tokens = 48
+    eng._reset_state()
+    assert (eng.max_num_seqs, eng.min_free, len(eng.free_slots)) == (48, 6, 48)
+
+
 def test_single_request_that_cannot_fit_raises():
     """With one active request left and no block for its next token, preemption cannot help: the
     reference raises ``CacheFullError`` (``continuous_api.py:1640-1646``)."""

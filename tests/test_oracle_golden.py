@@ -266,6 +266,29 @@ def test_cb_oracle_reproduces_reference_huginn_run(name):
     assert engine.launches == run["launches"]
 
 
+@pytest.mark.parametrize(
+    "name",
+    [
+        "replay_refill_chunked48",
+        "replay_refill_chunked48_async",
+        "replay_norefill_chunked48",
+        "replay_refill_seqs6",
+        "replay_refill_coda4",
+    ],
+)
+def test_oracle_reproduces_reference_knobs_run(name):
+    """Chunked prompts (48-token prefill budget) in both timings and without refill, a cap of 6
+    resident requests, and a coda minimum of 4: tokens and launches equal the reference's."""
+
+    data, shape, sd = _load_ouro("ouro_cfg0_knobs.json")
+    run = next(r for r in data["runs"] if r["name"] == name)
+    cfg = dataclasses.replace(_config(run, data), **run["config"])
+    engine = OracleEngine(shape, sd, cfg, torch.float32)
+    tokens = engine.generate(data["prompts"], data["max_new_tokens"], exit_depths=run["exit_depths"])
+    assert tokens == run["tokens"]
+    assert engine.launches == run["launches"]
+
+
 @pytest.mark.parametrize("name", ["live_gate_refill", "replay_refill", "replay_norefill", "replay_last_exited"])
 def test_oracle_reproduces_reference_run(golden, name):
     data, shape, sd = golden
