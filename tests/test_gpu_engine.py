@@ -45,7 +45,7 @@ def _host_space(shape, host_blocks: int) -> float | None:
 
 
 def _engine(shape, sd, *, kv_policy="single", refill=True, live=False, num_blocks=4096, max_model_len=2048, graphs=True,
-            gemm="cublas", async_mode=False, host_blocks=0):
+            gemm="cublas", async_mode=False, host_blocks=0, extra=None):
     model = OuroForCausalLM(shape)
     model.load_state_dict({k: v.to(torch.float32) for k, v in sd.items()})
     cfg = ContinuousDepthBatchingConfig(
@@ -61,6 +61,7 @@ def _engine(shape, sd, *, kv_policy="single", refill=True, live=False, num_block
         kv_pressure_mode="offload" if host_blocks else ("reserve" if kv_policy == "last_exited" else "recompute"),
         cpu_offload_space=_host_space(shape, host_blocks),
         max_model_len=max_model_len,
+        **(extra or {}),
     )
     eng = ContinuousDepthBatchingEngine.from_model(model, cfg, device="cuda", gemm_backend=gemm)
     assert eng.runner.pool.num_host_blocks == host_blocks
@@ -469,6 +470,39 @@ def test_cb_teacher_forced_logits():
     assert eng.launch_trace == o32.launches == o16.launches
     assert [k for k, _ in eng.lm_logits] == [k for k, _ in o16.logits] == [k for k, _ in o32.logits]
     rep = compare_lm_launches([lg for _, lg in eng.lm_logits], [lg for _, lg in o16.logits], [lg for _, lg in o32.logits])
+    print(rep)
+    assert_report(rep)
+
+
+def test_chunked_prefill_schedule_and_logits():
+    """Prompts chunked by a 48-token prefill budget (delayed timing): each later chunk's prefill
+    attends over the KV its earlier chunks cached. The launch trace equals the reference's
+    (``tests/golden/ouro_cfg0_knobs.json``) and, teacher-forced on the reference's tokens, every
+    LM-head launch meets the numerics criteria against the fp32 and bf16 oracles."""
+
+    data = json.loads((GOLDEN / "ouro_cfg0_knobs.json").read_text())
+    shape = OuroShape(**data["shape"])
+    run = next(r for r in data["runs"] if r["name"] == "replay_refill_chunked48_async")
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+    eng = _engine(shape, sd, async_mode=True, extra=run["config"])
+    eng.record_trace = True
+    eng.keep_logits = True
+    eng.generate_batch(
+        data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"],
+        forced_tokens=run["tokens"],
+    )
+    assert eng.launch_trace == run["launches"]
+    ocfg = OracleConfig(
+        block_size=16, num_blocks=4096, max_recurrent_steps=4, max_model_len=2048, synthetic_exit_replay=True,
+        delayed=True, **run["config"],
+    )
+    logits = []
+    for dtype in (torch.bfloat16, torch.float32):
+        o = OracleEngine(shape, sd, ocfg, dtype)
+        o.generate(data["prompts"], data["max_new_tokens"], exit_depths=run["exit_depths"], forced_tokens=run["tokens"])
+        assert o.launches == run["launches"]
+        logits.append([lg for _, lg in o.logits])
+    rep = compare_lm_launches([lg for _, lg in eng.lm_logits], logits[0], logits[1])
     print(rep)
     assert_report(rep)
 
