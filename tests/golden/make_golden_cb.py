@@ -16,7 +16,8 @@ the workload (recompute preemption), and with requests ending early on EOS ids o
 (pipelined, the finish is seen one tick late and the extra token computed meanwhile is dropped),
 and under ``kv_pressure_mode="offload"`` with host pools of 64, 3 and 2 blocks (a victim's blocks go to
 the host pool when they fit there and come back before it is scheduled again; otherwise recompute),
-and under ``"reserve"`` admission at 40 blocks (``max_model_len`` 512).
+under ``"reserve"`` admission at 40 blocks (``max_model_len`` 512), and with a 48-token prefill budget
+that chunks the prompts.
 Every launched batch is recorded in order: its kind, each
 request's (index, cached length, query length, samples-a-token flag) and block-table row, plus
 the logits of the LM-head rows. Output: ``tests/golden/ouro_cfg0_cb.json`` and
@@ -80,7 +81,7 @@ class CBRecorder:
 
 
 def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096, eos_token_id=None, stop_sequences=None,
-             host_blocks: int = 0, reserve: bool = False):
+             host_blocks: int = 0, reserve: bool = False, max_num_batched_tokens: int = 8192):
     from looped_cdb.continuous_batching.config import ContinuousBatchingConfig
     from looped_cdb.continuous_batching.continuous_api import ContinuousBatchingEngine
 
@@ -97,6 +98,7 @@ def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096, eos_token_i
         cpu_offload_space=host_blocks * 2 * mg.CFG0.num_hidden_layers * 16 * mg.CFG0.num_key_value_heads
         * mg.CFG0.head_dim * 4 / 1024**3 if host_blocks else None,
         max_model_len=512 if reserve else 2048,
+        max_num_batched_tokens=max_num_batched_tokens,
     )
     engine = ContinuousBatchingEngine.from_model(model, cfg)
     rec = CBRecorder(engine)
@@ -112,6 +114,7 @@ def run_case(name: str, *, async_mode: bool, num_blocks: int = 4096, eos_token_i
         "num_cpu_blocks": host_blocks,
         "kv_pressure_mode": cfg.kv_pressure_mode,
         "max_model_len": cfg.max_model_len,
+        "max_num_batched_tokens": cfg.max_num_batched_tokens,
         "eos_token_id": eos_token_id,
         "stop_sequences": stop_sequences,
         "tokens": [o.generated_tokens for o in outs],
@@ -198,6 +201,8 @@ def main() -> None:
         ("cb_async_blocks36_host3", True, 36, {"host_blocks": 3}),
         ("cb_async_reserve_blocks40", True, 40, {"reserve": True}),
         ("cb_sync_reserve_blocks40", False, 40, {"reserve": True}),
+        ("cb_async_chunked48", True, 4096, {"max_num_batched_tokens": 48}),
+        ("cb_sync_chunked48", False, 4096, {"max_num_batched_tokens": 48}),
     ):
         res, logits = run_case(name, async_mode=async_mode, num_blocks=nb, **kw)
         runs.append(res)

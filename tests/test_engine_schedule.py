@@ -265,6 +265,8 @@ CB_RUNS = [
     ("cb_async_blocks36_host3", 0),
     ("cb_async_reserve_blocks40", 0),
     ("cb_sync_reserve_blocks40", 0),
+    ("cb_async_chunked48", 0),
+    ("cb_sync_chunked48", 0),
 ]
 
 
@@ -285,6 +287,7 @@ def test_cb_schedule_matches_reference(name, preemptions):
         block_size=16, num_blocks=run["num_blocks"], max_recurrent_steps=shape.total_ut_steps,
         use_async_batching=run["async"], kv_policy="single", max_model_len=run["max_model_len"],
         kv_pressure_mode=run["kv_pressure_mode"], cpu_offload_space=1.0 if host else None,
+        max_num_batched_tokens=run["max_num_batched_tokens"],
     ).get_resolved()
     runner = _HostRunner(cfg, shape)
     runner.pool.num_host_blocks = host

@@ -205,6 +205,8 @@ def test_oracle_reproduces_reference_offload_run(name, counts):
         ("cb_async_blocks36_host3", 0),
         ("cb_async_reserve_blocks40", 0),
         ("cb_sync_reserve_blocks40", 0),
+        ("cb_async_chunked48", 0),
+        ("cb_sync_chunked48", 0),
     ],
 )
 def test_cb_oracle_reproduces_reference_run(name, preemptions):
@@ -221,6 +223,7 @@ def test_cb_oracle_reproduces_reference_run(name, preemptions):
     cfg = OracleConfig(
         block_size=16, num_blocks=run["num_blocks"], max_recurrent_steps=4, max_model_len=run["max_model_len"],
         kv_pressure_mode=run["kv_pressure_mode"], num_cpu_blocks=host,
+        max_num_batched_tokens=run["max_num_batched_tokens"],
     )
     engine = OracleCBEngine(shape, sd, cfg, torch.float32, async_mode=run["async"])
     tokens = engine.generate(
