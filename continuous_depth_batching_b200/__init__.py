@@ -7,7 +7,7 @@ full-depth continuous-batching baseline on the same kernels. Compute runs in ``l
 ABI in ``include/cdb_b200.h``) plus cuBLAS GEMMs; there is no CPU path.
 """
 
-from .cb_engine import ContinuousBatchingConfig, ContinuousBatchingEngine, ContinuousBatchingStats
+from .cb_engine import ContinuousBatchingConfig, ContinuousBatchingEngine, ContinuousBatchingStats, DecodeStepTiming
 from .config import ContinuousDepthBatchingConfig
 from .engine import (
     CacheFullError,
@@ -27,6 +27,7 @@ __all__ = [
     "ContinuousDepthBatchingConfig",
     "ContinuousDepthBatchingEngine",
     "ContinuousDepthBatchingStats",
+    "DecodeStepTiming",
     "GenerationOutput",
     "HuginnForCausalLM",
     "HuginnShape",

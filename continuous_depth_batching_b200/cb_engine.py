@@ -33,7 +33,7 @@ import torch
 from .config import DEFAULT_MAX_NUM_SEQS, ContinuousDepthBatchingConfig
 from .engine import CacheFullError, ContinuousDepthBatchingEngine, GenerationOutput, RequestStatus, _Req
 
-__all__ = ["ContinuousBatchingConfig", "ContinuousBatchingEngine", "ContinuousBatchingStats"]
+__all__ = ["ContinuousBatchingConfig", "ContinuousBatchingEngine", "ContinuousBatchingStats", "DecodeStepTiming"]
 
 
 @dataclass
@@ -84,6 +84,26 @@ class ContinuousBatchingStats:
     @property
     def mean_decode_batch_size(self) -> float:
         return self.decode_tokens / self.decode_batches if self.decode_batches else 0.0
+
+
+@dataclass
+class DecodeStepTiming:
+    """One steady-state decode step at full batch, prefill excluded (the reference's
+    ``DecodeStepTiming``, ``continuous_api.py:106-131``). ``per_step_ms`` is host wall clock over the
+    timed window (opened and closed by a device synchronisation) per step; ``gpu_per_step_ms`` the
+    same window in CUDA events on the engine stream. ``context_min`` / ``context_max`` bracket the
+    requests' KV lengths when the window opened."""
+
+    batch_size: int
+    context_length: int
+    context_min: int
+    context_max: int
+    warmup_decode_steps: int
+    timed_decode_steps: int
+    wall_elapsed_ms: float
+    gpu_elapsed_ms: float
+    per_step_ms: float
+    gpu_per_step_ms: float
 
 
 class ContinuousBatchingEngine(ContinuousDepthBatchingEngine):
@@ -221,6 +241,108 @@ class ContinuousBatchingEngine(ContinuousDepthBatchingEngine):
         st.kv_peak_blocks = self.runner.pool.pool.peak
         return outs
 
+    @torch.no_grad()
+    def measure_decode_step_latency(
+        self,
+        input_ids: list[list[int]],
+        *,
+        max_new_tokens: int,
+        warmup_decode_steps: int,
+        timed_decode_steps: int,
+        model_kwargs: dict | None = None,
+    ) -> DecodeStepTiming:
+        """Time one full-batch decode step at full depth, isolated from prefill
+        (``continuous_api.py:491-624``).
+
+        ``B`` equal-length prompts are submitted; once all ``B`` decode together (a decode batch of
+        ``B`` with nothing waiting) the next ``warmup_decode_steps`` such ticks settle, and the
+        following ``timed_decode_steps`` are timed. Build the engine with ``safety_margin=0`` so every
+        prompt prefills before decoding starts; ``max_new_tokens`` must outlast the window. Raises
+        if the batch drops below ``B`` inside the window or never reaches it."""
+
+        del model_kwargs
+        if warmup_decode_steps < 1:
+            raise ValueError("warmup_decode_steps must be >= 1 to settle the decode graph before timing")
+        if timed_decode_steps < 1:
+            raise ValueError("timed_decode_steps must be >= 1")
+        if max_new_tokens <= warmup_decode_steps + timed_decode_steps:
+            raise ValueError(
+                f"max_new_tokens ({max_new_tokens}) must exceed warmup+timed decode steps "
+                f"({warmup_decode_steps + timed_decode_steps})"
+            )
+        if not torch.cuda.is_available():
+            raise RuntimeError("measure_decode_step_latency requires CUDA for event timing")
+        self._validate_generate_inputs(input_ids, max_new_tokens)
+        batch = len(input_ids)
+        context = len(input_ids[0])
+        if any(len(p) != context for p in input_ids):
+            raise ValueError("measure_decode_step_latency expects equal-length prompts")
+        caps = self._validate(input_ids, max_new_tokens, None, None)
+        self._content_finish = False
+        self._forced = None
+        self._gate_live = False
+        self._delayed = False
+        reqs = []
+        for i, (p, m) in enumerate(zip(input_ids, caps, strict=True)):
+            r = _Req(i, list(p), m, [], set(), [], False)
+            r.log_base = i * m
+            reqs.append(r)
+        self.runner.reset(max(sum(caps), 1))
+        self._reset_state()
+        self.last_stats = ContinuousBatchingStats()
+        self._reqs = reqs
+        for r in reqs:
+            self.waiting[r.idx] = r
+        stream = self.runner.stream
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        full_ticks = 0
+        timing = False
+        wall0 = 0.0
+        ctx_min = ctx_max = context
+        in_flight = None
+        while self.active or self.waiting or in_flight is not None:
+            self._last_launch = None
+            try:
+                in_flight = self._tick(in_flight)
+            except CacheFullError as exc:
+                raise CacheFullError(
+                    f"could not assemble the full batch of {batch} requests at context {context}: the KV cache "
+                    "is exhausted before all requests are resident. Increase num_blocks, or reduce the batch "
+                    "size or context length."
+                ) from exc
+            launch = self._last_launch
+            if not (launch is not None and launch[0] and launch[1] == batch and not self.waiting):
+                if timing:
+                    raise RuntimeError("decode batch dropped below B inside the timed window")
+                continue
+            full_ticks += 1
+            if full_ticks < warmup_decode_steps:
+                continue
+            if full_ticks == warmup_decode_steps:
+                torch.cuda.synchronize()
+                lengths = [r.position for r in reqs]
+                ctx_min, ctx_max = min(lengths), max(lengths)
+                wall0 = time.perf_counter()
+                start.record(stream)
+                timing = True
+                continue
+            if full_ticks == warmup_decode_steps + timed_decode_steps:
+                stop.record(stream)
+                torch.cuda.synchronize()
+                wall_ms = (time.perf_counter() - wall0) * 1e3
+                gpu_ms = start.elapsed_time(stop)
+                return DecodeStepTiming(
+                    batch_size=batch, context_length=context, context_min=ctx_min, context_max=ctx_max,
+                    warmup_decode_steps=warmup_decode_steps, timed_decode_steps=timed_decode_steps,
+                    wall_elapsed_ms=wall_ms, gpu_elapsed_ms=gpu_ms, per_step_ms=wall_ms / timed_decode_steps,
+                    gpu_per_step_ms=gpu_ms / timed_decode_steps,
+                )
+        raise RuntimeError(
+            f"generation ended after {full_ticks} full-batch decode ticks before timing completed (need "
+            f"{warmup_decode_steps + timed_decode_steps}); the batch may never reach B={batch} at this context, "
+            "or max_new_tokens / the block budget is too small"
+        )
+
     # ------------------------------------------------------------------ scheduling
     def _will_finish(self, r: _Req) -> bool:
         """``will_finish_on_pending_token`` (``continuous_batching/requests.py:196-206``)."""
@@ -338,6 +460,7 @@ class ContinuousBatchingEngine(ContinuousDepthBatchingEngine):
         st = self.last_stats
         bs = self.cdb_config.block_size
         is_decode = all(q == 1 and r.status == RequestStatus.DECODING for r, q, _s in entries)
+        self._last_launch = (is_decode, len(entries))
         if self.record_trace:
             self.launch_trace.append(
                 {

@@ -375,3 +375,46 @@ def test_pressure_none_mode_raises_instead_of_stalling():
         eng.generate_batch(
             data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"]
         )
+
+
+class _FakeEvent:
+    """CUDA-event stand-in: every timed window reads 10 ms."""
+
+    def __init__(self, enable_timing=False):
+        self.recorded = False
+
+    def record(self, stream=None):
+        self.recorded = True
+
+    def elapsed_time(self, other):
+        assert self.recorded and other.recorded
+        return 10.0
+
+
+def test_cb_decode_step_latency_window(monkeypatch):
+    """``measure_decode_step_latency``: with every prompt prefilled first (``safety_margin=0``),
+    the window opens after ``warmup`` full-batch decode ticks and closes after ``timed`` more, at a
+    uniform context (prompt length + warm-up tokens). Events are faked: the control flow is what is
+    checked here."""
+
+    from continuous_depth_batching_b200 import ContinuousBatchingEngine
+    from continuous_depth_batching_b200.config import ContinuousDepthBatchingConfig as CDBConfig
+
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: True)
+    monkeypatch.setattr(torch.cuda, "Event", _FakeEvent)
+    monkeypatch.setattr(torch.cuda, "synchronize", lambda *a, **k: None)
+    shape = OuroShape(**_load("ouro_cfg0_cb.json")["shape"])
+    cfg = CDBConfig(block_size=16, num_blocks=256, max_recurrent_steps=4, kv_policy="single", max_model_len=512,
+                    safety_margin=0.0).get_resolved()
+    eng = ContinuousBatchingEngine(None, cfg, _HostRunner(cfg, shape), shape)
+    eng.record_trace = True
+    prompts = [[(7 * i + j) % shape.vocab_size for j in range(20)] for i in range(6)]
+    t = eng.measure_decode_step_latency(prompts, max_new_tokens=16, warmup_decode_steps=2, timed_decode_steps=5)
+    assert (t.batch_size, t.context_length, t.context_min, t.context_max) == (6, 20, 22, 22)
+    assert t.gpu_elapsed_ms == 10.0 and t.gpu_per_step_ms == 2.0 and t.per_step_ms >= 0
+    kinds = [launch["kind"] for launch in eng.launch_trace]
+    assert kinds == ["prefill"] + ["decode"] * 7
+    with pytest.raises(ValueError, match="must exceed"):
+        eng.measure_decode_step_latency(prompts, max_new_tokens=7, warmup_decode_steps=2, timed_decode_steps=5)
+    with pytest.raises(ValueError, match="equal-length"):
+        eng.measure_decode_step_latency([[1, 2], [3]], max_new_tokens=16, warmup_decode_steps=2, timed_decode_steps=5)

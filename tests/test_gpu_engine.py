@@ -507,6 +507,28 @@ def test_chunked_prefill_schedule_and_logits():
     assert_report(rep)
 
 
+def test_cb_decode_step_latency_probe():
+    """``ContinuousBatchingEngine.measure_decode_step_latency`` on the B200: six equal prompts all
+    prefill first (``safety_margin=0``), then 5 full-batch decode steps are timed after 2 warm-up
+    ones, at a uniform context; the timing is positive and the batches are one prefill then decodes."""
+
+    from continuous_depth_batching_b200 import ContinuousBatchingConfig, ContinuousBatchingEngine
+
+    data, shape = _golden()
+    sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"])
+    model = OuroForCausalLM(shape)
+    model.load_state_dict({k: v.to(torch.float32) for k, v in sd.items()})
+    cfg = ContinuousBatchingConfig(num_blocks=256, max_model_len=512, safety_margin=0.0)
+    eng = ContinuousBatchingEngine.from_model(model, cfg, device="cuda", kv_policy="single")
+    eng.record_trace = True
+    prompts = [[(7 * i + j) % shape.vocab_size for j in range(20)] for i in range(6)]
+    t = eng.measure_decode_step_latency(prompts, max_new_tokens=16, warmup_decode_steps=2, timed_decode_steps=5)
+    assert (t.batch_size, t.context_min, t.context_max) == (6, 22, 22)
+    assert t.gpu_per_step_ms > 0 and t.per_step_ms > 0
+    assert [launch["kind"] for launch in eng.launch_trace] == ["prefill"] + ["decode"] * 7
+    eng.runner.check_status()
+
+
 def test_teacher_forced_greedy_tokens_peaked_head():
     """Same criteria with a wide LM head (logit scale ~14 instead of ~1.4)."""
 
