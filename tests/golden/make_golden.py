@@ -426,7 +426,8 @@ def offload_main() -> None:
     ``kv_pressure_mode="offload"``. A stalled victim's blocks are swapped to a host pool of
     ``num_cpu_blocks`` blocks and restored (admitted ahead of fresh prompts) once blocks free up;
     a victim that does not fit the host pool falls back to recompute. Host pools of 64 blocks
-    (every victim fits), 2 and 1 (offload and recompute mixed), refill and no-refill, into
+    (every victim fits), 2 and 1 (offload and recompute mixed), refill and no-refill; and under
+    ``last_exited`` (4 KV slots per layer, every slot's blocks swapped; no recompute fallback), into
     ``ouro_cfg0_offload.json``.
     The host pool is given in GiB, as the reference's config takes it: ``num_cpu_blocks`` times
     the bytes of one block over all cache layers (K and V) in the cache dtype."""
@@ -435,13 +436,18 @@ def offload_main() -> None:
     gold = json.loads((HERE / "ouro_cfg0.json").read_text())
     block_bytes = 2 * CFG0.num_hidden_layers * 16 * CFG0.num_key_value_heads * CFG0.head_dim * 4
     runs = []
-    for refill, nb, cpu_blocks in ((True, 48, 64), (True, 40, 2), (True, 48, 1), (False, 40, 64), (False, 48, 2)):
+    for refill, nb, cpu_blocks, policy in (
+        (True, 48, 64, "single"), (True, 40, 2, "single"), (True, 48, 1, "single"), (False, 40, 64, "single"),
+        (False, 48, 2, "single"), (True, 40, 64, "last_exited"), (False, 40, 64, "last_exited"),
+    ):
         tag = "refill" if refill else "norefill"
-        depths = next(r for r in gold["runs"] if r["name"] == f"replay_{tag}")["exit_depths"]
+        src = "replay_last_exited" if policy == "last_exited" else f"replay_{tag}"
+        depths = next(r for r in gold["runs"] if r["name"] == src)["exit_depths"]
+        slots = CFG0.total_ut_steps if policy == "last_exited" else 1
+        name = f"replay_{tag}_blocks{nb}_host{cpu_blocks}" + ("_last_exited" if policy == "last_exited" else "")
         res, _ = run_case(
-            f"replay_{tag}_blocks{nb}_host{cpu_blocks}", kv_policy="single", refill=refill, live_gate=False,
-            exit_depths=depths, num_blocks=nb, pressure_mode="offload",
-            cpu_offload_space=cpu_blocks * block_bytes / 1024**3,
+            name, kv_policy=policy, refill=refill, live_gate=False, exit_depths=depths, num_blocks=nb,
+            pressure_mode="offload", cpu_offload_space=cpu_blocks * block_bytes * slots / 1024**3,
         )
         assert res["stats"]["num_cpu_blocks"] == cpu_blocks, res["stats"]
         res["num_blocks"] = nb

@@ -166,6 +166,8 @@ OFFLOAD_RUNS = [
     ("replay_refill_blocks48_host1", (2, 1, 1)),
     ("replay_norefill_blocks40_host64", (0, 1, 1)),
     ("replay_norefill_blocks48_host2", (1, 1, 1)),
+    ("replay_refill_blocks40_host64_last_exited", (0, 0, 0)),
+    ("replay_norefill_blocks40_host64_last_exited", (0, 1, 1)),
 ]
 
 
