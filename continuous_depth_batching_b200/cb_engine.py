@@ -180,7 +180,6 @@ class ContinuousBatchingEngine(ContinuousDepthBatchingEngine):
         its own samples; the engine still records its own argmax at every position."""
 
         del warmup, record_queue_samples
-        cfg = self.cdb_config
         caps = self._validate(input_ids, max_new_tokens, None, model_kwargs)
         eos = set()
         if eos_token_id is not None:
