@@ -1089,14 +1089,39 @@ class ContinuousDepthBatchingEngine:
                 batch.append(self.ready.popleft())
         return batch
 
-    def _carry_successor(self, r: _Req) -> _Item | None:
+    def _carry_successor(self, r: _Req, token: int | None = None) -> _Item | None:
         """Stage the next decode token of ``r`` ahead of its wave (eager re-entry,
         ``_select_eager_reentries``, ``continuous_api.py:1304-1327``): allocate its KV block now;
-        None when no block is free (a later wave's cohort scan picks it up)."""
+        None when no block is free (a later wave's cohort scan picks it up). ``token`` is the input
+        id when the host knows it (-1: the request's device token)."""
 
         if not self._alloc_one_decode(r):
             return None
-        return _Item(r, r.position, r.next_depth(), self.free_hidden.pop(), self._next_token_id(r))
+        tok = self._next_token_id(r) if token is None else token
+        return _Item(r, r.position, r.next_depth(), self.free_hidden.pop(), tok)
+
+    def _would_finish(self, r: _Req) -> bool:
+        """Whether recording the request's pending token will finish it (length, EOS, stop)."""
+
+        if r.generated + 1 >= r.max_new:
+            return True
+        if not self._content_finish:
+            return False
+        tok = r.pending_token
+        if tok in r.eos:
+            return True
+        gen = self._host_tokens(r) + [tok]
+        return any(s and len(gen) >= len(s) and gen[-len(s):] == s for s in r.stops)
+
+    def _consume_carried_coda(self, pending: list[_Req]) -> None:
+        """``_consume_no_refill_coda``: the boundary coda's tokens are recorded, and finished
+        requests retired (their blocks freed), once the next wave's first launch is queued."""
+
+        for r in pending:
+            if r.status == RequestStatus.FINISHED:
+                continue
+            if self._record_token(r):
+                self._retire(r)
 
     def _carry_after_prefill(self, sampled: list[_Req], budget: int) -> list[_Item]:
         """Delayed no-refill path: each prefilled request's first decode token is carried into
@@ -1113,26 +1138,32 @@ class ContinuousDepthBatchingEngine:
                 carried.append(it)
         return carried
 
-    def _carry_after_coda(self, items: list[_Item]) -> list[_Item]:
+    def _carry_after_coda(self, items: list[_Item]) -> tuple[list[_Item], list[_Req]]:
         """Delayed no-refill path: the wave's exiters' successors, staged at the boundary coda in
-        exit order, lead the next wave (``continuous_api.py:929-940``)."""
+        exit order, lead the next wave (``continuous_api.py:929-940``). The coda's tokens are
+        recorded during that wave (:meth:`_consume_carried_coda`); a request the token finishes
+        gets no successor, and one whose successor finds no KV block sits out a wave. Returns the
+        carried successors and the requests whose tokens are pending."""
 
-        carried = []
+        carried, pending = [], []
         for it in items:
             r = it.req
             self.free_hidden.append(it.hidden)
             if r.status == RequestStatus.FINISHED:
                 continue
             r.position += 1
-            if self._record_token(r):
-                self._retire(r)
+            pending.append(r)
+            if self._would_finish(r):
                 continue
-            if (nxt := self._carry_successor(r)) is not None:
+            tok = int(self._forced[r.idx][r.generated]) if self._forced is not None else -1
+            if (nxt := self._carry_successor(r, tok)) is not None:
                 carried.append(nxt)
-        return carried
+        return carried, pending
 
     def _no_refill_loop(self, arrivals) -> None:
         carried: list[_Item] = []  # delayed path: successors staged before their wave
+        coda_ids: set[int] = set()  # delayed path: the previous wave's exiters (its coda is in flight)
+        pending_coda: list[_Req] = []  # that coda's requests, whose tokens are recorded during the next wave
         while arrivals or self._has_pending():
             self._release_arrivals(arrivals)
             if not self._has_pending():
@@ -1156,7 +1187,10 @@ class ContinuousDepthBatchingEngine:
                 else:
                     self._consume_prefill(sampled, stage=False)
                 did_prefill = True
-            carried_ids = {it.req.idx for it in carried}
+            # every request of the in-flight boundary coda sits out this wave's scan
+            # (``continuous_api.py:829-834``)
+            carried_ids = {it.req.idx for it in carried} | coda_ids
+            coda_ids = set()
             cohort = [
                 r
                 for r in self.active.values()
@@ -1167,6 +1201,10 @@ class ContinuousDepthBatchingEngine:
             items = carried + [it for r in cohort if (it := self._stage_decode(r)) is not None]
             carried = []
             if not items:
+                if pending_coda:  # nothing launches: recording the carried coda is this wave's work
+                    self._consume_carried_coda(pending_coda)
+                    pending_coda = []
+                    continue
                 if not did_prefill and self.stalled:
                     self._preempt_stalled()
                     continue
@@ -1181,6 +1219,9 @@ class ContinuousDepthBatchingEngine:
                 for it in survivors:
                     it.step = step
                 live = self._run_recurrent(survivors)
+                if pending_coda:  # the previous wave's coda is recorded after this wave's first launch
+                    self._consume_carried_coda(pending_coda)
+                    pending_coda = []
                 forced = step == self.steps - 1
                 cont = []
                 for i, it in enumerate(survivors):
@@ -1196,7 +1237,8 @@ class ContinuousDepthBatchingEngine:
                     break
             self._run_coda(exited)
             if self._delayed:
-                carried = self._carry_after_coda(exited)
+                coda_ids = {it.req.idx for it in exited}
+                carried, pending_coda = self._carry_after_coda(exited)
             else:
                 self._consume_coda(exited, stage=False)
 

@@ -687,18 +687,38 @@ class OracleEngine:
                 batch.append(self.ready.popleft())
         return batch
 
-    def _carry_successor(self, r: Req) -> Item | None:
+    def _carry_successor(self, r: Req, token: int | None = None) -> Item | None:
         """Eager re-entry (``_select_eager_reentries``, ``continuous_api.py:1304-1327``)."""
 
         if not self._alloc_one_decode(r):
             return None
-        return Item(req=r, token=r.to_process[0], position=r.position, step=0, depth=r.next_depth())
+        tok = r.to_process[0] if token is None else token
+        return Item(req=r, token=tok, position=r.position, step=0, depth=r.next_depth())
+
+    def _finishes_on(self, r: Req, token: int) -> bool:
+        """Whether consuming ``token`` will finish ``r`` (length limit, EOS id, stop sequence)."""
+
+        gen = list(r.generated) + [token]
+        stop = any(len(q) and len(gen) >= len(q) and gen[-len(q):] == q for q in self.stops)
+        return token in self.eos or len(gen) >= r.max_new or stop
+
+    def _consume_carried_coda(self, pending: list[tuple[Req, int]]) -> None:
+        """``_consume_no_refill_coda``: the boundary coda's tokens are applied (and finished
+        requests retired, freeing their blocks) once the next wave's first launch is queued."""
+
+        for r, tok in pending:
+            if r.status == FINISHED:
+                continue
+            if self._update(r, tok):
+                self._retire(r)
 
     def _no_refill_loop(self) -> None:
         # Delayed mode carries a wave's exiters' successors (staged at its boundary coda, in exit
         # order) and each prefilled request's first decode token (up to the launch width) into
         # the next wave ahead of the cohort scan (``continuous_api.py:721-790, 815-944``).
         carried: list[Item] = []
+        coda_ids: set[int] = set()  # delayed path: the previous wave's exiters (its coda is in flight)
+        pending_coda: list[tuple[Req, int]] = []  # that coda's tokens, applied during the next wave
         while self._has_pending():
             # offloaded requests come back before admission, so the prefill gate sees them as
             # decoders, and join this wave's cohort (``continuous_api.py:656-658``)
@@ -726,7 +746,10 @@ class OracleEngine:
                 else:
                     self._consume_prefill(res, stage=False)
                 did_prefill = True
-            carried_ids = {it.req.idx for it in carried}
+            # every request of the in-flight boundary coda sits out this wave's scan, so one whose
+            # successor found no KV block joins a wave later (continuous_api.py:829-834, 929-940)
+            carried_ids = {it.req.idx for it in carried} | coda_ids
+            coda_ids = set()
             cohort = [
                 r
                 for r in self.active.values()
@@ -738,6 +761,10 @@ class OracleEngine:
             items = carried + [it for r in cohort if (it := self._stage_decode(r)) is not None]
             carried = []
             if not items:
+                if pending_coda:  # nothing launches: consuming the carried coda is this wave's work
+                    self._consume_carried_coda(pending_coda)
+                    pending_coda = []
+                    continue
                 if not did_prefill and self.stalled:
                     self._preempt_stalled()
                     continue
@@ -750,6 +777,9 @@ class OracleEngine:
                 for it in survivors:
                     it.step = step
                 gate = self._run_recurrent(survivors)
+                if pending_coda:  # the previous wave's coda is consumed after this wave's first launch
+                    self._consume_carried_coda(pending_coda)
+                    pending_coda = []
                 forced = step == self.cfg.max_recurrent_steps - 1
                 cont = []
                 for i, it in enumerate(survivors):
@@ -764,15 +794,18 @@ class OracleEngine:
                     break
             toks = self._run_coda(exited)
             if self.cfg.delayed:
+                coda_ids = {it.req.idx for it in exited}
                 for it, tok in zip(exited, toks, strict=True):
                     r = it.req
                     if r.status == FINISHED:
                         continue
+                    tok = self._next_token(r, tok)
                     r.position += 1
-                    if self._update(r, self._next_token(r, tok)):
-                        self._retire(r)
-                        continue
-                    if (nxt := self._carry_successor(r)) is not None:
+                    pending_coda.append((r, tok))
+                    # no successor for a token that finishes its request (the length limit, as the
+                    # reference predicts it; an EOS id or stop sequence, which this restatement reads
+                    # before staging); a successor that finds no KV block waits a wave
+                    if not self._finishes_on(r, tok) and (nxt := self._carry_successor(r, tok)) is not None:
                         carried.append(nxt)
             else:
                 self._consume_coda(exited, toks, stage=False)

@@ -287,7 +287,8 @@ def pressure_main() -> None:
     under the default ``kv_pressure_mode="recompute"``: refill at 56 blocks (decoders stall and are
     restaged), 48 and 40 blocks (stalled decoders are preempted by soft reset and re-prefilled), and
     no-refill at 48 and 40 blocks; then both loops at 40 blocks under ``"reserve"`` admission
-    (``max_model_len`` 512), into ``ouro_cfg0_pressure.json``."""
+    (``max_model_len`` 512); then both loops at 48 and 40 blocks in the reference's default timing
+    (delayed gate consumption), into ``ouro_cfg0_pressure.json``."""
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     gold = json.loads((HERE / "ouro_cfg0.json").read_text())
@@ -311,6 +312,17 @@ def pressure_main() -> None:
         res["num_blocks"] = 40
         res["kv_pressure_mode"] = "reserve"
         res["max_model_len"] = 512
+        runs.append(res)
+    # the reference's default timing (delayed gate consumption) under recompute pressure
+    agold = json.loads((HERE / "ouro_cfg0_async.json").read_text())
+    for refill, nb in ((True, 48), (True, 40), (False, 48), (False, 40)):
+        tag = "refill" if refill else "norefill"
+        depths = next(r for r in agold["runs"] if r["name"] == f"replay_{tag}_async")["exit_depths"]
+        res, _ = run_case(
+            f"replay_{tag}_blocks{nb}_async", kv_policy="single", refill=refill, live_gate=False, exit_depths=depths,
+            num_blocks=nb, async_mode=True,
+        )
+        res["num_blocks"] = nb
         runs.append(res)
     prompts, max_new = config0_workload()
     payload = {

@@ -150,6 +150,10 @@ PRESSURE = [
     ("replay_norefill_blocks40", 1),
     ("replay_refill_reserve_blocks40", 0),
     ("replay_norefill_reserve_blocks40", 0),
+    ("replay_refill_blocks48_async", 4),
+    ("replay_refill_blocks40_async", 3),
+    ("replay_norefill_blocks48_async", 2),
+    ("replay_norefill_blocks40_async", 1),
 ]
 
 

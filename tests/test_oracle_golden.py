@@ -136,6 +136,10 @@ def test_oracle_reproduces_reference_early_finish_run(name):
         ("replay_norefill_blocks40", 1),
         ("replay_refill_reserve_blocks40", 0),
         ("replay_norefill_reserve_blocks40", 0),
+        ("replay_refill_blocks48_async", 4),
+        ("replay_refill_blocks40_async", 3),
+        ("replay_norefill_blocks48_async", 2),
+        ("replay_norefill_blocks40_async", 1),
     ],
 )
 def test_oracle_reproduces_reference_pressure_run(name, preemptions):
@@ -143,7 +147,9 @@ def test_oracle_reproduces_reference_pressure_run(name, preemptions):
     at the head of the next tick, and when nothing can run the stalled request with the shortest
     context is reset to prompt + generated text and re-queued, blocking new admissions until a
     request retires. Under reserve admission the same pool admits a prompt only while every
-    admitted request's worst-case blocks fit, and nothing is preempted."""
+    admitted request's worst-case blocks fit, and nothing is preempted. In the delayed timing a
+    wave's boundary coda is consumed during the next wave, so its finished requests hold their
+    blocks until then and a successor that found no block sits that wave out."""
 
     data, shape, sd = _load_ouro("ouro_cfg0_pressure.json")
     run = next(r for r in data["runs"] if r["name"] == name)
