@@ -439,8 +439,8 @@ def offload_main() -> None:
     ``num_cpu_blocks`` blocks and restored (admitted ahead of fresh prompts) once blocks free up;
     a victim that does not fit the host pool falls back to recompute. Host pools of 64 blocks
     (every victim fits), 2 and 1 (offload and recompute mixed), refill and no-refill; and under
-    ``last_exited`` (4 KV slots per layer, every slot's blocks swapped; no recompute fallback), into
-    ``ouro_cfg0_offload.json``.
+    ``last_exited`` (4 KV slots per layer, every slot's blocks swapped; no recompute fallback); and
+    both loops in the delayed (default) timing, into ``ouro_cfg0_offload.json``.
     The host pool is given in GiB, as the reference's config takes it: ``num_cpu_blocks`` times
     the bytes of one block over all cache layers (K and V) in the cache dtype."""
 
@@ -462,6 +462,19 @@ def offload_main() -> None:
             pressure_mode="offload", cpu_offload_space=cpu_blocks * block_bytes * slots / 1024**3,
         )
         assert res["stats"]["num_cpu_blocks"] == cpu_blocks, res["stats"]
+        res["num_blocks"] = nb
+        res["num_cpu_blocks"] = cpu_blocks
+        runs.append(res)
+    # the reference's default timing (delayed gate consumption)
+    agold = json.loads((HERE / "ouro_cfg0_async.json").read_text())
+    for refill, nb, cpu_blocks in ((True, 40, 2), (False, 40, 64)):
+        tag = "refill" if refill else "norefill"
+        depths = next(r for r in agold["runs"] if r["name"] == f"replay_{tag}_async")["exit_depths"]
+        res, _ = run_case(
+            f"replay_{tag}_blocks{nb}_host{cpu_blocks}_async", kv_policy="single", refill=refill, live_gate=False,
+            exit_depths=depths, num_blocks=nb, pressure_mode="offload", async_mode=True,
+            cpu_offload_space=cpu_blocks * block_bytes / 1024**3,
+        )
         res["num_blocks"] = nb
         res["num_cpu_blocks"] = cpu_blocks
         runs.append(res)

@@ -174,6 +174,8 @@ OFFLOAD_RUNS = [
     ("replay_norefill_blocks48_host2", (1, 1, 1)),
     ("replay_refill_blocks40_host64_last_exited", (0, 0, 0)),
     ("replay_norefill_blocks40_host64_last_exited", (0, 1, 1)),
+    ("replay_refill_blocks40_host2_async", (1, 2, 2)),
+    ("replay_norefill_blocks40_host64_async", (0, 1, 1)),
 ]
 
 
