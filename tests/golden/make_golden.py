@@ -265,6 +265,16 @@ def finish_main() -> None:
             eos_token_id=[363, 924], stop_sequences=[[314, 314], [585, 585]],
         )
         runs.append(res)
+    # the same in the delayed (default) timing, with the async replay depths
+    agold = json.loads((HERE / "ouro_cfg0_async.json").read_text())
+    for name, refill in (("replay_refill_eos_stop_async", True), ("replay_norefill_eos_stop_async", False)):
+        tag = "refill" if refill else "norefill"
+        adepths = next(r for r in agold["runs"] if r["name"] == f"replay_{tag}_async")["exit_depths"]
+        res, _ = run_case(
+            name, kv_policy="single", refill=refill, live_gate=False, exit_depths=adepths, async_mode=True,
+            eos_token_id=[363, 924], stop_sequences=[[314, 314], [585, 585]],
+        )
+        runs.append(res)
     prompts, max_new = config0_workload()
     payload = {
         "generator": "tests/golden/make_golden.py --finish",

@@ -358,6 +358,20 @@ def test_resident_cap_resolves_to_the_token_budget():
     assert (eng.max_num_seqs, eng.min_free, len(eng.free_slots)) == (48, 6, 48)
 
 
+@pytest.mark.parametrize("name", ["replay_refill_eos_stop_async", "replay_norefill_eos_stop_async"])
+def test_early_finish_lengths_in_delayed_timing(name):
+    """Early finishes in the delayed timing, teacher-forced on the reference's tokens: every request
+    ends where the reference's does (the launches differ by the successors the reference stages and
+    cancels)."""
+
+    data = _load("ouro_cfg0_finish.json")
+    run = next(r for r in data["runs"] if r["name"] == name)
+    _eng, outs = _run(
+        data, run, data["num_blocks"], forced=run["tokens"], eos=run["eos_token_id"], stops=run["stop_sequences"]
+    )
+    assert [len(o.generated_tokens) for o in outs] == [len(t) for t in run["tokens"]]
+
+
 def test_single_request_that_cannot_fit_raises():
     """With one active request left and no block for its next token, preemption cannot help: the
     reference raises ``CacheFullError`` (``continuous_api.py:1640-1646``)."""

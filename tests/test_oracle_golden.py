@@ -110,6 +110,23 @@ def test_oracle_reproduces_reference_kv_policy_run(golden_policies, name):
     assert engine.refills == run["stats"]["scheduler_refills"]
 
 
+@pytest.mark.parametrize("name", ["replay_refill_eos_stop_async", "replay_norefill_eos_stop_async"])
+def test_oracle_early_finish_tokens_in_delayed_timing(name):
+    """Early finishes in the delayed timing: the reference stages a successor before it knows the
+    token and cancels it once an EOS or stop sequence is consumed; this restatement reads the token
+    first and stages none. The generated tokens (the finishing ones included) are the reference's;
+    the launches differ from the first such finish on, by the cancelled item or its KV block."""
+
+    data, shape, sd = _load_ouro("ouro_cfg0_finish.json")
+    run = next(r for r in data["runs"] if r["name"] == name)
+    engine = OracleEngine(shape, sd, _config(run, data), torch.float32)
+    tokens = engine.generate(
+        data["prompts"], data["max_new_tokens"], exit_depths=run["exit_depths"], eos_token_ids=run["eos_token_id"],
+        stop_sequences=run["stop_sequences"],
+    )
+    assert tokens == run["tokens"]
+
+
 @pytest.mark.parametrize("name", ["replay_refill_eos_stop", "replay_norefill_eos_stop"])
 def test_oracle_reproduces_reference_early_finish_run(name):
     """Requests finishing on EOS ids (kept in the output) or on stop sequences, refill on and off."""
