@@ -323,6 +323,15 @@ def pressure_main() -> None:
         res["kv_pressure_mode"] = "reserve"
         res["max_model_len"] = 512
         runs.append(res)
+    # first_then_shared (step 0 in slot 0, later steps share slot 1) under recompute pressure
+    pgold = json.loads((HERE / "ouro_cfg0_policies.json").read_text())
+    pdepths = next(r for r in pgold["runs"] if r["name"] == "replay_first_then_shared")["exit_depths"]
+    res, _ = run_case(
+        "replay_first_then_shared_blocks40", kv_policy="first_then_shared", refill=True, live_gate=False,
+        exit_depths=pdepths, num_blocks=40,
+    )
+    res["num_blocks"] = 40
+    runs.append(res)
     # the reference's default timing (delayed gate consumption) under recompute pressure
     agold = json.loads((HERE / "ouro_cfg0_async.json").read_text())
     for refill, nb in ((True, 48), (True, 40), (False, 48), (False, 40)):

@@ -154,6 +154,7 @@ PRESSURE = [
     ("replay_refill_blocks40_async", 3),
     ("replay_norefill_blocks48_async", 2),
     ("replay_norefill_blocks40_async", 1),
+    ("replay_first_then_shared_blocks40", 3),
 ]
 
 

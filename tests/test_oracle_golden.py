@@ -157,6 +157,7 @@ def test_oracle_reproduces_reference_early_finish_run(name):
         ("replay_refill_blocks40_async", 3),
         ("replay_norefill_blocks48_async", 2),
         ("replay_norefill_blocks40_async", 1),
+        ("replay_first_then_shared_blocks40", 3),
     ],
 )
 def test_oracle_reproduces_reference_pressure_run(name, preemptions):
