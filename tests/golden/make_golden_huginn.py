@@ -143,6 +143,7 @@ def run_case(
             "generated_tokens": stats.generated_tokens,
             "scheduler_refills": stats.scheduler_refills,
             "exit_depth_histogram": {str(k): v for k, v in sorted(stats.exit_depth_histogram.items())},
+            "recompute_preemptions": getattr(engine.offloading_manager, "num_recompute_preemptions", 0),
         },
         "launches": rec.launches,
     }
@@ -199,5 +200,27 @@ def main() -> None:
         print(r["name"], r["stats"])
 
 
+def pressure_main() -> None:
+    """``--pressure``: the synchronous replay (refill on) in a 40-block pool, where stalled decoders
+    are soft-reset and re-prefilled through the prelude, core and coda cache layers, into
+    ``huginn_small_pressure.json``."""
+
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    gold = json.loads((HERE / "huginn_small.json").read_text())
+    depths = next(r for r in gold["runs"] if r["name"] == "replay_refill")["exit_depths"]
+    res, _ = run_case("replay_refill_blocks40", kv_policy="single", refill=True, live_gate=False,
+                      exit_depths=depths, num_blocks=40)
+    res["num_blocks"] = 40
+    prompts, max_new = config0_workload()
+    payload = {"generator": "tests/golden/make_golden_huginn.py --pressure", "shape": SMALL.__dict__,
+               "embed_std": EMBED_STD, "weights_seed": 0, "prompts": prompts, "max_new_tokens": max_new,
+               "block_size": 16, "runs": [res]}
+    (HERE / "huginn_small_pressure.json").write_text(json.dumps(payload, separators=(",", ":")))
+    print(res["name"], res["stats"])
+
+
 if __name__ == "__main__":
+    if "--pressure" in sys.argv[1:]:
+        pressure_main()
+        raise SystemExit(0)
     main()

@@ -276,6 +276,22 @@ def test_cb_oracle_reproduces_reference_run(name, preemptions):
             np.testing.assert_allclose(lg.numpy(), logits[f"{name}_{i}"], rtol=0, atol=1e-5)
 
 
+def test_oracle_reproduces_reference_huginn_pressure_run():
+    """Huginn in a 40-block pool under recompute: stalled decoders are soft-reset and re-prefilled
+    through the prelude, core and coda cache layers; tokens and launches equal the reference's."""
+
+    data, shape, sd = _load_huginn("huginn_small_pressure.json")
+    run = data["runs"][0]
+    cfg = OracleConfig(
+        block_size=16, num_blocks=run["num_blocks"], max_recurrent_steps=shape.total_recurrent_steps,
+        max_model_len=2048, synthetic_exit_replay=True, refill=True, kv_policy="single",
+    )
+    engine = OracleEngine(shape, sd, cfg, torch.float32)
+    assert engine.generate(data["prompts"], data["max_new_tokens"], exit_depths=run["exit_depths"]) == run["tokens"]
+    assert engine.launches == run["launches"]
+    assert engine.stats["recompute_preemptions"] == run["stats"]["recompute_preemptions"] > 0
+
+
 @pytest.mark.parametrize("name", ["cb_async", "cb_sync"])
 def test_cb_oracle_reproduces_reference_huginn_run(name):
     """The CB baseline on the small Huginn shape (every recurrent step on its own KV slot, as the
