@@ -59,7 +59,6 @@ def parse() -> argparse.Namespace:
     p.add_argument("--requests", type=int, default=256)
     p.add_argument("--out-cap", type=int, default=1024, help="cap on output lengths (smaller = profiling case)")
     p.add_argument("--no-graph", action="store_true")
-    p.add_argument("--gemm", default="cublas", choices=["tcgen05", "cublas"], help="dense GEMM backend")
     p.add_argument("--lm-head", default="fused", choices=["fused", "gemm"],
                    help="LM head + argmax as one tcgen05 GEMM (fused) or a GEMM then an argmax kernel")
     p.add_argument("--num-blocks", type=int, default=16384, help="KV pool blocks (small for profiler captures)")
@@ -169,7 +168,7 @@ def build_engine(args, device):
         max_num_seqs=256,
     )
     eng = ContinuousDepthBatchingEngine.from_model(
-        model, cfg, device=device, gemm_backend=args.gemm, fused_lm_head=getattr(args, "lm_head", "fused") == "fused"
+        model, cfg, device=device, fused_lm_head=getattr(args, "lm_head", "fused") == "fused"
     )
     del model
     return eng, shape
@@ -392,7 +391,7 @@ def run_b200(args) -> None:
                 "exit_depth_histogram": {str(k): v for k, v in sorted(stats.exit_depth_histogram.items())},
                 "l2": "inputs larger than L2 (KV cache tens of GB, weights 2.5 GB)",
                 "cuda_graphs": not args.no_graph,
-                "gemm_backend": args.gemm,
+                "gemm": "libcdb stream-K tcgen05 (projections, fused SwiGLU, fused LM head + argmax)",
                 "lm_head": args.lm_head,
                 "parallelism": f"{world} independent request-sharded replicas (no collective)",
             },
@@ -547,8 +546,7 @@ def run_cb(args) -> None:
         max_model_len=4096, max_num_seqs=256,
     )
     eng = ContinuousBatchingEngine.from_model(
-        model, cfg, device=device, kv_policy="single", gemm_backend=args.gemm,
-        fused_lm_head=getattr(args, "lm_head", "fused") == "fused",
+        model, cfg, device=device, kv_policy="single", fused_lm_head=getattr(args, "lm_head", "fused") == "fused",
     )
     del model
     prompts, max_new, _depths = workload(replica_seed(args.seed, rank), args.requests, args.out_cap)
@@ -584,7 +582,7 @@ def run_cb(args) -> None:
         "dtype": "bf16",
         "data": "synthetic (the CDB line's seeded requests; every token at full depth)",
         "config": {"workload": "BASELINE config 1 requests, full-depth CB baseline", "requests": args.requests,
-                   "kv_policy": "single", "gemm": args.gemm, "use_async_batching": True},
+                   "kv_policy": "single", "use_async_batching": True},
         "batches": {"prefill": st.prefill_batches, "decode": st.decode_batches,
                     "mean_decode_batch": round(st.mean_decode_batch_size, 1)},
         "clocks": clocks.summary(),

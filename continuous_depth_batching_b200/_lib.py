@@ -45,7 +45,9 @@ _SIGNATURES: dict[str, list] = {
     ],
     "cdb_mlp_gateup_silu_gemm": [
         c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,  # x, ldx, w_gate_up, ldw, act, ld_act
-        c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,  # M, inter, K, splits, num_sms, status, stream
+        c_int, c_int, c_int, c_int,  # M, inter, K, max_ctas
+        c_void_p, c_int64, c_void_p, c_int,  # workspace, workspace_elems, counters, num_counters
+        c_int, c_void_p, c_void_p,  # num_sms, status, stream
     ],
     "cdb_attn_scratch_bytes": [c_int, c_int, c_int],
     "cdb_rope_append_kv": [
@@ -62,9 +64,11 @@ _SIGNATURES: dict[str, list] = {
         c_int, c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_void_p,
     ],
     "cdb_gemm_workspace_elems": [c_int, c_int, c_int, c_int],
+    "cdb_gemm_counter_elems": [c_int, c_int, c_int],
     "cdb_lm_head_argmax": [
         c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_int,  # x, ldx, w, ldw, M, vocab, K
         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,  # out_ids, out_rows, token_rows, table, keys, done
+        c_void_p, c_int64, c_void_p, c_int,  # workspace, workspace_elems, counters, num_counters
         c_int, c_void_p, c_void_p,  # num_sms, status, stream
     ],
     "cdb_rmsnorm": [
@@ -101,15 +105,16 @@ _SIGNATURES: dict[str, list] = {
     "cdb_qkv_rope_append_gemm": [
         c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int, c_int, c_void_p, c_int,
         c_int64, c_int, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int,
-        c_int, c_int, c_void_p, c_void_p,
+        c_int, c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_void_p,
     ],
     "cdb_o_proj_residual_norm_gemm": [
         c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
-        c_int64, c_int, c_int, c_int, c_float, c_int, c_void_p, c_void_p,
+        c_int64, c_int, c_int, c_int, c_float, c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_void_p,
     ],
     "cdb_down_residual_norm_gemm": [
         c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
-        c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_int, c_void_p, c_void_p,
+        c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_void_p, c_int64, c_void_p,
+        c_int, c_int, c_void_p, c_void_p,
     ],
     "cdb_schedule_tick": [
         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int,
@@ -126,7 +131,8 @@ _SIGNATURES: dict[str, list] = {
         c_void_p, c_void_p, c_void_p,
     ],
 }
-_RESTYPES = {"cdb_status_string": ctypes.c_char_p, "cdb_attn_scratch_bytes": c_int64, "cdb_gemm_workspace_elems": c_int64}
+_RESTYPES = {"cdb_status_string": ctypes.c_char_p, "cdb_attn_scratch_bytes": c_int64, "cdb_gemm_workspace_elems": c_int64,
+              "cdb_gemm_counter_elems": c_int}
 
 _LIB: ctypes.CDLL | None = None
 
@@ -177,7 +183,8 @@ def stream_ptr(stream: torch.cuda.Stream | None = None) -> int:
 
 
 _NO_LAUNCH = {
-    "cdb_version", "cdb_status_string", "cdb_attn_scratch_bytes", "cdb_gemm_workspace_elems", "cdb_schedule_queues_init",
+    "cdb_version", "cdb_status_string", "cdb_attn_scratch_bytes", "cdb_gemm_workspace_elems", "cdb_gemm_counter_elems",
+    "cdb_schedule_queues_init",
     "cdb_kv_blocks_host_copy",
 }
 # Kernels enqueued through this binding (device work only; graph replays are counted by the runner).
@@ -189,3 +196,22 @@ def call(name: str, *args) -> None:
     check(getattr(load(), name)(*args), name)
     if name not in _NO_LAUNCH:
         launch_count += 1
+
+
+class GemmWorkspace:
+    """Split-partial workspace and tile counters of the stream-K GEMM entry points
+    (``cdb_gemm_bf16``, ``cdb_mlp_gateup_silu_gemm``, ``cdb_lm_head_argmax``), sized for every
+    problem of up to ``max_tokens`` token rows and ``max_n`` output columns on ``num_sms`` CTAs.
+    Calls sharing one workspace must be ordered (one stream); the counters stay zeroed between
+    calls."""
+
+    def __init__(self, device: torch.device, max_tokens: int, max_n: int, num_sms: int) -> None:
+        bn = 256
+        self.ws = torch.zeros(2 * num_sms * 128 * bn, dtype=torch.float32, device=device)
+        tiles = -(-max_n // 128) * max(1, -(-max_tokens // bn))
+        self.ctr = torch.zeros(tiles, dtype=torch.int32, device=device)
+
+    def args(self) -> tuple:
+        """(workspace, workspace_elems, counters, num_counters) as the entry points take them."""
+
+        return ptr(self.ws), self.ws.numel(), ptr(self.ctr), self.ctr.numel()

@@ -118,7 +118,6 @@ class ContinuousBatchingEngine(ContinuousDepthBatchingEngine):
         dtype: torch.dtype | None = None,
         device: torch.device | str | None = None,
         kv_policy: str | None = None,
-        gemm_backend: str = "cublas",
         fused_lm_head: bool = True,
     ) -> ContinuousBatchingEngine:
         """Build the engine for an Ouro or Huginn causal LM (reference parameter names).
@@ -152,9 +151,7 @@ class ContinuousBatchingEngine(ContinuousDepthBatchingEngine):
             kv_pressure_mode=cb_config.kv_pressure_mode,
             cpu_offload_space=cb_config.cpu_offload_space,
         )
-        eng = super().from_model(
-            model, cdb, dtype=dtype, device=device, gemm_backend=gemm_backend, fused_lm_head=fused_lm_head
-        )
+        eng = super().from_model(model, cdb, dtype=dtype, device=device, fused_lm_head=fused_lm_head)
         eng.cb_config = cb_config
         return eng
 

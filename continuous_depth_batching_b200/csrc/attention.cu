@@ -341,8 +341,15 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
         const int my = base + lane < b1 ? bt[base + lane] : 0;
         const int cnt = min(32, b1 - base);
         for (int i = 0; i < cnt; ++i) {
-          const int block_id = __shfl_sync(0xffffffffu, my, i);
+          int block_id = __shfl_sync(0xffffffffu, my, i);
           if (lane == 0) {
+            // A block id outside the pool (a -1 hole in the table or a stale id) is recorded
+            // and page 0 is staged in its place, so the ring keeps its order; the output of
+            // that row is then not meaningful and the status word says so.
+            if (block_id < 0 || (int64_t)(block_id + 1) * kBlock > p.kv_rows) {
+              set_error(p.status, CDB_ERR_INDEX);
+              block_id = 0;
+            }
             if (mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
               mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
               uint8_t* dst = smem + stage * C::STAGE_BYTES;
@@ -1201,7 +1208,10 @@ extern "C" int cdb_paged_decode_attn_append_static(void* qkv, int64_t qkv_stride
                             num_items, num_heads, head_dim, status, st);
     if (rc != CDB_OK) return rc;
   }
+  // One plan chunk per attention CTA; the plan holds at most CDB_ATTN_PLAN_MAX_CHUNKS chunks, so
+  // the grid is clamped to that too (a wider grid would only add CTAs without work).
   if (num_ctas <= 0) num_ctas = 2 * 148;
+  num_ctas = num_ctas < kMaxPlanChunks ? num_ctas : kMaxPlanChunks;
   if (launch_pdl(attn_plan_kernel, dim3(1), dim3(1024), 0, st, item_pos, num_items, num_heads / hg, kMaxUnits,
                  scratch_items, num_ctas, header, static_cast<int4*>(units)) != cudaSuccess)
     return CDB_ERR_CUDA;
@@ -1235,7 +1245,6 @@ extern "C" int cdb_paged_decode_attn_append_static(void* qkv, int64_t qkv_stride
   p.kv = static_cast<__nv_bfloat16*>(kv_base);
   p.k_col = k_col;
   p.v_col = v_col;
-  if (num_ctas <= 0) num_ctas = 2 * 148;
   if (head_dim == 128) return launch_attn<128, 4>(map, p, num_ctas, st);
   if (head_dim == 64) return launch_attn<64, 4>(map, p, num_ctas, st);
   if (head_dim == 96) return launch_attn<96, 5>(map, p, num_ctas, st);

@@ -1,23 +1,38 @@
 // bf16 tensor-core GEMM for sm_100a on tcgen05/TMEM: C[M,N] = X[M,K] * W[N,K]^T.
 //
-// Decode-shaped problems have few token rows (M <= 256) and wide weights (N up to 49152), so
-// the weight is the MMA "A" operand (128 weight rows per tile, UMMA M=128) and the token rows
-// are the MMA "B" operand (UMMA N = BN in {32,64,128,256}); the fp32 accumulator lives in
-// tensor memory as [128 lanes = weight rows] x [BN columns = token rows].
+// Orientation. Decode-shaped problems have few token rows (M <= 256) and wide weights (N up to
+// 65536), so the weight is the MMA "A" operand (128 weight rows per tile, UMMA M = 128) and the
+// token rows are the MMA "B" operand (UMMA N = BN, M rounded up to 16, at most 256); the fp32
+// accumulator lives in tensor memory as [128 lanes = weight rows] x [BN columns = token rows].
+// Prefill-shaped problems tile the tokens by 256.
 //
-// One CTA = one (weight tile, token tile, K split), warp specialised:
-//   warp 0      TMA producer: 2-D tile loads of W[128 x 64] and X[BN x 64] (128-byte swizzle)
-//               into a STAGES-deep ring, completion on "full" mbarriers;
-//   warp 1      allocates TMEM and issues tcgen05.mma (one elected thread), releasing each
-//               stage with tcgen05.commit onto its "empty" mbarrier;
-//   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp reads its 32-lane quarter)
-//               into an fp32 tile in the drained stage ring.
-// Split-K (for the projections whose weight tiles cannot fill 148 SMs otherwise) keeps the
-// splits of one tile in one thread-block cluster (grid z = cluster z = splits <= 8): after a
-// cluster barrier every CTA reduces one slice of the tile from all ranks' shared memory
-// (distributed shared memory loads, rank order, so the sum is deterministic) and stores it as
-// bf16 with 8-byte vector stores. No global partials, counters or second pass.
-#include <cooperative_groups.h>
+// Work split (stream-K). The launch has G = min(#SMs, iterations) CTAs, one per SM. The
+// iteration space - every (output tile, 64-wide k block) pair, tiles in token-major order - is
+// cut into G equal contiguous ranges, so every SM streams the same number of weight bytes
+// whatever the tile count (a decode projection has 16-88 weight tiles for 148 SMs; one SM alone
+// streams only ~40 GB/s from HBM, so all of them must). A CTA's range covers the tail of one tile,
+// whole tiles and the head of another; a tile covered by one CTA is stored directly, a tile split
+// over CTAs is combined deterministically: every piece writes its fp32 partial to the caller's
+// workspace and bumps the tile's counter; the piece that arrives last sums all pieces in k order
+// (so the result does not depend on arrival order), applies the epilogue and resets the counter.
+// No CTA ever waits on another.
+//
+// Warp roles (224 threads, one CTA per SM):
+//   warp 0      weight producer: 2-D TMA tile loads W[128 x 64] (128-byte swizzle) into an SW-deep
+//               ring. Weights do not depend on the previous kernel, so this warp never waits for
+//               it: with programmatic dependent launch the weight stream starts while the
+//               predecessor is still finishing.
+//   warp 1      activation producer: waits for the predecessor (griddepcontrol.wait), then loads
+//               X[BN x 64] tiles into an SX-deep ring.
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp its 32-lane quarter) and store,
+//               or write/combine split partials.
+//   warp 6      allocates TMEM (two accumulator buffers, so the epilogue of one tile overlaps
+//               the main loop of the next) and issues tcgen05.mma from one thread.
+// Epilogues: 0 stores bf16(C); 1 (SwiGLU) reads weight rows as gate/up pairs and stores
+// bf16(bf16(silu(bf16(g))) * bf16(u)); 2 (LM head + greedy argmax) stores no logits and folds
+// each token's argmax into a 64-bit atomicMax key, the last CTA writing the token ids.
+// Every wait is bounded; a wait that runs out records CDB_ERR_DEVICE_TIMEOUT and the CTA winds
+// down (no CTA waits on another CTA, so nothing can hang on a peer).
 #include <cuda.h>
 
 #include <cstring>
@@ -31,45 +46,54 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle atom of bf16
-constexpr int THREADS = 192;
-constexpr int kMaxClusterSplits = 8;  // portable cluster size
+constexpr int W_BYTES = BM * BK * 2;
+constexpr int THREADS = 7 * 32;
+constexpr int kWarpW = 0, kWarpX = 1, kWarpMma = 6;
+constexpr int kEpiThreads = 128;
+constexpr int kSmemBudget = 200 * 1024;
 
-// Token-tile widths of at most 128 run two CTAs per SM (stage ring within ~110 KB), wider ones one
-// (ring within ~220 KB); the ring depth follows from the stage size, capped at 8.
-constexpr int ctas_per_sm_for(int bn) { return bn <= 128 ? 2 : 1; }
-constexpr int stages_for(int bn) {
-  const int stage = BM * BK * 2 + bn * BK * 2;
-  const int budget = (bn <= 128 ? 110 : 220) * 1024;
-  return budget / stage < 8 ? budget / stage : 8;
-}
+constexpr int cmin(int a, int b) { return a < b ? a : b; }
+constexpr int cmax(int a, int b) { return a > b ? a : b; }
+constexpr int pow2_at_least(int v) { return v <= 32 ? 32 : v <= 64 ? 64 : v <= 128 ? 128 : 256; }
 
-template <int BN, int STAGES>
+template <int BN>
 struct Cfg {
-  static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
-  // tcgen05.alloc takes a power of two >= 32 columns
-  static constexpr uint32_t TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr int X_BYTES = BN * BK * 2;
+  // Rings: wide token tiles split the budget evenly (prefill is MMA-bound and needs both operands
+  // deep); narrow ones keep a short activation ring (L2-resident X) and give the rest to weights.
+  static constexpr int SX = BN >= 128 ? kSmemBudget / (W_BYTES + X_BYTES) : cmax(3, cmin(8, 64 * 1024 / X_BYTES));
+  static constexpr int SW = BN >= 128 ? SX : cmin(12, (kSmemBudget - SX * X_BYTES) / W_BYTES);
+  static constexpr int ACC_STRIDE = pow2_at_least(BN);  // TMEM columns per accumulator buffer
+  static constexpr uint32_t TMEM_COLS = 2 * ACC_STRIDE;
+  static constexpr int CHUNKS = (BN + 31) / 32;
+  static constexpr int OFF_X = SW * W_BYTES;
+  static constexpr int OFF_BAR = OFF_X + SX * X_BYTES;
+  static constexpr int NBAR = 2 * SW + 2 * SX + 5;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int OFF_KEYS = (OFF_MISC + 64 + 7) / 8 * 8;  // argmax: [4 warps][32] keys
+  static constexpr int SMEM = OFF_KEYS + 4 * 32 * 8 + 1024;     // + alignment slack
   // kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both K-major, M=128, N=BN.
   static constexpr uint32_t IDESC =
       (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
-  static_assert(BN * BM * 4 <= STAGES * STAGE_BYTES, "fp32 partial tile must fit in the stage ring");
+  static_assert(SX >= 2 && SW >= 2, "rings");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(X_BYTES % 1024 == 0, "swizzled X stages stay 1024-byte aligned");
 };
 
 struct Params {
   __nv_bfloat16* c;
   int64_t ldc;
   int M, N, K;
-  int splits, kb_per_split, num_kb;  // splits == cluster size along z
-  int vec_store;                     // c 8-byte aligned and ldc % 4 == 0
+  int tiles_w, tiles_tok, kb;  // weight tiles, token tiles, k blocks per tile
+  long long iters;             // tiles * kb
+  float* ws;                   // split partials: [2 * G][BM * BN] fp32
+  int32_t* ctr;                // per-tile arrival counters (zero between calls)
+  int pair_store;              // EPI 0: c 4-byte aligned, ldc and N even
   int32_t* status;
-  // EPI 2 (LM head + argmax): per-token running keys, completion counter, outputs
+  // EPI 2 (LM head + argmax)
   unsigned long long* keys;
   int32_t* done;
-  int total_ctas;
   int64_t* out_ids;
   const int32_t* out_rows;
   const int32_t* token_rows;
@@ -77,7 +101,7 @@ struct Params {
 };
 
 // Orderable 64-bit key of (bf16 logit v, vocab index n): larger v wins, then the smaller index
-// (torch.argmax returns the first maximum).
+// (torch.argmax returns the first maximum). 0 is below every real key.
 __device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
   const uint32_t b = __float_as_uint(v);
   const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
@@ -128,7 +152,8 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -139,41 +164,157 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-// EPI 0: store c[m, n] = bf16(acc). EPI 1 (SwiGLU): weight rows are gate/up pairs
-// (row 2j = gate_j, row 2j+1 = up_j) and c[m, j] = bf16(bf16(silu(bf16(g))) * bf16(u)), the
-// rounding of OuroMLP's act_fn(gate_proj(x)) * up_proj(x) in bf16. EPI 2 (LM head + greedy
-// argmax, unsplit): no logits are stored; each token's argmax over the bf16 logits of the tile's
-// vocab rows is folded into keys[m] with atomicMax, and the last CTA writes the token ids.
-template <int BN, int STAGES, int EPI>
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"r"(kEpiThreads) : "memory"); }
+
+__device__ __forceinline__ float4 ld_cg_f4(const float4* p) {
+  float4 v;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+
+// Bounded mbarrier wait that also gives up once another role of the CTA has given up.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int32_t* status, volatile int* abort) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && *abort) return false;
+  }
+  set_error(status, CDB_ERR_DEVICE_TIMEOUT);
+  *abort = 1;
+  return false;
+}
+
+// Iteration range start of CTA g, and the CTA whose range holds iteration x.
+__device__ __forceinline__ long long range_start(long long iters, int G, int g) { return iters * g / G; }
+__device__ __forceinline__ int cta_of(long long iters, int G, long long x) { return (int)(((x + 1) * G - 1) / iters); }
+
+// Workspace slot of CTA g's piece of tile t: its first piece (the range starts inside tile t) or
+// its last one. Slot layout: float4 index (chunk * 8 + j / 4) * BM + row holds tokens j..j+3 of
+// the chunk for one weight row, so a warp moves 512 contiguous bytes per access.
+__device__ __forceinline__ int piece_slot(long long iters, int G, int g, long long tile_begin) {
+  return range_start(iters, G, g) >= tile_begin ? 2 * g : 2 * g + 1;
+}
+
+// Store one 32-token chunk of a finished tile: row n of the tile (this thread's TMEM lane), tokens
+// m0 .. m0 + 31 (in-tile columns col0 .. col0 + 31, valid below BN).
+template <int BN, int EPI>
+__device__ __forceinline__ void store_chunk(const Params& p, const float (&v)[32], int n, int m0, int col0, int lane,
+                                            unsigned long long* s_keys, int q) {
+  if constexpr (EPI == 0) {
+    if (p.pair_store) {
+      const bool even = (lane & 1) == 0;
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        const float a = v[j], b = v[j + 1];
+        const float pa = __shfl_xor_sync(0xffffffffu, a, 1);
+        const float pb = __shfl_xor_sync(0xffffffffu, b, 1);
+        const int jj = even ? j : j + 1;
+        const int tok = m0 + jj;
+        const int col = even ? n : n - 1;
+        if (col0 + jj < BN && tok < p.M && col < p.N)
+          *reinterpret_cast<uint32_t*>(p.c + (int64_t)tok * p.ldc + col) = even ? pack_bf16x2(a, pa) : pack_bf16x2(pb, b);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int tok = m0 + j;
+        if (col0 + j < BN && tok < p.M && n < p.N) p.c[(int64_t)tok * p.ldc + n] = f_to_bf16(v[j]);
+      }
+    }
+  } else if constexpr (EPI == 1) {
+    // rows (2i, 2i+1) = (gate_i, up_i) sit on lanes (2l, 2l+1); the even lane stores act[tok][i]
+    const bool even = (lane & 1) == 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float other = __shfl_xor_sync(0xffffffffu, v[j], 1);
+      const int tok = m0 + j;
+      if (even && col0 + j < BN && tok < p.M && n < p.N) {
+        const float g = round_bf16(v[j]), u = round_bf16(other);
+        const float s = round_bf16(g / (1.f + expf(-g)));
+        p.c[(int64_t)tok * p.ldc + n / 2] = f_to_bf16(s * u);
+      }
+    }
+  } else {
+    // Transpose-reduce: after 5 butterfly stages lane l holds the best key of chunk token l over
+    // the warp's 32 rows; the 4 epilogue warps then meet in shared memory.
+    unsigned long long k[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const bool ok = col0 + j < BN && m0 + j < p.M && n < p.N;
+      k[j] = ok ? argmax_key(round_bf16(v[j]), n) : 0ull;
+    }
+#pragma unroll
+    for (int h = 16; h >= 1; h >>= 1) {
+      const bool upper = (lane & h) != 0;
+#pragma unroll
+      for (int i = 0; i < h; ++i) {
+        const unsigned long long keep = upper ? k[i + h] : k[i];
+        const unsigned long long send = upper ? k[i] : k[i + h];
+        const unsigned long long got = __shfl_xor_sync(0xffffffffu, send, h);
+        k[i] = keep > got ? keep : got;
+      }
+    }
+    s_keys[q * 32 + lane] = k[0];
+    epi_bar();
+    if (q == 0) {
+      unsigned long long best = s_keys[lane];
+#pragma unroll
+      for (int w = 1; w < 4; ++w) best = s_keys[w * 32 + lane] > best ? s_keys[w * 32 + lane] : best;
+      if (best != 0ull && col0 + lane < BN && m0 + lane < p.M) atomicMax(p.keys + m0 + lane, best);
+    }
+    epi_bar();
+  }
+}
+
+template <int BN, int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, Params p) {
-  using C = Cfg<BN, STAGES>;
+  using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* accum = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-  float* red = reinterpret_cast<float*>(smem);  // [BN][BM] fp32 partial tile, after the mainloop
-  cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
+  uint8_t* wring = smem;
+  uint8_t* xring = smem + C::OFF_X;
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* wempty = wfull + C::SW;
+  uint64_t* xfull = wempty + C::SW;
+  uint64_t* xempty = xfull + C::SX;
+  uint64_t* afull = xempty + C::SX;
+  uint64_t* aempty = afull + 2;
+  uint64_t* mdrain = aempty + 2;  // the MMA issuer's last commit: every MMA done before TMEM is freed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
+  volatile int* s_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 16);
+  unsigned long long* s_keys = reinterpret_cast<unsigned long long*>(smem + C::OFF_KEYS);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int wtile = blockIdx.x, mtile = blockIdx.y, split = blockIdx.z;
-  const int kb0 = split * p.kb_per_split;
-  const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
+  const int G = gridDim.x;
+  const int g = blockIdx.x;
+  const long long it0 = range_start(p.iters, G, g);
+  const long long it1 = range_start(p.iters, G, g + 1);
+  const int kb = p.kb;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < C::SW; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int s = 0; s < C::SX; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&afull[b], 1);
+      mbar_init(&aempty[b], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(mdrain, 1);
+    *s_abort = 0;
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -182,201 +323,193 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_trigger();
-  if (warp != 0) pdl_wait();  // the producer waits after prefetching weights
 
-  if (warp == 0) {
+  if (warp == kWarpW) {
+    // ------------------------------------------------------------ weight producer
     if (lane == 0) {
       prefetch_tensormap(&map_w);
-      prefetch_tensormap(&map_x);
-      // Weights do not depend on the previous kernel: fill the first stages' weight tiles
-      // before waiting on it, then add the activation tiles.
-      const int npre = min(STAGES, kb1 - kb0);
-      for (int i = 0; i < npre; ++i) {
-        mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
-        tma_load_2d(smem + i * C::STAGE_BYTES, &map_w, &full[i], (kb0 + i) * BK, wtile * BM);
+      long long i = 0;
+      for (long long it = it0; it < it1; ++it, ++i) {
+        const int t = (int)(it / kb), k = (int)(it % kb);
+        const int wt = t % p.tiles_w;
+        const int s = (int)(i % C::SW);
+        if (!wait_or_abort(&wempty[s], (uint32_t)(((i / C::SW) & 1) ^ 1), p.status, s_abort)) break;
+        mbar_arrive_expect_tx(&wfull[s], W_BYTES);
+        tma_load_2d(wring + s * W_BYTES, &map_w, &wfull[s], k * BK, wt * BM);
       }
-      pdl_wait();
-      for (int i = 0; i < npre; ++i)
-        tma_load_2d(smem + i * C::STAGE_BYTES + C::A_BYTES, &map_x, &full[i], (kb0 + i) * BK, mtile * BN);
-      int stage = npre % STAGES;
-      uint32_t phase = (npre == STAGES) ? 1u : 0u;
-      int issued = npre;
-      for (int kb = kb0 + npre; kb < kb1; ++kb) {
-        if (!mbar_wait(&empty[stage], phase ^ 1u, p.status)) break;
-        uint8_t* a = smem + stage * C::STAGE_BYTES;
-        mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-        tma_load_2d(a, &map_w, &full[stage], kb * BK, wtile * BM);
-        tma_load_2d(a + C::A_BYTES, &map_x, &full[stage], kb * BK, mtile * BN);
-        ++issued;
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-      // Load j lands in stage j % STAGES and completes that barrier's phase of parity
-      // (j / STAGES) & 1. Wait (bounded) for the last load of every stage, so that no copy is
-      // still in flight when the ring is reused for the partial tile or the CTA exits.
-      for (int j = max(0, issued - STAGES); j < issued; ++j)
-        mbar_wait(&full[j % STAGES], (uint32_t)((j / STAGES) & 1), p.status);
+      // no copy may still be in flight when the CTA exits (bounded waits that ignore an abort)
+      for (long long j = (i > C::SW ? i - C::SW : 0); j < i; ++j)
+        mbar_wait(&wfull[j % C::SW], (uint32_t)((j / C::SW) & 1), p.status);
     }
-  } else if (warp == 1) {
+  } else if (warp == kWarpX) {
+    // ------------------------------------------------------------ activation producer
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait(&full[stage], phase, p.status)) break;
-        tc_fence_after();
-        const uint32_t a = smem_u32(smem + stage * C::STAGE_BYTES);
-        const uint32_t b = a + C::A_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          umma_bf16(tmem, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), C::IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(&empty[stage]);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
+      prefetch_tensormap(&map_x);
+      pdl_wait();
+      long long i = 0;
+      for (long long it = it0; it < it1; ++it, ++i) {
+        const int t = (int)(it / kb), k = (int)(it % kb);
+        const int tt = t / p.tiles_w;
+        const int s = (int)(i % C::SX);
+        if (!wait_or_abort(&xempty[s], (uint32_t)(((i / C::SX) & 1) ^ 1), p.status, s_abort)) break;
+        mbar_arrive_expect_tx(&xfull[s], C::X_BYTES);
+        tma_load_2d(xring + s * C::X_BYTES, &map_x, &xfull[s], k * BK, tt * BN);
       }
-      umma_commit(accum);
+      for (long long j = (i > C::SX ? i - C::SX : 0); j < i; ++j)
+        mbar_wait(&xfull[j % C::SX], (uint32_t)((j / C::SX) & 1), p.status);
+    }
+  } else if (warp == kWarpMma) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      long long i = 0;
+      int seg = 0;
+      bool ok = true;
+      for (long long it = it0; it < it1 && ok; ++seg) {
+        const long long t = it / kb;
+        const long long seg_end = (t + 1) * kb < it1 ? (t + 1) * kb : it1;
+        const int buf = seg & 1;
+        if (!wait_or_abort(&aempty[buf], (uint32_t)(((seg >> 1) & 1) ^ 1), p.status, s_abort)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * C::ACC_STRIDE);
+        for (bool first = true; it < seg_end; ++it, ++i, first = false) {
+          const int ws = (int)(i % C::SW), xs = (int)(i % C::SX);
+          if (!wait_or_abort(&wfull[ws], (uint32_t)((i / C::SW) & 1), p.status, s_abort) ||
+              !wait_or_abort(&xfull[xs], (uint32_t)((i / C::SX) & 1), p.status, s_abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(wring + ws * W_BYTES);
+          const uint32_t b = smem_u32(xring + xs * C::X_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_bf16(d, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), C::IDESC, (!first || kk > 0) ? 1u : 0u);
+          umma_commit(&wempty[ws]);
+          umma_commit(&xempty[xs]);
+        }
+        if (ok) umma_commit(&afull[buf]);
+      }
+      // On every path (an abandoned wait included) no MMA may still run when TMEM is freed.
+      umma_commit(mdrain);
+      mbar_wait(mdrain, 0, p.status);
     }
     __syncwarp();
-  }
-  // The producer's loads have all landed and the MMA warp has issued its final commit.
-  __syncthreads();
-  if (warp >= 2) {
-    // ------------------------------------------------------------------ epilogue (warps 2..5)
-    // TMEM -> this CTA's fp32 partial tile red[token][weight row] in the stage ring, which is
-    // free once the accumulator barrier fires (every MMA, the ring's only reader, completed).
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const bool ok = mbar_wait(accum, 0, p.status);
-    tc_fence_after();
-    if (ok) {
+    const int et = threadIdx.x - 64;
+    const int row = q * 32 + lane;
+    pdl_wait();  // outputs, workspace and counters may still be in use by the predecessor
+    int seg = 0;
+    for (long long it = it0; it < it1; ++seg) {
+      const long long t = it / kb;
+      const long long tile_begin = t * kb;
+      const long long seg_end = (t + 1) * kb < it1 ? (t + 1) * kb : it1;
+      const bool full = it == tile_begin && seg_end == tile_begin + kb;
+      it = seg_end;
+      const int buf = seg & 1;
+      if (et == 0) *s_flag = wait_or_abort(&afull[buf], (uint32_t)((seg >> 1) & 1), p.status, s_abort) ? 1 : 0;
+      epi_bar();
+      if (!*s_flag) break;
+      epi_bar();  // everyone has read the flag before it is reused
+      tc_fence_after();
+      const int wt = (int)(t % p.tiles_w), tt = (int)(t / p.tiles_w);
+      const int n = wt * BM + row;
+      const int mbase = tt * BN;
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * C::ACC_STRIDE);
+      if (full) {
+        // Whole tile in this CTA: store chunk by chunk, then release the buffer (the MMA warp
+        // meanwhile fills the other one).
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, r);
+        for (int c = 0; c < C::CHUNKS; ++c) {
+          float v[32];
+          tmem_ld32(taddr + c * 32, v);
+          store_chunk<BN, EPI>(p, v, n, mbase + c * 32, c * 32, lane, s_keys, q);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&aempty[buf]);
+        continue;
+      }
+      // Split tile: publish this piece, then the last piece to arrive combines.
+      float4* mine = reinterpret_cast<float4*>(p.ws + (size_t)piece_slot(p.iters, G, g, tile_begin) * (BM * BN));
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c0 + j < BN) red[(c0 + j) * BM + q * 32 + lane] = __uint_as_float(r[j]);
+      for (int c = 0; c < C::CHUNKS; ++c) {
+        float v[32];
+        tmem_ld32(taddr + c * 32, v);
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4)
+          if (c * 32 + j4 * 4 < BN) mine[(c * 8 + j4) * BM + row] = make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&aempty[buf]);
+      const int ga = cta_of(p.iters, G, tile_begin);
+      const int gb = cta_of(p.iters, G, tile_begin + kb - 1);
+      __threadfence();
+      epi_bar();
+      if (et == 0) {
+        const int old = atomicAdd(p.ctr + t, 1);
+        *s_flag = old == gb - ga;
+        if (old == gb - ga) p.ctr[t] = 0;  // every piece has arrived: ready for the next call
+      }
+      epi_bar();
+      const bool last = *s_flag;
+      epi_bar();
+      if (!last) continue;
+      __threadfence();
+#pragma unroll 1
+      for (int c = 0; c < C::CHUNKS; ++c) {
+        float4 acc[8];
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) acc[j4] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int gg = ga; gg <= gb; ++gg) {
+          const float4* src = reinterpret_cast<const float4*>(p.ws + (size_t)piece_slot(p.iters, G, gg, tile_begin) * (BM * BN));
+          float4 part[8];
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4)
+            part[j4] = (c * 32 + j4 * 4 < BN) ? ld_cg_f4(src + (c * 8 + j4) * BM + row) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            acc[j4].x += part[j4].x;
+            acc[j4].y += part[j4].y;
+            acc[j4].z += part[j4].z;
+            acc[j4].w += part[j4].w;
+          }
+        }
+        float v[32];
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          v[4 * j4] = acc[j4].x;
+          v[4 * j4 + 1] = acc[j4].y;
+          v[4 * j4 + 2] = acc[j4].z;
+          v[4 * j4 + 3] = acc[j4].w;
+        }
+        store_chunk<BN, EPI>(p, v, n, mbase + c * 32, c * 32, lane, s_keys, q);
+      }
+    }
+    if constexpr (EPI == 2) {
+      // Every CTA counts itself done after its last key update; the last one writes the ids.
+      __threadfence();
+      epi_bar();
+      if (et == 0) *s_flag = atomicAdd(p.done, 1) == G - 1;
+      epi_bar();
+      if (*s_flag) {
+        __threadfence();
+        for (int m = et; m < p.M; m += kEpiThreads) {
+          const unsigned long long k = atomicExch(p.keys + m, 0ull);
+          const int64_t id = (int64_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+          const int orow = p.out_rows ? p.out_rows[m] : m;
+          if (orow >= 0) p.out_ids[orow] = id;
+          if (p.token_rows != nullptr && p.token_rows[m] >= 0) p.token_table[p.token_rows[m]] = (int32_t)id;
+        }
+        if (et == 0) atomicExch(p.done, 0);
       }
     }
   }
   tc_fence_before();
-  // Every thread of every CTA of the cluster passes both cluster barriers exactly once, error
-  // paths included, so no CTA can wait on one that has left.
-  cluster.sync();
-
-  if constexpr (EPI == 2) {
-    // One warp per token: the max over this tile's 128 vocab rows, then one atomic per token.
-    __shared__ int s_last;
-    const int m_base = mtile * BN;
-    for (int m = warp; m < BN && m_base + m < p.M; m += THREADS / 32) {
-      const float4 v = reinterpret_cast<const float4*>(red)[m * (BM / 4) + lane];
-      const float vals[4] = {v.x, v.y, v.z, v.w};
-      unsigned long long best = 0;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int n = wtile * BM + lane * 4 + j;
-        if (n < p.N) {
-          const unsigned long long k = argmax_key(round_bf16(vals[j]), n);
-          best = k > best ? k : best;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
-        best = t > best ? t : best;
-      }
-      if (lane == 0 && best != 0) atomicMax(p.keys + m_base + m, best);
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence();
-      s_last = atomicAdd(p.done, 1) == p.total_ctas - 1;
-    }
-    __syncthreads();
-    if (s_last) {
-      // every other CTA's atomics precede its counter increment: read and reset the keys
-      __threadfence();
-      for (int m = threadIdx.x; m < p.M; m += THREADS) {
-        const unsigned long long k = atomicExch(p.keys + m, 0ull);
-        const int64_t id = (int64_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
-        const int orow = p.out_rows ? p.out_rows[m] : m;
-        if (orow >= 0) p.out_ids[orow] = id;
-        if (p.token_rows != nullptr && p.token_rows[m] >= 0) p.token_table[p.token_rows[m]] = (int32_t)id;
-      }
-      if (threadIdx.x == 0) atomicExch(p.done, 0);
-    }
-  } else
-  // Deterministic K-split reduction through distributed shared memory: the cluster holds the
-  // tile's `splits` CTAs; rank r sums slice r of the tile over all ranks in rank order and
-  // stores it as bf16 (4 consecutive weight rows = 4 consecutive output columns per thread).
-  {
-    const int ns = p.splits;
-    const int rank = (int)cluster.block_rank();
-    constexpr int kVec = BM / 4;  // float4 per token row of the partial tile
-    constexpr int kTotal = BN * kVec;
-    const int per = (kTotal + ns - 1) / ns;
-    const int e_beg = rank * per;
-    const int e_end = min(e_beg + per, kTotal);
-    const int m_base = mtile * BN;
-    const bool vec_store = p.vec_store;
-    // Element e of the tile is float4 e of every rank's partial (token e / kVec, weight rows
-    // 4 * (e % kVec) ..). Without a split the partial is this CTA's own shared memory.
-    const float4* src[kMaxClusterSplits];
-#pragma unroll
-    for (int sp = 0; sp < kMaxClusterSplits; ++sp)
-      src[sp] = ns == 1 ? reinterpret_cast<const float4*>(red)
-                        : cluster.map_shared_rank(reinterpret_cast<const float4*>(red), sp < ns ? sp : 0);
-    constexpr int U = 4;  // elements in flight per thread
-    for (int e0 = e_beg + (int)threadIdx.x; e0 < e_end; e0 += U * THREADS) {
-      float4 acc[U];
-#pragma unroll
-      for (int q = 0; q < U; ++q) {
-        const int e = e0 + q * THREADS;
-        if (e < e_end) {
-          acc[q] = src[0][e];
-#pragma unroll
-          for (int sp = 1; sp < kMaxClusterSplits; ++sp)
-            if (sp < ns) {
-              const float4 t = src[sp][e];
-              acc[q].x += t.x;
-              acc[q].y += t.y;
-              acc[q].z += t.z;
-              acc[q].w += t.w;
-            }
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < U; ++q) {
-        const int e = e0 + q * THREADS;
-        if (e >= e_end) continue;
-        const int gm = m_base + e / kVec;
-        const int gn = wtile * BM + (e % kVec) * 4;
-        if (gm >= p.M || gn >= p.N) continue;
-        if constexpr (EPI == 1) {
-          // N % 4 == 0 here: (gate_j, up_j, gate_j+1, up_j+1) -> act[j], act[j+1], j = gn / 2.
-          const float g0 = round_bf16(acc[q].x), u0 = round_bf16(acc[q].y);
-          const float g1 = round_bf16(acc[q].z), u1 = round_bf16(acc[q].w);
-          const float s0 = round_bf16(g0 / (1.f + expf(-g0)));
-          const float s1 = round_bf16(g1 / (1.f + expf(-g1)));
-          *reinterpret_cast<uint32_t*>(p.c + (int64_t)gm * p.ldc + gn / 2) = pack_bf16x2(s0 * u0, s1 * u1);
-        } else {
-          __nv_bfloat16* dst = p.c + (int64_t)gm * p.ldc + gn;
-          if (vec_store && gn + 3 < p.N) {
-            *reinterpret_cast<uint2*>(dst) =
-                make_uint2(pack_bf16x2(acc[q].x, acc[q].y), pack_bf16x2(acc[q].z, acc[q].w));
-          } else {
-            const float a4[4] = {acc[q].x, acc[q].y, acc[q].z, acc[q].w};
-            for (int j = 0; j < 4 && gn + j < p.N; ++j) dst[j] = f_to_bf16(a4[j]);
-          }
-        }
-      }
-    }
-  }
-  cluster.sync();  // peers finished reading this CTA's partial tile
-  if (warp == 1) {
+  __syncthreads();
+  if (warp == kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
@@ -444,172 +577,111 @@ static int matrix_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t c
   return CDB_OK;
 }
 
-template <int BN, int STAGES>
-static cudaLaunchConfig_t launch_config(dim3 grid, int splits, cudaStream_t st, cudaLaunchAttribute (&attr)[2]) {
-  using C = Cfg<BN, STAGES>;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(THREADS);
-  cfg.dynamicSmemBytes = C::SMEM;
-  cfg.stream = st;
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = 1;
-  attr[1].val.clusterDim.y = 1;
-  attr[1].val.clusterDim.z = splits;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  return cfg;
-}
-
-// Split s <= want with the least estimated time. A launch of `clusters` clusters of s CTAs (one
-// cluster per output tile) runs in ceil(clusters / max_active(s)) waves, max_active from
-// cudaOccupancyMaxActiveClusters (queried once per size and remembered), and each CTA does 1/s of
-// the tile's K work: time ~ waves / s. Ties go to fewer waves (less fixed cost per wave).
-template <int BN, int STAGES, int EPI>
-static int schedulable_splits(int want, int clusters) {
-  static std::mutex mu;
-  static int max_active[kMaxClusterSplits + 1];
-  static bool known[kMaxClusterSplits + 1] = {};
-  std::lock_guard<std::mutex> lock(mu);
-  int best = 1, best_waves = 0;
-  double best_cost = 0.0;
-  for (int s = 1; s <= want; ++s) {
-    if (!known[s]) {
-      cudaLaunchAttribute attr[2];
-      cudaLaunchConfig_t cfg = launch_config<BN, STAGES>(dim3(1, 1, s), s, nullptr, attr);
-      int n = 0;
-      max_active[s] = cudaOccupancyMaxActiveClusters(&n, gemm_kernel<BN, STAGES, EPI>, &cfg) == cudaSuccess ? n : 0;
-      cudaGetLastError();
-      known[s] = true;
-    }
-    if (max_active[s] <= 0) continue;
-    const int waves = (clusters + max_active[s] - 1) / max_active[s];
-    const double cost = (double)waves / s;
-    if (best_waves == 0 || cost < best_cost - 1e-9 || (cost < best_cost + 1e-9 && waves < best_waves)) {
-      best = s;
-      best_waves = waves;
-      best_cost = cost;
-    }
-  }
-  return best;
-}
-
-template <int BN, int STAGES, int EPI>
-static int launch(const CUtensorMap& mw, const CUtensorMap& mx, Params p, int tiles_n, int tiles_m, int splits,
-                  cudaStream_t st) {
-  using C = Cfg<BN, STAGES>;
+template <int BN, int EPI>
+static int launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, int ctas, cudaStream_t st) {
+  using C = Cfg<BN>;
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(gemm_kernel<BN, STAGES, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
       return CDB_ERR_CUDA;
     attr_set = true;
   }
-  prefer_max_shared(reinterpret_cast<const void*>(gemm_kernel<BN, STAGES, EPI>));
-  int s = schedulable_splits<BN, STAGES, EPI>(splits, tiles_n * tiles_m);
-  int kb_per = (p.num_kb + s - 1) / s;
-  s = (p.num_kb + kb_per - 1) / kb_per;  // no empty split
-  p.splits = s;
-  p.kb_per_split = kb_per;
-  p.total_ctas = tiles_n * tiles_m * s;
-  cudaLaunchAttribute attr[2];
-  cudaLaunchConfig_t cfg = launch_config<BN, STAGES>(dim3(tiles_n, tiles_m, s), s, st, attr);
-  return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, STAGES, EPI>, mw, mx, p) == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
+  prefer_max_shared(reinterpret_cast<const void*>(gemm_kernel<BN, EPI>));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ctas);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, EPI>, mw, mx, p) == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
 }
 
 // Token-tile width for M token rows: M rounded up to a multiple of 16 (the UMMA N step for
 // M = 128) up to 256; wider problems tile the tokens by 256.
-static int tile_n_for(int M) { return M >= 256 ? 256 : ((max(M, 16) + 15) / 16) * 16; }
-static int ctas_per_sm(int bn) { return ctas_per_sm_for(bn); }
+static int tile_n_for(int M) { return M >= 256 ? 256 : ((M + 15) / 16) * 16; }
 
-}  // namespace gemm
-}  // namespace cdb
+struct Shape {
+  int bn, tiles_w, tiles_tok, kb, ctas;
+  long long iters;
+};
 
-using namespace cdb;
+static Shape shape_for(int M, int N, int K, int max_ctas, int num_sms) {
+  Shape s;
+  s.bn = tile_n_for(M);
+  s.tiles_w = (N + BM - 1) / BM;
+  s.tiles_tok = (M + s.bn - 1) / s.bn;
+  s.kb = (K + BK - 1) / BK;
+  s.iters = (long long)s.tiles_w * s.tiles_tok * s.kb;
+  int g = num_sms > 0 ? num_sms : 148;
+  if (max_ctas > 0 && max_ctas < g) g = max_ctas;
+  s.ctas = (int)(s.iters < g ? s.iters : g);
+  return s;
+}
 
-namespace cdb {
-namespace gemm {
-
-// Shared host path of the plain and SwiGLU GEMMs: c = epilogue(x[M,K] * w[N,K]^T).
+// Shared host path of the three epilogues: c = epilogue(x[M,K] * w[N,K]^T).
 template <int EPI>
 static int run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int M, int N, int K,
-               int splits, int num_sms, int32_t* status, cudaStream_t st, const Params* epi2 = nullptr) {
+               int max_ctas, float* workspace, int64_t workspace_elems, int32_t* counters, int num_counters,
+               int num_sms, int32_t* status, cudaStream_t st, const Params* epi2 = nullptr) {
   if (K % 8 != 0 || ldx % 8 != 0 || ldw % 8 != 0 || ldx < K || ldw < K) return CDB_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return CDB_ERR_INVALID_ARGUMENT;
-  const int bn = tile_n_for(M);
-  const int tiles_n = (N + BM - 1) / BM;
-  const int tiles_m = (M + bn - 1) / bn;
-  const int num_kb = (K + BK - 1) / BK;
-  if (num_sms <= 0) num_sms = 148;
-  int s = splits;
-  if (s <= 0) {
-    // Fill the resident CTA slots with (weight tile, token tile, K split) CTAs, at least two
-    // k-blocks per split.
-    const int tiles = tiles_n * tiles_m;
-    const int slots = num_sms * ctas_per_sm(bn);
-    s = tiles >= slots ? 1 : slots / tiles;
-    s = min(s, max(1, num_kb / 2));
-  }
-  s = max(1, min(min(s, kMaxClusterSplits), num_kb));
-  if (EPI == 2) s = 1;  // the argmax epilogue reads whole (unsplit) logit tiles
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15)) return CDB_ERR_INVALID_ARGUMENT;
+  const Shape s = shape_for(M, N, K, max_ctas, num_sms);
+  if ((long long)s.tiles_w * s.tiles_tok > num_counters || counters == nullptr) return CDB_ERR_INVALID_ARGUMENT;
+  if ((int64_t)2 * s.ctas * BM * s.bn > workspace_elems || workspace == nullptr) return CDB_ERR_INVALID_ARGUMENT;
   CUtensorMap mw, mx;
   int rc = matrix_map(&mw, w, N, K, ldw, BM);
   if (rc != CDB_OK) return rc;
-  rc = matrix_map(&mx, x, M, K, ldx, bn);
+  rc = matrix_map(&mx, x, M, K, ldx, s.bn);
   if (rc != CDB_OK) return rc;
   Params p;
+  std::memset(&p, 0, sizeof(p));
   p.c = static_cast<__nv_bfloat16*>(c);
   p.ldc = ldc;
   p.M = M;
   p.N = N;
   p.K = K;
-  p.splits = s;
-  p.kb_per_split = num_kb;
-  p.num_kb = num_kb;
-  p.vec_store = ((reinterpret_cast<uintptr_t>(c) & 7) == 0 && ldc % 4 == 0) ? 1 : 0;
+  p.tiles_w = s.tiles_w;
+  p.tiles_tok = s.tiles_tok;
+  p.kb = s.kb;
+  p.iters = s.iters;
+  p.ws = workspace;
+  p.ctr = counters;
+  p.pair_store = ((reinterpret_cast<uintptr_t>(c) & 3) == 0 && ldc % 2 == 0 && N % 2 == 0) ? 1 : 0;
   p.status = status;
-  p.keys = epi2 ? epi2->keys : nullptr;
-  p.done = epi2 ? epi2->done : nullptr;
-  p.total_ctas = 0;
-  p.out_ids = epi2 ? epi2->out_ids : nullptr;
-  p.out_rows = epi2 ? epi2->out_rows : nullptr;
-  p.token_rows = epi2 ? epi2->token_rows : nullptr;
-  p.token_table = epi2 ? epi2->token_table : nullptr;
-  switch (bn) {
-    case 16:
-      return launch<16, stages_for(16), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
-    case 32:
-      return launch<32, stages_for(32), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
-    case 48:
-      return launch<48, stages_for(48), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
-    case 64:
-      return launch<64, stages_for(64), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
-    case 80:
-      return launch<80, stages_for(80), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
-    case 96:
-      return launch<96, stages_for(96), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
-    case 112:
-      return launch<112, stages_for(112), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
-    case 128:
-      return launch<128, stages_for(128), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
-    case 144:
-      return launch<144, stages_for(144), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
-    case 160:
-      return launch<160, stages_for(160), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
-    case 176:
-      return launch<176, stages_for(176), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
-    case 192:
-      return launch<192, stages_for(192), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
-    case 208:
-      return launch<208, stages_for(208), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
-    case 224:
-      return launch<224, stages_for(224), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
-    case 240:
-      return launch<240, stages_for(240), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
-    case 256:
-      return launch<256, stages_for(256), EPI>(mw, mx, p, tiles_n, tiles_m, s, st);
+  if (epi2 != nullptr) {
+    p.keys = epi2->keys;
+    p.done = epi2->done;
+    p.out_ids = epi2->out_ids;
+    p.out_rows = epi2->out_rows;
+    p.token_rows = epi2->token_rows;
+    p.token_table = epi2->token_table;
+  }
+  switch (s.bn) {
+#define CDB_GEMM_CASE(B) \
+  case B:                \
+    return launch<B, EPI>(mw, mx, p, s.ctas, st);
+    CDB_GEMM_CASE(16)
+    CDB_GEMM_CASE(32)
+    CDB_GEMM_CASE(48)
+    CDB_GEMM_CASE(64)
+    CDB_GEMM_CASE(80)
+    CDB_GEMM_CASE(96)
+    CDB_GEMM_CASE(112)
+    CDB_GEMM_CASE(128)
+    CDB_GEMM_CASE(144)
+    CDB_GEMM_CASE(160)
+    CDB_GEMM_CASE(176)
+    CDB_GEMM_CASE(192)
+    CDB_GEMM_CASE(208)
+    CDB_GEMM_CASE(224)
+    CDB_GEMM_CASE(240)
+    CDB_GEMM_CASE(256)
+#undef CDB_GEMM_CASE
     default:
       return CDB_ERR_UNSUPPORTED;
   }
@@ -619,49 +691,52 @@ static int run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, 
 }  // namespace cdb
 
 extern "C" int cdb_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int M,
-                             int N, int K, int splits, float* workspace, int64_t workspace_elems, int32_t* counters,
+                             int N, int K, int max_ctas, float* workspace, int64_t workspace_elems, int32_t* counters,
                              int num_counters, int num_sms, int32_t* status, void* stream) {
-  (void)workspace;
-  (void)workspace_elems;
-  (void)counters;
-  (void)num_counters;
   if (M <= 0 || N <= 0 || K <= 0) return M == 0 ? CDB_OK : CDB_ERR_INVALID_ARGUMENT;
   if (ldc < N) return CDB_ERR_INVALID_ARGUMENT;
-  return cdb::gemm::run<0>(x, ldx, w, ldw, c, ldc, M, N, K, splits, num_sms, status, static_cast<cudaStream_t>(stream));
+  return cdb::gemm::run<0>(x, ldx, w, ldw, c, ldc, M, N, K, max_ctas, workspace, workspace_elems, counters,
+                           num_counters, num_sms, status, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int cdb_mlp_gateup_silu_gemm(const void* x, int64_t ldx, const void* w_gate_up, int64_t ldw, void* act,
-                                        int64_t ld_act, int M, int inter, int K, int splits, int num_sms,
+                                        int64_t ld_act, int M, int inter, int K, int max_ctas, float* workspace,
+                                        int64_t workspace_elems, int32_t* counters, int num_counters, int num_sms,
                                         int32_t* status, void* stream) {
   if (M <= 0 || inter <= 0 || K <= 0) return M == 0 ? CDB_OK : CDB_ERR_INVALID_ARGUMENT;
-  if (inter % 2 != 0 || ld_act < inter || ld_act % 2 != 0 || (reinterpret_cast<uintptr_t>(act) & 3))
-    return CDB_ERR_INVALID_ARGUMENT;
-  return cdb::gemm::run<1>(x, ldx, w_gate_up, ldw, act, ld_act, M, 2 * inter, K, splits, num_sms, status,
-                           static_cast<cudaStream_t>(stream));
+  if (ld_act < inter || (reinterpret_cast<uintptr_t>(act) & 1)) return CDB_ERR_INVALID_ARGUMENT;
+  return cdb::gemm::run<1>(x, ldx, w_gate_up, ldw, act, ld_act, M, 2 * inter, K, max_ctas, workspace,
+                           workspace_elems, counters, num_counters, num_sms, status, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int cdb_lm_head_argmax(const void* x, int64_t ldx, const void* w, int64_t ldw, int M, int vocab, int K,
                                   int64_t* out_ids, const int32_t* out_rows, const int32_t* token_rows,
-                                  int32_t* token_table, uint64_t* keys, int32_t* done, int num_sms,
+                                  int32_t* token_table, uint64_t* keys, int32_t* done, float* workspace,
+                                  int64_t workspace_elems, int32_t* counters, int num_counters, int num_sms,
                                   int32_t* status, void* stream) {
   if (M <= 0 || vocab <= 0 || K <= 0) return M == 0 ? CDB_OK : CDB_ERR_INVALID_ARGUMENT;
   if (out_ids == nullptr || keys == nullptr || done == nullptr || (token_rows != nullptr && token_table == nullptr))
     return CDB_ERR_INVALID_ARGUMENT;
   cdb::gemm::Params e;
+  std::memset(&e, 0, sizeof(e));
   e.keys = reinterpret_cast<unsigned long long*>(keys);
   e.done = done;
   e.out_ids = out_ids;
   e.out_rows = out_rows;
   e.token_rows = token_rows;
   e.token_table = token_table;
-  return cdb::gemm::run<2>(x, ldx, w, ldw, nullptr, 0, M, vocab, K, 1, num_sms, status,
-                           static_cast<cudaStream_t>(stream), &e);
+  return cdb::gemm::run<2>(x, ldx, w, ldw, nullptr, 0, M, vocab, K, 0, workspace, workspace_elems, counters,
+                           num_counters, num_sms, status, static_cast<cudaStream_t>(stream), &e);
 }
 
 extern "C" int64_t cdb_gemm_workspace_elems(int M, int N, int K, int num_sms) {
-  (void)M;
-  (void)N;
-  (void)K;
-  (void)num_sms;
-  return 0;  // K splits reduce inside a thread-block cluster; no global workspace
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const cdb::gemm::Shape s = cdb::gemm::shape_for(M, N, K, 0, num_sms);
+  return (int64_t)2 * s.ctas * cdb::gemm::BM * s.bn;
+}
+
+extern "C" int cdb_gemm_counter_elems(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const cdb::gemm::Shape s = cdb::gemm::shape_for(M, N, K, 0, 148);
+  return s.tiles_w * s.tiles_tok;
 }

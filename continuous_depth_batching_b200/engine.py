@@ -222,7 +222,6 @@ class ContinuousDepthBatchingEngine:
         dtype: torch.dtype | None = None,
         model_adapter=None,
         device: torch.device | str | None = None,
-        gemm_backend: str = "cublas",
         fused_lm_head: bool = True,
     ) -> ContinuousDepthBatchingEngine:
         """Build an engine for an Ouro or Huginn causal LM given by its parameters (reference names).
@@ -232,10 +231,10 @@ class ContinuousDepthBatchingEngine:
         :class:`~.huginn.HuginnForCausalLM`); ``config.model_type`` picks the family, as
         ``resolve_cdb_model_adapter`` does (``model_adapter.py:105-122``). Weights are packed to bf16 on ``device``
         (default: the model's device if CUDA, else ``cuda``). ``dtype`` other than bf16 is rejected:
-        the kernels compute in bf16 with fp32 accumulation. ``gemm_backend`` picks the per-layer
-        projections (``"cublas"`` or the library's ``"tcgen05"`` GEMMs with the fused SwiGLU);
-        ``fused_lm_head`` runs the LM head and the greedy argmax as one tcgen05 GEMM with no logits
-        in HBM (``cdb_lm_head_argmax``) instead of a GEMM followed by ``cdb_argmax``.
+        the kernels compute in bf16 with fp32 accumulation; every projection runs on the library's
+        tcgen05 GEMM (SwiGLU fused into the gate/up projection). ``fused_lm_head`` runs the LM head
+        and the greedy argmax as one tcgen05 GEMM with no logits in HBM (``cdb_lm_head_argmax``)
+        instead of a GEMM followed by ``cdb_argmax``.
         """
 
         if model_adapter is not None:
@@ -285,7 +284,6 @@ class ContinuousDepthBatchingEngine:
             max_num_seqs=cfg.max_num_seqs,
             max_num_batched_tokens=cfg.max_num_batched_tokens,
             use_cuda_graph=cfg.use_cuda_graph,
-            gemm_backend=gemm_backend,
             fused_lm_head=fused_lm_head,
         )
         if cfg.kv_pressure_mode == "offload" and cfg.cpu_offload_space:

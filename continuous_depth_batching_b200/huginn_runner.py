@@ -40,8 +40,8 @@ from .runner import SCRATCH_ITEMS, OuroRunner
 class PackedHuginnWeights:
     """bf16 device weights per stage and block.
 
-    ``fc`` is ``[gate; up]`` as stored (cuBLAS path + ``cdb_silu_mul``) or row pairs
-    ``(gate_j, up_j)`` for ``cdb_mlp_gateup_silu_gemm``; ``qk_bias`` is ``[2, H, D]``.
+    ``fc`` holds row pairs ``(gate_j, up_j)`` (the stored ``[gate; up]`` interleaved) for
+    ``cdb_mlp_gateup_silu_gemm``; ``qk_bias`` is ``[2, H, D]``.
     """
 
     wte: torch.Tensor
@@ -51,9 +51,7 @@ class PackedHuginnWeights:
     ln_f: torch.Tensor
 
     @classmethod
-    def from_state_dict(
-        cls, shape: HuginnShape, sd: dict[str, torch.Tensor], device: torch.device, fc_interleaved: bool
-    ) -> PackedHuginnWeights:
+    def from_state_dict(cls, shape: HuginnShape, sd: dict[str, torch.Tensor], device: torch.device) -> PackedHuginnWeights:
         def g(name: str) -> torch.Tensor:
             return sd[name].detach().to(device=device, dtype=torch.bfloat16).contiguous()
 
@@ -64,8 +62,7 @@ class PackedHuginnWeights:
             for layer in range(shape.stage_layers(stage)):
                 p = f"transformer.{stage}.{layer}."
                 fc = g(p + "mlp.fc.weight")
-                if fc_interleaved:
-                    fc = torch.stack([fc[:i], fc[i:]], dim=1).reshape(2 * i, fc.shape[1]).contiguous()
+                fc = torch.stack([fc[:i], fc[i:]], dim=1).reshape(2 * i, fc.shape[1]).contiguous()
                 entry: dict[str, torch.Tensor | None] = {
                     "Wqkv": g(p + "attn.Wqkv.weight"),
                     "proj": g(p + "attn.proj.weight"),
@@ -104,7 +101,6 @@ class HuginnRunner(OuroRunner):
         max_num_seqs: int,
         max_num_batched_tokens: int,
         use_cuda_graph: bool = True,
-        gemm_backend: str = "tcgen05",
         fused_lm_head: bool = True,
     ) -> None:
         layout = LoopedKvLayout(
@@ -124,10 +120,10 @@ class HuginnRunner(OuroRunner):
             max_num_seqs=max_num_seqs,
             max_num_batched_tokens=max_num_batched_tokens,
             use_cuda_graph=use_cuda_graph,
-            gemm_backend=gemm_backend,
             fused_lm_head=fused_lm_head,
+            max_gemm_n=max(shape.vocab_size, 2 * shape.intermediate_size, 3 * shape.n_embd),
         )
-        self.w = PackedHuginnWeights.from_state_dict(shape, state_dict, device, fc_interleaved=gemm_backend == "tcgen05")
+        self.w = PackedHuginnWeights.from_state_dict(shape, state_dict, device)
         E, I = shape.n_embd, shape.intermediate_size
         self.qkv_width = 3 * E
         self.k_col, self.v_col = E, 2 * E
@@ -138,7 +134,6 @@ class HuginnRunner(OuroRunner):
         self.qkv = torch.zeros(rows, 3 * E, **bf)
         self.attn = torch.zeros(rows, E, **bf)
         self.o = torch.zeros(rows, E, **bf)
-        self.gu = torch.zeros(rows, 2 * I, **bf)
         self.act = torch.zeros(rows, I, **bf)
         self.m = torch.zeros(rows, E, **bf)
         self.ad_in = torch.zeros(rows, 2 * E, **bf)  # [state | injection] rows of the adapter GEMM
@@ -189,19 +184,7 @@ class HuginnRunner(OuroRunner):
         )
 
     def _mlp(self, n: int, bw) -> None:
-        s = self.shape
-        if self.gemm_backend == "tcgen05":
-            _lib.call(
-                "cdb_mlp_gateup_silu_gemm", _lib.ptr(self.h), self.h.stride(0), _lib.ptr(bw["fc"]), bw["fc"].stride(0),
-                _lib.ptr(self.act), self.act.stride(0), n, s.intermediate_size, s.n_embd, 0, self.num_sms,
-                _lib.ptr(self.status), self._sp(),
-            )
-        else:
-            self._mm(self.h[:n], bw["fc"], self.gu[:n])
-            _lib.call(
-                "cdb_silu_mul", _lib.ptr(self.gu), self.gu.stride(0), _lib.ptr(self.act), self.act.stride(0), n,
-                s.intermediate_size, self._sp(),
-            )
+        self._gate_up(self.h[:n], bw["fc"], self.act[:n])
 
     def _blocks(self, stage, n, cache_layer_of, item_slot, item_pos, append, last_xd, last_rows, last_w2) -> None:
         """The blocks of one stage over rows [0, n): x in ``xw``, norm_1(x) in ``h`` on entry.

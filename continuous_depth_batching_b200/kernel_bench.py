@@ -143,8 +143,7 @@ def run_gemm(args) -> dict:
     x = torch.randn(m, k, device=dev).to(torch.bfloat16)
     w = (0.02 * torch.randn(n, k, device=dev)).to(torch.bfloat16)
     c = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
-    ws = torch.zeros(32 << 20, dtype=torch.float32, device=dev)
-    ctr = torch.zeros(1 << 14, dtype=torch.int32, device=dev)
+    ws = _lib.GemmWorkspace(dev, m, n, 148)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
@@ -152,7 +151,7 @@ def run_gemm(args) -> dict:
     def tc():
         _lib.call(
             "cdb_gemm_bf16", _lib.ptr(x), x.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(c), c.stride(0), m, n, k,
-            args.splits, _lib.ptr(ws), ws.numel(), _lib.ptr(ctr), ctr.numel(), 148, _lib.ptr(status), stream.cuda_stream,
+            args.ctas, *ws.args(), 148, _lib.ptr(status), stream.cuda_stream,
         )
 
     def cublas():
@@ -177,7 +176,7 @@ def run_gemm(args) -> dict:
 def run_gemm_chain(args) -> dict:
     """Per-GEMM time inside a CUDA graph of ``--layers`` GEMMs of one shape on different weights
     (the shape of a decode step's projections, launch gaps and PDL overlap included), for cuBLAS
-    and for cdb_gemm_bf16 at each K split (0 = the automatic choice)."""
+    and for cdb_gemm_bf16 at several persistent CTA counts (0 = one per SM)."""
 
     dev = torch.device("cuda")
     torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
@@ -186,17 +185,18 @@ def run_gemm_chain(args) -> dict:
     x = torch.randn(m, k, device=dev).to(torch.bfloat16)
     out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = _lib.GemmWorkspace(dev, m, n, 148)
     stream = torch.cuda.Stream()
     res = {"m": m, "n": n, "k": k, "layers": layers, "us_per_gemm": {}}
-    for split in ["cublas", 0, 1, 2, 4, 8]:
-        def body(split=split):
+    for ctas in ["cublas", 0, 120, 96, 74]:
+        def body(ctas=ctas):
             for layer in range(layers):
-                if split == "cublas":
+                if ctas == "cublas":
                     torch.mm(x, w[layer].t(), out=out)
                 else:
                     _lib.call(
                         "cdb_gemm_bf16", _lib.ptr(x), x.stride(0), _lib.ptr(w[layer]), w.stride(1), _lib.ptr(out),
-                        out.stride(0), m, n, k, split, None, 0, None, 0, 148, _lib.ptr(status), stream.cuda_stream,
+                        out.stride(0), m, n, k, ctas, *ws.args(), 148, _lib.ptr(status), stream.cuda_stream,
                     )
 
         with torch.cuda.stream(stream):
@@ -209,7 +209,7 @@ def run_gemm_chain(args) -> dict:
             for _ in range(args.warmup):
                 graph.replay()
             ms = _events_ms(graph.replay, args.iters, stream)
-        res["us_per_gemm"][str(split)] = round(ms * 1e3 / layers, 2)
+        res["us_per_gemm"][str(ctas)] = round(ms * 1e3 / layers, 2)
         del graph
     if int(status.item()) != 0:
         raise RuntimeError(_lib.load().cdb_status_string(int(status.item())).decode())
@@ -228,6 +228,7 @@ def run_lm_head(args) -> dict:
     keys = torch.zeros(m, dtype=torch.int64, device=dev)
     done = torch.zeros(1, dtype=torch.int32, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = _lib.GemmWorkspace(dev, m, v, 148)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
@@ -235,7 +236,7 @@ def run_lm_head(args) -> dict:
     def fused():
         _lib.call(
             "cdb_lm_head_argmax", _lib.ptr(x), k, _lib.ptr(w), k, m, v, k, _lib.ptr(ids), None, None, None,
-            _lib.ptr(keys), _lib.ptr(done), 148, _lib.ptr(status), sp,
+            _lib.ptr(keys), _lib.ptr(done), *ws.args(), 148, _lib.ptr(status), sp,
         )
 
     def unfused():
@@ -269,7 +270,7 @@ def main(argv=None) -> None:
     g.add_argument("--m", type=int, default=80)
     g.add_argument("--n", type=int, default=2048)
     g.add_argument("--k", type=int, default=2048)
-    g.add_argument("--splits", type=int, default=0)
+    g.add_argument("--ctas", type=int, default=0, help="persistent CTAs (0 = one per SM)")
     g.add_argument("--only", choices=["tcgen05", "cublas"], default=None)
     lm = sub.add_parser("lm_head")
     lm.add_argument("--m", type=int, default=32)

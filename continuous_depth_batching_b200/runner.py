@@ -15,7 +15,9 @@ per row) and replays the CUDA graph of its padded bucket (``model_runner.py:896-
 attention work plan, then per shared layer ``RMSNorm -> QKV GEMM -> ragged paged attention (RoPE +
 KV append fused) -> O GEMM -> residual+norm -> gate/up GEMM -> SwiGLU -> down GEMM ->
 residual+norm``, the last norm scattering into the bank and computing the exit-gate logit.
-Dense GEMMs run on cuBLAS through ``torch.mm``; everything else is libcdb_b200.
+Every kernel is libcdb_b200's: the projections and the LM head run on its stream-K tcgen05 GEMM
+(``cdb_gemm_bf16``, SwiGLU fused into the gate/up projection, greedy argmax fused into the LM
+head), which shares one split-partial workspace per replica.
 """
 
 from __future__ import annotations
@@ -79,8 +81,8 @@ class Uploader:
 class PackedOuroWeights:
     """bf16 device weights with the projections the kernels fuse concatenated.
 
-    ``w_gu`` is ``[gate; up]`` stacked (the cuBLAS path then runs ``cdb_silu_mul``) or, with
-    ``gu_interleaved``, row pairs ``(gate_j, up_j)`` as ``cdb_mlp_gateup_silu_gemm`` reads them.
+    ``w_qkv`` is ``[q; k; v]`` stacked; ``w_gu`` holds row pairs ``(gate_j, up_j)`` as
+    ``cdb_mlp_gateup_silu_gemm`` reads them.
     """
 
     embed: torch.Tensor
@@ -95,17 +97,13 @@ class PackedOuroWeights:
     lm_head: torch.Tensor
 
     @classmethod
-    def from_state_dict(
-        cls, shape: OuroShape, sd: dict[str, torch.Tensor], device: torch.device, gu_interleaved: bool = False
-    ) -> PackedOuroWeights:
+    def from_state_dict(cls, shape: OuroShape, sd: dict[str, torch.Tensor], device: torch.device) -> PackedOuroWeights:
         def g(name: str) -> torch.Tensor:
             return sd[name].detach().to(device=device, dtype=torch.bfloat16).contiguous()
 
         def gate_up(p: str) -> torch.Tensor:
             gate, up = g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")
-            if gu_interleaved:
-                return torch.stack([gate, up], dim=1).reshape(2 * gate.shape[0], gate.shape[1]).contiguous()
-            return torch.cat([gate, up]).contiguous()
+            return torch.stack([gate, up], dim=1).reshape(2 * gate.shape[0], gate.shape[1]).contiguous()
 
         L = shape.num_hidden_layers
         pre = [f"model.layers.{i}." for i in range(L)]
@@ -167,9 +165,9 @@ class OuroRunner:
         max_num_seqs: int,
         max_num_batched_tokens: int,
         use_cuda_graph: bool = True,
-        gemm_backend: str = "tcgen05",
         fused_lm_head: bool = True,
     ) -> None:
+        I = shape.intermediate_size
         self._init_device(
             shape,
             device=device,
@@ -185,16 +183,15 @@ class OuroRunner:
             max_num_seqs=max_num_seqs,
             max_num_batched_tokens=max_num_batched_tokens,
             use_cuda_graph=use_cuda_graph,
-            gemm_backend=gemm_backend,
             fused_lm_head=fused_lm_head,
+            max_gemm_n=max(shape.vocab_size, 2 * I, 3 * shape.num_attention_heads * shape.head_dim),
         )
-        self.w = PackedOuroWeights.from_state_dict(shape, state_dict, device, gu_interleaved=gemm_backend == "tcgen05")
+        self.w = PackedOuroWeights.from_state_dict(shape, state_dict, device)
         H, D = shape.hidden_size, shape.head_dim
         Hq = shape.num_attention_heads * D
         Hk = shape.num_key_value_heads * D
         self.qkv_width = Hq + 2 * Hk
         self.k_col, self.v_col = Hq, Hq + Hk
-        I = shape.intermediate_size
         rows = self.rows
         bf = dict(dtype=torch.bfloat16, device=device)
         self.xw = torch.zeros(rows, H, **bf)
@@ -202,7 +199,6 @@ class OuroRunner:
         self.qkv = torch.zeros(rows, self.qkv_width, **bf)
         self.attn = torch.zeros(rows, Hq, **bf)
         self.o = torch.zeros(rows, H, **bf)
-        self.gu = torch.zeros(rows, 2 * I, **bf)
         self.act = torch.zeros(rows, I, **bf)
         self.m = torch.zeros(rows, H, **bf)
         self.gate_out = torch.zeros(max_num_seqs, **bf)
@@ -232,18 +228,14 @@ class OuroRunner:
         max_num_seqs: int,
         max_num_batched_tokens: int,
         use_cuda_graph: bool,
-        gemm_backend: str,
         fused_lm_head: bool = True,
+        max_gemm_n: int = 65536,
     ) -> None:
-        """Model-independent device state: KV pool, stream, uploads, attention scratch, graphs."""
+        """Model-independent device state: KV pool, stream, uploads, GEMM and attention scratch, graphs."""
 
         if device.type != "cuda":
             raise RuntimeError("the B200 CDB runner needs a CUDA device; there is no CPU path")
         _lib.load()
-        # cuBLAS may otherwise reduce split-K partial sums of bf16 GEMMs in bf16; keep fp32.
-        torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
-        if gemm_backend not in ("tcgen05", "cublas"):
-            raise ValueError(f"gemm_backend must be 'tcgen05' or 'cublas', got {gemm_backend!r}")
         self.shape = shape
         self.device = device
         self.kv_policy = kv_policy
@@ -251,7 +243,6 @@ class OuroRunner:
         self.block_size = block_size
         self.max_num_seqs = max_num_seqs
         self.use_cuda_graph = use_cuda_graph
-        self.gemm_backend = gemm_backend
         self.layout = layout
         self.pool = PagedKVPool(
             num_cache_layers=layout.num_cache_layers,
@@ -266,12 +257,11 @@ class OuroRunner:
         self.stream = torch.cuda.Stream(device=device)
         self.uploader = Uploader(device)
         self.num_sms = torch.cuda.get_device_properties(device).multi_processor_count
-        # kept for cdb_gemm_bf16's (unused) workspace arguments
-        self.gemm_ws = torch.zeros(1, dtype=torch.float32, device=device)
-        self.gemm_ctr = torch.zeros(1, dtype=torch.int32, device=device)
         self.attn_ctas = 2 * self.num_sms
         D = shape.head_dim
         self.rows = max(max_num_seqs, max_num_batched_tokens)
+        # split partials + tile counters of the stream-K GEMM, shared by every projection (one stream)
+        self.gemm = _lib.GemmWorkspace(device, self.rows, max_gemm_n, self.num_sms)
         self.token_table = torch.zeros(max_num_seqs, dtype=torch.int32, device=device)
         self.token_log = torch.zeros(1, dtype=torch.int64, device=device)
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
@@ -285,8 +275,8 @@ class OuroRunner:
         self.part_ml = torch.zeros(SCRATCH_ITEMS * nh * 64 * 2, dtype=torch.float32, device=device)
         self.counters = torch.zeros(SCRATCH_ITEMS * nh, dtype=torch.int32, device=device)
         self.scale = float(D) ** -0.5
-        # LM head + greedy argmax in one tcgen05 GEMM (no logits in HBM; cdb_lm_head_argmax) with
-        # either projection backend, unless logits are kept for inspection
+        # LM head + greedy argmax in one tcgen05 GEMM (no logits in HBM; cdb_lm_head_argmax),
+        # unless logits are kept for inspection
         self.fused_lm_head = fused_lm_head
         self.lm_keys = torch.zeros(max_num_seqs, dtype=torch.int64, device=device)
         self.lm_done = torch.zeros(1, dtype=torch.int32, device=device)
@@ -303,8 +293,8 @@ class OuroRunner:
             _lib.call(
                 "cdb_lm_head_argmax", _lib.ptr(x), x.stride(0), _lib.ptr(w), w.stride(0), n, s.vocab_size,
                 x.shape[1], _lib.ptr(self.token_log), _lib.ptr(out_rows), _lib.ptr(token_rows),
-                _lib.ptr(self.token_table), _lib.ptr(self.lm_keys), _lib.ptr(self.lm_done), self.num_sms,
-                _lib.ptr(self.status), self._sp(),
+                _lib.ptr(self.token_table), _lib.ptr(self.lm_keys), _lib.ptr(self.lm_done), *self.gemm.args(),
+                self.num_sms, _lib.ptr(self.status), self._sp(),
             )
             return None
         self._mm(x[:n], w, self.logits[:n])
@@ -358,16 +348,22 @@ class OuroRunner:
         return torch.cuda.current_stream(self.device).cuda_stream
 
     def _mm(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> None:
-        """out = a @ w^T: the tcgen05 GEMM of libcdb (``gemm_backend='tcgen05'``) or cuBLAS."""
+        """out = a @ w^T on the library's stream-K tcgen05 GEMM."""
 
-        if self.gemm_backend == "cublas":
-            torch.mm(a, w.t(), out=out)
-            return
         m, k = a.shape
         _lib.call(
             "cdb_gemm_bf16", _lib.ptr(a), a.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(out), out.stride(0),
-            m, w.shape[0], k, 0, _lib.ptr(self.gemm_ws), self.gemm_ws.numel(), _lib.ptr(self.gemm_ctr),
-            self.gemm_ctr.numel(), self.num_sms, _lib.ptr(self.status), self._sp(),
+            m, w.shape[0], k, 0, *self.gemm.args(), self.num_sms, _lib.ptr(self.status), self._sp(),
+        )
+
+    def _gate_up(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> None:
+        """out = silu(a @ Wg^T) * (a @ Wu^T) for interleaved gate/up rows ``w`` (one GEMM)."""
+
+        m, k = a.shape
+        _lib.call(
+            "cdb_mlp_gateup_silu_gemm", _lib.ptr(a), a.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(out),
+            out.stride(0), m, w.shape[0] // 2, k, 0, *self.gemm.args(), self.num_sms, _lib.ptr(self.status),
+            self._sp(),
         )
 
     # ------------------------------------------------------------------ stage bodies
@@ -443,55 +439,26 @@ class OuroRunner:
                     s.num_attention_heads, s.head_dim, self.block_size, sp,
                 )
                 self._prefill_attention(base_layer + l)
-            if self.gemm_backend == "tcgen05":
-                _lib.call(
-                    "cdb_o_proj_residual_norm_gemm", _lib.ptr(self.attn), self.attn.stride(0), _lib.ptr(w.w_o[l]),
-                    w.w_o[l].stride(0), _lib.ptr(self.o), self.o.stride(0), _lib.ptr(self.xw), self.xw.stride(0),
-                    _lib.ptr(w.norms["input_layernorm_2"][l]), _lib.ptr(w.norms["post_attention_layernorm"][l]),
-                    _lib.ptr(self.h), self.h.stride(0), n, H, w.w_o[l].shape[1], eps, self.num_sms,
-                    _lib.ptr(self.status), sp,
-                )
-            else:
-                self._mm(self.attn[:n], w.w_o[l], self.o[:n])
-                _lib.call(
-                    "cdb_add_rmsnorm", _lib.ptr(self.xw), self.xw.stride(0), _lib.ptr(self.o), self.o.stride(0),
-                    _lib.ptr(w.norms["input_layernorm_2"][l]), _lib.ptr(w.norms["post_attention_layernorm"][l]),
-                    _lib.ptr(self.h), self.h.stride(0), None, None, None, None, n, H, eps, sp,
-                )
-            if self.gemm_backend == "tcgen05":
-                _lib.call(
-                    "cdb_mlp_gateup_silu_gemm", _lib.ptr(self.h), self.h.stride(0), _lib.ptr(w.w_gu[l]),
-                    w.w_gu[l].stride(0), _lib.ptr(self.act), self.act.stride(0), n, I, H, 0, self.num_sms,
-                    _lib.ptr(self.status), sp,
-                )
-            else:
-                self._mm(self.h[:n], w.w_gu[l], self.gu[:n])
-                _lib.call(
-                    "cdb_silu_mul", _lib.ptr(self.gu), self.gu.stride(0), _lib.ptr(self.act), self.act.stride(0), n, I, sp
-                )
+            self._mm(self.attn[:n], w.w_o[l], self.o[:n])
+            _lib.call(
+                "cdb_add_rmsnorm", _lib.ptr(self.xw), self.xw.stride(0), _lib.ptr(self.o), self.o.stride(0),
+                _lib.ptr(w.norms["input_layernorm_2"][l]), _lib.ptr(w.norms["post_attention_layernorm"][l]),
+                _lib.ptr(self.h), self.h.stride(0), None, None, None, None, n, H, eps, sp,
+            )
+            self._gate_up(self.h[:n], w.w_gu[l], self.act[:n])
             # x += norm(m); then the next layer's input norm, or after the last layer the final norm
             # scattered into the bank (and the exit-gate logit)
             last = l == L - 1
             w_next = w.final_norm if last else w.norms["input_layernorm"][l + 1]
             y, y_rows = (final_dst, final_rows) if last else (self.h, None)
             g = last and gate
-            if self.gemm_backend == "tcgen05":
-                _lib.call(
-                    "cdb_down_residual_norm_gemm", _lib.ptr(self.act), self.act.stride(0), _lib.ptr(w.w_down[l]),
-                    w.w_down[l].stride(0), _lib.ptr(self.m), self.m.stride(0), _lib.ptr(self.xw), self.xw.stride(0),
-                    _lib.ptr(w.norms["post_attention_layernorm_2"][l]), _lib.ptr(w_next), _lib.ptr(y), y.stride(0),
-                    _lib.ptr(y_rows), _lib.ptr(w.gate_w) if g else None, _lib.ptr(w.gate_b) if g else None,
-                    _lib.ptr(self.gate_out) if g else None, n, H, w.w_down[l].shape[1], eps, self.num_sms,
-                    _lib.ptr(self.status), sp,
-                )
-            else:
-                self._mm(self.act[:n], w.w_down[l], self.m[:n])
-                _lib.call(
-                    "cdb_add_rmsnorm", _lib.ptr(self.xw), self.xw.stride(0), _lib.ptr(self.m), self.m.stride(0),
-                    _lib.ptr(w.norms["post_attention_layernorm_2"][l]), _lib.ptr(w_next), _lib.ptr(y), y.stride(0),
-                    _lib.ptr(y_rows), _lib.ptr(w.gate_w) if g else None, _lib.ptr(w.gate_b) if g else None,
-                    _lib.ptr(self.gate_out) if g else None, n, H, eps, sp,
-                )
+            self._mm(self.act[:n], w.w_down[l], self.m[:n])
+            _lib.call(
+                "cdb_add_rmsnorm", _lib.ptr(self.xw), self.xw.stride(0), _lib.ptr(self.m), self.m.stride(0),
+                _lib.ptr(w.norms["post_attention_layernorm_2"][l]), _lib.ptr(w_next), _lib.ptr(y), y.stride(0),
+                _lib.ptr(y_rows), _lib.ptr(w.gate_w) if g else None, _lib.ptr(w.gate_b) if g else None,
+                _lib.ptr(self.gate_out) if g else None, n, H, eps, sp,
+            )
 
     def _recurrent_body(self, meta: torch.Tensor, n: int, kv_slot: int, gate: bool) -> None:
         s = self.shape

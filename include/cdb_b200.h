@@ -159,27 +159,33 @@ int cdb_rope_append_kv(void* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_c
 /* bf16 tensor-core GEMM on tcgen05/TMEM: c[M,N] = x[M,K] * w[N,K]^T (fp32 accumulation, bf16
  * store). Replaces the nn.Linear projections of the shared block and the LM head
  * (OuroAttention q/k/v/o_proj modeling_ouro.py:371-374,431; OuroMLP gate/up/down :162-168;
- * lm_head adapters/ouro.py:321-329), which the reference runs on cuBLAS through ATen.
+ * Huginn Wqkv/proj/fc/mlp.proj modeling_huginn.py:239-242,310-316; lm_head adapters/ouro.py:321-329),
+ * which the reference runs on cuBLAS through ATen.
  *   x, w       row-major bf16, leading dimensions ldx, ldw (multiples of 8), 16-byte aligned.
- *   splits     K splits, clamped to [1, 8] (<= 0: chosen from the tile count and num_sms).
- *              The splits of one output tile run as one thread-block cluster and reduce
- *              through distributed shared memory, so no global scratch is used:
- *              workspace/workspace_elems/counters/num_counters are ignored (may be NULL/0).
- * Deterministic: split partials are summed in split order. */
+ *   max_ctas   persistent CTAs (<= 0: num_sms). The (tile, k block) iterations are divided
+ *              evenly over them (stream-K); a tile split across CTAs is combined through
+ *              `workspace` by the piece that finishes last, summing the pieces in k order
+ *              (deterministic for a given M, N, K and CTA count).
+ *   workspace  fp32, >= cdb_gemm_workspace_elems(M, N, K, num_sms) elements, 16-byte aligned.
+ *   counters   int32, >= cdb_gemm_counter_elems(M, N, K) elements, zeroed before first use;
+ *              every call leaves them zeroed. Calls sharing workspace/counters must be ordered
+ *              (one stream). */
 int cdb_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, int64_t ldc, int M, int N, int K,
-                  int splits, float* workspace, int64_t workspace_elems, int32_t* counters, int num_counters,
+                  int max_ctas, float* workspace, int64_t workspace_elems, int32_t* counters, int num_counters,
                   int num_sms, int32_t* status, void* stream);
 
 /* Fused MLP input half: act[M, inter] = silu(x * Wg^T) * (x * Wu^T) with the reference's bf16
  * rounding (gate and up rounded to bf16, silu rounded to bf16, product rounded to bf16), in one
  * tcgen05 GEMM whose epilogue applies SwiGLU. Replaces OuroMLP.forward's
- * act_fn(gate_proj(x)) * up_proj(x) (modeling_ouro.py:162-168).
+ * act_fn(gate_proj(x)) * up_proj(x) (modeling_ouro.py:162-168) and Huginn's gated MLP
+ * (modeling_huginn.py:310-316).
  *   w_gate_up  bf16 [2*inter, K] with rows interleaved: row 2j = gate_proj row j,
- *              row 2j+1 = up_proj row j. inter even; act 4-byte aligned, ld_act even.
- *   splits, num_sms, status: as cdb_gemm_bf16. */
+ *              row 2j+1 = up_proj row j. act 2-byte aligned, ld_act >= inter.
+ *   max_ctas, workspace, counters, num_sms, status: as cdb_gemm_bf16 with N = 2*inter. */
 int cdb_mlp_gateup_silu_gemm(const void* x, int64_t ldx, const void* w_gate_up, int64_t ldw, void* act,
-                             int64_t ld_act, int M, int inter, int K, int splits, int num_sms, int32_t* status,
-                             void* stream);
+                             int64_t ld_act, int M, int inter, int K, int max_ctas, float* workspace,
+                             int64_t workspace_elems, int32_t* counters, int num_counters, int num_sms,
+                             int32_t* status, void* stream);
 
 /* LM head + greedy argmax in one tcgen05 GEMM, without storing logits (the coda's lm_head,
  * adapters/ouro.py:321-329, then argmax, _run_coda_forward_graphed model_runner.py:1064-1125):
@@ -187,13 +193,19 @@ int cdb_mlp_gateup_silu_gemm(const void* x, int64_t ldx, const void* w_gate_up, 
  *   out_ids[out_rows ? out_rows[r] : r] = id[r] (skipped when out_rows[r] < 0); if token_rows is
  *   not NULL and token_rows[r] >= 0, also token_table[token_rows[r]] = id[r].
  *   keys [M] uint64 and done [1] int32: scratch that must start zeroed; the call leaves it zeroed.
- *   Calls sharing keys/done must be ordered (one stream). x/w as cdb_gemm_bf16. */
+ *   workspace/counters as cdb_gemm_bf16 with N = vocab. Calls sharing keys/done/workspace/
+ *   counters must be ordered (one stream). x/w as cdb_gemm_bf16. */
 int cdb_lm_head_argmax(const void* x, int64_t ldx, const void* w, int64_t ldw, int M, int vocab, int K,
                        int64_t* out_ids, const int32_t* out_rows, const int32_t* token_rows, int32_t* token_table,
-                       uint64_t* keys, int32_t* done, int num_sms, int32_t* status, void* stream);
+                       uint64_t* keys, int32_t* done, float* workspace, int64_t workspace_elems, int32_t* counters,
+                       int num_counters, int num_sms, int32_t* status, void* stream);
 
-/* fp32 workspace elements cdb_gemm_bf16 needs: always 0 (kept for callers sizing a buffer). */
+/* fp32 workspace elements a GEMM of this shape needs (split partials: 2 per CTA, 128 x token-tile
+ * floats each). */
 int64_t cdb_gemm_workspace_elems(int M, int N, int K, int num_sms);
+
+/* int32 tile counters a GEMM of this shape needs (one per 128-row x token-tile output tile). */
+int cdb_gemm_counter_elems(int M, int N, int K);
 
 /* ---------------------------------------------------------------------------------------
  * Row-wise fused elementwise kernels (bf16 activations, fp32 math, bf16 rounding at the
@@ -229,8 +241,8 @@ int cdb_qkv_rope_append_gemm(const void* x, int64_t ldx, const void* w_qkv, int6
                              int num_cache_layers, int64_t kv_rows, int cache_layer, const int32_t* block_table,
                              int64_t block_table_stride, const int32_t* item_slot, const int32_t* item_pos,
                              int rope_mode, const void* rope_cos, const void* rope_sin, const void* qk_bias,
-                             int num_heads, int head_dim, int block_size, int num_sms, int32_t* status,
-                             void* stream);
+                             int num_heads, int head_dim, int block_size, float* workspace, int64_t workspace_elems,
+                             int32_t* counters, int num_counters, int num_sms, int32_t* status, void* stream);
 
 /* O projection with Ouro's post-attention sandwich: proj = attn * w_o^T; x <- bf16(x +
  * norm_post(proj)); y = norm_next(x) (OuroDecoderLayer.forward, modeling_ouro.py:470-490:
@@ -239,7 +251,8 @@ int cdb_qkv_rope_append_gemm(const void* x, int64_t ldx, const void* w_qkv, int6
 int cdb_o_proj_residual_norm_gemm(const void* attn, int64_t ld_attn, const void* w_o, int64_t ldw, void* proj,
                                   int64_t ld_proj, void* x, int64_t x_stride, const void* w_norm_post,
                                   const void* w_norm_next, void* y, int64_t y_stride, int num_rows, int hidden,
-                                  int K, float eps, int num_sms, int32_t* status, void* stream);
+                                  int K, float eps, float* workspace, int64_t workspace_elems, int32_t* counters,
+                                  int num_counters, int num_sms, int32_t* status, void* stream);
 
 /* Down projection with the MLP sandwich: proj = act * w_down^T; x <- bf16(x + norm_post(proj));
  * y[y_rows[r]] = norm_next(x[r]) (y_rows NULL: y[r]; rows with y_rows[r] < 0 skipped) and, with
@@ -250,7 +263,8 @@ int cdb_down_residual_norm_gemm(const void* act, int64_t ld_act, const void* w_d
                                 int64_t ld_proj, void* x, int64_t x_stride, const void* w_norm_post,
                                 const void* w_norm_next, void* y, int64_t y_stride, const int32_t* y_rows,
                                 const void* gate_w, const void* gate_b, void* gate_out, int num_rows, int hidden,
-                                int K, float eps, int num_sms, int32_t* status, void* stream);
+                                int K, float eps, float* workspace, int64_t workspace_elems, int32_t* counters,
+                                int num_counters, int num_sms, int32_t* status, void* stream);
 
 /* act[r] = bf16(bf16(silu(g)) * u) with gu[r] = [g (inter) | u (inter)] (OuroMLP.forward,
  * modeling_ouro.py:166-169). */

@@ -45,7 +45,7 @@ def _host_space(shape, host_blocks: int) -> float | None:
 
 
 def _engine(shape, sd, *, kv_policy="single", refill=True, live=False, num_blocks=4096, max_model_len=2048, graphs=True,
-            gemm="cublas", async_mode=False, host_blocks=0, extra=None):
+            async_mode=False, host_blocks=0, extra=None):
     model = OuroForCausalLM(shape)
     model.load_state_dict({k: v.to(torch.float32) for k, v in sd.items()})
     cfg = ContinuousDepthBatchingConfig(
@@ -63,7 +63,7 @@ def _engine(shape, sd, *, kv_policy="single", refill=True, live=False, num_block
         max_model_len=max_model_len,
         **(extra or {}),
     )
-    eng = ContinuousDepthBatchingEngine.from_model(model, cfg, device="cuda", gemm_backend=gemm)
+    eng = ContinuousDepthBatchingEngine.from_model(model, cfg, device="cuda")
     assert eng.runner.pool.num_host_blocks == host_blocks
     return eng
 
@@ -561,8 +561,8 @@ def test_last_exited_copy_teacher_forced():
     assert_report(_compare_teacher_forced(shape, sd, prompts, max_new, depths, kv_policy="last_exited"))
 
 
-def test_tcgen05_backend_schedule_and_fused_lm_head():
-    """The all-library GEMM path (tcgen05 projections, fused SwiGLU, LM head + argmax in one GEMM):
+def test_schedule_and_fused_lm_head():
+    """The engine's GEMM path (tcgen05 projections, fused SwiGLU, LM head + argmax in one GEMM):
     bit-exact schedule vs the reference trace, and, teacher-forced on the reference tokens, the
     fused LM head's greedy tokens equal the argmax of the same engine's stored logits (unfused
     LM head) at >= 99% of positions."""
@@ -570,7 +570,7 @@ def test_tcgen05_backend_schedule_and_fused_lm_head():
     data, shape = _golden()
     run = next(r for r in data["runs"] if r["name"] == "replay_refill")
     sd = random_ouro_state_dict(shape, seed=0, gate_std=data["gate_std"], lm_head_std=0.2)
-    fused = _engine(shape, sd, gemm="tcgen05")
+    fused = _engine(shape, sd)
     assert fused.runner.fused_lm_head
     fused.record_trace = True
     outs_a = fused.generate_batch(
@@ -578,7 +578,7 @@ def test_tcgen05_backend_schedule_and_fused_lm_head():
         forced_tokens=run["tokens"],
     )
     assert fused.launch_trace == run["launches"]
-    plain = _engine(shape, sd, gemm="tcgen05")
+    plain = _engine(shape, sd)
     plain.keep_logits = True
     outs_b = plain.generate_batch(
         data["prompts"], max_new_tokens=data["max_new_tokens"], eos_token_id=None, exit_depths=run["exit_depths"],

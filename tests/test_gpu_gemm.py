@@ -5,8 +5,9 @@ accumulates in fp32 and rounds once, so every element is within one bf16 roundin
 reference plus fp32 summation-order noise: |c - ref| <= 2^-8 |ref| + 2^-12 * ||x_row|| ||w_row||.
 Shapes cover the Ouro-1.4B projections (N 6144/2048/11264/2048, K 2048/5632, LM head 49152),
 token counts from 1 to prefill sizes, M/N/K tails (odd output widths take the scalar store
-path), automatic and forced K splits (clamped to the 8-CTA cluster), and repeated calls (the
-cluster reduction must give bit-identical results).
+path), persistent CTA counts from one CTA (every tile in one range) to one per SM (tiles split
+over CTAs and combined through the workspace), and repeated calls (the combine sums pieces in k
+order, so results are bit-identical and the tile counters come back zeroed).
 """
 
 from __future__ import annotations
@@ -22,18 +23,16 @@ DEV = "cuda"
 
 class Gemm:
     def __init__(self):
-        self.ws = torch.zeros(64 << 20, dtype=torch.float32, device=DEV)
-        self.ctr = torch.zeros(8192, dtype=torch.int32, device=DEV)
+        self.work = _lib.GemmWorkspace(torch.device(DEV), 2048, 65536, 148)
         self.status = torch.zeros(1, dtype=torch.int32, device=DEV)
 
-    def __call__(self, x, w, splits=0, out=None):
+    def __call__(self, x, w, ctas=0, out=None):
         m, k = x.shape
         n = w.shape[0]
         c = torch.empty(m, n, dtype=torch.bfloat16, device=DEV) if out is None else out
         _lib.call(
             "cdb_gemm_bf16", _lib.ptr(x), x.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(c), c.stride(0), m, n, k,
-            splits, _lib.ptr(self.ws), self.ws.numel(), _lib.ptr(self.ctr), self.ctr.numel(), 148,
-            _lib.ptr(self.status), torch.cuda.current_stream().cuda_stream,
+            ctas, *self.work.args(), 148, _lib.ptr(self.status), torch.cuda.current_stream().cuda_stream,
         )
         return c
 
@@ -69,17 +68,19 @@ def test_gemm_matches_fp32_reference(gemm, m, n, k):
     _check(c, x, w)
 
 
-@pytest.mark.parametrize("m", [200, 24, 60])
-@pytest.mark.parametrize("splits", [1, 2, 5, 16])
-def test_gemm_forced_splits_and_repeat(gemm, splits, m):
-    g = torch.Generator(device=DEV).manual_seed(splits)
+@pytest.mark.parametrize("m", [200, 24, 60, 600])
+@pytest.mark.parametrize("ctas", [1, 7, 74, 148])
+def test_gemm_cta_counts_and_repeat(gemm, ctas, m):
+    g = torch.Generator(device=DEV).manual_seed(ctas)
     x = torch.randn(m, 2048, device=DEV, generator=g).to(torch.bfloat16)
     w = (0.05 * torch.randn(2048, 2048, device=DEV, generator=g)).to(torch.bfloat16)
-    first = gemm(x, w, splits=splits)
+    first = gemm(x, w, ctas=ctas)
     for _ in range(3):
-        again = gemm(x, w, splits=splits)
+        again = gemm(x, w, ctas=ctas)
         torch.cuda.synchronize()
         assert torch.equal(first, again)  # deterministic across calls
+    assert int(gemm.status.item()) == 0
+    assert int(gemm.work.ctr.abs().sum().item()) == 0  # counters left zeroed
     _check(first, x, w)
 
 
@@ -98,7 +99,7 @@ def test_gemm_strided_operands_and_output(gemm):
 @pytest.mark.parametrize("m,inter,k", [(1, 5632, 2048), (80, 5632, 2048), (256, 5632, 2048), (700, 704, 256), (33, 504, 520)])
 def test_gateup_silu_gemm(gemm, m, inter, k):
     """cdb_mlp_gateup_silu_gemm == plain GEMM on the same interleaved weight + cdb_silu_mul
-    (bit-exact: same tiles and splits), and within one bf16 rounding of gate/up of the fp32
+    (bit-exact: same tiles and stream-K pieces), and within one bf16 rounding of gate/up of the fp32
     reference act_fn(x Wg^T) * (x Wu^T) with the reference's bf16 rounding points."""
 
     g = torch.Generator(device=DEV).manual_seed(m + inter + k)
@@ -110,7 +111,7 @@ def test_gateup_silu_gemm(gemm, m, inter, k):
     sp = torch.cuda.current_stream().cuda_stream
     _lib.call(
         "cdb_mlp_gateup_silu_gemm", _lib.ptr(x), x.stride(0), _lib.ptr(w_il), w_il.stride(0), _lib.ptr(act),
-        act.stride(0), m, inter, k, 0, 148, _lib.ptr(gemm.status), sp,
+        act.stride(0), m, inter, k, 0, *gemm.work.args(), 148, _lib.ptr(gemm.status), sp,
     )
     gu_il = gemm(x, w_il)
     gu = torch.cat([gu_il[:, 0::2], gu_il[:, 1::2]], dim=1).contiguous()
@@ -138,9 +139,9 @@ def test_gateup_silu_gemm(gemm, m, inter, k):
 
 @pytest.mark.parametrize("m,vocab,k", [(1, 49152, 2048), (7, 1000, 512), (80, 49152, 2048), (130, 65536, 480), (300, 4096, 256)])
 def test_lm_head_argmax_matches_logits_argmax(gemm, m, vocab, k):
-    """cdb_lm_head_argmax == torch.argmax (first maximum) of the unsplit GEMM's bf16 logits, exactly
-    (same tiles, same accumulation), with the output-row and token-table scatters, twice in a row
-    (the key/counter scratch must come back zeroed)."""
+    """cdb_lm_head_argmax == torch.argmax (first maximum) of the plain GEMM's bf16 logits, exactly
+    (same tiles, same stream-K pieces, same accumulation), with the output-row and token-table
+    scatters, twice in a row (the key/counter scratch must come back zeroed)."""
 
     g = torch.Generator(device=DEV).manual_seed(m + vocab)
     x = torch.randn(m, k, device=DEV, generator=g).to(torch.bfloat16)
@@ -153,13 +154,13 @@ def test_lm_head_argmax_matches_logits_argmax(gemm, m, vocab, k):
     table = torch.full((m + 3,), -5, dtype=torch.int32, device=DEV)
     token_rows = torch.arange(m, dtype=torch.int32, device=DEV) + 3
     sp = torch.cuda.current_stream().cuda_stream
-    logits = gemm(x, w, splits=1)
+    logits = gemm(x, w)
     ref = logits.float().argmax(dim=-1)
     for _ in range(2):
         _lib.call(
             "cdb_lm_head_argmax", _lib.ptr(x), x.stride(0), _lib.ptr(w), w.stride(0), m, vocab, k, _lib.ptr(out),
-            _lib.ptr(out_rows), _lib.ptr(token_rows), _lib.ptr(table), _lib.ptr(keys), _lib.ptr(done), 148,
-            _lib.ptr(gemm.status), sp,
+            _lib.ptr(out_rows), _lib.ptr(token_rows), _lib.ptr(table), _lib.ptr(keys), _lib.ptr(done),
+            *gemm.work.args(), 148, _lib.ptr(gemm.status), sp,
         )
         torch.cuda.synchronize()
         assert int(gemm.status.item()) == 0
@@ -167,6 +168,7 @@ def test_lm_head_argmax_matches_logits_argmax(gemm, m, vocab, k):
         assert int(out[1]) == -7  # row 0 was skipped
         assert torch.equal(table[3:].long(), ref)
         assert int(keys.abs().sum()) == 0 and int(done.item()) == 0
+        assert int(gemm.work.ctr.abs().sum().item()) == 0
 
 
 def _sp():
@@ -201,13 +203,13 @@ def test_residual_norm_gemms_match_separate_calls(gemm, m, hidden, k, last):
             _lib.call(
                 "cdb_down_residual_norm_gemm", _lib.ptr(a), a.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(proj),
                 proj.stride(0), _lib.ptr(x), x.stride(0), _lib.ptr(wa), _lib.ptr(wn), _lib.ptr(y), y.stride(0),
-                _lib.ptr(rows), *g, m, hidden, k, 1e-6, 148, _lib.ptr(gemm.status), _sp(),
+                _lib.ptr(rows), *g, m, hidden, k, 1e-6, *gemm.work.args(), 148, _lib.ptr(gemm.status), _sp(),
             )
         elif fused:
             _lib.call(
                 "cdb_o_proj_residual_norm_gemm", _lib.ptr(a), a.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(proj),
                 proj.stride(0), _lib.ptr(x), x.stride(0), _lib.ptr(wa), _lib.ptr(wn), _lib.ptr(y), y.stride(0), m,
-                hidden, k, 1e-6, 148, _lib.ptr(gemm.status), _sp(),
+                hidden, k, 1e-6, *gemm.work.args(), 148, _lib.ptr(gemm.status), _sp(),
             )
         else:
             gemm(a, w, out=proj)
@@ -259,7 +261,8 @@ def test_qkv_rope_append_gemm_matches_separate_calls(gemm, heads, d, rope_mode, 
         if fused:
             _lib.call(
                 "cdb_qkv_rope_append_gemm", _lib.ptr(x), x.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(qkv),
-                qkv.stride(0), hd, 2 * hd, n, k, *common, heads, d, bs, 148, _lib.ptr(gemm.status), _sp(),
+                qkv.stride(0), hd, 2 * hd, n, k, *common, heads, d, bs, *gemm.work.args(), 148,
+                _lib.ptr(gemm.status), _sp(),
             )
         else:
             gemm(x, w, out=qkv)

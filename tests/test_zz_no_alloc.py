@@ -139,11 +139,20 @@ def test_static_scratch_limits_rejected():
     wide = Case(132, 128, 1, 16, seed=2)
     rc = lib.cdb_paged_decode_attn_append_static(*_static_args(wide, wide.qkv, wide.kv, wide.qkv, 0, 1, 1, status, stream))
     assert rc == SCRATCH_LIMIT
-    # 8193 rows x 4 head groups: the work plan would exceed 32768 units. Rejected on the host
-    # before anything is enqueued, so the buffers of a one-row case suffice.
-    small = Case(16, 128, 1, 16, seed=3)
+    # 8193 rows x 4 head groups: the work plan would exceed 32768 units. Every buffer the call
+    # names is sized for 8193 rows (qkv, out, item_pos, item_slot, block-table rows; every row at
+    # position 0 of block 0), so even if the limit check let the call through, the launch would
+    # stay inside its buffers; the expected outcome is still the rejection.
+    many = Case(16, 128, 1, 16, seed=3)
+    n = 8193
+    many.n = n
+    many.table = torch.zeros(n, many.max_blocks, dtype=torch.int32, device=DEV)
+    many.pos = torch.zeros(n, dtype=torch.int32, device=DEV)
+    many.slots = torch.arange(n, dtype=torch.int32, device=DEV)
+    many.qkv = torch.zeros(n, 3 * 16 * 128, dtype=torch.bfloat16, device=DEV)
+    many_out = torch.zeros(n, 16 * 128, dtype=torch.bfloat16, device=DEV)
     rc = lib.cdb_paged_decode_attn_append_static(
-        *_static_args(small, small.qkv, small.kv, small.qkv, 0, 1, 8193, status, stream)
+        *_static_args(many, many.qkv, many.kv, many_out, 0, 1, n, status, stream)
     )
     assert rc == SCRATCH_LIMIT
     assert b"static scratch" in lib.cdb_status_string(SCRATCH_LIMIT)
