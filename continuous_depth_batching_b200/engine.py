@@ -33,9 +33,10 @@ from enum import IntEnum
 import torch
 
 from .config import ContinuousDepthBatchingConfig, validate_exit_threshold
-from .kv_cache import copies_exit_kv, kv_slot_for_step, resolve_kv_slots_per_layer
 from .huginn import HuginnShape
 from .huginn_runner import HuginnRunner
+from .kv_cache import copies_exit_kv, kv_slot_for_step, resolve_kv_slots_per_layer
+from .model_adapter import resolve_cdb_model_adapter
 from .ouro import OuroShape
 from .runner import OuroRunner
 
@@ -237,14 +238,13 @@ class ContinuousDepthBatchingEngine:
         instead of a GEMM followed by ``cdb_argmax``.
         """
 
-        if model_adapter is not None:
-            raise NotImplementedError("custom model adapters are not supported by the B200 engine")
+        # The reference's plugin seam: no adapter (inferred from the model), the reference's Ouro /
+        # Huginn adapters, or this package's; see model_adapter.py for what is rejected and why.
+        adapter = resolve_cdb_model_adapter(model, model_adapter)
         if dtype not in (None, torch.bfloat16):
             raise NotImplementedError(f"the B200 kernels run bf16; got dtype={dtype}")
         config = getattr(model, "config", None)
-        model_type = getattr(config, "model_type", None) if config is not None else None
-        if model_type not in ("ouro", "huginn"):
-            raise TypeError(f"Continuous depth batching requires an Ouro or Huginn model; got {type(model)!r}")
+        model_type = adapter.family
         cfg = cdb_config.get_resolved()
         # ``resolve_max_num_seqs`` (``scheduler_base.py:49-66``, applied at ``continuous_api.py:328``):
         # a decode launch writes one row per resident request into buffers sized by the prefill
@@ -289,7 +289,11 @@ class ContinuousDepthBatchingEngine:
         if cfg.kv_pressure_mode == "offload" and cfg.cpu_offload_space:
             # ``OffloadingManager._compute_num_cpu_blocks`` (``offloading_manager.py:134-144``)
             runner.pool.attach_host_pool(int(cfg.cpu_offload_space * 1024**3) // runner.pool.block_bytes)
-        return cls(model, cfg, runner, shape)
+        adapter.configure_recurrent_steps(cfg.max_recurrent_steps)
+        adapter.configure_kv_policy(cfg.kv_policy, cfg.kv_slots_per_layer)
+        eng = cls(model, cfg, runner, shape)
+        eng.model_adapter = adapter
+        return eng
 
     # ------------------------------------------------------------------ public API
     @torch.no_grad()
