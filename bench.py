@@ -13,11 +13,19 @@ A step is one ``generate_batch`` over the whole request set (prefill included, a
 reference's ``generated_tokens / wall_time`` metric, ``benchmarks/metrics.py:274-278``).
 ``value`` is generated tokens / device time (CUDA events on the engine stream, max over ranks);
 ``e2e`` is the same through the public API measured on the host clock, which includes the prompt
-upload and the token read-back of every step. Under torchrun each rank is an independent replica
-with its own seeded request set (``scaling: weak``); nothing crosses GPUs inside the timed region.
+upload and the token read-back of every step. Under torchrun the ranks are independent engine
+replicas serving one seeded trace of 256 x N requests, request i on rank i mod N (``scaling:
+weak``: 256 concurrent requests per GPU); nothing crosses GPUs inside the timed region.
+
+``--config 4`` runs BASELINE config 4 instead: one 8192-request trace with seeded Poisson arrivals
+at 200 requests/s in total (lengths and depths as config 1), request i on rank i mod N with its
+arrival offset, one pass; whole-box tokens/s = all generated tokens / the slowest rank's time
+(``scaling: strong``: the trace is fixed, more GPUs share it).
 
 ``--impl reference`` times the CPU restatement of the reference engine (``oracle/``, the only
-place bench.py runs it) on the host cores over a bounded prefix of the same workload.
+place bench.py runs it) on the host cores over a bounded sample of the same workload (the first
+4 config-1 requests at their full prompt lengths, 16 new tokens each); the b200 line reports its
+own tokens/s on that same sample (``same_sample``) beside it.
 
 ``--engine cb`` times the full-depth continuous-batching baseline (``ContinuousBatchingEngine``,
 the reference's CB comparison engine) on the same kernels, graphs and workload, and prints its
@@ -66,6 +74,10 @@ def parse() -> argparse.Namespace:
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--engine", default="cdb", choices=["cdb", "cb"],
                    help="cdb: the CDB engine (the headline); cb: the full-depth continuous-batching baseline")
+    p.add_argument("--config", type=int, default=1, choices=[1, 4],
+                   help="1: 256 concurrent requests per GPU (the headline); 4: the 8192-request Poisson trace")
+    p.add_argument("--rate", type=float, default=200.0, help="config 4: total arrival rate, requests/s")
+    p.add_argument("--trace-requests", type=int, default=8192, help="config 4: requests in the trace")
     return p.parse_args()
 
 
@@ -91,15 +103,42 @@ def aggregate(dev_s: float, wall_s: float, tokens: float, device) -> tuple[float
 
 
 def replica_seed(seed: int, rank: int) -> int:
-    """Each replica serves its own seeded request set (request-sharded, weak scaling)."""
+    """Seed of the trace every rank draws from (one trace, split round-robin by ``shard``)."""
 
-    return seed + 1000 * rank
+    del rank
+    return seed
 
 
 def workload(seed: int, n: int, out_cap: int):
     from oracle.workloads import ouro_lognormal_workload
 
     return ouro_lognormal_workload(n, vocab_size=OURO_1P4B["vocab_size"], seed=seed, out_cap=out_cap, depth_probs=DEPTH_P)
+
+
+def shard(items: list, rank: int, world: int) -> list:
+    """Request i of a trace goes to rank i mod world."""
+
+    return items[rank::world]
+
+
+def rank_workload(seed: int, per_rank: int, out_cap: int, rank: int, world: int):
+    """This rank's share of one seeded trace of ``per_rank * world`` requests (the config-1 mix)."""
+
+    prompts, max_new, depths = workload(replica_seed(seed, rank), per_rank * world, out_cap)
+    return shard(prompts, rank, world), shard(max_new, rank, world), shard(depths, rank, world)
+
+
+def config4_trace(seed: int, n: int, rate: float, out_cap: int):
+    """n requests with the config-1 lengths and depths and seeded Poisson arrival
+    offsets at ``rate`` requests/s in total."""
+
+    import numpy as np
+
+    from oracle.workloads import poisson_arrival_offsets
+
+    prompts, max_new, depths = workload(seed, n, out_cap)
+    arrivals = poisson_arrival_offsets(np.random.default_rng(seed + 1), n, rate)
+    return prompts, max_new, depths, arrivals
 
 
 class ClockSampler:
@@ -286,7 +325,7 @@ def run_b200(args) -> None:
         # a rank that never arrives ends the others' collective with an error after this timeout
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     eng, shape = build_engine(args, device)
-    prompts, max_new, depths = workload(replica_seed(args.seed, rank), args.requests, args.out_cap)
+    prompts, max_new, depths = rank_workload(args.seed, args.requests, args.out_cap, rank, world)
     stream = eng.runner.stream
 
     def step():
@@ -414,6 +453,7 @@ def run_b200(args) -> None:
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
+            line["same_sample"] = gpu_on_cpu_sample(eng)
             line["cpu_baseline"] = cpu_baseline(seconds=20.0)
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -442,18 +482,46 @@ def flop_bound_summary(shape, stats) -> dict:
     }
 
 
+CPU_SAMPLE_REQUESTS = 4
+CPU_SAMPLE_NEW_TOKENS = 16
+
+
 def cpu_sample_workload():
-    """Bounded sample of the config-1 workload for the CPU oracle: first 2 requests, 4 tokens each."""
+    """Bounded sample of the config-1 workload for the CPU baseline: the trace's first 4 requests
+    at their full prompt lengths (221, 180, 334 and 218 tokens), 16 new tokens each, the first 15
+    replayed exit depths of each."""
 
-    prompts, max_new, depths = workload(0, 256, 1024)
-    k, new = 2, 4
-    prompts = [p[:256] for p in prompts[:k]]
-    max_new = [new] * k
-    depths = [d[: new - 1] for d in depths[:k]]
-    return prompts, max_new, depths
+    prompts, _max_new, depths = workload(0, 256, 1024)
+    k, new = CPU_SAMPLE_REQUESTS, CPU_SAMPLE_NEW_TOKENS
+    return prompts[:k], [new] * k, [d[: new - 1] for d in depths[:k]]
 
 
-def cpu_baseline(seconds: float = 20.0) -> dict:
+def sample_description() -> str:
+    return (f"the first {CPU_SAMPLE_REQUESTS} config-1 requests at full prompt lengths, {CPU_SAMPLE_NEW_TOKENS} new "
+            "tokens each, replayed depths (prefill included)")
+
+
+def gpu_on_cpu_sample(eng, reps: int = 5) -> dict:
+    """The B200 engine's tokens/s on the CPU baseline's sample (device time, CUDA events), so the
+    two arms can be compared on identical work."""
+
+    prompts, max_new, depths = cpu_sample_workload()
+    stream = eng.runner.stream
+    eng.generate_batch(prompts, max_new_tokens=max_new, eos_token_id=None, exit_depths=depths)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    tokens = 0
+    for _ in range(reps):
+        outs = eng.generate_batch(prompts, max_new_tokens=max_new, eos_token_id=None, exit_depths=depths)
+        tokens += sum(len(o.generated_tokens) for o in outs)
+    b.record(stream)
+    b.synchronize()
+    return {"value": round(tokens / (a.elapsed_time(b) / 1e3), 1), "unit": UNIT, "sample": sample_description(),
+            "runs": reps}
+
+
+def cpu_baseline(seconds: float = 20.0, max_runs: int = 3) -> dict:
     """Time the CPU restatement of the reference engine (oracle/) on this host's cores."""
 
     from continuous_depth_batching_b200.ouro import OuroShape, random_ouro_state_dict
@@ -472,7 +540,7 @@ def cpu_baseline(seconds: float = 20.0) -> dict:
         out = eng.generate(prompts, max_new, exit_depths=depths)
         tokens += sum(len(x) for x in out)
         runs += 1
-        if time.perf_counter() - t0 > seconds or runs >= 3:
+        if time.perf_counter() - t0 > seconds or runs >= max_runs:
             break
     dt = time.perf_counter() - t0
     cpu_model = ""
@@ -490,8 +558,7 @@ def cpu_baseline(seconds: float = 20.0) -> dict:
         "cpu_model": cpu_model,
         "dtype": "fp32",
         "kind": "port",
-        "sample": f"{runs} x generate of the first {len(prompts)} config-1 requests (prompts cut to 256 tokens), "
-        f"{max_new[0]} new tokens each, fp32 on the host CPU",
+        "sample": f"{runs} x generate of {sample_description()}, fp32 on the host CPU",
     }
 
 
@@ -502,7 +569,7 @@ def run_reference(args) -> None:
     t_all = []
     vals = []
     for i in range(args.warmup + args.steps):
-        b = cpu_baseline(seconds=5.0)
+        b = cpu_baseline(seconds=5.0, max_runs=1)
         if i >= args.warmup:
             vals.append(b["value"])
             t_all.append(b)
@@ -520,7 +587,7 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": "BASELINE config 1 (bounded CPU prefix, see cpu_baseline.sample)"},
+        "config": {"workload": f"BASELINE config 1 sample: {sample_description()}"},
         "cpu_baseline": {**t_all[-1], "value": round(v, 3)} if t_all else None,
         "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -589,12 +656,85 @@ def run_cb(args) -> None:
     }))
 
 
+def run_config4(args) -> None:
+    """one seeded Poisson trace shared round-robin by the ranks, one pass."""
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=device)
+    eng, _shape = build_engine(args, device)
+    prompts, max_new, depths, arrivals = config4_trace(args.seed, args.trace_requests, args.rate, args.out_cap)
+    mine = list(range(rank, len(prompts), world))
+    p_m = [prompts[i] for i in mine]
+    n_m = [max_new[i] for i in mine]
+    d_m = [depths[i] for i in mine]
+    a_m = [arrivals[i] for i in mine]
+    # warm-up: graphs for every launch width up to 256 rows, on this rank's first requests
+    k = min(256, len(p_m))
+    for _ in range(max(1, args.warmup)):
+        eng.generate_batch(p_m[:k], max_new_tokens=[min(8, m) for m in n_m[:k]], eos_token_id=None,
+                           exit_depths=[d[: min(8, m) - 1] for d, m in zip(d_m[:k], n_m[:k], strict=True)])
+    torch.cuda.synchronize()
+    stream = eng.runner.stream
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        t0 = time.perf_counter()
+        ev0.record(stream)
+        outs = eng.generate_batch(p_m, max_new_tokens=n_m, eos_token_id=None, exit_depths=d_m, arrival_offsets_s=a_m)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    dev_s = ev0.elapsed_time(ev1) / 1e3
+    tokens = sum(len(o.generated_tokens) for o in outs)
+    dev_max, wall_max, total = aggregate(dev_s, wall, float(tokens), device)
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC,
+            "value": round(total / dev_max, 1),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": 1,
+            "warmup": max(1, args.warmup),
+            "ms_per_step": round(dev_max * 1e3, 2),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded lognormal lengths, uniform token ids, categorical depths, Poisson arrivals)",
+            "config": {
+                "workload": f"BASELINE config 4: {args.trace_requests} requests, Poisson arrivals at {args.rate} req/s "
+                "total, request i on rank i mod N, Ouro-1.4B random-init, refill on",
+                "last_arrival_s": round(arrivals[-1], 2),
+                "parallelism": f"{world} request-sharded replicas (no collective on the hot path)",
+                "tokens": int(total),
+            },
+            "e2e": {"value": round(total / wall_max, 1), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": int(total) * 8},
+            "rank0_tokens_per_s": round(tokens / dev_s, 1),
+            "clocks": clocks.summary(),
+        }), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif args.engine == "cb":
         run_cb(args)
+    elif args.config == 4:
+        run_config4(args)
     else:
         run_b200(args)
 

@@ -2,7 +2,8 @@
 
 Each rank of ``bench.py`` is an independent engine replica; the only cross-rank step is the
 aggregation after the timed region (max of the times, sum of the tokens), tested here with two
-gloo ranks. Replicas get distinct seeded request sets.
+gloo ranks. The ranks share one seeded trace, request i on rank i mod N: their shards are disjoint
+and together are the whole trace (config 1 per rank and the config-4 Poisson trace alike).
 """
 
 from __future__ import annotations
@@ -30,8 +31,10 @@ def _worker(rank: int, world: int, port: int, out) -> None:
         import bench
 
         dev, wall, tok = bench.aggregate(1.0 + rank, 2.0 + 3 * rank, 100.0 * (rank + 1), torch.device("cpu"))
-        prompts, max_new, depths = bench.workload(bench.replica_seed(0, rank), 4, 16)
-        out.put((rank, dev, wall, tok, prompts[0][:5], sum(max_new)))
+        prompts, max_new, depths = bench.rank_workload(0, 4, 16, rank, world)
+        _p, _m, _d, arrivals = bench.config4_trace(0, 10, 200.0, 16)
+        mine = bench.shard(arrivals, rank, world)
+        out.put((rank, dev, wall, tok, [p[:5] for p in prompts], sum(max_new), mine))
     finally:
         dist.destroy_process_group()
 
@@ -47,9 +50,15 @@ def test_two_rank_aggregation_and_distinct_shards():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for rank, dev, wall, tok, _head, _n in results:
+    for rank, dev, wall, tok, _heads, _n, _arr in results:
         assert dev == 2.0 and wall == 5.0 and tok == 300.0, rank
-    assert results[0][4] != results[1][4]  # different request sets per replica
+    import bench
+
+    whole, _m, _d = bench.workload(bench.replica_seed(0, 0), 8, 16)
+    assert results[0][4] == [p[:5] for p in whole[0::2]] and results[1][4] == [p[:5] for p in whole[1::2]]
+    _p, _m, _d, arrivals = bench.config4_trace(0, 10, 200.0, 16)
+    assert sorted(results[0][6] + results[1][6]) == sorted(arrivals)
+    assert arrivals == sorted(arrivals) and arrivals[0] == 0.0
 
 
 def test_single_process_aggregation_is_identity():
