@@ -74,8 +74,10 @@ def parse() -> argparse.Namespace:
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--engine", default="cdb", choices=["cdb", "cb"],
                    help="cdb: the CDB engine (the headline); cb: the full-depth continuous-batching baseline")
-    p.add_argument("--config", type=int, default=1, choices=[1, 4],
-                   help="1: 256 concurrent requests per GPU (the headline); 4: the 8192-request Poisson trace")
+    p.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4],
+                   help="BASELINE config: 1 (the headline) Ouro-1.4B, 256 concurrent requests per GPU; 2 Ouro-2.6B, "
+                   "last_exited KV, Poisson 20 req/s; 3 Huginn-0125, S=32; 4 the 8192-request Poisson trace")
+    p.add_argument("--no-refill", action="store_true", help="config 2: the no-refill (wave) arm")
     p.add_argument("--rate", type=float, default=200.0, help="config 4: total arrival rate, requests/s")
     p.add_argument("--trace-requests", type=int, default=8192, help="config 4: requests in the trace")
     return p.parse_args()
@@ -126,6 +128,26 @@ def rank_workload(seed: int, per_rank: int, out_cap: int, rank: int, world: int)
 
     prompts, max_new, depths = workload(replica_seed(seed, rank), per_rank * world, out_cap)
     return shard(prompts, rank, world), shard(max_new, rank, world), shard(depths, rank, world)
+
+
+def config_workload(args, rank: int, world: int):
+    """(prompts, max_new_tokens, exit_depths, arrival offsets or None) of this rank for ``--config``."""
+
+    import numpy as np
+
+    from oracle.workloads import huginn_workload, ouro_lognormal_workload, poisson_arrival_offsets
+
+    if args.config == 3:
+        p, m, d = huginn_workload(args.requests * world, vocab_size=65536, seed=args.seed, new_tokens=256, max_depth=32)
+        return shard(p, rank, world), shard(m, rank, world), shard(d, rank, world), None
+    if args.config == 2:
+        n = args.requests * world
+        p, m, d = ouro_lognormal_workload(n, vocab_size=OURO_1P4B["vocab_size"], seed=args.seed, out_cap=args.out_cap,
+                                          depth_probs=DEPTH_P2)
+        arr = poisson_arrival_offsets(np.random.default_rng(args.seed + 1), n, 20.0 * world)
+        return shard(p, rank, world), shard(m, rank, world), shard(d, rank, world), shard(arr, rank, world)
+    p, m, d = rank_workload(args.seed, args.requests, args.out_cap, rank, world)
+    return p, m, d, None
 
 
 def config4_trace(seed: int, n: int, rate: float, out_cap: int):
@@ -189,23 +211,41 @@ class ClockSampler:
         }
 
 
-def build_engine(args, device):
-    from continuous_depth_batching_b200 import ContinuousDepthBatchingConfig, ContinuousDepthBatchingEngine, OuroForCausalLM, OuroShape
+OURO_2P6B = {**OURO_1P4B, "num_hidden_layers": 48}
+DEPTH_P2 = (0.1, 0.2, 0.3, 0.4)
+# KV blocks of config 2 (48 layers x 4 last_exited slots: 25 MB per block) within ~140 GB of HBM
+CONFIG2_BLOCKS = 5600
 
-    shape = OuroShape(**OURO_1P4B)
-    model = OuroForCausalLM.random_init(shape, seed=1234, dtype=torch.bfloat16, device=device)
-    cfg = ContinuousDepthBatchingConfig(
-        block_size=16,
-        num_blocks=args.num_blocks,
-        max_recurrent_steps=4,
-        synthetic_exit_replay=True,
-        use_async_batching=False,
-        use_cuda_graph=not args.no_graph,
-        refill=True,
-        kv_policy="single",
-        max_model_len=4096,
-        max_num_seqs=256,
+
+def build_engine(args, device):
+    from continuous_depth_batching_b200 import (
+        ContinuousDepthBatchingConfig,
+        ContinuousDepthBatchingEngine,
+        HuginnForCausalLM,
+        OuroForCausalLM,
+        OuroShape,
     )
+    from continuous_depth_batching_b200.huginn import HuginnShape
+
+    config = getattr(args, "config", 1)
+    common = dict(block_size=16, synthetic_exit_replay=True, use_async_batching=False, use_cuda_graph=not args.no_graph,
+                  max_model_len=4096, max_num_seqs=256)
+    if config == 3:
+        shape = HuginnShape()  # Huginn-0125: 2/4/2 blocks, 5280 wide, 55 x 96 heads, SwiGLU 17920, vocab 65536
+        model = HuginnForCausalLM.random_init(shape, seed=1234, dtype=torch.bfloat16, device=device)
+        cfg = ContinuousDepthBatchingConfig(num_blocks=args.num_blocks, max_recurrent_steps=32, refill=True,
+                                            kv_policy="single", **common)
+    elif config == 2:
+        shape = OuroShape(**OURO_2P6B)
+        model = OuroForCausalLM.random_init(shape, seed=1234, dtype=torch.bfloat16, device=device)
+        cfg = ContinuousDepthBatchingConfig(num_blocks=min(args.num_blocks, CONFIG2_BLOCKS), max_recurrent_steps=4,
+                                            refill=not args.no_refill, kv_policy="last_exited",
+                                            kv_pressure_mode="reserve", **common)
+    else:
+        shape = OuroShape(**OURO_1P4B)
+        model = OuroForCausalLM.random_init(shape, seed=1234, dtype=torch.bfloat16, device=device)
+        cfg = ContinuousDepthBatchingConfig(num_blocks=args.num_blocks, max_recurrent_steps=4, refill=True,
+                                            kv_policy="single", **common)
     eng = ContinuousDepthBatchingEngine.from_model(
         model, cfg, device=device, fused_lm_head=getattr(args, "lm_head", "fused") == "fused"
     )
@@ -234,6 +274,7 @@ def attention_roofline(eng, shape, launches: list[tuple[list[int], list[int]]], 
 
     r = eng.runner
     D, H = shape.head_dim, shape.num_attention_heads
+    rope_mode = 2 if D == 96 else 1  # Huginn's interleaved fp32 RoPE tables, else Ouro's split-half
     total_bytes, total_ms, n = 0.0, 0.0, 0
     stream = r.stream
     for slots, pos in launches:
@@ -246,10 +287,10 @@ def attention_roofline(eng, shape, launches: list[tuple[list[int], list[int]]], 
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = 10
         with torch.cuda.stream(stream):
-            r._attention(b, 0, meta[0], meta[1], 2, 1)  # warm
+            r._attention(b, 0, meta[0], meta[1], 2, rope_mode)  # warm
             start.record(stream)
             for _ in range(reps):
-                r._attention(b, 0, meta[0], meta[1], 2, 1)
+                r._attention(b, 0, meta[0], meta[1], 2, rope_mode)
             end.record(stream)
         end.synchronize()
         ms = start.elapsed_time(end) / reps
@@ -324,12 +365,17 @@ def run_b200(args) -> None:
         # ranks wait for one another only at the start/end barriers and the result reduction;
         # a rank that never arrives ends the others' collective with an error after this timeout
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    if args.config == 3 and args.requests == 256:
+        args.requests = 128  # 128 requests
+    if args.config == 2 and args.requests == 256:
+        args.requests = 512  # 512 requests
     eng, shape = build_engine(args, device)
-    prompts, max_new, depths = rank_workload(args.seed, args.requests, args.out_cap, rank, world)
+    prompts, max_new, depths, arrivals = config_workload(args, rank, world)
     stream = eng.runner.stream
 
     def step():
-        return eng.generate_batch(prompts, max_new_tokens=max_new, eos_token_id=None, exit_depths=depths)
+        return eng.generate_batch(prompts, max_new_tokens=max_new, eos_token_id=None, exit_depths=depths,
+                                  arrival_offsets_s=arrivals)
 
     for _ in range(args.warmup):
         step()
@@ -398,11 +444,13 @@ def run_b200(args) -> None:
         roof = attention_roofline(eng, shape, sample, peak_gbs)
         roof["peak_source"] = peak_src
         peaks = json.loads(peaks_path.read_text()) if peaks_path.exists() else {}
-        whole = step_roofline(
-            shape, rec_positions, coda_sizes, prefill_batches, local_dev_s, peak_gbs,
-            peaks.get("bf16_tflops_sustained", 1400.0),
-        )
-        whole["scope"] = "rank 0, all timed steps; peaks: measured HBM copy and sustained cuBLAS bf16"
+        whole = None
+        if args.config != 3:
+            whole = step_roofline(
+                shape, rec_positions, coda_sizes, prefill_batches, local_dev_s, peak_gbs,
+                peaks.get("bf16_tflops_sustained", 1400.0),
+            )
+            whole["scope"] = "rank 0, all timed steps; peaks: measured HBM copy and sustained cuBLAS bf16"
         prompt_bytes = sum(len(p) for p in prompts) * 4 * 3
         line = {
             "metric": METRIC,
@@ -418,8 +466,8 @@ def run_b200(args) -> None:
             "dtype": "bf16",
             "data": "synthetic (seeded lognormal lengths, uniform token ids, categorical exit depths)",
             "config": {
-                "workload": "BASELINE config 1: Ouro-1.4B random-init, 256 concurrent requests, lognormal lengths, "
-                "replayed categorical depths (0.2,0.3,0.3,0.2), kv single, block 16, refill on",
+                "workload": CONFIG_LABELS[args.config] + ("" if args.config != 2 else
+                                                          (", refill off" if args.no_refill else ", refill on")),
                 "requests_per_gpu": args.requests,
                 "out_cap": args.out_cap,
                 "generated_tokens_per_step_per_gpu": gen_tokens // max(args.steps, 1),
@@ -452,7 +500,7 @@ def run_b200(args) -> None:
             "step_roofline": whole,
             "clocks": clocks.summary(),
         }
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and args.config == 1:
             line["same_sample"] = gpu_on_cpu_sample(eng)
             line["cpu_baseline"] = cpu_baseline(seconds=20.0)
         print(json.dumps(line), flush=True)
@@ -461,23 +509,35 @@ def run_b200(args) -> None:
         torch.distributed.destroy_process_group()
 
 
+CONFIG_LABELS = {
+    1: "BASELINE config 1: Ouro-1.4B random-init, 256 concurrent requests, lognormal lengths, replayed categorical "
+       "depths (0.2,0.3,0.3,0.2), kv single, block 16, refill on",
+    2: "BASELINE config 2: Ouro-2.6B (48 layers) random-init, 512 requests, Poisson arrivals at 20 req/s, lognormal "
+       "lengths, categorical depths (0.1,0.2,0.3,0.4), per-step KV as last_exited with reserve admission, block 16",
+    3: "BASELINE config 3: Huginn-0125 random-init (2/4/2 blocks, 5280 wide, 55x96 heads), 128 requests, prompts "
+       "U[64,512], 256 new tokens, truncated geometric depths (mean 12, 1..32), kv single, block 16, refill on",
+}
+
+
 def flop_bound_summary(shape, stats) -> dict:
     """The eq. (1) FLOP bound on the speed-up of this run's exit schedule over full depth
     (``continuous_depth_batching_b200.flop_bound``), from the model's stage weights (counted on a
     ``meta``-device model) and the mean recurrent steps per decoded token of the last step."""
 
-    from continuous_depth_batching_b200 import OuroForCausalLM
+    from continuous_depth_batching_b200 import HuginnForCausalLM, OuroForCausalLM
     from continuous_depth_batching_b200.flop_bound import stage_flops
 
+    huginn = hasattr(shape, "n_embd")
+    steps = shape.total_recurrent_steps if huginn else shape.total_ut_steps
     with torch.device("meta"):
-        f = stage_flops(OuroForCausalLM(shape))
-    mean_depth = stats.recurrent_steps / stats.coda_tokens if stats.coda_tokens else float(shape.total_ut_steps)
+        f = stage_flops(HuginnForCausalLM(shape) if huginn else OuroForCausalLM(shape))
+    mean_depth = stats.recurrent_steps / stats.coda_tokens if stats.coda_tokens else float(steps)
     return {
         **f.to_json_dict(),
         "f0_over_fr": round(f.f0_over_fr, 4),
         "mean_recurrent_steps": round(mean_depth, 4),
-        "max_depth": shape.total_ut_steps,
-        "ideal_speedup_vs_full_depth": round(f.ideal_speedup(max_depth=shape.total_ut_steps, mean_depth=mean_depth), 4),
+        "max_depth": steps,
+        "ideal_speedup_vs_full_depth": round(f.ideal_speedup(max_depth=steps, mean_depth=mean_depth), 4),
         "note": "compare with this line's value over `bench.py --engine cb` (same kernels, every token at full depth)",
     }
 
