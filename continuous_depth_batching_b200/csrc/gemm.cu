@@ -33,6 +33,15 @@
 // each token's argmax into a 64-bit atomicMax key, the last CTA writing the token ids.
 // Every wait is bounded; a wait that runs out records CDB_ERR_DEVICE_TIMEOUT and the CTA winds
 // down (no CTA waits on another CTA, so nothing can hang on a peer).
+//
+// Split mode. When a problem has fewer output tiles than SMs (every decode-shaped projection),
+// stream-K would cut each tile into many pieces and leave one CTA to read them all back. There
+// the K range of each tile is split over a thread-block cluster instead (grid x = tiles * s,
+// cluster (s, 1, 1), s <= 8): each CTA runs one piece, stages its fp32 partial tile in its own
+// drained ring, and after a cluster barrier every rank sums one slice of the tile over all ranks'
+// shared memory, in rank order (deterministic), and stores it. The ring is sized so two CTAs fit
+// on an SM: the next kernel's CTAs can then start (and stream weights) beside this one's.
+#include <cooperative_groups.h>
 #include <cuda.h>
 
 #include <cstring>
@@ -89,7 +98,8 @@ struct Params {
   long long iters;             // tiles * kb
   float* ws;                   // split partials: [2 * G][BM * BN] fp32
   int32_t* ctr;                // per-tile arrival counters (zero between calls)
-  int pair_store;              // EPI 0: c 4-byte aligned, ldc and N even
+  int pair_store;              // EPI 0: c 4-byte aligned, ldc and N even (EPI 1: act 4-byte aligned, ldc even)
+  int vec_store;               // split mode EPI 0: c 8-byte aligned, ldc % 4 == 0
   int32_t* status;
   // EPI 2 (LM head + argmax)
   unsigned long long* keys;
@@ -515,6 +525,225 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------ split mode
+constexpr int kMaxSplits = 8;  // portable cluster size
+constexpr int kSplitRing = 104 * 1024;
+
+template <int BN>
+struct SCfg {
+  static constexpr int X_BYTES = BN * BK * 2;
+  static constexpr int PART = BN * BM * 4;  // fp32 partial tile, staged in the drained ring
+  static constexpr int RING = PART > kSplitRing ? PART : kSplitRing;
+  static constexpr int SX = cmax(2, cmin(4, 32 * 1024 / X_BYTES));
+  static constexpr int SW = cmin(8, (RING - SX * X_BYTES) / W_BYTES);
+  static constexpr uint32_t TMEM_COLS = (uint32_t)pow2_at_least(BN);
+  static constexpr int CHUNKS = (BN + 31) / 32;
+  static constexpr int OFF_X = SW * W_BYTES;
+  static constexpr int OFF_BAR = RING;
+  static constexpr int NBAR = 2 * SW + 2 * SX + 2;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM = OFF_MISC + 64 + 1024;
+  static constexpr uint32_t IDESC = Cfg<BN>::IDESC;
+  static_assert(SW >= 2 && OFF_X + SX * X_BYTES <= RING, "split rings");
+};
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_split_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, Params p,
+                      int splits, int kb_per_split) {
+  using C = SCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* wring = smem;
+  uint8_t* xring = smem + C::OFF_X;
+  float* red = reinterpret_cast<float*>(smem);  // [BN][BM] fp32 partial, after the main loop
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* wempty = wfull + C::SW;
+  uint64_t* xfull = wempty + C::SW;
+  uint64_t* xempty = xfull + C::SX;
+  uint64_t* afull = xempty + C::SX;
+  uint64_t* mdrain = afull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
+  cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int rank = (int)cluster.block_rank();
+  const int wt = blockIdx.x / splits, tt = blockIdx.y;
+  const int k0 = rank * kb_per_split;
+  const int k1 = min(k0 + kb_per_split, p.kb);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::SW; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], 1);
+    }
+    for (int s = 0; s < C::SX; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);
+    }
+    mbar_init(afull, 1);
+    mbar_init(mdrain, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+
+  if (warp == kWarpW) {
+    if (lane == 0) {
+      prefetch_tensormap(&map_w);
+      int i = 0;
+      for (int k = k0; k < k1; ++k, ++i) {
+        const int s = i % C::SW;
+        if (!wait_or_abort(&wempty[s], (uint32_t)(((i / C::SW) & 1) ^ 1), p.status, s_abort)) break;
+        mbar_arrive_expect_tx(&wfull[s], W_BYTES);
+        tma_load_2d(wring + s * W_BYTES, &map_w, &wfull[s], k * BK, wt * BM);
+      }
+      for (int j = (i > C::SW ? i - C::SW : 0); j < i; ++j)
+        mbar_wait(&wfull[j % C::SW], (uint32_t)((j / C::SW) & 1), p.status);
+    }
+  } else if (warp == kWarpX) {
+    if (lane == 0) {
+      prefetch_tensormap(&map_x);
+      pdl_wait();
+      int i = 0;
+      for (int k = k0; k < k1; ++k, ++i) {
+        const int s = i % C::SX;
+        if (!wait_or_abort(&xempty[s], (uint32_t)(((i / C::SX) & 1) ^ 1), p.status, s_abort)) break;
+        mbar_arrive_expect_tx(&xfull[s], C::X_BYTES);
+        tma_load_2d(xring + s * C::X_BYTES, &map_x, &xfull[s], k * BK, tt * BN);
+      }
+      for (int j = (i > C::SX ? i - C::SX : 0); j < i; ++j)
+        mbar_wait(&xfull[j % C::SX], (uint32_t)((j / C::SX) & 1), p.status);
+    }
+  } else if (warp == kWarpMma) {
+    if (lane == 0) {
+      bool ok = true;
+      int i = 0;
+      for (int k = k0; k < k1; ++k, ++i) {
+        const int ws = i % C::SW, xs = i % C::SX;
+        if (!wait_or_abort(&wfull[ws], (uint32_t)((i / C::SW) & 1), p.status, s_abort) ||
+            !wait_or_abort(&xfull[xs], (uint32_t)((i / C::SX) & 1), p.status, s_abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a = smem_u32(wring + ws * W_BYTES);
+        const uint32_t b = smem_u32(xring + xs * C::X_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          umma_bf16(tmem, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), C::IDESC, (i > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&wempty[ws]);
+        umma_commit(&xempty[xs]);
+      }
+      if (ok) umma_commit(afull);
+      umma_commit(mdrain);
+      mbar_wait(mdrain, 0, p.status);
+    }
+    __syncwarp();
+  } else {
+    // epilogue warps: TMEM -> this CTA's fp32 partial red[token][weight row] in the drained ring
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    pdl_wait();
+    const bool ok = wait_or_abort(afull, 0, p.status, s_abort);
+    tc_fence_after();
+    if (ok) {
+#pragma unroll 1
+      for (int c = 0; c < C::CHUNKS; ++c) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c * 32 + j < BN) red[(c * 32 + j) * BM + row] = v[j];
+      }
+    }
+  }
+  tc_fence_before();
+  // Every thread of every CTA of the cluster passes both cluster barriers exactly once, error paths
+  // included, so no CTA can wait on one that has left.
+  cluster.sync();
+  {
+    // Rank r sums slice r of the tile over all ranks in rank order and stores it: element e is
+    // float4 e of every rank's partial (token e / (BM / 4), weight rows 4 * (e % (BM / 4)) ..).
+    constexpr int kVec = BM / 4;
+    constexpr int kTotal = BN * kVec;
+    const int per = (kTotal + splits - 1) / splits;
+    const int e_beg = rank * per;
+    const int e_end = min(e_beg + per, kTotal);
+    const float4* src[kMaxSplits];
+#pragma unroll
+    for (int sp = 0; sp < kMaxSplits; ++sp)
+      src[sp] = cluster.map_shared_rank(reinterpret_cast<const float4*>(red), sp < splits ? sp : 0);
+    constexpr int U = 4;  // elements in flight per thread
+    for (int e0 = e_beg + (int)threadIdx.x; e0 < e_end; e0 += U * THREADS) {
+      float4 acc[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int e = e0 + u * THREADS;
+        acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (e < e_end) {
+          acc[u] = src[0][e];
+#pragma unroll
+          for (int sp = 1; sp < kMaxSplits; ++sp)
+            if (sp < splits) {
+              const float4 t = src[sp][e];
+              acc[u].x += t.x;
+              acc[u].y += t.y;
+              acc[u].z += t.z;
+              acc[u].w += t.w;
+            }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int e = e0 + u * THREADS;
+        if (e >= e_end) continue;
+        const int gm = tt * BN + e / kVec;
+        const int gn = wt * BM + (e % kVec) * 4;
+        if (gm >= p.M || gn >= p.N) continue;
+        if constexpr (EPI == 1) {
+          // (gate_j, up_j, gate_j+1, up_j+1) -> act[j], act[j+1], j = gn / 2 (N % 4 == 0 here)
+          const float g0 = round_bf16(acc[u].x), u0 = round_bf16(acc[u].y);
+          const float g1 = round_bf16(acc[u].z), u1 = round_bf16(acc[u].w);
+          const float s0 = round_bf16(g0 / (1.f + expf(-g0)));
+          const float s1 = round_bf16(g1 / (1.f + expf(-g1)));
+          __nv_bfloat16* dst = p.c + (int64_t)gm * p.ldc + gn / 2;
+          if (p.pair_store) {
+            *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(s0 * u0, s1 * u1);
+          } else {
+            dst[0] = f_to_bf16(s0 * u0);
+            if (gn + 2 < p.N) dst[1] = f_to_bf16(s1 * u1);
+          }
+        } else {
+          __nv_bfloat16* dst = p.c + (int64_t)gm * p.ldc + gn;
+          if (p.vec_store && gn + 3 < p.N) {
+            *reinterpret_cast<uint2*>(dst) =
+                make_uint2(pack_bf16x2(acc[u].x, acc[u].y), pack_bf16x2(acc[u].z, acc[u].w));
+          } else {
+            const float a4[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
+            for (int j = 0; j < 4 && gn + j < p.N; ++j) dst[j] = f_to_bf16(a4[j]);
+          }
+        }
+      }
+    }
+  }
+  cluster.sync();  // peers finished reading this CTA's partial tile
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -600,6 +829,10 @@ static int launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p,
   return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, EPI>, mw, mx, p) == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
 }
 
+template <int BN, int EPI>
+static int launch_split(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, int splits, int kb_per_split,
+                        int tiles_w, int tiles_tok, cudaStream_t st);
+
 // Token-tile width for M token rows: M rounded up to a multiple of 16 (the UMMA N step for
 // M = 128) up to 256; wider problems tile the tokens by 256.
 static int tile_n_for(int M) { return M >= 256 ? 256 : ((M + 15) / 16) * 16; }
@@ -620,6 +853,106 @@ static Shape shape_for(int M, int N, int K, int max_ctas, int num_sms) {
   if (max_ctas > 0 && max_ctas < g) g = max_ctas;
   s.ctas = (int)(s.iters < g ? s.iters : g);
   return s;
+}
+
+template <int BN, int EPI>
+static cudaLaunchConfig_t split_config(dim3 grid, int splits, cudaStream_t st, cudaLaunchAttribute (&attr)[2]) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = SCfg<BN>::SMEM;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = splits;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cfg;
+}
+
+template <int BN, int EPI>
+static bool split_attr_ready() {
+  static int state = 0;  // 0 unknown, 1 ok, -1 failed
+  if (state == 0) {
+    state = cudaFuncSetAttribute(gemm_split_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 SCfg<BN>::SMEM) == cudaSuccess ? 1 : -1;
+    prefer_max_shared(reinterpret_cast<const void*>(gemm_split_kernel<BN, EPI>));
+  }
+  return state == 1;
+}
+
+// Clusters of s CTAs that can be resident at once (cudaOccupancyMaxActiveClusters, remembered).
+template <int BN, int EPI>
+static int max_active_clusters(int s) {
+  static std::mutex mu;
+  static int known[kMaxSplits + 1] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (known[s] == 0) {
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = split_config<BN, EPI>(dim3(s), s, nullptr, attr);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_split_kernel<BN, EPI>, &cfg) != cudaSuccess) n = 0;
+    cudaGetLastError();
+    known[s] = n > 0 ? n : -1;
+  }
+  return known[s];
+}
+
+// Split count for a problem of `tiles` output tiles and kb k-blocks: the s <= 8 whose busiest SM
+// streams the fewest k-blocks, given how many clusters of s fit at once (more than that runs in
+// waves); ties go to the smaller split (less to reduce).
+template <int BN, int EPI>
+static void choose_split(int tiles, int kb, int num_sms, int* splits, int* kb_per_split) {
+  const int cps = 2 * SCfg<BN>::SMEM <= 228 * 1024 ? 2 : 1;  // CTAs of this kernel that fit on one SM
+  long long best_cost = -1;
+  *splits = 1;
+  *kb_per_split = kb;
+  for (int s = 1; s <= kMaxSplits && s <= kb; ++s) {
+    const int kbs = (kb + s - 1) / s;
+    const int se = (kb + kbs - 1) / kbs;  // no empty split
+    if (se != s) continue;
+    const int cap = max_active_clusters<BN, EPI>(s);
+    if (cap <= 0) continue;
+    const long long waves = (tiles + cap - 1) / cap;
+    const long long in_wave = tiles < cap ? tiles : cap;
+    long long per_sm = (in_wave * s + num_sms - 1) / num_sms;
+    if (per_sm > cps) per_sm = cps;
+    const long long cost = waves * per_sm * kbs;
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      *splits = s;
+      *kb_per_split = kbs;
+    }
+  }
+}
+
+template <int BN, int EPI>
+static int launch_split(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, int splits, int kb_per_split,
+                        int tiles_w, int tiles_tok, cudaStream_t st) {
+  if (!split_attr_ready<BN, EPI>()) return CDB_ERR_CUDA;
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = split_config<BN, EPI>(dim3(tiles_w * splits, tiles_tok), splits, st, attr);
+  return cudaLaunchKernelEx(&cfg, gemm_split_kernel<BN, EPI>, mw, mx, p, splits, kb_per_split) == cudaSuccess
+             ? CDB_OK
+             : CDB_ERR_CUDA;
+}
+
+// Split mode when the tiles cannot fill the SMs (EPI 0 and 1; the LM head always has more tiles).
+template <int BN, int EPI>
+static int dispatch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, const struct Shape& s, int num_sms,
+                    bool split, cudaStream_t st) {
+  if constexpr (EPI != 2) {
+    if (split) {
+      if (!split_attr_ready<BN, EPI>()) return CDB_ERR_CUDA;
+      int splits = 1, kbs = p.kb;
+      choose_split<BN, EPI>(s.tiles_w * s.tiles_tok, p.kb, num_sms, &splits, &kbs);
+      return launch_split<BN, EPI>(mw, mx, p, splits, kbs, s.tiles_w, s.tiles_tok, st);
+    }
+  }
+  return launch<BN, EPI>(mw, mx, p, s.ctas, st);
 }
 
 // Shared host path of the three epilogues: c = epilogue(x[M,K] * w[N,K]^T).
@@ -652,7 +985,11 @@ static int run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, 
   p.ws = workspace;
   p.ctr = counters;
   p.pair_store = ((reinterpret_cast<uintptr_t>(c) & 3) == 0 && ldc % 2 == 0 && N % 2 == 0) ? 1 : 0;
+  p.vec_store = ((reinterpret_cast<uintptr_t>(c) & 7) == 0 && ldc % 4 == 0) ? 1 : 0;
   p.status = status;
+  const int sms = num_sms > 0 ? num_sms : 148;
+  // split mode for problems with fewer tiles than SMs; the SwiGLU epilogue there pairs 4 rows
+  const bool split = EPI != 2 && max_ctas <= 0 && (long long)s.tiles_w * s.tiles_tok < sms && (EPI != 1 || N % 4 == 0);
   if (epi2 != nullptr) {
     p.keys = epi2->keys;
     p.done = epi2->done;
@@ -664,7 +1001,7 @@ static int run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, 
   switch (s.bn) {
 #define CDB_GEMM_CASE(B) \
   case B:                \
-    return launch<B, EPI>(mw, mx, p, s.ctas, st);
+    return dispatch<B, EPI>(mw, mx, p, s, sms, split, st);
     CDB_GEMM_CASE(16)
     CDB_GEMM_CASE(32)
     CDB_GEMM_CASE(48)

@@ -7,7 +7,9 @@ Shapes cover the Ouro-1.4B projections (N 6144/2048/11264/2048, K 2048/5632, LM 
 token counts from 1 to prefill sizes, M/N/K tails (odd output widths take the scalar store
 path), persistent CTA counts from one CTA (every tile in one range) to one per SM (tiles split
 over CTAs and combined through the workspace), and repeated calls (the combine sums pieces in k
-order, so results are bit-identical and the tile counters come back zeroed).
+order, so results are bit-identical and the tile counters come back zeroed). Problems with fewer
+tiles than SMs take the split mode (K split over a thread-block cluster, reduced through
+distributed shared memory) unless a CTA count is forced.
 """
 
 from __future__ import annotations
@@ -154,7 +156,7 @@ def test_lm_head_argmax_matches_logits_argmax(gemm, m, vocab, k):
     table = torch.full((m + 3,), -5, dtype=torch.int32, device=DEV)
     token_rows = torch.arange(m, dtype=torch.int32, device=DEV) + 3
     sp = torch.cuda.current_stream().cuda_stream
-    logits = gemm(x, w)
+    logits = gemm(x, w, ctas=148)  # the LM head's own stream-K decomposition (one CTA per SM)
     ref = logits.float().argmax(dim=-1)
     for _ in range(2):
         _lib.call(
