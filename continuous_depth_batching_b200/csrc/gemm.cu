@@ -37,10 +37,13 @@
 // Split mode. When a problem has fewer output tiles than SMs (every decode-shaped projection),
 // stream-K would cut each tile into many pieces and leave one CTA to read them all back. There
 // the K range of each tile is split over a thread-block cluster instead (grid x = tiles * s,
-// cluster (s, 1, 1), s <= 8): each CTA runs one piece, stages its fp32 partial tile in its own
-// drained ring, and after a cluster barrier every rank sums one slice of the tile over all ranks'
-// shared memory, in rank order (deterministic), and stores it. The ring is sized so two CTAs fit
-// on an SM: the next kernel's CTAs can then start (and stream weights) beside this one's.
+// cluster (s, 1, 1), s <= 8): each CTA runs one piece, writes its fp32 partial to the workspace and
+// arrives (remote mbarrier arrive) on every rank's gather barrier; rank r owns a slice of the
+// tile's weight rows and, once all pieces have arrived, sums them in rank order (deterministic)
+// and stores. No cluster-wide barrier follows the main loop (a cluster is co-resident by
+// construction, so a rank waiting for its peers cannot starve them; the wait is still bounded).
+// The ring is sized so two CTAs fit on an SM: the next kernel's CTAs can then start (and stream
+// weights) beside this one's.
 #include <cooperative_groups.h>
 #include <cuda.h>
 
@@ -532,21 +535,52 @@ constexpr int kSplitRing = 104 * 1024;
 template <int BN>
 struct SCfg {
   static constexpr int X_BYTES = BN * BK * 2;
-  static constexpr int PART = BN * BM * 4;  // fp32 partial tile, staged in the drained ring
-  static constexpr int RING = PART > kSplitRing ? PART : kSplitRing;
+  static constexpr int RING = kSplitRing;
   static constexpr int SX = cmax(2, cmin(4, 32 * 1024 / X_BYTES));
   static constexpr int SW = cmin(8, (RING - SX * X_BYTES) / W_BYTES);
   static constexpr uint32_t TMEM_COLS = (uint32_t)pow2_at_least(BN);
   static constexpr int CHUNKS = (BN + 31) / 32;
   static constexpr int OFF_X = SW * W_BYTES;
   static constexpr int OFF_BAR = RING;
-  static constexpr int NBAR = 2 * SW + 2 * SX + 2;
+  static constexpr int NBAR = 2 * SW + 2 * SX + 3;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 64 + 1024;
   static constexpr uint32_t IDESC = Cfg<BN>::IDESC;
   static_assert(SW >= 2 && OFF_X + SX * X_BYTES <= RING, "split rings");
 };
 
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
+// Arrive (release, cluster scope) on the mbarrier at the same shared offset in CTA `rank` of the cluster.
+__device__ __forceinline__ void mbar_arrive_remote(uint64_t* bar, int rank) {
+  asm volatile(
+      "{\n\t.reg .b32 ra;\n\t"
+      "mapa.shared::cluster.u32 ra, %0, %1;\n\t"
+      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra];\n\t}" ::"r"(smem_u32(bar)),
+      "r"(rank)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// The split pieces of one tile run as one cluster. Each piece writes its fp32 partial to the
+// workspace (slot = the CTA's linear index, the stream-K piece layout) and arrives on the gather
+// barrier of every rank; rank r owns weight rows [r * RP, (r + 1) * RP) of the tile and, once all
+// pieces have arrived, sums them for its rows in rank order (deterministic) and stores. No CTA
+// waits on more than its own slice, and nothing follows the stores.
 template <int BN, int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_split_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, Params p,
@@ -556,23 +590,24 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* wring = smem;
   uint8_t* xring = smem + C::OFF_X;
-  float* red = reinterpret_cast<float*>(smem);  // [BN][BM] fp32 partial, after the main loop
   uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* wempty = wfull + C::SW;
   uint64_t* xfull = wempty + C::SW;
   uint64_t* xempty = xfull + C::SX;
   uint64_t* afull = xempty + C::SX;
   uint64_t* mdrain = afull + 1;
+  uint64_t* gather = mdrain + 1;  // one arrival per piece of this tile
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
-  cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
+  volatile int* s_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 16);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int rank = (int)cluster.block_rank();
+  const int rank = (int)(blockIdx.x % splits);  // == the CTA's rank in its (splits, 1, 1) cluster
   const int wt = blockIdx.x / splits, tt = blockIdx.y;
   const int k0 = rank * kb_per_split;
   const int k1 = min(k0 + kb_per_split, p.kb);
+  const int piece0 = blockIdx.y * gridDim.x + wt * splits;  // workspace slot of this tile's rank 0
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::SW; ++s) {
@@ -585,6 +620,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     mbar_init(afull, 1);
     mbar_init(mdrain, 1);
+    mbar_init(gather, splits);
     *s_abort = 0;
     fence_barrier_init();
   }
@@ -596,6 +632,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Every thread announces that its CTA's barriers are initialised; remote arrivals wait on it.
+  cluster_arrive_relaxed();
   pdl_trigger();
 
   if (warp == kWarpW) {
@@ -651,93 +689,100 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     __syncwarp();
   } else {
-    // epilogue warps: TMEM -> this CTA's fp32 partial red[token][weight row] in the drained ring
+    // ------------------------------------------------------------ epilogue (warps 2..5)
     const int q = warp & 3;
     const int row = q * 32 + lane;
-    pdl_wait();
+    const int et = threadIdx.x - 64;
+    pdl_wait();  // the workspace and outputs may still be in use by the predecessor
     const bool ok = wait_or_abort(afull, 0, p.status, s_abort);
     tc_fence_after();
+    // 1. This piece's partial -> workspace slot (float4 (chunk * 8 + j / 4) * BM + row).
+    float4* mine = reinterpret_cast<float4*>(p.ws + (size_t)(piece0 + rank) * (BM * BN));
     if (ok) {
 #pragma unroll 1
       for (int c = 0; c < C::CHUNKS; ++c) {
         float v[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c * 32 + j < BN) red[(c * 32 + j) * BM + row] = v[j];
+        for (int j4 = 0; j4 < 8; ++j4)
+          if (c * 32 + j4 * 4 < BN)
+            mine[(c * 8 + j4) * BM + row] = make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
       }
     }
+    __threadfence();
+    __syncwarp();
+    cluster_wait();  // every CTA of the cluster has initialised its gather barrier
+    epi_bar();
+    if (et == 0)
+      for (int r = 0; r < splits; ++r) mbar_arrive_remote(gather, r);
+    // 2. Wait for every piece, then reduce this rank's rows in rank order and store.
+    if (et == 0) {
+      bool got = false;
+      for (uint32_t i = 0; i < kSpinLimit; ++i)
+        if (mbar_try_wait_cluster(gather, 0)) {
+          got = true;
+          break;
+        }
+      if (!got) set_error(p.status, CDB_ERR_DEVICE_TIMEOUT);
+      *s_flag = got ? 1 : 0;
+    }
+    epi_bar();
+    if (*s_flag) {
+      constexpr int kCols = BN / 4;  // float4 columns (4 tokens each)
+      int rp = (BM + splits - 1) / splits;
+      rp = (rp + 1) & ~1;  // even, so SwiGLU gate/up row pairs stay in one slice
+      const int r0 = rank * rp;
+      const int r1 = min(BM, r0 + rp);
+      const int rows = r1 - r0;
+      const float4* base = reinterpret_cast<const float4*>(p.ws + (size_t)piece0 * (BM * BN));
+      if constexpr (EPI == 1) {
+        const int pairs = rows / 2;
+        for (int e = et; e < pairs * kCols; e += kEpiThreads) {
+          const int rr = r0 + 2 * (e % pairs), col = e / pairs;
+          float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
+          for (int sp = 0; sp < splits; ++sp) {
+            const float4* src = base + (size_t)sp * (BM * BN / 4) + col * BM + rr;
+            const float4 a = ld_cg_f4(src), b = ld_cg_f4(src + 1);
+            g.x += a.x; g.y += a.y; g.z += a.z; g.w += a.w;
+            u.x += b.x; u.y += b.y; u.z += b.z; u.w += b.w;
+          }
+          const int n = wt * BM + rr;  // gate row (even); act column n / 2
+          const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int tok = tt * BN + col * 4 + j;
+            if (tok < p.M && n < p.N) {
+              const float gf = round_bf16(gv[j]), uf = round_bf16(uv[j]);
+              const float sl = round_bf16(gf / (1.f + expf(-gf)));
+              p.c[(int64_t)tok * p.ldc + n / 2] = f_to_bf16(sl * uf);
+            }
+          }
+        }
+      } else {
+        for (int e = et; e < rows * kCols; e += kEpiThreads) {
+          const int rr = r0 + e % rows, col = e / rows;
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int sp = 0; sp < splits; ++sp) {
+            const float4 a = ld_cg_f4(base + (size_t)sp * (BM * BN / 4) + col * BM + rr);
+            acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+          }
+          const int n = wt * BM + rr;
+          const float av[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int tok = tt * BN + col * 4 + j;
+            if (tok < p.M && n < p.N) p.c[(int64_t)tok * p.ldc + n] = f_to_bf16(av[j]);
+          }
+        }
+      }
+    }
+  }
+  if (warp < 2 || warp > 5) {  // the epilogue warps waited above; pair every other arrive with a wait
+    __syncwarp();
+    cluster_wait();
   }
   tc_fence_before();
-  // Every thread of every CTA of the cluster passes both cluster barriers exactly once, error paths
-  // included, so no CTA can wait on one that has left.
-  cluster.sync();
-  {
-    // Rank r sums slice r of the tile over all ranks in rank order and stores it: element e is
-    // float4 e of every rank's partial (token e / (BM / 4), weight rows 4 * (e % (BM / 4)) ..).
-    constexpr int kVec = BM / 4;
-    constexpr int kTotal = BN * kVec;
-    const int per = (kTotal + splits - 1) / splits;
-    const int e_beg = rank * per;
-    const int e_end = min(e_beg + per, kTotal);
-    const float4* src[kMaxSplits];
-#pragma unroll
-    for (int sp = 0; sp < kMaxSplits; ++sp)
-      src[sp] = cluster.map_shared_rank(reinterpret_cast<const float4*>(red), sp < splits ? sp : 0);
-    constexpr int U = 4;  // elements in flight per thread
-    for (int e0 = e_beg + (int)threadIdx.x; e0 < e_end; e0 += U * THREADS) {
-      float4 acc[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int e = e0 + u * THREADS;
-        acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (e < e_end) {
-          acc[u] = src[0][e];
-#pragma unroll
-          for (int sp = 1; sp < kMaxSplits; ++sp)
-            if (sp < splits) {
-              const float4 t = src[sp][e];
-              acc[u].x += t.x;
-              acc[u].y += t.y;
-              acc[u].z += t.z;
-              acc[u].w += t.w;
-            }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int e = e0 + u * THREADS;
-        if (e >= e_end) continue;
-        const int gm = tt * BN + e / kVec;
-        const int gn = wt * BM + (e % kVec) * 4;
-        if (gm >= p.M || gn >= p.N) continue;
-        if constexpr (EPI == 1) {
-          // (gate_j, up_j, gate_j+1, up_j+1) -> act[j], act[j+1], j = gn / 2 (N % 4 == 0 here)
-          const float g0 = round_bf16(acc[u].x), u0 = round_bf16(acc[u].y);
-          const float g1 = round_bf16(acc[u].z), u1 = round_bf16(acc[u].w);
-          const float s0 = round_bf16(g0 / (1.f + expf(-g0)));
-          const float s1 = round_bf16(g1 / (1.f + expf(-g1)));
-          __nv_bfloat16* dst = p.c + (int64_t)gm * p.ldc + gn / 2;
-          if (p.pair_store) {
-            *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(s0 * u0, s1 * u1);
-          } else {
-            dst[0] = f_to_bf16(s0 * u0);
-            if (gn + 2 < p.N) dst[1] = f_to_bf16(s1 * u1);
-          }
-        } else {
-          __nv_bfloat16* dst = p.c + (int64_t)gm * p.ldc + gn;
-          if (p.vec_store && gn + 3 < p.N) {
-            *reinterpret_cast<uint2*>(dst) =
-                make_uint2(pack_bf16x2(acc[u].x, acc[u].y), pack_bf16x2(acc[u].z, acc[u].w));
-          } else {
-            const float a4[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
-            for (int j = 0; j < 4 && gn + j < p.N; ++j) dst[j] = f_to_bf16(a4[j]);
-          }
-        }
-      }
-    }
-  }
-  cluster.sync();  // peers finished reading this CTA's partial tile
+  __syncthreads();
   if (warp == kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
@@ -943,12 +988,13 @@ static int launch_split(const CUtensorMap& mw, const CUtensorMap& mx, const Para
 // Split mode when the tiles cannot fill the SMs (EPI 0 and 1; the LM head always has more tiles).
 template <int BN, int EPI>
 static int dispatch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, const struct Shape& s, int num_sms,
-                    bool split, cudaStream_t st) {
+                    bool split, int64_t workspace_elems, cudaStream_t st) {
   if constexpr (EPI != 2) {
     if (split) {
       if (!split_attr_ready<BN, EPI>()) return CDB_ERR_CUDA;
       int splits = 1, kbs = p.kb;
       choose_split<BN, EPI>(s.tiles_w * s.tiles_tok, p.kb, num_sms, &splits, &kbs);
+      if ((int64_t)s.tiles_w * s.tiles_tok * splits * BM * BN > workspace_elems) return CDB_ERR_INVALID_ARGUMENT;
       return launch_split<BN, EPI>(mw, mx, p, splits, kbs, s.tiles_w, s.tiles_tok, st);
     }
   }
@@ -1001,7 +1047,7 @@ static int run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, 
   switch (s.bn) {
 #define CDB_GEMM_CASE(B) \
   case B:                \
-    return dispatch<B, EPI>(mw, mx, p, s, sms, split, st);
+    return dispatch<B, EPI>(mw, mx, p, s, sms, split, workspace_elems, st);
     CDB_GEMM_CASE(16)
     CDB_GEMM_CASE(32)
     CDB_GEMM_CASE(48)

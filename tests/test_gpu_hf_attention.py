@@ -58,7 +58,7 @@ def _module(layer: int, d: int):
 @pytest.mark.parametrize("heads,d", [(16, 128), (4, 64), (5, 96)])
 def test_decode_branch_matches_cpu_contract(heads, d):
     gen = torch.Generator().manual_seed(heads * d)
-    nb, b, width = 96, 20, 6
+    nb, b, width = 160, 20, 6
     cache = Cache(3, (nb + 2) * BS, heads, d, "cpu", gen)
     gpu_cache = cache.copy_to("cuda")
     seqlen = torch.randint(0, width * BS, (b,), generator=gen)
