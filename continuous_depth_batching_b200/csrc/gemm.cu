@@ -959,6 +959,8 @@ static void choose_split(int tiles, int kb, int num_sms, int* splits, int* kb_pe
     const int kbs = (kb + s - 1) / s;
     const int se = (kb + kbs - 1) / kbs;  // no empty split
     if (se != s) continue;
+    // one wave that the workspace (2 pieces per SM) holds
+    if ((long long)tiles * s > 2LL * num_sms || (long long)tiles * s > (long long)cps * num_sms) continue;
     const int cap = max_active_clusters<BN, EPI>(s);
     if (cap <= 0) continue;
     const long long waves = (tiles + cap - 1) / cap;
