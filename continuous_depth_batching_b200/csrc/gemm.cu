@@ -34,16 +34,10 @@
 // Every wait is bounded; a wait that runs out records CDB_ERR_DEVICE_TIMEOUT and the CTA winds
 // down (no CTA waits on another CTA, so nothing can hang on a peer).
 //
-// Split mode. When a problem has fewer output tiles than SMs (every decode-shaped projection),
-// stream-K would cut each tile into many pieces and leave one CTA to read them all back. There
-// the K range of each tile is split over a thread-block cluster instead (grid x = tiles * s,
-// cluster (s, 1, 1), s <= 8): each CTA runs one piece, writes its fp32 partial to the workspace and
-// arrives (remote mbarrier arrive) on every rank's gather barrier; rank r owns a slice of the
-// tile's weight rows and, once all pieces have arrived, sums them in rank order (deterministic)
-// and stores. No cluster-wide barrier follows the main loop (a cluster is co-resident by
-// construction, so a rank waiting for its peers cannot starve them; the wait is still bounded).
-// The ring is sized so two CTAs fit on an SM: the next kernel's CTAs can then start (and stream
-// weights) beside this one's.
+// Split mode (gemm_cluster.cuh). When a problem has fewer output tiles than SMs (every
+// decode-shaped projection), stream-K would cut each tile into many pieces and leave one CTA to
+// read them all back; there the K range of each tile is split over a thread-block cluster whose
+// ranks reduce the partial tile through distributed shared memory instead.
 #include <cooperative_groups.h>
 #include <cuda.h>
 
@@ -528,267 +522,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-// ------------------------------------------------------------------ split mode
-constexpr int kMaxSplits = 8;  // portable cluster size
-constexpr int kSplitRing = 104 * 1024;
-
-template <int BN>
-struct SCfg {
-  static constexpr int X_BYTES = BN * BK * 2;
-  static constexpr int RING = kSplitRing;
-  static constexpr int SX = cmax(2, cmin(4, 32 * 1024 / X_BYTES));
-  static constexpr int SW = cmin(8, (RING - SX * X_BYTES) / W_BYTES);
-  static constexpr uint32_t TMEM_COLS = (uint32_t)pow2_at_least(BN);
-  static constexpr int CHUNKS = (BN + 31) / 32;
-  static constexpr int OFF_X = SW * W_BYTES;
-  static constexpr int OFF_BAR = RING;
-  static constexpr int NBAR = 2 * SW + 2 * SX + 3;
-  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int SMEM = OFF_MISC + 64 + 1024;
-  static constexpr uint32_t IDESC = Cfg<BN>::IDESC;
-  static_assert(SW >= 2 && OFF_X + SX * X_BYTES <= RING, "split rings");
-};
-
-__device__ __forceinline__ void cluster_arrive_relaxed() {
-  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
-
-// Arrive (release, cluster scope) on the mbarrier at the same shared offset in CTA `rank` of the cluster.
-__device__ __forceinline__ void mbar_arrive_remote(uint64_t* bar, int rank) {
-  asm volatile(
-      "{\n\t.reg .b32 ra;\n\t"
-      "mapa.shared::cluster.u32 ra, %0, %1;\n\t"
-      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra];\n\t}" ::"r"(smem_u32(bar)),
-      "r"(rank)
-      : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-// The split pieces of one tile run as one cluster. Each piece writes its fp32 partial to the
-// workspace (slot = the CTA's linear index, the stream-K piece layout) and arrives on the gather
-// barrier of every rank; rank r owns weight rows [r * RP, (r + 1) * RP) of the tile and, once all
-// pieces have arrived, sums them for its rows in rank order (deterministic) and stores. No CTA
-// waits on more than its own slice, and nothing follows the stores.
-template <int BN, int EPI>
-__global__ void __launch_bounds__(THREADS, 1)
-    gemm_split_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, Params p,
-                      int splits, int kb_per_split) {
-  using C = SCfg<BN>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* wring = smem;
-  uint8_t* xring = smem + C::OFF_X;
-  uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* wempty = wfull + C::SW;
-  uint64_t* xfull = wempty + C::SW;
-  uint64_t* xempty = xfull + C::SX;
-  uint64_t* afull = xempty + C::SX;
-  uint64_t* mdrain = afull + 1;
-  uint64_t* gather = mdrain + 1;  // one arrival per piece of this tile
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
-  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
-  volatile int* s_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 16);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int rank = (int)(blockIdx.x % splits);  // == the CTA's rank in its (splits, 1, 1) cluster
-  const int wt = blockIdx.x / splits, tt = blockIdx.y;
-  const int k0 = rank * kb_per_split;
-  const int k1 = min(k0 + kb_per_split, p.kb);
-  const int piece0 = blockIdx.y * gridDim.x + wt * splits;  // workspace slot of this tile's rank 0
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < C::SW; ++s) {
-      mbar_init(&wfull[s], 1);
-      mbar_init(&wempty[s], 1);
-    }
-    for (int s = 0; s < C::SX; ++s) {
-      mbar_init(&xfull[s], 1);
-      mbar_init(&xempty[s], 1);
-    }
-    mbar_init(afull, 1);
-    mbar_init(mdrain, 1);
-    mbar_init(gather, splits);
-    *s_abort = 0;
-    fence_barrier_init();
-  }
-  if (warp == kWarpMma) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  // Every thread announces that its CTA's barriers are initialised; remote arrivals wait on it.
-  cluster_arrive_relaxed();
-  pdl_trigger();
-
-  if (warp == kWarpW) {
-    if (lane == 0) {
-      prefetch_tensormap(&map_w);
-      int i = 0;
-      for (int k = k0; k < k1; ++k, ++i) {
-        const int s = i % C::SW;
-        if (!wait_or_abort(&wempty[s], (uint32_t)(((i / C::SW) & 1) ^ 1), p.status, s_abort)) break;
-        mbar_arrive_expect_tx(&wfull[s], W_BYTES);
-        tma_load_2d(wring + s * W_BYTES, &map_w, &wfull[s], k * BK, wt * BM);
-      }
-      for (int j = (i > C::SW ? i - C::SW : 0); j < i; ++j)
-        mbar_wait(&wfull[j % C::SW], (uint32_t)((j / C::SW) & 1), p.status);
-    }
-  } else if (warp == kWarpX) {
-    if (lane == 0) {
-      prefetch_tensormap(&map_x);
-      pdl_wait();
-      int i = 0;
-      for (int k = k0; k < k1; ++k, ++i) {
-        const int s = i % C::SX;
-        if (!wait_or_abort(&xempty[s], (uint32_t)(((i / C::SX) & 1) ^ 1), p.status, s_abort)) break;
-        mbar_arrive_expect_tx(&xfull[s], C::X_BYTES);
-        tma_load_2d(xring + s * C::X_BYTES, &map_x, &xfull[s], k * BK, tt * BN);
-      }
-      for (int j = (i > C::SX ? i - C::SX : 0); j < i; ++j)
-        mbar_wait(&xfull[j % C::SX], (uint32_t)((j / C::SX) & 1), p.status);
-    }
-  } else if (warp == kWarpMma) {
-    if (lane == 0) {
-      bool ok = true;
-      int i = 0;
-      for (int k = k0; k < k1; ++k, ++i) {
-        const int ws = i % C::SW, xs = i % C::SX;
-        if (!wait_or_abort(&wfull[ws], (uint32_t)((i / C::SW) & 1), p.status, s_abort) ||
-            !wait_or_abort(&xfull[xs], (uint32_t)((i / C::SX) & 1), p.status, s_abort)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t a = smem_u32(wring + ws * W_BYTES);
-        const uint32_t b = smem_u32(xring + xs * C::X_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
-          umma_bf16(tmem, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), C::IDESC, (i > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&wempty[ws]);
-        umma_commit(&xempty[xs]);
-      }
-      if (ok) umma_commit(afull);
-      umma_commit(mdrain);
-      mbar_wait(mdrain, 0, p.status);
-    }
-    __syncwarp();
-  } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5)
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
-    const int et = threadIdx.x - 64;
-    pdl_wait();  // the workspace and outputs may still be in use by the predecessor
-    const bool ok = wait_or_abort(afull, 0, p.status, s_abort);
-    tc_fence_after();
-    // 1. This piece's partial -> workspace slot (float4 (chunk * 8 + j / 4) * BM + row).
-    float4* mine = reinterpret_cast<float4*>(p.ws + (size_t)(piece0 + rank) * (BM * BN));
-    if (ok) {
-#pragma unroll 1
-      for (int c = 0; c < C::CHUNKS; ++c) {
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
-#pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4)
-          if (c * 32 + j4 * 4 < BN)
-            mine[(c * 8 + j4) * BM + row] = make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
-      }
-    }
-    __threadfence();
-    __syncwarp();
-    cluster_wait();  // every CTA of the cluster has initialised its gather barrier
-    epi_bar();
-    if (et == 0)
-      for (int r = 0; r < splits; ++r) mbar_arrive_remote(gather, r);
-    // 2. Wait for every piece, then reduce this rank's rows in rank order and store.
-    if (et == 0) {
-      bool got = false;
-      for (uint32_t i = 0; i < kSpinLimit; ++i)
-        if (mbar_try_wait_cluster(gather, 0)) {
-          got = true;
-          break;
-        }
-      if (!got) set_error(p.status, CDB_ERR_DEVICE_TIMEOUT);
-      *s_flag = got ? 1 : 0;
-    }
-    epi_bar();
-    if (*s_flag) {
-      constexpr int kCols = BN / 4;  // float4 columns (4 tokens each)
-      int rp = (BM + splits - 1) / splits;
-      rp = (rp + 1) & ~1;  // even, so SwiGLU gate/up row pairs stay in one slice
-      const int r0 = rank * rp;
-      const int r1 = min(BM, r0 + rp);
-      const int rows = r1 - r0;
-      const float4* base = reinterpret_cast<const float4*>(p.ws + (size_t)piece0 * (BM * BN));
-      if constexpr (EPI == 1) {
-        const int pairs = rows / 2;
-        for (int e = et; e < pairs * kCols; e += kEpiThreads) {
-          const int rr = r0 + 2 * (e % pairs), col = e / pairs;
-          float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
-          for (int sp = 0; sp < splits; ++sp) {
-            const float4* src = base + (size_t)sp * (BM * BN / 4) + col * BM + rr;
-            const float4 a = ld_cg_f4(src), b = ld_cg_f4(src + 1);
-            g.x += a.x; g.y += a.y; g.z += a.z; g.w += a.w;
-            u.x += b.x; u.y += b.y; u.z += b.z; u.w += b.w;
-          }
-          const int n = wt * BM + rr;  // gate row (even); act column n / 2
-          const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int tok = tt * BN + col * 4 + j;
-            if (tok < p.M && n < p.N) {
-              const float gf = round_bf16(gv[j]), uf = round_bf16(uv[j]);
-              const float sl = round_bf16(gf / (1.f + expf(-gf)));
-              p.c[(int64_t)tok * p.ldc + n / 2] = f_to_bf16(sl * uf);
-            }
-          }
-        }
-      } else {
-        for (int e = et; e < rows * kCols; e += kEpiThreads) {
-          const int rr = r0 + e % rows, col = e / rows;
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int sp = 0; sp < splits; ++sp) {
-            const float4 a = ld_cg_f4(base + (size_t)sp * (BM * BN / 4) + col * BM + rr);
-            acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
-          }
-          const int n = wt * BM + rr;
-          const float av[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int tok = tt * BN + col * 4 + j;
-            if (tok < p.M && n < p.N) p.c[(int64_t)tok * p.ldc + n] = f_to_bf16(av[j]);
-          }
-        }
-      }
-    }
-  }
-  if (warp < 2 || warp > 5) {  // the epilogue warps waited above; pair every other arrive with a wait
-    __syncwarp();
-    cluster_wait();
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == kWarpMma) {
-    tc_fence_after();
-    tmem_dealloc(tmem, C::TMEM_COLS);
-  }
-}
-
 // ------------------------------------------------------------------ host side
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -874,10 +607,6 @@ static int launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p,
   return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, EPI>, mw, mx, p) == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
 }
 
-template <int BN, int EPI>
-static int launch_split(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, int splits, int kb_per_split,
-                        int tiles_w, int tiles_tok, cudaStream_t st);
-
 // Token-tile width for M token rows: M rounded up to a multiple of 16 (the UMMA N step for
 // M = 128) up to 256; wider problems tile the tokens by 256.
 static int tile_n_for(int M) { return M >= 256 ? 256 : ((M + 15) / 16) * 16; }
@@ -900,104 +629,27 @@ static Shape shape_for(int M, int N, int K, int max_ctas, int num_sms) {
   return s;
 }
 
-template <int BN, int EPI>
-static cudaLaunchConfig_t split_config(dim3 grid, int splits, cudaStream_t st, cudaLaunchAttribute (&attr)[2]) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(THREADS);
-  cfg.dynamicSmemBytes = SCfg<BN>::SMEM;
-  cfg.stream = st;
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = splits;
-  attr[1].val.clusterDim.y = 1;
-  attr[1].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  return cfg;
-}
+#include "gemm_cluster.cuh"
 
-template <int BN, int EPI>
-static bool split_attr_ready() {
-  static int state = 0;  // 0 unknown, 1 ok, -1 failed
-  if (state == 0) {
-    state = cudaFuncSetAttribute(gemm_split_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 SCfg<BN>::SMEM) == cudaSuccess ? 1 : -1;
-    prefer_max_shared(reinterpret_cast<const void*>(gemm_split_kernel<BN, EPI>));
-  }
-  return state == 1;
-}
-
-// Clusters of s CTAs that can be resident at once (cudaOccupancyMaxActiveClusters, remembered).
-template <int BN, int EPI>
-static int max_active_clusters(int s) {
-  static std::mutex mu;
-  static int known[kMaxSplits + 1] = {};
-  std::lock_guard<std::mutex> lock(mu);
-  if (known[s] == 0) {
-    cudaLaunchAttribute attr[2];
-    cudaLaunchConfig_t cfg = split_config<BN, EPI>(dim3(s), s, nullptr, attr);
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, gemm_split_kernel<BN, EPI>, &cfg) != cudaSuccess) n = 0;
-    cudaGetLastError();
-    known[s] = n > 0 ? n : -1;
-  }
-  return known[s];
-}
-
-// Split count for a problem of `tiles` output tiles and kb k-blocks: the s <= 8 whose busiest SM
-// streams the fewest k-blocks, given how many clusters of s fit at once (more than that runs in
-// waves); ties go to the smaller split (less to reduce).
-template <int BN, int EPI>
-static void choose_split(int tiles, int kb, int num_sms, int* splits, int* kb_per_split) {
-  const int cps = 2 * SCfg<BN>::SMEM <= 228 * 1024 ? 2 : 1;  // CTAs of this kernel that fit on one SM
-  long long best_cost = -1;
-  *splits = 1;
-  *kb_per_split = kb;
-  for (int s = 1; s <= kMaxSplits && s <= kb; ++s) {
-    const int kbs = (kb + s - 1) / s;
-    const int se = (kb + kbs - 1) / kbs;  // no empty split
-    if (se != s) continue;
-    // one wave that the workspace (2 pieces per SM) holds
-    if ((long long)tiles * s > 2LL * num_sms || (long long)tiles * s > (long long)cps * num_sms) continue;
-    const int cap = max_active_clusters<BN, EPI>(s);
-    if (cap <= 0) continue;
-    const long long waves = (tiles + cap - 1) / cap;
-    const long long in_wave = tiles < cap ? tiles : cap;
-    long long per_sm = (in_wave * s + num_sms - 1) / num_sms;
-    if (per_sm > cps) per_sm = cps;
-    const long long cost = waves * per_sm * kbs;
-    if (best_cost < 0 || cost < best_cost) {
-      best_cost = cost;
-      *splits = s;
-      *kb_per_split = kbs;
-    }
-  }
-}
-
-template <int BN, int EPI>
-static int launch_split(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, int splits, int kb_per_split,
-                        int tiles_w, int tiles_tok, cudaStream_t st) {
-  if (!split_attr_ready<BN, EPI>()) return CDB_ERR_CUDA;
-  cudaLaunchAttribute attr[2];
-  cudaLaunchConfig_t cfg = split_config<BN, EPI>(dim3(tiles_w * splits, tiles_tok), splits, st, attr);
-  return cudaLaunchKernelEx(&cfg, gemm_split_kernel<BN, EPI>, mw, mx, p, splits, kb_per_split) == cudaSuccess
-             ? CDB_OK
-             : CDB_ERR_CUDA;
-}
-
-// Split mode when the tiles cannot fill the SMs (EPI 0 and 1; the LM head always has more tiles).
+// Split mode (gemm_cluster.cuh) when the tiles cannot fill the SMs (EPI 0 and 1; the LM head
+// always has more tiles), stream-K otherwise.
 template <int BN, int EPI>
 static int dispatch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, const struct Shape& s, int num_sms,
-                    bool split, int64_t workspace_elems, cudaStream_t st) {
+                    bool split, cudaStream_t st) {
   if constexpr (EPI != 2) {
     if (split) {
-      if (!split_attr_ready<BN, EPI>()) return CDB_ERR_CUDA;
-      int splits = 1, kbs = p.kb;
-      choose_split<BN, EPI>(s.tiles_w * s.tiles_tok, p.kb, num_sms, &splits, &kbs);
-      if ((int64_t)s.tiles_w * s.tiles_tok * splits * BM * BN > workspace_elems) return CDB_ERR_INVALID_ARGUMENT;
-      return launch_split<BN, EPI>(mw, mx, p, splits, kbs, s.tiles_w, s.tiles_tok, st);
+      cl::CParams c;
+      c.c = p.c;
+      c.ldc = p.ldc;
+      c.M = p.M;
+      c.N = p.N;
+      c.K = p.K;
+      c.splits = 1;
+      c.kb_per_split = p.kb;
+      c.num_kb = p.kb;
+      c.vec_store = p.vec_store;
+      c.status = p.status;
+      return cl::launch_cluster<BN, EPI>(mw, mx, c, s.tiles_w, s.tiles_tok, num_sms, st);
     }
   }
   return launch<BN, EPI>(mw, mx, p, s.ctas, st);
@@ -1049,7 +701,7 @@ static int run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, 
   switch (s.bn) {
 #define CDB_GEMM_CASE(B) \
   case B:                \
-    return dispatch<B, EPI>(mw, mx, p, s, sms, split, workspace_elems, st);
+    return dispatch<B, EPI>(mw, mx, p, s, sms, split, st);
     CDB_GEMM_CASE(16)
     CDB_GEMM_CASE(32)
     CDB_GEMM_CASE(48)
