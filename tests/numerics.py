@@ -6,8 +6,11 @@ that compounds over layers and recurrent steps. Three references run the same in
 oracle ("truth", no intermediate rounding), the bf16 oracle (the reference's rounding points,
 standing in for the reference's own bf16 path) and the GPU. The bars:
 
-* accuracy: the GPU's max-abs error against fp32 is no worse than the bf16 oracle's own error
-  against fp32, up to 25%;
+* accuracy: the GPU's RMS error against fp32 is no worse than the bf16 oracle's own RMS error
+  against fp32, up to 25%; its max-abs error is no worse than the oracle's, up to 50% (the
+  maximum over hundreds of thousands of logits is an extreme-value statistic: two evaluations
+  that differ only in fp32 summation order land on either side of each other there by chance,
+  while their RMS errors agree closely);
 * consistency: the GPU differs from the bf16 oracle by less than the bf16 oracle differs from
   fp32 (two bf16 evaluations of the same network are closer to each other than to the truth);
 * greedy tokens: the GPU's argmax equals the bf16 oracle's at >= 99% of the *decided* positions,
@@ -40,6 +43,7 @@ def compare_lm_launches(gpu: list[torch.Tensor], ref16: list[torch.Tensor], trut
     r = torch.cat([x.float().cpu() for x in ref16])
     t = torch.cat([x.float().cpu() for x in truth])
     diff = (g - r).abs().max().item()
+    rms = lambda a, b: ((a - b) ** 2).mean().sqrt().item()  # noqa: E731
     top2 = r.topk(2, dim=-1).values
     margin = top2[:, 0] - top2[:, 1]
     same = g.argmax(-1) == r.argmax(-1)
@@ -47,6 +51,8 @@ def compare_lm_launches(gpu: list[torch.Tensor], ref16: list[torch.Tensor], trut
     return {
         "gpu_err": (g - t).abs().max().item(),
         "ref_err": (r - t).abs().max().item(),
+        "gpu_rms": rms(g, t),
+        "ref_rms": rms(r, t),
         "gpu_vs_ref": diff,
         "logit_scale": r.abs().max().item(),
         "agree_all": same.float().mean().item(),
@@ -57,6 +63,7 @@ def compare_lm_launches(gpu: list[torch.Tensor], ref16: list[torch.Tensor], trut
 
 
 def assert_report(rep: dict, floor: float = 1e-3) -> None:
-    assert rep["gpu_err"] <= 1.25 * rep["ref_err"] + floor, rep
+    assert rep["gpu_rms"] <= 1.25 * rep["ref_rms"] + floor, rep
+    assert rep["gpu_err"] <= 1.5 * rep["ref_err"] + floor, rep
     assert rep["gpu_vs_ref"] <= rep["ref_err"] + floor, rep
     assert rep["agree_decided"] >= 0.99, rep
