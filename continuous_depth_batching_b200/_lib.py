@@ -207,7 +207,8 @@ class GemmWorkspace:
 
     def __init__(self, device: torch.device, max_tokens: int, max_n: int, num_sms: int) -> None:
         bn = 256
-        self.ws = torch.zeros(2 * num_sms * 128 * bn, dtype=torch.float32, device=device)
+        tile_rows = 256 if max_tokens > 256 else 128  # weight rows of one tile: 256 for prefill shapes
+        self.ws = torch.zeros(2 * num_sms * tile_rows * bn, dtype=torch.float32, device=device)
         tiles = -(-max_n // 128) * max(1, -(-max_tokens // bn))
         self.ctr = torch.zeros(tiles, dtype=torch.int32, device=device)
 

@@ -57,31 +57,44 @@ constexpr int THREADS = 7 * 32;
 constexpr int kWarpW = 0, kWarpX = 1, kWarpMma = 6;
 constexpr int kEpiThreads = 128;
 constexpr int kSmemBudget = 200 * 1024;
+constexpr int kStgPitch = (BM + 8) * 2;  // bytes per staged token row (16-byte aligned, bank-skewed)
+constexpr int kStgBytes = 32 * kStgPitch;
 
 constexpr int cmin(int a, int b) { return a < b ? a : b; }
 constexpr int cmax(int a, int b) { return a > b ? a : b; }
 constexpr int pow2_at_least(int v) { return v <= 32 ? 32 : v <= 64 ? 64 : v <= 128 ? 128 : 256; }
 
-template <int BN>
+// WM = weight tiles per CTA tile: 1 (128 weight rows; two TMEM accumulator buffers, so the
+// epilogue of one tile overlaps the main loop of the next) or 2 (256 weight rows x 256 tokens for
+// prefill: two accumulators sharing every activation tile, which cuts the shared-memory fill per
+// FLOP by a third; one buffer, the epilogue runs between tiles).
+template <int BN, int WM = 1>
 struct Cfg {
   static constexpr int X_BYTES = BN * BK * 2;
+  static constexpr int W_STAGE = WM * W_BYTES;
   // Rings: wide token tiles split the budget evenly (prefill is MMA-bound and needs both operands
   // deep); narrow ones keep a short activation ring (L2-resident X) and give the rest to weights.
-  static constexpr int SX = BN >= 128 ? kSmemBudget / (W_BYTES + X_BYTES) : cmax(3, cmin(8, 64 * 1024 / X_BYTES));
-  static constexpr int SW = BN >= 128 ? SX : cmin(12, (kSmemBudget - SX * X_BYTES) / W_BYTES);
-  static constexpr int ACC_STRIDE = pow2_at_least(BN);  // TMEM columns per accumulator buffer
-  static constexpr uint32_t TMEM_COLS = 2 * ACC_STRIDE;
+  static constexpr int SX = BN >= 128 ? kSmemBudget / (W_STAGE + X_BYTES) : cmax(3, cmin(8, 64 * 1024 / X_BYTES));
+  static constexpr int SW = BN >= 128 ? SX : cmin(12, (kSmemBudget - SX * X_BYTES) / W_STAGE);
+  static constexpr int ACC_STRIDE = pow2_at_least(BN);  // TMEM columns of one 128-row accumulator
+  static constexpr int NBUF = WM == 1 ? 2 : 1;          // accumulator buffers
+  static constexpr int ACC_SPAN = WM * ACC_STRIDE;      // TMEM columns of one buffer
+  static constexpr uint32_t TMEM_COLS = NBUF * ACC_SPAN;
+  static constexpr int TM = WM * BM;  // weight rows per CTA tile
   static constexpr int CHUNKS = (BN + 31) / 32;
-  static constexpr int OFF_X = SW * W_BYTES;
+  static constexpr int OFF_X = SW * W_STAGE;
   static constexpr int OFF_BAR = OFF_X + SX * X_BYTES;
-  static constexpr int NBAR = 2 * SW + 2 * SX + 5;
+  static constexpr int NBAR = 2 * SW + 2 * SX + 7;  // rings, 2 accumulator x 2, drain, 2 fixup
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int OFF_KEYS = (OFF_MISC + 64 + 7) / 8 * 8;  // argmax: [4 warps][32] keys
-  static constexpr int SMEM = OFF_KEYS + 4 * 32 * 8 + 1024;     // + alignment slack
+  static constexpr int OFF_KEYS = (OFF_MISC + 64 + 7) / 8 * 8;  // argmax: [4 warps][32] keys, then [BN] best
+  static constexpr int OFF_STG = (OFF_KEYS + (4 * 32 + BN) * 8 + 15) / 16 * 16;  // 2 staging tiles
+  static constexpr int SMEM = OFF_STG + 2 * kStgBytes + 1024;                      // + alignment slack
   // kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both K-major, M=128, N=BN.
   static constexpr uint32_t IDESC =
       (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+  static_assert(WM == 1 || BN == 256, "two weight tiles per CTA tile only for 256-token tiles");
+  static_assert(TMEM_COLS <= 512, "TMEM");
   static_assert(SX >= 2 && SW >= 2, "rings");
   static_assert(SMEM <= 227 * 1024, "shared memory");
   static_assert(X_BYTES % 1024 == 0, "swizzled X stages stay 1024-byte aligned");
@@ -93,10 +106,11 @@ struct Params {
   int M, N, K;
   int tiles_w, tiles_tok, kb;  // weight tiles, token tiles, k blocks per tile
   long long iters;             // tiles * kb
-  float* ws;                   // split partials: [2 * G][BM * BN] fp32
+  float* ws;                   // split partials: [2 * G][WM * BM * BN] fp32
   int32_t* ctr;                // per-tile arrival counters (zero between calls)
   int pair_store;              // EPI 0: c 4-byte aligned, ldc and N even (EPI 1: act 4-byte aligned, ldc even)
   int vec_store;               // split mode EPI 0: c 8-byte aligned, ldc % 4 == 0
+  int vec16;                   // stream-K EPI 0/1: c 16-byte aligned, ldc % 8 == 0
   int32_t* status;
   // EPI 2 (LM head + argmax)
   unsigned long long* keys;
@@ -205,48 +219,79 @@ __device__ __forceinline__ int piece_slot(long long iters, int G, int g, long lo
   return range_start(iters, G, g) >= tile_begin ? 2 * g : 2 * g + 1;
 }
 
-// Store one 32-token chunk of a finished tile: row n of the tile (this thread's TMEM lane), tokens
-// m0 .. m0 + 31 (in-tile columns col0 .. col0 + 31, valid below BN).
+// Bulk copy global -> shared (async proxy), completing on an mbarrier's transaction count.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ int ld_acquire(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Emit one 32-token chunk of a finished tile. v[j] = accumulator of weight row n0 + row (this
+// thread's TMEM lane) and token m0 + j (in-tile column col0 + j, valid below BN).
+//   EPI 0: bf16 values go through a [32 token][128 row] staging tile in shared memory and leave as
+//          16-byte stores, 256 contiguous bytes per token row.
+//   EPI 1: weight rows (2i, 2i+1) = (gate_i, up_i) sit on lanes (2l, 2l+1); the even lane stages
+//          act[token][i] (64 columns per 128 rows), stored the same way.
+//   EPI 2: no logits: the best (logit, index) key of every token over the 128 rows is folded into
+//          the CTA's per-token best (s_best), flushed to the global keys once per token tile.
+// One named barrier per chunk; the staging tile alternates between two buffers, so a buffer is
+// rewritten only after every thread has passed the next chunk's barrier.
+
 template <int BN, int EPI>
-__device__ __forceinline__ void store_chunk(const Params& p, const float (&v)[32], int n, int m0, int col0, int lane,
-                                            unsigned long long* s_keys, int q) {
-  if constexpr (EPI == 0) {
-    if (p.pair_store) {
+__device__ __forceinline__ void emit_chunk(const Params& p, const float (&v)[32], int n0, int row, int m0, int col0,
+                                           int lane, int q, int et, uint8_t* stg, unsigned long long* s_keys,
+                                           unsigned long long* s_best) {
+  if constexpr (EPI == 0 || EPI == 1) {
+    __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stg);
+    constexpr int kRowElems = kStgPitch / 2;
+    if constexpr (EPI == 0) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) st[j * kRowElems + row] = f_to_bf16(v[j]);
+    } else {
       const bool even = (lane & 1) == 0;
 #pragma unroll
-      for (int j = 0; j < 32; j += 2) {
-        const float a = v[j], b = v[j + 1];
-        const float pa = __shfl_xor_sync(0xffffffffu, a, 1);
-        const float pb = __shfl_xor_sync(0xffffffffu, b, 1);
-        const int jj = even ? j : j + 1;
-        const int tok = m0 + jj;
-        const int col = even ? n : n - 1;
-        if (col0 + jj < BN && tok < p.M && col < p.N)
-          *reinterpret_cast<uint32_t*>(p.c + (int64_t)tok * p.ldc + col) = even ? pack_bf16x2(a, pa) : pack_bf16x2(pb, b);
-      }
-    } else {
-#pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const int tok = m0 + j;
-        if (col0 + j < BN && tok < p.M && n < p.N) p.c[(int64_t)tok * p.ldc + n] = f_to_bf16(v[j]);
+        const float other = __shfl_xor_sync(0xffffffffu, v[j], 1);
+        if (even) {
+          const float g = round_bf16(v[j]), u = round_bf16(other);
+          const float s = round_bf16(g / (1.f + expf(-g)));
+          st[j * kRowElems + row / 2] = f_to_bf16(s * u);
+        }
       }
     }
-  } else if constexpr (EPI == 1) {
-    // rows (2i, 2i+1) = (gate_i, up_i) sit on lanes (2l, 2l+1); the even lane stores act[tok][i]
-    const bool even = (lane & 1) == 0;
+    epi_bar();
+    // output columns of this chunk: [c0, c0 + cols) of a row-major [M, ncols] matrix
+    constexpr int cols = EPI == 0 ? BM : BM / 2;
+    constexpr int vecs = cols / 8;  // 16-byte vectors per token row
+    const int c0 = EPI == 0 ? n0 : n0 / 2;
+    const int ncols = EPI == 0 ? p.N : p.N / 2;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float other = __shfl_xor_sync(0xffffffffu, v[j], 1);
-      const int tok = m0 + j;
-      if (even && col0 + j < BN && tok < p.M && n < p.N) {
-        const float g = round_bf16(v[j]), u = round_bf16(other);
-        const float s = round_bf16(g / (1.f + expf(-g)));
-        p.c[(int64_t)tok * p.ldc + n / 2] = f_to_bf16(s * u);
+    for (int k = 0; k < 32 * vecs / kEpiThreads; ++k) {
+      const int idx = et + k * kEpiThreads;
+      const int tok = idx / vecs, vc = idx % vecs;
+      const int m = m0 + tok, n = c0 + vc * 8;
+      if (col0 + tok >= BN || m >= p.M || n >= ncols) continue;
+      const uint4 val = *reinterpret_cast<const uint4*>(stg + tok * kStgPitch + vc * 16);
+      __nv_bfloat16* dst = p.c + (int64_t)m * p.ldc + n;
+      if (p.vec16 && n + 8 <= ncols) {
+        *reinterpret_cast<uint4*>(dst) = val;
+      } else {
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&val);
+        for (int i = 0; i < 8 && n + i < ncols; ++i) dst[i] = e[i];
       }
     }
   } else {
     // Transpose-reduce: after 5 butterfly stages lane l holds the best key of chunk token l over
     // the warp's 32 rows; the 4 epilogue warps then meet in shared memory.
+    (void)stg;
+    (void)et;
+    const int n = n0 + row;
     unsigned long long k[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -266,20 +311,33 @@ __device__ __forceinline__ void store_chunk(const Params& p, const float (&v)[32
     }
     s_keys[q * 32 + lane] = k[0];
     epi_bar();
-    if (q == 0) {
-      unsigned long long best = s_keys[lane];
+    if (q == 0 && col0 + lane < BN) {
+      unsigned long long best = s_best[col0 + lane];
 #pragma unroll
-      for (int w = 1; w < 4; ++w) best = s_keys[w * 32 + lane] > best ? s_keys[w * 32 + lane] : best;
-      if (best != 0ull && col0 + lane < BN && m0 + lane < p.M) atomicMax(p.keys + m0 + lane, best);
+      for (int w = 0; w < 4; ++w) best = s_keys[w * 32 + lane] > best ? s_keys[w * 32 + lane] : best;
+      s_best[col0 + lane] = best;
     }
     epi_bar();
   }
 }
 
-template <int BN, int EPI>
+// EPI 2: fold the CTA's per-token best keys of token tile starting at mbase into the global keys
+// (one atomicMax per token and CTA) and clear them. Called by all epilogue threads.
+template <int BN>
+__device__ __forceinline__ void flush_keys(const Params& p, unsigned long long* s_best, int mbase, int et) {
+  epi_bar();
+  for (int j = et; j < BN; j += kEpiThreads) {
+    const unsigned long long b = s_best[j];
+    if (b != 0ull && mbase + j < p.M) atomicMax(p.keys + mbase + j, b);
+    s_best[j] = 0ull;
+  }
+  epi_bar();
+}
+
+template <int BN, int EPI, int WM>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, Params p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, WM>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* wring = smem;
@@ -291,10 +349,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* afull = xempty + C::SX;
   uint64_t* aempty = afull + 2;
   uint64_t* mdrain = aempty + 2;  // the MMA issuer's last commit: every MMA done before TMEM is freed
+  uint64_t* fbar = mdrain + 1;    // [2] owner fixup: bulk copies of the other pieces
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
   volatile int* s_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 16);
   unsigned long long* s_keys = reinterpret_cast<unsigned long long*>(smem + C::OFF_KEYS);
+  unsigned long long* s_best = s_keys + 4 * 32;  // EPI 2: the CTA's best key per token of a token tile
+  uint8_t* stg = smem + C::OFF_STG;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -313,11 +374,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&xfull[s], 1);
       mbar_init(&xempty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < C::NBUF; ++b) {
       mbar_init(&afull[b], 1);
       mbar_init(&aempty[b], 4);  // one arrival per epilogue warp
     }
     mbar_init(mdrain, 1);
+    mbar_init(&fbar[0], 1);
+    mbar_init(&fbar[1], 1);
     *s_abort = 0;
     fence_barrier_init();
   }
@@ -341,13 +404,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int wt = t % p.tiles_w;
         const int s = (int)(i % C::SW);
         if (!wait_or_abort(&wempty[s], (uint32_t)(((i / C::SW) & 1) ^ 1), p.status, s_abort)) break;
-        mbar_arrive_expect_tx(&wfull[s], W_BYTES);
-        tma_load_2d(wring + s * W_BYTES, &map_w, &wfull[s], k * BK, wt * BM);
+        mbar_arrive_expect_tx(&wfull[s], C::W_STAGE);
+#pragma unroll
+        for (int w = 0; w < WM; ++w)
+          tma_load_2d(wring + s * C::W_STAGE + w * W_BYTES, &map_w, &wfull[s], k * BK, wt * C::TM + w * BM);
       }
       // no copy may still be in flight when the CTA exits (bounded waits that ignore an abort)
       for (long long j = (i > C::SW ? i - C::SW : 0); j < i; ++j)
         mbar_wait(&wfull[j % C::SW], (uint32_t)((j / C::SW) & 1), p.status);
     }
+    __syncwarp();  // the warp reaches the final block barrier converged
   } else if (warp == kWarpX) {
     // ------------------------------------------------------------ activation producer
     if (lane == 0) {
@@ -365,6 +431,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (long long j = (i > C::SX ? i - C::SX : 0); j < i; ++j)
         mbar_wait(&xfull[j % C::SX], (uint32_t)((j / C::SX) & 1), p.status);
     }
+    __syncwarp();
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -374,10 +441,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (long long it = it0; it < it1 && ok; ++seg) {
         const long long t = it / kb;
         const long long seg_end = (t + 1) * kb < it1 ? (t + 1) * kb : it1;
-        const int buf = seg & 1;
-        if (!wait_or_abort(&aempty[buf], (uint32_t)(((seg >> 1) & 1) ^ 1), p.status, s_abort)) break;
+        const int buf = seg % C::NBUF;
+        if (!wait_or_abort(&aempty[buf], (uint32_t)(((seg / C::NBUF) & 1) ^ 1), p.status, s_abort)) break;
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(buf * C::ACC_STRIDE);
+        const uint32_t d = tmem + (uint32_t)(buf * C::ACC_SPAN);
         for (bool first = true; it < seg_end; ++it, ++i, first = false) {
           const int ws = (int)(i % C::SW), xs = (int)(i % C::SX);
           if (!wait_or_abort(&wfull[ws], (uint32_t)((i / C::SW) & 1), p.status, s_abort) ||
@@ -386,11 +453,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a = smem_u32(wring + ws * W_BYTES);
+          const uint32_t a = smem_u32(wring + ws * C::W_STAGE);
           const uint32_t b = smem_u32(xring + xs * C::X_BYTES);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            umma_bf16(d, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), C::IDESC, (!first || kk > 0) ? 1u : 0u);
+#pragma unroll
+            for (int w = 0; w < WM; ++w)
+              umma_bf16(d + (uint32_t)(w * C::ACC_STRIDE), sw128_desc(a + w * W_BYTES + kk * 32), sw128_desc(b + kk * 32),
+                        C::IDESC, (!first || kk > 0) ? 1u : 0u);
           umma_commit(&wempty[ws]);
           umma_commit(&xempty[xs]);
         }
@@ -407,95 +477,197 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int et = threadIdx.x - 64;
     const int row = q * 32 + lane;
     pdl_wait();  // outputs, workspace and counters may still be in use by the predecessor
-    int seg = 0;
+    if constexpr (EPI == 2) {
+      for (int j = et; j < BN; j += kEpiThreads) s_best[j] = 0ull;
+    }
+    int seg = 0, emitted = 0, best_tt = -1;
     for (long long it = it0; it < it1; ++seg) {
       const long long t = it / kb;
       const long long tile_begin = t * kb;
       const long long seg_end = (t + 1) * kb < it1 ? (t + 1) * kb : it1;
       const bool full = it == tile_begin && seg_end == tile_begin + kb;
       it = seg_end;
-      const int buf = seg & 1;
-      if (et == 0) *s_flag = wait_or_abort(&afull[buf], (uint32_t)((seg >> 1) & 1), p.status, s_abort) ? 1 : 0;
+      const int buf = seg % C::NBUF;
+      if (et == 0) *s_flag = wait_or_abort(&afull[buf], (uint32_t)((seg / C::NBUF) & 1), p.status, s_abort) ? 1 : 0;
       epi_bar();
       if (!*s_flag) break;
       epi_bar();  // everyone has read the flag before it is reused
       tc_fence_after();
       const int wt = (int)(t % p.tiles_w), tt = (int)(t / p.tiles_w);
-      const int n = wt * BM + row;
       const int mbase = tt * BN;
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * C::ACC_STRIDE);
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * C::ACC_SPAN);
+      if constexpr (EPI == 2) {
+        if (tt != best_tt) {
+          if (best_tt >= 0) flush_keys<BN>(p, s_best, best_tt * BN, et);
+          best_tt = tt;
+        }
+      }
       if (full) {
-        // Whole tile in this CTA: store chunk by chunk, then release the buffer (the MMA warp
-        // meanwhile fills the other one).
+        // Whole tile in this CTA: emit chunk by chunk, then release the buffer (the MMA warp
+        // meanwhile fills the other one, when there are two).
 #pragma unroll 1
-        for (int c = 0; c < C::CHUNKS; ++c) {
+        for (int hc = 0; hc < WM * C::CHUNKS; ++hc, ++emitted) {
+          const int w = hc / C::CHUNKS, c = hc % C::CHUNKS;
           float v[32];
-          tmem_ld32(taddr + c * 32, v);
-          store_chunk<BN, EPI>(p, v, n, mbase + c * 32, c * 32, lane, s_keys, q);
+          tmem_ld32(taddr + w * C::ACC_STRIDE + c * 32, v);
+          emit_chunk<BN, EPI>(p, v, wt * C::TM + w * BM, row, mbase + c * 32, c * 32, lane, q, et,
+                              stg + (emitted & 1) * kStgBytes, s_keys, s_best);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&aempty[buf]);
         continue;
       }
-      // Split tile: publish this piece, then the last piece to arrive combines.
-      float4* mine = reinterpret_cast<float4*>(p.ws + (size_t)piece_slot(p.iters, G, g, tile_begin) * (BM * BN));
+      // Split tile. Its owner is the CTA holding the tile's first k block: the tile is the last
+      // segment of the owner's range, while every other piece is the first segment of a later
+      // range, so the other pieces are (nearly) done when the owner gets here.
+      const int ga = cta_of(p.iters, G, tile_begin);
+      const int gb = cta_of(p.iters, G, tile_begin + kb - 1);
+      // piece layout in a workspace slot: float4 ((w * BN / 4) + chunk * 8 + j / 4) * BM + row
+      if (g != ga) {
+        float4* mine = reinterpret_cast<float4*>(p.ws + (size_t)piece_slot(p.iters, G, g, tile_begin) * (C::TM * BN));
+#pragma unroll 1
+        for (int hc = 0; hc < WM * C::CHUNKS; ++hc) {
+          const int w = hc / C::CHUNKS, c = hc % C::CHUNKS;
+          float v[32];
+          tmem_ld32(taddr + w * C::ACC_STRIDE + c * 32, v);
 #pragma unroll
-      for (int c = 0; c < C::CHUNKS; ++c) {
-        float v[32];
-        tmem_ld32(taddr + c * 32, v);
+          for (int j4 = 0; j4 < 8; ++j4)
+            if (c * 32 + j4 * 4 < BN)
+              mine[(w * (BN / 4) + c * 8 + j4) * BM + row] =
+                  make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&aempty[buf]);
+        __threadfence();
+        epi_bar();
+        if (et == 0) atomicAdd(p.ctr + t, 1);
+        continue;
+      }
+      // Owner: wait until the other gb - ga pieces are published, then add them in CTA order to
+      // this CTA's own accumulator (own + piece(ga+1) + ... + piece(gb): the same order in every
+      // run). The W and X rings are idle now (this is the range's last segment and every MMA has
+      // completed), so the pieces come into shared memory by bulk copies, double-buffered in
+      // batches of chunks.
+      const int others = gb - ga;
+      if (et == 0) {
+        bool ok = false;
+        for (uint32_t i = 0; i < (kSpinLimit >> 4); ++i) {
+          if (ld_acquire(p.ctr + t) >= others) {
+            ok = true;
+            break;
+          }
+          if (*s_abort) break;
+          __nanosleep(64);
+        }
+        if (ok) {
+          p.ctr[t] = 0;  // every piece has arrived: ready for the next call
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+        } else {
+          set_error(p.status, CDB_ERR_DEVICE_TIMEOUT);
+          *s_abort = 1;
+        }
+        *s_flag = ok ? 1 : 0;
+      }
+      epi_bar();
+      if (!*s_flag) break;
+      epi_bar();
+      constexpr int kChunkBytes = BM * 32 * 4;   // one 32-column chunk of a 128-row piece
+      constexpr int kHalf = C::OFF_BAR / 2;      // half of the ring bytes
+      constexpr int kTotalChunks = WM * C::CHUNKS;
+      const int batch = kHalf / (others * kChunkBytes);
+      const float* piece0 = p.ws + (size_t)piece_slot(p.iters, G, ga + 1, tile_begin) * (C::TM * BN);
+      const size_t piece_stride = 2 * (size_t)(C::TM * BN);  // slot 2g of consecutive CTAs
+      auto chunk_floats = [](int ch) { return ((ch / C::CHUNKS) * (BN / 4) + (ch % C::CHUNKS) * 8) * BM * 4; };
+      auto chunk_bytes = [](int ch) { return BM * 16 * min(8, BN / 4 - (ch % C::CHUNKS) * 8); };
+      if (batch >= 1) {
+        auto issue = [&](int b0, int half) {
+          uint32_t bytes = 0;
+          for (int ch = b0; ch < b0 + batch && ch < kTotalChunks; ++ch) bytes += (uint32_t)(others * chunk_bytes(ch));
+          mbar_arrive_expect_tx(&fbar[half], bytes);
+          for (int ch = b0; ch < b0 + batch && ch < kTotalChunks; ++ch)
+            for (int pi = 0; pi < others; ++pi)
+              bulk_load(smem + half * kHalf + ((ch - b0) * others + pi) * kChunkBytes,
+                        piece0 + pi * piece_stride + chunk_floats(ch), (uint32_t)chunk_bytes(ch), &fbar[half]);
+        };
+        const int nbatch = (kTotalChunks + batch - 1) / batch;
+        int issued = 0;  // batches issued (tracked by et == 0)
+        if (et == 0) {
+          issue(0, 0);
+          issued = 1;
+          if (nbatch > 1) {
+            issue(batch, 1);
+            issued = 2;
+          }
+        }
+        int bi = 0;
+        for (int b0 = 0; b0 < kTotalChunks; b0 += batch, ++bi) {
+          const int half = bi & 1;
+          if (et == 0) *s_flag = wait_or_abort(&fbar[half], (uint32_t)((bi >> 1) & 1), p.status, s_abort) ? 1 : 0;
+          epi_bar();
+          if (!*s_flag) {
+            // no bulk copy may still be in flight when the CTA exits (bounded waits)
+            if (et == 0)
+              for (int bj = bi; bj < issued; ++bj) mbar_wait(&fbar[bj & 1], (uint32_t)((bj >> 1) & 1), p.status);
+            break;
+          }
+#pragma unroll 1
+          for (int ch = b0; ch < b0 + batch && ch < kTotalChunks; ++ch, ++emitted) {
+            const int w = ch / C::CHUNKS, c = ch % C::CHUNKS;
+            float v[32];
+            tmem_ld32(taddr + w * C::ACC_STRIDE + c * 32, v);
+            for (int pi = 0; pi < others; ++pi) {
+              const float4* src = reinterpret_cast<const float4*>(smem + half * kHalf + ((ch - b0) * others + pi) * kChunkBytes);
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4)
-          if (c * 32 + j4 * 4 < BN) mine[(c * 8 + j4) * BM + row] = make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]);
+              for (int j4 = 0; j4 < 8; ++j4)
+                if (c * 32 + j4 * 4 < BN) {
+                  const float4 x = src[j4 * BM + row];
+                  v[4 * j4] += x.x;
+                  v[4 * j4 + 1] += x.y;
+                  v[4 * j4 + 2] += x.z;
+                  v[4 * j4 + 3] += x.w;
+                }
+            }
+            emit_chunk<BN, EPI>(p, v, wt * C::TM + w * BM, row, mbase + c * 32, c * 32, lane, q, et,
+                                stg + (emitted & 1) * kStgBytes, s_keys, s_best);
+          }
+          epi_bar();  // every thread is done with this half before it is refilled
+          if (et == 0 && bi + 2 < nbatch) {
+            issue(b0 + 2 * batch, half);
+            ++issued;
+          }
+        }
+      } else {
+        // too many pieces for the ring: read them straight from the workspace
+        __threadfence();
+#pragma unroll 1
+        for (int ch = 0; ch < kTotalChunks; ++ch, ++emitted) {
+          const int w = ch / C::CHUNKS, c = ch % C::CHUNKS;
+          float v[32];
+          tmem_ld32(taddr + w * C::ACC_STRIDE + c * 32, v);
+          for (int pi = 0; pi < others; ++pi) {
+            const float4* src = reinterpret_cast<const float4*>(piece0 + pi * piece_stride + chunk_floats(ch));
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4)
+              if (c * 32 + j4 * 4 < BN) {
+                const float4 x = ld_cg_f4(src + j4 * BM + row);
+                v[4 * j4] += x.x;
+                v[4 * j4 + 1] += x.y;
+                v[4 * j4 + 2] += x.z;
+                v[4 * j4 + 3] += x.w;
+              }
+          }
+          emit_chunk<BN, EPI>(p, v, wt * C::TM + w * BM, row, mbase + c * 32, c * 32, lane, q, et,
+                              stg + (emitted & 1) * kStgBytes, s_keys, s_best);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&aempty[buf]);
-      const int ga = cta_of(p.iters, G, tile_begin);
-      const int gb = cta_of(p.iters, G, tile_begin + kb - 1);
-      __threadfence();
-      epi_bar();
-      if (et == 0) {
-        const int old = atomicAdd(p.ctr + t, 1);
-        *s_flag = old == gb - ga;
-        if (old == gb - ga) p.ctr[t] = 0;  // every piece has arrived: ready for the next call
-      }
-      epi_bar();
-      const bool last = *s_flag;
-      epi_bar();
-      if (!last) continue;
-      __threadfence();
-#pragma unroll 1
-      for (int c = 0; c < C::CHUNKS; ++c) {
-        float4 acc[8];
-#pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) acc[j4] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int gg = ga; gg <= gb; ++gg) {
-          const float4* src = reinterpret_cast<const float4*>(p.ws + (size_t)piece_slot(p.iters, G, gg, tile_begin) * (BM * BN));
-          float4 part[8];
-#pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4)
-            part[j4] = (c * 32 + j4 * 4 < BN) ? ld_cg_f4(src + (c * 8 + j4) * BM + row) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
-            acc[j4].x += part[j4].x;
-            acc[j4].y += part[j4].y;
-            acc[j4].z += part[j4].z;
-            acc[j4].w += part[j4].w;
-          }
-        }
-        float v[32];
-#pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          v[4 * j4] = acc[j4].x;
-          v[4 * j4 + 1] = acc[j4].y;
-          v[4 * j4 + 2] = acc[j4].z;
-          v[4 * j4 + 3] = acc[j4].w;
-        }
-        store_chunk<BN, EPI>(p, v, n, mbase + c * 32, c * 32, lane, s_keys, q);
-      }
     }
     if constexpr (EPI == 2) {
+      if (best_tt >= 0) flush_keys<BN>(p, s_best, best_tt * BN, et);
       // Every CTA counts itself done after its last key update; the last one writes the ids.
       __threadfence();
       epi_bar();
@@ -584,16 +756,17 @@ static int matrix_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t c
   return CDB_OK;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int WM>
 static int launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, int ctas, cudaStream_t st) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, WM>;
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(gemm_kernel<BN, EPI, WM>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+        cudaSuccess)
       return CDB_ERR_CUDA;
     attr_set = true;
   }
-  prefer_max_shared(reinterpret_cast<const void*>(gemm_kernel<BN, EPI>));
+  prefer_max_shared(reinterpret_cast<const void*>(gemm_kernel<BN, EPI, WM>));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas);
   cfg.blockDim = dim3(THREADS);
@@ -604,7 +777,7 @@ static int launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, EPI>, mw, mx, p) == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
+  return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, EPI, WM>, mw, mx, p) == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
 }
 
 // Token-tile width for M token rows: M rounded up to a multiple of 16 (the UMMA N step for
@@ -612,14 +785,17 @@ static int launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p,
 static int tile_n_for(int M) { return M >= 256 ? 256 : ((M + 15) / 16) * 16; }
 
 struct Shape {
-  int bn, tiles_w, tiles_tok, kb, ctas;
+  int bn, wm, tiles_w, tiles_tok, kb, ctas;
   long long iters;
 };
 
+// Problems with more than one 256-token tile (prefill) take 256 x 256 tiles (two weight tiles
+// per CTA tile); decode-sized ones 128 weight rows per tile.
 static Shape shape_for(int M, int N, int K, int max_ctas, int num_sms) {
   Shape s;
   s.bn = tile_n_for(M);
-  s.tiles_w = (N + BM - 1) / BM;
+  s.wm = M > 256 ? 2 : 1;
+  s.tiles_w = (N + s.wm * BM - 1) / (s.wm * BM);
   s.tiles_tok = (M + s.bn - 1) / s.bn;
   s.kb = (K + BK - 1) / BK;
   s.iters = (long long)s.tiles_w * s.tiles_tok * s.kb;
@@ -649,10 +825,13 @@ static int dispatch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& 
       c.num_kb = p.kb;
       c.vec_store = p.vec_store;
       c.status = p.status;
-      return cl::launch_cluster<BN, EPI>(mw, mx, c, s.tiles_w, s.tiles_tok, num_sms, st);
+      return cl::launch_cluster<BN, EPI>(mw, mx, c, (p.N + BM - 1) / BM, s.tiles_tok, num_sms, st);
     }
   }
-  return launch<BN, EPI>(mw, mx, p, s.ctas, st);
+  if constexpr (BN == 256) {
+    if (s.wm == 2) return launch<BN, EPI, 2>(mw, mx, p, s.ctas, st);
+  }
+  return launch<BN, EPI, 1>(mw, mx, p, s.ctas, st);
 }
 
 // Shared host path of the three epilogues: c = epilogue(x[M,K] * w[N,K]^T).
@@ -665,7 +844,7 @@ static int run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, 
   if ((reinterpret_cast<uintptr_t>(workspace) & 15)) return CDB_ERR_INVALID_ARGUMENT;
   const Shape s = shape_for(M, N, K, max_ctas, num_sms);
   if ((long long)s.tiles_w * s.tiles_tok > num_counters || counters == nullptr) return CDB_ERR_INVALID_ARGUMENT;
-  if ((int64_t)2 * s.ctas * BM * s.bn > workspace_elems || workspace == nullptr) return CDB_ERR_INVALID_ARGUMENT;
+  if ((int64_t)2 * s.ctas * s.wm * BM * s.bn > workspace_elems || workspace == nullptr) return CDB_ERR_INVALID_ARGUMENT;
   CUtensorMap mw, mx;
   int rc = matrix_map(&mw, w, N, K, ldw, BM);
   if (rc != CDB_OK) return rc;
@@ -686,10 +865,12 @@ static int run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, 
   p.ctr = counters;
   p.pair_store = ((reinterpret_cast<uintptr_t>(c) & 3) == 0 && ldc % 2 == 0 && N % 2 == 0) ? 1 : 0;
   p.vec_store = ((reinterpret_cast<uintptr_t>(c) & 7) == 0 && ldc % 4 == 0) ? 1 : 0;
+  p.vec16 = ((reinterpret_cast<uintptr_t>(c) & 15) == 0 && ldc % 8 == 0) ? 1 : 0;
   p.status = status;
   const int sms = num_sms > 0 ? num_sms : 148;
   // split mode for problems with fewer tiles than SMs; the SwiGLU epilogue there pairs 4 rows
-  const bool split = EPI != 2 && max_ctas <= 0 && (long long)s.tiles_w * s.tiles_tok < sms && (EPI != 1 || N % 4 == 0);
+  const long long tiles128 = (long long)((N + BM - 1) / BM) * s.tiles_tok;
+  const bool split = EPI != 2 && max_ctas <= 0 && tiles128 < sms && (EPI != 1 || N % 4 == 0);
   if (epi2 != nullptr) {
     p.keys = epi2->keys;
     p.done = epi2->done;
@@ -769,7 +950,7 @@ extern "C" int cdb_lm_head_argmax(const void* x, int64_t ldx, const void* w, int
 extern "C" int64_t cdb_gemm_workspace_elems(int M, int N, int K, int num_sms) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const cdb::gemm::Shape s = cdb::gemm::shape_for(M, N, K, 0, num_sms);
-  return (int64_t)2 * s.ctas * cdb::gemm::BM * s.bn;
+  return (int64_t)2 * s.ctas * s.wm * cdb::gemm::BM * s.bn;
 }
 
 extern "C" int cdb_gemm_counter_elems(int M, int N, int K) {

@@ -125,6 +125,7 @@ __global__ void __launch_bounds__(THREADS_CL, 1)
       for (int j = max(0, issued - STAGES); j < issued; ++j)
         mbar_wait(&full[j % STAGES], (uint32_t)((j / STAGES) & 1), p.status);
     }
+    __syncwarp();  // the warp reaches the block and cluster barriers converged
   } else if (warp == 1) {
     if (lane == 0) {
       int stage = 0;

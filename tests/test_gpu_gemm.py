@@ -57,7 +57,8 @@ def _check(c, x, w):
         (1, 6144, 2048), (7, 2048, 2048), (33, 11264, 2048), (64, 2048, 5632), (100, 6144, 2048),
         (256, 6144, 2048), (256, 2048, 2048), (256, 11264, 2048), (256, 2048, 5632), (96, 49152, 2048),
         (300, 768, 256), (1024, 1408, 256), (2048, 6144, 2048), (16, 256, 704), (130, 1000, 520),
-        (5, 1001, 512), (40, 130, 4096), (24, 2048, 5632),
+        (5, 1001, 512), (40, 130, 4096), (24, 2048, 5632), (700, 1000, 520), (513, 11264, 2048),
+        (4096, 2048, 5632),
     ],
 )
 def test_gemm_matches_fp32_reference(gemm, m, n, k):
@@ -139,7 +140,8 @@ def test_gateup_silu_gemm(gemm, m, inter, k):
     assert not bad.any(), f"{int(bad.sum())} out of bound; max err {(act.float() - ref).abs().max().item():.3e}"
 
 
-@pytest.mark.parametrize("m,vocab,k", [(1, 49152, 2048), (7, 1000, 512), (80, 49152, 2048), (130, 65536, 480), (300, 4096, 256)])
+@pytest.mark.parametrize("m,vocab,k", [(1, 49152, 2048), (7, 1000, 512), (80, 49152, 2048), (130, 65536, 480), (300, 4096, 256),
+                                          (600, 49152, 2048)])
 def test_lm_head_argmax_matches_logits_argmax(gemm, m, vocab, k):
     """cdb_lm_head_argmax == torch.argmax (first maximum) of the plain GEMM's bf16 logits, exactly
     (same tiles, same stream-K pieces, same accumulation), with the output-row and token-table
