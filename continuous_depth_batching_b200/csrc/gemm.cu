@@ -236,7 +236,7 @@ __device__ __forceinline__ int ld_acquire(const int32_t* p) {
 // thread's TMEM lane) and token m0 + j (in-tile column col0 + j, valid below BN).
 //   EPI 0: bf16 values go through a [32 token][128 row] staging tile in shared memory and leave as
 //          16-byte stores, 256 contiguous bytes per token row.
-//   EPI 1: weight rows (2i, 2i+1) = (gate_i, up_i) sit on lanes (2l, 2l+1); the even lane stages
+//   EPI 1: weight rows (2i, 2i+1) = (gate_i, up_i) sit on lanes (2l, 2l+1); the pair stages
 //          act[token][i] (64 columns per 128 rows), stored the same way.
 //   EPI 2: no logits: the best (logit, index) key of every token over the 128 rows is folded into
 //          the CTA's per-token best (s_best), flushed to the global keys once per token tile.
@@ -254,15 +254,15 @@ __device__ __forceinline__ void emit_chunk(const Params& p, const float (&v)[32]
 #pragma unroll
       for (int j = 0; j < 32; ++j) st[j * kRowElems + row] = f_to_bf16(v[j]);
     } else {
-      const bool even = (lane & 1) == 0;
+      // lanes 2l and 2l+1 split the chunk's tokens: the even lane takes the even tokens and the
+      // odd lane the odd ones, one shuffle per token pair
+      const int odd = lane & 1;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float other = __shfl_xor_sync(0xffffffffu, v[j], 1);
-        if (even) {
-          const float g = round_bf16(v[j]), u = round_bf16(other);
-          const float s = round_bf16(g / (1.f + expf(-g)));
-          st[j * kRowElems + row / 2] = f_to_bf16(s * u);
-        }
+      for (int j = 0; j < 32; j += 2) {
+        const float x = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
+        const float g = round_bf16(odd ? x : v[j]), u = round_bf16(odd ? v[j + 1] : x);
+        const float s = round_bf16(g / (1.f + expf(-g)));
+        st[(j + odd) * kRowElems + row / 2] = f_to_bf16(s * u);
       }
     }
     epi_bar();
@@ -790,11 +790,13 @@ struct Shape {
 };
 
 // Problems with more than one 256-token tile (prefill) take 256 x 256 tiles (two weight tiles
-// per CTA tile); decode-sized ones 128 weight rows per tile.
-static Shape shape_for(int M, int N, int K, int max_ctas, int num_sms) {
+// per CTA tile) for the plain and argmax epilogues; decode-sized ones, and the SwiGLU epilogue
+// (whose arithmetic must overlap the next tile's main loop, which needs two accumulator
+// buffers), 128 weight rows per tile.
+static Shape shape_for(int M, int N, int K, int max_ctas, int num_sms, int epi = 0) {
   Shape s;
   s.bn = tile_n_for(M);
-  s.wm = M > 256 ? 2 : 1;
+  s.wm = M > 256 && epi != 1 ? 2 : 1;
   s.tiles_w = (N + s.wm * BM - 1) / (s.wm * BM);
   s.tiles_tok = (M + s.bn - 1) / s.bn;
   s.kb = (K + BK - 1) / BK;
@@ -842,7 +844,7 @@ static int run(const void* x, int64_t ldx, const void* w, int64_t ldw, void* c, 
   if (K % 8 != 0 || ldx % 8 != 0 || ldw % 8 != 0 || ldx < K || ldw < K) return CDB_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return CDB_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(workspace) & 15)) return CDB_ERR_INVALID_ARGUMENT;
-  const Shape s = shape_for(M, N, K, max_ctas, num_sms);
+  const Shape s = shape_for(M, N, K, max_ctas, num_sms, EPI);
   if ((long long)s.tiles_w * s.tiles_tok > num_counters || counters == nullptr) return CDB_ERR_INVALID_ARGUMENT;
   if ((int64_t)2 * s.ctas * s.wm * BM * s.bn > workspace_elems || workspace == nullptr) return CDB_ERR_INVALID_ARGUMENT;
   CUtensorMap mw, mx;
@@ -955,6 +957,6 @@ extern "C" int64_t cdb_gemm_workspace_elems(int M, int N, int K, int num_sms) {
 
 extern "C" int cdb_gemm_counter_elems(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  const cdb::gemm::Shape s = cdb::gemm::shape_for(M, N, K, 0, 148);
+  const cdb::gemm::Shape s = cdb::gemm::shape_for(M, N, K, 0, 148, 1);  // 128-row tiles: the most tiles
   return s.tiles_w * s.tiles_tok;
 }

@@ -4,6 +4,7 @@
     python -m continuous_depth_batching_b200.kernel_bench gemm --m 80 --n 2048 --k 2048
     python -m continuous_depth_batching_b200.kernel_bench lm_head --m 32 --vocab 49152 --k 2048
     python -m continuous_depth_batching_b200.kernel_bench gemm_chain --m 80 --n 6144 --k 2048
+    python -m continuous_depth_batching_b200.kernel_bench prefill_rows --rows 8192
 
 ``attention`` builds a one-cache-layer paged KV pool with the Ouro-1.4B head shape (16 heads x
 128), gives each row a context drawn uniformly from [context/2, 3*context/2), and times the
@@ -12,7 +13,9 @@ default), the rope/append kernel followed by the attention kernel (``--append 1`
 single launch the engine uses (``--append 2``, split-half RoPE). Algorithmic bytes per launch are
 ``attention_bytes`` below. ``gemm`` times ``cdb_gemm_bf16`` against ``torch.mm`` (cuBLAS) on one
 shape, flushing L2 between launches so weights stream from HBM as they do in a decode step.
-Each prints one JSON line.
+``prefill_rows`` times, each alone, the row-parallel kernels of one prefill layer at ``--rows``
+tokens (Ouro-1.4B widths): the SwiGLU GEMM (against cuBLAS + ``cdb_silu_mul``), the RoPE + KV
+append and the residual + sandwich norm. Each prints one JSON line.
 """
 
 from __future__ import annotations
@@ -255,6 +258,83 @@ def run_lm_head(args) -> dict:
     return res
 
 
+def run_prefill_rows(args) -> dict:
+    """Prefill-width row kernels, each timed alone with an L2 flush before every launch."""
+
+    dev = torch.device("cuda")
+    torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+    t, hidden, inter, heads, d = args.rows, 2048, 5632, 16, 128
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    x = torch.randn(t, hidden, device=dev, generator=g).to(torch.bfloat16)
+    w_gu = (0.02 * torch.randn(2 * inter, hidden, device=dev, generator=g)).to(torch.bfloat16)
+    act = torch.empty(t, inter, device=dev, dtype=torch.bfloat16)
+    gu = torch.empty(t, 2 * inter, device=dev, dtype=torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = _lib.GemmWorkspace(dev, t, 2 * inter, 148)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    # RoPE + append: every row its own position in a fresh request, blocks laid out in order
+    hs = heads * d
+    qkv = torch.randn(t, 3 * hs, device=dev, generator=g).to(torch.bfloat16)
+    nblk = (t + BLOCK - 1) // BLOCK
+    pool = torch.zeros(2, nblk * BLOCK, heads, d, device=dev, dtype=torch.bfloat16)
+    table = torch.arange(nblk, device=dev, dtype=torch.int32).view(1, nblk)
+    slot = torch.zeros(t, device=dev, dtype=torch.int32)
+    pos = torch.arange(t, device=dev, dtype=torch.int32)
+    inv = 1.0 / (10000.0 ** (torch.arange(0, d, 2, dtype=torch.float32, device=dev) / d))
+    emb = torch.arange(t + 1, dtype=torch.float32, device=dev)[:, None] * inv[None, :]
+    emb = torch.cat((emb, emb), dim=-1)
+    cos, sin = emb.cos().to(torch.bfloat16).contiguous(), emb.sin().to(torch.bfloat16).contiguous()
+    # residual + sandwich norm
+    res_x = torch.randn(t, hidden, device=dev, generator=g).to(torch.bfloat16)
+    a = torch.randn(t, hidden, device=dev, generator=g).to(torch.bfloat16)
+    wn = torch.ones(hidden, device=dev, dtype=torch.bfloat16)
+    y = torch.empty(t, hidden, device=dev, dtype=torch.bfloat16)
+
+    def gateup():
+        _lib.call(
+            "cdb_mlp_gateup_silu_gemm", _lib.ptr(x), hidden, _lib.ptr(w_gu), hidden, _lib.ptr(act), inter, t, inter,
+            hidden, 0, *ws.args(), 148, _lib.ptr(status), sp,
+        )
+
+    def gateup_cublas():
+        torch.mm(x, w_gu.t(), out=gu)
+        _lib.call("cdb_silu_mul", _lib.ptr(gu), 2 * inter, _lib.ptr(act), inter, t, inter, sp)
+
+    def rope():
+        _lib.call(
+            "cdb_rope_append_kv", _lib.ptr(qkv), 3 * hs, hs, 2 * hs, _lib.ptr(pool), 1, nblk * BLOCK, 0,
+            _lib.ptr(table), nblk, _lib.ptr(slot), _lib.ptr(pos), 1, _lib.ptr(cos), _lib.ptr(sin), None, t, heads,
+            d, BLOCK, sp,
+        )
+
+    def norm():
+        _lib.call(
+            "cdb_add_rmsnorm", _lib.ptr(res_x), hidden, _lib.ptr(a), hidden, _lib.ptr(wn), _lib.ptr(wn), _lib.ptr(y),
+            hidden, None, None, None, None, t, hidden, 1e-6, sp,
+        )
+
+    res = {"rows": t}
+    for name, fn, byts, flops in (
+        ("gateup_silu_tcgen05", gateup, 2 * (2 * inter * hidden + t * hidden + t * inter), 2 * t * 2 * inter * hidden),
+        ("gateup_cublas_plus_silu_mul", gateup_cublas, 2 * (2 * inter * hidden + t * hidden + t * inter),
+         2 * t * 2 * inter * hidden),
+        ("rope_append", rope, 2 * 6 * t * hs, 0),
+        ("add_rmsnorm", norm, 2 * 4 * t * hidden, 0),
+    ):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        ms = _events_ms(fn, args.iters, stream, flush)
+        res[name] = {"us": round(ms * 1e3, 2), "gbs": round(byts / (ms * 1e-3) / 1e9, 1)}
+        if flops:
+            res[name]["tflops"] = round(flops / (ms * 1e-3) / 1e12, 1)
+    if int(status.item()) != 0:
+        raise RuntimeError(_lib.load().cdb_status_string(int(status.item())).decode())
+    return res
+
+
 def main(argv=None) -> None:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     sub = p.add_subparsers(dest="kernel", required=True)
@@ -281,12 +361,15 @@ def main(argv=None) -> None:
     gc.add_argument("--n", type=int, default=2048)
     gc.add_argument("--k", type=int, default=2048)
     gc.add_argument("--layers", type=int, default=24)
-    for s in (a, g, lm, gc):
+    pr = sub.add_parser("prefill_rows")
+    pr.add_argument("--rows", type=int, default=8192)
+    for s in (a, g, lm, gc, pr):
         s.add_argument("--warmup", type=int, default=3)
         s.add_argument("--iters", type=int, default=20)
         s.add_argument("--seed", type=int, default=0)
     args = p.parse_args(argv)
-    res = {"attention": run_attention, "gemm": run_gemm, "lm_head": run_lm_head, "gemm_chain": run_gemm_chain}[
+    res = {"attention": run_attention, "gemm": run_gemm, "lm_head": run_lm_head, "gemm_chain": run_gemm_chain,
+           "prefill_rows": run_prefill_rows}[
         args.kernel
     ](args)
     print(json.dumps(res))
