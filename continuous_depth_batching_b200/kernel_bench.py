@@ -191,7 +191,7 @@ def run_gemm_chain(args) -> dict:
     ws = _lib.GemmWorkspace(dev, m, n, 148)
     stream = torch.cuda.Stream()
     res = {"m": m, "n": n, "k": k, "layers": layers, "us_per_gemm": {}}
-    for ctas in ["cublas", 0, 120, 96, 74]:
+    for ctas in ["cublas", *[int(c) for c in args.ctas_list.split(",")]]:
         def body(ctas=ctas):
             for layer in range(layers):
                 if ctas == "cublas":
@@ -361,6 +361,8 @@ def main(argv=None) -> None:
     gc.add_argument("--n", type=int, default=2048)
     gc.add_argument("--k", type=int, default=2048)
     gc.add_argument("--layers", type=int, default=24)
+    gc.add_argument("--ctas-list", default="0,148,120,96,74",
+                    help="comma-separated CTA counts (0 = the library's choice; > 0 forces stream-K)")
     pr = sub.add_parser("prefill_rows")
     pr.add_argument("--rows", type=int, default=8192)
     for s in (a, g, lm, gc, pr):
