@@ -65,6 +65,10 @@ _SIGNATURES: dict[str, list] = {
     ],
     "cdb_gemm_workspace_elems": [c_int, c_int, c_int, c_int],
     "cdb_gemm_counter_elems": [c_int, c_int, c_int],
+    "cdb_gemm_bf16_partials": [
+        c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+    ],
+    "cdb_gemm_partial_splits": [c_int, c_int, c_int, c_int],
     "cdb_lm_head_argmax": [
         c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_int,  # x, ldx, w, ldw, M, vocab, K
         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,  # out_ids, out_rows, token_rows, table, keys, done
@@ -76,6 +80,10 @@ _SIGNATURES: dict[str, list] = {
     ],
     "cdb_add_rmsnorm": [
         c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
+        c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p,
+    ],
+    "cdb_add_rmsnorm_parts": [
+        c_void_p, c_int64, c_void_p, c_int, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
         c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p,
     ],
     "cdb_silu_mul": [c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_void_p],
@@ -184,6 +192,7 @@ def stream_ptr(stream: torch.cuda.Stream | None = None) -> int:
 
 _NO_LAUNCH = {
     "cdb_version", "cdb_status_string", "cdb_attn_scratch_bytes", "cdb_gemm_workspace_elems", "cdb_gemm_counter_elems",
+    "cdb_gemm_partial_splits",
     "cdb_schedule_queues_init",
     "cdb_kv_blocks_host_copy",
 }

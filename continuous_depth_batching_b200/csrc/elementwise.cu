@@ -131,9 +131,39 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_kernel(const __nv_bfloat1
   store_row(y + (int64_t)r * ys, hidden, v);
 }
 
+// Row of a = bf16(sum over the split-K partial planes, in plane order) from fp32 partials
+// ap[z * pstride + d] (the GEMM's own reduction order, so a equals what the GEMM would store).
+template <int NC>
+__device__ __forceinline__ void load_parts(const float* ap, int nparts, int64_t pstride, int hidden, RowRegs<NC>& r) {
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int d = (c * kRowThreads + threadIdx.x) * 8;
+    float s[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s[k] = 0.f;
+    if (d < hidden) {
+      const float4* p0 = reinterpret_cast<const float4*>(ap + d);
+      float4 lo = p0[0], hi = p0[1];
+      s[0] = lo.x, s[1] = lo.y, s[2] = lo.z, s[3] = lo.w, s[4] = hi.x, s[5] = hi.y, s[6] = hi.z, s[7] = hi.w;
+#pragma unroll 4
+      for (int z = 1; z < nparts; ++z) {
+        const float4* pz = reinterpret_cast<const float4*>(ap + z * pstride + d);
+        lo = pz[0];
+        hi = pz[1];
+        s[0] += lo.x, s[1] += lo.y, s[2] += lo.z, s[3] += lo.w, s[4] += hi.x, s[5] += hi.y, s[6] += hi.z, s[7] += hi.w;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) r.v[c][k] = round_bf16(s[k]);
+  }
+}
+
+// a is either a bf16 row (a, as) or, when ap != nullptr, the sum of nparts fp32 split-K partial
+// planes ap + z * pstride (row r at ap + r * hidden) that a split GEMM left unreduced.
 template <int NC>
 __global__ void __launch_bounds__(kRowThreads) add_rmsnorm_kernel(__nv_bfloat16* x, int64_t xs, const __nv_bfloat16* a,
-                                                                  int64_t as, const __nv_bfloat16* wa,
+                                                                  int64_t as, const float* ap, int nparts,
+                                                                  int64_t pstride, const __nv_bfloat16* wa,
                                                                   const __nv_bfloat16* wn, __nv_bfloat16* y, int64_t ys,
                                                                   const int32_t* y_rows, const __nv_bfloat16* gw,
                                                                   const __nv_bfloat16* gb, __nv_bfloat16* gout,
@@ -149,10 +179,14 @@ __global__ void __launch_bounds__(kRowThreads) add_rmsnorm_kernel(__nv_bfloat16*
   const int dst = y_rows ? y_rows[r] : r;
   if (dst < 0) return;
   RowRaw<NC> ar, xr;
-  load_raw(a + (int64_t)r * as, hidden, ar);
-  load_raw(x + (int64_t)r * xs, hidden, xr);
   RowRegs<NC> av, xv;
-  unpack_row(ar, av);
+  load_raw(x + (int64_t)r * xs, hidden, xr);
+  if (ap != nullptr) {
+    load_parts(ap + (int64_t)r * hidden, nparts, pstride, hidden, av);
+  } else {
+    load_raw(a + (int64_t)r * as, hidden, ar);
+    unpack_row(ar, av);
+  }
   rms_inplace(av, war, hidden, eps, red);
   unpack_row(xr, xv);
 #pragma unroll
@@ -508,10 +542,32 @@ extern "C" int cdb_add_rmsnorm(void* x, int64_t x_stride, const void* a, int64_t
   with_row_chunks(hidden, [&](auto nc) {
     launch_pdl(add_rmsnorm_kernel<decltype(nc)::value>, dim3(num_rows), dim3(kRowThreads), 0,
                static_cast<cudaStream_t>(stream), static_cast<__nv_bfloat16*>(x), x_stride,
-               static_cast<const __nv_bfloat16*>(a), a_stride, static_cast<const __nv_bfloat16*>(w_a),
+               static_cast<const __nv_bfloat16*>(a), a_stride, static_cast<const float*>(nullptr), 0, (int64_t)0,
+               static_cast<const __nv_bfloat16*>(w_a),
                static_cast<const __nv_bfloat16*>(w_next), static_cast<__nv_bfloat16*>(y), y_stride, y_rows,
                static_cast<const __nv_bfloat16*>(gate_w), static_cast<const __nv_bfloat16*>(gate_b),
                static_cast<__nv_bfloat16*>(gate_out), hidden, eps);
+  });
+  return check_launch();
+}
+
+extern "C" int cdb_add_rmsnorm_parts(void* x, int64_t x_stride, const float* a_parts, int num_parts,
+                                     int64_t part_stride, const void* w_a, const void* w_next, void* y,
+                                     int64_t y_stride, const int32_t* y_rows, const void* gate_w, const void* gate_b,
+                                     void* gate_out, int num_rows, int hidden, float eps, void* stream) {
+  if (hidden % 8 != 0 || hidden > kRowThreads * kMaxChunks * 8 || num_rows < 0) return CDB_ERR_INVALID_ARGUMENT;
+  if (gate_w != nullptr && (gate_b == nullptr || gate_out == nullptr)) return CDB_ERR_INVALID_ARGUMENT;
+  if (a_parts == nullptr || num_parts < 1 || (reinterpret_cast<uintptr_t>(a_parts) & 15) || part_stride % 4 != 0 ||
+      part_stride < (int64_t)num_rows * hidden)
+    return CDB_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return CDB_OK;
+  with_row_chunks(hidden, [&](auto nc) {
+    launch_pdl(add_rmsnorm_kernel<decltype(nc)::value>, dim3(num_rows), dim3(kRowThreads), 0,
+               static_cast<cudaStream_t>(stream), static_cast<__nv_bfloat16*>(x), x_stride,
+               static_cast<const __nv_bfloat16*>(nullptr), (int64_t)0, a_parts, num_parts, part_stride,
+               static_cast<const __nv_bfloat16*>(w_a), static_cast<const __nv_bfloat16*>(w_next),
+               static_cast<__nv_bfloat16*>(y), y_stride, y_rows, static_cast<const __nv_bfloat16*>(gate_w),
+               static_cast<const __nv_bfloat16*>(gate_b), static_cast<__nv_bfloat16*>(gate_out), hidden, eps);
   });
   return check_launch();
 }

@@ -949,6 +949,75 @@ extern "C" int cdb_lm_head_argmax(const void* x, int64_t ldx, const void* w, int
                            num_counters, num_sms, status, static_cast<cudaStream_t>(stream), &e);
 }
 
+namespace cdb {
+namespace gemm {
+static int run_partials(const void* x, int64_t ldx, const void* w, int64_t ldw, float* parts, int64_t part_stride,
+                        int M, int N, int K, int splits, int32_t* status, cudaStream_t st) {
+  if (K % 8 != 0 || ldx % 8 != 0 || ldw % 8 != 0 || ldx < K || ldw < K) return CDB_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) return CDB_ERR_INVALID_ARGUMENT;
+  if (parts == nullptr || (reinterpret_cast<uintptr_t>(parts) & 3) || part_stride < (int64_t)M * N) return CDB_ERR_INVALID_ARGUMENT;
+  const int bn = tile_n_for(M);
+  const int num_kb = (K + BK - 1) / BK;
+  if (splits < 1 || splits > cl::kMaxPartSplits || splits > num_kb) return CDB_ERR_INVALID_ARGUMENT;
+  CUtensorMap mw, mx;
+  int rc = matrix_map(&mw, w, N, K, ldw, BM);
+  if (rc != CDB_OK) return rc;
+  rc = matrix_map(&mx, x, M, K, ldx, bn);
+  if (rc != CDB_OK) return rc;
+  cl::CParams c;
+  std::memset(&c, 0, sizeof(c));
+  c.M = M;
+  c.N = N;
+  c.K = K;
+  c.splits = splits;
+  c.num_kb = num_kb;
+  c.status = status;
+  c.parts = parts;
+  c.part_stride = part_stride;
+  const int tiles_n = (N + BM - 1) / BM, tiles_m = (M + bn - 1) / bn;
+  switch (bn) {
+#define CDB_PART_CASE(B) \
+  case B:                \
+    return cl::launch_partials<B>(mw, mx, c, tiles_n, tiles_m, st);
+    CDB_PART_CASE(16)
+    CDB_PART_CASE(32)
+    CDB_PART_CASE(48)
+    CDB_PART_CASE(64)
+    CDB_PART_CASE(80)
+    CDB_PART_CASE(96)
+    CDB_PART_CASE(112)
+    CDB_PART_CASE(128)
+    CDB_PART_CASE(144)
+    CDB_PART_CASE(160)
+    CDB_PART_CASE(176)
+    CDB_PART_CASE(192)
+    CDB_PART_CASE(208)
+    CDB_PART_CASE(224)
+    CDB_PART_CASE(240)
+    CDB_PART_CASE(256)
+#undef CDB_PART_CASE
+    default:
+      return CDB_ERR_UNSUPPORTED;
+  }
+}
+}  // namespace gemm
+}  // namespace cdb
+
+extern "C" int cdb_gemm_partial_splits(int M, int N, int K, int num_sms) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const int bn = cdb::gemm::tile_n_for(M);
+  const int tiles = ((N + cdb::gemm::BM - 1) / cdb::gemm::BM) * ((M + bn - 1) / bn);
+  return cdb::gemm::cl::partial_splits(bn, tiles, (K + cdb::gemm::BK - 1) / cdb::gemm::BK, num_sms > 0 ? num_sms : 148);
+}
+
+extern "C" int cdb_gemm_bf16_partials(const void* x, int64_t ldx, const void* w, int64_t ldw, float* parts,
+                                      int64_t part_stride, int M, int N, int K, int splits, int32_t* status,
+                                      void* stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return M == 0 ? CDB_OK : CDB_ERR_INVALID_ARGUMENT;
+  return cdb::gemm::run_partials(x, ldx, w, ldw, parts, part_stride, M, N, K, splits, status,
+                                 static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int64_t cdb_gemm_workspace_elems(int M, int N, int K, int num_sms) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const cdb::gemm::Shape s = cdb::gemm::shape_for(M, N, K, 0, num_sms);

@@ -51,6 +51,8 @@ struct CParams {
   int splits, kb_per_split, num_kb;  // splits == cluster size along z
   int vec_store;                     // c 8-byte aligned and ldc % 4 == 0
   int32_t* status;
+  float* parts;                      // EPI 3: fp32 partial planes, split z at parts + z * part_stride ([M][N])
+  int64_t part_stride;
 };
 
 template <int BN, int STAGES, int EPI>
@@ -150,6 +152,36 @@ __global__ void __launch_bounds__(THREADS_CL, 1)
   }
   // the producer's loads have all landed and the MMA warp has issued its final commit
   __syncthreads();
+  if constexpr (EPI == 3) {
+    // Unreduced: this split's fp32 partial goes straight to its plane (a warp stores 128
+    // consecutive bytes of one token row per instruction); the consumer sums the planes.
+    if (warp >= 2) {
+      const int q = warp & 3;
+      const bool ok = mbar_wait(accum, 0, p.status);
+      tc_fence_after();
+      const int n = wtile * BM + q * 32 + lane;
+      float* plane = p.parts + (int64_t)split * p.part_stride;
+      if (ok) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          float v[32];
+          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int m = mtile * BN + c0 + j;
+            if (c0 + j < BN && m < p.M && n < p.N) plane[(int64_t)m * p.N + n] = v[j];
+          }
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+    return;
+  }
   if (warp >= 2) {
     // TMEM -> this CTA's fp32 partial tile red[token][weight row] in the stage ring, free once the
     // accumulator barrier fires (every MMA, the ring's only reader, has completed)
@@ -327,6 +359,51 @@ static int launch_cluster(const CUtensorMap& mw, const CUtensorMap& mx, CParams 
       cluster_config<BN, STAGES>(nullptr, dim3(tiles_n, tiles_m, s), s, st, attr);
   return cudaLaunchKernelEx(&cfg, gemm_cluster_kernel<BN, STAGES, EPI>, mw, mx, p) == cudaSuccess ? CDB_OK
                                                                                                  : CDB_ERR_CUDA;
+}
+
+// Split count of the unreduced mode: fill the resident CTA slots, at least two k-blocks per
+// split, at most kPartSplitsPreferred planes (every plane is written by the GEMM and read back by
+// the consumer; in a graph of 24 o_proj + norm pairs at 80 rows, 4-6 planes took 9.1-9.3 us per
+// pair against 10.4 us at 16 and 11.1 us for the reduced GEMM + norm). Callers may pass up to
+// kMaxPartSplits.
+constexpr int kMaxPartSplits = 16;
+constexpr int kPartSplitsPreferred = 6;
+static int partial_splits(int bn, int tiles, int num_kb, int num_sms) {
+  const int slots = num_sms * (bn <= 128 ? 2 : 1);
+  int want = tiles >= slots ? 1 : slots / tiles;
+  want = min(want, max(1, num_kb / 2));
+  want = max(1, min(want, kPartSplitsPreferred));
+  const int kb_per = (num_kb + want - 1) / want;
+  return (num_kb + kb_per - 1) / kb_per;  // no empty split
+}
+
+template <int BN>
+static int launch_partials(const CUtensorMap& mw, const CUtensorMap& mx, CParams p, int tiles_n, int tiles_m,
+                           cudaStream_t st) {
+  constexpr int STAGES = stages_for(BN);
+  using C = CCfg<BN, STAGES>;
+  static int attr_state = 0;
+  if (attr_state == 0) {
+    attr_state = cudaFuncSetAttribute(gemm_cluster_kernel<BN, STAGES, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      C::SMEM) == cudaSuccess ? 1 : -1;
+    prefer_max_shared(reinterpret_cast<const void*>(gemm_cluster_kernel<BN, STAGES, 3>));
+  }
+  if (attr_state != 1) return CDB_ERR_CUDA;
+  const int s = p.splits;
+  p.kb_per_split = (p.num_kb + s - 1) / s;
+  if ((p.num_kb + p.kb_per_split - 1) / p.kb_per_split != s) return CDB_ERR_INVALID_ARGUMENT;  // an empty split
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles_n, tiles_m, s);
+  cfg.blockDim = dim3(THREADS_CL);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_cluster_kernel<BN, STAGES, 3>, mw, mx, p) == cudaSuccess ? CDB_OK
+                                                                                               : CDB_ERR_CUDA;
 }
 
 }  // namespace cl

@@ -219,6 +219,72 @@ def run_gemm_chain(args) -> dict:
     return res
 
 
+def run_proj_norm_chain(args) -> dict:
+    """Per-layer time of a projection followed by the residual sandwich norm, inside a CUDA graph
+    of ``--layers`` such pairs on different weights: cdb_gemm_bf16 (split-K reduced in the
+    GEMM) + cdb_add_rmsnorm, against cdb_gemm_bf16_partials (planes left unreduced) +
+    cdb_add_rmsnorm_parts at each split count of ``--splits-list`` (0 = the library's choice)."""
+
+    dev = torch.device("cuda")
+    m, n, k, layers = args.m, args.n, args.k, args.layers
+    w = (0.02 * torch.randn(layers, n, k, device=dev)).to(torch.bfloat16)
+    a = torch.randn(m, k, device=dev).to(torch.bfloat16)
+    proj = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    x = torch.randn(m, n, device=dev).to(torch.bfloat16)
+    y = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    wn = torch.ones(n, device=dev, dtype=torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = _lib.GemmWorkspace(dev, m, n, 148)
+    parts = torch.zeros(16 * m * n + 16, dtype=torch.float32, device=dev)
+    stride = m * n + (-(m * n)) % 4
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+    auto = _lib.load().cdb_gemm_partial_splits(m, n, k, 148)
+    res = {"m": m, "n": n, "k": k, "layers": layers, "library_splits": auto, "us_per_layer": {}}
+    kb = -(-k // 64)
+    for mode in ["reduced", *[int(v) for v in args.splits_list.split(",")]]:
+        splits = auto if mode == 0 else mode
+        if mode != "reduced" and -(-kb // -(-kb // splits)) != splits:
+            continue  # a split would be empty
+
+        def body(mode=mode, splits=splits):
+            for layer in range(layers):
+                if mode == "reduced":
+                    _lib.call(
+                        "cdb_gemm_bf16", _lib.ptr(a), k, _lib.ptr(w[layer]), k, _lib.ptr(proj), n, m, n, k, 0,
+                        *ws.args(), 148, _lib.ptr(status), sp,
+                    )
+                    _lib.call(
+                        "cdb_add_rmsnorm", _lib.ptr(x), n, _lib.ptr(proj), n, _lib.ptr(wn), _lib.ptr(wn), _lib.ptr(y), n,
+                        None, None, None, None, m, n, 1e-6, sp,
+                    )
+                else:
+                    _lib.call(
+                        "cdb_gemm_bf16_partials", _lib.ptr(a), k, _lib.ptr(w[layer]), k, _lib.ptr(parts), stride, m, n,
+                        k, splits, _lib.ptr(status), sp,
+                    )
+                    _lib.call(
+                        "cdb_add_rmsnorm_parts", _lib.ptr(x), n, _lib.ptr(parts), splits, stride, _lib.ptr(wn),
+                        _lib.ptr(wn), _lib.ptr(y), n, None, None, None, None, m, n, 1e-6, sp,
+                    )
+
+        with torch.cuda.stream(stream):
+            body()
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            body()
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                graph.replay()
+            ms = _events_ms(graph.replay, args.iters, stream)
+        res["us_per_layer"][str(mode if mode == "reduced" else splits)] = round(ms * 1e3 / layers, 2)
+        del graph
+    if int(status.item()) != 0:
+        raise RuntimeError(_lib.load().cdb_status_string(int(status.item())).decode())
+    return res
+
+
 def run_lm_head(args) -> dict:
     """cdb_lm_head_argmax against torch.mm (cuBLAS) + cdb_argmax on the same rows."""
 
@@ -363,15 +429,21 @@ def main(argv=None) -> None:
     gc.add_argument("--layers", type=int, default=24)
     gc.add_argument("--ctas-list", default="0,148,120,96,74",
                     help="comma-separated CTA counts (0 = the library's choice; > 0 forces stream-K)")
+    pn = sub.add_parser("proj_norm_chain")
+    pn.add_argument("--m", type=int, default=80)
+    pn.add_argument("--n", type=int, default=2048)
+    pn.add_argument("--k", type=int, default=2048)
+    pn.add_argument("--layers", type=int, default=24)
+    pn.add_argument("--splits-list", default="0,4,6,8,12,16")
     pr = sub.add_parser("prefill_rows")
     pr.add_argument("--rows", type=int, default=8192)
-    for s in (a, g, lm, gc, pr):
+    for s in (a, g, lm, gc, pr, pn):
         s.add_argument("--warmup", type=int, default=3)
         s.add_argument("--iters", type=int, default=20)
         s.add_argument("--seed", type=int, default=0)
     args = p.parse_args(argv)
     res = {"attention": run_attention, "gemm": run_gemm, "lm_head": run_lm_head, "gemm_chain": run_gemm_chain,
-           "prefill_rows": run_prefill_rows}[
+           "prefill_rows": run_prefill_rows, "proj_norm_chain": run_proj_norm_chain}[
         args.kernel
     ](args)
     print(json.dumps(res))

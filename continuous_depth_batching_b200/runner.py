@@ -356,6 +356,23 @@ class OuroRunner:
             m, w.shape[0], k, 0, *self.gemm.args(), self.num_sms, _lib.ptr(self.status), self._sp(),
         )
 
+    def _mm_norm(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, x, w_a, w_next, y, y_rows,
+                 gate_w, gate_b, gate_out) -> None:
+        """out = a @ w^T, then the residual sandwich norm x += norm(out; w_a), y = norm(x; w_next)
+        (cdb_add_rmsnorm). The split-K GEMM reduces its partials itself: leaving them unreduced
+        for the norm to sum (cdb_gemm_bf16_partials + cdb_add_rmsnorm_parts) was 2 us faster per
+        pair in an isolated graph chain but 1% slower over the bench's decode step."""
+
+        m = a.shape[0]
+        H = self.shape.hidden_size
+        sp = self._sp()
+        self._mm(a, w, out)
+        _lib.call(
+            "cdb_add_rmsnorm", _lib.ptr(x), x.stride(0), _lib.ptr(out), out.stride(0), _lib.ptr(w_a),
+            _lib.ptr(w_next), _lib.ptr(y), y.stride(0), _lib.ptr(y_rows), _lib.ptr(gate_w), _lib.ptr(gate_b),
+            _lib.ptr(gate_out), m, H, self.shape.rms_norm_eps, sp,
+        )
+
     def _gate_up(self, a: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> None:
         """out = silu(a @ Wg^T) * (a @ Wu^T) for interleaved gate/up rows ``w`` (one GEMM)."""
 
@@ -423,7 +440,6 @@ class OuroRunner:
         """All shared layers over rows ``[0, n)`` of the work buffers; residual stream in ``xw``."""
 
         s, w = self.shape, self.w
-        H, I, eps = s.hidden_size, s.intermediate_size, s.rms_norm_eps
         L = s.num_hidden_layers
         sp = self._sp()
         for l in range(L):
@@ -439,11 +455,9 @@ class OuroRunner:
                     s.num_attention_heads, s.head_dim, self.block_size, sp,
                 )
                 self._prefill_attention(base_layer + l)
-            self._mm(self.attn[:n], w.w_o[l], self.o[:n])
-            _lib.call(
-                "cdb_add_rmsnorm", _lib.ptr(self.xw), self.xw.stride(0), _lib.ptr(self.o), self.o.stride(0),
-                _lib.ptr(w.norms["input_layernorm_2"][l]), _lib.ptr(w.norms["post_attention_layernorm"][l]),
-                _lib.ptr(self.h), self.h.stride(0), None, None, None, None, n, H, eps, sp,
+            self._mm_norm(
+                self.attn[:n], w.w_o[l], self.o[:n], self.xw, w.norms["input_layernorm_2"][l],
+                w.norms["post_attention_layernorm"][l], self.h, None, None, None, None,
             )
             self._gate_up(self.h[:n], w.w_gu[l], self.act[:n])
             # x += norm(m); then the next layer's input norm, or after the last layer the final norm
@@ -452,12 +466,9 @@ class OuroRunner:
             w_next = w.final_norm if last else w.norms["input_layernorm"][l + 1]
             y, y_rows = (final_dst, final_rows) if last else (self.h, None)
             g = last and gate
-            self._mm(self.act[:n], w.w_down[l], self.m[:n])
-            _lib.call(
-                "cdb_add_rmsnorm", _lib.ptr(self.xw), self.xw.stride(0), _lib.ptr(self.m), self.m.stride(0),
-                _lib.ptr(w.norms["post_attention_layernorm_2"][l]), _lib.ptr(w_next), _lib.ptr(y), y.stride(0),
-                _lib.ptr(y_rows), _lib.ptr(w.gate_w) if g else None, _lib.ptr(w.gate_b) if g else None,
-                _lib.ptr(self.gate_out) if g else None, n, H, eps, sp,
+            self._mm_norm(
+                self.act[:n], w.w_down[l], self.m[:n], self.xw, w.norms["post_attention_layernorm_2"][l], w_next,
+                y, y_rows, w.gate_w if g else None, w.gate_b if g else None, self.gate_out if g else None,
             )
 
     def _recurrent_body(self, meta: torch.Tensor, n: int, kv_slot: int, gate: bool) -> None:

@@ -207,6 +207,23 @@ int64_t cdb_gemm_workspace_elems(int M, int N, int K, int num_sms);
 /* int32 tile counters a GEMM of this shape needs (one per 128-row x token-tile output tile). */
 int cdb_gemm_counter_elems(int M, int N, int K);
 
+/* Split-K GEMM left unreduced, for a consumer that sums the planes while it reads them
+ * (cdb_add_rmsnorm_parts): parts[z * part_stride + m * N + n] = the fp32 sum over split z's k
+ * blocks of x[m, k] * w[n, k], for z < splits. Split z covers k blocks [z * ceil(kb / splits),
+ * ...) of the kb = ceil(K / 64) blocks, and a consumer summing the planes in z order gets exactly
+ * the value the reduced split mode of cdb_gemm_bf16 would store for the same split count.
+ * Serves decode-width projections (few 128-row tiles) without any cross-CTA reduction.
+ * splits in [1, 16], no empty split (use cdb_gemm_partial_splits); part_stride >= M * N;
+ * parts 4-byte aligned. Replaces the nn.Linear o_proj / down_proj (modeling_ouro.py) as the
+ * producer half of a projection + residual-norm pair. */
+int cdb_gemm_bf16_partials(const void* x, int64_t ldx, const void* w, int64_t ldw, float* parts, int64_t part_stride,
+                           int M, int N, int K, int splits, int32_t* status, void* stream);
+
+/* The split count cdb_gemm_bf16_partials should use for this shape on num_sms SMs (toward two
+ * CTAs per SM for token tiles up to 128, at least two k blocks per split, at most 6: more planes
+ * cost more in plane traffic than they gain in streaming CTAs). */
+int cdb_gemm_partial_splits(int M, int N, int K, int num_sms);
+
 /* ---------------------------------------------------------------------------------------
  * Row-wise fused elementwise kernels (bf16 activations, fp32 math, bf16 rounding at the
  * points PyTorch rounds). Optional index arrays (nullable) gather input rows / scatter output
@@ -229,6 +246,15 @@ int cdb_rmsnorm(const void* x, int64_t x_stride, const int32_t* x_rows, const vo
 int cdb_add_rmsnorm(void* x, int64_t x_stride, const void* a, int64_t a_stride, const void* w_a,
                     const void* w_next, void* y, int64_t y_stride, const int32_t* y_rows, const void* gate_w,
                     const void* gate_b, void* gate_out, int num_rows, int hidden, float eps, void* stream);
+
+/* cdb_add_rmsnorm with a[r] = bf16(sum over z < num_parts, in z order, of a_parts[z * part_stride +
+ * r * hidden + d]): the unreduced planes of cdb_gemm_bf16_partials (N = hidden), so the pair
+ * GEMM -> norm equals cdb_gemm_bf16 -> cdb_add_rmsnorm at the same split count. a_parts 16-byte
+ * aligned, part_stride a multiple of 4 and >= num_rows * hidden. */
+int cdb_add_rmsnorm_parts(void* x, int64_t x_stride, const float* a_parts, int num_parts, int64_t part_stride,
+                          const void* w_a, const void* w_next, void* y, int64_t y_stride, const int32_t* y_rows,
+                          const void* gate_w, const void* gate_b, void* gate_out, int num_rows, int hidden,
+                          float eps, void* stream);
 
 /* QKV projection with RoPE and the KV append: qkv[M, v_col + H*D] = x * w_qkv^T (cdb_gemm_bf16),
  * then q rotated in place, k rotated, and k/v written at each row's position (cdb_rope_append_kv;

@@ -277,3 +277,68 @@ def test_qkv_rope_append_gemm_matches_separate_calls(gemm, heads, d, rope_mode, 
     assert torch.equal(outs[0][0], outs[1][0])
     assert torch.equal(outs[0][1], outs[1][1])
     assert not torch.equal(outs[1][1], kv0)
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 2048, 2048), (37, 2048, 5632), (80, 2048, 2048), (80, 2048, 5632),
+                                   (200, 2048, 2048), (256, 512, 1408), (16, 1000, 520)])
+def test_unreduced_split_planes_and_norm(gemm, m, n, k):
+    """cdb_gemm_bf16_partials leaves one fp32 plane per K split: the planes sum (in split order) to
+    the fp32 reference within the GEMM bound, and cdb_add_rmsnorm_parts on them equals
+    cdb_add_rmsnorm on a = bf16(that sum) bit for bit (residual stream, normed output, gate)."""
+
+    torch.manual_seed(m * 3 + n + k)
+    a = torch.randn(m, k, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=DEV) * k**-0.5).to(torch.bfloat16)
+    splits = _lib.load().cdb_gemm_partial_splits(m, n, k, 148)
+    kb = -(-k // 64)
+    assert 1 <= splits <= 16 and splits <= kb
+    stride = m * n + 4  # planes need not be packed
+    stride += (-stride) % 4
+    parts = torch.full((splits * stride,), float("nan"), dtype=torch.float32, device=DEV)
+    for _ in range(2):  # the second call rewrites every plane element with the same values
+        _lib.call(
+            "cdb_gemm_bf16_partials", _lib.ptr(a), a.stride(0), _lib.ptr(w), w.stride(0), _lib.ptr(parts), stride,
+            m, n, k, splits, _lib.ptr(gemm.status), _sp(),
+        )
+        torch.cuda.synchronize()
+    assert int(gemm.status.item()) == 0
+    planes = [parts[z * stride: z * stride + m * n].view(m, n) for z in range(splits)]
+    total = planes[0].clone()
+    for z in range(1, splits):
+        total += planes[z]
+    assert not torch.isnan(total).any()
+    # each plane is the product over its own k blocks
+    per = -(-kb // splits) * 64
+    for z in (0, splits - 1):
+        ref_z = a[:, z * per: (z + 1) * per].float() @ w[:, z * per: (z + 1) * per].float().t()
+        assert (planes[z] - ref_z).abs().max().item() <= 1e-3 * (1 + ref_z.abs().max().item())
+    _check(total.to(torch.bfloat16), a, w)
+    if n % 8:
+        return
+    x0 = torch.randn(m, n, device=DEV).to(torch.bfloat16)
+    wa = (1 + 0.1 * torch.randn(n, device=DEV)).to(torch.bfloat16)
+    wn = (1 + 0.1 * torch.randn(n, device=DEV)).to(torch.bfloat16)
+    gw = (0.05 * torch.randn(n, device=DEV)).to(torch.bfloat16)
+    gb = torch.tensor([0.25], device=DEV).to(torch.bfloat16)
+    results = []
+    for from_parts in (False, True):
+        x = x0.clone()
+        y = torch.zeros(m, n, dtype=torch.bfloat16, device=DEV)
+        gout = torch.zeros(m, dtype=torch.bfloat16, device=DEV)
+        if from_parts:
+            _lib.call(
+                "cdb_add_rmsnorm_parts", _lib.ptr(x), x.stride(0), _lib.ptr(parts), splits, stride, _lib.ptr(wa),
+                _lib.ptr(wn), _lib.ptr(y), y.stride(0), None, _lib.ptr(gw), _lib.ptr(gb), _lib.ptr(gout), m, n,
+                1e-6, _sp(),
+            )
+        else:
+            proj = total.to(torch.bfloat16)
+            _lib.call(
+                "cdb_add_rmsnorm", _lib.ptr(x), x.stride(0), _lib.ptr(proj), proj.stride(0), _lib.ptr(wa),
+                _lib.ptr(wn), _lib.ptr(y), y.stride(0), None, _lib.ptr(gw), _lib.ptr(gb), _lib.ptr(gout), m, n,
+                1e-6, _sp(),
+            )
+        torch.cuda.synchronize()
+        results.append((x, y, gout))
+    for ref, got in zip(results[0], results[1], strict=True):
+        assert torch.equal(ref, got)
