@@ -26,10 +26,15 @@ constexpr int THREADS_CL = 192;
 constexpr int kMaxClusterSplits = 8;  // portable cluster size
 
 constexpr int ctas_per_sm_for(int bn) { return bn <= 128 ? 2 : 1; }
-constexpr int stages_for(int bn) {
+// Ring stages: ~110 KB so two CTAs share an SM (token tiles up to 128), ~220 KB otherwise. `wide`
+// is the one-CTA-per-SM ring (up to 12 stages in 200 KB) for problems whose tiles cannot fill two
+// CTAs per SM even at the largest cluster (o_proj and down_proj at decode widths: 16 tiles x 8
+// splits = 128 CTAs); there the deeper ring keeps a CTA's whole K slice in flight.
+constexpr int stages_for(int bn, bool wide = false) {
   const int stage = BM * BK * 2 + bn * BK * 2;
-  const int budget = (bn <= 128 ? 110 : 220) * 1024;
-  return budget / stage < 8 ? budget / stage : 8;
+  const int budget = (wide ? 200 : bn <= 128 ? 110 : 220) * 1024;
+  const int cap = wide ? 12 : 8;
+  return budget / stage < cap ? budget / stage : cap;
 }
 
 template <int BN, int STAGES>
@@ -42,6 +47,8 @@ struct CCfg {
   static constexpr uint32_t TMEM_COLS = (uint32_t)pow2_at_least(BN);
   static constexpr uint32_t IDESC = Cfg<BN>::IDESC;
   static_assert(BN * BM * 4 <= STAGES * STAGE_BYTES, "fp32 partial tile must fit in the stage ring");
+  static_assert(2 * STAGES * 8 + 3 * 8 + 4 <= BAR_BYTES, "barriers");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
 struct CParams {
@@ -330,10 +337,9 @@ static int schedulable_splits(int want, int clusters) {
   return best;
 }
 
-template <int BN, int EPI>
-static int launch_cluster(const CUtensorMap& mw, const CUtensorMap& mx, CParams p, int tiles_n, int tiles_m,
-                          int num_sms, cudaStream_t st) {
-  constexpr int STAGES = stages_for(BN);
+template <int BN, int STAGES, int EPI>
+static int launch_cluster_with(const CUtensorMap& mw, const CUtensorMap& mx, CParams p, int tiles_n, int tiles_m,
+                               int slots, cudaStream_t st) {
   using C = CCfg<BN, STAGES>;
   static int attr_state = 0;
   if (attr_state == 0) {
@@ -345,7 +351,6 @@ static int launch_cluster(const CUtensorMap& mw, const CUtensorMap& mx, CParams 
   // Fill the resident CTA slots with (weight tile, token tile, K split) CTAs, at least two
   // k-blocks per split.
   const int tiles = tiles_n * tiles_m;
-  const int slots = num_sms * ctas_per_sm_for(BN);
   int want = tiles >= slots ? 1 : slots / tiles;
   want = min(want, max(1, p.num_kb / 2));
   want = max(1, min(want, kMaxClusterSplits));
@@ -359,6 +364,20 @@ static int launch_cluster(const CUtensorMap& mw, const CUtensorMap& mx, CParams 
       cluster_config<BN, STAGES>(nullptr, dim3(tiles_n, tiles_m, s), s, st, attr);
   return cudaLaunchKernelEx(&cfg, gemm_cluster_kernel<BN, STAGES, EPI>, mw, mx, p) == cudaSuccess ? CDB_OK
                                                                                                  : CDB_ERR_CUDA;
+}
+
+// Two CTAs per SM with ~110 KB rings, or, when even the largest clusters leave SMs without a
+// second CTA (tiles x 8 <= SMs), one CTA per SM with the wide ring. In a 24-GEMM graph at 80
+// tokens the wide ring took o_proj 2048x2048 from 8.3 to 7.8 us and down 2048x5632 from 11.8 to
+// 10.9 us, and was slower for QKV (48 tiles) and gate/up (88 tiles), which fill two CTAs per SM.
+template <int BN, int EPI>
+static int launch_cluster(const CUtensorMap& mw, const CUtensorMap& mx, CParams p, int tiles_n, int tiles_m,
+                          int num_sms, cudaStream_t st) {
+  if constexpr (BN <= 128) {
+    if (tiles_n * tiles_m * kMaxClusterSplits <= num_sms)
+      return launch_cluster_with<BN, stages_for(BN, true), EPI>(mw, mx, p, tiles_n, tiles_m, num_sms, st);
+  }
+  return launch_cluster_with<BN, stages_for(BN), EPI>(mw, mx, p, tiles_n, tiles_m, num_sms * ctas_per_sm_for(BN), st);
 }
 
 // Split count of the unreduced mode: fill the resident CTA slots, at least two k-blocks per
