@@ -6,33 +6,42 @@
 // accumulator lives in tensor memory as [128 lanes = weight rows] x [BN columns = token rows].
 // Prefill-shaped problems tile the tokens by 256.
 //
-// Work split (stream-K). The launch has G = min(#SMs, iterations) CTAs, one per SM. The
-// iteration space - every (output tile, 64-wide k block) pair, tiles in token-major order - is
-// cut into G equal contiguous ranges, so every SM streams the same number of weight bytes
-// whatever the tile count (a decode projection has 16-88 weight tiles for 148 SMs; one SM alone
-// streams only ~40 GB/s from HBM, so all of them must). A CTA's range covers the tail of one tile,
-// whole tiles and the head of another; a tile covered by one CTA is stored directly, a tile split
-// over CTAs is combined deterministically: every piece writes its fp32 partial to the caller's
-// workspace and bumps the tile's counter; the piece that arrives last sums all pieces in k order
-// (so the result does not depend on arrival order), applies the epilogue and resets the counter.
-// No CTA ever waits on another.
+// Work split (stream-K). The launch has G = min(#SMs, iterations) CTAs, one per SM (two per SM
+// for token tiles narrower than 128, each with a smaller ring). The iteration space - every
+// (output tile, 64-wide k block) pair, tiles in token-major order - is cut into G equal contiguous
+// ranges, so every SM streams the same number of bytes whatever the tile count. A CTA's range
+// covers the tail of one tile, whole tiles and the head of another; a tile covered by one CTA is
+// stored directly. A tile split over CTAs belongs to the CTA holding its first k block (for that
+// CTA it is the range's last segment); every other piece is the first segment of a later range.
+// Those pieces write their fp32 partial to the caller's workspace and bump the tile's counter;
+// the owner waits for the counter (bounded), bulk-copies the pieces into its now idle rings and
+// adds them to its own accumulator in CTA order (so the result does not depend on timing), runs
+// the epilogue and resets the counter. Owners wait only on later CTAs' first segments, which wait
+// on nothing, so the waits cannot form a cycle; all G CTAs are co-resident by construction.
 //
-// Warp roles (224 threads, one CTA per SM):
+// Tiles: above 256 tokens the plain and argmax epilogues use 256 weight rows x 256 tokens (two
+// 128-row accumulators sharing every activation tile); otherwise 128 weight rows x BN tokens with
+// two TMEM buffers, so one tile's epilogue overlaps the next tile's main loop.
+//
+// Warp roles (224 threads):
 //   warp 0      weight producer: 2-D TMA tile loads W[128 x 64] (128-byte swizzle) into an SW-deep
 //               ring. Weights do not depend on the previous kernel, so this warp never waits for
 //               it: with programmatic dependent launch the weight stream starts while the
 //               predecessor is still finishing.
 //   warp 1      activation producer: waits for the predecessor (griddepcontrol.wait), then loads
 //               X[BN x 64] tiles into an SX-deep ring.
-//   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp its 32-lane quarter) and store,
-//               or write/combine split partials.
-//   warp 6      allocates TMEM (two accumulator buffers, so the epilogue of one tile overlaps
-//               the main loop of the next) and issues tcgen05.mma from one thread.
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp its 32-lane quarter) and emit it
+//               through a shared-memory staging tile as 16-byte stores, or publish / combine
+//               split pieces.
+//   warp 6      allocates TMEM and issues tcgen05.mma from one thread.
+// Every role branch ends converged (__syncwarp) before the final block barrier, which guards the
+// TMEM free.
 // Epilogues: 0 stores bf16(C); 1 (SwiGLU) reads weight rows as gate/up pairs and stores
-// bf16(bf16(silu(bf16(g))) * bf16(u)); 2 (LM head + greedy argmax) stores no logits and folds
-// each token's argmax into a 64-bit atomicMax key, the last CTA writing the token ids.
+// bf16(bf16(silu(bf16(g))) * bf16(u)); 2 (LM head + greedy argmax) stores no logits: each CTA
+// keeps its best 64-bit (logit, index) key per token in shared memory, folds it into the global
+// keys with one atomicMax per token and token tile, and the last CTA writes the token ids.
 // Every wait is bounded; a wait that runs out records CDB_ERR_DEVICE_TIMEOUT and the CTA winds
-// down (no CTA waits on another CTA, so nothing can hang on a peer).
+// down.
 //
 // Split mode (gemm_cluster.cuh). When a problem has fewer output tiles than SMs (every
 // decode-shaped projection), stream-K would cut each tile into many pieces and leave one CTA to
@@ -57,6 +66,7 @@ constexpr int THREADS = 7 * 32;
 constexpr int kWarpW = 0, kWarpX = 1, kWarpMma = 6;
 constexpr int kEpiThreads = 128;
 constexpr int kSmemBudget = 200 * 1024;
+constexpr int kNarrowRing = 88 * 1024;  // ring bytes of a narrow-token-tile CTA (two CTAs per SM)
 constexpr int kStgPitch = (BM + 8) * 2;  // bytes per staged token row (16-byte aligned, bank-skewed)
 constexpr int kStgBytes = 32 * kStgPitch;
 
@@ -73,9 +83,12 @@ struct Cfg {
   static constexpr int X_BYTES = BN * BK * 2;
   static constexpr int W_STAGE = WM * W_BYTES;
   // Rings: wide token tiles split the budget evenly (prefill is MMA-bound and needs both operands
-  // deep); narrow ones keep a short activation ring (L2-resident X) and give the rest to weights.
-  static constexpr int SX = BN >= 128 ? kSmemBudget / (W_STAGE + X_BYTES) : cmax(3, cmin(8, 64 * 1024 / X_BYTES));
-  static constexpr int SW = BN >= 128 ? SX : cmin(12, (kSmemBudget - SX * X_BYTES) / W_STAGE);
+  // deep). Narrow ones (decode widths: the LM head, wide SwiGLU projections) run two CTAs per SM,
+  // each with a 3-deep activation ring (X is L2-resident) and ~88 KB of weight ring: two CTAs
+  // streaming per SM pulled the Huginn-0125 LM head (65536 x 5280) at 5.1 TB/s against 4.4 TB/s
+  // for one CTA with a 12-deep ring.
+  static constexpr int SX = BN >= 128 ? kSmemBudget / (W_STAGE + X_BYTES) : 3;
+  static constexpr int SW = BN >= 128 ? SX : cmin(12, (kNarrowRing - SX * X_BYTES) / W_STAGE);
   static constexpr int ACC_STRIDE = pow2_at_least(BN);  // TMEM columns of one 128-row accumulator
   static constexpr int NBUF = WM == 1 ? 2 : 1;          // accumulator buffers
   static constexpr int ACC_SPAN = WM * ACC_STRIDE;      // TMEM columns of one buffer
@@ -97,6 +110,7 @@ struct Cfg {
   static_assert(TMEM_COLS <= 512, "TMEM");
   static_assert(SX >= 2 && SW >= 2, "rings");
   static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(BN >= 128 || 2 * (SMEM + 1024) <= 228 * 1024, "narrow token tiles: two CTAs per SM");
   static_assert(X_BYTES % 1024 == 0, "swizzled X stages stay 1024-byte aligned");
 };
 
@@ -335,7 +349,7 @@ __device__ __forceinline__ void flush_keys(const Params& p, unsigned long long* 
 }
 
 template <int BN, int EPI, int WM>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS, (BN < 128 ? 2 : 1))
     gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, Params p) {
   using C = Cfg<BN, WM>;
   extern __shared__ uint8_t smem_raw[];
@@ -801,7 +815,7 @@ static Shape shape_for(int M, int N, int K, int max_ctas, int num_sms, int epi =
   s.tiles_tok = (M + s.bn - 1) / s.bn;
   s.kb = (K + BK - 1) / BK;
   s.iters = (long long)s.tiles_w * s.tiles_tok * s.kb;
-  int g = num_sms > 0 ? num_sms : 148;
+  int g = (num_sms > 0 ? num_sms : 148) * (s.bn < 128 ? 2 : 1);  // narrow token tiles: two CTAs per SM
   if (max_ctas > 0 && max_ctas < g) g = max_ctas;
   s.ctas = (int)(s.iters < g ? s.iters : g);
   return s;
