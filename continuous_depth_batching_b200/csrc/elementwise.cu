@@ -302,7 +302,10 @@ __global__ void embed_kernel(const __nv_bfloat16* table, int hidden, int vocab, 
   const int dst = out_rows ? out_rows[r] : r;
   if (dst < 0) return;
   int id = ids ? ids[r] : -1;
-  if (id < 0 && id_src != nullptr) id = token_table[id_src[r]];
+  if (id < 0 && id_src != nullptr) {
+    const int slot = id_src[r];
+    id = slot >= 0 ? token_table[slot] : -1;  // a negative slot has no device token: reported below
+  }
   __nv_bfloat16* o = out + (int64_t)dst * os;
   if (id < 0 || id >= vocab) {
     if (threadIdx.x == 0) set_error(status, CDB_ERR_INDEX);

@@ -18,6 +18,11 @@ in the stages, following ``HuginnCDBAdapter`` (``continuous_depth_batching/adapt
 * prefill: ``HuginnForCausalLM.forward`` at full depth over a varlen batch of prompt chunks
   (prelude, ``total_recurrent_steps`` core steps from a zero state, coda).
 
+Decode prelude and coda launches replay CUDA graphs per padded batch size, as the recurrent
+launch does; padding rows carry position -1 (no attention work, no KV append) and bank / output
+rows -1 (nothing stored). A prelude padding row embeds token 0 (id 0, slot 0): an id of -1 would
+read the request's device token through slot -1.
+
 Every block (``HuginnBlock.forward``, ``modeling_huginn.py:333-336``) is
 ``QKV GEMM -> q/k bias + interleaved fp32 RoPE + KV append -> paged attention -> proj GEMM ->
 x = norm_2(o + x), h = norm_3(x) -> fc GEMM + SwiGLU -> mlp proj GEMM -> x = norm_4(m + x),
@@ -28,12 +33,13 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from . import _lib
 from .huginn import BLOCK_NORM_NAMES, STAGES, HuginnShape, huginn_rope_tables
 from .kv_cache import LoopedKvLayout
-from .runner import SCRATCH_ITEMS, OuroRunner
+from .runner import SCRATCH_ITEMS, OuroRunner, _Graph
 
 
 @dataclass
@@ -146,6 +152,7 @@ class HuginnRunner(OuroRunner):
         self.logits = torch.zeros(max_num_seqs, shape.vocab_size, **bf)
         self.lm_in = torch.zeros(max_num_seqs, E, **bf)
         self.rope_cos, self.rope_sin = huginn_rope_tables(shape, max_model_len + 1, device)
+        self.stage_graphs: dict[tuple[str, int], _Graph] = {}
 
     # ------------------------------------------------------------------ cache-layer layout
     def coda_cache_layer(self, layer: int) -> int:
@@ -253,26 +260,91 @@ class HuginnRunner(OuroRunner):
             )
 
     # ------------------------------------------------------------------ stages
+    def _prelude_body(self, meta: torch.Tensor, n: int) -> None:
+        """meta rows: token id (-1: the request's device token), request slot, bank slot, position."""
+
+        s = self.shape
+        _lib.call(
+            "cdb_embed", _lib.ptr(self.w.wte), s.n_embd, s.vocab_size, _lib.ptr(meta[0]), _lib.ptr(meta[1]),
+            _lib.ptr(self.token_table), _lib.ptr(self.xw), self.xw.stride(0), None, n, s.embed_scale,
+            _lib.ptr(self.status), self._sp(),
+        )
+        self._plan(meta[3], n, 1)
+        self._first_norm(n, "prelude")
+        self._blocks("prelude", n, lambda l: l, meta[1], meta[3], True, self.inj_bank, meta[2], None)
+
+    def _coda_body(self, meta: torch.Tensor, n: int, keep_logits: bool = False):
+        """meta rows: bank slot, token-log row, request slot, position."""
+
+        self._plan(meta[3], n, 1)
+        first = self.w.blocks["coda"][0]["norm_1"]
+        self._sandwich(n, self.state_bank, x_rows=meta[0], w1=self.w.ln_f, xd=self.xw, w2=first, y=self.h)
+        self._blocks("coda", n, self.coda_cache_layer, meta[2], meta[3], True, self.xw, None, self.w.ln_f)
+        return self._lm_head_argmax(self.h, n, self.w.lm_head, meta[1], meta[2], keep_logits)
+
+    #: metadata of a padding row per stage (token id, slot, bank, position / bank, log, slot, position)
+    _STAGE_PAD = {"prelude": (0, 0, -1, -1), "coda": (-1, -1, -1, -1)}
+
+    def _stage_meta_host(self, kind: str, bucket: int) -> np.ndarray:
+        pad = np.asarray(self._STAGE_PAD[kind], dtype=np.int32)[:, None]
+        return np.repeat(pad, bucket, axis=1)
+
+    def _stage_graph(self, kind: str, bucket: int) -> _Graph:
+        """The prelude or coda launch at ``bucket`` rows, captured once (padding rows: position -1,
+        bank and output rows -1)."""
+
+        key = (kind, bucket)
+        g = self.stage_graphs.get(key)
+        if g is not None:
+            return g
+        body = self._prelude_body if kind == "prelude" else self._coda_body
+        meta = torch.from_numpy(self._stage_meta_host(kind, bucket)).to(self.device)
+        with torch.cuda.stream(self.stream):  # warm up on an all-padding batch
+            body(meta, bucket)
+        self.stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        before = _lib.launch_count
+        with torch.cuda.graph(graph, pool=self.graph_pool, stream=self.stream):
+            body(meta, bucket)
+        captured = _lib.launch_count - before
+        self.stats.captured_calls += captured
+        if self.graph_pool is None:
+            self.graph_pool = graph.pool()
+        g = _Graph(graph=graph, meta=meta, launches=captured)
+        self.stage_graphs[key] = g
+        return g
+
+    def _replay_stage(self, kind: str, rows: list[list[int]]) -> None:
+        n = len(rows[0])
+        bucket = next(b for b in self.buckets if b >= n)
+        g = self._stage_graph(kind, bucket)
+        meta_host = self._stage_meta_host(kind, bucket)
+        for i, row in enumerate(rows):
+            meta_host[i, :n] = row
+        self.uploader.upload(meta_host, self.stream, out=g.meta)
+        with torch.cuda.stream(self.stream):
+            g.graph.replay()
+        self.stats.replayed_launches += g.launches
+
+    def _graphable(self, n: int) -> bool:
+        return self.use_cuda_graph and n <= self.buckets[-1]
+
     def prelude(self, token_ids: list[int], req_slots: list[int], hidden: list[int], positions=None) -> None:
         """``run_prelude`` for each item's token at its position; the output goes to ``inj_bank``."""
 
         if positions is None:
             raise ValueError("the Huginn prelude attends: positions are required")
-        s = self.shape
         n = len(token_ids)
         if n == 0:
             return
         self.flush_block_edits()
-        meta = self.upload([token_ids, req_slots, hidden, positions]).view(4, n)
+        rows = [list(token_ids), list(req_slots), list(hidden), list(positions)]
+        if self._graphable(n):
+            self._replay_stage("prelude", rows)
+            return
+        meta = self.upload(rows).view(4, n)
         with torch.cuda.stream(self.stream):
-            _lib.call(
-                "cdb_embed", _lib.ptr(self.w.wte), s.n_embd, s.vocab_size, _lib.ptr(meta[0]), _lib.ptr(meta[1]),
-                _lib.ptr(self.token_table), _lib.ptr(self.xw), self.xw.stride(0), None, n, s.embed_scale,
-                _lib.ptr(self.status), self._sp(),
-            )
-            self._plan(meta[3], n, 1)
-            self._first_norm(n, "prelude")
-            self._blocks("prelude", n, lambda l: l, meta[1], meta[3], True, self.inj_bank, meta[2], None)
+            self._prelude_body(meta, n)
 
     def coda(
         self, hidden: list[int], log_rows: list[int], req_slots: list[int], keep_logits: bool = False, positions=None
@@ -281,16 +353,15 @@ class HuginnRunner(OuroRunner):
 
         if positions is None:
             raise ValueError("the Huginn coda attends: positions are required")
-        s = self.shape
         n = len(hidden)
         self.flush_block_edits()
-        meta = self.upload([hidden, log_rows, req_slots, positions]).view(4, n)
+        rows = [list(hidden), list(log_rows), list(req_slots), list(positions)]
+        if self._graphable(n) and not (keep_logits or not self.fused_lm_head):
+            self._replay_stage("coda", rows)
+            return None
+        meta = self.upload(rows).view(4, n)
         with torch.cuda.stream(self.stream):
-            self._plan(meta[3], n, 1)
-            first = self.w.blocks["coda"][0]["norm_1"]
-            self._sandwich(n, self.state_bank, x_rows=meta[0], w1=self.w.ln_f, xd=self.xw, w2=first, y=self.h)
-            self._blocks("coda", n, self.coda_cache_layer, meta[2], meta[3], True, self.xw, None, self.w.ln_f)
-            return self._lm_head_argmax(self.h, n, self.w.lm_head, meta[1], meta[2], keep_logits)
+            return self._coda_body(meta, n, keep_logits)
 
     def prefill(
         self,

@@ -225,3 +225,33 @@ def test_huginn_cb_baseline_matches_reference_and_oracle(async_mode):
     rep = compare_lm_launches([lg for _, lg in eng.lm_logits], [lg for _, lg in o16.logits], [lg for _, lg in o32.logits])
     print(rep)
     assert_report(rep)
+
+
+def test_huginn_graphed_fused_coda_matches_stored_logits():
+    """The decode prelude and coda replay CUDA graphs (padded to the bucket size, padding rows at
+    position -1); the coda's fused LM head + argmax there must pick the argmax of the logits the
+    eager coda stores for the same teacher-forced inputs at >= 99% of positions (the two launches
+    run the GEMMs at different padded widths, so near-ties may flip)."""
+
+    data, shape = _golden()
+    run = next(r for r in data["runs"] if r["name"] == "replay_refill")
+    sd = random_huginn_state_dict(shape, seed=0, embed_std=data["embed_std"])
+    prompts, max_new, depths = data["prompts"], data["max_new_tokens"], run["exit_depths"]
+    _o32, toks = _oracle(shape, sd, prompts, max_new, depths, torch.float32)
+    preds = []
+    for keep in (False, True):
+        eng = _engine(shape, sd)
+        eng.record_trace = True
+        eng.keep_logits = keep
+        outs = eng.generate_batch(prompts, max_new_tokens=max_new, eos_token_id=None, exit_depths=depths,
+                                  forced_tokens=toks)
+        eng.runner.check_status()
+        assert eng.launch_trace == run["launches"]
+        kinds = {kind for kind, _bucket in eng.runner.stage_graphs}
+        assert kinds == ({"prelude"} if keep else {"prelude", "coda"}), kinds
+        preds.append([t for o in outs for t in o.generated_tokens])
+    n = len(preds[0])
+    assert n == len(preds[1]) == sum(max_new)
+    agree = sum(int(a == b) for a, b in zip(preds[0], preds[1], strict=True)) / n
+    print({"graphed_fused_vs_eager_stored": agree, "tokens": n})
+    assert agree >= 0.99
