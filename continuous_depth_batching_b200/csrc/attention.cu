@@ -51,7 +51,7 @@ struct AttnCfg {
   static constexpr int CONSUMERS = HG * WPH;
   static constexpr int THREADS = (CONSUMERS + 1) * 32;
   static constexpr int MERGE_FLOATS = D + 2;
-  static constexpr int SMEM = NSTAGE * STAGE_BYTES + 2 * NSTAGE * 8 + HG * MERGE_FLOATS * 4 + 64;
+  static constexpr int SMEM = NSTAGE * STAGE_BYTES + 3 * NSTAGE * 8 + HG * MERGE_FLOATS * 4 + 64;
   static_assert(DPL % 8 == 0, "QK lane slice must be whole 16-byte chunks");
   static_assert(TPW % TPP == 0, "tokens per warp must be whole passes");
 };
@@ -73,6 +73,7 @@ struct AttnParams {
   float* part_ml;
   int32_t* counters;
   int num_heads;
+  int num_items;  // rows of item_slot / item_pos
   float scale_log2;
   int32_t* status;
   // Fused append (append == 2): q is read unrotated and rotated in registers; the warp that
@@ -296,7 +297,8 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NSTAGE * C::STAGE_BYTES);
   uint64_t* empty = full + C::NSTAGE;
-  float* merge = reinterpret_cast<float*>(empty + C::NSTAGE);
+  uint64_t* spec = empty + C::NSTAGE;  // completion of the speculative first pages
+  float* merge = reinterpret_cast<float*>(spec + C::NSTAGE);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -304,12 +306,51 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
     for (int s = 0; s < C::NSTAGE; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], C::CONSUMERS);
+      mbar_init(&spec[s], 1);
     }
     fence_barrier_init();
   }
   if (warp == C::CONSUMERS && lane == 0) prefetch_tensormap(&map);
   __syncthreads();
   pdl_trigger();
+  // Speculative first pages (fused append only). The cached pages of positions below each row's
+  // new token do not depend on the previous kernel, so before griddepcontrol.wait the producer
+  // reads the plan, the block table and the first pages' block ids - as written by kernels that
+  // may be still in flight, so possibly stale - and starts loading up to NSTAGE pages into the
+  // ring, completing on `spec` instead of `full`. After the wait the producer walks the real
+  // plan; a page whose (head group, block id) matches the speculated one is handed to the
+  // consumers by a plain arrival on `full` once it has landed, any other page is loaded again
+  // (after the speculative copy into its stage has landed). The new token's own position is never
+  // read from a staged page in the fused mode, so a page loaded before its append is correct.
+  int spec_n = 0, spec_hg = -1;
+  int spec_ids[C::NSTAGE];
+#pragma unroll
+  for (int i = 0; i < C::NSTAGE; ++i) spec_ids[i] = -1;
+  if (p.fused && warp == C::CONSUMERS && lane == 0) {
+    const int nch = p.hdr[1];
+    if ((int)blockIdx.x < nch && nch <= kMaxPlanChunks) {
+      int u0, u1;
+      chunk_units(p.hdr, blockIdx.x, u0, u1);
+      if (u0 >= 0 && u0 < u1) {
+        const Unit unit = decode_unit(p.units[u0]);
+        const int slot = unit.row >= 0 && unit.row < p.num_items ? p.item_slot[unit.row] : -1;
+        if (slot >= 0 && unit.b0 >= 0 && unit.b0 < unit.b1 && unit.b1 <= p.bt_stride) {
+          const int32_t* bt = p.block_table + (int64_t)slot * p.bt_stride;
+          spec_n = min(C::NSTAGE, unit.b1 - unit.b0);
+          spec_hg = unit.hg;
+          for (int i = 0; i < spec_n; ++i) {
+            int id = bt[unit.b0 + i];
+            if (id < 0 || (int64_t)(id + 1) * kBlock > p.kv_rows) id = 0;
+            spec_ids[i] = id;
+            mbar_arrive_expect_tx(&spec[i], C::STAGE_BYTES);
+            uint8_t* dst = smem + i * C::STAGE_BYTES;
+            tma_load_4d(dst, &map, &spec[i], 0, spec_hg * HG, id * kBlock, 2 * p.cache_layer);
+            tma_load_4d(dst + C::TILE_BYTES, &map, &spec[i], 0, spec_hg * HG, id * kBlock, 2 * p.cache_layer + 1);
+          }
+        }
+      }
+    }
+  }
   pdl_wait();
 
   const int n_chunks = p.hdr[1];
@@ -320,6 +361,7 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
     int stage = 0;
     uint32_t phase = 0;
     bool alive = true;
+    int issued = 0;  // pages handed to the ring so far (lane 0)
     for (int c = blockIdx.x; c < n_chunks && alive; c += gridDim.x) {
     int u0, u1;
     chunk_units(p.hdr, c, u0, u1);
@@ -350,7 +392,14 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
               set_error(p.status, CDB_ERR_INDEX);
               block_id = 0;
             }
-            if (mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
+            if (issued < spec_n) {
+              // one of the speculative pages' stages: let that copy land before the stage is used
+              if (!mbar_wait(&spec[issued], 0, p.status)) alive = false;
+            }
+            if (!alive) {
+            } else if (issued < spec_n && spec_ids[issued] == block_id && spec_hg == unit.hg) {
+              mbar_arrive(&full[stage]);  // the speculative copy is this page
+            } else if (mbar_wait(&empty[stage], phase ^ 1u, p.status)) {
               mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
               uint8_t* dst = smem + stage * C::STAGE_BYTES;
               tma_load_4d(dst, &map, &full[stage], 0, unit.hg * HG, block_id * kBlock, 2 * p.cache_layer);
@@ -359,6 +408,7 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
             } else {
               alive = false;
             }
+            ++issued;
           }
           alive = __shfl_sync(0xffffffffu, alive, 0);
           if (!alive) break;
@@ -371,6 +421,9 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
       if (app_pos >= 0 && alive) append_store<D, HG>(p, unit.hg, app_pos, app);
     }
     }
+    // no speculative copy may still be in flight when the CTA exits (bounded waits)
+    if (lane == 0)
+      for (int i = issued; i < spec_n; ++i) mbar_wait(&spec[i], 0, p.status);
     return;
   }
 
@@ -1062,6 +1115,7 @@ extern "C" int cdb_paged_decode_attn_append(void* qkv, int64_t qkv_stride, int64
   p.part_ml = part_ml;
   p.counters = counters;
   p.num_heads = num_heads;
+  p.num_items = num_items;
   p.scale_log2 = scale * kLog2e;
   p.status = status;
   p.fused = append == 2;
@@ -1235,6 +1289,7 @@ extern "C" int cdb_paged_decode_attn_append_static(void* qkv, int64_t qkv_stride
   p.part_ml = part_ml;
   p.counters = counters;
   p.num_heads = num_heads;
+  p.num_items = num_items;
   p.scale_log2 = scale * kLog2e;
   p.status = status;
   p.fused = append == 2;
