@@ -664,11 +664,13 @@ __global__ void __launch_bounds__(AttnCfg<D, HG>::THREADS) decode_attn_kernel(co
     if (!last) continue;
     const int64_t base = ((int64_t)item * p.num_heads + head) * kMaxSplits;
     float mx = -INFINITY;
+#pragma unroll 4
     for (int sp = 0; sp < nsplit; ++sp) mx = fmaxf(mx, __ldcg(p.part_ml + 2 * (base + sp)));
     float lsum = 0.f;
     float acc[2 * C::PPL];
 #pragma unroll
     for (int i = 0; i < 2 * C::PPL; ++i) acc[i] = 0.f;
+#pragma unroll 4
     for (int sp = 0; sp < nsplit; ++sp) {
       const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + 2 * (base + sp)));
       const float w = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - mx);
