@@ -93,8 +93,8 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(Params p) {
   uint8_t* sv = sk + 2 * TK * PITCH;        // [2][TK][D]
   const uint32_t sq_u = smem_u32(sq), sk_u = smem_u32(sk), sv_u = smem_u32(sv);
 
-  const int4 tile = p.tiles[blockIdx.x];
-  const int head = blockIdx.y;
+  const int4 tile = p.tiles[blockIdx.y];  // heads vary fastest: a tile's heads launch together
+  const int head = blockIdx.x;
   const int row0 = tile.x, nrows = tile.y, slot = tile.z, pos0 = tile.w;
   const int kv_len = pos0 + nrows;
   const int n_kt = (kv_len + TK - 1) / TK;
@@ -268,7 +268,8 @@ static int launch(const Params& p, int num_tiles, cudaStream_t st) {
       return CDB_ERR_CUDA;
     attr = true;
   }
-  dim3 grid(num_tiles, p.num_heads);
+  if (num_tiles > 65535) return CDB_ERR_INVALID_ARGUMENT;  // grid y
+  dim3 grid(p.num_heads, num_tiles);
   launch_pdl(prefill_attn_kernel<D>, dim3(grid), dim3(128), SMEM, st, p);
   return cudaPeekAtLastError() == cudaSuccess ? CDB_OK : CDB_ERR_CUDA;
 }

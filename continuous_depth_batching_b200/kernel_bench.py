@@ -285,6 +285,49 @@ def run_proj_norm_chain(args) -> dict:
     return res
 
 
+def run_prefill_attention(args) -> dict:
+    """cdb_prefill_attention over ``--prompts`` fresh prompts of ``--length`` tokens each (causal,
+    the chunk's K/V already in the paged cache), L2 flushed before every launch. FLOPs count the
+    causal QK^T and PV products: 4 * heads * head_dim * L (L + 1) / 2 per prompt."""
+
+    from .runner import OuroRunner
+
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    heads, d, n_p, length = args.heads, args.head_dim, args.prompts, args.length
+    t = n_p * length
+    nb = (length + BLOCK - 1) // BLOCK
+    kv_rows = (n_p * nb + 2) * BLOCK
+    kv = torch.randn(1, 2, kv_rows, heads, d, device=dev, generator=g).to(torch.bfloat16)
+    table = torch.randperm(n_p * nb, device=dev, generator=g).to(torch.int32).view(n_p, nb)
+    hd = heads * d
+    qkv = torch.randn(t, 3 * hd, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(t, hd, device=dev, dtype=torch.bfloat16)
+    item_slot = [r for r in range(n_p) for _ in range(length)]
+    item_pos = [i for _ in range(n_p) for i in range(length)]
+    tiles = torch.tensor(OuroRunner.prefill_tiles(item_slot, item_pos), dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def launch():
+        _lib.call(
+            "cdb_prefill_attention", _lib.ptr(qkv), qkv.stride(0), hd, 2 * hd, _lib.ptr(out), out.stride(0),
+            _lib.ptr(kv), 1, kv_rows, 0, _lib.ptr(table), table.stride(0), _lib.ptr(tiles), tiles.shape[0], heads,
+            d, BLOCK, d**-0.5, _lib.ptr(status), stream.cuda_stream,
+        )
+
+    for _ in range(args.warmup):
+        launch()
+    torch.cuda.synchronize()
+    ms = _events_ms(launch, args.iters, stream, flush)
+    if int(status.item()) != 0:
+        raise RuntimeError(_lib.load().cdb_status_string(int(status.item())).decode())
+    flops = n_p * 4 * heads * d * length * (length + 1) / 2
+    return {"kernel": f"cdb::prefill::prefill_attn_kernel<{d}>", "prompts": n_p, "length": length, "tokens": t,
+            "tiles": int(tiles.shape[0]), "us": round(ms * 1e3, 2), "tflops": round(flops / (ms * 1e-3) / 1e12, 1)}
+
+
 def run_lm_head(args) -> dict:
     """cdb_lm_head_argmax against torch.mm (cuBLAS) + cdb_argmax on the same rows."""
 
@@ -429,6 +472,11 @@ def main(argv=None) -> None:
     gc.add_argument("--layers", type=int, default=24)
     gc.add_argument("--ctas-list", default="0,148,120,96,74",
                     help="comma-separated CTA counts (0 = the library's choice; > 0 forces stream-K)")
+    pa = sub.add_parser("prefill_attention")
+    pa.add_argument("--prompts", type=int, default=32)
+    pa.add_argument("--length", type=int, default=256)
+    pa.add_argument("--heads", type=int, default=16)
+    pa.add_argument("--head-dim", type=int, default=128)
     pn = sub.add_parser("proj_norm_chain")
     pn.add_argument("--m", type=int, default=80)
     pn.add_argument("--n", type=int, default=2048)
@@ -437,13 +485,14 @@ def main(argv=None) -> None:
     pn.add_argument("--splits-list", default="0,4,6,8,12,16")
     pr = sub.add_parser("prefill_rows")
     pr.add_argument("--rows", type=int, default=8192)
-    for s in (a, g, lm, gc, pr, pn):
+    for s in (a, g, lm, gc, pr, pn, pa):
         s.add_argument("--warmup", type=int, default=3)
         s.add_argument("--iters", type=int, default=20)
         s.add_argument("--seed", type=int, default=0)
     args = p.parse_args(argv)
     res = {"attention": run_attention, "gemm": run_gemm, "lm_head": run_lm_head, "gemm_chain": run_gemm_chain,
-           "prefill_rows": run_prefill_rows, "proj_norm_chain": run_proj_norm_chain}[
+           "prefill_rows": run_prefill_rows, "proj_norm_chain": run_proj_norm_chain,
+           "prefill_attention": run_prefill_attention}[
         args.kernel
     ](args)
     print(json.dumps(res))

@@ -420,7 +420,9 @@ class OuroRunner:
 
     @staticmethod
     def prefill_tiles(item_slot: list[int], item_pos: list[int], tile_rows: int = 64) -> list[tuple[int, int, int, int]]:
-        """Split prefill rows into runs of <= 64 consecutive positions of one request."""
+        """Split prefill rows into runs of <= 64 consecutive positions of one request, ordered by
+        the keys they attend to, most first: the kernel's CTAs start in tile order, so the longest
+        tiles start first and the short ones fill the tail."""
 
         tiles: list[tuple[int, int, int, int]] = []
         start = 0
@@ -434,6 +436,7 @@ class OuroRunner:
             ):
                 tiles.append((start, i - start, item_slot[start], item_pos[start]))
                 start = i
+        tiles.sort(key=lambda t: -(t[3] + t[1]))  # stable: ties keep row order
         return tiles
 
     def _layer_stack(self, n: int, base_layer: int, item_slot, item_pos, append: int, final_dst, final_rows, gate: bool):
