@@ -80,17 +80,21 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
 }
 
 template <int D>
-__global__ void __launch_bounds__(128) prefill_attn_kernel(Params p) {
+__global__ void __launch_bounds__(128, 3) prefill_attn_kernel(Params p) {
   pdl_trigger();
   pdl_wait();
   constexpr int NCH = D / 8;   // 16-byte chunks per row
   constexpr int KS = D / 16;   // k-steps over the head dim
   constexpr int NT = D / 8;    // n-tiles of the output
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* sq = smem;
   constexpr int PITCH = RowPitch<D>::BYTES;
-  uint8_t* sk = smem + TQ * PITCH;          // [2][TK][D]
+  uint8_t* sk = smem;                       // [2][TK][D]
   uint8_t* sv = sk + 2 * TK * PITCH;        // [2][TK][D]
+  // Q is staged in the second K buffer (TQ == TK rows), which the first prefetch overwrites only
+  // after every warp holds its Q fragments in registers: 64 KB of shared memory instead of 80, so
+  // three CTAs share an SM.
+  static_assert(TQ == TK, "Q borrows a K buffer");
+  uint8_t* sq = sk + TK * PITCH;
   const uint32_t sq_u = smem_u32(sq), sk_u = smem_u32(sk), sv_u = smem_u32(sv);
 
   const int4 tile = p.tiles[blockIdx.y];  // heads vary fastest: a tile's heads launch together
@@ -139,6 +143,7 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(Params p) {
     const int c = 2 * kk + (lane >> 4);
     ldsm_x4(sq_u + swz<D>(r, c), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
   }
+  __syncthreads();  // every warp has its Q fragments: the K buffer holding Q may be refilled
 
   float o[NT][4];
 #pragma unroll
@@ -260,7 +265,7 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(Params p) {
 
 template <int D>
 static int launch(const Params& p, int num_tiles, cudaStream_t st) {
-  constexpr int SMEM = TQ * RowPitch<D>::BYTES + 4 * TK * RowPitch<D>::BYTES;
+  constexpr int SMEM = 4 * TK * RowPitch<D>::BYTES;  // K and V double buffers (Q borrows one)
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(prefill_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) !=
