@@ -877,7 +877,14 @@ __global__ void rope_append_kernel(__nv_bfloat16* qkv, int64_t qkv_stride, int64
 // vector, 16-byte loads and stores. Every q chunk is read before any is rewritten in place (the
 // split-half rotation reads a partner chunk another thread owns). Same arithmetic as
 // rope_append_kernel (rope_load / rope_apply restate rope_pair per chunk).
-__global__ void rope_append_vec_kernel(__nv_bfloat16* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col,
+// One CTA per row, one thread per 8-element chunk of the row's heads. Rows of up to 256 chunks
+// (16 heads x 128) take the MAXT = 256 instantiation, bounded to 64 registers so four CTAs stay
+// resident per SM (the unbounded build took 68 and fit three); the kernel is latency-bound, one
+// row per CTA behind a chain of index loads. Wider rows (55 heads x 96) take MAXT = 1024, whose
+// bound also keeps a 1024-thread launch within the SM's 65,536 registers.
+template <int MAXT>
+__global__ void __launch_bounds__(MAXT, (MAXT <= 256 ? 4 : 1))
+    rope_append_vec_kernel(__nv_bfloat16* qkv, int64_t qkv_stride, int64_t k_col, int64_t v_col,
                                        __nv_bfloat16* kv, int64_t kv_rows, int cache_layer, const int32_t* block_table,
                                        int64_t bt_stride, const int32_t* item_slot, const int32_t* item_pos,
                                        int rope_mode, const void* rope_cos, const void* rope_sin,
@@ -1024,10 +1031,12 @@ static int launch_rope_append(void* qkv, int64_t qkv_stride, int64_t k_col, int6
                           ((reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin)) & 15) == 0) &&
                          (qkv_stride & 7) == 0 && (k_col & 7) == 0 && (v_col & 7) == 0;
   if (head_dim % 8 == 0 && chunks <= 1024 && aligned16) {
-    return launch_pdl(rope_append_vec_kernel, dim3(num_items), dim3(((chunks + 31) / 32) * 32), 0, st,
-                      static_cast<__nv_bfloat16*>(qkv), qkv_stride, k_col, v_col, static_cast<__nv_bfloat16*>(kv_base),
-                      kv_rows, cache_layer, block_table, bt_stride, item_slot, item_pos, rope_mode, rope_cos, rope_sin,
-                      static_cast<const __nv_bfloat16*>(qk_bias), num_heads, head_dim, status) == cudaSuccess
+    const int threads = ((chunks + 31) / 32) * 32;
+    auto* kern = threads <= 256 ? rope_append_vec_kernel<256> : rope_append_vec_kernel<1024>;
+    return launch_pdl(kern, dim3(num_items), dim3(threads), 0, st, static_cast<__nv_bfloat16*>(qkv), qkv_stride, k_col,
+                      v_col, static_cast<__nv_bfloat16*>(kv_base), kv_rows, cache_layer, block_table, bt_stride,
+                      item_slot, item_pos, rope_mode, rope_cos, rope_sin, static_cast<const __nv_bfloat16*>(qk_bias),
+                      num_heads, head_dim, status) == cudaSuccess
                ? CDB_OK
                : CDB_ERR_CUDA;
   }
