@@ -105,8 +105,11 @@ def run_attention(args) -> dict:
         1.0, 1e-4, dim, device=dev
     )[None, :]
     cos, sin = tab.cos().to(torch.bfloat16).contiguous(), tab.sin().to(torch.bfloat16).contiguous()
+    # the plan cuts the work into 2 * num_sms chunks, one per attention CTA: size it for --ctas
+    if args.ctas < 2 or args.ctas % 2:
+        raise SystemExit("--ctas must be an even number >= 2 (the plan makes two chunks per SM)")
     _lib.call(
-        "cdb_attn_plan", _lib.ptr(pos_d), args.rows, append, heads, dim, BLOCK, cap, scratch_items, 148,
+        "cdb_attn_plan", _lib.ptr(pos_d), args.rows, append, heads, dim, BLOCK, cap, scratch_items, args.ctas // 2,
         _lib.ptr(hdr), _lib.ptr(units), sp,
     )
 
