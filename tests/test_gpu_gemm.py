@@ -9,7 +9,9 @@ path), persistent CTA counts from one CTA (every tile in one range) to one per S
 over CTAs and combined through the workspace), and repeated calls (the combine sums pieces in k
 order, so results are bit-identical and the tile counters come back zeroed). Problems with fewer
 tiles than SMs take the split mode (K split over a thread-block cluster, reduced through
-distributed shared memory) unless a CTA count is forced.
+distributed shared memory) unless a CTA count is forced; problems above 256 token rows with at
+least two 256 x 256 tiles per SM pair take the CTA-pair mode (cta_group::2 MMAs) unless a CTA
+count is forced.
 """
 
 from __future__ import annotations
@@ -87,6 +89,26 @@ def test_gemm_cta_counts_and_repeat(gemm, ctas, m):
     _check(first, x, w)
 
 
+@pytest.mark.parametrize("m,n,k", [(2048, 6144, 2048), (8192, 2048, 5632), (4000, 5000, 520), (2304, 4352, 1024)])
+def test_pair_tiles_repeat_and_counters(gemm, m, n, k):
+    """Above 256 token rows, with at least two 256 x 256 pair tiles per SM pair, the library's
+    choice is the CTA-pair mode (tcgen05.mma.cta_group::2, stream-K over pairs with the split tiles
+    combined per half; ragged M and N included): within the fp32 bound, bit-identical across
+    calls, tile counters left zeroed."""
+
+    g = torch.Generator(device=DEV).manual_seed(m + n + k)
+    x = torch.randn(m, k, device=DEV, generator=g).to(torch.bfloat16)
+    w = (0.05 * torch.randn(n, k, device=DEV, generator=g)).to(torch.bfloat16)
+    first = gemm(x, w)
+    for _ in range(2):
+        again = gemm(x, w)
+        torch.cuda.synchronize()
+        assert torch.equal(first, again)
+    assert int(gemm.status.item()) == 0
+    assert int(gemm.work.ctr.abs().sum().item()) == 0
+    _check(first, x, w)
+
+
 def test_gemm_strided_operands_and_output(gemm):
     g = torch.Generator(device=DEV).manual_seed(3)
     big = torch.randn(64, 3000, device=DEV, generator=g).to(torch.bfloat16)
@@ -99,7 +121,11 @@ def test_gemm_strided_operands_and_output(gemm):
     assert out[:, 512:].abs().sum().item() == 0
 
 
-@pytest.mark.parametrize("m,inter,k", [(1, 5632, 2048), (80, 5632, 2048), (256, 5632, 2048), (700, 704, 256), (33, 504, 520)])
+@pytest.mark.parametrize(
+    "m,inter,k",
+    [(1, 5632, 2048), (80, 5632, 2048), (256, 5632, 2048), (700, 704, 256), (33, 504, 520), (8192, 5632, 2048),
+     (3000, 2000, 520)],
+)
 def test_gateup_silu_gemm(gemm, m, inter, k):
     """cdb_mlp_gateup_silu_gemm == plain GEMM on the same interleaved weight + cdb_silu_mul
     (bit-exact: same tiles and stream-K pieces), and within one bf16 rounding of gate/up of the fp32
