@@ -47,6 +47,12 @@
 // decode-shaped projection), stream-K would cut each tile into many pieces and leave one CTA to
 // read them all back; there the K range of each tile is split over a thread-block cluster whose
 // ranks reduce the partial tile through distributed shared memory instead.
+//
+// Pair mode (gemm_pair.cuh). Above 256 tokens, with at least two 256 x 256 tiles per pair of SMs,
+// the plain and SwiGLU epilogues run on 2-CTA clusters issuing tcgen05.mma.cta_group::2: each CTA
+// holds half of a 256 x 256 accumulator, which leaves TMEM room for two buffers, and the work is
+// stream-K over the pairs. The one-SM stream-K kernel below serves the LM head and the problems
+// pair mode does not take.
 #include <cooperative_groups.h>
 #include <cuda.h>
 
